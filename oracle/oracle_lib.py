@@ -1,0 +1,450 @@
+"""ctypes wrappers for the oracle libraries (test infrastructure only).
+
+``Oracle``     -- liboracle.so, the C++ restatement in vesper_oracle.cpp.
+``Reference``  -- _ref/libvesper_ref_nc.so (or libvesper_ref.so), the reference IVF-PQ
+                  sources compiled in place plus ref_bridge.cpp.
+
+Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg of bench.py import
+this module, and only to check or time the CPU side.  The product package never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libvesper_ref.so")
+REF_NC_SO = os.path.join(HERE, "_ref", "libvesper_ref_nc.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_sz = C.c_size_t
+_u32 = C.c_uint32
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Oracle:
+    """The restated reference arithmetic (bit-exact with the -ffp-contract=off build)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle oracle`")
+        L = self.lib = C.CDLL(path)
+        L.orc_l2_sq.restype = C.c_float
+        L.orc_l2_sq.argtypes = [_f32p, _f32p, _sz]
+        L.orc_inner_product.restype = C.c_float
+        L.orc_inner_product.argtypes = [_f32p, _f32p, _sz]
+        L.orc_assign.argtypes = [_f32p, _sz, _f32p, _u32, _sz, _u32p, C.c_void_p]
+        L.orc_coarse_probe.argtypes = [_f32p, _sz, _f32p, _u32, _sz, _u32, _u32p, _f32p]
+        L.orc_rotate.argtypes = [_f32p, _f32p, _sz, _sz, _f32p]
+        L.orc_rotate_T.argtypes = [_f32p, _f32p, _sz, _sz, _f32p]
+        L.orc_pq_encode.argtypes = [_f32p, _sz, _f32p, _u32, _u32, _sz, _u8p]
+        L.orc_pq_decode.argtypes = [_u8p, _sz, _f32p, _u32, _u32, _sz, _f32p]
+        L.orc_pq_lut.argtypes = [_f32p, _f32p, _u32, _u32, _sz, _f32p]
+        L.orc_adc.restype = C.c_float
+        L.orc_adc.argtypes = [_f32p, _u8p, _u32, _u32]
+        L.orc_ivfpq_add.argtypes = [_f32p, _sz, _f32p, _u32, _sz, C.c_void_p, _f32p, _u32, _u32,
+                                    _u32p, _u8p]
+        L.orc_ivfpq_search_batch.argtypes = [_f32p, _sz, _f32p, _u32, _sz, C.c_void_p, _f32p, _u32,
+                                             _u32, _u64p, _u64p, _u8p, _u32, _u32, _u64p, _f32p, _u32p]
+        L.orc_flat_topk.argtypes = [C.c_int, _f32p, _sz, _f32p, _u32, _sz, _u32, _u32p, _f32p]
+        L.orc_kmeanspp_init.argtypes = [_f32p, _sz, _sz, _u32, _u32, _f32p, _u32p]
+        L.orc_lloyd_assign.restype = C.c_float
+        L.orc_lloyd_assign.argtypes = [_f32p, _sz, _f32p, _u32, _sz, _u32p]
+        L.orc_lloyd_update.argtypes = [_f32p, _sz, _sz, _u32p, _u32, _f32p]
+        L.orc_elkan_update_centroid.argtypes = [_f32p, _sz, _u32p, _sz, _u32, _f32p]
+        L.orc_kmeans_elkan.restype = C.c_int
+        L.orc_kmeans_elkan.argtypes = [_f32p, _sz, _sz, _u32, _u32, C.c_float, _u32, _f32p, _u32p,
+                                       C.POINTER(_u32), C.POINTER(C.c_float)]
+        L.orc_pq_train.restype = C.c_int
+        L.orc_pq_train.argtypes = [_f32p, _sz, _sz, _u32, _u32, _f32p]
+
+    # -- primitives
+    def l2_sq(self, a, b):
+        a, b = _f32(a), _f32(b)
+        return float(self.lib.orc_l2_sq(a, b, a.size))
+
+    def inner_product(self, a, b):
+        a, b = _f32(a), _f32(b)
+        return float(self.lib.orc_inner_product(a, b, a.size))
+
+    def assign(self, x, c):
+        x, c = _f32(x), _f32(c)
+        out = np.zeros(x.shape[0], np.uint32)
+        self.lib.orc_assign(x, x.shape[0], c, c.shape[0], x.shape[1], out, None)
+        return out
+
+    def coarse_probe(self, q, c, nprobe):
+        q, c = _f32(q), _f32(c)
+        npb = min(nprobe, c.shape[0])
+        lists = np.zeros((q.shape[0], npb), np.uint32)
+        d = np.zeros((q.shape[0], npb), np.float32)
+        self.lib.orc_coarse_probe(q, q.shape[0], c, c.shape[0], q.shape[1], nprobe, lists, d)
+        return lists, d
+
+    def rotate(self, x, R):
+        x, R = _f32(x), _f32(R)
+        out = np.zeros_like(x)
+        self.lib.orc_rotate(x, R, x.shape[0], x.shape[1], out)
+        return out
+
+    def rotate_T(self, x, R):
+        x, R = _f32(x), _f32(R)
+        out = np.zeros_like(x)
+        self.lib.orc_rotate_T(x, R, x.shape[0], x.shape[1], out)
+        return out
+
+    def pq_encode(self, x, cb, m):
+        """cb: [m*ksub, dsub]."""
+        x, cb = _f32(x), _f32(cb)
+        ksub = cb.shape[0] // m
+        codes = np.zeros((x.shape[0], m), np.uint8)
+        self.lib.orc_pq_encode(x, x.shape[0], cb, m, ksub, cb.shape[1], codes)
+        return codes
+
+    def pq_decode(self, codes, cb, m):
+        codes, cb = np.ascontiguousarray(codes, np.uint8), _f32(cb)
+        ksub = cb.shape[0] // m
+        out = np.zeros((codes.shape[0], m * cb.shape[1]), np.float32)
+        self.lib.orc_pq_decode(codes, codes.shape[0], cb, m, ksub, cb.shape[1], out)
+        return out
+
+    def pq_lut(self, r, cb, m):
+        r, cb = _f32(r), _f32(cb)
+        ksub = cb.shape[0] // m
+        lut = np.zeros((m, ksub), np.float32)
+        self.lib.orc_pq_lut(r, cb, m, ksub, cb.shape[1], lut)
+        return lut
+
+    def adc(self, lut, code):
+        lut = _f32(lut)
+        code = np.ascontiguousarray(code, np.uint8)
+        return float(self.lib.orc_adc(lut, code, lut.shape[0], lut.shape[1]))
+
+    def ivfpq_add(self, x, c, R, cb, m):
+        x, c, cb = _f32(x), _f32(c), _f32(cb)
+        ksub = cb.shape[0] // m
+        assign = np.zeros(x.shape[0], np.uint32)
+        codes = np.zeros((x.shape[0], m), np.uint8)
+        Rp = None if R is None else _f32(R)
+        self.lib.orc_ivfpq_add(x, x.shape[0], c, c.shape[0], x.shape[1],
+                               None if Rp is None else Rp.ctypes.data, cb, m, ksub, assign, codes)
+        return assign, codes
+
+    def ivfpq_search(self, q, c, R, cb, m, list_offsets, ids, codes, k, nprobe):
+        q, c, cb = _f32(q), _f32(c), _f32(cb)
+        ksub = cb.shape[0] // m
+        nq = q.shape[0]
+        out_ids = np.zeros((nq, k), np.uint64)
+        out_d = np.zeros((nq, k), np.float32)
+        counts = np.zeros(nq, np.uint32)
+        Rp = None if R is None else _f32(R)
+        self.lib.orc_ivfpq_search_batch(
+            q, nq, c, c.shape[0], q.shape[1], None if Rp is None else Rp.ctypes.data, cb, m, ksub,
+            np.ascontiguousarray(list_offsets, np.uint64), np.ascontiguousarray(ids, np.uint64),
+            np.ascontiguousarray(codes, np.uint8), k, nprobe, out_ids, out_d, counts)
+        return out_ids, out_d, counts
+
+    def flat_topk(self, op, q, base, k):
+        q, base = _f32(q), _f32(base)
+        idx = np.zeros((q.shape[0], k), np.uint32)
+        sc = np.zeros((q.shape[0], k), np.float32)
+        self.lib.orc_flat_topk(op, q, q.shape[0], base, base.shape[0], q.shape[1], k, idx, sc)
+        return idx, sc
+
+    def kmeanspp_init(self, x, k, seed):
+        x = _f32(x)
+        c = np.zeros((k, x.shape[1]), np.float32)
+        idx = np.zeros(k, np.uint32)
+        self.lib.orc_kmeanspp_init(x, x.shape[0], x.shape[1], k, seed, c, idx)
+        return c, idx
+
+    def lloyd_assign(self, x, c):
+        x, c = _f32(x), _f32(c)
+        out = np.zeros(x.shape[0], np.uint32)
+        inertia = self.lib.orc_lloyd_assign(x, x.shape[0], c, c.shape[0], x.shape[1], out)
+        return out, float(inertia)
+
+    def lloyd_update(self, x, assign, c):
+        x = _f32(x)
+        c = _f32(c).copy()
+        self.lib.orc_lloyd_update(x, x.shape[0], x.shape[1], np.ascontiguousarray(assign, np.uint32),
+                                  c.shape[0], c)
+        return c
+
+    def elkan_update(self, x, assign, c):
+        x = _f32(x)
+        c = _f32(c).copy()
+        self.lib.orc_elkan_update_centroid(x, x.shape[1], np.ascontiguousarray(assign, np.uint32),
+                                           x.shape[0], c.shape[0], c)
+        return c
+
+    def kmeans_elkan(self, x, k, max_iter=25, eps=1e-4, seed=42):
+        x = _f32(x)
+        c = np.zeros((k, x.shape[1]), np.float32)
+        a = np.zeros(x.shape[0], np.uint32)
+        it = _u32(0)
+        inertia = C.c_float(0)
+        rc = self.lib.orc_kmeans_elkan(x, x.shape[0], x.shape[1], k, max_iter, eps, seed, c, a,
+                                       C.byref(it), C.byref(inertia))
+        if rc != 0:
+            raise ValueError("kmeans_elkan: n < k")
+        return c, a, it.value, inertia.value
+
+    def pq_train(self, x, m, nbits):
+        x = _f32(x)
+        dsub = x.shape[1] // m
+        cb = np.zeros(((1 << nbits) * m, dsub), np.float32)
+        rc = self.lib.orc_pq_train(x, x.shape[0], x.shape[1], m, nbits, cb)
+        if rc != 0:
+            raise ValueError("pq_train: dim % m != 0")
+        return cb
+
+
+class Reference:
+    """The reference implementation itself, compiled from its sources (oracle/Makefile)."""
+
+    def __init__(self, path: str = REF_NC_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref` where the reference is mounted")
+        L = self.lib = C.CDLL(path)
+        L.rb_last_error.restype = C.c_char_p
+        L.rb_l2_sq.restype = C.c_float
+        L.rb_l2_sq.argtypes = [_f32p, _f32p, _sz]
+        L.rb_inner_product.restype = C.c_float
+        L.rb_inner_product.argtypes = [_f32p, _f32p, _sz]
+        L.rb_ivfpq_create.restype = C.c_void_p
+        L.rb_ivfpq_destroy.argtypes = [C.c_void_p]
+        L.rb_ivfpq_train.restype = C.c_int
+        L.rb_ivfpq_train.argtypes = [C.c_void_p, _f32p, _sz, _sz, _u32, _u32, _u32, C.c_int, C.c_int,
+                                     _u32, C.c_float, _u32, _sz, _u32]
+        L.rb_ivfpq_add.restype = C.c_int
+        L.rb_ivfpq_add.argtypes = [C.c_void_p, _u64p, _f32p, _sz]
+        L.rb_ivfpq_search_batch.restype = C.c_int
+        L.rb_ivfpq_search_batch.argtypes = [C.c_void_p, _f32p, _sz, _u32, _u32, _u64p, _f32p, _u32p]
+        L.rb_ivfpq_save.restype = C.c_int
+        L.rb_ivfpq_save.argtypes = [C.c_void_p, C.c_char_p]
+        L.rb_ivfpq_load.restype = C.c_int
+        L.rb_ivfpq_load.argtypes = [C.c_void_p, C.c_char_p]
+        L.rb_kmeanspp_init.argtypes = [_f32p, _sz, _sz, _u32, _u32, _f32p]
+        for fn in ("rb_kmeans_elkan", "rb_kmeans_lloyd"):
+            getattr(L, fn).restype = C.c_int
+            getattr(L, fn).argtypes = [_f32p, _sz, _sz, _u32, _u32, C.c_float, _u32, _f32p, _u32p,
+                                       C.POINTER(_u32), C.POINTER(C.c_float)]
+        L.rb_kmeans_assign.restype = C.c_float
+        L.rb_kmeans_assign.argtypes = [_f32p, _sz, _f32p, _u32, _sz, _u32p]
+        L.rb_kmeans_update.argtypes = [_f32p, _sz, _sz, _u32p, _u32, _f32p]
+        L.rb_pq_create.restype = C.c_void_p
+        L.rb_pq_create.argtypes = [_u32, _u32]
+        L.rb_pq_destroy.argtypes = [C.c_void_p]
+        L.rb_pq_train.restype = C.c_int
+        L.rb_pq_train.argtypes = [C.c_void_p, _f32p, _sz, _sz]
+        L.rb_pq_import.argtypes = [C.c_void_p, _sz, _f32p, _sz]
+        L.rb_pq_export.argtypes = [C.c_void_p, _f32p]
+        L.rb_pq_encode.argtypes = [C.c_void_p, _f32p, _sz, _u8p]
+        L.rb_pq_lut.argtypes = [C.c_void_p, _f32p, _f32p]
+        L.rb_pq_adc.argtypes = [C.c_void_p, _f32p, _u8p, _sz, _f32p]
+        L.rb_flat_topk.argtypes = [C.c_int, _f32p, _sz, _f32p, _u32, _sz, _u32, _u32p, _f32p]
+
+    def error(self):
+        return self.lib.rb_last_error().decode()
+
+    def l2_sq(self, a, b):
+        a, b = _f32(a), _f32(b)
+        return float(self.lib.rb_l2_sq(a, b, a.size))
+
+    def inner_product(self, a, b):
+        a, b = _f32(a), _f32(b)
+        return float(self.lib.rb_inner_product(a, b, a.size))
+
+    def kmeanspp_init(self, x, k, seed):
+        x = _f32(x)
+        c = np.zeros((k, x.shape[1]), np.float32)
+        self.lib.rb_kmeanspp_init(x, x.shape[0], x.shape[1], k, seed, c)
+        return c
+
+    def _kmeans(self, fn, x, k, max_iter, eps, seed):
+        x = _f32(x)
+        c = np.zeros((k, x.shape[1]), np.float32)
+        a = np.zeros(x.shape[0], np.uint32)
+        it = _u32(0)
+        inertia = C.c_float(0)
+        rc = fn(x, x.shape[0], x.shape[1], k, max_iter, eps, seed, c, a, C.byref(it), C.byref(inertia))
+        if rc != 0:
+            raise ValueError(self.error())
+        return c, a, it.value, inertia.value
+
+    def kmeans_elkan(self, x, k, max_iter=25, eps=1e-4, seed=42):
+        return self._kmeans(self.lib.rb_kmeans_elkan, x, k, max_iter, eps, seed)
+
+    def kmeans_lloyd(self, x, k, max_iter=25, eps=1e-4, seed=42):
+        return self._kmeans(self.lib.rb_kmeans_lloyd, x, k, max_iter, eps, seed)
+
+    def kmeans_assign(self, x, c):
+        x, c = _f32(x), _f32(c)
+        out = np.zeros(x.shape[0], np.uint32)
+        inertia = self.lib.rb_kmeans_assign(x, x.shape[0], c, c.shape[0], x.shape[1], out)
+        return out, float(inertia)
+
+    def kmeans_update(self, x, assign, c):
+        x = _f32(x)
+        c = _f32(c).copy()
+        self.lib.rb_kmeans_update(x, x.shape[0], x.shape[1], np.ascontiguousarray(assign, np.uint32),
+                                  c.shape[0], c)
+        return c
+
+    def flat_topk(self, op, q, base, k):
+        q, base = _f32(q), _f32(base)
+        idx = np.zeros((q.shape[0], k), np.uint32)
+        sc = np.zeros((q.shape[0], k), np.float32)
+        self.lib.rb_flat_topk(op, q, q.shape[0], base, base.shape[0], q.shape[1], k, idx, sc)
+        return idx, sc
+
+    def pq(self, m, nbits):
+        return RefPq(self, m, nbits)
+
+    def ivfpq(self):
+        return RefIvfPq(self)
+
+
+class RefPq:
+    def __init__(self, ref: Reference, m: int, nbits: int):
+        self.ref, self.m, self.ksub = ref, m, 1 << nbits
+        self.h = ref.lib.rb_pq_create(m, nbits)
+        self.dsub = 0
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.rb_pq_destroy(self.h)
+            self.h = None
+
+    def train(self, x):
+        x = _f32(x)
+        self.dsub = x.shape[1] // self.m
+        if self.ref.lib.rb_pq_train(self.h, x, x.shape[0], x.shape[1]) != 0:
+            raise ValueError(self.ref.error())
+
+    def import_codebooks(self, cb):
+        cb = _f32(cb)
+        self.dsub = cb.shape[1]
+        self.ref.lib.rb_pq_import(self.h, cb.shape[1], cb, cb.size)
+
+    def codebooks(self):
+        out = np.zeros((self.m * self.ksub, self.dsub), np.float32)
+        self.ref.lib.rb_pq_export(self.h, out)
+        return out
+
+    def encode(self, x):
+        x = _f32(x)
+        codes = np.zeros((x.shape[0], self.m), np.uint8)
+        self.ref.lib.rb_pq_encode(self.h, x, x.shape[0], codes)
+        return codes
+
+    def lut(self, q):
+        out = np.zeros((self.m, self.ksub), np.float32)
+        self.ref.lib.rb_pq_lut(self.h, _f32(q), out)
+        return out
+
+    def adc(self, q, codes):
+        codes = np.ascontiguousarray(codes, np.uint8)
+        out = np.zeros(codes.shape[0], np.float32)
+        self.ref.lib.rb_pq_adc(self.h, _f32(q), codes, codes.shape[0], out)
+        return out
+
+
+class RefIvfPq:
+    def __init__(self, ref: Reference):
+        self.ref = ref
+        self.h = ref.lib.rb_ivfpq_create()
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.rb_ivfpq_destroy(self.h)
+            self.h = None
+
+    def train(self, x, nlist, m, nbits=8, use_opq=False, brute_assign=True, max_iter=25,
+              epsilon=1e-4, seed=42, opq_sample_n=20000, opq_iter=10):
+        x = _f32(x)
+        rc = self.ref.lib.rb_ivfpq_train(self.h, x, x.shape[1], x.shape[0], nlist, m, nbits,
+                                         int(use_opq), int(brute_assign), max_iter, epsilon, seed,
+                                         opq_sample_n, opq_iter)
+        if rc != 0:
+            raise ValueError(self.ref.error())
+
+    def add(self, ids, x):
+        x = _f32(x)
+        rc = self.ref.lib.rb_ivfpq_add(self.h, np.ascontiguousarray(ids, np.uint64), x, x.shape[0])
+        if rc != 0:
+            raise ValueError(self.ref.error())
+
+    def search(self, q, k, nprobe):
+        q = _f32(q)
+        nq = q.shape[0]
+        ids = np.zeros((nq, k), np.uint64)
+        d = np.zeros((nq, k), np.float32)
+        counts = np.zeros(nq, np.uint32)
+        rc = self.ref.lib.rb_ivfpq_search_batch(self.h, q, nq, k, nprobe, ids, d, counts)
+        if rc != 0:
+            raise ValueError(self.ref.error())
+        return ids, d, counts
+
+    def save(self, directory):
+        if self.ref.lib.rb_ivfpq_save(self.h, directory.encode()) != 0:
+            raise IOError(self.ref.error())
+
+    def load(self, directory):
+        if self.ref.lib.rb_ivfpq_load(self.h, directory.encode()) != 0:
+            raise IOError(self.ref.error())
+
+
+def read_ivfpq_v10(path: str) -> dict:
+    """Parse an ``ivfpq.bin`` v1.0 file (the layout IvfPqIndex::save writes,
+    src/index/ivf_pq.cpp:4412-4490) into arrays: centroids, codebooks [m*ksub, dsub],
+    rotation or None, and the inverted lists as CSR (list_offsets, ids, codes) in
+    list order, entries in file order.  Verifies the FNV-1a-64 trailer."""
+    raw = open(path, "rb").read()
+    if raw[:8] != b"IVFPQv10":
+        raise ValueError("not a v1.0 IVF-PQ file")
+    h = 1469598103934665603
+    body = raw[:-12]
+    arr = np.frombuffer(body, np.uint8)
+    # FNV-1a 64 over the body (vectorised in chunks would be faster; files here are small)
+    for b in arr.tobytes():
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    if raw[-12:-8] != b"CHKS" or int.from_bytes(raw[-8:], "little") != h:
+        raise ValueError("checksum mismatch")
+    off = 8
+    ver_major, ver_minor = np.frombuffer(raw, np.uint16, 2, off); off += 4
+    flags, dim, nlist, m, nbits, dsub = np.frombuffer(raw, np.uint32, 6, off); off += 24
+    nvec = int(np.frombuffer(raw, np.uint64, 1, off)[0]); off += 8
+    code_size = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4
+    off += 8  # build timestamp
+    meta_len = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4 + meta_len
+    dim, nlist, m, nbits, dsub = int(dim), int(nlist), int(m), int(nbits), int(dsub)
+    cent = np.frombuffer(raw, np.float32, nlist * dim, off).reshape(nlist, dim).copy(); off += nlist * dim * 4
+    ksub = 1 << nbits
+    cb = np.frombuffer(raw, np.float32, m * ksub * dsub, off).reshape(m * ksub, dsub).copy(); off += cb.nbytes
+    R = None
+    if flags & 1:
+        R = np.frombuffer(raw, np.float32, dim * dim, off).reshape(dim, dim).copy(); off += R.nbytes
+    lists_count = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4
+    offs = np.zeros(lists_count + 1, np.uint64)
+    ids, codes = [], []
+    for li in range(lists_count):
+        sz = int(np.frombuffer(raw, np.uint64, 1, off)[0]); off += 8
+        rec = np.frombuffer(raw, np.uint8, sz * (8 + m), off).reshape(sz, 8 + m); off += sz * (8 + m)
+        ids.append(rec[:, :8].copy().view(np.uint64).reshape(-1))
+        codes.append(rec[:, 8:].copy())
+        offs[li + 1] = offs[li] + sz
+    return dict(dim=dim, nlist=nlist, m=m, nbits=nbits, dsub=dsub, nvec=nvec, flags=int(flags),
+                centroids=cent, codebooks=cb, rotation=R, list_offsets=offs,
+                ids=np.concatenate(ids) if ids else np.zeros(0, np.uint64),
+                codes=np.concatenate(codes) if codes else np.zeros((0, m), np.uint8))
