@@ -1,0 +1,122 @@
+/* B200 extensions to the Vesper IVF-PQ C ABI (libvesper_c.so).
+ *
+ * The reference's C struct carries only nlist/m/nbits and k/nprobe
+ * (include/vesper/c/vesper.h:43-52); everything else in IvfPqTrainParams /
+ * IvfPqSearchParams (include/vesper/index/ivf_pq.hpp:59-117) is reachable only from
+ * its C++ API.  These entry points expose those fields, plus device-resident search
+ * and per-stage timings.  All existing vesper.h symbols stay ABI-identical.
+ */
+#ifndef VESPER_B200_EXT_H
+#define VESPER_B200_EXT_H
+
+#include "vesper.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Full training parameters (IvfPqTrainParams, ivf_pq.hpp:59-106).  Set struct_size to
+ * sizeof(vesper_ivfpq_train_params_ex_t); vesper_ivfpq_train_params_ex_init fills the
+ * reference defaults. */
+typedef struct vesper_ivfpq_train_params_ex_s {
+  size_t struct_size;
+  uint32_t nlist;
+  uint32_t m;
+  uint32_t nbits;
+  uint32_t max_iter;       /* k-means iterations, default 25 */
+  float epsilon;           /* k-means convergence threshold, default 1e-4 */
+  int use_opq;             /* default 1 */
+  uint32_t opq_iter;       /* default 10 (the alternation runs at most 3) */
+  size_t opq_sample_n;     /* default 20000 */
+  int opq_init_pca;        /* 1 = PCA (default), 0 = identity */
+  uint32_t seed;           /* default 42 */
+  int verbose;
+} vesper_ivfpq_train_params_ex_t;
+
+VESPER_C_API void vesper_ivfpq_train_params_ex_init(vesper_ivfpq_train_params_ex_t* p);
+
+/* IvfPqIndex::train with every field of IvfPqTrainParams (ivf_pq.hpp:161-163). */
+VESPER_C_API vesper_status_t vesper_ivfpq_train_ex(vesper_index_t* index, const float* base_vectors,
+                                                   size_t dim, size_t n,
+                                                   const vesper_ivfpq_train_params_ex_t* params);
+
+/* vesper_ivfpq_train_ex / vesper_ivfpq_add with the input vectors (and ids) in device
+ * memory of the index's GPU: no host staging of the data set. */
+VESPER_C_API vesper_status_t vesper_ivfpq_train_ex_device(vesper_index_t* index, const float* d_base_vectors,
+                                                          size_t dim, size_t n,
+                                                          const vesper_ivfpq_train_params_ex_t* params);
+VESPER_C_API vesper_status_t vesper_ivfpq_add_device(vesper_index_t* index, const uint64_t* d_ids,
+                                                     const float* d_base_vectors, size_t n);
+
+/* Report of the last train call: whether the OPQ rotation was kept and the two
+ * reconstruction errors the keep/drop decision compared (ivf_pq.cpp:2730-2748). */
+typedef struct vesper_ivfpq_train_report_s {
+  int opq_kept;
+  double err_unrot;
+  double err_opq;
+  uint32_t coarse_iterations;
+  float train_time_sec;
+} vesper_ivfpq_train_report_t;
+VESPER_C_API vesper_status_t vesper_ivfpq_get_train_report(const vesper_index_t* index,
+                                                           vesper_ivfpq_train_report_t* out);
+
+/* Search arithmetic: FAST builds the lookup table once per query (distances equal the
+ * exact ones to fp32 rounding); EXACT reproduces the reference's per-(query, list)
+ * lookup tables and rotations operation for operation (bit-identical results). */
+typedef enum vesper_search_mode_e { VESPER_SEARCH_FAST = 0, VESPER_SEARCH_EXACT = 1 } vesper_search_mode_t;
+
+typedef struct vesper_ivfpq_search_params_ex_s {
+  size_t struct_size;
+  uint32_t k;              /* at most 1024 */
+  uint32_t nprobe;         /* clamped to nlist, at most 1024 */
+  uint32_t mode;           /* vesper_search_mode_t */
+} vesper_ivfpq_search_params_ex_t;
+
+/* vesper_ivfpq_search_batch with a search mode; out_counts (may be NULL) receives the
+ * number of real results per query (the rest of each row is padding). */
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_ex(const vesper_index_t* index,
+                                                          const float* queries, size_t nq,
+                                                          const vesper_ivfpq_search_params_ex_t* params,
+                                                          uint64_t* out_ids, float* out_distances,
+                                                          uint32_t* out_counts);
+
+/* Same, with queries and outputs in device memory of the index's GPU (no host copies). */
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device(const vesper_index_t* index,
+                                                              const float* d_queries, size_t nq,
+                                                              const vesper_ivfpq_search_params_ex_t* params,
+                                                              uint64_t* d_out_ids, float* d_out_distances,
+                                                              uint32_t* d_out_counts);
+
+/* Device time per stage of the last search call (CUDA events, milliseconds). */
+typedef struct vesper_ivfpq_timings_s {
+  float coarse_ms;   /* query-centroid distances */
+  float select_ms;   /* top-nprobe selection */
+  float rotate_ms;   /* OPQ rotation of queries / residuals */
+  float scan_ms;     /* lookup tables + inverted-list scan + per-list top-k */
+  float merge_ms;    /* per-query merge (EXACT mode) */
+  float total_ms;
+  uint64_t scanned_entries; /* sum over queries of the probed lists' sizes */
+} vesper_ivfpq_timings_t;
+VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index,
+                                                           vesper_ivfpq_timings_t* out);
+
+/* Install a trained model (centroids [nlist x dim], codebooks [m * 2^nbits x dim/m],
+ * rotation [dim x dim] or NULL) and empty the lists.  Used to search or add with a
+ * model trained elsewhere, e.g. by the reference CPU implementation. */
+VESPER_C_API vesper_status_t vesper_ivfpq_set_model(vesper_index_t* index, size_t dim, uint32_t nlist,
+                                                    uint32_t m, uint32_t nbits, const float* centroids,
+                                                    const float* codebooks, const float* rotation);
+
+/* Copy out the inverted lists: offsets [nlist + 1], ids [n_vectors], codes
+ * [n_vectors x m], entries list-contiguous in insertion order.  Any pointer may be NULL. */
+VESPER_C_API vesper_status_t vesper_ivfpq_get_lists(const vesper_index_t* index, uint64_t* out_offsets,
+                                                    uint64_t* out_ids, uint8_t* out_codes);
+
+/* Number of CUDA devices visible to the library. */
+VESPER_C_API int vesper_b200_device_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VESPER_B200_EXT_H */

@@ -1,0 +1,104 @@
+"""Generate the golden fixtures in tests/golden/ from the reference implementation.
+
+Run where the reference sources are mounted and oracle/_ref is built
+(`make -C oracle`):
+
+    python tests/golden/make_golden.py /root/reference
+
+Outputs (all small, committed):
+  pq_lut_small.json     algorithms/fixtures/pq/pq_lut_small.json with its arithmetic
+                        expressions evaluated (the original is not valid JSON)
+  l2_ip_small.json      algorithms/fixtures/distance_kernels/l2_ip_small.json
+  ivfpq_<case>/ivfpq.bin   indexes trained and filled by the reference IvfPqIndex
+                           (brute-force coarse assigner), saved by its own save()
+  ivfpq_<case>.npz      the base vectors and queries used, and the reference's
+                        search results for several (k, nprobe)
+  kmeans_small.npz      reference k-means++ / Elkan / Lloyd / PQ-train outputs
+"""
+from __future__ import annotations
+
+import json
+import os
+import re
+import shutil
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "..", "..", "oracle"))
+from oracle_lib import Reference  # noqa: E402
+
+# (case name, dim, nlist, m, use_opq, n_base, n_train, mixture centres, sigma)
+CASES = [
+    ("plain_d32_m8", 32, 16, 8, False, 2000, 1500, 40, 0.1),    # dsub = 4 (all scalar tail)
+    ("plain_d64_m8", 64, 24, 8, False, 2000, 1500, 50, 0.1),    # dsub = 8 (one FMA lane step)
+    ("opq_d32_m4", 32, 16, 4, True, 2000, 1500, 40, 0.2),       # OPQ kept/dropped by the reference
+    ("odd_d20_m5", 20, 8, 5, False, 800, 600, 20, 0.1),         # dim % 8 != 0 coarse tail
+]
+SEARCHES = [(10, 4), (10, 16), (100, 8), (5, 1), (3, 64)]
+
+
+def mixture(n, d, ncent, sigma, seed):
+    g = np.random.default_rng(seed)
+    cent = g.uniform(-1, 1, (ncent, d)).astype(np.float32)
+    lab = g.integers(0, ncent, n)
+    return (cent[lab] + sigma * g.standard_normal((n, d))).astype(np.float32)
+
+
+def convert_fixtures(ref_root):
+    src = os.path.join(ref_root, "algorithms", "fixtures", "pq", "pq_lut_small.json")
+    text = open(src).read()
+    # evaluate "a + b" literal expressions so the file parses as JSON
+    text = re.sub(r"(-?\d+\.\d+)\s*\+\s*(-?\d+\.\d+)", lambda mt: repr(float(mt.group(1)) + float(mt.group(2))), text)
+    json.dump(json.loads(text), open(os.path.join(HERE, "pq_lut_small.json"), "w"), indent=1)
+    src = os.path.join(ref_root, "algorithms", "fixtures", "distance_kernels", "l2_ip_small.json")
+    json.dump(json.load(open(src)), open(os.path.join(HERE, "l2_ip_small.json"), "w"), indent=1)
+
+
+def make_ivfpq(ref: Reference):
+    for (name, d, nlist, m, opq, nb, nt, nc, sigma) in CASES:
+        x = mixture(nb, d, nc, sigma, 11)
+        q = mixture(40, d, nc, sigma, 12)
+        idx = ref.ivfpq()
+        idx.train(x[:nt], nlist, m, 8, use_opq=opq, brute_assign=True, opq_sample_n=1200)
+        # An empty index (trained model only) for add parity.
+        out_model = os.path.join(HERE, f"ivfpq_{name}_model")
+        shutil.rmtree(out_model, ignore_errors=True)
+        idx.save(out_model)
+        idx.add(np.arange(nb, dtype=np.uint64) * 3 + 7, x)
+        out = os.path.join(HERE, f"ivfpq_{name}")
+        shutil.rmtree(out, ignore_errors=True)
+        idx.save(out)
+        res = {}
+        for k, npb in SEARCHES:
+            ids, dist, cnt = idx.search(q, k, npb)
+            res[f"ids_{k}_{npb}"] = ids
+            res[f"d_{k}_{npb}"] = dist
+            res[f"n_{k}_{npb}"] = cnt
+        np.savez_compressed(os.path.join(HERE, f"ivfpq_{name}.npz"), base=x, queries=q, n_train=nt, **res)
+        print("wrote", name)
+
+
+def make_kmeans(ref: Reference):
+    x = mixture(3000, 16, 60, 0.05, 21)
+    kpp = ref.kmeanspp_init(x, 48, 42)
+    c_e, a_e, it_e, in_e = ref.kmeans_elkan(x, 48, 25, 1e-4, 42)
+    c_l, a_l, it_l, in_l = ref.kmeans_lloyd(x, 48, 20, 0.0, 42)
+    asg, inert = ref.kmeans_assign(x, kpp)
+    upd = ref.kmeans_update(x, asg, kpp)
+    pq = ref.pq(4, 8)
+    pq.train(x)
+    np.savez_compressed(os.path.join(HERE, "kmeans_small.npz"), x=x, kpp=kpp, elkan_c=c_e, elkan_a=a_e,
+                        elkan_it=it_e, elkan_inertia=in_e, lloyd_c=c_l, lloyd_a=a_l, lloyd_it=it_l,
+                        lloyd_inertia=in_l, assign=asg, assign_inertia=inert, update=upd,
+                        pq_cb=pq.codebooks())
+    print("wrote kmeans_small")
+
+
+if __name__ == "__main__":
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    convert_fixtures(ref_root)
+    ref = Reference()
+    make_ivfpq(ref)
+    make_kmeans(ref)

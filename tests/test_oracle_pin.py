@@ -1,0 +1,142 @@
+"""Pin the oracle (oracle/vesper_oracle.cpp) before trusting it as the checker.
+
+Against the reference's own fixtures (algorithms/fixtures/*, converted by
+tests/golden/make_golden.py), against indexes and k-means runs produced by the
+reference implementation itself (tests/golden/*), against restatements of the
+reference's unit tests, and -- where oracle/_ref is built -- against the reference
+library on fresh random inputs.  Everything here must be bit-exact.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import CASES, GOLDEN, SEARCHES, golden_case
+
+
+def test_fixture_pq_lut_small(oracle):
+    # algorithms/fixtures/pq/pq_lut_small.json: ADC = sum of LUT entries in order.
+    fx = json.load(open(os.path.join(GOLDEN, "pq_lut_small.json")))
+    lut = np.zeros((fx["m"], 1 << fx["nbits"]), np.float32)
+    for s, row in enumerate(fx["lut"]):
+        lut[s, :len(row)] = row
+    exp = {e["id"]: e["dist"] for e in fx["expected_dist"]}
+    for c in fx["codes"]:
+        assert oracle.adc(lut, np.array(c["u"], np.uint8)) == np.float32(exp[c["id"]])
+
+
+def test_fixture_l2_ip_small(oracle):
+    # algorithms/fixtures/distance_kernels/l2_ip_small.json.  Its l2 for id 2 (4.0)
+    # contradicts its own vectors: a - b = [0, 0, 2, -2], so ||a - b||^2 = 8.  No
+    # reference test reads this file, and the reference library returns 8.0 for it
+    # (checked against oracle/_ref in test_oracle_vs_reference_random), so the oracle
+    # is pinned to the library's value there and to the fixture everywhere else.
+    fx = json.load(open(os.path.join(GOLDEN, "l2_ip_small.json")))
+    exp = {e["id"]: e for e in fx["expected"]}
+    fixture_defects = {2: 8.0}
+    for v in fx["vectors"]:
+        a, b = np.array(v["a"], np.float32), np.array(v["b"], np.float32)
+        assert oracle.l2_sq(a, b) == fixture_defects.get(v["id"], exp[v["id"]]["l2"])
+        assert oracle.inner_product(a, b) == exp[v["id"]]["ip"]
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_golden_search(oracle, name):
+    """The reference's own search results on its own saved index."""
+    f, _, data = golden_case(name)
+    for k, npb in SEARCHES:
+        ids, d, cnt = oracle.ivfpq_search(data["queries"], f["centroids"], f["rotation"], f["codebooks"],
+                                          f["m"], f["list_offsets"], f["ids"], f["codes"], k, npb)
+        assert np.array_equal(cnt, data[f"n_{k}_{npb}"])
+        assert np.array_equal(ids, data[f"ids_{k}_{npb}"]), (name, k, npb)
+        assert np.array_equal(d, data[f"d_{k}_{npb}"]), (name, k, npb)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_golden_add(oracle, name):
+    """Coarse assignment, list order and PQ codes of the reference's add()."""
+    f, model, data = golden_case(name)
+    base = data["base"]
+    a, codes = oracle.ivfpq_add(base, model["centroids"], model["rotation"], model["codebooks"], model["m"])
+    order = np.argsort(a, kind="stable")
+    offs = np.zeros(model["nlist"] + 1, np.uint64)
+    offs[1:] = np.cumsum(np.bincount(a, minlength=model["nlist"]))
+    assert np.array_equal(offs, f["list_offsets"])
+    assert np.array_equal((order * 3 + 7).astype(np.uint64), f["ids"])
+    assert np.array_equal(codes[order], f["codes"])
+
+
+def test_golden_kmeans(oracle):
+    g = dict(np.load(os.path.join(GOLDEN, "kmeans_small.npz")))
+    x = g["x"]
+    c, _ = oracle.kmeanspp_init(x, 48, 42)
+    assert np.array_equal(c, g["kpp"])
+    c, a, it, inertia = oracle.kmeans_elkan(x, 48, 25, 1e-4, 42)
+    assert np.array_equal(c, g["elkan_c"]) and np.array_equal(a, g["elkan_a"])
+    assert it == int(g["elkan_it"]) and inertia == float(g["elkan_inertia"])
+    asg, inert = oracle.lloyd_assign(x, g["kpp"])
+    assert np.array_equal(asg, g["assign"]) and np.float32(inert) == np.float32(g["assign_inertia"])
+    assert np.array_equal(oracle.lloyd_update(x, asg, g["kpp"]), g["update"])
+    assert np.array_equal(oracle.pq_train(x, 4, 8), g["pq_cb"])
+
+
+def test_unit_topk_ties(oracle):
+    # tests/unit/kernels_topk_ties_test.cpp: equal scores go to the smaller index.
+    C = np.array([[1, 0], [-1, 0], [0, 2]], np.float32)
+    idx, _ = oracle.flat_topk(0, np.zeros((1, 2), np.float32), C, 2)
+    assert list(idx[0]) == [0, 1]
+    C = np.array([[1, 0], [1, 0], [0, 1]], np.float32)
+    idx, _ = oracle.flat_topk(1, np.array([[1, 0]], np.float32), C, 2)
+    assert list(idx[0]) == [0, 1]
+
+
+def test_unit_pq_lut_vs_adc(oracle):
+    # tests/unit/pq_lut_tests.cpp: scan distance == manual LUT accumulation.
+    rng = np.random.default_rng(7)
+    train = rng.uniform(-1, 1, (4000, 32)).astype(np.float32)
+    cb = oracle.pq_train(train, 8, 4)
+    data = rng.uniform(-1, 1, (65, 32)).astype(np.float32)
+    codes = oracle.pq_encode(data, cb, 8)
+    q = rng.uniform(-1, 1, 32).astype(np.float32)
+    lut = oracle.pq_lut(q, cb, 8)
+    for i in range(65):
+        manual = np.float32(0)
+        for s in range(8):
+            manual = np.float32(manual + lut[s, codes[i, s]])
+        assert oracle.adc(lut, codes[i]) == manual
+
+
+def test_unit_pq_self_distance(oracle):
+    # tests/unit/pq_fastscan_parity_tests.cpp: ADC to its own code == decode error (1e-5).
+    rng = np.random.default_rng(123456)
+    train = rng.uniform(-1, 1, (4096, 32)).astype(np.float32)
+    cb = oracle.pq_train(train, 8, 6)
+    data = rng.uniform(-1, 1, (65, 32)).astype(np.float32)
+    codes = oracle.pq_encode(data, cb, 8)
+    dec = oracle.pq_decode(codes, cb, 8)
+    for i in range(65):
+        adc = oracle.adc(oracle.pq_lut(data[i], cb, 8), codes[i])
+        exact = float(np.sum((data[i].astype(np.float64) - dec[i]) ** 2))
+        assert abs(adc - exact) <= 1e-5 * max(1.0, exact)
+
+
+def test_oracle_vs_reference_random(oracle, reference):
+    """Fresh random inputs: oracle == reference library, bit for bit."""
+    rng = np.random.default_rng(99)
+    a, b = np.array([0, 0, 1, -1], np.float32), np.array([0, 0, -1, 1], np.float32)
+    assert reference.l2_sq(a, b) == oracle.l2_sq(a, b) == 8.0
+    for n in (1, 5, 8, 13, 16, 100, 768):
+        a, b = rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32)
+        assert oracle.l2_sq(a, b) == reference.l2_sq(a, b)
+        assert oracle.inner_product(a, b) == reference.inner_product(a, b)
+    x = rng.standard_normal((1500, 12)).astype(np.float32)
+    assert np.array_equal(oracle.kmeanspp_init(x, 30, 7)[0], reference.kmeanspp_init(x, 30, 7))
+    e1, e2 = oracle.kmeans_elkan(x, 30, 25, 1e-4, 7), reference.kmeans_elkan(x, 30, 25, 1e-4, 7)
+    assert np.array_equal(e1[0], e2[0]) and np.array_equal(e1[1], e2[1])
+    base = rng.standard_normal((3000, 40)).astype(np.float32)
+    q = rng.standard_normal((17, 40)).astype(np.float32)
+    for op in (0, 1):
+        i1, s1 = oracle.flat_topk(op, q, base, 25)
+        i2, s2 = reference.flat_topk(op, q, base, 25)
+        assert np.array_equal(i1, i2) and np.array_equal(s1, s2)

@@ -1,0 +1,133 @@
+"""ctypes binding of libvesper_c.so (include/vesper.h + include/vesper_b200.h).
+
+The library is built in-tree by vesper_db_b200/build.py.  There is no fallback: if
+the shared library is missing, loading raises instead of silently using anything else.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libvesper_c.so")
+
+VESPER_OK = 0
+VESPER_ERROR_UNKNOWN = 1
+VESPER_ERROR_INVALID_PARAM = 2
+VESPER_ERROR_NOT_TRAINED = 3
+VESPER_ERROR_IO = 4
+VESPER_ERROR_INTERNAL = 5
+
+SEARCH_FAST = 0
+SEARCH_EXACT = 1
+
+# Every symbol the headers in include/ declare.
+EXPORTED = [
+    "vesper_get_last_error", "vesper_version", "vesper_ivfpq_create", "vesper_ivfpq_destroy",
+    "vesper_ivfpq_train", "vesper_ivfpq_add", "vesper_ivfpq_search", "vesper_ivfpq_search_batch",
+    "vesper_ivfpq_is_trained", "vesper_ivfpq_get_dimension", "vesper_ivfpq_get_stats",
+    "vesper_ivfpq_set_metadata_json", "vesper_ivfpq_get_metadata_json", "vesper_ivfpq_save",
+    "vesper_ivfpq_load",
+    "vesper_ivfpq_train_params_ex_init", "vesper_ivfpq_train_ex", "vesper_ivfpq_get_train_report",
+    "vesper_ivfpq_search_batch_ex", "vesper_ivfpq_search_batch_device", "vesper_ivfpq_get_last_timings",
+    "vesper_ivfpq_set_model", "vesper_ivfpq_get_lists", "vesper_b200_device_count",
+    "vesper_ivfpq_train_ex_device", "vesper_ivfpq_add_device",
+]
+
+
+class TrainParams(C.Structure):
+    _fields_ = [("nlist", C.c_uint32), ("m", C.c_uint32), ("nbits", C.c_uint32)]
+
+
+class SearchParams(C.Structure):
+    _fields_ = [("k", C.c_uint32), ("nprobe", C.c_uint32)]
+
+
+class Stats(C.Structure):
+    _fields_ = [("n_vectors", C.c_size_t), ("n_lists", C.c_size_t), ("m", C.c_size_t),
+                ("memory_bytes", C.c_size_t), ("avg_list_size", C.c_float)]
+
+
+class TrainParamsEx(C.Structure):
+    _fields_ = [("struct_size", C.c_size_t), ("nlist", C.c_uint32), ("m", C.c_uint32),
+                ("nbits", C.c_uint32), ("max_iter", C.c_uint32), ("epsilon", C.c_float),
+                ("use_opq", C.c_int), ("opq_iter", C.c_uint32), ("opq_sample_n", C.c_size_t),
+                ("opq_init_pca", C.c_int), ("seed", C.c_uint32), ("verbose", C.c_int)]
+
+
+class TrainReport(C.Structure):
+    _fields_ = [("opq_kept", C.c_int), ("err_unrot", C.c_double), ("err_opq", C.c_double),
+                ("coarse_iterations", C.c_uint32), ("train_time_sec", C.c_float)]
+
+
+class SearchParamsEx(C.Structure):
+    _fields_ = [("struct_size", C.c_size_t), ("k", C.c_uint32), ("nprobe", C.c_uint32),
+                ("mode", C.c_uint32)]
+
+
+class Timings(C.Structure):
+    _fields_ = [("coarse_ms", C.c_float), ("select_ms", C.c_float), ("rotate_ms", C.c_float),
+                ("scan_ms", C.c_float), ("merge_ms", C.c_float), ("total_ms", C.c_float),
+                ("scanned_entries", C.c_uint64)]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Load libvesper_c.so and declare its prototypes (idempotent)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"{path} is missing: build it with `python -m vesper_db_b200.build` "
+                "(the engine has no CPU fallback)")
+        L = C.CDLL(path)
+        vp, st = C.c_void_p, C.c_int
+        f32p, u64p, u32p, u8p = (C.POINTER(C.c_float), C.POINTER(C.c_uint64),
+                                 C.POINTER(C.c_uint32), C.POINTER(C.c_uint8))
+        proto = {
+            "vesper_get_last_error": (C.c_char_p, []),
+            "vesper_version": (C.c_char_p, []),
+            "vesper_ivfpq_create": (st, [C.POINTER(vp)]),
+            "vesper_ivfpq_destroy": (st, [vp]),
+            "vesper_ivfpq_train": (st, [vp, f32p, C.c_size_t, C.c_size_t, C.POINTER(TrainParams)]),
+            "vesper_ivfpq_add": (st, [vp, u64p, f32p, C.c_size_t]),
+            "vesper_ivfpq_search": (st, [vp, f32p, C.POINTER(SearchParams), u64p, f32p]),
+            "vesper_ivfpq_search_batch": (st, [vp, f32p, C.c_size_t, C.POINTER(SearchParams), u64p, f32p]),
+            "vesper_ivfpq_is_trained": (st, [vp, C.POINTER(C.c_int)]),
+            "vesper_ivfpq_get_dimension": (st, [vp, C.POINTER(C.c_size_t)]),
+            "vesper_ivfpq_get_stats": (st, [vp, C.POINTER(Stats)]),
+            "vesper_ivfpq_set_metadata_json": (st, [vp, C.c_char_p]),
+            "vesper_ivfpq_get_metadata_json": (st, [vp, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+            "vesper_ivfpq_save": (st, [vp, C.c_char_p]),
+            "vesper_ivfpq_load": (st, [vp, C.c_char_p]),
+            "vesper_ivfpq_train_params_ex_init": (None, [C.POINTER(TrainParamsEx)]),
+            "vesper_ivfpq_train_ex": (st, [vp, f32p, C.c_size_t, C.c_size_t, C.POINTER(TrainParamsEx)]),
+            "vesper_ivfpq_get_train_report": (st, [vp, C.POINTER(TrainReport)]),
+            "vesper_ivfpq_search_batch_ex": (st, [vp, f32p, C.c_size_t, C.POINTER(SearchParamsEx), u64p,
+                                                  f32p, u32p]),
+            "vesper_ivfpq_search_batch_device": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx), vp, vp,
+                                                      vp]),
+            "vesper_ivfpq_get_last_timings": (st, [vp, C.POINTER(Timings)]),
+            "vesper_ivfpq_set_model": (st, [vp, C.c_size_t, C.c_uint32, C.c_uint32, C.c_uint32, f32p, f32p,
+                                            f32p]),
+            "vesper_ivfpq_get_lists": (st, [vp, u64p, u64p, u8p]),
+            "vesper_b200_device_count": (C.c_int, []),
+            "vesper_ivfpq_train_ex_device": (st, [vp, vp, C.c_size_t, C.c_size_t, C.POINTER(TrainParamsEx)]),
+            "vesper_ivfpq_add_device": (st, [vp, vp, vp, C.c_size_t]),
+        }
+        for name, (res, args) in proto.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+        return L

@@ -1,0 +1,1099 @@
+// Host orchestration of the B200 IVF-PQ index (mirror of the reference's
+// IvfPqIndex::Impl, src/index/ivf_pq.cpp).  All arithmetic on vectors runs in the
+// CUDA kernels declared in kernels*.cuh; this file owns state, chunking, the
+// k-means++ random stream and the file format.
+#include "ivf_pq_gpu.hpp"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <filesystem>
+#include <fstream>
+#include <limits>
+#include <mutex>
+#include <random>
+#include <thread>
+
+#include "kernels.cuh"
+#include "kernels_opq.cuh"
+#include "kernels_train.cuh"
+
+namespace vesper::index {
+
+using core::error;
+using core::error_code;
+using vgpu::DeviceBuffer;
+
+namespace {
+
+constexpr size_t kDistBudget = size_t(512) << 20;  // bytes per distance-matrix chunk
+
+auto fail(error_code c, std::string msg, std::string comp = "ivf_pq") {
+    return std::unexpected(error{c, std::move(msg), std::move(comp)});
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) vgpu::check(cudaSetDevice(dev), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Pinned host staging buffer (grow-only).
+struct Pinned {
+    void* p = nullptr;
+    size_t bytes = 0;
+    ~Pinned() { if (p) cudaFreeHost(p); }
+    template <class T>
+    T* get(size_t n) {
+        const size_t need = n * sizeof(T);
+        if (need > bytes) {
+            if (p) cudaFreeHost(p);
+            vgpu::check(cudaMallocHost(&p, need), "cudaMallocHost");
+            bytes = need;
+        }
+        return static_cast<T*>(p);
+    }
+};
+
+template <class T>
+void h2d(T* d, const T* h, size_t n, cudaStream_t st) {
+    if (n) vgpu::check(cudaMemcpyAsync(d, h, n * sizeof(T), cudaMemcpyHostToDevice, st), "h2d");
+}
+template <class T>
+void d2h(T* h, const T* d, size_t n, cudaStream_t st) {
+    if (n) vgpu::check(cudaMemcpyAsync(h, d, n * sizeof(T), cudaMemcpyDeviceToHost, st), "d2h");
+}
+template <class T>
+void d2d(T* dst, const T* src, size_t n, cudaStream_t st) {
+    if (n) vgpu::check(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyDeviceToDevice, st), "d2d");
+}
+void sync(cudaStream_t st) { vgpu::check(cudaStreamSynchronize(st), "cudaStreamSynchronize"); }
+
+bool env_flag(const char* name) {
+    const char* v = std::getenv(name);
+    return v && v[0] == '1';
+}
+
+}  // namespace
+
+class IvfPqIndex::Impl {
+public:
+    Impl() {
+        vgpu::check(cudaGetDevice(&dev), "cudaGetDevice");
+        vgpu::check(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate");
+        for (auto& e : ev) vgpu::check(cudaEventCreate(&e), "cudaEventCreate");
+    }
+    ~Impl() {
+        if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
+        for (auto& e : ev) if (e) cudaEventDestroy(e);
+    }
+
+    // ------------------------------------------------------------------ state
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[6] = {};
+    mutable std::mutex mu;
+
+    bool trained = false;
+    size_t dim = 0, dsub = 0;
+    IvfPqTrainParams params;
+    uint32_t ksub = 256;
+    bool has_rot = false;
+    std::string metadata_json;
+
+    std::vector<float> h_cent, h_cb, h_rot;
+    std::vector<uint64_t> h_offs;   // [nlist + 1]
+
+    DeviceBuffer<float> d_cent, d_cb, d_rot, d_rotT, d_rc;
+    DeviceBuffer<uint64_t> d_offs, d_ids;
+    DeviceBuffer<uint8_t> d_codes;
+    DeviceBuffer<float> d_vterm;
+    size_t n_vectors = 0;
+
+    double t_assign_ms = 0, t_encode_ms = 0, t_lists_ms = 0;
+    mutable SearchTimings timings;
+
+    // search workspace (grow-only), guarded by mu
+    mutable DeviceBuffer<float> w_q, w_D, w_probe_d, w_rq, w_rres, w_cand_d, w_out_d;
+    mutable DeviceBuffer<uint32_t> w_probe, w_cand_pos, w_cand_n, w_out_n, w_pair_q;
+    mutable DeviceBuffer<uint64_t> w_out_ids;
+    mutable DeviceBuffer<unsigned long long> w_scanned;
+    mutable Pinned pin_a, pin_b, pin_c;
+
+    uint32_t nlist() const { return params.nlist; }
+    uint32_t m() const { return params.m; }
+
+    // ------------------------------------------------------------------ helpers
+    void upload_model() {
+        d_cent.resize(h_cent.size());
+        h2d(d_cent.data(), h_cent.data(), h_cent.size(), st);
+        d_cb.resize(h_cb.size());
+        h2d(d_cb.data(), h_cb.data(), h_cb.size(), st);
+        if (has_rot) {
+            d_rot.resize(dim * dim);
+            h2d(d_rot.data(), h_rot.data(), dim * dim, st);
+            d_rotT.resize(dim * dim);
+            vgpu::launch_transpose(d_rot.data(), (int)dim, d_rotT.data(), st);
+            d_rc.resize(h_cent.size());
+            vgpu::launch_rotate_fast(d_cent.data(), nlist(), (int)dim, d_rot.data(), d_rc.data(), st);
+        } else {
+            d_rot.release();
+            d_rotT.release();
+            d_rc.resize(h_cent.size());
+            d2d(d_rc.data(), d_cent.data(), h_cent.size(), st);
+        }
+    }
+
+    void reset_lists() {
+        h_offs.assign(nlist() + 1, 0);
+        d_offs.resize(nlist() + 1);
+        h2d(d_offs.data(), h_offs.data(), h_offs.size(), st);
+        d_ids.release();
+        d_codes.release();
+        d_vterm.release();
+        n_vectors = 0;
+    }
+
+    void recompute_vterms() {
+        d_vterm.resize(std::max<size_t>(n_vectors, 1));
+        vgpu::launch_vector_terms(d_rc.data(), (int)nlist(), (int)dim, d_cb.data(), (int)m(), (int)ksub,
+                                  (int)dsub, d_offs.data(), d_codes.data(), (long long)n_vectors,
+                                  d_vterm.data(), st);
+    }
+
+    // Brute-force assignment with chunked distance tiles (the reference's brute
+    // branch, src/index/ivf_pq.cpp:3252-3265).  keep != nullptr -> Elkan tie rule.
+    void assign_rows(const float* d_x, size_t n, int d, const float* d_c, uint32_t k, uint32_t* d_assign,
+                     float* d_mind, bool keep, DeviceBuffer<float>& D) const {
+        const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * k)));
+        D.reserve(rows * k);
+        for (size_t r0 = 0; r0 < n; r0 += rows) {
+            const size_t nr = std::min(rows, n - r0);
+            vgpu::launch_l2_dist(d_x + r0 * (size_t)d, (long long)nr, d_c, (int)k, d, D.data(), (long long)k, st);
+            vgpu::launch_row_argmin(D.data(), (long long)nr, (int)k, (long long)k,
+                                    keep ? d_assign + r0 : nullptr, d_assign + r0,
+                                    d_mind ? d_mind + r0 : nullptr, st);
+        }
+    }
+
+    // Sum of a device float array in index order, in fp64 (host).
+    double ordered_sum(const float* d, size_t n) const {
+        float* h = pin_a.get<float>(n);
+        d2h(h, d, n, st);
+        sync(st);
+        double t = 0.0;
+        for (size_t i = 0; i < n; ++i) t += h[i];
+        return t;
+    }
+
+    // ------------------------------------------------------------------ k-means
+    // k-means++ (src/index/kmeans.cpp:45-89): the D^2 vector comes from the GPU, the
+    // cumulative sum, the draws and lower_bound run on the host with the same
+    // std::mt19937 / libstdc++ distributions as the reference.
+    void kmeanspp(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c) {
+        std::mt19937 gen(seed);
+        std::uniform_int_distribution<size_t> first(0, n - 1);
+        size_t idx = first(gen);
+        d2d(d_c, d_x + idx * d, (size_t)d, st);
+        DeviceBuffer<float> mind(n);
+        vgpu::launch_fill(mind.data(), (long long)n, std::numeric_limits<float>::max(), st);
+        float* h = pin_b.get<float>(n);
+        std::vector<double> cum(n);
+        for (uint32_t c = 1; c < k; ++c) {
+            vgpu::launch_kpp_update(d_x, (long long)n, d, d_c + (size_t)(c - 1) * d, mind.data(), st);
+            d2h(h, mind.data(), n, st);
+            sync(st);
+            cum[0] = h[0];
+            for (size_t i = 1; i < n; ++i) cum[i] = cum[i - 1] + h[i];
+            std::uniform_real_distribution<double> sd(0.0, cum.back());
+            const double target = sd(gen);
+            idx = (size_t)(std::lower_bound(cum.begin(), cum.end(), target) - cum.begin());
+            d2d(d_c + (size_t)c * d, d_x + idx * d, (size_t)d, st);
+        }
+    }
+
+    struct KmOut { uint32_t iterations; float inertia; };
+
+    // KmeansElkan::cluster (src/index/kmeans_elkan.cpp:293-430) semantics: exact
+    // E-step (Elkan prunes only provably-farther centroids, so its assignment is the
+    // strict-< arg-min that keeps the current centroid on a tie), convergence test on
+    // the fp64-summed inertia before the M-step, Kahan M-step in point order.
+    KmOut kmeans(const float* d_x, size_t n, int d, uint32_t k, uint32_t max_iter, float eps,
+                 uint32_t seed, float* d_c, uint32_t* d_assign) {
+        kmeanspp(d_x, n, d, k, seed, d_c);
+        DeviceBuffer<float> mind(n), D;
+        DeviceBuffer<uint32_t> order(n), seg(k + 1);
+        vgpu::GroupWork gw;
+        assign_rows(d_x, n, d, d_c, k, d_assign, mind.data(), false, D);
+        float prev = std::numeric_limits<float>::max();
+        uint32_t it = 0;
+        for (; it < max_iter; ++it) {
+            if (it > 0) assign_rows(d_x, n, d, d_c, k, d_assign, mind.data(), true, D);
+            const float inertia = (float)ordered_sum(mind.data(), n);
+            const float change = std::fabs(prev - inertia) / (prev + 1e-10f);
+            if (change < eps) break;
+            prev = inertia;
+            vgpu::group_by_key(d_assign, (long long)n, (int)k, order.data(), seg.data(), gw, st);
+            vgpu::launch_segment_mean(d_x, d, order.data(), seg.data(), (int)k, 1, d_c, st);
+        }
+        sync(st);
+        return {it, prev};
+    }
+
+    // FastScanPq::train (src/index/pq_fastscan.cpp:15-76): one k-means per sub-space,
+    // all sub-spaces advanced together on the GPU.  x: [n x dim] device rows.
+    void pq_train(const float* d_x, size_t n, float* d_out_cb) {
+        const int M = (int)m(), DS = (int)dsub, K = (int)ksub, D = (int)dim;
+        vgpu::check(cudaMemsetAsync(d_out_cb, 0, sizeof(float) * (size_t)M * K * DS, st), "memset cb");
+        if (n < (size_t)K) return;  // the reference's sub-k-means fails; codebooks stay 0
+        std::vector<std::mt19937> gens;
+        for (int s = 0; s < M; ++s) gens.emplace_back(42u + (uint32_t)s);
+        std::vector<uint32_t> pick(M);
+        DeviceBuffer<uint32_t> d_pick(M);
+        DeviceBuffer<float> picks((size_t)M * DS), mind((size_t)M * n);
+        for (int s = 0; s < M; ++s) {
+            std::uniform_int_distribution<size_t> first(0, n - 1);
+            pick[s] = (uint32_t)first(gens[s]);
+        }
+        h2d(d_pick.data(), pick.data(), M, st);
+        vgpu::launch_pq_gather_picks(d_x, D, M, DS, d_pick.data(), 0, K, picks.data(), d_out_cb, st);
+        vgpu::launch_fill(mind.data(), (long long)M * n, std::numeric_limits<float>::max(), st);
+        float* h = pin_b.get<float>((size_t)M * n);
+        const unsigned nthreads = std::max(1u, std::min<unsigned>(std::thread::hardware_concurrency(), (unsigned)M));
+        for (int c = 1; c < K; ++c) {
+            vgpu::launch_pq_kpp_update(d_x, (long long)n, D, M, DS, picks.data(), mind.data(), st);
+            d2h(h, mind.data(), (size_t)M * n, st);
+            sync(st);
+            auto work = [&](unsigned t) {
+                std::vector<double> cum(n);
+                for (int s = (int)t; s < M; s += (int)nthreads) {
+                    const float* hs = h + (size_t)s * n;
+                    cum[0] = hs[0];
+                    for (size_t i = 1; i < n; ++i) cum[i] = cum[i - 1] + hs[i];
+                    std::uniform_real_distribution<double> sd(0.0, cum.back());
+                    const double target = sd(gens[s]);
+                    pick[s] = (uint32_t)(std::lower_bound(cum.begin(), cum.end(), target) - cum.begin());
+                }
+            };
+            std::vector<std::thread> pool;
+            for (unsigned t = 1; t < nthreads; ++t) pool.emplace_back(work, t);
+            work(0);
+            for (auto& th : pool) th.join();
+            h2d(d_pick.data(), pick.data(), M, st);
+            vgpu::launch_pq_gather_picks(d_x, D, M, DS, d_pick.data(), c, K, picks.data(), d_out_cb, st);
+        }
+        // Elkan iterations per sub-space.
+        DeviceBuffer<uint32_t> codes((size_t)M * n), keys((size_t)M * n), order((size_t)M * n),
+            seg((size_t)M * K + 1);
+        DeviceBuffer<int> d_active(M);
+        std::vector<int> active(M, 1);
+        std::vector<float> prev(M, std::numeric_limits<float>::max());
+        vgpu::GroupWork gw;
+        h2d(d_active.data(), active.data(), M, st);
+        vgpu::launch_pq_assign(d_x, (long long)n, D, M, K, DS, d_out_cb, codes.data(), mind.data(), 0,
+                               nullptr, st);
+        for (uint32_t it = 0; it < 25; ++it) {
+            if (it > 0)
+                vgpu::launch_pq_assign(d_x, (long long)n, D, M, K, DS, d_out_cb, codes.data(), mind.data(),
+                                       1, d_active.data(), st);
+            d2h(h, mind.data(), (size_t)M * n, st);
+            sync(st);
+            bool any = false;
+            for (int s = 0; s < M; ++s) {
+                if (!active[s]) continue;
+                double t = 0.0;
+                const float* hs = h + (size_t)s * n;
+                for (size_t i = 0; i < n; ++i) t += hs[i];
+                const float inertia = (float)t;
+                const float change = std::fabs(prev[s] - inertia) / (prev[s] + 1e-10f);
+                if (change < 1e-4f) { active[s] = 0; continue; }
+                prev[s] = inertia;
+                any = true;
+            }
+            if (!any) break;
+            h2d(d_active.data(), active.data(), M, st);
+            vgpu::launch_pq_keys(codes.data(), (long long)n, M, K, keys.data(), st);
+            vgpu::group_by_key(keys.data(), (long long)M * n, M * K, order.data(), seg.data(), gw, st);
+            vgpu::launch_pq_segment_mean(d_x, (long long)n, D, M, DS, K, order.data(), seg.data(),
+                                         d_active.data(), d_out_cb, st);
+        }
+        sync(st);
+    }
+
+    // Mean squared reconstruction error (compute_error lambda, ivf_pq.cpp:2468-2490):
+    // encode -> decode (-> R^T) -> l2 to the original residual, fp64 mean.
+    double recon_error(const float* d_enc_in, const float* d_res, size_t n, const float* d_cbk,
+                       const float* d_RT) {
+        DeviceBuffer<uint8_t> codes(n * m());
+        DeviceBuffer<float> dec(n * dim), back, l2(n);
+        vgpu::launch_pq_encode(d_enc_in, (long long)n, (int)m(), (int)ksub, (int)dsub, d_cbk, codes.data(), st);
+        vgpu::launch_pq_decode(codes.data(), (long long)n, (int)m(), (int)ksub, (int)dsub, d_cbk, dec.data(), st);
+        const float* cmp = dec.data();
+        if (d_RT) {
+            back.resize(n * dim);
+            vgpu::launch_residual_rotate(dec.data(), nullptr, nullptr, nullptr, (long long)n, (int)dim, d_RT,
+                                         back.data(), st);
+            cmp = back.data();
+        }
+        vgpu::launch_row_l2(cmp, d_res, (long long)n, (int)dim, l2.data(), st);
+        return ordered_sum(l2.data(), n) / (double)n;
+    }
+
+    // learn_opq_rotation (src/index/ivf_pq.cpp:2769-2945) on device residual rows.
+    std::expected<void, error> learn_opq_rotation(const float* d_x, size_t n) {
+        if (n < dim * 2)
+            return fail(error_code::precondition_failed, "Not enough data for OPQ rotation learning");
+        const int d = (int)dim;
+        DeviceBuffer<double> mean(dim), cov(dim * dim), E(dim * dim), work(3 * dim + 4);
+        vgpu::launch_col_mean(d_x, (long long)n, d, mean.data(), st);
+        vgpu::launch_cross_fp64(d_x, d_x, (long long)n, d, mean.data(), mean.data(), cov.data(), st);
+        vgpu::launch_daxpby(cov.data(), cov.data(), (long long)dim * dim, 0.0, 1.0 / (double)(n - 1), st);
+        vgpu::power_iteration_pca(cov.data(), d, 100, 1e-6, E.data(), work.data(), st);
+        std::vector<double> hE(dim * dim);
+        d2h(hE.data(), E.data(), dim * dim, st);
+        sync(st);
+        h_rot.assign(dim * dim, 0.0f);
+        for (size_t i = 0; i < dim * dim; ++i) h_rot[i] = (float)hE[i];
+        // Orthogonality check with identity fallback (:2924-2942).
+        bool bad = false;
+        for (size_t i = 0; i < dim && !bad; ++i)
+            for (size_t j = i + 1; j < dim; ++j) {
+                double dot = 0.0;
+                for (size_t k = 0; k < dim; ++k) dot += h_rot[i * dim + k] * h_rot[j * dim + k];
+                if (std::abs(dot) > 0.01) { bad = true; break; }
+            }
+        if (bad) {
+            std::fill(h_rot.begin(), h_rot.end(), 0.0f);
+            for (size_t k = 0; k < dim; ++k) h_rot[k * dim + k] = 1.0f;
+        }
+        return {};
+    }
+
+    // Orthogonal polar factor of C (d x d, fp64, device) by Newton-Schulz; result in
+    // float R (host).
+    std::vector<float> polar_factor(DeviceBuffer<double>& C) {
+        const int d = (int)dim;
+        std::vector<double> hC(dim * dim);
+        d2h(hC.data(), C.data(), dim * dim, st);
+        sync(st);
+        double fro = 0.0;
+        for (double v : hC) fro += v * v;
+        fro = std::sqrt(fro);
+        std::vector<float> R(dim * dim, 0.0f);
+        if (!(fro > 0.0)) {
+            for (size_t k = 0; k < dim; ++k) R[k * dim + k] = 1.0f;
+            return R;
+        }
+        DeviceBuffer<double> X(dim * dim), T(dim * dim), Y(dim * dim);
+        d2d(X.data(), C.data(), dim * dim, st);
+        vgpu::launch_daxpby(X.data(), X.data(), (long long)dim * dim, 0.0, 1.0 / fro, st);
+        for (int it = 0; it < 80; ++it) {
+            vgpu::launch_dgemm(X.data(), X.data(), T.data(), d, 1, 0, 1.0, 0.0, st);   // T = X^T X
+            d2d(Y.data(), X.data(), dim * dim, st);
+            vgpu::launch_dgemm(X.data(), T.data(), Y.data(), d, 0, 0, -0.5, 1.5, st);  // Y = 1.5X - 0.5 X T
+            std::swap(X, Y);
+        }
+        std::vector<double> hX(dim * dim);
+        d2h(hX.data(), X.data(), dim * dim, st);
+        sync(st);
+        for (size_t i = 0; i < dim * dim; ++i) R[i] = (float)hX[i];
+        return R;
+    }
+
+    std::expected<IvfPqTrainStats, error> train(const float* data, size_t dim_, size_t n,
+                                                const IvfPqTrainParams& p, bool on_device) {
+        if (n < p.nlist)
+            return fail(error_code::precondition_failed, "Not enough training data for nlist centroids");
+        if (p.m == 0 || dim_ % p.m != 0)
+            return fail(error_code::precondition_failed, "Dimension must be divisible by number of subquantizers");
+        if (p.nbits == 0 || p.nbits > 8)
+            return fail(error_code::precondition_failed, "nbits must be in [1, 8] (codes are stored as bytes)");
+        if (p.nlist == 0)
+            return fail(error_code::precondition_failed, "nlist must be > 0");
+        const auto t0 = std::chrono::steady_clock::now();
+        trained = false;
+        params = p;
+        dim = dim_;
+        dsub = dim / p.m;
+        ksub = 1u << p.nbits;
+        has_rot = false;
+        h_rot.clear();
+        if (params.nlist < 1024 && params.use_centroid_ann) params.use_centroid_ann = false;
+
+        DeviceBuffer<float> x_own;
+        const float* xp = data;
+        if (!on_device) {
+            x_own.resize(n * dim);
+            h2d(x_own.data(), data, n * dim, st);
+            xp = x_own.data();
+        }
+        d_cent.resize((size_t)nlist() * dim);
+        DeviceBuffer<uint32_t> assign(n);
+        IvfPqTrainStats stats;
+        // Step 1: coarse quantizer (train_coarse_quantizer, :561-671).
+        auto km = kmeans(xp, n, (int)dim, nlist(), p.max_iter, p.epsilon, p.seed, d_cent.data(),
+                         assign.data());
+        stats.coarse_iterations = km.iterations;
+        h_cent.resize((size_t)nlist() * dim);
+        d2h(h_cent.data(), d_cent.data(), h_cent.size(), st);
+
+        // Residuals of the training data w.r.t. the nearest centroid (:477-494, :2414-2432).
+        DeviceBuffer<float> D, res(n * dim);
+        assign_rows(xp, n, (int)dim, d_cent.data(), nlist(), assign.data(), nullptr, false, D);
+        vgpu::launch_residual_rotate(xp, nullptr, d_cent.data(), assign.data(), (long long)n, (int)dim,
+                                     nullptr, res.data(), st);
+        x_own.release();
+        D.release();
+
+        // Step 2: OPQ PCA initialisation (:457-519).
+        if (p.use_opq && p.opq_init == OpqInit::PCA) {
+            const size_t cap = p.opq_sample_n > 0 ? p.opq_sample_n : 50000;
+            const size_t n_pca = std::min(n, cap);
+            if (n_pca == n) {
+                if (auto r = learn_opq_rotation(res.data(), n); !r) return std::unexpected(r.error());
+            } else {
+                std::vector<uint32_t> idx(n_pca);
+                const double stride = (double)n / (double)n_pca;
+                for (size_t i = 0; i < n_pca; ++i) {
+                    size_t j = (size_t)(i * stride);
+                    if (j >= n) j = n - 1;
+                    idx[i] = (uint32_t)j;
+                }
+                DeviceBuffer<uint32_t> d_idx(n_pca);
+                DeviceBuffer<float> samp(n_pca * dim);
+                h2d(d_idx.data(), idx.data(), n_pca, st);
+                vgpu::launch_gather_rows(res.data(), (int)dim, d_idx.data(), (long long)n_pca, samp.data(), st);
+                if (auto r = learn_opq_rotation(samp.data(), n_pca); !r) return std::unexpected(r.error());
+            }
+        }
+
+        // Step 3: product quantizer (+ OPQ alternation) (:2398-2767).
+        d_cb.resize((size_t)m() * ksub * dsub);
+        DeviceBuffer<float> cb_unrot((size_t)m() * ksub * dsub);
+        pq_train(res.data(), n, cb_unrot.data());
+        const double err_unrot = recon_error(res.data(), res.data(), n, cb_unrot.data(), nullptr);
+        stats.err_unrot = err_unrot;
+        double err_best = std::numeric_limits<double>::infinity();
+        DeviceBuffer<float> cb_opq;
+        std::vector<float> R_best;
+        if (p.use_opq) {
+            if (h_rot.empty()) {
+                h_rot.assign(dim * dim, 0.0f);
+                for (size_t k = 0; k < dim; ++k) h_rot[k * dim + k] = 1.0f;
+            }
+            const uint32_t iters = std::max<uint32_t>(1, std::min<uint32_t>(p.opq_iter, 3));
+            const size_t cap = p.opq_sample_n > 0 ? p.opq_sample_n : 20000;
+            const size_t n_opq = std::min(n, cap);
+            DeviceBuffer<float> R(dim * dim), RT(dim * dim), rot(n_opq * dim), cbt((size_t)m() * ksub * dsub),
+                Y(n_opq * dim), Yb(n_opq * dim), l2(n_opq);
+            DeviceBuffer<uint8_t> codes(n_opq * m());
+            DeviceBuffer<double> C(dim * dim);
+            const auto topq = std::chrono::steady_clock::now();
+            double prev_err = std::numeric_limits<double>::infinity();
+            uint32_t stall = 0;
+            for (uint32_t it = 0; it < iters; ++it) {
+                h2d(R.data(), h_rot.data(), dim * dim, st);
+                vgpu::launch_transpose(R.data(), (int)dim, RT.data(), st);
+                vgpu::launch_residual_rotate(res.data(), nullptr, nullptr, nullptr, (long long)n_opq, (int)dim,
+                                             R.data(), rot.data(), st);
+                pq_train(rot.data(), n_opq, cbt.data());
+                vgpu::launch_pq_encode(rot.data(), (long long)n_opq, (int)m(), (int)ksub, (int)dsub, cbt.data(),
+                                       codes.data(), st);
+                vgpu::launch_pq_decode(codes.data(), (long long)n_opq, (int)m(), (int)ksub, (int)dsub, cbt.data(),
+                                       Y.data(), st);
+                vgpu::launch_residual_rotate(Y.data(), nullptr, nullptr, nullptr, (long long)n_opq, (int)dim,
+                                             RT.data(), Yb.data(), st);
+                vgpu::launch_row_l2(Yb.data(), res.data(), (long long)n_opq, (int)dim, l2.data(), st);
+                const double err_it = ordered_sum(l2.data(), n_opq) / (double)n_opq;
+                stats.errors.push_back((float)err_it);
+                if (err_it < err_best) { err_best = err_it; R_best = h_rot; }
+                if (std::isfinite(prev_err)) {
+                    const double denom = std::max(prev_err, 1e-12);
+                    if ((prev_err - err_it) / denom < 1e-4) ++stall; else stall = 0;
+                }
+                prev_err = err_it;
+                if (stall >= 2) break;
+                const auto el = std::chrono::duration_cast<std::chrono::milliseconds>(
+                                    std::chrono::steady_clock::now() - topq).count();
+                if (el > 120000) break;
+                // Procrustes on the sample: C = X^T Y / n, R = polar(C).
+                vgpu::launch_cross_fp64(res.data(), Y.data(), (long long)n_opq, (int)dim, nullptr, nullptr,
+                                        C.data(), st);
+                vgpu::launch_daxpby(C.data(), C.data(), (long long)dim * dim, 0.0, 1.0 / (double)n_opq, st);
+                h_rot = polar_factor(C);
+            }
+            if (!R_best.empty()) h_rot = R_best;
+            if (err_best < std::numeric_limits<double>::infinity()) {
+                DeviceBuffer<float> rot_full(n * dim);
+                h2d(R.data(), h_rot.data(), dim * dim, st);
+                vgpu::launch_residual_rotate(res.data(), nullptr, nullptr, nullptr, (long long)n, (int)dim,
+                                             R.data(), rot_full.data(), st);
+                cb_opq.resize((size_t)m() * ksub * dsub);
+                pq_train(rot_full.data(), n, cb_opq.data());
+            }
+        }
+        stats.err_opq = err_best;
+        const bool force = env_flag("VESPER_IVFPQ_FORCE_OPQ");
+        if ((force && p.use_opq && !h_rot.empty() && cb_opq.size()) || err_best < err_unrot) {
+            d2d(d_cb.data(), cb_opq.data(), d_cb.size(), st);
+            has_rot = true;
+        } else {
+            d2d(d_cb.data(), cb_unrot.data(), d_cb.size(), st);
+            h_rot.clear();
+            has_rot = false;
+        }
+        stats.opq_kept = has_rot;
+        h_cb.resize(d_cb.size());
+        d2h(h_cb.data(), d_cb.data(), h_cb.size(), st);
+        sync(st);
+        upload_model();
+        reset_lists();
+        sync(st);
+        trained = true;
+        stats.iterations = 25;
+        stats.train_time_sec = std::chrono::duration<float>(std::chrono::steady_clock::now() - t0).count();
+        return stats;
+    }
+
+    // ------------------------------------------------------------------ add
+    std::expected<void, error> add(const uint64_t* ids, const float* data, size_t n, bool on_device) {
+        if (!trained) return fail(error_code::precondition_failed, "Index must be trained before adding vectors");
+        if (n == 0) return {};
+        const auto ta = std::chrono::steady_clock::now();
+        const size_t M = m();
+        DeviceBuffer<uint32_t> assign(n);
+        DeviceBuffer<uint8_t> new_codes(n * M);
+        {
+            const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * std::max<size_t>(nlist(), dim))));
+            DeviceBuffer<float> x(on_device ? 0 : rows * dim), res(rows * dim), D;
+            for (size_t r0 = 0; r0 < n; r0 += rows) {
+                const size_t nr = std::min(rows, n - r0);
+                const float* xr = data + r0 * dim;
+                if (!on_device) {
+                    h2d(x.data(), xr, nr * dim, st);
+                    xr = x.data();
+                }
+                assign_rows(xr, nr, (int)dim, d_cent.data(), nlist(), assign.data() + r0, nullptr, false, D);
+                vgpu::launch_residual_rotate(xr, nullptr, d_cent.data(), assign.data() + r0, (long long)nr,
+                                             (int)dim, has_rot ? d_rot.data() : nullptr, res.data(), st);
+                vgpu::launch_pq_encode(res.data(), (long long)nr, (int)M, (int)ksub, (int)dsub, d_cb.data(),
+                                       new_codes.data() + r0 * M, st);
+            }
+        }
+        sync(st);
+        const auto tb = std::chrono::steady_clock::now();
+        // Append to the lists in input order (:3410-3427): stable destinations on host.
+        std::vector<uint32_t> ha(n);
+        d2h(ha.data(), assign.data(), n, st);
+        sync(st);
+        const uint32_t L = nlist();
+        std::vector<uint64_t> cnt(L, 0);
+        for (size_t i = 0; i < n; ++i) cnt[ha[i]]++;
+        std::vector<uint64_t> new_offs(L + 1, 0);
+        for (uint32_t l = 0; l < L; ++l) new_offs[l + 1] = new_offs[l] + (h_offs[l + 1] - h_offs[l]) + cnt[l];
+        std::vector<uint64_t> cursor(L);
+        for (uint32_t l = 0; l < L; ++l) cursor[l] = new_offs[l] + (h_offs[l + 1] - h_offs[l]);
+        std::vector<uint64_t> dest(n);
+        for (size_t i = 0; i < n; ++i) dest[i] = cursor[ha[i]]++;
+        const size_t total = n_vectors + n;
+        DeviceBuffer<uint8_t> codes(total * M);
+        DeviceBuffer<uint64_t> allids(total), d_new_offs(L + 1), d_dest(n), d_newids(n);
+        h2d(d_new_offs.data(), new_offs.data(), L + 1, st);
+        h2d(d_dest.data(), dest.data(), n, st);
+        if (on_device) d2d(d_newids.data(), ids, n, st); else h2d(d_newids.data(), ids, n, st);
+        if (n_vectors)
+            vgpu::launch_csr_move(d_codes.data(), d_ids.data(), d_offs.data(), d_new_offs.data(), (int)L, (int)M,
+                                  codes.data(), allids.data(), st);
+        vgpu::launch_csr_scatter(new_codes.data(), d_newids.data(), d_dest.data(), (long long)n, (int)M,
+                                 codes.data(), allids.data(), st);
+        d_codes = std::move(codes);
+        d_ids = std::move(allids);
+        d_offs = std::move(d_new_offs);
+        h_offs = std::move(new_offs);
+        n_vectors = total;
+        recompute_vterms();
+        sync(st);
+        const auto tc = std::chrono::steady_clock::now();
+        if (params.timings_enabled || params.verbose || env_flag("VESPER_TIMING")) {
+            t_assign_ms += std::chrono::duration<double, std::milli>(tb - ta).count();
+            t_lists_ms += std::chrono::duration<double, std::milli>(tc - tb).count();
+        }
+        return {};
+    }
+
+    // ------------------------------------------------------------------ search
+    std::expected<void, error> search_flat(const float* queries, size_t nq, const IvfPqSearchParams& sp,
+                                           uint64_t* out_ids, float* out_d, uint32_t* out_n,
+                                           bool on_device) const {
+        if (!trained) return fail(error_code::precondition_failed, "Index must be trained before searching");
+        if (sp.k == 0) return fail(error_code::invalid_argument, "k must be > 0");
+        if (sp.k > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "k above 1024 is not supported by the GPU path");
+        if (nq == 0) return {};
+        uint32_t np = std::min(sp.nprobe, nlist());
+        if (env_flag("VESPER_IVFPQ_PROBE_ALL")) np = nlist();
+        if (np == 0) {  // nothing probed: every result is padding
+            if (on_device) {
+                vgpu::check(cudaMemsetAsync(out_ids, 0, nq * sp.k * sizeof(uint64_t), st), "memset");
+                vgpu::check(cudaMemsetAsync(out_d, 0, nq * sp.k * sizeof(float), st), "memset");
+                if (out_n) vgpu::check(cudaMemsetAsync(out_n, 0, nq * sizeof(uint32_t), st), "memset");
+                sync(st);
+            } else {
+                std::fill(out_ids, out_ids + nq * sp.k, 0);
+                std::fill(out_d, out_d + nq * sp.k, 0.0f);
+                if (out_n) std::fill(out_n, out_n + nq, 0u);
+            }
+            return {};
+        }
+        if (np > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "nprobe above 1024 is not supported by the GPU path");
+        std::lock_guard<std::mutex> lock(mu);
+        const uint32_t k = sp.k;
+        const bool exact = sp.mode == SearchMode::Exact;
+        // Chunk queries so the coarse distance tile and the exact-path buffers stay bounded.
+        size_t qc = std::max<size_t>(1, kDistBudget / (sizeof(float) * (size_t)nlist()));
+        if (exact && has_rot) qc = std::min(qc, std::max<size_t>(1, kDistBudget / (sizeof(float) * np * dim)));
+        qc = std::min(qc, nq);
+        w_D.reserve(qc * nlist());
+        w_probe.reserve(qc * np);
+        w_probe_d.reserve(qc * np);
+        if (!on_device) {
+            w_q.reserve(qc * dim);
+            w_out_ids.reserve(qc * k);
+            w_out_d.reserve(qc * k);
+            w_out_n.reserve(qc);
+        }
+        if (exact) {
+            w_cand_d.reserve(qc * np * k);
+            w_cand_pos.reserve(qc * np * k);
+            w_cand_n.reserve(qc * np);
+            if (has_rot) {
+                w_rres.reserve(qc * np * dim);
+                w_pair_q.reserve(qc * np);
+            }
+        } else {
+            w_rq.reserve(qc * dim);
+        }
+        SearchTimings tm;
+        w_scanned.reserve(1);
+        vgpu::check(cudaMemsetAsync(w_scanned.data(), 0, sizeof(unsigned long long), st), "memset");
+        for (size_t q0 = 0; q0 < nq; q0 += qc) {
+            const size_t nc = std::min(qc, nq - q0);
+            const float* dq;
+            uint64_t* oid;
+            float* od;
+            uint32_t* on;
+            if (on_device) {
+                dq = queries + q0 * dim;
+                oid = out_ids + q0 * k;
+                od = out_d + q0 * k;
+                on = out_n ? out_n + q0 : nullptr;
+            } else {
+                h2d(w_q.data(), queries + q0 * dim, nc * dim, st);
+                dq = w_q.data();
+                oid = w_out_ids.data();
+                od = w_out_d.data();
+                on = w_out_n.data();
+            }
+            cudaEventRecord(ev[0], st);
+            vgpu::launch_l2_dist(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, w_D.data(),
+                                 (long long)nlist(), st);
+            cudaEventRecord(ev[1], st);
+            vgpu::launch_row_topk(w_D.data(), (long long)nc, (int)nlist(), (long long)nlist(), (int)np,
+                                  w_probe.data(), w_probe_d.data(), st);
+            cudaEventRecord(ev[2], st);
+            vgpu::launch_probe_sizes(w_probe.data(), (long long)(nc * np), d_offs.data(), w_scanned.data(), st);
+            if (exact) {
+                const float* rres = nullptr;
+                if (has_rot) {
+                    std::vector<uint32_t> pq(nc * np);
+                    for (size_t i = 0; i < nc * np; ++i) pq[i] = (uint32_t)(i / np);
+                    h2d(w_pair_q.data(), pq.data(), pq.size(), st);
+                    vgpu::launch_residual_rotate(dq, w_pair_q.data(), d_cent.data(), w_probe.data(),
+                                                 (long long)(nc * np), (int)dim, d_rot.data(), w_rres.data(), st);
+                    rres = w_rres.data();
+                }
+                cudaEventRecord(ev[3], st);
+                vgpu::launch_scan_exact(dq, (long long)nc, (int)dim, d_cent.data(), rres, w_probe.data(), (int)np,
+                                        d_cb.data(), (int)m(), (int)ksub, (int)dsub, d_offs.data(), d_codes.data(),
+                                        (int)k, w_cand_d.data(), w_cand_pos.data(), w_cand_n.data(), st);
+                cudaEventRecord(ev[4], st);
+                vgpu::launch_merge(w_cand_d.data(), w_cand_pos.data(), w_cand_n.data(), (long long)nc, (int)np,
+                                   (int)k, w_probe.data(), d_offs.data(), d_ids.data(), oid, od, on, st);
+            } else {
+                const float* rq = dq;
+                if (has_rot) {
+                    vgpu::launch_rotate_fast(dq, (long long)nc, (int)dim, d_rot.data(), w_rq.data(), st);
+                    rq = w_rq.data();
+                }
+                cudaEventRecord(ev[3], st);
+                vgpu::launch_scan_fast(rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
+                                       has_rot ? d_rc.data() : nullptr, (int)np,
+                                       d_cb.data(), (int)m(), (int)ksub, (int)dsub, d_offs.data(), d_codes.data(),
+                                       d_vterm.data(), d_ids.data(), (int)k, oid, od, on, st);
+                cudaEventRecord(ev[4], st);
+            }
+            cudaEventRecord(ev[5], st);
+            if (!on_device) {
+                d2h(out_ids + q0 * k, oid, nc * k, st);
+                d2h(out_d + q0 * k, od, nc * k, st);
+                if (out_n) d2h(out_n + q0, on, nc, st);
+            }
+            sync(st);
+            float a = 0;
+            cudaEventElapsedTime(&a, ev[0], ev[1]); tm.coarse_ms += a;
+            cudaEventElapsedTime(&a, ev[1], ev[2]); tm.select_ms += a;
+            cudaEventElapsedTime(&a, ev[2], ev[3]); tm.rotate_ms += a;
+            cudaEventElapsedTime(&a, ev[3], ev[4]); tm.scan_ms += a;
+            cudaEventElapsedTime(&a, ev[4], ev[5]); tm.merge_ms += a;
+            cudaEventElapsedTime(&a, ev[0], ev[5]); tm.total_ms += a;
+        }
+        unsigned long long scanned = 0;
+        d2h(&scanned, w_scanned.data(), 1, st);
+        sync(st);
+        tm.scanned_entries = scanned;
+        timings = tm;
+        return {};
+    }
+};
+
+// ====================================================================== public API
+IvfPqIndex::IvfPqIndex() : impl_(std::make_unique<Impl>()) {}
+IvfPqIndex::~IvfPqIndex() = default;
+IvfPqIndex::IvfPqIndex(IvfPqIndex&&) noexcept = default;
+IvfPqIndex& IvfPqIndex::operator=(IvfPqIndex&&) noexcept = default;
+
+auto IvfPqIndex::train(const float* data, std::size_t dim, std::size_t n, const IvfPqTrainParams& params)
+    -> std::expected<IvfPqTrainStats, core::error> {
+    return train_device(data, dim, n, params, false);
+}
+
+auto IvfPqIndex::train_device(const float* data, std::size_t dim, std::size_t n,
+                              const IvfPqTrainParams& params, bool on_device)
+    -> std::expected<IvfPqTrainStats, core::error> {
+    DeviceGuard g(impl_->dev);
+    try {
+        std::lock_guard<std::mutex> lock(impl_->mu);
+        return impl_->train(data, dim, n, params, on_device);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    } catch (const std::bad_alloc&) {
+        return fail(error_code::out_of_memory, "bad_alloc in train");
+    }
+}
+
+auto IvfPqIndex::add(const std::uint64_t* ids, const float* data, std::size_t n)
+    -> std::expected<void, core::error> {
+    return add_device(ids, data, n, false);
+}
+
+auto IvfPqIndex::add_device(const std::uint64_t* ids, const float* data, std::size_t n, bool on_device)
+    -> std::expected<void, core::error> {
+    DeviceGuard g(impl_->dev);
+    try {
+        std::lock_guard<std::mutex> lock(impl_->mu);
+        return impl_->add(ids, data, n, on_device);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    } catch (const std::bad_alloc&) {
+        return fail(error_code::out_of_memory, "bad_alloc in add() residuals/rotation");
+    }
+}
+
+auto IvfPqIndex::search_batch_flat(const float* queries, std::size_t n_queries,
+                                   const IvfPqSearchParams& params, std::uint64_t* out_ids,
+                                   float* out_dist, std::uint32_t* out_counts, bool on_device) const
+    -> std::expected<void, core::error> {
+    DeviceGuard g(impl_->dev);
+    try {
+        return impl_->search_flat(queries, n_queries, params, out_ids, out_dist, out_counts, on_device);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    }
+}
+
+auto IvfPqIndex::search_batch(const float* queries, std::size_t n_queries, const IvfPqSearchParams& params) const
+    -> std::expected<std::vector<std::vector<std::pair<std::uint64_t, float>>>, core::error> {
+    const size_t k = params.k;
+    std::vector<uint64_t> ids(n_queries * k);
+    std::vector<float> d(n_queries * k);
+    std::vector<uint32_t> cnt(n_queries);
+    auto r = search_batch_flat(queries, n_queries, params, ids.data(), d.data(), cnt.data(), false);
+    if (!r) return std::unexpected(r.error());
+    std::vector<std::vector<std::pair<std::uint64_t, float>>> out(n_queries);
+    for (size_t q = 0; q < n_queries; ++q)
+        for (uint32_t i = 0; i < cnt[q]; ++i) out[q].emplace_back(ids[q * k + i], d[q * k + i]);
+    return out;
+}
+
+auto IvfPqIndex::search(const float* query, const IvfPqSearchParams& params) const
+    -> std::expected<std::vector<std::pair<std::uint64_t, float>>, core::error> {
+    auto r = search_batch(query, 1, params);
+    if (!r) return std::unexpected(r.error());
+    return std::move((*r)[0]);
+}
+
+void IvfPqIndex::set_metadata_json(std::string_view json) { impl_->metadata_json.assign(json); }
+auto IvfPqIndex::get_metadata_json() const -> std::string { return impl_->metadata_json; }
+
+auto IvfPqIndex::get_stats() const noexcept -> Stats {
+    Stats s;
+    const auto& I = *impl_;
+    s.n_vectors = I.n_vectors;
+    s.n_lists = I.params.nlist;
+    s.m = I.params.m;
+    s.code_size = I.params.m;
+    s.memory_bytes = sizeof(Impl) + I.d_cent.bytes() + I.d_cb.bytes() + I.d_rot.bytes() + I.d_rotT.bytes() +
+                     I.d_rc.bytes() + I.d_offs.bytes() + I.d_ids.bytes() + I.d_codes.bytes() + I.d_vterm.bytes();
+    s.avg_list_size = I.n_vectors > 0 && I.params.nlist ? (float)I.n_vectors / (float)I.params.nlist : 0.0f;
+    s.timings_enabled = I.params.verbose || I.params.timings_enabled || env_flag("VESPER_TIMING");
+    if (s.timings_enabled) { s.t_assign_ms = I.t_assign_ms; s.t_encode_ms = I.t_encode_ms; s.t_lists_ms = I.t_lists_ms; }
+    return s;
+}
+
+auto IvfPqIndex::is_trained() const noexcept -> bool { return impl_->trained; }
+auto IvfPqIndex::dimension() const noexcept -> std::size_t { return impl_->dim; }
+auto IvfPqIndex::last_search_timings() const -> SearchTimings { return impl_->timings; }
+auto IvfPqIndex::params() const -> IvfPqTrainParams { return impl_->params; }
+
+auto IvfPqIndex::clear() -> void {
+    DeviceGuard g(impl_->dev);
+    std::lock_guard<std::mutex> lock(impl_->mu);
+    if (impl_->trained) { impl_->reset_lists(); sync(impl_->st); }
+}
+
+auto IvfPqIndex::reset() -> void {
+    DeviceGuard g(impl_->dev);
+    impl_ = std::make_unique<Impl>();
+}
+
+auto IvfPqIndex::centroids() const -> std::vector<float> { return impl_->h_cent; }
+auto IvfPqIndex::codebooks() const -> std::vector<float> { return impl_->h_cb; }
+auto IvfPqIndex::rotation() const -> std::vector<float> { return impl_->h_rot; }
+auto IvfPqIndex::list_offsets() const -> std::vector<std::uint64_t> { return impl_->h_offs; }
+
+auto IvfPqIndex::list_ids() const -> std::vector<std::uint64_t> {
+    DeviceGuard g(impl_->dev);
+    std::vector<uint64_t> v(impl_->n_vectors);
+    d2h(v.data(), impl_->d_ids.data(), v.size(), impl_->st);
+    sync(impl_->st);
+    return v;
+}
+
+auto IvfPqIndex::list_codes() const -> std::vector<std::uint8_t> {
+    DeviceGuard g(impl_->dev);
+    std::vector<uint8_t> v(impl_->n_vectors * impl_->params.m);
+    d2h(v.data(), impl_->d_codes.data(), v.size(), impl_->st);
+    sync(impl_->st);
+    return v;
+}
+
+auto IvfPqIndex::set_model(std::size_t dim, std::uint32_t nlist, std::uint32_t m, std::uint32_t nbits,
+                           const float* cent, const float* cb, const float* rot)
+    -> std::expected<void, core::error> {
+    if (dim == 0 || nlist == 0 || m == 0 || dim % m != 0 || nbits == 0 || nbits > 8)
+        return fail(error_code::invalid_argument, "invalid model shape");
+    DeviceGuard g(impl_->dev);
+    try {
+        auto& I = *impl_;
+        std::lock_guard<std::mutex> lock(I.mu);
+        I.params = IvfPqTrainParams{};
+        I.params.nlist = nlist;
+        I.params.m = m;
+        I.params.nbits = nbits;
+        I.params.use_opq = rot != nullptr;
+        I.dim = dim;
+        I.dsub = dim / m;
+        I.ksub = 1u << nbits;
+        I.h_cent.assign(cent, cent + (size_t)nlist * dim);
+        I.h_cb.assign(cb, cb + (size_t)m * I.ksub * I.dsub);
+        I.has_rot = rot != nullptr;
+        if (rot) I.h_rot.assign(rot, rot + dim * dim); else I.h_rot.clear();
+        I.upload_model();
+        I.reset_lists();
+        sync(I.st);
+        I.trained = true;
+        return {};
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    }
+}
+
+// ---------------------------------------------------------------------- persistence
+namespace {
+struct Fnv {
+    uint64_t h = 1469598103934665603ull;
+    void update(const void* p, size_t n) {
+        const auto* b = static_cast<const uint8_t*>(p);
+        for (size_t i = 0; i < n; ++i) { h ^= b[i]; h *= 1099511628211ull; }
+    }
+};
+}  // namespace
+
+// IvfPqIndex::save v1.0 layout (src/index/ivf_pq.cpp:4412-4490): magic, version,
+// flags, dims, centroids, codebooks, optional R, lists as (id, code) entries, FNV-1a
+// trailer.  The directory is created; the file is <path>/ivfpq.bin.
+auto IvfPqIndex::save(const std::string& path) const -> std::expected<void, core::error> {
+    namespace fs = std::filesystem;
+    const auto& I = *impl_;
+    if (!I.trained) return fail(error_code::internal, "PQ not trained", "ivf_pq.save");
+    std::error_code fec;
+    fs::create_directories(path, fec);
+    if (fec) return fail(error_code::io_failed, "Failed to create directory: " + path, "ivf_pq.save");
+    const std::string file_path = path + "/ivfpq.bin";
+    std::ofstream f(file_path, std::ios::binary);
+    if (!f) return fail(error_code::io_failed, "Failed to open file for writing: " + file_path, "ivf_pq.save");
+    std::vector<uint64_t> ids = list_ids();
+    std::vector<uint8_t> codes = list_codes();
+    Fnv fnv;
+    std::vector<char> buf;
+    buf.reserve(1 << 20);
+    auto put = [&](const void* p, size_t n) {
+        fnv.update(p, n);
+        const char* c = static_cast<const char*>(p);
+        buf.insert(buf.end(), c, c + n);
+        if (buf.size() > (8u << 20)) { f.write(buf.data(), (std::streamsize)buf.size()); buf.clear(); }
+    };
+    const char magic[8] = {'I', 'V', 'F', 'P', 'Q', 'v', '1', '0'};
+    put(magic, 8);
+    const uint16_t vmaj = 1, vmin = 0;
+    put(&vmaj, 2);
+    put(&vmin, 2);
+    const uint32_t flags = (I.params.use_opq && I.has_rot) ? 1u : 0u;
+    put(&flags, 4);
+    const uint32_t dim = (uint32_t)I.dim, nlist = I.params.nlist, m = I.params.m, nbits = I.params.nbits,
+                   dsub = (uint32_t)I.dsub, code_size = m;
+    const uint64_t nvec = I.n_vectors;
+    const uint64_t ts = (uint64_t)std::chrono::system_clock::to_time_t(std::chrono::system_clock::now());
+    put(&dim, 4); put(&nlist, 4); put(&m, 4); put(&nbits, 4); put(&dsub, 4);
+    put(&nvec, 8); put(&code_size, 4); put(&ts, 8);
+    const uint32_t meta_len = 0;
+    put(&meta_len, 4);
+    put(I.h_cent.data(), I.h_cent.size() * 4);
+    put(I.h_cb.data(), I.h_cb.size() * 4);
+    if (flags & 1u) put(I.h_rot.data(), I.h_rot.size() * 4);
+    put(&nlist, 4);
+    for (uint32_t l = 0; l < nlist; ++l) {
+        const uint64_t b = I.h_offs[l], e = I.h_offs[l + 1];
+        const uint64_t sz = e - b;
+        put(&sz, 8);
+        for (uint64_t j = b; j < e; ++j) {
+            put(&ids[j], 8);
+            put(codes.data() + j * m, m);
+        }
+    }
+    const char tail[4] = {'C', 'H', 'K', 'S'};
+    buf.insert(buf.end(), tail, tail + 4);
+    const char* hp = reinterpret_cast<const char*>(&fnv.h);
+    buf.insert(buf.end(), hp, hp + 8);
+    f.write(buf.data(), (std::streamsize)buf.size());
+    if (!f) return fail(error_code::io_failed, "Failed writing " + file_path, "ivf_pq.save");
+    return {};
+}
+
+// IvfPqIndex::load for the v1.0 layout (src/index/ivf_pq.cpp:4493-4966, monolithic
+// branch): every field is validated and the FNV-1a trailer must match.
+auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core::error> {
+    const std::string file_path = path + "/ivfpq.bin";
+    std::ifstream f(file_path, std::ios::binary);
+    if (!f) return fail(error_code::not_found, "Index file not found: " + file_path, "ivf_pq.load");
+    f.seekg(0, std::ios::end);
+    const std::streamoff fsize = f.tellg();
+    if (fsize < 64) return fail(error_code::config_invalid, "File too small", "ivf_pq.load");
+    f.seekg(0, std::ios::beg);
+    std::vector<char> raw((size_t)fsize);
+    f.read(raw.data(), fsize);
+    if (f.gcount() != fsize) return fail(error_code::io_failed, "Failed reading file", "ivf_pq.load");
+    size_t off = 0;
+    const size_t body_end = (size_t)fsize - 12;
+    auto get = [&](void* p, size_t n) -> bool {
+        if (off + n > body_end) return false;
+        std::memcpy(p, raw.data() + off, n);
+        off += n;
+        return true;
+    };
+    char magic[8];
+    if (!get(magic, 8)) return fail(error_code::io_failed, "Failed reading magic", "ivf_pq.load");
+    if (std::string_view(magic, 8) == std::string_view("IVFPQv11", 8))
+        return fail(error_code::unsupported, "v1.1 sectioned files are not supported by this loader", "ivf_pq.load");
+    if (std::string_view(magic, 8) != std::string_view("IVFPQv10", 8))
+        return fail(error_code::config_invalid, "Magic mismatch", "ivf_pq.load");
+    uint16_t vmaj = 0, vmin = 0;
+    if (!get(&vmaj, 2) || !get(&vmin, 2)) return fail(error_code::io_failed, "Failed reading version", "ivf_pq.load");
+    if (vmaj != 1) return fail(error_code::config_invalid, "Unsupported version", "ivf_pq.load");
+    uint32_t flags = 0, dim = 0, nlist = 0, m = 0, nbits = 0, dsub = 0, code_size = 0, meta_len = 0;
+    uint64_t nvec = 0, ts = 0;
+    if (!get(&flags, 4) || !get(&dim, 4) || !get(&nlist, 4) || !get(&m, 4) || !get(&nbits, 4) || !get(&dsub, 4) ||
+        !get(&nvec, 8) || !get(&code_size, 4) || !get(&ts, 8) || !get(&meta_len, 4))
+        return fail(error_code::io_failed, "Failed reading header", "ivf_pq.load");
+    if (dim == 0 || m == 0 || nlist == 0 || nbits == 0 || nbits > 8 || dsub * m != dim)
+        return fail(error_code::config_invalid, "Invalid header dimensions", "ivf_pq.load");
+    if (meta_len > 64u * 1024u) return fail(error_code::config_invalid, "Metadata too large", "ivf_pq.load");
+    std::string meta(meta_len, '\0');
+    if (meta_len && !get(meta.data(), meta_len)) return fail(error_code::io_failed, "Failed reading metadata", "ivf_pq.load");
+    const uint32_t ksub = 1u << nbits;
+    std::vector<float> cent((size_t)nlist * dim), cb((size_t)m * ksub * dsub), rot;
+    if (!get(cent.data(), cent.size() * 4)) return fail(error_code::io_failed, "Failed reading centroid row", "ivf_pq.load");
+    if (!get(cb.data(), cb.size() * 4)) return fail(error_code::io_failed, "Failed reading PQ codebooks", "ivf_pq.load");
+    if (flags & 1u) {
+        rot.resize((size_t)dim * dim);
+        if (!get(rot.data(), rot.size() * 4)) return fail(error_code::io_failed, "Failed reading OPQ rotation", "ivf_pq.load");
+    }
+    uint32_t lists_count = 0;
+    if (!get(&lists_count, 4)) return fail(error_code::io_failed, "Failed reading lists_count", "ivf_pq.load");
+    if (lists_count != nlist) return fail(error_code::config_invalid, "lists_count mismatch", "ivf_pq.load");
+    std::vector<uint64_t> offs(nlist + 1, 0), ids;
+    std::vector<uint8_t> codes;
+    for (uint32_t l = 0; l < nlist; ++l) {
+        uint64_t sz = 0;
+        if (!get(&sz, 8)) return fail(error_code::io_failed, "Failed reading list size", "ivf_pq.load");
+        if (sz > (body_end - off) / (8 + (uint64_t)m)) return fail(error_code::io_failed, "Failed reading id", "ivf_pq.load");
+        offs[l + 1] = offs[l] + sz;
+        const size_t base = ids.size();
+        ids.resize(base + sz);
+        codes.resize((base + sz) * m);
+        for (uint64_t j = 0; j < sz; ++j) {
+            get(&ids[base + j], 8);
+            get(codes.data() + (base + j) * m, m);
+        }
+    }
+    if (std::memcmp(raw.data() + body_end, "CHKS", 4) != 0)
+        return fail(error_code::config_invalid, "Missing checksum trailer", "ivf_pq.load");
+    uint64_t chk = 0;
+    std::memcpy(&chk, raw.data() + body_end + 4, 8);
+    Fnv fnv;
+    fnv.update(raw.data(), off);
+    if (off != body_end || chk != fnv.h) return fail(error_code::config_invalid, "Checksum mismatch", "ivf_pq.load");
+
+    IvfPqIndex index;
+    auto r = index.set_model(dim, nlist, m, nbits, cent.data(), cb.data(), rot.empty() ? nullptr : rot.data());
+    if (!r) return std::unexpected(r.error());
+    auto& I = *index.impl_;
+    DeviceGuard g(I.dev);
+    try {
+        I.params.use_opq = (flags & 1u) != 0;
+        I.h_offs = offs;
+        I.n_vectors = ids.size();
+        I.d_offs.resize(nlist + 1);
+        h2d(I.d_offs.data(), offs.data(), offs.size(), I.st);
+        I.d_ids.resize(std::max<size_t>(ids.size(), 1));
+        h2d(I.d_ids.data(), ids.data(), ids.size(), I.st);
+        I.d_codes.resize(std::max<size_t>(codes.size(), 1));
+        h2d(I.d_codes.data(), codes.data(), codes.size(), I.st);
+        I.recompute_vterms();
+        sync(I.st);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    }
+    return index;
+}
+
+}  // namespace vesper::index

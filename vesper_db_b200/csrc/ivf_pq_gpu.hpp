@@ -1,0 +1,189 @@
+// B200 IVF-PQ index: the host-side mirror of the reference's IvfPqIndex
+// (include/vesper/index/ivf_pq.hpp:140-386).  Same method names, argument meaning and
+// error behaviour; the work runs in the CUDA kernels of this directory.
+//
+// Data layout in HBM (one index = one device):
+//   centroids   float [nlist x dim]            coarse quantizer
+//   codebooks   float [m x ksub x dsub]        PQ codebooks (export_codebooks layout)
+//   rotation    float [dim x dim]              OPQ matrix R (row-vector convention x*R)
+//   rot_T       float [dim x dim]              R transposed (apply_rotation_T)
+//   rc          float [nlist x dim]            centroids * R (fast scan)
+//   list_offs   u64   [nlist + 1]              CSR offsets of the inverted lists
+//   codes       u8    [N x m]                  PQ codes, list-contiguous, insertion order
+//   ids         u64   [N]                      user ids, same order
+//   vterm       float [N]                      per-vector term of the fast scan
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <expected>
+#include <memory>
+#include <string>
+#include <string_view>
+#include <utility>
+#include <vector>
+
+namespace vesper::core {
+
+// Error taxonomy (include/vesper/error.hpp:19-44).
+enum class error_code : std::uint32_t {
+    ok = 0,
+    io_failed = 1001,
+    config_invalid = 2001,
+    precondition_failed = 4001,
+    out_of_memory = 5002,
+    not_found = 6001,
+    internal = 9001,
+    invalid_argument = 9002,
+    out_of_range = 9004,
+    unsupported = 9005,
+};
+
+struct error {
+    error_code code{error_code::internal};
+    std::string message;
+    std::string component;
+};
+
+}  // namespace vesper::core
+
+namespace vesper::index {
+
+enum class OpqInit { Identity, PCA };
+enum class CoarseAssigner { Brute, HNSW, KDTree, Projection };
+enum class KmeansInit { KMeansPlusPlus, KMeansParallel };
+
+// Search arithmetic.  Exact: every distance, LUT and rotation in the reference's
+// operation order (bit-identical results).  Fast: lookup table built once per query
+// (distance = ||q - c||^2 + u(x) + sum_s T_q[s][code]); distances agree with Exact to
+// fp32 rounding (well inside 1e-4 relative).
+enum class SearchMode : std::uint32_t { Fast = 0, Exact = 1 };
+
+// ivf_pq.hpp:59-106 (fields the GPU engine reads; the rest are accepted and ignored:
+// every coarse assigner of the reference returns the exact nearest centroid, which
+// is what the GPU computes by brute force).
+struct IvfPqTrainParams {
+    std::uint32_t nlist{256};
+    std::uint32_t m{8};
+    std::uint32_t nbits{8};
+    std::uint32_t max_iter{25};
+    float epsilon{1e-4f};
+    bool verbose{false};
+    bool use_opq{true};
+    std::uint32_t opq_iter{10};
+    std::size_t opq_sample_n{20000};
+    OpqInit opq_init{OpqInit::PCA};
+    std::uint32_t seed{42};
+    KmeansInit kmeans_init_method{KmeansInit::KMeansPlusPlus};
+    CoarseAssigner coarse_assigner{CoarseAssigner::KDTree};
+    bool use_centroid_ann{true};
+    bool timings_enabled{false};
+};
+
+// ivf_pq.hpp:109-117, plus the GPU search mode.
+struct IvfPqSearchParams {
+    std::uint32_t nprobe{8};
+    std::uint32_t k{10};
+    std::uint32_t cand_k{0};
+    bool use_exact_rerank{false};
+    std::uint32_t rerank_k{0};
+    SearchMode mode{SearchMode::Fast};
+};
+
+struct IvfPqTrainStats {
+    std::uint32_t iterations{0};
+    float final_error{0.0f};
+    float train_time_sec{0.0f};
+    std::vector<float> errors;
+    // GPU additions: what the trainer decided / measured.
+    bool opq_kept{false};
+    double err_unrot{0.0};
+    double err_opq{0.0};
+    std::uint32_t coarse_iterations{0};
+};
+
+// Per-stage device times of the last search_batch call (CUDA events, ms).
+struct SearchTimings {
+    float coarse_ms{0}, select_ms{0}, rotate_ms{0}, scan_ms{0}, merge_ms{0}, total_ms{0};
+    std::uint64_t scanned_entries{0};   // sum over queries of the probed lists' sizes
+};
+
+class IvfPqIndex {
+public:
+    IvfPqIndex();
+    ~IvfPqIndex();
+    IvfPqIndex(IvfPqIndex&&) noexcept;
+    IvfPqIndex& operator=(IvfPqIndex&&) noexcept;
+    IvfPqIndex(const IvfPqIndex&) = delete;
+    IvfPqIndex& operator=(const IvfPqIndex&) = delete;
+
+    auto train(const float* data, std::size_t dim, std::size_t n, const IvfPqTrainParams& params)
+        -> std::expected<IvfPqTrainStats, core::error>;
+    auto add(const std::uint64_t* ids, const float* data, std::size_t n)
+        -> std::expected<void, core::error>;
+    // train / add with the inputs in device memory of the index's GPU when on_device.
+    auto train_device(const float* data, std::size_t dim, std::size_t n, const IvfPqTrainParams& params,
+                      bool on_device) -> std::expected<IvfPqTrainStats, core::error>;
+    auto add_device(const std::uint64_t* ids, const float* data, std::size_t n, bool on_device)
+        -> std::expected<void, core::error>;
+    auto search(const float* query, const IvfPqSearchParams& params) const
+        -> std::expected<std::vector<std::pair<std::uint64_t, float>>, core::error>;
+    auto search_batch(const float* queries, std::size_t n_queries, const IvfPqSearchParams& params) const
+        -> std::expected<std::vector<std::vector<std::pair<std::uint64_t, float>>>, core::error>;
+
+    // Flat-output batch search (the C ABI's layout): out_ids/out_dist [nq x k], padded
+    // like vesper_ivfpq_search_batch; out_counts (optional) receives the number of
+    // real results per query.  `on_device` = all four pointers are device pointers.
+    auto search_batch_flat(const float* queries, std::size_t n_queries,
+                           const IvfPqSearchParams& params, std::uint64_t* out_ids,
+                           float* out_dist, std::uint32_t* out_counts, bool on_device) const
+        -> std::expected<void, core::error>;
+
+    void set_metadata_json(std::string_view json);
+    auto get_metadata_json() const -> std::string;
+
+    struct Stats {
+        std::size_t n_vectors{0};
+        std::size_t n_lists{0};
+        std::size_t m{0};
+        std::size_t code_size{0};
+        std::size_t memory_bytes{0};
+        float avg_list_size{0.0f};
+        bool timings_enabled{false};
+        double t_assign_ms{0.0};
+        double t_encode_ms{0.0};
+        double t_lists_ms{0.0};
+    };
+    auto get_stats() const noexcept -> Stats;
+    auto is_trained() const noexcept -> bool;
+    auto dimension() const noexcept -> std::size_t;
+    auto clear() -> void;
+    auto reset() -> void;
+    auto last_search_timings() const -> SearchTimings;
+
+    // Model access (host copies) for tests and tools.
+    auto centroids() const -> std::vector<float>;
+    auto codebooks() const -> std::vector<float>;
+    auto rotation() const -> std::vector<float>;
+    auto list_offsets() const -> std::vector<std::uint64_t>;
+    auto list_ids() const -> std::vector<std::uint64_t>;
+    auto list_codes() const -> std::vector<std::uint8_t>;
+    auto params() const -> IvfPqTrainParams;
+
+    // Install a pre-trained model (centroids [nlist x dim], codebooks [m*ksub x dsub],
+    // optional rotation [dim x dim]); clears the lists.
+    auto set_model(std::size_t dim, std::uint32_t nlist, std::uint32_t m, std::uint32_t nbits,
+                   const float* centroids, const float* codebooks, const float* rotation)
+        -> std::expected<void, core::error>;
+
+    // Persistence: v1.0 monolithic layout in <path>/ivfpq.bin (ivf_pq.cpp:4412-4490).
+    auto save(const std::string& path) const -> std::expected<void, core::error>;
+    static auto load(const std::string& path) -> std::expected<IvfPqIndex, core::error>;
+
+    class Impl;
+
+private:
+    std::unique_ptr<Impl> impl_;
+};
+
+}  // namespace vesper::index

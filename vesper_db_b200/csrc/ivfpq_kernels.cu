@@ -1,0 +1,778 @@
+// B200 kernels for the IVF-PQ search and add paths.
+//
+// Exact kernels reproduce the reference arithmetic bit for bit:
+//   * distances in the AVX2 lane order (common.cuh: l2_ref / hsum8),
+//   * rotations as sequential-k dots with a rounded multiply and a rounded add
+//     (apply_rotation, src/index/ivf_pq.cpp:2947-2968),
+//   * ADC sums in sub-quantizer order from 0.0f (pq_fastscan.hpp:284-317).
+// The fast scan (scan_fast_kernel) regroups the ADC algebra so the lookup table is
+// built once per query instead of once per (query, list); its distances agree with
+// the exact ones to fp32 rounding.
+#include <cfloat>
+
+#include "kernels.cuh"
+#include "select.cuh"
+
+namespace vgpu {
+
+// =====================================================================================
+// Exact L2 distance tiles:  D[i][j] = l2_ref(x_i, c_j)
+//
+// CTA tile 64 rows x 32 centroids, 256 threads, each thread 4 rows x 2 centroids x 8
+// lane accumulators.  The dimension loop runs over [0, floor(dim/8)*8) in chunks of
+// 32 staged in shared memory; element k always feeds lane k%8, so the chunking does
+// not change the order of any lane's FMA chain.  Padding past floor(dim/8)*8 is zero,
+// which adds exact zeros.  The scalar tail (dim%8 elements) is applied after hsum8.
+// =====================================================================================
+namespace {
+constexpr int DT_Q = 64, DT_C = 32, DT_K = 32, DT_P = DT_K + 4;
+}
+
+__global__ void __launch_bounds__(256) l2_dist_kernel(const float* __restrict__ x, long long nx,
+                                                      const float* __restrict__ c, int nc, int dim,
+                                                      float* __restrict__ D, long long ldd) {
+    __shared__ __align__(16) float Xs[DT_Q][DT_P];
+    __shared__ __align__(16) float Cs[DT_C][DT_P];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qrow = (warp >> 1) * 16 + (lane >> 3) * 4;
+    const int ccol = (warp & 1) * 16 + (lane & 7) * 2;
+    const long long q0 = (long long)blockIdx.x * DT_Q;
+    const long long c0 = (long long)blockIdx.y * DT_C;
+    const int simd_end = dim & ~7;
+
+    float acc[4][2][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int l = 0; l < 8; ++l) acc[i][j][l] = 0.0f;
+
+    for (int k0 = 0; k0 < simd_end; k0 += DT_K) {
+        {
+            const int r = tid >> 2, s = (tid & 3) * 8;
+            const long long g = q0 + r;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int kk = k0 + s + j;
+                Xs[r][s + j] = (g < nx && kk < simd_end) ? x[g * dim + kk] : 0.0f;
+            }
+        }
+        {
+            const int r = tid >> 3, s = (tid & 7) * 4;
+            const long long g = c0 + r;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kk = k0 + s + j;
+                Cs[r][s + j] = (g < nc && kk < simd_end) ? c[g * dim + kk] : 0.0f;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < DT_K; kk += 4) {
+            float4 xv[4], cv[2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&Xs[qrow + i][kk]);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) cv[j] = *reinterpret_cast<const float4*>(&Cs[ccol + j][kk]);
+            const int lb = kk & 7;  // compile-time after unrolling: 0 or 4
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    float d;
+                    d = __fsub_rn(xv[i].x, cv[j].x); acc[i][j][lb + 0] = __fmaf_rn(d, d, acc[i][j][lb + 0]);
+                    d = __fsub_rn(xv[i].y, cv[j].y); acc[i][j][lb + 1] = __fmaf_rn(d, d, acc[i][j][lb + 1]);
+                    d = __fsub_rn(xv[i].z, cv[j].z); acc[i][j][lb + 2] = __fmaf_rn(d, d, acc[i][j][lb + 2]);
+                    d = __fsub_rn(xv[i].w, cv[j].w); acc[i][j][lb + 3] = __fmaf_rn(d, d, acc[i][j][lb + 3]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const long long g = q0 + qrow + i;
+        if (g >= nx) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const long long h = c0 + ccol + j;
+            if (h >= nc) continue;
+            float r = hsum8(acc[i][j]);
+            for (int t = simd_end; t < dim; ++t) {
+                const float d = __fsub_rn(x[g * dim + t], c[h * dim + t]);
+                r = __fadd_rn(r, __fmul_rn(d, d));
+            }
+            D[g * ldd + h] = r;
+        }
+    }
+}
+
+void launch_l2_dist(const float* x, long long nx, const float* c, int nc, int dim, float* D,
+                    long long ldd, cudaStream_t st) {
+    if (nx <= 0 || nc <= 0) return;
+    dim3 grid(ceil_div(nx, DT_Q), ceil_div(nc, DT_C));
+    l2_dist_kernel<<<grid, 256, 0, st>>>(x, nx, c, nc, dim, D, ldd);
+    VGPU_LAUNCH("l2_dist_kernel");
+}
+
+// =====================================================================================
+// Streaming top-k over long rows: the row is consumed in chunks; each round selects
+// the k best of [carried k | chunk].  Carried entries always precede the chunk, so
+// position order equals column order among equal values.
+// =====================================================================================
+namespace {
+constexpr int SEL_NT = 256;
+constexpr int SEL_CH = 2048;
+}
+
+template <int NT>
+__device__ int carry_round(float* buf, int carry_n, int chunk_n, int k, float* carry_d,
+                           uint32_t* carry_tag, uint32_t* tag_tmp, unsigned long long* sortb,
+                           SelectSmem& sm, uint32_t chunk_tag0) {
+    // buf[0..carry_n) already holds carry_d; buf[carry_n..) the chunk values.
+    const int n = carry_n + chunk_n;
+    const int got = block_select_k<NT>(buf, n, k, sortb, sm);
+    for (int i = threadIdx.x; i < got; i += NT) {
+        const uint32_t pos = (uint32_t)(sortb[i] & 0xffffffffull);
+        tag_tmp[i] = pos < (uint32_t)carry_n ? carry_tag[pos] : chunk_tag0 + (pos - carry_n);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < got; i += NT) {
+        carry_d[i] = key_float((uint32_t)(sortb[i] >> 32));
+        carry_tag[i] = tag_tmp[i];
+    }
+    __syncthreads();
+    return got;
+}
+
+struct TopkSmem {
+    float buf[kMaxK + SEL_CH];
+    float carry_d[kMaxK];
+    uint32_t carry_tag[kMaxK];
+    uint32_t tag_tmp[kMaxK];
+    unsigned long long sortb[kMaxK];
+    SelectSmem sel;
+};
+
+__global__ void __launch_bounds__(SEL_NT) row_topk_kernel(const float* __restrict__ D, int ncols,
+                                                          long long ldd, int k,
+                                                          uint32_t* __restrict__ out_idx,
+                                                          float* __restrict__ out_val) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    TopkSmem& S = *reinterpret_cast<TopkSmem*>(smem_raw);
+    const long long row = blockIdx.x;
+    const float* d = D + row * ldd;
+    int carry_n = 0;
+    for (int c0 = 0; c0 < ncols; c0 += SEL_CH) {
+        const int cn = min(SEL_CH, ncols - c0);
+        for (int i = threadIdx.x; i < carry_n; i += SEL_NT) S.buf[i] = S.carry_d[i];
+        for (int i = threadIdx.x; i < cn; i += SEL_NT) S.buf[carry_n + i] = d[c0 + i];
+        __syncthreads();
+        carry_n = carry_round<SEL_NT>(S.buf, carry_n, cn, k, S.carry_d, S.carry_tag, S.tag_tmp,
+                                      S.sortb, S.sel, (uint32_t)c0);
+    }
+    for (int i = threadIdx.x; i < k; i += SEL_NT) {
+        out_idx[row * k + i] = i < carry_n ? S.carry_tag[i] : 0u;
+        out_val[row * k + i] = i < carry_n ? S.carry_d[i] : FLT_MAX;
+    }
+}
+
+void launch_row_topk(const float* D, long long n_rows, int ncols, long long ldd, int k,
+                     uint32_t* out_idx, float* out_val, cudaStream_t st) {
+    if (n_rows <= 0) return;
+    if (k > kMaxK) throw CudaError("row_topk: k exceeds the supported maximum");
+    const size_t smem = sizeof(TopkSmem);
+    VGPU_CHECK(cudaFuncSetAttribute(row_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    row_topk_kernel<<<(unsigned)n_rows, SEL_NT, smem, st>>>(D, ncols, ldd, k, out_idx, out_val);
+    VGPU_LAUNCH("row_topk_kernel");
+}
+
+// =====================================================================================
+// Row arg-min with the reference's strict-< scan semantics.
+// =====================================================================================
+__global__ void __launch_bounds__(256) row_argmin_kernel(const float* __restrict__ D, int ncols,
+                                                         long long ldd,
+                                                         const uint32_t* __restrict__ keep,
+                                                         uint32_t* __restrict__ out_idx,
+                                                         float* __restrict__ out_val) {
+    __shared__ unsigned long long red[8];
+    const long long row = blockIdx.x;
+    const float* d = D + row * ldd;
+    unsigned long long best = ~0ull;
+    for (int j = threadIdx.x; j < ncols; j += 256) {
+        const unsigned long long v = ((unsigned long long)float_key(d[j]) << 32) | (uint32_t)j;
+        best = v < best ? v : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v < best ? v : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) best = red[w] < best ? red[w] : best;
+        red[0] = best;
+        float mv = key_float((uint32_t)(best >> 32));
+        uint32_t mi = (uint32_t)(best & 0xffffffffu);
+        // A strict `<` scan starting from FLT_MAX never moves off index 0 unless some
+        // value is below FLT_MAX.
+        if (!(mv < FLT_MAX)) { mi = 0; mv = FLT_MAX; }
+        if (keep) {
+            const uint32_t kc = keep[row];
+            if (d[kc] == mv) mi = kc;
+        }
+        out_idx[row] = mi;
+        if (out_val) out_val[row] = mv;
+    }
+}
+
+void launch_row_argmin(const float* D, long long n_rows, int ncols, long long ldd,
+                       const uint32_t* keep, uint32_t* out_idx, float* out_val, cudaStream_t st) {
+    if (n_rows <= 0) return;
+    row_argmin_kernel<<<(unsigned)n_rows, 256, 0, st>>>(D, ncols, ldd, keep, out_idx, out_val);
+    VGPU_LAUNCH("row_argmin_kernel");
+}
+
+// =====================================================================================
+// Residual + rotation, exact order: out[r][j] = sum_k a[r][k] * R[k][j], a = x - c.
+// CTA tile 64 rows x 64 columns, 256 threads, 4x4 outputs per thread, k staged in
+// chunks of 32 and consumed in increasing order (one rounded multiply and one rounded
+// add per term, exactly as the reference's scalar loop).
+// =====================================================================================
+namespace {
+constexpr int RT_R = 64, RT_C = 64, RT_K = 32;
+}
+
+__global__ void __launch_bounds__(256) residual_rotate_kernel(
+    const float* __restrict__ x, const uint32_t* __restrict__ xidx, const float* __restrict__ c,
+    const uint32_t* __restrict__ cidx, long long rows, int dim, const float* __restrict__ R,
+    float* __restrict__ out) {
+    __shared__ __align__(16) float As[RT_R][RT_K + 1];
+    __shared__ __align__(16) float Bs[RT_K][RT_C + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const long long r0 = (long long)blockIdx.x * RT_R;
+    const int j0 = blockIdx.y * RT_C;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+    for (int k0 = 0; k0 < dim; k0 += RT_K) {
+        for (int e = tid; e < RT_R * RT_K; e += 256) {
+            const int r = e / RT_K, kk = e % RT_K;
+            const long long g = r0 + r;
+            float v = 0.0f;
+            if (g < rows && k0 + kk < dim) {
+                const long long xr = xidx ? (long long)xidx[g] : g;
+                v = x[xr * dim + k0 + kk];
+                if (c) v = __fsub_rn(v, c[(long long)cidx[g] * dim + k0 + kk]);
+            }
+            As[r][kk] = v;
+        }
+        for (int e = tid; e < RT_K * RT_C; e += 256) {
+            const int kk = e / RT_C, j = e % RT_C;
+            Bs[kk][j] = (k0 + kk < dim && j0 + j < dim) ? R[(long long)(k0 + kk) * dim + j0 + j] : 0.0f;
+        }
+        __syncthreads();
+        const int kmax = min(RT_K, dim - k0);
+        for (int kk = 0; kk < kmax; ++kk) {
+            float a[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[ty * 4 + i][kk];
+            const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[i][0] = __fadd_rn(acc[i][0], __fmul_rn(a[i], b.x));
+                acc[i][1] = __fadd_rn(acc[i][1], __fmul_rn(a[i], b.y));
+                acc[i][2] = __fadd_rn(acc[i][2], __fmul_rn(a[i], b.z));
+                acc[i][3] = __fadd_rn(acc[i][3], __fmul_rn(a[i], b.w));
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const long long g = r0 + ty * 4 + i;
+        if (g >= rows) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int col = j0 + tx * 4 + j;
+            if (col < dim) out[g * dim + col] = acc[i][j];
+        }
+    }
+}
+
+__global__ void residual_copy_kernel(const float* __restrict__ x, const uint32_t* __restrict__ xidx,
+                                     const float* __restrict__ c, const uint32_t* __restrict__ cidx,
+                                     long long rows, int dim, float* __restrict__ out) {
+    const long long total = rows * dim;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / dim;
+        const int k = (int)(e % dim);
+        const long long xr = xidx ? (long long)xidx[r] : r;
+        float v = x[xr * dim + k];
+        if (c) v = __fsub_rn(v, c[(long long)cidx[r] * dim + k]);
+        out[e] = v;
+    }
+}
+
+void launch_residual_rotate(const float* x, const uint32_t* xidx, const float* c,
+                            const uint32_t* cidx, long long rows, int dim, const float* R,
+                            float* out, cudaStream_t st) {
+    if (rows <= 0) return;
+    if (!R) {
+        const long long total = rows * dim;
+        const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 32);
+        residual_copy_kernel<<<blocks, 256, 0, st>>>(x, xidx, c, cidx, rows, dim, out);
+        VGPU_LAUNCH("residual_copy_kernel");
+        return;
+    }
+    dim3 grid(ceil_div(rows, RT_R), ceil_div(dim, RT_C));
+    residual_rotate_kernel<<<grid, 256, 0, st>>>(x, xidx, c, cidx, rows, dim, R, out);
+    VGPU_LAUNCH("residual_rotate_kernel");
+}
+
+void launch_rotate_fast(const float* x, long long rows, int dim, const float* R, float* out,
+                        cudaStream_t st) {
+    launch_residual_rotate(x, nullptr, nullptr, nullptr, rows, dim, R, out, st);
+}
+
+// =====================================================================================
+// PQ encode: one thread per (vector, sub-space); the sub-space codebook is staged in
+// shared memory when it fits.  Strict `<` from FLT_MAX -> lowest code wins ties
+// (find_nearest_code, src/index/pq_fastscan.cpp:78-99).
+// =====================================================================================
+template <int DS>
+__global__ void __launch_bounds__(128) pq_encode_kernel(const float* __restrict__ x, long long n,
+                                                        int m, int ksub, int dsub_rt,
+                                                        const float* __restrict__ cb,
+                                                        uint8_t* __restrict__ codes, int cb_in_smem) {
+    extern __shared__ __align__(16) float ycb[];
+    const int dsub = DS > 0 ? DS : dsub_rt;
+    const int s = blockIdx.y;
+    const float* y = cb + (long long)s * ksub * dsub;
+    if (cb_in_smem) {
+        for (int e = threadIdx.x; e < ksub * dsub; e += blockDim.x) ycb[e] = y[e];
+        __syncthreads();
+        y = ycb;
+    }
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* v = x + i * (long long)m * dsub + (long long)s * dsub;
+    float best = FLT_MAX;
+    int code = 0;
+    if (DS > 0) {
+        float vr[DS > 0 ? DS : 1];
+#pragma unroll
+        for (int e = 0; e < DS; ++e) vr[e] = v[e];
+        for (int j = 0; j < ksub; ++j) {
+            const float d = l2_ref(vr, y + j * DS, DS);
+            if (d < best) { best = d; code = j; }
+        }
+    } else {
+        for (int j = 0; j < ksub; ++j) {
+            const float d = l2_ref(v, y + (long long)j * dsub, dsub);
+            if (d < best) { best = d; code = j; }
+        }
+    }
+    codes[i * m + s] = (uint8_t)code;
+}
+
+void launch_pq_encode(const float* x, long long n, int m, int ksub, int dsub, const float* cb,
+                      uint8_t* codes, cudaStream_t st) {
+    if (n <= 0) return;
+    const size_t cb_bytes = (size_t)ksub * dsub * sizeof(float);
+    const int in_smem = cb_bytes <= 96 * 1024 ? 1 : 0;
+    const size_t smem = in_smem ? cb_bytes : 0;
+    dim3 grid(ceil_div(n, 128), m);
+#define VGPU_ENC(DSV)                                                                              \
+    do {                                                                                           \
+        VGPU_CHECK(cudaFuncSetAttribute(pq_encode_kernel<DSV>,                                     \
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));  \
+        pq_encode_kernel<DSV><<<grid, 128, smem, st>>>(x, n, m, ksub, dsub, cb, codes, in_smem);   \
+    } while (0)
+    if (dsub == 4) VGPU_ENC(4);
+    else if (dsub == 8) VGPU_ENC(8);
+    else if (dsub == 16) VGPU_ENC(16);
+    else VGPU_ENC(0);
+#undef VGPU_ENC
+    VGPU_LAUNCH("pq_encode_kernel");
+}
+
+// =====================================================================================
+// Exact scan: one CTA per (query, probe rank).  Builds the (query, list) LUT in shared
+// memory with l2_ref over each codeword (compute_lookup_tables order), sums each
+// entry's LUT values in sub-quantizer order from 0.0f, and keeps the k best of the
+// list by (distance, list position).
+// =====================================================================================
+struct ScanSmemTail {
+    float carry_d[kMaxK];
+    uint32_t carry_tag[kMaxK];
+    uint32_t tag_tmp[kMaxK];
+    unsigned long long sortb[kMaxK];
+    SelectSmem sel;
+};
+
+__global__ void __launch_bounds__(SEL_NT) scan_exact_kernel(
+    const float* __restrict__ queries, int dim, const float* __restrict__ centroids,
+    const float* __restrict__ rres, const uint32_t* __restrict__ probe, int nprobe,
+    const float* __restrict__ cb, int m, int ksub, int dsub, const uint64_t* __restrict__ offs,
+    const uint8_t* __restrict__ codes, int k, float* __restrict__ cand_d,
+    uint32_t* __restrict__ cand_pos, uint32_t* __restrict__ cand_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const long long q = blockIdx.x;
+    const int t = blockIdx.y;
+    const long long pair = q * nprobe + t;
+    float* r = reinterpret_cast<float*>(smem_raw);                       // [dim]
+    float* lut = r + ((dim + 3) & ~3);                                   // [m * ksub]
+    float* buf = lut + (((size_t)m * ksub + 3) & ~(size_t)3);                                 // [kMaxK + SEL_CH]
+    ScanSmemTail& S = *reinterpret_cast<ScanSmemTail*>(buf + kMaxK + SEL_CH);
+
+    const uint32_t l = probe[pair];
+    if (rres) {
+        for (int d = threadIdx.x; d < dim; d += SEL_NT) r[d] = rres[pair * dim + d];
+    } else {
+        const float* qv = queries + q * dim;
+        const float* cv = centroids + (long long)l * dim;
+        for (int d = threadIdx.x; d < dim; d += SEL_NT) r[d] = __fsub_rn(qv[d], cv[d]);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < m * ksub; e += SEL_NT) {
+        const int s = e / ksub, j = e % ksub;
+        lut[e] = l2_ref(r + s * dsub, cb + ((long long)s * ksub + j) * dsub, dsub);
+    }
+    __syncthreads();
+    const uint64_t base = offs[l];
+    const long long L = (long long)(offs[l + 1] - base);
+    int carry_n = 0;
+    for (long long c0 = 0; c0 < L; c0 += SEL_CH) {
+        const int cn = (int)min((long long)SEL_CH, L - c0);
+        for (int i = threadIdx.x; i < carry_n; i += SEL_NT) buf[i] = S.carry_d[i];
+        for (int i = threadIdx.x; i < cn; i += SEL_NT) {
+            const uint8_t* code = codes + (base + c0 + i) * (uint64_t)m;
+            float dd = 0.0f;
+            for (int s = 0; s < m; ++s) dd = __fadd_rn(dd, lut[s * ksub + code[s]]);
+            buf[carry_n + i] = dd;
+        }
+        __syncthreads();
+        carry_n = carry_round<SEL_NT>(buf, carry_n, cn, k, S.carry_d, S.carry_tag, S.tag_tmp,
+                                      S.sortb, S.sel, (uint32_t)c0);
+    }
+    for (int i = threadIdx.x; i < carry_n; i += SEL_NT) {
+        cand_d[pair * k + i] = S.carry_d[i];
+        cand_pos[pair * k + i] = S.carry_tag[i];
+    }
+    if (threadIdx.x == 0) cand_n[pair] = (uint32_t)carry_n;
+}
+
+void launch_scan_exact(const float* queries, long long nq, int dim, const float* centroids,
+                       const float* rres, const uint32_t* probe, int nprobe, const float* cb, int m,
+                       int ksub, int dsub, const uint64_t* list_offsets, const uint8_t* codes,
+                       int k, float* cand_d, uint32_t* cand_pos, uint32_t* cand_n,
+                       cudaStream_t st) {
+    if (nq <= 0 || nprobe <= 0) return;
+    if (k > kMaxK) throw CudaError("scan_exact: k exceeds the supported maximum");
+    const size_t smem = ((size_t)((dim + 3) & ~3) + (((size_t)m * ksub + 3) & ~(size_t)3) + kMaxK + SEL_CH) * sizeof(float) +
+                        sizeof(ScanSmemTail);
+    if (smem > 227 * 1024) throw CudaError("scan_exact: LUT does not fit in shared memory");
+    VGPU_CHECK(cudaFuncSetAttribute(scan_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)nq, nprobe);
+    scan_exact_kernel<<<grid, SEL_NT, smem, st>>>(queries, dim, centroids, rres, probe, nprobe, cb, m,
+                                                  ksub, dsub, list_offsets, codes, k, cand_d, cand_pos,
+                                                  cand_n);
+    VGPU_LAUNCH("scan_exact_kernel");
+}
+
+// =====================================================================================
+// Merge per query: candidates of probe rank t sit at [t*k, t*k + cand_n) sorted by
+// (distance, list position); concatenated in probe order they are in scan order, so
+// the streaming select's position tie-break is the scan-order tie-break.
+// =====================================================================================
+__global__ void __launch_bounds__(SEL_NT) merge_kernel(
+    const float* __restrict__ cand_d, const uint32_t* __restrict__ cand_pos,
+    const uint32_t* __restrict__ cand_n, int nprobe, int k, const uint32_t* __restrict__ probe,
+    const uint64_t* __restrict__ offs, const uint64_t* __restrict__ ids,
+    uint64_t* __restrict__ out_ids, float* __restrict__ out_d, uint32_t* __restrict__ out_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    TopkSmem& S = *reinterpret_cast<TopkSmem*>(smem_raw);
+    __shared__ uint32_t chunk_tags[SEL_CH];
+    const long long q = blockIdx.x;
+    int carry_n = 0;
+    int t = 0;
+    while (t < nprobe) {
+        // Gather whole probe runs into a chunk of at most SEL_CH entries.
+        __shared__ int s_cn, s_tend;
+        if (threadIdx.x == 0) {
+            int cn = 0, te = t;
+            while (te < nprobe) {
+                const int c = (int)cand_n[q * nprobe + te];
+                if (cn + c > SEL_CH && te > t) break;
+                cn += c; ++te;
+                if (cn >= SEL_CH) break;
+            }
+            s_cn = cn; s_tend = te;
+        }
+        __syncthreads();
+        const int cn = s_cn, te = s_tend;
+        for (int i = threadIdx.x; i < carry_n; i += SEL_NT) S.buf[i] = S.carry_d[i];
+        if (threadIdx.x == 0) {
+            int o = 0;
+            for (int tt = t; tt < te; ++tt) {
+                const int c = (int)cand_n[q * nprobe + tt];
+                for (int i = 0; i < c; ++i) chunk_tags[o + i] = ((uint32_t)tt << 16) | (uint32_t)i;
+                o += c;
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < cn; i += SEL_NT) {
+            const uint32_t tg = chunk_tags[i];
+            const long long pair = q * nprobe + (tg >> 16);
+            S.buf[carry_n + i] = cand_d[pair * k + (tg & 0xffffu)];
+        }
+        __syncthreads();
+        // Select; map positions to tags (probe << 16 | rank within probe run).
+        const int n = carry_n + cn;
+        const int got = block_select_k<SEL_NT>(S.buf, n, k, S.sortb, S.sel);
+        for (int i = threadIdx.x; i < got; i += SEL_NT) {
+            const uint32_t pos = (uint32_t)(S.sortb[i] & 0xffffffffull);
+            S.tag_tmp[i] = pos < (uint32_t)carry_n ? S.carry_tag[pos] : chunk_tags[pos - carry_n];
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < got; i += SEL_NT) {
+            S.carry_d[i] = key_float((uint32_t)(S.sortb[i] >> 32));
+            S.carry_tag[i] = S.tag_tmp[i];
+        }
+        __syncthreads();
+        carry_n = got;
+        t = te;
+    }
+    for (int i = threadIdx.x; i < k; i += SEL_NT) {
+        if (i < carry_n) {
+            const uint32_t tg = S.carry_tag[i];
+            const uint32_t tt = tg >> 16, rk = tg & 0xffffu;
+            const long long pair = q * nprobe + tt;
+            const uint32_t l = probe[pair];
+            const uint64_t e = offs[l] + cand_pos[pair * k + rk];
+            out_ids[q * k + i] = ids[e];
+            out_d[q * k + i] = S.carry_d[i];
+        } else {
+            out_ids[q * k + i] = 0;
+            out_d[q * k + i] = carry_n > 0 ? S.carry_d[carry_n - 1] : 0.0f;
+        }
+    }
+    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)carry_n;
+}
+
+void launch_merge(const float* cand_d, const uint32_t* cand_pos, const uint32_t* cand_n,
+                  long long nq, int nprobe, int k, const uint32_t* probe,
+                  const uint64_t* list_offsets, const uint64_t* ids, uint64_t* out_ids,
+                  float* out_d, uint32_t* out_n, cudaStream_t st) {
+    if (nq <= 0) return;
+    if (k > kMaxK || nprobe > 65535) throw CudaError("merge: k or nprobe exceeds the supported maximum");
+    const size_t smem = sizeof(TopkSmem);
+    VGPU_CHECK(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    merge_kernel<<<(unsigned)nq, SEL_NT, smem, st>>>(cand_d, cand_pos, cand_n, nprobe, k, probe,
+                                                     list_offsets, ids, out_ids, out_d, out_n);
+    VGPU_LAUNCH("merge_kernel");
+}
+
+// =====================================================================================
+// Fast scan: one CTA per query.  T_q[s][j] = -2 <(Rq)_s, y_sj> lives in shared memory
+// for the whole query; each entry's distance is (||q - c_l||^2 + u(x)) + sum_s T_q.
+// The running top-k is carried across chunks and lists in scan order.
+// =====================================================================================
+__global__ void __launch_bounds__(SEL_NT) scan_fast_kernel(
+    const float* __restrict__ rq, int dim, const uint32_t* __restrict__ probe,
+    const float* __restrict__ probe_d, const float* __restrict__ rc, int nprobe,
+    const float* __restrict__ cb, int m, int ksub,
+    int dsub, const uint64_t* __restrict__ offs, const uint8_t* __restrict__ codes,
+    const float* __restrict__ vterm, const uint64_t* __restrict__ ids, int k,
+    uint64_t* __restrict__ out_ids, float* __restrict__ out_d, uint32_t* __restrict__ out_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const long long q = blockIdx.x;
+    float* qv = reinterpret_cast<float*>(smem_raw);                       // [dim]
+    float* lut = qv + ((dim + 3) & ~3);                                   // [m * ksub]
+    float* buf = lut + (((size_t)m * ksub + 3) & ~(size_t)3);                                  // [kMaxK + SEL_CH]
+    ScanSmemTail& S = *reinterpret_cast<ScanSmemTail*>(buf + kMaxK + SEL_CH);
+    for (int d = threadIdx.x; d < dim; d += SEL_NT) qv[d] = rq[q * dim + d];
+    __syncthreads();
+    for (int e = threadIdx.x; e < m * ksub; e += SEL_NT) {
+        const int s = e / ksub, j = e % ksub;
+        const float* y = cb + ((long long)s * ksub + j) * dsub;
+        const float* v = qv + s * dsub;
+        float acc = 0.0f;
+        for (int t = 0; t < dsub; ++t) acc = __fmaf_rn(v[t], y[t], acc);
+        lut[e] = -2.0f * acc;
+    }
+    __syncthreads();
+    __shared__ float s_base;
+    int carry_n = 0;
+    for (int t = 0; t < nprobe; ++t) {
+        const long long pr = q * nprobe + t;
+        const uint32_t l = probe[pr];
+        if (rc) {
+            // ||Rq - Rc_l||^2: the rotation need not be exactly orthogonal, so the
+            // coarse distance ||q - c_l||^2 is not reused here.
+            if (threadIdx.x < 32) {
+                const float* cl = rc + (long long)l * dim;
+                float acc = 0.0f;
+                for (int d = threadIdx.x; d < dim; d += 32) {
+                    const float df = qv[d] - cl[d];
+                    acc = fmaf(df, df, acc);
+                }
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (threadIdx.x == 0) s_base = acc;
+            }
+            __syncthreads();
+        } else if (threadIdx.x == 0) {
+            s_base = probe_d[pr];
+        }
+        __syncthreads();
+        const float base_d = s_base;
+        const uint64_t base = offs[l];
+        const long long L = (long long)(offs[l + 1] - base);
+        for (long long c0 = 0; c0 < L; c0 += SEL_CH) {
+            const int cn = (int)min((long long)SEL_CH, L - c0);
+            for (int i = threadIdx.x; i < carry_n; i += SEL_NT) buf[i] = S.carry_d[i];
+            for (int i = threadIdx.x; i < cn; i += SEL_NT) {
+                const uint64_t e = base + c0 + i;
+                const uint8_t* code = codes + e * (uint64_t)m;
+                float acc = 0.0f;
+                for (int s = 0; s < m; ++s) acc = __fadd_rn(acc, lut[s * ksub + code[s]]);
+                buf[carry_n + i] = __fadd_rn(__fadd_rn(base_d, vterm[e]), acc);
+            }
+            __syncthreads();
+            carry_n = carry_round<SEL_NT>(buf, carry_n, cn, k, S.carry_d, S.carry_tag, S.tag_tmp,
+                                          S.sortb, S.sel, (uint32_t)(base + c0));
+        }
+    }
+    for (int i = threadIdx.x; i < k; i += SEL_NT) {
+        if (i < carry_n) {
+            out_ids[q * k + i] = ids[S.carry_tag[i]];
+            out_d[q * k + i] = S.carry_d[i];
+        } else {
+            out_ids[q * k + i] = 0;
+            out_d[q * k + i] = carry_n > 0 ? S.carry_d[carry_n - 1] : 0.0f;
+        }
+    }
+    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)carry_n;
+}
+
+void launch_scan_fast(const float* rq, long long nq, int dim, const uint32_t* probe,
+                      const float* probe_d, const float* rc, int nprobe, const float* cb, int m, int ksub,
+                      int dsub,
+                      const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
+                      const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
+                      uint32_t* out_n, cudaStream_t st) {
+    if (nq <= 0) return;
+    if (k > kMaxK) throw CudaError("scan_fast: k exceeds the supported maximum");
+    const size_t smem = ((size_t)((dim + 3) & ~3) + (((size_t)m * ksub + 3) & ~(size_t)3) + kMaxK + SEL_CH) * sizeof(float) +
+                        sizeof(ScanSmemTail);
+    if (smem > 227 * 1024) throw CudaError("scan_fast: LUT does not fit in shared memory");
+    VGPU_CHECK(cudaFuncSetAttribute(scan_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    scan_fast_kernel<<<(unsigned)nq, SEL_NT, smem, st>>>(rq, dim, probe, probe_d, rc, nprobe, cb, m, ksub,
+                                                         dsub, list_offsets, codes, vterm, ids, k,
+                                                         out_ids, out_d, out_n);
+    VGPU_LAUNCH("scan_fast_kernel");
+}
+
+// =====================================================================================
+// Per-vector term of the fast scan, fp64: u(x) = sum_s ||y||^2 + 2 <(Rc_l)_s, y>.
+// One CTA per list.
+// =====================================================================================
+__global__ void __launch_bounds__(256) vector_terms_kernel(const float* __restrict__ rc, int dim,
+                                                           const float* __restrict__ cb, int m,
+                                                           int ksub, int dsub,
+                                                           const uint64_t* __restrict__ offs,
+                                                           const uint8_t* __restrict__ codes,
+                                                           float* __restrict__ vterm) {
+    const int l = blockIdx.x;
+    const float* c = rc + (long long)l * dim;
+    for (uint64_t e = offs[l] + threadIdx.x; e < offs[l + 1]; e += blockDim.x) {
+        const uint8_t* code = codes + e * (uint64_t)m;
+        double u = 0.0;
+        for (int s = 0; s < m; ++s) {
+            const float* y = cb + ((long long)s * ksub + code[s]) * dsub;
+            const float* cs = c + s * dsub;
+            for (int t = 0; t < dsub; ++t) {
+                const double yv = y[t];
+                u += yv * yv + 2.0 * (double)cs[t] * yv;
+            }
+        }
+        vterm[e] = (float)u;
+    }
+}
+
+void launch_vector_terms(const float* rc, int nlist, int dim, const float* cb, int m, int ksub,
+                         int dsub, const uint64_t* list_offsets, const uint8_t* codes,
+                         long long n_entries, float* vterm, cudaStream_t st) {
+    if (nlist <= 0 || n_entries <= 0) return;
+    vector_terms_kernel<<<nlist, 256, 0, st>>>(rc, dim, cb, m, ksub, dsub, list_offsets, codes, vterm);
+    VGPU_LAUNCH("vector_terms_kernel");
+}
+
+// Sum of the probed lists' sizes (bytes scanned = this * m): one atomic per warp.
+__global__ void probe_sizes_kernel(const uint32_t* __restrict__ probe, long long n,
+                                   const uint64_t* __restrict__ offs, unsigned long long* out) {
+    unsigned long long s = 0;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint32_t l = probe[i];
+        s += offs[l + 1] - offs[l];
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0 && s) atomicAdd(out, s);
+}
+
+void launch_probe_sizes(const uint32_t* probe, long long n, const uint64_t* list_offsets,
+                        unsigned long long* out, cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 4);
+    probe_sizes_kernel<<<blocks, 256, 0, st>>>(probe, n, list_offsets, out);
+    VGPU_LAUNCH("probe_sizes_kernel");
+}
+
+// =====================================================================================
+// CSR maintenance for add().
+// =====================================================================================
+__global__ void csr_move_kernel(const uint8_t* __restrict__ old_codes, const uint64_t* __restrict__ old_ids,
+                                const uint64_t* __restrict__ old_off, const uint64_t* __restrict__ new_off,
+                                int m, uint8_t* __restrict__ codes, uint64_t* __restrict__ ids) {
+    const int l = blockIdx.x;
+    const uint64_t ob = old_off[l], nb = new_off[l];
+    const uint64_t len = old_off[l + 1] - ob;
+    for (uint64_t i = threadIdx.x; i < len; i += blockDim.x) ids[nb + i] = old_ids[ob + i];
+    for (uint64_t b = threadIdx.x; b < len * m; b += blockDim.x) codes[nb * m + b] = old_codes[ob * m + b];
+}
+
+__global__ void csr_scatter_kernel(const uint8_t* __restrict__ new_codes, const uint64_t* __restrict__ new_ids,
+                                   const uint64_t* __restrict__ dest, long long n, int m,
+                                   uint8_t* __restrict__ codes, uint64_t* __restrict__ ids) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint64_t d = dest[i];
+        ids[d] = new_ids[i];
+        for (int s = 0; s < m; ++s) codes[d * m + s] = new_codes[i * m + s];
+    }
+}
+
+void launch_csr_move(const uint8_t* old_codes, const uint64_t* old_ids, const uint64_t* old_off,
+                     const uint64_t* new_off, int nlist, int m, uint8_t* codes, uint64_t* ids,
+                     cudaStream_t st) {
+    if (nlist <= 0) return;
+    csr_move_kernel<<<nlist, 256, 0, st>>>(old_codes, old_ids, old_off, new_off, m, codes, ids);
+    VGPU_LAUNCH("csr_move_kernel");
+}
+
+void launch_csr_scatter(const uint8_t* new_codes, const uint64_t* new_ids, const uint64_t* dest,
+                        long long n, int m, uint8_t* codes, uint64_t* ids, cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+    csr_scatter_kernel<<<blocks, 256, 0, st>>>(new_codes, new_ids, dest, n, m, codes, ids);
+    VGPU_LAUNCH("csr_scatter_kernel");
+}
+
+}  // namespace vgpu

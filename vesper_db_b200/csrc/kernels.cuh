@@ -1,0 +1,104 @@
+// Launch wrappers for the B200 IVF-PQ kernels (definitions in ivfpq_kernels.cu and
+// kmeans_kernels.cu).  All pointers are device pointers; all launches go to `st`.
+#pragma once
+
+#include "common.cuh"
+
+namespace vgpu {
+
+constexpr int kMaxK = 1024;        // largest k / nprobe the selection kernels accept
+constexpr int kScanChunk = 2048;   // list entries scored per selection round
+
+// D[i][j] = ||x_i - c_j||^2 in reference lane order, for i < nx, j < nc; D row stride ldd.
+void launch_l2_dist(const float* x, long long nx, const float* c, int nc, int dim, float* D,
+                    long long ldd, cudaStream_t st);
+
+// Per row of D (n_rows x ncols, stride ldd): the k smallest (value, column) pairs in
+// ascending order -> out_idx[row*k + t], out_val[row*k + t].
+void launch_row_topk(const float* D, long long n_rows, int ncols, long long ldd, int k,
+                     uint32_t* out_idx, float* out_val, cudaStream_t st);
+
+// Per row: arg-min with a strict `<` scan from FLT_MAX (lowest column wins ties);
+// when `keep` is given, a row keeps keep[row] if that column ties the minimum
+// (Elkan's assignment rule).  Writes the index and the minimum.
+void launch_row_argmin(const float* D, long long n_rows, int ncols, long long ldd,
+                       const uint32_t* keep, uint32_t* out_idx, float* out_val, cudaStream_t st);
+
+// out[r][j] = sum_k (x[xrow(r)][k] - c[crow(r)][k]) * R[k][j], sequential in k with a
+// rounded product and a rounded add (apply_rotation order).  xrow(r) = xidx ? xidx[r] : r,
+// crow(r) = cidx ? cidx[r] : -1 (no subtraction when cidx is null).  R may be null
+// (plain residual copy).
+void launch_residual_rotate(const float* x, const uint32_t* xidx, const float* c,
+                            const uint32_t* cidx, long long rows, int dim, const float* R,
+                            float* out, cudaStream_t st);
+
+// codes[i][s] = arg-min_j l2(x_i[s*dsub:(s+1)*dsub], cb[s][j]) (strict <, lowest j).
+void launch_pq_encode(const float* x, long long n, int m, int ksub, int dsub, const float* cb,
+                      uint8_t* codes, cudaStream_t st);
+
+// Exact per-(query, probe) LUT + scan + local top-k.  pair p = (q, t) with list
+// probe[q*nprobe + t]; residuals either given per pair (rres: rotated residual rows,
+// one per pair) or formed as query - centroid.  Output per pair: up to k candidates
+// sorted by (distance, list position) in cand_d / cand_pos, count in cand_n.
+void launch_scan_exact(const float* queries, long long nq, int dim, const float* centroids,
+                       const float* rres, const uint32_t* probe, int nprobe, const float* cb, int m,
+                       int ksub, int dsub, const uint64_t* list_offsets, const uint8_t* codes,
+                       int k, float* cand_d, uint32_t* cand_pos, uint32_t* cand_n,
+                       cudaStream_t st);
+
+// Per query: merge nprobe sorted candidate runs into the final top-k by
+// (distance, probe rank, list position); map to ids; pad short results the way the
+// reference C ABI does (ids 0, distance = last valid or 0).
+void launch_merge(const float* cand_d, const uint32_t* cand_pos, const uint32_t* cand_n,
+                  long long nq, int nprobe, int k, const uint32_t* probe,
+                  const uint64_t* list_offsets, const uint64_t* ids, uint64_t* out_ids,
+                  float* out_d, uint32_t* out_n, cudaStream_t st);
+
+// Fast search path (distances within fp32 rounding of the exact ones):
+// dist(q, x) = ||q - c_l||^2 + u(x) + sum_s T_q[s][code_s(x)].
+// T_q[s][j] = -2 <(Rq)_s, y_sj> is built per query in shared memory; u(x) is the
+// per-vector term stored at add time.  One CTA per query scans all its probed lists.
+// rc (rotated centroids) given -> the per-list base term is ||Rq - Rc_l||^2 computed
+// in the kernel; rc null -> the coarse distance probe_d is the base term.
+void launch_scan_fast(const float* rq, long long nq, int dim, const uint32_t* probe,
+                      const float* probe_d, const float* rc, int nprobe, const float* cb, int m, int ksub,
+                      int dsub,
+                      const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
+                      const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
+                      uint32_t* out_n, cudaStream_t st);
+
+// u(x) = sum_s ( ||y_s,c_s||^2 + 2 <(R c_l)_s, y_s,c_s> ) for every CSR entry, with
+// rc = rotated centroids [nlist x dim]; accumulated in fp64, rounded once.
+void launch_vector_terms(const float* rc, int nlist, int dim, const float* cb, int m, int ksub,
+                         int dsub, const uint64_t* list_offsets, const uint8_t* codes,
+                         long long n_entries, float* vterm, cudaStream_t st);
+
+// Plain fp32 GEMM-like product out = x * R (no ordering guarantee; used only for the
+// fast path's Rq and Rc, which are inside the fast path's tolerance).
+void launch_rotate_fast(const float* x, long long rows, int dim, const float* R, float* out,
+                        cudaStream_t st);
+
+// *out += sum over the n probe entries of the probed list's size.
+void launch_probe_sizes(const uint32_t* probe, long long n, const uint64_t* list_offsets,
+                        unsigned long long* out, cudaStream_t st);
+
+// CSR rebuild helpers for add(): move old entries to their new offsets, scatter new
+// entries to precomputed destinations.
+void launch_csr_move(const uint8_t* old_codes, const uint64_t* old_ids, const uint64_t* old_off,
+                     const uint64_t* new_off, int nlist, int m, uint8_t* codes, uint64_t* ids,
+                     cudaStream_t st);
+void launch_csr_scatter(const uint8_t* new_codes, const uint64_t* new_ids, const uint64_t* dest,
+                        long long n, int m, uint8_t* codes, uint64_t* ids, cudaStream_t st);
+
+// ----------------------------------------------------------------------- k-means
+// k-means++ D^2 update: mind[i] = min(mind[i], l2(x_i, c)).
+void launch_kpp_update(const float* x, long long n, int dim, const float* c, float* mind,
+                       cudaStream_t st);
+// Segmented M-step.  order: point indices grouped by cluster (ascending within a
+// cluster), seg: [k+1] offsets.  kahan=1 -> Kahan fp64 sum times (1/count)
+// (KmeansElkan update_centroid); kahan=0 -> fp64 sum / count (Lloyd).  Empty clusters
+// keep their centroid.
+void launch_segment_mean(const float* x, int dim, const uint32_t* order, const uint32_t* seg,
+                         int k, int kahan, float* centroids, cudaStream_t st);
+
+}  // namespace vgpu

@@ -1,0 +1,99 @@
+// B200 kernels for k-means training (coarse quantizer and PQ sub-quantizers).
+//
+//   * kpp_update: the D^2 refresh of k-means++ (src/index/kmeans.cpp:61-67), one
+//     reference-order distance per point.
+//   * points are grouped by cluster with a stable sort (group_by_key in
+//     train_kernels.cu), so the M-step sums points in the order the reference
+//     gathers them (src/index/kmeans_elkan.cpp:354-356).
+//   * segment_mean: the M-step as a segmented reduction.  One thread owns one
+//     (cluster, dimension) pair and walks the cluster's points in order:
+//       kahan = 1: Kahan-compensated fp64 sum times (1/count) (update_centroid,
+//                  src/index/kmeans_elkan.cpp:31-56);
+//       kahan = 0: plain fp64 sum divided by count (kmeans_update_centroids,
+//                  src/index/kmeans.cpp:107-135).
+//     Empty clusters keep their previous centroid in both.
+#include <cfloat>
+
+#include "kernels.cuh"
+
+namespace vgpu {
+
+__global__ void kpp_update_kernel(const float* __restrict__ x, long long n, int dim,
+                                  const float* __restrict__ c, float* __restrict__ mind) {
+    // One warp per point: lanes 0..7 hold the eight lane accumulators of a strided
+    // walk; lane l accumulates elements l, l+8, l+16, ... in order, exactly as lane l
+    // of the AVX2 kernel does.  Lanes 8..31 idle on the FMA chain (the chain length
+    // is dim/8, so this stays memory-bound).
+    const int lane = threadIdx.x & 31;
+    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    const int simd_end = dim & ~7;
+    for (long long i = warp; i < n; i += nwarps) {
+        const float* p = x + i * dim;
+        float acc = 0.0f;
+        if (lane < 8)
+            for (int t = lane; t < simd_end; t += 8) {
+                const float d = __fsub_rn(p[t], c[t]);
+                acc = __fmaf_rn(d, d, acc);
+            }
+        // hsum8 over lanes 0..7: ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7))
+        const float a4 = __shfl_down_sync(0xffffffffu, acc, 4);
+        const float s = __fadd_rn(a4, acc);          // lanes 0..3: s_l = a_{l+4} + a_l
+        const float s1 = __shfl_down_sync(0xffffffffu, s, 1);
+        const float s2 = __shfl_down_sync(0xffffffffu, s, 2);
+        const float s3 = __shfl_down_sync(0xffffffffu, s, 3);
+        if (lane == 0) {
+            float r = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+            for (int t = simd_end; t < dim; ++t) {
+                const float d = __fsub_rn(p[t], c[t]);
+                r = __fadd_rn(r, __fmul_rn(d, d));
+            }
+            const float old = mind[i];
+            mind[i] = r < old ? r : old;   // std::min(old, r)
+        }
+    }
+}
+
+void launch_kpp_update(const float* x, long long n, int dim, const float* c, float* mind,
+                       cudaStream_t st) {
+    if (n <= 0) return;
+    const long long warps = n;
+    const int blocks = (int)std::min<long long>((warps * 32 + 255) / 256, 148LL * 64);
+    kpp_update_kernel<<<blocks, 256, 0, st>>>(x, n, dim, c, mind);
+    VGPU_LAUNCH("kpp_update_kernel");
+}
+
+__global__ void segment_mean_kernel(const float* __restrict__ x, int dim,
+                                    const uint32_t* __restrict__ order,
+                                    const uint32_t* __restrict__ seg, int kahan,
+                                    float* __restrict__ centroids) {
+    const int c = blockIdx.x;
+    const uint32_t b = seg[c], e = seg[c + 1];
+    if (b == e) return;  // empty cluster keeps its centroid
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+        double sum = 0.0, comp = 0.0;
+        if (kahan) {
+            for (uint32_t j = b; j < e; ++j) {
+                const double y = (double)x[(long long)order[j] * dim + d] - comp;
+                const double t = sum + y;
+                comp = (t - sum) - y;
+                sum = t;
+            }
+            const double scale = 1.0 / (double)(e - b);
+            centroids[(long long)c * dim + d] = (float)(sum * scale);
+        } else {
+            for (uint32_t j = b; j < e; ++j) sum += (double)x[(long long)order[j] * dim + d];
+            centroids[(long long)c * dim + d] = (float)(sum / (double)(e - b));
+        }
+    }
+}
+
+void launch_segment_mean(const float* x, int dim, const uint32_t* order, const uint32_t* seg,
+                         int k, int kahan, float* centroids, cudaStream_t st) {
+    if (k <= 0) return;
+    const int threads = dim >= 256 ? 256 : ((dim + 31) / 32) * 32;
+    segment_mean_kernel<<<k, threads, 0, st>>>(x, dim, order, seg, kahan, centroids);
+    VGPU_LAUNCH("segment_mean_kernel");
+}
+
+}  // namespace vgpu

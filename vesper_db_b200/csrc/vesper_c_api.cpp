@@ -1,0 +1,377 @@
+// C ABI of the B200 IVF-PQ engine: the reference's vesper_ivfpq_* surface
+// (include/vesper/c/vesper.h, src/c/vesper_c_api.cpp) over vesper::index::IvfPqIndex,
+// plus the extensions declared in include/vesper_b200.h.
+//
+// Status mapping follows the reference: NULL arguments -> INVALID_PARAM without
+// touching the last error; an error returned by train/add/search -> INVALID_PARAM
+// with its message; save/load -> IO; std::exception -> INTERNAL; anything else ->
+// UNKNOWN.  The last error is a thread-local string.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <memory>
+#include <new>
+#include <string>
+
+#include "../../include/vesper_b200.h"
+#include "ivf_pq_gpu.hpp"
+
+using vesper::index::IvfPqIndex;
+using vesper::index::IvfPqSearchParams;
+using vesper::index::IvfPqTrainParams;
+using vesper::index::IvfPqTrainStats;
+using vesper::index::SearchMode;
+
+struct vesper_index_t {
+    std::unique_ptr<IvfPqIndex> ivfpq;
+    IvfPqTrainStats last_train;
+};
+
+namespace {
+thread_local std::string g_last_error;
+void set_error(const std::string& s) { g_last_error = s; }
+void clear_error() { g_last_error.clear(); }
+
+template <class F>
+vesper_status_t guarded(const char* what, F&& f) {
+    try {
+        return f();
+    } catch (const std::bad_alloc&) {
+        set_error("allocation failure");
+        return VESPER_ERROR_INTERNAL;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return VESPER_ERROR_INTERNAL;
+    } catch (...) {
+        set_error(std::string("unknown error in ") + what);
+        return VESPER_ERROR_UNKNOWN;
+    }
+}
+
+// Pad rows beyond counts[q] the way the reference does (vesper_c_api.cpp:243-253).
+// The engine already pads; this keeps the contract explicit for search().
+}  // namespace
+
+extern "C" {
+
+VESPER_C_API const char* vesper_get_last_error(void) { return g_last_error.c_str(); }
+VESPER_C_API const char* vesper_version(void) { return "dev"; }
+
+VESPER_C_API vesper_status_t vesper_ivfpq_is_trained(const vesper_index_t* index, int* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("is_trained", [&] { *out = index->ivfpq->is_trained() ? 1 : 0; return VESPER_OK; });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_dimension(const vesper_index_t* index, size_t* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("get_dimension", [&] { *out = index->ivfpq->dimension(); return VESPER_OK; });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_stats(const vesper_index_t* index, vesper_ivfpq_stats_t* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("get_stats", [&] {
+        const auto s = index->ivfpq->get_stats();
+        out->n_vectors = s.n_vectors;
+        out->n_lists = s.n_lists;
+        out->m = s.m;
+        out->memory_bytes = s.memory_bytes;
+        out->avg_list_size = s.avg_list_size;
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_set_metadata_json(vesper_index_t* index, const char* json) {
+    if (!index || !index->ivfpq || !json) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("set_metadata_json", [&] { index->ivfpq->set_metadata_json(json); return VESPER_OK; });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_metadata_json(const vesper_index_t* index, char* out_buffer,
+                                                            size_t buffer_size, size_t* out_required) {
+    if (!index || !index->ivfpq) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("get_metadata_json", [&] {
+        const std::string s = index->ivfpq->get_metadata_json();
+        const size_t required = s.size() + 1;
+        if (out_required) *out_required = required;
+        if (!out_buffer || buffer_size == 0) return VESPER_OK;
+        if (buffer_size < required) {
+            set_error("buffer too small for metadata json");
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        std::memcpy(out_buffer, s.c_str(), required);
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_create(vesper_index_t** out_index) {
+    if (!out_index) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("create", [&] {
+        auto h = std::make_unique<vesper_index_t>();
+        h->ivfpq = std::make_unique<IvfPqIndex>();
+        *out_index = h.release();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_destroy(vesper_index_t* index) {
+    clear_error();
+    return guarded("destroy", [&] { delete index; return VESPER_OK; });
+}
+
+static vesper_status_t do_train(vesper_index_t* index, const float* base, size_t dim, size_t n,
+                                const IvfPqTrainParams& tp, bool on_device = false) {
+    return guarded("train", [&] {
+        auto r = index->ivfpq->train_device(base, dim, n, tp, on_device);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        index->last_train = *r;
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_train(vesper_index_t* index, const float* base, size_t dim,
+                                                size_t n, const vesper_ivfpq_train_params_t* params) {
+    if (!index || !index->ivfpq || !base || !params || dim == 0 || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    IvfPqTrainParams tp;
+    tp.nlist = params->nlist;
+    tp.m = params->m;
+    tp.nbits = params->nbits;
+    tp.timings_enabled = false;
+    return do_train(index, base, dim, n, tp);
+}
+
+VESPER_C_API void vesper_ivfpq_train_params_ex_init(vesper_ivfpq_train_params_ex_t* p) {
+    if (!p) return;
+    std::memset(p, 0, sizeof(*p));
+    p->struct_size = sizeof(*p);
+    p->nlist = 256;
+    p->m = 8;
+    p->nbits = 8;
+    p->max_iter = 25;
+    p->epsilon = 1e-4f;
+    p->use_opq = 1;
+    p->opq_iter = 10;
+    p->opq_sample_n = 20000;
+    p->opq_init_pca = 1;
+    p->seed = 42;
+}
+
+static IvfPqTrainParams to_params(const vesper_ivfpq_train_params_ex_t* p) {
+    IvfPqTrainParams tp;
+    tp.nlist = p->nlist;
+    tp.m = p->m;
+    tp.nbits = p->nbits;
+    tp.max_iter = p->max_iter;
+    tp.epsilon = p->epsilon;
+    tp.use_opq = p->use_opq != 0;
+    tp.opq_iter = p->opq_iter;
+    tp.opq_sample_n = p->opq_sample_n;
+    tp.opq_init = p->opq_init_pca ? vesper::index::OpqInit::PCA : vesper::index::OpqInit::Identity;
+    tp.seed = p->seed;
+    tp.verbose = p->verbose != 0;
+    return tp;
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_train_ex(vesper_index_t* index, const float* base, size_t dim,
+                                                   size_t n, const vesper_ivfpq_train_params_ex_t* p) {
+    if (!index || !index->ivfpq || !base || !p || dim == 0 || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < sizeof(vesper_ivfpq_train_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return do_train(index, base, dim, n, to_params(p), false);
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_train_ex_device(vesper_index_t* index, const float* d_base, size_t dim,
+                                                          size_t n, const vesper_ivfpq_train_params_ex_t* p) {
+    if (!index || !index->ivfpq || !d_base || !p || dim == 0 || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < sizeof(vesper_ivfpq_train_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return do_train(index, d_base, dim, n, to_params(p), true);
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_add_device(vesper_index_t* index, const uint64_t* d_ids,
+                                                     const float* d_base, size_t n) {
+    if (!index || !index->ivfpq || !d_ids || !d_base || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("add", [&] {
+        auto r = index->ivfpq->add_device(d_ids, d_base, n, true);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_train_report(const vesper_index_t* index,
+                                                           vesper_ivfpq_train_report_t* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    out->opq_kept = index->last_train.opq_kept ? 1 : 0;
+    out->err_unrot = index->last_train.err_unrot;
+    out->err_opq = index->last_train.err_opq;
+    out->coarse_iterations = index->last_train.coarse_iterations;
+    out->train_time_sec = index->last_train.train_time_sec;
+    return VESPER_OK;
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_add(vesper_index_t* index, const uint64_t* ids, const float* base,
+                                              size_t n) {
+    if (!index || !index->ivfpq || !ids || !base || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("add", [&] {
+        auto r = index->ivfpq->add(ids, base, n);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
+static vesper_status_t do_search(const vesper_index_t* index, const float* q, size_t nq, uint32_t k,
+                                 uint32_t nprobe, uint32_t mode, uint64_t* ids, float* d, uint32_t* counts,
+                                 bool on_device) {
+    IvfPqSearchParams sp;
+    sp.k = k;
+    sp.nprobe = nprobe;
+    sp.mode = mode == VESPER_SEARCH_EXACT ? SearchMode::Exact : SearchMode::Fast;
+    return guarded("search", [&] {
+        auto r = index->ivfpq->search_batch_flat(q, nq, sp, ids, d, counts, on_device);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_search(const vesper_index_t* index, const float* query,
+                                                 const vesper_ivfpq_search_params_t* params, uint64_t* out_ids,
+                                                 float* out_d) {
+    if (!index || !index->ivfpq || !query || !params || !out_ids || !out_d) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return do_search(index, query, 1, params->k, params->nprobe, VESPER_SEARCH_FAST, out_ids, out_d, nullptr,
+                     false);
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch(const vesper_index_t* index, const float* queries,
+                                                       size_t nq, const vesper_ivfpq_search_params_t* params,
+                                                       uint64_t* out_ids, float* out_d) {
+    if (!index || !index->ivfpq || !queries || !params || !out_ids || !out_d || nq == 0)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return do_search(index, queries, nq, params->k, params->nprobe, VESPER_SEARCH_FAST, out_ids, out_d, nullptr,
+                     false);
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_ex(const vesper_index_t* index, const float* queries,
+                                                          size_t nq, const vesper_ivfpq_search_params_ex_t* p,
+                                                          uint64_t* out_ids, float* out_d, uint32_t* out_counts) {
+    if (!index || !index->ivfpq || !queries || !p || !out_ids || !out_d || nq == 0)
+        return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < sizeof(vesper_ivfpq_search_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return do_search(index, queries, nq, p->k, p->nprobe, p->mode, out_ids, out_d, out_counts, false);
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device(const vesper_index_t* index, const float* d_q,
+                                                              size_t nq, const vesper_ivfpq_search_params_ex_t* p,
+                                                              uint64_t* d_ids, float* d_d, uint32_t* d_counts) {
+    if (!index || !index->ivfpq || !d_q || !p || !d_ids || !d_d || nq == 0) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < sizeof(vesper_ivfpq_search_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return do_search(index, d_q, nq, p->k, p->nprobe, p->mode, d_ids, d_d, d_counts, true);
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index, vesper_ivfpq_timings_t* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    const auto t = index->ivfpq->last_search_timings();
+    out->coarse_ms = t.coarse_ms;
+    out->select_ms = t.select_ms;
+    out->rotate_ms = t.rotate_ms;
+    out->scan_ms = t.scan_ms;
+    out->merge_ms = t.merge_ms;
+    out->total_ms = t.total_ms;
+    out->scanned_entries = t.scanned_entries;
+    return VESPER_OK;
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_set_model(vesper_index_t* index, size_t dim, uint32_t nlist, uint32_t m,
+                                                    uint32_t nbits, const float* centroids, const float* codebooks,
+                                                    const float* rotation) {
+    if (!index || !index->ivfpq || !centroids || !codebooks) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("set_model", [&] {
+        auto r = index->ivfpq->set_model(dim, nlist, m, nbits, centroids, codebooks, rotation);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_lists(const vesper_index_t* index, uint64_t* out_offsets,
+                                                    uint64_t* out_ids, uint8_t* out_codes) {
+    if (!index || !index->ivfpq) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("get_lists", [&] {
+        if (out_offsets) {
+            const auto o = index->ivfpq->list_offsets();
+            std::memcpy(out_offsets, o.data(), o.size() * sizeof(uint64_t));
+        }
+        if (out_ids) {
+            const auto v = index->ivfpq->list_ids();
+            std::memcpy(out_ids, v.data(), v.size() * sizeof(uint64_t));
+        }
+        if (out_codes) {
+            const auto v = index->ivfpq->list_codes();
+            std::memcpy(out_codes, v.data(), v.size());
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_save(const vesper_index_t* index, const char* file_path) {
+    if (!index || !index->ivfpq || !file_path) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("save", [&] {
+        auto r = index->ivfpq->save(file_path);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_IO;
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_load(vesper_index_t* index, const char* file_path) {
+    if (!index || !file_path) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("load", [&] {
+        auto r = IvfPqIndex::load(file_path);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_IO;
+        }
+        index->ivfpq = std::make_unique<IvfPqIndex>(std::move(*r));
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API int vesper_b200_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+}  // extern "C"
