@@ -96,6 +96,7 @@ typedef struct vesper_ivfpq_timings_s {
   float merge_ms;    /* per-query merge (EXACT mode) */
   float total_ms;
   uint64_t scanned_entries; /* sum over queries of the probed lists' sizes */
+  uint32_t kernel_launches; /* kernels launched by the call */
 } vesper_ivfpq_timings_t;
 VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index,
                                                            vesper_ivfpq_timings_t* out);

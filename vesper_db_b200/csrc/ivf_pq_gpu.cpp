@@ -124,7 +124,7 @@ public:
     mutable SearchTimings timings;
 
     // search workspace (grow-only), guarded by mu
-    mutable DeviceBuffer<float> w_q, w_D, w_probe_d, w_rq, w_rres, w_cand_d, w_out_d;
+    mutable DeviceBuffer<float> w_q, w_D, w_probe_d, w_rq, w_rres, w_cand_d, w_out_d, w_T;
     mutable DeviceBuffer<uint32_t> w_probe, w_cand_pos, w_cand_n, w_out_n, w_pair_q;
     mutable DeviceBuffer<uint64_t> w_out_ids;
     mutable DeviceBuffer<unsigned long long> w_scanned;
@@ -681,6 +681,7 @@ public:
             }
         } else {
             w_rq.reserve(qc * dim);
+            w_T.reserve(qc * (size_t)m() * ksub);
         }
         SearchTimings tm;
         w_scanned.reserve(1);
@@ -734,14 +735,17 @@ public:
                     vgpu::launch_rotate_fast(dq, (long long)nc, (int)dim, d_rot.data(), w_rq.data(), st);
                     rq = w_rq.data();
                 }
+                vgpu::launch_lut_fast(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)ksub, (int)dsub,
+                                      w_T.data(), st);
                 cudaEventRecord(ev[3], st);
-                vgpu::launch_scan_fast(rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
-                                       has_rot ? d_rc.data() : nullptr, (int)np,
-                                       d_cb.data(), (int)m(), (int)ksub, (int)dsub, d_offs.data(), d_codes.data(),
-                                       d_vterm.data(), d_ids.data(), (int)k, oid, od, on, st);
+                vgpu::launch_scan_fast2(w_T.data(), rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
+                                        has_rot ? d_rc.data() : nullptr, (int)np, (int)m(), (int)ksub,
+                                        d_offs.data(), d_codes.data(), d_vterm.data(), d_ids.data(), (int)k,
+                                        oid, od, on, st);
                 cudaEventRecord(ev[4], st);
             }
             cudaEventRecord(ev[5], st);
+            tm.kernel_launches += 3 + (exact ? 2 : 2) + (has_rot ? 1 : 0);
             if (!on_device) {
                 d2h(out_ids + q0 * k, oid, nc * k, st);
                 d2h(out_d + q0 * k, od, nc * k, st);

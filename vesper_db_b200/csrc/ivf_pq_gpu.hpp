@@ -106,6 +106,7 @@ struct IvfPqTrainStats {
 struct SearchTimings {
     float coarse_ms{0}, select_ms{0}, rotate_ms{0}, scan_ms{0}, merge_ms{0}, total_ms{0};
     std::uint64_t scanned_entries{0};   // sum over queries of the probed lists' sizes
+    std::uint32_t kernel_launches{0};   // kernels this library launched for the call
 };
 
 class IvfPqIndex {

@@ -5,7 +5,7 @@
 //   * rotations as sequential-k dots with a rounded multiply and a rounded add
 //     (apply_rotation, src/index/ivf_pq.cpp:2947-2968),
 //   * ADC sums in sub-quantizer order from 0.0f (pq_fastscan.hpp:284-317).
-// The fast scan (scan_fast_kernel) regroups the ADC algebra so the lookup table is
+// The fast scan (lut_fast_kernel + scan_fast2_kernel) regroups the ADC algebra so the table is
 // built once per query instead of once per (query, list); its distances agree with
 // the exact ones to fp32 rounding.
 #include <cfloat>
@@ -580,106 +580,6 @@ void launch_merge(const float* cand_d, const uint32_t* cand_pos, const uint32_t*
 }
 
 // =====================================================================================
-// Fast scan: one CTA per query.  T_q[s][j] = -2 <(Rq)_s, y_sj> lives in shared memory
-// for the whole query; each entry's distance is (||q - c_l||^2 + u(x)) + sum_s T_q.
-// The running top-k is carried across chunks and lists in scan order.
-// =====================================================================================
-__global__ void __launch_bounds__(SEL_NT) scan_fast_kernel(
-    const float* __restrict__ rq, int dim, const uint32_t* __restrict__ probe,
-    const float* __restrict__ probe_d, const float* __restrict__ rc, int nprobe,
-    const float* __restrict__ cb, int m, int ksub,
-    int dsub, const uint64_t* __restrict__ offs, const uint8_t* __restrict__ codes,
-    const float* __restrict__ vterm, const uint64_t* __restrict__ ids, int k,
-    uint64_t* __restrict__ out_ids, float* __restrict__ out_d, uint32_t* __restrict__ out_n) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const long long q = blockIdx.x;
-    float* qv = reinterpret_cast<float*>(smem_raw);                       // [dim]
-    float* lut = qv + ((dim + 3) & ~3);                                   // [m * ksub]
-    float* buf = lut + (((size_t)m * ksub + 3) & ~(size_t)3);                                  // [kMaxK + SEL_CH]
-    ScanSmemTail& S = *reinterpret_cast<ScanSmemTail*>(buf + kMaxK + SEL_CH);
-    for (int d = threadIdx.x; d < dim; d += SEL_NT) qv[d] = rq[q * dim + d];
-    __syncthreads();
-    for (int e = threadIdx.x; e < m * ksub; e += SEL_NT) {
-        const int s = e / ksub, j = e % ksub;
-        const float* y = cb + ((long long)s * ksub + j) * dsub;
-        const float* v = qv + s * dsub;
-        float acc = 0.0f;
-        for (int t = 0; t < dsub; ++t) acc = __fmaf_rn(v[t], y[t], acc);
-        lut[e] = -2.0f * acc;
-    }
-    __syncthreads();
-    __shared__ float s_base;
-    int carry_n = 0;
-    for (int t = 0; t < nprobe; ++t) {
-        const long long pr = q * nprobe + t;
-        const uint32_t l = probe[pr];
-        if (rc) {
-            // ||Rq - Rc_l||^2: the rotation need not be exactly orthogonal, so the
-            // coarse distance ||q - c_l||^2 is not reused here.
-            if (threadIdx.x < 32) {
-                const float* cl = rc + (long long)l * dim;
-                float acc = 0.0f;
-                for (int d = threadIdx.x; d < dim; d += 32) {
-                    const float df = qv[d] - cl[d];
-                    acc = fmaf(df, df, acc);
-                }
-                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                if (threadIdx.x == 0) s_base = acc;
-            }
-            __syncthreads();
-        } else if (threadIdx.x == 0) {
-            s_base = probe_d[pr];
-        }
-        __syncthreads();
-        const float base_d = s_base;
-        const uint64_t base = offs[l];
-        const long long L = (long long)(offs[l + 1] - base);
-        for (long long c0 = 0; c0 < L; c0 += SEL_CH) {
-            const int cn = (int)min((long long)SEL_CH, L - c0);
-            for (int i = threadIdx.x; i < carry_n; i += SEL_NT) buf[i] = S.carry_d[i];
-            for (int i = threadIdx.x; i < cn; i += SEL_NT) {
-                const uint64_t e = base + c0 + i;
-                const uint8_t* code = codes + e * (uint64_t)m;
-                float acc = 0.0f;
-                for (int s = 0; s < m; ++s) acc = __fadd_rn(acc, lut[s * ksub + code[s]]);
-                buf[carry_n + i] = __fadd_rn(__fadd_rn(base_d, vterm[e]), acc);
-            }
-            __syncthreads();
-            carry_n = carry_round<SEL_NT>(buf, carry_n, cn, k, S.carry_d, S.carry_tag, S.tag_tmp,
-                                          S.sortb, S.sel, (uint32_t)(base + c0));
-        }
-    }
-    for (int i = threadIdx.x; i < k; i += SEL_NT) {
-        if (i < carry_n) {
-            out_ids[q * k + i] = ids[S.carry_tag[i]];
-            out_d[q * k + i] = S.carry_d[i];
-        } else {
-            out_ids[q * k + i] = 0;
-            out_d[q * k + i] = carry_n > 0 ? S.carry_d[carry_n - 1] : 0.0f;
-        }
-    }
-    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)carry_n;
-}
-
-void launch_scan_fast(const float* rq, long long nq, int dim, const uint32_t* probe,
-                      const float* probe_d, const float* rc, int nprobe, const float* cb, int m, int ksub,
-                      int dsub,
-                      const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
-                      const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
-                      uint32_t* out_n, cudaStream_t st) {
-    if (nq <= 0) return;
-    if (k > kMaxK) throw CudaError("scan_fast: k exceeds the supported maximum");
-    const size_t smem = ((size_t)((dim + 3) & ~3) + (((size_t)m * ksub + 3) & ~(size_t)3) + kMaxK + SEL_CH) * sizeof(float) +
-                        sizeof(ScanSmemTail);
-    if (smem > 227 * 1024) throw CudaError("scan_fast: LUT does not fit in shared memory");
-    VGPU_CHECK(cudaFuncSetAttribute(scan_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    scan_fast_kernel<<<(unsigned)nq, SEL_NT, smem, st>>>(rq, dim, probe, probe_d, rc, nprobe, cb, m, ksub,
-                                                         dsub, list_offsets, codes, vterm, ids, k,
-                                                         out_ids, out_d, out_n);
-    VGPU_LAUNCH("scan_fast_kernel");
-}
-
-// =====================================================================================
 // Per-vector term of the fast scan, fp64: u(x) = sum_s ||y||^2 + 2 <(Rc_l)_s, y>.
 // One CTA per list.
 // =====================================================================================
@@ -773,6 +673,238 @@ void launch_csr_scatter(const uint8_t* new_codes, const uint64_t* new_ids, const
     const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
     csr_scatter_kernel<<<blocks, 256, 0, st>>>(new_codes, new_ids, dest, n, m, codes, ids);
     VGPU_LAUNCH("csr_scatter_kernel");
+}
+
+}  // namespace vgpu
+
+namespace vgpu {
+
+// =====================================================================================
+// Fast path, stage 1: per-query lookup tables for a batch of queries,
+//   T[q][s][j] = -2 <(Rq)_s, y_sj>.
+// CTA = (32 queries, one sub-space): the sub-space codebook is staged once in shared
+// memory (transposed, so consecutive codewords are consecutive banks) and reused by
+// all 32 queries; outputs are written coalesced along j.
+// =====================================================================================
+__global__ void __launch_bounds__(256) lut_fast_kernel(const float* __restrict__ rq, long long nq,
+                                                       int dim, const float* __restrict__ cb, int m,
+                                                       int ksub, int dsub, float* __restrict__ T) {
+    extern __shared__ __align__(16) float sm[];
+    float* Yt = sm;                       // [dsub][ksub]
+    float* Q = sm + (size_t)dsub * ksub;  // [32][dsub]
+    const int s = blockIdx.y;
+    const long long q0 = (long long)blockIdx.x * 32;
+    const float* y = cb + (long long)s * ksub * dsub;
+    for (int e = threadIdx.x; e < ksub * dsub; e += blockDim.x) {
+        const int j = e / dsub, t = e % dsub;
+        Yt[t * ksub + j] = y[e];
+    }
+    for (int e = threadIdx.x; e < 32 * dsub; e += blockDim.x) {
+        const int qi = e / dsub, t = e % dsub;
+        Q[e] = (q0 + qi < nq) ? rq[(q0 + qi) * dim + (long long)s * dsub + t] : 0.0f;
+    }
+    __syncthreads();
+    const long long row = (long long)m * ksub;
+    for (int e = threadIdx.x; e < 32 * ksub; e += blockDim.x) {
+        const int qi = e / ksub, j = e % ksub;
+        if (q0 + qi >= nq) continue;
+        float acc = 0.0f;
+        for (int t = 0; t < dsub; ++t) acc = fmaf(Q[qi * dsub + t], Yt[t * ksub + j], acc);
+        T[(q0 + qi) * row + (long long)s * ksub + j] = -2.0f * acc;
+    }
+}
+
+void launch_lut_fast(const float* rq, long long nq, int dim, const float* cb, int m, int ksub, int dsub,
+                     float* T, cudaStream_t st) {
+    if (nq <= 0) return;
+    const size_t smem = ((size_t)dsub * ksub + 32 * (size_t)dsub) * sizeof(float);
+    if (smem > 200 * 1024) throw CudaError("lut_fast: sub-space codebook too large for shared memory");
+    VGPU_CHECK(cudaFuncSetAttribute(lut_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid(ceil_div(nq, 32), m);
+    lut_fast_kernel<<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, ksub, dsub, T);
+    VGPU_LAUNCH("lut_fast_kernel");
+}
+
+// =====================================================================================
+// Fast path, stage 2: inverted-list scan with a running top-k.
+//
+// One CTA per query; the query's table (m x ksub fp32) is copied into shared memory.
+// Lists are scanned in probe order, 256 entries per round (one per thread).  Each
+// entry gets the 64-bit key (order-preserving distance bits << 32 | scan position);
+// only keys below the current k-th key tau are appended to a shared candidate buffer,
+// which is merged with the running top-k (bitonic sort) when it could overflow and at
+// the end.  The key order is (distance, scan position), so ties resolve to the earlier
+// scanned entry, as in the exact path.
+// =====================================================================================
+namespace {
+constexpr int FS_NT = 256;
+constexpr int FS_CB = 512;   // candidate buffer entries (>= 2 rounds of FS_NT)
+}
+
+template <int MC>
+__device__ __forceinline__ float adc_sum(const uint8_t* __restrict__ code, const float* __restrict__ lut,
+                                         int m_rt, int ksub) {
+    float acc = 0.0f;
+    if (MC > 0) {
+        const uint4* c4 = reinterpret_cast<const uint4*>(code);
+#pragma unroll
+        for (int v = 0; v < MC / 16; ++v) {
+            const uint4 w = __ldg(c4 + v);
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int b = 0; b < 16; ++b) {
+                const uint32_t byte = (words[b >> 2] >> ((b & 3) * 8)) & 0xffu;
+                acc = __fadd_rn(acc, lut[(v * 16 + b) * ksub + byte]);
+            }
+        }
+    } else {
+        for (int s = 0; s < m_rt; ++s) acc = __fadd_rn(acc, lut[s * ksub + code[s]]);
+    }
+    return acc;
+}
+
+template <int MC>
+__global__ void __launch_bounds__(FS_NT, 2) scan_fast2_kernel(
+    const float* __restrict__ T, const float* __restrict__ rq, int dim,
+    const uint32_t* __restrict__ probe, const float* __restrict__ probe_d, const float* __restrict__ rc,
+    int nprobe, int m_rt, int ksub, const uint64_t* __restrict__ offs, const uint8_t* __restrict__ codes,
+    const float* __restrict__ vterm, const uint64_t* __restrict__ ids, int k, int kp2, int bp2,
+    uint64_t* __restrict__ out_ids, float* __restrict__ out_d, uint32_t* __restrict__ out_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int m = MC > 0 ? MC : m_rt;
+    float* lut = reinterpret_cast<float*>(smem_raw);                              // [m*ksub]
+    unsigned long long* buf = reinterpret_cast<unsigned long long*>(lut + (((size_t)m * ksub + 3) & ~(size_t)3));
+    unsigned long long* top = buf + bp2;                                          // [kp2]
+    uint32_t* prefix = reinterpret_cast<uint32_t*>(top + kp2);                     // [nprobe + 1]
+    __shared__ uint32_t cnt;
+    __shared__ int have;
+    __shared__ unsigned long long tau;
+    __shared__ float s_base;
+
+    const long long q = blockIdx.x;
+    {
+        const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * ksub);
+        float4* dst = reinterpret_cast<float4*>(lut);
+        const int n4 = (m * ksub) >> 2;
+        for (int i = threadIdx.x; i < n4; i += FS_NT) dst[i] = __ldg(src + i);
+        for (int i = (n4 << 2) + threadIdx.x; i < m * ksub; i += FS_NT) lut[i] = T[q * (long long)m * ksub + i];
+    }
+    if (threadIdx.x == 0) { cnt = 0; have = 0; tau = ~0ull; }
+    __syncthreads();
+
+    auto merge = [&]() {
+        // buf[0..cnt) candidates; append the current top, sort, keep k.
+        const int c = (int)cnt, h = have;
+        const int n = c + h;
+        const int p2 = next_pow2(n < 2 ? 2 : n);
+        for (int i = threadIdx.x; i < h; i += FS_NT) buf[c + i] = top[i];
+        for (int i = n + threadIdx.x; i < p2; i += FS_NT) buf[i] = ~0ull;
+        bitonic_sort_u64<FS_NT>(buf, p2);
+        const int nh = n < k ? n : k;
+        for (int i = threadIdx.x; i < nh; i += FS_NT) top[i] = buf[i];
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            have = nh;
+            cnt = 0;
+            tau = (nh == k) ? top[k - 1] : ~0ull;
+        }
+        __syncthreads();
+    };
+
+    uint32_t seq_base = 0;
+    for (int t = 0; t < nprobe; ++t) {
+        const long long pr = q * nprobe + t;
+        const uint32_t l = probe[pr];
+        if (threadIdx.x == 0) prefix[t] = seq_base;
+        if (rc) {
+            if (threadIdx.x < 32) {
+                const float* cl = rc + (long long)l * dim;
+                const float* qv = rq + q * dim;
+                float acc = 0.0f;
+                for (int d = threadIdx.x; d < dim; d += 32) {
+                    const float df = qv[d] - cl[d];
+                    acc = fmaf(df, df, acc);
+                }
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (threadIdx.x == 0) s_base = acc;
+            }
+        } else if (threadIdx.x == 0) {
+            s_base = probe_d[pr];
+        }
+        __syncthreads();
+        const float base_d = s_base;
+        const uint64_t b = offs[l];
+        const uint32_t L = (uint32_t)(offs[l + 1] - b);
+        for (uint32_t r0 = 0; r0 < L; r0 += FS_NT) {
+            const uint32_t i = r0 + threadIdx.x;
+            if (i < L) {
+                const uint64_t e = b + i;
+                const float acc = adc_sum<MC>(codes + e * (uint64_t)m, lut, m, ksub);
+                const float dist = __fadd_rn(__fadd_rn(base_d, __ldg(vterm + e)), acc);
+                const unsigned long long key = ((unsigned long long)float_key(dist) << 32) | (seq_base + i);
+                if (key < tau) {
+                    const uint32_t slot = atomicAdd(&cnt, 1u);
+                    buf[slot] = key;
+                }
+            }
+            __syncthreads();
+            if (cnt > (uint32_t)(FS_CB - FS_NT)) merge();
+        }
+        seq_base += L;
+    }
+    if (threadIdx.x == 0) prefix[nprobe] = seq_base;
+    __syncthreads();
+    if (cnt > 0) merge();
+    const int h = have;
+    for (int i = threadIdx.x; i < k; i += FS_NT) {
+        if (i < h) {
+            const unsigned long long key = top[i];
+            const uint32_t sq = (uint32_t)(key & 0xffffffffull);
+            int lo = 0, hi = nprobe;  // find t with prefix[t] <= sq < prefix[t+1]
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (prefix[mid] <= sq) lo = mid; else hi = mid;
+            }
+            // skip empty lists that share the same prefix value
+            while (lo + 1 < nprobe && prefix[lo + 1] <= sq) ++lo;
+            const uint32_t l = probe[q * nprobe + lo];
+            out_ids[q * k + i] = ids[offs[l] + (sq - prefix[lo])];
+            out_d[q * k + i] = key_float((uint32_t)(key >> 32));
+        } else {
+            out_ids[q * k + i] = 0;
+            out_d[q * k + i] = h > 0 ? key_float((uint32_t)(top[h - 1] >> 32)) : 0.0f;
+        }
+    }
+    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)h;
+}
+
+void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
+                       const float* probe_d, const float* rc, int nprobe, int m, int ksub,
+                       const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
+                       const uint64_t* ids, int k, uint64_t* out_ids, float* out_d, uint32_t* out_n,
+                       cudaStream_t st) {
+    if (nq <= 0) return;
+    if (k > kMaxK) throw CudaError("scan_fast: k exceeds the supported maximum");
+    const int kp2 = next_pow2(k < 2 ? 2 : k);
+    const int bp2 = next_pow2(FS_CB + kp2);   // merge buffer: candidates + current top, padded
+    const size_t smem = (((size_t)m * ksub + 3) & ~(size_t)3) * sizeof(float) +
+                        (size_t)(bp2 + kp2) * sizeof(unsigned long long) + (size_t)(nprobe + 1) * 4;
+    if (smem > 227 * 1024) throw CudaError("scan_fast: lookup table does not fit in shared memory");
+#define VGPU_SF2(MCV)                                                                             \
+    do {                                                                                          \
+        VGPU_CHECK(cudaFuncSetAttribute(scan_fast2_kernel<MCV>,                                   \
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        scan_fast2_kernel<MCV><<<(unsigned)nq, FS_NT, smem, st>>>(                                \
+            T, rq, dim, probe, probe_d, rc, nprobe, m, ksub, list_offsets, codes, vterm, ids, k,  \
+            kp2, bp2, out_ids, out_d, out_n);                                                     \
+    } while (0)
+    if (m == 16) VGPU_SF2(16);
+    else if (m == 32) VGPU_SF2(32);
+    else if (m == 64) VGPU_SF2(64);
+    else if (m == 96) VGPU_SF2(96);
+    else VGPU_SF2(0);
+#undef VGPU_SF2
+    VGPU_LAUNCH("scan_fast2_kernel");
 }
 
 }  // namespace vgpu

@@ -55,17 +55,18 @@ void launch_merge(const float* cand_d, const uint32_t* cand_pos, const uint32_t*
                   float* out_d, uint32_t* out_n, cudaStream_t st);
 
 // Fast search path (distances within fp32 rounding of the exact ones):
-// dist(q, x) = ||q - c_l||^2 + u(x) + sum_s T_q[s][code_s(x)].
-// T_q[s][j] = -2 <(Rq)_s, y_sj> is built per query in shared memory; u(x) is the
-// per-vector term stored at add time.  One CTA per query scans all its probed lists.
-// rc (rotated centroids) given -> the per-list base term is ||Rq - Rc_l||^2 computed
-// in the kernel; rc null -> the coarse distance probe_d is the base term.
-void launch_scan_fast(const float* rq, long long nq, int dim, const uint32_t* probe,
-                      const float* probe_d, const float* rc, int nprobe, const float* cb, int m, int ksub,
-                      int dsub,
-                      const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
-                      const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
-                      uint32_t* out_n, cudaStream_t st);
+// dist(q, x) = ||Rq - Rc_l||^2 + u(x) + sum_s T_q[s][code_s(x)], with
+// T_q[s][j] = -2 <(Rq)_s, y_sj> (one table per query) and u(x) the per-vector term
+// stored at add time.
+// Fast path in two stages: T[q] = per-query tables [m x ksub] for a batch, then a scan
+// with a running top-k filtered by the current k-th (distance, scan position) key.
+void launch_lut_fast(const float* rq, long long nq, int dim, const float* cb, int m, int ksub, int dsub,
+                     float* T, cudaStream_t st);
+void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
+                       const float* probe_d, const float* rc, int nprobe, int m, int ksub,
+                       const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
+                       const uint64_t* ids, int k, uint64_t* out_ids, float* out_d, uint32_t* out_n,
+                       cudaStream_t st);
 
 // u(x) = sum_s ( ||y_s,c_s||^2 + 2 <(R c_l)_s, y_s,c_s> ) for every CSR entry, with
 // rc = rotated centroids [nlist x dim]; accumulated in fp64, rounded once.

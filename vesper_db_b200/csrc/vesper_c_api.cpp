@@ -302,6 +302,7 @@ VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t*
     out->merge_ms = t.merge_ms;
     out->total_ms = t.total_ms;
     out->scanned_entries = t.scanned_entries;
+    out->kernel_launches = t.kernel_launches;
     return VESPER_OK;
 }
 

@@ -102,6 +102,23 @@ class IvfPqIndex:
         _check(self._lib, self._lib.vesper_ivfpq_add(self._h, _ptr(ids, C.c_uint64), _ptr(x, C.c_float),
                                                      x.shape[0]))
 
+    def train_device(self, x_ptr: int, n: int, dim: int, nlist: int, m: int, nbits: int = 8, *,
+                     use_opq: bool = True, max_iter: int = 25, epsilon: float = 1e-4, seed: int = 42,
+                     opq_iter: int = 10, opq_sample_n: int = 20000, verbose: bool = False) -> TrainReport:
+        """Train from n x dim float32 rows already in device memory (x_ptr)."""
+        p = N.TrainParamsEx()
+        self._lib.vesper_ivfpq_train_params_ex_init(C.byref(p))
+        p.nlist, p.m, p.nbits, p.max_iter, p.epsilon = nlist, m, nbits, max_iter, epsilon
+        p.use_opq, p.seed, p.opq_iter, p.opq_sample_n, p.verbose = int(use_opq), seed, opq_iter, opq_sample_n, int(verbose)
+        _check(self._lib, self._lib.vesper_ivfpq_train_ex_device(self._h, C.c_void_p(x_ptr), dim, n, C.byref(p)))
+        r = N.TrainReport()
+        _check(self._lib, self._lib.vesper_ivfpq_get_train_report(self._h, C.byref(r)))
+        return TrainReport(bool(r.opq_kept), r.err_unrot, r.err_opq, r.coarse_iterations, r.train_time_sec)
+
+    def add_device(self, ids_ptr: int, x_ptr: int, n: int):
+        """Add n vectors whose ids (uint64) and rows (float32) are in device memory."""
+        _check(self._lib, self._lib.vesper_ivfpq_add_device(self._h, C.c_void_p(ids_ptr), C.c_void_p(x_ptr), n))
+
     def set_model(self, centroids, codebooks, rotation=None, nbits: int = 8):
         c, cb = _f32(centroids), _f32(codebooks)
         nlist, dim = c.shape
