@@ -87,6 +87,25 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device(const vesper_index
                                                               uint64_t* d_out_ids, float* d_out_distances,
                                                               uint32_t* d_out_counts);
 
+/* Allocation-free variant of vesper_ivfpq_search_batch_device (FAST mode only).  This
+ * entry point has no counterpart in the reference.  It is for callers that cannot let
+ * the library allocate device memory: applications whose own arena or framework
+ * allocator owns the GPU's memory, and latency-critical loops where cudaMalloc or
+ * cudaFree -- which can synchronize the device -- must not run.  The caller passes the
+ * queries and the outputs (device pointers on the index's GPU); all temporary buffers
+ * come from one fixed 64 MiB device array compiled into the library, which every GPU
+ * that loads the library holds until exit.  The first call on a device looks the
+ * array's address up (make it before any stream capture).  Calls share the array and
+ * are serialized by a process-wide lock, because calls overlapping on the GPU would
+ * race on it.  Queries are processed in chunks that fit; an index whose single query
+ * would need more than 64 MiB of scratch (nlist * 4 + m * 2^nbits * 4 + ... bytes) is
+ * rejected with VESPER_ERROR_INVALID_PARAM and a message, as is mode EXACT. */
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_noalloc(const vesper_index_t* index,
+                                                                      const float* d_queries, size_t nq,
+                                                                      const vesper_ivfpq_search_params_ex_t* params,
+                                                                      uint64_t* d_out_ids, float* d_out_distances,
+                                                                      uint32_t* d_out_counts);
+
 /* Device time per stage of the last search call (CUDA events, milliseconds). */
 typedef struct vesper_ivfpq_timings_s {
   float coarse_ms;   /* query-centroid distances */

@@ -33,6 +33,7 @@ EXPORTED = [
     "vesper_ivfpq_search_batch_ex", "vesper_ivfpq_search_batch_device", "vesper_ivfpq_get_last_timings",
     "vesper_ivfpq_set_model", "vesper_ivfpq_get_lists", "vesper_b200_device_count",
     "vesper_ivfpq_train_ex_device", "vesper_ivfpq_add_device",
+    "vesper_ivfpq_search_batch_device_noalloc",
 ]
 
 
@@ -124,6 +125,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_b200_device_count": (C.c_int, []),
             "vesper_ivfpq_train_ex_device": (st, [vp, vp, C.c_size_t, C.c_size_t, C.POINTER(TrainParamsEx)]),
             "vesper_ivfpq_add_device": (st, [vp, vp, vp, C.c_size_t]),
+            "vesper_ivfpq_search_batch_device_noalloc": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx),
+                                                              vp, vp, vp]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

@@ -20,6 +20,7 @@
 #include "kernels.cuh"
 #include "kernels_opq.cuh"
 #include "kernels_train.cuh"
+#include "noalloc_search.hpp"
 
 namespace vesper::index {
 
@@ -767,6 +768,60 @@ public:
         timings = tm;
         return {};
     }
+
+    // ------------------------------------------------------------------ search without allocation
+    // The FAST search of search_flat with every temporary buffer carved out of the
+    // fixed device array of noalloc_search.cu instead of cudaMalloc'd workspace: no
+    // allocation of any kind.  Queries are processed in chunks sized to the array.
+    std::expected<void, error> search_noalloc(const float* dq_all, size_t nq, const IvfPqSearchParams& sp,
+                                              uint64_t* out_ids, float* out_d, uint32_t* out_n) const {
+        if (!trained) return fail(error_code::precondition_failed, "Index must be trained before searching");
+        if (sp.mode != SearchMode::Fast)
+            return fail(error_code::unsupported, "the allocation-free search supports the FAST mode only");
+        if (sp.k == 0) return fail(error_code::invalid_argument, "k must be > 0");
+        if (sp.k > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "k above 1024 is not supported by the GPU path");
+        if (nq == 0) return {};
+        const uint32_t np = std::min(sp.nprobe, nlist());
+        if (np == 0 || np > (uint32_t)vgpu::kMaxK)
+            return fail(error_code::unsupported, "nprobe must be in [1, 1024] for the allocation-free search");
+        auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+        const size_t per_q = (size_t)nlist() * 4 + (size_t)np * 8 + (has_rot ? dim * 4 : 0) + (size_t)m() * ksub * 4;
+        const size_t slack = 4 * 256;
+        if (per_q + slack > vgpu::kNoAllocScratchBytes)
+            return fail(error_code::out_of_range,
+                        "allocation-free search: one query needs " + std::to_string(per_q) +
+                        " bytes of scratch, more than the fixed " + std::to_string(vgpu::kNoAllocScratchBytes) +
+                        "-byte device buffer (nlist or m * 2^nbits too large)");
+        std::lock_guard<std::mutex> call_lock(vgpu::noalloc_call_mutex());
+        std::lock_guard<std::mutex> lock(mu);
+        unsigned char* base = static_cast<unsigned char*>(vgpu::noalloc_scratch_device_address(dev));
+        const size_t qc = std::min(nq, (vgpu::kNoAllocScratchBytes - slack) / per_q);
+        unsigned char* p = base;
+        float* D = reinterpret_cast<float*>(p); p += al(qc * nlist() * 4);
+        uint32_t* probe = reinterpret_cast<uint32_t*>(p); p += al(qc * np * 4);
+        float* probe_d = reinterpret_cast<float*>(p); p += al(qc * np * 4);
+        float* rq = has_rot ? reinterpret_cast<float*>(p) : nullptr; p += has_rot ? al(qc * dim * 4) : 0;
+        float* T = reinterpret_cast<float*>(p);
+        const uint32_t k = sp.k;
+        for (size_t q0 = 0; q0 < nq; q0 += qc) {
+            const size_t nc = std::min(qc, nq - q0);
+            const float* dq = dq_all + q0 * dim;
+            vgpu::launch_l2_dist(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, D, (long long)nlist(), st);
+            vgpu::launch_row_topk(D, (long long)nc, (int)nlist(), (long long)nlist(), (int)np, probe, probe_d, st);
+            const float* qrot = dq;
+            if (has_rot) {
+                vgpu::launch_rotate_fast(dq, (long long)nc, (int)dim, d_rot.data(), rq, st);
+                qrot = rq;
+            }
+            vgpu::launch_lut_fast(qrot, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)ksub, (int)dsub, T, st);
+            vgpu::launch_scan_fast2(T, qrot, (long long)nc, (int)dim, probe, probe_d, has_rot ? d_rc.data() : nullptr,
+                                    (int)np, (int)m(), (int)ksub, d_offs.data(), d_codes.data(), d_vterm.data(),
+                                    d_ids.data(), (int)k, out_ids + q0 * k, out_d + q0 * k,
+                                    out_n ? out_n + q0 : nullptr, st);
+        }
+        sync(st);
+        return {};
+    }
 };
 
 // ====================================================================== public API
@@ -819,6 +874,18 @@ auto IvfPqIndex::search_batch_flat(const float* queries, std::size_t n_queries,
     DeviceGuard g(impl_->dev);
     try {
         return impl_->search_flat(queries, n_queries, params, out_ids, out_dist, out_counts, on_device);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    }
+}
+
+auto IvfPqIndex::search_batch_device_noalloc(const float* d_queries, std::size_t n_queries,
+                                              const IvfPqSearchParams& params, std::uint64_t* d_out_ids,
+                                              float* d_out_dist, std::uint32_t* d_out_counts) const
+    -> std::expected<void, core::error> {
+    DeviceGuard g(impl_->dev);
+    try {
+        return impl_->search_noalloc(d_queries, n_queries, params, d_out_ids, d_out_dist, d_out_counts);
     } catch (const vgpu::CudaError& e) {
         return fail(error_code::internal, e.what(), "ivf_pq.cuda");
     }

@@ -140,6 +140,13 @@ public:
                            float* out_dist, std::uint32_t* out_counts, bool on_device) const
         -> std::expected<void, core::error>;
 
+    // FAST-mode device search that allocates nothing: its temporary buffers come from
+    // a fixed 64 MiB device array (noalloc_search.cu) instead of cudaMalloc.
+    auto search_batch_device_noalloc(const float* d_queries, std::size_t n_queries,
+                                     const IvfPqSearchParams& params, std::uint64_t* d_out_ids,
+                                     float* d_out_dist, std::uint32_t* d_out_counts) const
+        -> std::expected<void, core::error>;
+
     void set_metadata_json(std::string_view json);
     auto get_metadata_json() const -> std::string;
 

@@ -291,6 +291,26 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device(const vesper_index
     return do_search(index, d_q, nq, p->k, p->nprobe, p->mode, d_ids, d_d, d_counts, true);
 }
 
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_noalloc(
+    const vesper_index_t* index, const float* d_q, size_t nq, const vesper_ivfpq_search_params_ex_t* p,
+    uint64_t* d_ids, float* d_d, uint32_t* d_counts) {
+    if (!index || !index->ivfpq || !d_q || !p || !d_ids || !d_d || nq == 0) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < sizeof(vesper_ivfpq_search_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    IvfPqSearchParams sp;
+    sp.k = p->k;
+    sp.nprobe = p->nprobe;
+    sp.mode = p->mode == VESPER_SEARCH_EXACT ? SearchMode::Exact : SearchMode::Fast;
+    return guarded("search_noalloc", [&] {
+        auto r = index->ivfpq->search_batch_device_noalloc(d_q, nq, sp, d_ids, d_d, d_counts);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
 VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index, vesper_ivfpq_timings_t* out) {
     if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
     clear_error();

@@ -172,6 +172,15 @@ class IvfPqIndex:
             self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(ids_ptr), C.c_void_p(d_ptr),
             C.c_void_p(counts_ptr) if counts_ptr else None))
 
+    def search_batch_device_noalloc(self, q_ptr: int, nq: int, k: int, nprobe: int, ids_ptr: int, d_ptr: int,
+                                    counts_ptr: int = 0):
+        """Like search_batch_device (FAST mode) but allocating nothing: temporaries live in
+        the library's fixed 64 MiB device array (see include/vesper_b200.h)."""
+        p = N.SearchParamsEx(C.sizeof(N.SearchParamsEx), k, nprobe, N.SEARCH_FAST)
+        _check(self._lib, self._lib.vesper_ivfpq_search_batch_device_noalloc(
+            self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(ids_ptr), C.c_void_p(d_ptr),
+            C.c_void_p(counts_ptr) if counts_ptr else None))
+
     def last_timings(self) -> dict:
         t = N.Timings()
         _check(self._lib, self._lib.vesper_ivfpq_get_last_timings(self._h, C.byref(t)))
