@@ -50,6 +50,8 @@ NPROBE = 32
 SWEEP = (8, 32, 128)
 N_TRAIN = 131_072
 CHUNK = 125_000           # base rows per generator chunk (80 chunks; divisible by 1/2/4/8)
+SCAN_KERNELS = {1: "scan_exact_kernel", 2: "scan_fast2_kernel", 3: "scan_blocked_kernel"}
+COARSE_KERNELS = {1: "l2_dist_kernel (CUDA cores)", 2: "tc_screen_kernel (tcgen05 tf32) + screen_select_kernel"}
 METRIC = "QPS at matched recall@10 (IVF-PQ, 10k-query batch) at 1/2/4/8 B200 vs CPU ref"
 WORKLOAD = ("IVF-PQ+OPQ search: N=10,000,000 x d=768 fp32 (mixture of 50,000 anisotropic Gaussians, "
             "sigma~U[0.01,0.2]), nlist=16384, m=96x8 bits, OPQ 768x768, 10,000 queries, k=10, L2, nprobe=32")
@@ -423,11 +425,12 @@ def main():
         "e2e": {"value": NQ / (e2e_step / 1e3), "unit": "queries/s", "h2d_bytes_per_step": NQ * DIM * 4,
                 "d2h_bytes_per_step": NQ * K * 12, "ms_per_step": e2e_step},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "scan_fast2_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": SCAN_KERNELS.get(timings["scan_variant"], "?"), "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_source": peak_kind, "traffic": None,
                      "algorithmic_bytes_per_launch": bytes_per_launch, "scan_ms": scan_avg},
         "stage_ms": {k2: v for k2, v in timings.items() if k2.endswith("_ms")},
+        "coarse_kernel": COARSE_KERNELS.get(timings["coarse_variant"], "?"),
         "build": {"data_s": t_data, "train_s": t_train, "add_s": t_add, "opq_kept": rep.opq_kept,
                   "err_unrot": rep.err_unrot, "err_opq": rep.err_opq},
         "clocks": clk.summary(),

@@ -116,6 +116,8 @@ typedef struct vesper_ivfpq_timings_s {
   float total_ms;
   uint64_t scanned_entries; /* sum over queries of the probed lists' sizes */
   uint32_t kernel_launches; /* kernels launched by the call */
+  uint32_t scan_variant;    /* 1 exact per-(query, list) tables, 2 per-query tables, 3 blocked layout */
+  uint32_t coarse_variant;  /* 1 CUDA-core exact distances, 2 tensor-core screen + exact refine */
 } vesper_ivfpq_timings_t;
 VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index,
                                                            vesper_ivfpq_timings_t* out);

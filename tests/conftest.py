@@ -14,7 +14,7 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); run with -m gpu")
 
 
-CASES = ["plain_d32_m8", "plain_d64_m8", "opq_d32_m4", "odd_d20_m5"]
+CASES = ["plain_d32_m8", "plain_d64_m8", "opq_d32_m4", "odd_d20_m5", "plain_d64_n128"]
 SEARCHES = [(10, 4), (10, 16), (100, 8), (5, 1), (3, 64)]
 
 

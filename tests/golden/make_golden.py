@@ -35,6 +35,7 @@ CASES = [
     ("plain_d64_m8", 64, 24, 8, False, 2000, 1500, 50, 0.1),    # dsub = 8 (one FMA lane step)
     ("opq_d32_m4", 32, 16, 4, True, 2000, 1500, 40, 0.2),       # OPQ kept/dropped by the reference
     ("odd_d20_m5", 20, 8, 5, False, 800, 600, 20, 0.1),         # dim % 8 != 0 coarse tail
+    ("plain_d64_n128", 64, 128, 16, False, 6000, 4000, 300, 0.1),  # nlist >= 64: tensor-core coarse path
 ]
 SEARCHES = [(10, 4), (10, 16), (100, 8), (5, 1), (3, 64)]
 

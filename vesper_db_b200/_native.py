@@ -70,7 +70,8 @@ class SearchParamsEx(C.Structure):
 class Timings(C.Structure):
     _fields_ = [("coarse_ms", C.c_float), ("select_ms", C.c_float), ("rotate_ms", C.c_float),
                 ("scan_ms", C.c_float), ("merge_ms", C.c_float), ("total_ms", C.c_float),
-                ("scanned_entries", C.c_uint64), ("kernel_launches", C.c_uint32)]
+                ("scanned_entries", C.c_uint64), ("kernel_launches", C.c_uint32),
+                ("scan_variant", C.c_uint32), ("coarse_variant", C.c_uint32)]
 
 
 _lib = None

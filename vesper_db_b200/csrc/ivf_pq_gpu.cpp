@@ -19,6 +19,7 @@
 
 #include "kernels.cuh"
 #include "kernels_opq.cuh"
+#include "kernels_tc.cuh"
 #include "kernels_train.cuh"
 #include "noalloc_search.hpp"
 
@@ -85,6 +86,18 @@ bool env_flag(const char* name) {
     return v && v[0] == '1';
 }
 
+// Nearest-centroid search on the tensor cores (tcgen05 screen + exact refine) unless
+// the shapes or the pointer alignment rule it out, or VGPU_COARSE=exact asks for the
+// CUDA-core kernels; both give the same (exact) result.
+bool use_tc(const float* x, const float* c, int d, uint32_t k) {
+    static const bool off = [] {
+        const char* v = std::getenv("VGPU_COARSE");
+        return v && std::string(v) == "exact";
+    }();
+    return !off && k >= 64 && vgpu::tc_screen_supported(d) &&
+           ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15) == 0;
+}
+
 }  // namespace
 
 class IvfPqIndex::Impl {
@@ -115,11 +128,18 @@ public:
     std::vector<float> h_cent, h_cb, h_rot;
     std::vector<uint64_t> h_offs;   // [nlist + 1]
 
-    DeviceBuffer<float> d_cent, d_cb, d_rot, d_rotT, d_rc;
+    DeviceBuffer<float> d_cent, d_cb, d_rot, d_rotT, d_rc, d_cn;
+    mutable DeviceBuffer<int> d_err;
+    mutable DeviceBuffer<float> w_xn, w_cn;
     DeviceBuffer<uint64_t> d_offs, d_ids;
     DeviceBuffer<uint8_t> d_codes;
     DeviceBuffer<float> d_vterm;
     size_t n_vectors = 0;
+    // Blocked copy of the lists for the FAST scan (built after every add / load).
+    bool has_blocks = false;
+    DeviceBuffer<uint64_t> d_blk_off;
+    DeviceBuffer<uint8_t> d_bcodes;
+    DeviceBuffer<float> d_bvterm;
 
     double t_assign_ms = 0, t_encode_ms = 0, t_lists_ms = 0;
     mutable SearchTimings timings;
@@ -138,6 +158,8 @@ public:
     void upload_model() {
         d_cent.resize(h_cent.size());
         h2d(d_cent.data(), h_cent.data(), h_cent.size(), st);
+        d_cn.resize(nlist());
+        vgpu::launch_row_norms(d_cent.data(), nlist(), (int)dim, d_cn.data(), st);
         d_cb.resize(h_cb.size());
         h2d(d_cb.data(), h_cb.data(), h_cb.size(), st);
         if (has_rot) {
@@ -163,6 +185,27 @@ public:
         d_codes.release();
         d_vterm.release();
         n_vectors = 0;
+        has_blocks = false;
+        d_bcodes.release();
+        d_bvterm.release();
+    }
+
+    void rebuild_blocks() {
+        has_blocks = false;
+        d_bcodes.release();
+        d_bvterm.release();
+        if (!vgpu::scan_blocked_supported((int)m(), (int)ksub)) return;
+        std::vector<uint64_t> boff(nlist() + 1, 0);
+        for (uint32_t l = 0; l < nlist(); ++l) boff[l + 1] = boff[l] + (h_offs[l + 1] - h_offs[l] + 127) / 128;
+        const uint64_t nb = boff[nlist()];
+        d_blk_off.resize(nlist() + 1);
+        h2d(d_blk_off.data(), boff.data(), boff.size(), st);
+        d_bcodes.resize(std::max<uint64_t>(nb, 1) * 128 * m());
+        d_bvterm.resize(std::max<uint64_t>(nb, 1) * 128);
+        if (nb) vgpu::launch_build_blocks(d_codes.data(), d_vterm.data(), d_offs.data(), d_blk_off.data(), (int)m(),
+                                          (int)nlist(), d_bcodes.data(), d_bvterm.data(), st);
+        sync(st);
+        has_blocks = true;
     }
 
     void recompute_vterms() {
@@ -178,13 +221,43 @@ public:
                      float* d_mind, bool keep, DeviceBuffer<float>& D) const {
         const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * k)));
         D.reserve(rows * k);
+        const bool tc = use_tc(d_x, d_c, d, k);
+        if (tc) {
+            w_cn.reserve(k);
+            w_xn.reserve(rows);
+            vgpu::launch_row_norms(d_c, k, d, w_cn.data(), st);
+            reset_err();
+        }
         for (size_t r0 = 0; r0 < n; r0 += rows) {
             const size_t nr = std::min(rows, n - r0);
-            vgpu::launch_l2_dist(d_x + r0 * (size_t)d, (long long)nr, d_c, (int)k, d, D.data(), (long long)k, st);
-            vgpu::launch_row_argmin(D.data(), (long long)nr, (int)k, (long long)k,
-                                    keep ? d_assign + r0 : nullptr, d_assign + r0,
-                                    d_mind ? d_mind + r0 : nullptr, st);
+            const float* xr = d_x + r0 * (size_t)d;
+            if (tc) {
+                vgpu::launch_row_norms(xr, (long long)nr, d, w_xn.data(), st);
+                vgpu::launch_tc_screen(xr, (long long)nr, d_c, (int)k, d, w_xn.data(), w_cn.data(), D.data(),
+                                       (long long)k, d_err.data(), st);
+                vgpu::launch_screen_select(D.data(), (long long)nr, (long long)k, (int)k, xr, d, d_c, w_xn.data(),
+                                           w_cn.data(), 1, keep ? d_assign + r0 : nullptr, d_assign + r0,
+                                           d_mind ? d_mind + r0 : nullptr, d_err.data(), st);
+            } else {
+                vgpu::launch_l2_dist(xr, (long long)nr, d_c, (int)k, d, D.data(), (long long)k, st);
+                vgpu::launch_row_argmin(D.data(), (long long)nr, (int)k, (long long)k,
+                                        keep ? d_assign + r0 : nullptr, d_assign + r0,
+                                        d_mind ? d_mind + r0 : nullptr, st);
+            }
         }
+        if (tc) check_err();
+    }
+
+    void reset_err() const {
+        d_err.reserve(1);
+        vgpu::check(cudaMemsetAsync(d_err.data(), 0, sizeof(int), st), "memset err");
+    }
+    // Reads the device error word of the tensor-core kernels (synchronizes the stream).
+    void check_err() const {
+        int e = 0;
+        d2h(&e, d_err.data(), 1, st);
+        sync(st);
+        if (e) throw vgpu::CudaError("tensor-core screen: bounded wait expired (code " + std::to_string(e) + ")");
     }
 
     // Sum of a device float array in index order, in fp64 (host).
@@ -623,6 +696,7 @@ public:
         h_offs = std::move(new_offs);
         n_vectors = total;
         recompute_vterms();
+        rebuild_blocks();
         sync(st);
         const auto tc = std::chrono::steady_clock::now();
         if (params.timings_enabled || params.verbose || env_flag("VESPER_TIMING")) {
@@ -705,12 +779,27 @@ public:
                 od = w_out_d.data();
                 on = w_out_n.data();
             }
+            const bool tc = use_tc(dq, d_cent.data(), (int)dim, nlist());
             cudaEventRecord(ev[0], st);
-            vgpu::launch_l2_dist(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, w_D.data(),
-                                 (long long)nlist(), st);
+            if (tc) {
+                w_xn.reserve(qc);
+                reset_err();
+                vgpu::launch_row_norms(dq, (long long)nc, (int)dim, w_xn.data(), st);
+                vgpu::launch_tc_screen(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, w_xn.data(),
+                                       d_cn.data(), w_D.data(), (long long)nlist(), d_err.data(), st);
+            } else {
+                vgpu::launch_l2_dist(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, w_D.data(),
+                                     (long long)nlist(), st);
+            }
             cudaEventRecord(ev[1], st);
-            vgpu::launch_row_topk(w_D.data(), (long long)nc, (int)nlist(), (long long)nlist(), (int)np,
-                                  w_probe.data(), w_probe_d.data(), st);
+            if (tc) {
+                vgpu::launch_screen_select(w_D.data(), (long long)nc, (long long)nlist(), (int)nlist(), dq, (int)dim,
+                                           d_cent.data(), w_xn.data(), d_cn.data(), (int)np, nullptr, w_probe.data(),
+                                           w_probe_d.data(), d_err.data(), st);
+            } else {
+                vgpu::launch_row_topk(w_D.data(), (long long)nc, (int)nlist(), (long long)nlist(), (int)np,
+                                      w_probe.data(), w_probe_d.data(), st);
+            }
             cudaEventRecord(ev[2], st);
             vgpu::launch_probe_sizes(w_probe.data(), (long long)(nc * np), d_offs.data(), w_scanned.data(), st);
             if (exact) {
@@ -736,23 +825,36 @@ public:
                     vgpu::launch_rotate_fast(dq, (long long)nc, (int)dim, d_rot.data(), w_rq.data(), st);
                     rq = w_rq.data();
                 }
-                vgpu::launch_lut_fast(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)ksub, (int)dsub,
-                                      w_T.data(), st);
-                cudaEventRecord(ev[3], st);
-                vgpu::launch_scan_fast2(w_T.data(), rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
-                                        has_rot ? d_rc.data() : nullptr, (int)np, (int)m(), (int)ksub,
-                                        d_offs.data(), d_codes.data(), d_vterm.data(), d_ids.data(), (int)k,
-                                        oid, od, on, st);
+                if (has_blocks) {
+                    vgpu::launch_lut_blocked(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)dsub,
+                                             w_T.data(), st);
+                    cudaEventRecord(ev[3], st);
+                    vgpu::launch_scan_blocked(w_T.data(), rq, (long long)nc, (int)dim, w_probe.data(),
+                                              w_probe_d.data(), has_rot ? d_rc.data() : nullptr, (int)np, (int)m(),
+                                              d_offs.data(), d_blk_off.data(), d_bcodes.data(), d_bvterm.data(),
+                                              d_ids.data(), (int)k, oid, od, on, st);
+                } else {
+                    vgpu::launch_lut_fast(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)ksub, (int)dsub,
+                                          w_T.data(), st);
+                    cudaEventRecord(ev[3], st);
+                    vgpu::launch_scan_fast2(w_T.data(), rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
+                                            has_rot ? d_rc.data() : nullptr, (int)np, (int)m(), (int)ksub,
+                                            d_offs.data(), d_codes.data(), d_vterm.data(), d_ids.data(), (int)k,
+                                            oid, od, on, st);
+                }
                 cudaEventRecord(ev[4], st);
             }
             cudaEventRecord(ev[5], st);
-            tm.kernel_launches += 3 + (exact ? 2 : 2) + (has_rot ? 1 : 0);
+            tm.kernel_launches += 3 + (exact ? 2 : 2) + (has_rot ? 1 : 0) + (tc ? 1 : 0);
+            tm.scan_variant = exact ? 1u : (has_blocks ? 3u : 2u);
+            tm.coarse_variant = tc ? 2u : 1u;
             if (!on_device) {
                 d2h(out_ids + q0 * k, oid, nc * k, st);
                 d2h(out_d + q0 * k, od, nc * k, st);
                 if (out_n) d2h(out_n + q0, on, nc, st);
             }
             sync(st);
+            if (tc) check_err();
             float a = 0;
             cudaEventElapsedTime(&a, ev[0], ev[1]); tm.coarse_ms += a;
             cudaEventElapsedTime(&a, ev[1], ev[2]); tm.select_ms += a;
@@ -923,7 +1025,8 @@ auto IvfPqIndex::get_stats() const noexcept -> Stats {
     s.m = I.params.m;
     s.code_size = I.params.m;
     s.memory_bytes = sizeof(Impl) + I.d_cent.bytes() + I.d_cb.bytes() + I.d_rot.bytes() + I.d_rotT.bytes() +
-                     I.d_rc.bytes() + I.d_offs.bytes() + I.d_ids.bytes() + I.d_codes.bytes() + I.d_vterm.bytes();
+                     I.d_rc.bytes() + I.d_offs.bytes() + I.d_ids.bytes() + I.d_codes.bytes() + I.d_vterm.bytes() +
+                     I.d_blk_off.bytes() + I.d_bcodes.bytes() + I.d_bvterm.bytes();
     s.avg_list_size = I.n_vectors > 0 && I.params.nlist ? (float)I.n_vectors / (float)I.params.nlist : 0.0f;
     s.timings_enabled = I.params.verbose || I.params.timings_enabled || env_flag("VESPER_TIMING");
     if (s.timings_enabled) { s.t_assign_ms = I.t_assign_ms; s.t_encode_ms = I.t_encode_ms; s.t_lists_ms = I.t_lists_ms; }
@@ -1160,6 +1263,7 @@ auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core
         I.d_codes.resize(std::max<size_t>(codes.size(), 1));
         h2d(I.d_codes.data(), codes.data(), codes.size(), I.st);
         I.recompute_vterms();
+        I.rebuild_blocks();
         sync(I.st);
     } catch (const vgpu::CudaError& e) {
         return fail(error_code::internal, e.what(), "ivf_pq.cuda");

@@ -107,6 +107,8 @@ struct SearchTimings {
     float coarse_ms{0}, select_ms{0}, rotate_ms{0}, scan_ms{0}, merge_ms{0}, total_ms{0};
     std::uint64_t scanned_entries{0};   // sum over queries of the probed lists' sizes
     std::uint32_t kernel_launches{0};   // kernels this library launched for the call
+    std::uint32_t scan_variant{0};      // 1 exact per-list LUT, 2 per-query LUT, 3 blocked per-query LUT
+    std::uint32_t coarse_variant{0};    // 1 CUDA-core exact distances, 2 tensor-core screen + exact refine
 };
 
 class IvfPqIndex {

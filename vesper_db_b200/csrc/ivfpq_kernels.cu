@@ -908,3 +908,292 @@ void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, c
 }
 
 }  // namespace vgpu
+
+namespace vgpu {
+
+// =====================================================================================
+// Fast path, blocked layout ("scan layout").
+//
+// Each list is cut into blocks of 128 entries (the last one padded).  Inside a block,
+// lane l of a warp owns entries 4l..4l+3 and at step r looks up sub-space
+//   s(l, r) = G*floor(r/G) + ((l + r) mod G),     G = 32 (or 16/8/4 when m is smaller),
+// so the 32 lanes of a warp touch 32 different sub-spaces at every step.  The block
+// stores, for each step r, each lane's 4 code bytes as one word, 4 steps per 16-byte
+// segment, lane-contiguous:  byte((r/4*32 + l)*16 + (r%4)*4 + j) = code(4l + j, s(l, r)),
+// so a warp reads a block with fully coalesced 16-byte loads and no staging.  The
+// per-query table is laid out as Tb[(g*256 + c)*G + (s mod G)] (g = s / G): the bank of
+// a lookup is its sub-space, and the lookups of one step never conflict.
+// =====================================================================================
+
+__host__ __device__ inline int scan_group(int m) {
+    return (m % 32 == 0) ? 32 : (m % 16 == 0) ? 16 : (m % 8 == 0) ? 8 : (m % 4 == 0) ? 4 : 0;
+}
+
+// One thread per (entry, sub-space) of the CSR codes -> blocked layout; vterm likewise.
+__global__ void build_blocks_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ vterm,
+                                    const uint64_t* __restrict__ offs, const uint64_t* __restrict__ blk_off,
+                                    int m, int G, int nlist, uint8_t* __restrict__ bcodes,
+                                    float* __restrict__ bvterm) {
+    const int l = blockIdx.x;
+    const uint64_t b0 = offs[l];
+    const uint64_t L = offs[l + 1] - b0;
+    const uint64_t nb = blk_off[l + 1] - blk_off[l];
+    const uint64_t total = nb * 128 * (uint64_t)m;
+    for (uint64_t e = threadIdx.x; e < total; e += blockDim.x) {
+        const uint64_t p = e / m;            // position in list (padded)
+        const int s = (int)(e % m);
+        const uint64_t blk = blk_off[l] + p / 128;
+        const int c = (int)(p % 128), lane = c >> 2, j = c & 3;
+        const int g = s / G, s_lo = s % G;
+        const int r = g * G + ((s_lo - lane) % G + G) % G;
+        const uint64_t off = blk * 128ull * m + (uint64_t)((r >> 2) * 32 + lane) * 16 + (r & 3) * 4 + j;
+        bcodes[off] = p < L ? codes[(b0 + p) * (uint64_t)m + s] : (uint8_t)0;
+        if (s == 0) bvterm[blk * 128 + c] = p < L ? vterm[b0 + p] : 0.0f;
+    }
+}
+
+void launch_build_blocks(const uint8_t* codes, const float* vterm, const uint64_t* offs, const uint64_t* blk_off,
+                         int m, int nlist, uint8_t* bcodes, float* bvterm, cudaStream_t st) {
+    const int G = scan_group(m);
+    if (G == 0) throw CudaError("build_blocks: m must be a multiple of 4");
+    if (nlist <= 0) return;
+    build_blocks_kernel<<<nlist, 256, 0, st>>>(codes, vterm, offs, blk_off, m, G, nlist, bcodes, bvterm);
+    VGPU_LAUNCH("build_blocks_kernel");
+}
+
+// Tables in the blocked order, T[q][(g*256 + c)*G + s_lo] = -2 <(Rq)_s, y_sc>.
+__global__ void __launch_bounds__(256) lut_blocked_kernel(const float* __restrict__ rq, long long nq, int dim,
+                                                          const float* __restrict__ cb, int m, int dsub, int G,
+                                                          float* __restrict__ T) {
+    extern __shared__ __align__(16) float sm[];
+    float* Yt = sm;                      // [dsub][256]
+    float* Q = sm + (size_t)dsub * 256;  // [32][dsub]
+    const int s = blockIdx.y;
+    const long long q0 = (long long)blockIdx.x * 32;
+    const float* y = cb + (long long)s * 256 * dsub;
+    for (int e = threadIdx.x; e < 256 * dsub; e += blockDim.x) {
+        const int j = e / dsub, t = e % dsub;
+        Yt[t * 256 + j] = y[e];
+    }
+    for (int e = threadIdx.x; e < 32 * dsub; e += blockDim.x) {
+        const int qi = e / dsub, t = e % dsub;
+        Q[e] = (q0 + qi < nq) ? rq[(q0 + qi) * dim + (long long)s * dsub + t] : 0.0f;
+    }
+    __syncthreads();
+    const long long row = (long long)m * 256;
+    const int g = s / G, s_lo = s % G;
+    for (int e = threadIdx.x; e < 32 * 256; e += blockDim.x) {
+        const int qi = e / 256, j = e % 256;
+        if (q0 + qi >= nq) continue;
+        float acc = 0.0f;
+        for (int t = 0; t < dsub; ++t) acc = fmaf(Q[qi * dsub + t], Yt[t * 256 + j], acc);
+        T[(q0 + qi) * row + ((long long)g * 256 + j) * G + s_lo] = -2.0f * acc;
+    }
+}
+
+void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb, int m, int dsub, float* T,
+                        cudaStream_t st) {
+    if (nq <= 0) return;
+    const int G = scan_group(m);
+    const size_t smem = ((size_t)dsub * 256 + 32 * (size_t)dsub) * sizeof(float);
+    if (smem > 200 * 1024) throw CudaError("lut_blocked: sub-space codebook too large for shared memory");
+    VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid(ceil_div(nq, 32), m);
+    lut_blocked_kernel<<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, dsub, G, T);
+    VGPU_LAUNCH("lut_blocked_kernel");
+}
+
+namespace {
+constexpr int FB_NT = 512;                    // 16 warps; one 128-entry block per warp per round
+constexpr int FB_WARPS = FB_NT / 32;
+constexpr int FB_ROUND = FB_WARPS * 128;      // entries per round
+constexpr int FB_CB = FB_ROUND;               // candidate buffer: one round (merged every round)
+constexpr int FB_PF = 8;                      // 16-byte code segments a lane keeps in flight
+}
+
+template <int MC, int G>
+__global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
+    const float* __restrict__ T, const float* __restrict__ rq, int dim,
+    const uint32_t* __restrict__ probe, const float* __restrict__ probe_d, const float* __restrict__ rc,
+    int nprobe, const uint64_t* __restrict__ offs, const uint64_t* __restrict__ blk_off,
+    const uint8_t* __restrict__ bcodes, const float* __restrict__ bvterm, const uint64_t* __restrict__ ids,
+    int k, int kp2, int bp2, uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
+    uint32_t* __restrict__ out_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    constexpr int m = MC;
+    float* lut = reinterpret_cast<float*>(smem_raw);                                   // [m*256]
+    unsigned long long* buf = reinterpret_cast<unsigned long long*>(lut + m * 256);     // [bp2]
+    unsigned long long* top = buf + bp2;                                               // [kp2]
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(top + kp2);                         // [nprobe+1]
+    uint32_t* bprefix = eprefix + (nprobe + 1);                                        // [nprobe+1]
+    float* base = reinterpret_cast<float*>(bprefix + (nprobe + 1));                     // [nprobe]
+    __shared__ uint32_t cnt;
+    __shared__ int have;
+    __shared__ unsigned long long tau;
+
+    const long long q = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    {
+        const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * 256);
+        float4* dst = reinterpret_cast<float4*>(lut);
+        for (int i = threadIdx.x; i < m * 64; i += FB_NT) dst[i] = __ldg(src + i);
+    }
+    // Per-probe prefixes (entries, blocks) and base terms.
+    if (threadIdx.x == 0) {
+        uint32_t ep = 0, bp = 0;
+        for (int t = 0; t < nprobe; ++t) {
+            const uint32_t l = probe[q * nprobe + t];
+            eprefix[t] = ep;
+            bprefix[t] = bp;
+            ep += (uint32_t)(offs[l + 1] - offs[l]);
+            bp += (uint32_t)(blk_off[l + 1] - blk_off[l]);
+        }
+        eprefix[nprobe] = ep;
+        bprefix[nprobe] = bp;
+        cnt = 0; have = 0; tau = ~0ull;
+    }
+    for (int t = warp; t < nprobe; t += FB_WARPS) {
+        const long long pr = q * nprobe + t;
+        float b;
+        if (rc) {
+            const float* cl = rc + (long long)probe[pr] * dim;
+            const float* qv = rq + q * dim;
+            float acc = 0.0f;
+            for (int d = lane; d < dim; d += 32) {
+                const float df = qv[d] - cl[d];
+                acc = fmaf(df, df, acc);
+            }
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            b = acc;
+        } else {
+            b = probe_d[pr];
+        }
+        if (lane == 0) base[t] = b;
+    }
+    __syncthreads();
+
+    auto merge = [&]() {
+        const int c = (int)cnt, h = have;
+        const int n = c + h;
+        const int p2 = next_pow2(n < 2 ? 2 : n);
+        for (int i = threadIdx.x; i < h; i += FB_NT) buf[c + i] = top[i];
+        for (int i = n + threadIdx.x; i < p2; i += FB_NT) buf[i] = ~0ull;
+        bitonic_sort_u64<FB_NT>(buf, p2);
+        const int nh = n < k ? n : k;
+        for (int i = threadIdx.x; i < nh; i += FB_NT) top[i] = buf[i];
+        __syncthreads();
+        if (threadIdx.x == 0) { have = nh; cnt = 0; tau = (nh == k) ? top[k - 1] : ~0ull; }
+        __syncthreads();
+    };
+
+    const uint32_t NB = bprefix[nprobe];
+    for (uint32_t r0 = 0; r0 < NB; r0 += FB_WARPS) {
+        const uint32_t bi = r0 + warp;
+        if (bi < NB) {
+            int lo = 0, hi = nprobe;  // largest t with bprefix[t] <= bi
+            while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (bprefix[mid] <= bi) lo = mid; else hi = mid; }
+            const uint32_t l = probe[q * nprobe + lo];
+            const uint32_t b = bi - bprefix[lo];
+            const uint64_t gblk = blk_off[l] + b;
+            const uint32_t L = eprefix[lo + 1] - eprefix[lo];
+            const uint4* src = reinterpret_cast<const uint4*>(bcodes + gblk * 128ull * m) + lane;
+            float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+            // m/4 segments of 16 bytes per lane, fetched FB_PF at a time ahead of use.
+#pragma unroll
+            for (int r0 = 0; r0 < m / 4; r0 += FB_PF) {
+                uint4 w[FB_PF];
+#pragma unroll
+                for (int u = 0; u < FB_PF; ++u)
+                    if (r0 + u < m / 4) w[u] = __ldg(src + (r0 + u) * 32);
+#pragma unroll
+                for (int u = 0; u < FB_PF; ++u) {
+                    if (r0 + u >= m / 4) break;
+                    const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const int r = (r0 + u) * 4 + jj;
+                        const int g = r / G;
+                        const int s_lo = (lane + r) & (G - 1);
+                        const float* tb = lut + (g * 256) * G + s_lo;
+                        const uint32_t v = ws[jj];
+                        acc0 += tb[(v & 0xffu) * G];
+                        acc1 += tb[((v >> 8) & 0xffu) * G];
+                        acc2 += tb[((v >> 16) & 0xffu) * G];
+                        acc3 += tb[(v >> 24) * G];
+                    }
+                }
+            }
+            const float4 vt = __ldg(reinterpret_cast<const float4*>(bvterm + gblk * 128) + lane);
+            const float bd = base[lo];
+            const float accs[4] = {acc0, acc1, acc2, acc3};
+            const float vts[4] = {vt.x, vt.y, vt.z, vt.w};
+            const uint32_t p0 = b * 128 + lane * 4;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t p = p0 + j;
+                if (p < L) {
+                    const float dist = (bd + vts[j]) + accs[j];
+                    const unsigned long long key =
+                        ((unsigned long long)float_key(dist) << 32) | (eprefix[lo] + p);
+                    if (key < tau) {
+                        const uint32_t slot = atomicAdd(&cnt, 1u);
+                        buf[slot] = key;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (cnt > 0) merge();
+    }
+    const int h = have;
+    for (int i = threadIdx.x; i < k; i += FB_NT) {
+        if (i < h) {
+            const unsigned long long key = top[i];
+            const uint32_t sq = (uint32_t)(key & 0xffffffffull);
+            int lo = 0, hi = nprobe;
+            while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (eprefix[mid] <= sq) lo = mid; else hi = mid; }
+            const uint32_t l = probe[q * nprobe + lo];
+            out_ids[q * k + i] = ids[offs[l] + (sq - eprefix[lo])];
+            out_d[q * k + i] = key_float((uint32_t)(key >> 32));
+        } else {
+            out_ids[q * k + i] = 0;
+            out_d[q * k + i] = h > 0 ? key_float((uint32_t)(top[h - 1] >> 32)) : 0.0f;
+        }
+    }
+    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)h;
+}
+
+bool scan_blocked_supported(int m, int ksub) {
+    return ksub == 256 && (m == 16 || m == 32 || m == 64 || m == 96 || m == 128);
+}
+
+void launch_scan_blocked(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
+                         const float* probe_d, const float* rc, int nprobe, int m, const uint64_t* offs,
+                         const uint64_t* blk_off, const uint8_t* bcodes, const float* bvterm, const uint64_t* ids,
+                         int k, uint64_t* out_ids, float* out_d, uint32_t* out_n, cudaStream_t st) {
+    if (nq <= 0) return;
+    if (k > kMaxK) throw CudaError("scan_blocked: k exceeds the supported maximum");
+    const int kp2 = next_pow2(k < 2 ? 2 : k);
+    const int bp2 = next_pow2(FB_CB + kp2);
+    const size_t smem = (size_t)m * 256 * sizeof(float) + (size_t)(bp2 + kp2) * sizeof(unsigned long long) +
+                        (size_t)(nprobe + 1) * 8 + (size_t)nprobe * 4;
+    if (smem > 227 * 1024) throw CudaError("scan_blocked: lookup table does not fit in shared memory");
+#define VGPU_SB(MCV, GV)                                                                          \
+    do {                                                                                          \
+        VGPU_CHECK(cudaFuncSetAttribute(scan_blocked_kernel<MCV, GV>,                             \
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+        scan_blocked_kernel<MCV, GV><<<(unsigned)nq, FB_NT, smem, st>>>(                          \
+            T, rq, dim, probe, probe_d, rc, nprobe, offs, blk_off, bcodes, bvterm, ids, k, kp2,   \
+            bp2, out_ids, out_d, out_n);                                                          \
+    } while (0)
+    if (m == 16) VGPU_SB(16, 16);
+    else if (m == 32) VGPU_SB(32, 32);
+    else if (m == 64) VGPU_SB(64, 32);
+    else if (m == 96) VGPU_SB(96, 32);
+    else if (m == 128) VGPU_SB(128, 32);
+    else throw CudaError("scan_blocked: unsupported m");
+#undef VGPU_SB
+    VGPU_LAUNCH("scan_blocked_kernel");
+}
+
+}  // namespace vgpu

@@ -68,6 +68,18 @@ void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, c
                        const uint64_t* ids, int k, uint64_t* out_ids, float* out_d, uint32_t* out_n,
                        cudaStream_t st);
 
+// Blocked scan layout (see ivfpq_kernels.cu): lists cut into 128-entry blocks whose
+// code bytes are pre-rotated so a warp's lookups never share a bank.
+bool scan_blocked_supported(int m, int ksub);
+void launch_build_blocks(const uint8_t* codes, const float* vterm, const uint64_t* offs, const uint64_t* blk_off,
+                         int m, int nlist, uint8_t* bcodes, float* bvterm, cudaStream_t st);
+void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb, int m, int dsub, float* T,
+                        cudaStream_t st);
+void launch_scan_blocked(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
+                         const float* probe_d, const float* rc, int nprobe, int m, const uint64_t* offs,
+                         const uint64_t* blk_off, const uint8_t* bcodes, const float* bvterm, const uint64_t* ids,
+                         int k, uint64_t* out_ids, float* out_d, uint32_t* out_n, cudaStream_t st);
+
 // u(x) = sum_s ( ||y_s,c_s||^2 + 2 <(R c_l)_s, y_s,c_s> ) for every CSR entry, with
 // rc = rotated centroids [nlist x dim]; accumulated in fp64, rounded once.
 void launch_vector_terms(const float* rc, int nlist, int dim, const float* cb, int m, int ksub,

@@ -1,0 +1,470 @@
+// Tensor-core (tcgen05, kind::tf32) screening of query-centroid distances, followed
+// by an exact refine, for the coarse probe, add() assignment and the k-means E-step.
+//
+// Stage 1 (tc_screen_kernel): S = X * C^T on the 5th-generation tensor cores.  One CTA
+// computes a 128 x 256 tile: a TMA producer thread streams 128x32 and 256x32 fp32 tiles
+// (128-byte swizzle) through a 4-stage shared-memory ring, one thread issues
+// tcgen05.mma.kind::tf32 (M=128, N=256, K=8) into a TMEM accumulator (256 columns),
+// and the four warps read it back with tcgen05.ld and write
+//     Dt = ||x||^2 + ||c||^2 - 2 S
+// to global memory.  TF32 operands are truncated to 10 mantissa bits, so Dt is only a
+// screen: |Dt - d_ref| <= eps(x, c) (bound below), with d_ref the reference-order
+// distance of common.cuh.
+//
+// Stage 2 (screen_select_kernel): per row, U* = the k-th smallest upper bound
+// Dt + eps; every centroid whose lower bound Dt - eps is <= U* is recomputed exactly
+// (l2 in the reference's lane order) and the k smallest (exact distance, index) pairs
+// are selected.  A centroid outside the band cannot be among the k nearest, so the
+// result equals the exact top-k / arg-min (ties to the lowest index; with `keep`, the
+// current assignment wins a tie, as in KmeansElkan::assign_with_bounds).
+//
+// Every mbarrier wait is bounded; on timeout the kernel records an error code, stops
+// issuing work, and still frees its TMEM before returning.
+#include <cuda.h>
+#include <cfloat>
+
+#include "kernels.cuh"
+#include "kernels_tc.cuh"
+#include "select.cuh"
+
+namespace vgpu {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4;            // 16 KB
+constexpr int B_BYTES = BN * BK * 4;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint32_t TMEM_COLS = 256;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 B,
+// 8-row core groups 1024 B apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+    d |= (uint64_t)1 << 46;             // version
+    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant__ CUtensorMap map_x,
+                                                           const __grid_constant__ CUtensorMap map_c, int nx,
+                                                           int nc, int dim, const float* __restrict__ xn,
+                                                           const float* __restrict__ cn, float* __restrict__ Dt,
+                                                           long long ldd, int* __restrict__ err) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accum = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    __shared__ int s_fail;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int kt = (dim + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // TMA producer.
+        for (int t = 0; t < kt; ++t) {
+            const int s = t % STAGES;
+            if (t >= STAGES && !mbar_wait(&empty[s], ((t / STAGES) - 1) & 1)) { s_fail = 1; break; }
+            unsigned char* a = smem + s * STAGE_BYTES;
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(a, &map_x, t * BK, m0, &full[s]);
+            tma_load_2d(a + A_BYTES, &map_c, t * BK, n0, &full[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer.
+        bool ok = true;
+        for (int t = 0; t < kt && ok; ++t) {
+            const int s = t % STAGES;
+            if (!mbar_wait(&full[s], (t / STAGES) & 1)) { s_fail = 2; ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
+            const uint64_t ad = sw128_kmajor_desc(a), bd = sw128_kmajor_desc(a + A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk)  // K = 8 tf32 = 32 bytes per MMA
+                mma_tf32(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), (t > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&empty[s]);
+        }
+        mma_commit(accum);
+    }
+    __syncwarp();
+    // Epilogue: thread (warp w, lane l) owns accumulator row 32w + l.
+    const bool acc_ok = mbar_wait(accum, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!acc_ok) s_fail = 3;
+    __syncthreads();
+    if (s_fail == 0) {
+        const int row = m0 + warp * 32 + lane;
+        const float rn = row < nx ? xn[row] : 0.0f;
+        for (int ch = 0; ch < BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(ch * 32), r);
+            if (row < nx) {
+                float* out = Dt + (long long)row * ldd + n0 + ch * 32;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int col = n0 + ch * 32 + j;
+                    if (col < nc) out[j] = (rn + cn[col]) - 2.0f * __uint_as_float(r[j]);
+                }
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        atomicExch(err, s_fail);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// ---------------------------------------------------------------------------------
+// Host: tensor maps through the driver entry point (no libcuda link dependency).
+// ---------------------------------------------------------------------------------
+namespace {
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        check(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q), "cudaGetDriverEntryPoint");
+        if (!p || q != cudaDriverEntryPointSuccess) throw CudaError("cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+CUtensorMap make_map(const float* base, long long rows, int dim, int box_rows) {
+    CUtensorMap m;
+    const cuuint64_t gdim[2] = {(cuuint64_t)dim, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)dim * sizeof(float)};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride,
+                                   box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed");
+    return m;
+}
+}  // namespace
+
+bool tc_screen_supported(int dim) {
+    return dim % 4 == 0 && dim >= 32;
+}
+
+void launch_tc_screen(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
+                      float* Dt, long long ldd, int* err, cudaStream_t st) {
+    if (nx <= 0 || nc <= 0) return;
+    if (!tc_screen_supported(dim)) throw CudaError("tc_screen: dim must be a multiple of 4 and >= 32");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
+        throw CudaError("tc_screen: operands must be 16-byte aligned");
+    const CUtensorMap mx = make_map(x, nx, dim, BM);
+    const CUtensorMap mc = make_map(c, nc, dim, BN);
+    static bool attr = false;
+    if (!attr) {
+        check(cudaFuncSetAttribute(tc_screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+              "cudaFuncSetAttribute(tc_screen)");
+        attr = true;
+    }
+    dim3 grid(ceil_div(nc, BN), ceil_div(nx, BM));
+    tc_screen_kernel<<<grid, 128, SMEM_BYTES, st>>>(mx, mc, (int)nx, nc, dim, xn, cn, Dt, ldd, err);
+    check(cudaGetLastError(), "tc_screen_kernel");
+}
+
+// ---------------------------------------------------------------------------------
+// Row norms (fp64 accumulate, one rounding) for the screen.
+// ---------------------------------------------------------------------------------
+__global__ void row_norms_kernel(const float* __restrict__ x, long long n, int dim, float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long i = warp; i < n; i += nw) {
+        double s = 0.0;
+        for (int d = lane; d < dim; d += 32) { const double v = x[i * dim + d]; s += v * v; }
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) out[i] = (float)s;
+    }
+}
+
+void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n * 32 + 255) / 256, 148LL * 32);
+    row_norms_kernel<<<blocks, 256, 0, st>>>(x, n, dim, out);
+    check(cudaGetLastError(), "row_norms_kernel");
+}
+
+// ---------------------------------------------------------------------------------
+// Stage 2: band selection, exact refine, top-k.
+// ---------------------------------------------------------------------------------
+namespace {
+constexpr int SS_NT = 256;
+constexpr int SS_CAP = 4096;   // candidates refined per pass
+
+// Screening error bound.  tf32 truncation of both operands (relative 2^-10 each), fp32
+// accumulation over dim products, fp32 rounding of the epilogue and of the norms, and
+// the reference-order rounding of d_ref; times a safety factor of 2.
+__device__ __forceinline__ float screen_eps(float xn, float cn, float dt, int dim) {
+    const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;   // 2^-9 + (dim+8) 2^-23
+    const float xc = sqrtf(xn * cn);
+    const float e = 2.0f * a * xc + 2.384e-7f * (xn + cn + 2.0f * xc) +
+                    (float)(dim / 8 + 8) * 1.1920929e-7f * fabsf(dt);
+    return 2.0f * e + 1e-30f;
+}
+
+// Exact l2 for up to 4 candidates per warp: lane group g = lane / 8 takes candidate g,
+// lane (lane % 8) plays AVX2 lane l, then an 8-lane hsum in the reference order.
+__device__ __forceinline__ float warp_l2_group(const float* __restrict__ x, const float* __restrict__ c, int dim,
+                                               bool active) {
+    const int lane = threadIdx.x & 31, l = lane & 7;
+    const int simd_end = dim & ~7;
+    float acc = 0.0f;
+    if (active)
+        for (int t = l; t < simd_end; t += 8) {
+            const float d = __fsub_rn(x[t], c[t]);
+            acc = __fmaf_rn(d, d, acc);
+        }
+    const float a4 = __shfl_down_sync(0xffffffffu, acc, 4, 8);
+    const float s = __fadd_rn(a4, acc);
+    const float s1 = __shfl_down_sync(0xffffffffu, s, 1, 8);
+    const float s2 = __shfl_down_sync(0xffffffffu, s, 2, 8);
+    const float s3 = __shfl_down_sync(0xffffffffu, s, 3, 8);
+    float r = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+    if (active)
+        for (int t = simd_end; t < dim; ++t) {
+            const float d = __fsub_rn(x[t], c[t]);
+            r = __fadd_rn(r, __fmul_rn(d, d));
+        }
+    return r;  // valid in lane l == 0 of each group
+}
+
+struct ScreenSmem {
+    float exact[SS_CAP + kMaxK];
+    uint32_t idx[SS_CAP + kMaxK];
+    unsigned long long sortb[8192];   // >= next_pow2(SS_CAP + kMaxK)
+    uint32_t warp_tmp[33];
+    uint32_t hist[256];
+    uint32_t remaining, thresh, count;
+    float keep_val;
+    SelectSmem sel;
+};
+}  // namespace
+
+__global__ void __launch_bounds__(SS_NT) screen_select_kernel(
+    const float* __restrict__ Dt, long long ldd, int nc, const float* __restrict__ x, int dim,
+    const float* __restrict__ cent, const float* __restrict__ xn, const float* __restrict__ cn, int k,
+    const uint32_t* __restrict__ keep, uint32_t* __restrict__ out_idx, float* __restrict__ out_val, int* err) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ScreenSmem& S = *reinterpret_cast<ScreenSmem*>(smem_raw);
+    const long long row = blockIdx.x;
+    const float* drow = Dt + row * ldd;
+    const float* xr = x + row * dim;
+    const float rn = xn[row];
+    const int kk = k < nc ? k : nc;
+    const uint32_t kc = keep ? keep[row] : 0xffffffffu;
+    if (threadIdx.x == 0) S.keep_val = FLT_MAX;
+
+    // 1) U* = kk-th smallest upper bound (4-pass radix select on order-preserving keys).
+    uint32_t prefix = 0, mask = 0;
+    if (threadIdx.x == 0) S.remaining = (uint32_t)kk;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += SS_NT) S.hist[i] = 0;
+        __syncthreads();
+        for (int c = threadIdx.x; c < nc; c += SS_NT) {
+            const float dt = drow[c];
+            const uint32_t key = float_key(dt + screen_eps(rn, cn[c], dt, dim));
+            if ((key & mask) == prefix) atomicAdd(&S.hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t rem = S.remaining, acc = 0, b = 0;
+            for (; b < 256; ++b) { const uint32_t h = S.hist[b]; if (acc + h >= rem) break; acc += h; }
+            S.remaining = rem - acc;
+            S.thresh = b;
+        }
+        __syncthreads();
+        prefix |= S.thresh << shift;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    const float ustar = key_float(prefix);
+
+    // 2) Candidates in index order (lower bound <= U*), refined exactly, selected with a
+    //    running top-kk by (exact distance, index).
+    int carry = 0;
+    int base = 0;
+    while (base < nc) {
+        // gather up to SS_CAP candidates after the carried ones
+        if (threadIdx.x == 0) S.count = 0;
+        __syncthreads();
+        int c0 = base;
+        for (; c0 < nc; c0 += SS_NT) {
+            const int c = c0 + threadIdx.x;
+            bool cand = false;
+            if (c < nc) {
+                const float dt = drow[c];
+                cand = (dt - screen_eps(rn, cn[c], dt, dim)) <= ustar;
+            }
+            uint32_t tot;
+            const uint32_t r = block_rank<SS_NT>(cand, S.warp_tmp, &tot);
+            const uint32_t cur = S.count;
+            if (cand && cur + r < (uint32_t)SS_CAP) S.idx[carry + cur + r] = (uint32_t)c;
+            __syncthreads();
+            if (threadIdx.x == 0) S.count = cur + tot;
+            __syncthreads();
+            if (S.count >= (uint32_t)(SS_CAP - SS_NT)) { c0 += SS_NT; break; }
+        }
+        base = c0;
+        const int nnew = (int)min(S.count, (uint32_t)SS_CAP);
+        if (S.count > (uint32_t)SS_CAP && threadIdx.x == 0) atomicExch(err, 10);
+        // exact distances for the new candidates: 4 per warp per step
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int b0 = warp * 4; b0 < nnew; b0 += (SS_NT / 32) * 4) {
+            const int ci = b0 + (lane >> 3);
+            const bool act = ci < nnew;
+            const uint32_t c = act ? S.idx[carry + ci] : 0u;
+            const float v = warp_l2_group(xr, cent + (long long)c * dim, dim, act);
+            if (act && (lane & 7) == 0) {
+                S.exact[carry + ci] = v;
+                if (c == kc) S.keep_val = v;
+            }
+        }
+        __syncthreads();
+        const int n = carry + nnew;
+        const int got = block_select_k<SS_NT>(S.exact, n, kk, S.sortb, S.sel);
+        // compact the winners to the front (positions are into exact/idx)
+        for (int i = threadIdx.x; i < got; i += SS_NT) {
+            const uint32_t pos = (uint32_t)(S.sortb[i] & 0xffffffffull);
+            S.sortb[i] = ((unsigned long long)float_key(S.exact[pos]) << 32) | S.idx[pos];
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < got; i += SS_NT) {
+            S.exact[i] = key_float((uint32_t)(S.sortb[i] >> 32));
+            S.idx[i] = (uint32_t)(S.sortb[i] & 0xffffffffull);
+        }
+        __syncthreads();
+        carry = got;
+    }
+    // 3) Output in (exact distance, index) order; with `keep`, a tie with the current
+    //    assignment keeps it.
+    if (threadIdx.x == 0 && keep && carry >= 1 && S.keep_val == S.exact[0]) S.idx[0] = kc;
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += SS_NT) {
+        out_idx[row * k + i] = i < carry ? S.idx[i] : 0u;
+        if (out_val) out_val[row * k + i] = i < carry ? S.exact[i] : FLT_MAX;
+    }
+}
+
+void launch_screen_select(const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
+                          const float* cent, const float* xn, const float* cn, int k, const uint32_t* keep,
+                          uint32_t* out_idx, float* out_val, int* err, cudaStream_t st) {
+    if (n_rows <= 0) return;
+    if (k > kMaxK) throw CudaError("screen_select: k exceeds the supported maximum");
+    const size_t smem = sizeof(ScreenSmem);
+    static bool attr = false;
+    if (!attr) {
+        check(cudaFuncSetAttribute(screen_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+              "cudaFuncSetAttribute(screen_select)");
+        attr = true;
+    }
+    screen_select_kernel<<<(unsigned)n_rows, SS_NT, smem, st>>>(Dt, ldd, nc, x, dim, cent, xn, cn, k, keep, out_idx,
+                                                                 out_val, err);
+    check(cudaGetLastError(), "screen_select_kernel");
+}
+
+}  // namespace vgpu

@@ -323,6 +323,8 @@ VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t*
     out->total_ms = t.total_ms;
     out->scanned_entries = t.scanned_entries;
     out->kernel_launches = t.kernel_launches;
+    out->scan_variant = t.scan_variant;
+    out->coarse_variant = t.coarse_variant;
     return VESPER_OK;
 }
 
