@@ -220,12 +220,13 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
 
     from vesper_db_b200 import IvfPqIndex
+    from vesper_db_b200.shard import chunks_of, merge_topk
     t_build0 = time.perf_counter()
     centres, sigmas = gen_centres(torch, dev)
     queries = gen_rows(torch, dev, centres, sigmas, NQ, 5678)
     n_chunks = N_BASE // CHUNK
     shard_world = world if args.impl == "ours" else 1
-    my_chunks = [c for c in range(n_chunks) if c % shard_world == (rank if args.impl == "ours" else 0)]
+    my_chunks = chunks_of(rank if args.impl == "ours" else 0, shard_world, n_chunks)
     n_local = len(my_chunks) * CHUNK
     base = torch.empty((n_local, DIM), device=dev)
     ids = torch.empty(n_local, dtype=torch.int64, device=dev)
@@ -252,13 +253,7 @@ def main():
     chunks = [(base[j * CHUNK:(j + 1) * CHUNK], my_chunks[j] * CHUNK) for j in range(len(my_chunks))]
     gt_d, gt_i = exact_topk_gt(torch, queries, chunks, K)
     if world > 1 and args.impl == "ours":
-        ad = [torch.empty_like(gt_d) for _ in range(world)]
-        ai = [torch.empty_like(gt_i) for _ in range(world)]
-        dist.all_gather(ad, gt_d)
-        dist.all_gather(ai, gt_i)
-        cd, ci = torch.cat(ad, 1), torch.cat(ai, 1)
-        gt_d, sel = torch.topk(cd, K, dim=1, largest=False)
-        gt_i = torch.gather(ci, 1, sel)
+        gt_d, gt_i = merge_topk(gt_d, gt_i, K)
     del base, chunks
     torch.cuda.synchronize()
     gt_np = gt_i.cpu().numpy()
@@ -319,17 +314,15 @@ def main():
     out_d = torch.empty((NQ, K), dtype=torch.float32, device=dev)
     out_n = torch.empty(NQ, dtype=torch.int32, device=dev)
 
+    slot = torch.arange(K, device=dev)[None, :]
+
     def one_search(nprobe):
         index.search_batch_device(queries.data_ptr(), NQ, K, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
                                   out_n.data_ptr())
         if world > 1:
-            ad = [torch.empty_like(out_d) for _ in range(world)]
-            ai = [torch.empty_like(out_ids) for _ in range(world)]
-            dist.all_gather(ad, out_d)
-            dist.all_gather(ai, out_ids)
-            cd, ci = torch.cat(ad, 1), torch.cat(ai, 1)
-            md, sel = torch.topk(cd, K, dim=1, largest=False)
-            return md, torch.gather(ci, 1, sel)
+            # padded slots (fewer than k results on this shard) must not win the merge
+            d = torch.where(slot < out_n[:, None], out_d, torch.full_like(out_d, float("inf")))
+            return merge_topk(d, out_ids, K)
         return out_d, out_ids
 
     def barrier():
@@ -387,17 +380,15 @@ def main():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         e0.record()
-        hid, hd = index.search_batch_c(q_host_np, K, NPROBE)
-        if world > 1:
-            # merge across ranks: results back to the device, all_gather, top-k, to host
-            td = torch.from_numpy(hd).to(dev)
-            ti = torch.from_numpy(hid.astype(np.int64)).to(dev)
-            ad = [torch.empty_like(td) for _ in range(world)]
-            ai = [torch.empty_like(ti) for _ in range(world)]
-            dist.all_gather(ad, td)
-            dist.all_gather(ai, ti)
-            md, sel = torch.topk(torch.cat(ad, 1), K, dim=1, largest=False)
-            torch.gather(torch.cat(ai, 1), 1, sel).cpu()
+        if world == 1:
+            index.search_batch_c(q_host_np, K, NPROBE)
+        else:
+            # per-shard search through the C ABI with host buffers (counts mark the
+            # padding), then the merge across ranks and the merged result to the host
+            hid, hd, hcnt = index.search_batch(q_host_np, K, NPROBE)
+            hd = np.where(np.arange(K)[None, :] < hcnt[:, None], hd, np.inf).astype(np.float32)
+            md, mi = merge_topk(torch.from_numpy(hd).to(dev), torch.from_numpy(hid.astype(np.int64)).to(dev), K)
+            mi.cpu()
         e1.record()
         barrier()
         if s >= args.warmup:

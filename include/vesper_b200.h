@@ -134,6 +134,53 @@ VESPER_C_API vesper_status_t vesper_ivfpq_set_model(vesper_index_t* index, size_
 VESPER_C_API vesper_status_t vesper_ivfpq_get_lists(const vesper_index_t* index, uint64_t* out_offsets,
                                                     uint64_t* out_ids, uint8_t* out_codes);
 
+/* k-means on the GPU of the calling thread's current device.  The reference reaches
+ * k-means from C++ only -- kmeans_cluster (src/index/kmeans.cpp:137-252) and
+ * KmeansElkan::cluster (src/index/kmeans_elkan.cpp:293-430) -- so these entry points
+ * have no C counterpart there; they take the fields of KmeansParams
+ * (include/vesper/index/kmeans.hpp:26-36) that the two functions read.
+ * Both algorithms start from the reference's k-means++ (kmeans.cpp:45-89, same
+ * std::mt19937 draws) and produce the same assignments and centroids:
+ *   ELKAN  convergence test on the inertia of the current assignment, Kahan fp64 mean
+ *          x (1/count), a point keeps its centroid on a distance tie; result.inertia is
+ *          the inertia the loop stopped at (the reference's return value);
+ *   LLOYD  one run of kmeans_cluster (n_redo = 1): lowest index wins a tie, fp64 sum /
+ *          count, and after the loop one more mean update and the inertia of the final
+ *          assignment (an fp64 sum of per-point distances; the reference sums it in a
+ *          float running total, which differs by that total's rounding).
+ * Errors as the reference: k == 0 or n < k -> VESPER_ERROR_INVALID_PARAM with its message. */
+typedef enum vesper_kmeans_algorithm_e { VESPER_KMEANS_ELKAN = 0, VESPER_KMEANS_LLOYD = 1 } vesper_kmeans_algorithm_t;
+
+typedef struct vesper_kmeans_params_s {
+  size_t struct_size;      /* sizeof(vesper_kmeans_params_t) */
+  uint32_t k;
+  uint32_t max_iter;       /* default 25 */
+  float epsilon;           /* default 1e-4 */
+  uint32_t seed;           /* default 42 */
+  uint32_t algorithm;      /* vesper_kmeans_algorithm_t, default ELKAN */
+} vesper_kmeans_params_t;
+
+typedef struct vesper_kmeans_result_s {
+  uint32_t iterations;
+  float inertia;
+  float time_sec;          /* wall time of the call */
+} vesper_kmeans_result_t;
+
+VESPER_C_API void vesper_kmeans_params_init(vesper_kmeans_params_t* p);
+
+/* data [n x dim] host; out_centroids [k x dim] host; out_assignments [n] host or NULL;
+ * out_result may be NULL. */
+VESPER_C_API vesper_status_t vesper_kmeans_fit(const float* data, size_t n, size_t dim,
+                                               const vesper_kmeans_params_t* params, float* out_centroids,
+                                               uint32_t* out_assignments, vesper_kmeans_result_t* out_result);
+
+/* Same with data, centroids and assignments in device memory of the current device.
+ * The inputs must be complete when the call starts (it does not order itself after
+ * work queued on the caller's streams); the outputs are complete when it returns. */
+VESPER_C_API vesper_status_t vesper_kmeans_fit_device(const float* d_data, size_t n, size_t dim,
+                                                      const vesper_kmeans_params_t* params, float* d_out_centroids,
+                                                      uint32_t* d_out_assignments, vesper_kmeans_result_t* out_result);
+
 /* Number of CUDA devices visible to the library. */
 VESPER_C_API int vesper_b200_device_count(void);
 

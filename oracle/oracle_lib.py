@@ -64,6 +64,8 @@ class Oracle:
         L.orc_kmeans_elkan.restype = C.c_int
         L.orc_kmeans_elkan.argtypes = [_f32p, _sz, _sz, _u32, _u32, C.c_float, _u32, _f32p, _u32p,
                                        C.POINTER(_u32), C.POINTER(C.c_float)]
+        L.orc_kmeans_lloyd.restype = C.c_int
+        L.orc_kmeans_lloyd.argtypes = L.orc_kmeans_elkan.argtypes
         L.orc_pq_train.restype = C.c_int
         L.orc_pq_train.argtypes = [_f32p, _sz, _sz, _u32, _u32, _f32p]
 
@@ -197,6 +199,18 @@ class Oracle:
                                        C.byref(it), C.byref(inertia))
         if rc != 0:
             raise ValueError("kmeans_elkan: n < k")
+        return c, a, it.value, inertia.value
+
+    def kmeans_lloyd(self, x, k, max_iter=25, eps=1e-4, seed=42):
+        x = _f32(x)
+        c = np.zeros((k, x.shape[1]), np.float32)
+        a = np.zeros(x.shape[0], np.uint32)
+        it = _u32(0)
+        inertia = C.c_float(0)
+        rc = self.lib.orc_kmeans_lloyd(x, x.shape[0], x.shape[1], k, max_iter, eps, seed, c, a,
+                                       C.byref(it), C.byref(inertia))
+        if rc != 0:
+            raise ValueError("kmeans_lloyd: n < k or k == 0")
         return c, a, it.value, inertia.value
 
     def pq_train(self, x, m, nbits):

@@ -432,6 +432,39 @@ void orc_lloyd_update(const float* x, size_t n, size_t dim, const uint32_t* assi
                 c[size_t(a) * dim + d] = static_cast<float>(sums[size_t(a) * dim + d] / cnt[a]);
 }
 
+// kmeans_cluster (src/index/kmeans.cpp:137-252) with n_redo = 1: k-means++, Lloyd
+// iterations (assign, convergence test on the fp32-cast fp64 inertia, update), one more
+// update after the loop, and the returned inertia recomputed as the reference's final
+// single fp32 running sum over every (point, dimension) term (:230-241).
+int orc_kmeans_lloyd(const float* x, size_t n, size_t dim, uint32_t k, uint32_t max_iter,
+                     float eps, uint32_t seed, float* out_c, uint32_t* out_assign,
+                     uint32_t* out_iters, float* out_inertia) {
+    if (n < k) return 2;
+    if (k == 0) return 3;
+    kmeanspp(x, n, dim, k, seed, out_c, nullptr);
+    std::vector<uint32_t> asg(n);
+    float prev = std::numeric_limits<float>::max();
+    uint32_t it = 0;
+    for (; it < max_iter; ++it) {
+        const float inertia = orc_lloyd_assign(x, n, out_c, k, dim, asg.data());
+        const float change = std::fabs(prev - inertia) / (prev + 1e-10f);
+        if (change < eps) break;
+        prev = inertia;
+        orc_lloyd_update(x, n, dim, asg.data(), k, out_c);
+    }
+    orc_lloyd_update(x, n, dim, asg.data(), k, out_c);
+    float total = 0.0f;
+    for (size_t i = 0; i < n; ++i)
+        for (size_t d = 0; d < dim; ++d) {
+            const float diff = x[i * dim + d] - out_c[size_t(asg[i]) * dim + d];
+            total += diff * diff;
+        }
+    if (out_assign) std::copy(asg.begin(), asg.end(), out_assign);
+    if (out_iters) *out_iters = it;
+    if (out_inertia) *out_inertia = total;
+    return 0;
+}
+
 // Elkan M-step for every cluster: indices gathered in point order
 // (src/index/kmeans_elkan.cpp:354-356), then update_centroid.
 void orc_elkan_update_centroid(const float* x, size_t dim, const uint32_t* assign, size_t n,

@@ -63,6 +63,9 @@ void orc_elkan_update_centroid(const float* x, size_t dim, const uint32_t* assig
 int orc_kmeans_elkan(const float* x, size_t n, size_t dim, uint32_t k, uint32_t max_iter,
                      float eps, uint32_t seed, float* out_c, uint32_t* out_assign,
                      uint32_t* out_iters, float* out_inertia);
+int orc_kmeans_lloyd(const float* x, size_t n, size_t dim, uint32_t k, uint32_t max_iter,
+                     float eps, uint32_t seed, float* out_c, uint32_t* out_assign,
+                     uint32_t* out_iters, float* out_inertia);
 int orc_pq_train(const float* x, size_t n, size_t dim, uint32_t m, uint32_t nbits, float* out_cb);
 
 #ifdef __cplusplus

@@ -66,6 +66,32 @@ def test_train_params_ex_defaults():
     assert abs(p.epsilon - 1e-4) < 1e-9
 
 
+def test_kmeans_params_and_precondition_errors():
+    """kmeans_cluster's checks (src/index/kmeans.cpp:141-151) run before any device work."""
+    import numpy as np
+    lib = N.load()
+    p = N.KmeansParams()
+    lib.vesper_kmeans_params_init(C.byref(p))
+    assert p.struct_size == C.sizeof(N.KmeansParams)
+    assert (p.k, p.max_iter, p.seed, p.algorithm) == (256, 25, 42, N.KMEANS_ELKAN)
+    assert abs(p.epsilon - 1e-4) < 1e-9
+    x = np.zeros((10, 4), np.float32)
+    c = np.zeros((64, 4), np.float32)
+    f32 = C.POINTER(C.c_float)
+    xp, cp = x.ctypes.data_as(f32), c.ctypes.data_as(f32)
+    p.k = 11
+    assert lib.vesper_kmeans_fit(xp, 10, 4, C.byref(p), cp, None, None) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_get_last_error() == b"Not enough data points for k clusters"
+    p.k = 0
+    assert lib.vesper_kmeans_fit(xp, 10, 4, C.byref(p), cp, None, None) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_get_last_error() == b"k must be > 0"
+    p.k, p.algorithm = 4, 7
+    assert lib.vesper_kmeans_fit(xp, 10, 4, C.byref(p), cp, None, None) == N.VESPER_ERROR_INVALID_PARAM
+    p.algorithm = N.KMEANS_LLOYD
+    assert lib.vesper_kmeans_fit(None, 10, 4, C.byref(p), cp, None, None) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_kmeans_fit_device(None, 10, 4, C.byref(p), None, None, None) == N.VESPER_ERROR_INVALID_PARAM
+
+
 def test_missing_library_fails_loudly(tmp_path):
     N_mod = N
     saved = N_mod._lib

@@ -79,6 +79,11 @@ def test_golden_kmeans(oracle):
     assert np.array_equal(asg, g["assign"]) and np.float32(inert) == np.float32(g["assign_inertia"])
     assert np.array_equal(oracle.lloyd_update(x, asg, g["kpp"]), g["update"])
     assert np.array_equal(oracle.pq_train(x, 4, 8), g["pq_cb"])
+    c, a, it, inertia = oracle.kmeans_lloyd(x, 48, 20, 0.0, 42)
+    assert np.array_equal(c, g["lloyd_c"]) and np.array_equal(a, g["lloyd_a"])
+    assert it == int(g["lloyd_it"])
+    # the final inertia is the reference's sequential fp32 running sum, restated in order
+    assert inertia == float(g["lloyd_inertia"])
 
 
 def test_unit_topk_ties(oracle):
@@ -134,6 +139,9 @@ def test_oracle_vs_reference_random(oracle, reference):
     assert np.array_equal(oracle.kmeanspp_init(x, 30, 7)[0], reference.kmeanspp_init(x, 30, 7))
     e1, e2 = oracle.kmeans_elkan(x, 30, 25, 1e-4, 7), reference.kmeans_elkan(x, 30, 25, 1e-4, 7)
     assert np.array_equal(e1[0], e2[0]) and np.array_equal(e1[1], e2[1])
+    l1, l2 = oracle.kmeans_lloyd(x, 30, 10, 0.0, 7), reference.kmeans_lloyd(x, 30, 10, 0.0, 7)
+    assert np.array_equal(l1[0], l2[0]) and np.array_equal(l1[1], l2[1]) and l1[2] == l2[2]
+    assert abs(l1[3] - l2[3]) <= 1e-5 * l2[3]
     base = rng.standard_normal((3000, 40)).astype(np.float32)
     q = rng.standard_normal((17, 40)).astype(np.float32)
     for op in (0, 1):

@@ -34,7 +34,11 @@ EXPORTED = [
     "vesper_ivfpq_set_model", "vesper_ivfpq_get_lists", "vesper_b200_device_count",
     "vesper_ivfpq_train_ex_device", "vesper_ivfpq_add_device",
     "vesper_ivfpq_search_batch_device_noalloc",
+    "vesper_kmeans_params_init", "vesper_kmeans_fit", "vesper_kmeans_fit_device",
 ]
+
+KMEANS_ELKAN = 0
+KMEANS_LLOYD = 1
 
 
 class TrainParams(C.Structure):
@@ -72,6 +76,15 @@ class Timings(C.Structure):
                 ("scan_ms", C.c_float), ("merge_ms", C.c_float), ("total_ms", C.c_float),
                 ("scanned_entries", C.c_uint64), ("kernel_launches", C.c_uint32),
                 ("scan_variant", C.c_uint32), ("coarse_variant", C.c_uint32)]
+
+
+class KmeansParams(C.Structure):
+    _fields_ = [("struct_size", C.c_size_t), ("k", C.c_uint32), ("max_iter", C.c_uint32),
+                ("epsilon", C.c_float), ("seed", C.c_uint32), ("algorithm", C.c_uint32)]
+
+
+class KmeansResult(C.Structure):
+    _fields_ = [("iterations", C.c_uint32), ("inertia", C.c_float), ("time_sec", C.c_float)]
 
 
 _lib = None
@@ -128,6 +141,11 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_ivfpq_add_device": (st, [vp, vp, vp, C.c_size_t]),
             "vesper_ivfpq_search_batch_device_noalloc": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx),
                                                               vp, vp, vp]),
+            "vesper_kmeans_params_init": (None, [C.POINTER(KmeansParams)]),
+            "vesper_kmeans_fit": (st, [f32p, C.c_size_t, C.c_size_t, C.POINTER(KmeansParams), f32p, u32p,
+                                       C.POINTER(KmeansResult)]),
+            "vesper_kmeans_fit_device": (st, [vp, C.c_size_t, C.c_size_t, C.POINTER(KmeansParams), vp, vp,
+                                              C.POINTER(KmeansResult)]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

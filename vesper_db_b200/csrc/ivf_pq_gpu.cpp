@@ -21,6 +21,7 @@
 #include "kernels_opq.cuh"
 #include "kernels_tc.cuh"
 #include "kernels_train.cuh"
+#include "kmeans_gpu.hpp"
 #include "noalloc_search.hpp"
 
 namespace vesper::index {
@@ -86,18 +87,6 @@ bool env_flag(const char* name) {
     return v && v[0] == '1';
 }
 
-// Nearest-centroid search on the tensor cores (tcgen05 screen + exact refine) unless
-// the shapes or the pointer alignment rule it out, or VGPU_COARSE=exact asks for the
-// CUDA-core kernels; both give the same (exact) result.
-bool use_tc(const float* x, const float* c, int d, uint32_t k) {
-    static const bool off = [] {
-        const char* v = std::getenv("VGPU_COARSE");
-        return v && std::string(v) == "exact";
-    }();
-    return !off && k >= 64 && vgpu::tc_screen_supported(d) &&
-           ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15) == 0;
-}
-
 }  // namespace
 
 class IvfPqIndex::Impl {
@@ -150,6 +139,7 @@ public:
     mutable DeviceBuffer<uint64_t> w_out_ids;
     mutable DeviceBuffer<unsigned long long> w_scanned;
     mutable Pinned pin_a, pin_b, pin_c;
+    mutable std::unique_ptr<vgpu::KmeansEngine> kme;
 
     uint32_t nlist() const { return params.nlist; }
     uint32_t m() const { return params.m; }
@@ -215,37 +205,13 @@ public:
                                   d_vterm.data(), st);
     }
 
-    // Brute-force assignment with chunked distance tiles (the reference's brute
-    // branch, src/index/ivf_pq.cpp:3252-3265).  keep != nullptr -> Elkan tie rule.
-    void assign_rows(const float* d_x, size_t n, int d, const float* d_c, uint32_t k, uint32_t* d_assign,
-                     float* d_mind, bool keep, DeviceBuffer<float>& D) const {
-        const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * k)));
-        D.reserve(rows * k);
-        const bool tc = use_tc(d_x, d_c, d, k);
-        if (tc) {
-            w_cn.reserve(k);
-            w_xn.reserve(rows);
-            vgpu::launch_row_norms(d_c, k, d, w_cn.data(), st);
-            reset_err();
-        }
-        for (size_t r0 = 0; r0 < n; r0 += rows) {
-            const size_t nr = std::min(rows, n - r0);
-            const float* xr = d_x + r0 * (size_t)d;
-            if (tc) {
-                vgpu::launch_row_norms(xr, (long long)nr, d, w_xn.data(), st);
-                vgpu::launch_tc_screen(xr, (long long)nr, d_c, (int)k, d, w_xn.data(), w_cn.data(), D.data(),
-                                       (long long)k, d_err.data(), st);
-                vgpu::launch_screen_select(D.data(), (long long)nr, (long long)k, (int)k, xr, d, d_c, w_xn.data(),
-                                           w_cn.data(), 1, keep ? d_assign + r0 : nullptr, d_assign + r0,
-                                           d_mind ? d_mind + r0 : nullptr, d_err.data(), st);
-            } else {
-                vgpu::launch_l2_dist(xr, (long long)nr, d_c, (int)k, d, D.data(), (long long)k, st);
-                vgpu::launch_row_argmin(D.data(), (long long)nr, (int)k, (long long)k,
-                                        keep ? d_assign + r0 : nullptr, d_assign + r0,
-                                        d_mind ? d_mind + r0 : nullptr, st);
-            }
-        }
-        if (tc) check_err();
+    // Brute-force assignment (the reference's brute branch, src/index/ivf_pq.cpp:3252-3265).
+    void assign_rows(const float* d_x, size_t n, int d, const float* d_c, uint32_t k, uint32_t* d_assign) const {
+        kmeans_engine().assign(d_x, n, d, d_c, k, d_assign, nullptr, false);
+    }
+    vgpu::KmeansEngine& kmeans_engine() const {
+        if (!kme) kme = std::make_unique<vgpu::KmeansEngine>(st);
+        return *kme;
     }
 
     void reset_err() const {
@@ -268,60 +234,6 @@ public:
         double t = 0.0;
         for (size_t i = 0; i < n; ++i) t += h[i];
         return t;
-    }
-
-    // ------------------------------------------------------------------ k-means
-    // k-means++ (src/index/kmeans.cpp:45-89): the D^2 vector comes from the GPU, the
-    // cumulative sum, the draws and lower_bound run on the host with the same
-    // std::mt19937 / libstdc++ distributions as the reference.
-    void kmeanspp(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c) {
-        std::mt19937 gen(seed);
-        std::uniform_int_distribution<size_t> first(0, n - 1);
-        size_t idx = first(gen);
-        d2d(d_c, d_x + idx * d, (size_t)d, st);
-        DeviceBuffer<float> mind(n);
-        vgpu::launch_fill(mind.data(), (long long)n, std::numeric_limits<float>::max(), st);
-        float* h = pin_b.get<float>(n);
-        std::vector<double> cum(n);
-        for (uint32_t c = 1; c < k; ++c) {
-            vgpu::launch_kpp_update(d_x, (long long)n, d, d_c + (size_t)(c - 1) * d, mind.data(), st);
-            d2h(h, mind.data(), n, st);
-            sync(st);
-            cum[0] = h[0];
-            for (size_t i = 1; i < n; ++i) cum[i] = cum[i - 1] + h[i];
-            std::uniform_real_distribution<double> sd(0.0, cum.back());
-            const double target = sd(gen);
-            idx = (size_t)(std::lower_bound(cum.begin(), cum.end(), target) - cum.begin());
-            d2d(d_c + (size_t)c * d, d_x + idx * d, (size_t)d, st);
-        }
-    }
-
-    struct KmOut { uint32_t iterations; float inertia; };
-
-    // KmeansElkan::cluster (src/index/kmeans_elkan.cpp:293-430) semantics: exact
-    // E-step (Elkan prunes only provably-farther centroids, so its assignment is the
-    // strict-< arg-min that keeps the current centroid on a tie), convergence test on
-    // the fp64-summed inertia before the M-step, Kahan M-step in point order.
-    KmOut kmeans(const float* d_x, size_t n, int d, uint32_t k, uint32_t max_iter, float eps,
-                 uint32_t seed, float* d_c, uint32_t* d_assign) {
-        kmeanspp(d_x, n, d, k, seed, d_c);
-        DeviceBuffer<float> mind(n), D;
-        DeviceBuffer<uint32_t> order(n), seg(k + 1);
-        vgpu::GroupWork gw;
-        assign_rows(d_x, n, d, d_c, k, d_assign, mind.data(), false, D);
-        float prev = std::numeric_limits<float>::max();
-        uint32_t it = 0;
-        for (; it < max_iter; ++it) {
-            if (it > 0) assign_rows(d_x, n, d, d_c, k, d_assign, mind.data(), true, D);
-            const float inertia = (float)ordered_sum(mind.data(), n);
-            const float change = std::fabs(prev - inertia) / (prev + 1e-10f);
-            if (change < eps) break;
-            prev = inertia;
-            vgpu::group_by_key(d_assign, (long long)n, (int)k, order.data(), seg.data(), gw, st);
-            vgpu::launch_segment_mean(d_x, d, order.data(), seg.data(), (int)k, 1, d_c, st);
-        }
-        sync(st);
-        return {it, prev};
     }
 
     // FastScanPq::train (src/index/pq_fastscan.cpp:15-76): one k-means per sub-space,
@@ -515,19 +427,18 @@ public:
         DeviceBuffer<uint32_t> assign(n);
         IvfPqTrainStats stats;
         // Step 1: coarse quantizer (train_coarse_quantizer, :561-671).
-        auto km = kmeans(xp, n, (int)dim, nlist(), p.max_iter, p.epsilon, p.seed, d_cent.data(),
-                         assign.data());
+        auto km = kmeans_engine().fit(xp, n, (int)dim, nlist(), p.max_iter, p.epsilon, p.seed, true,
+                                      d_cent.data(), assign.data());
         stats.coarse_iterations = km.iterations;
         h_cent.resize((size_t)nlist() * dim);
         d2h(h_cent.data(), d_cent.data(), h_cent.size(), st);
 
         // Residuals of the training data w.r.t. the nearest centroid (:477-494, :2414-2432).
-        DeviceBuffer<float> D, res(n * dim);
-        assign_rows(xp, n, (int)dim, d_cent.data(), nlist(), assign.data(), nullptr, false, D);
+        DeviceBuffer<float> res(n * dim);
+        assign_rows(xp, n, (int)dim, d_cent.data(), nlist(), assign.data());
         vgpu::launch_residual_rotate(xp, nullptr, d_cent.data(), assign.data(), (long long)n, (int)dim,
                                      nullptr, res.data(), st);
         x_own.release();
-        D.release();
 
         // Step 2: OPQ PCA initialisation (:457-519).
         if (p.use_opq && p.opq_init == OpqInit::PCA) {
@@ -649,7 +560,7 @@ public:
         DeviceBuffer<uint8_t> new_codes(n * M);
         {
             const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * std::max<size_t>(nlist(), dim))));
-            DeviceBuffer<float> x(on_device ? 0 : rows * dim), res(rows * dim), D;
+            DeviceBuffer<float> x(on_device ? 0 : rows * dim), res(rows * dim);
             for (size_t r0 = 0; r0 < n; r0 += rows) {
                 const size_t nr = std::min(rows, n - r0);
                 const float* xr = data + r0 * dim;
@@ -657,7 +568,7 @@ public:
                     h2d(x.data(), xr, nr * dim, st);
                     xr = x.data();
                 }
-                assign_rows(xr, nr, (int)dim, d_cent.data(), nlist(), assign.data() + r0, nullptr, false, D);
+                assign_rows(xr, nr, (int)dim, d_cent.data(), nlist(), assign.data() + r0);
                 vgpu::launch_residual_rotate(xr, nullptr, d_cent.data(), assign.data() + r0, (long long)nr,
                                              (int)dim, has_rot ? d_rot.data() : nullptr, res.data(), st);
                 vgpu::launch_pq_encode(res.data(), (long long)nr, (int)M, (int)ksub, (int)dsub, d_cb.data(),
@@ -779,7 +690,7 @@ public:
                 od = w_out_d.data();
                 on = w_out_n.data();
             }
-            const bool tc = use_tc(dq, d_cent.data(), (int)dim, nlist());
+            const bool tc = vgpu::use_tensor_cores(dq, d_cent.data(), (int)dim, nlist());
             cudaEventRecord(ev[0], st);
             if (tc) {
                 w_xn.reserve(qc);

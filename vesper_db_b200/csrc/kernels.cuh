@@ -113,5 +113,8 @@ void launch_kpp_update(const float* x, long long n, int dim, const float* c, flo
 // keep their centroid.
 void launch_segment_mean(const float* x, int dim, const uint32_t* order, const uint32_t* seg,
                          int k, int kahan, float* centroids, cudaStream_t st);
+// out[i] = l2(x_i, c[assign[i]]) in reference order.
+void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,
+                        cudaStream_t st);
 
 }  // namespace vgpu

@@ -1,0 +1,151 @@
+// GPU k-means engine (see kmeans_gpu.hpp).
+#include "kmeans_gpu.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <limits>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "kernels_tc.cuh"
+
+namespace vgpu {
+
+namespace {
+constexpr size_t kDistBudget = size_t(512) << 20;  // bytes per distance-matrix chunk
+}  // namespace
+
+bool use_tensor_cores(const float* x, const float* c, int d, uint32_t k) {
+    static const bool off = [] {
+        const char* v = std::getenv("VGPU_COARSE");
+        return v && std::string(v) == "exact";
+    }();
+    return !off && k >= 64 && tc_screen_supported(d) &&
+           ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15) == 0;
+}
+
+KmeansEngine::~KmeansEngine() {
+    if (pin_) cudaFreeHost(pin_);
+}
+
+float* KmeansEngine::pinned(size_t n) {
+    if (n * sizeof(float) > pin_bytes_) {
+        if (pin_) cudaFreeHost(pin_);
+        check(cudaMallocHost(&pin_, n * sizeof(float)), "cudaMallocHost");
+        pin_bytes_ = n * sizeof(float);
+    }
+    return static_cast<float*>(pin_);
+}
+
+double KmeansEngine::ordered_sum(const float* d, size_t n) {
+    float* h = pinned(n);
+    check(cudaMemcpyAsync(h, d, n * sizeof(float), cudaMemcpyDeviceToHost, st_), "d2h");
+    check(cudaStreamSynchronize(st_), "sync");
+    double t = 0.0;
+    for (size_t i = 0; i < n; ++i) t += h[i];
+    return t;
+}
+
+void KmeansEngine::assign(const float* d_x, size_t n, int d, const float* d_c, uint32_t k, uint32_t* d_assign,
+                          float* d_mind, bool keep) {
+    const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * k)));
+    D_.reserve(rows * k);
+    const bool tc = use_tensor_cores(d_x, d_c, d, k);
+    if (tc) {
+        cn_.reserve(k);
+        xn_.reserve(rows);
+        err_.reserve(1);
+        launch_row_norms(d_c, k, d, cn_.data(), st_);
+        check(cudaMemsetAsync(err_.data(), 0, sizeof(int), st_), "memset err");
+    }
+    for (size_t r0 = 0; r0 < n; r0 += rows) {
+        const size_t nr = std::min(rows, n - r0);
+        const float* xr = d_x + r0 * (size_t)d;
+        if (tc) {
+            launch_row_norms(xr, (long long)nr, d, xn_.data(), st_);
+            launch_tc_screen(xr, (long long)nr, d_c, (int)k, d, xn_.data(), cn_.data(), D_.data(), (long long)k,
+                             err_.data(), st_);
+            launch_screen_select(D_.data(), (long long)nr, (long long)k, (int)k, xr, d, d_c, xn_.data(), cn_.data(), 1,
+                                 keep ? d_assign + r0 : nullptr, d_assign + r0, d_mind ? d_mind + r0 : nullptr,
+                                 err_.data(), st_);
+        } else {
+            launch_l2_dist(xr, (long long)nr, d_c, (int)k, d, D_.data(), (long long)k, st_);
+            launch_row_argmin(D_.data(), (long long)nr, (int)k, (long long)k, keep ? d_assign + r0 : nullptr,
+                              d_assign + r0, d_mind ? d_mind + r0 : nullptr, st_);
+        }
+    }
+    if (tc) {
+        int e = 0;
+        check(cudaMemcpyAsync(&e, err_.data(), sizeof(int), cudaMemcpyDeviceToHost, st_), "d2h err");
+        check(cudaStreamSynchronize(st_), "sync");
+        if (e) throw CudaError("tensor-core screen: bounded wait expired (code " + std::to_string(e) + ")");
+    }
+}
+
+// The D^2 vector comes from the GPU; the fp64 prefix sum, the draws and lower_bound
+// run on the host with the reference's std::mt19937 and libstdc++ distributions.
+void KmeansEngine::kmeanspp(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c) {
+    std::mt19937 gen(seed);
+    std::uniform_int_distribution<size_t> first(0, n - 1);
+    size_t idx = first(gen);
+    check(cudaMemcpyAsync(d_c, d_x + idx * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, st_), "d2d");
+    kpp_.reserve(n);
+    launch_fill(kpp_.data(), (long long)n, std::numeric_limits<float>::max(), st_);
+    float* h = pinned(n);
+    std::vector<double> cum(n);
+    for (uint32_t c = 1; c < k; ++c) {
+        launch_kpp_update(d_x, (long long)n, d, d_c + (size_t)(c - 1) * d, kpp_.data(), st_);
+        check(cudaMemcpyAsync(h, kpp_.data(), n * sizeof(float), cudaMemcpyDeviceToHost, st_), "d2h");
+        check(cudaStreamSynchronize(st_), "sync");
+        cum[0] = h[0];
+        for (size_t i = 1; i < n; ++i) cum[i] = cum[i - 1] + h[i];
+        std::uniform_real_distribution<double> sd(0.0, cum.back());
+        const double target = sd(gen);
+        idx = (size_t)(std::lower_bound(cum.begin(), cum.end(), target) - cum.begin());
+        check(cudaMemcpyAsync(d_c + (size_t)c * d, d_x + idx * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, st_),
+              "d2d");
+    }
+}
+
+// Elkan (KmeansElkan::cluster): exact E-step with the keep-on-tie rule (Elkan prunes
+// only provably farther centroids), convergence test on the fp64-summed inertia
+// before the M-step, Kahan M-step in point order; returns the last converged-from
+// inertia and the iteration count, as the reference does.
+// Lloyd (kmeans_cluster): lowest-index E-step, the same test, fp64 sum / count
+// M-step; after the loop one more M-step and the inertia of the final assignment.
+KmeansResultGpu KmeansEngine::fit(const float* d_x, size_t n, int d, uint32_t k, uint32_t max_iter, float eps,
+                                  uint32_t seed, bool elkan, float* d_c, uint32_t* d_assign) {
+    kmeanspp(d_x, n, d, k, seed, d_c);
+    mind_.reserve(n);
+    order_.reserve(n);
+    seg_.reserve(k + 1);
+    if (elkan) assign(d_x, n, d, d_c, k, d_assign, mind_.data(), false);
+    float prev = std::numeric_limits<float>::max();
+    uint32_t it = 0;
+    for (; it < max_iter; ++it) {
+        if (!elkan || it > 0) assign(d_x, n, d, d_c, k, d_assign, mind_.data(), elkan);
+        const float inertia = (float)ordered_sum(mind_.data(), n);
+        const float change = std::fabs(prev - inertia) / (prev + 1e-10f);
+        if (change < eps) break;
+        prev = inertia;
+        group_by_key(d_assign, (long long)n, (int)k, order_.data(), seg_.data(), gw_, st_);
+        launch_segment_mean(d_x, d, order_.data(), seg_.data(), (int)k, elkan ? 1 : 0, d_c, st_);
+    }
+    KmeansResultGpu r;
+    r.iterations = it;
+    if (elkan) {
+        r.inertia = prev;
+    } else {
+        group_by_key(d_assign, (long long)n, (int)k, order_.data(), seg_.data(), gw_, st_);
+        launch_segment_mean(d_x, d, order_.data(), seg_.data(), (int)k, 0, d_c, st_);
+        launch_assigned_l2(d_x, d_c, d_assign, (long long)n, d, mind_.data(), st_);
+        r.inertia = (float)ordered_sum(mind_.data(), n);
+    }
+    check(cudaStreamSynchronize(st_), "sync");
+    return r;
+}
+
+}  // namespace vgpu

@@ -97,3 +97,48 @@ void launch_segment_mean(const float* x, int dim, const uint32_t* order, const u
 }
 
 }  // namespace vgpu
+
+namespace vgpu {
+
+// out[i] = l2_ref(x_i, c[assign[i]]) (one warp per row, lanes 0..7 run the 8 chains).
+__global__ void assigned_l2_kernel(const float* __restrict__ x, const float* __restrict__ c,
+                                   const uint32_t* __restrict__ assign, long long n, int dim,
+                                   float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    const int simd_end = dim & ~7;
+    for (long long i = warp; i < n; i += nw) {
+        const float* p = x + i * dim;
+        const float* q = c + (long long)assign[i] * dim;
+        float acc = 0.0f;
+        if (lane < 8)
+            for (int t = lane; t < simd_end; t += 8) {
+                const float d = __fsub_rn(p[t], q[t]);
+                acc = __fmaf_rn(d, d, acc);
+            }
+        const float a4 = __shfl_down_sync(0xffffffffu, acc, 4);
+        const float s = __fadd_rn(a4, acc);
+        const float s1 = __shfl_down_sync(0xffffffffu, s, 1);
+        const float s2 = __shfl_down_sync(0xffffffffu, s, 2);
+        const float s3 = __shfl_down_sync(0xffffffffu, s, 3);
+        if (lane == 0) {
+            float r = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+            for (int t = simd_end; t < dim; ++t) {
+                const float d = __fsub_rn(p[t], q[t]);
+                r = __fadd_rn(r, __fmul_rn(d, d));
+            }
+            out[i] = r;
+        }
+    }
+}
+
+void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,
+                        cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n * 32 + 255) / 256, 148LL * 64);
+    assigned_l2_kernel<<<blocks, 256, 0, st>>>(x, c, assign, n, dim, out);
+    VGPU_LAUNCH("assigned_l2_kernel");
+}
+
+}  // namespace vgpu

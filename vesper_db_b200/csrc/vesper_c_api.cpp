@@ -8,6 +8,7 @@
 // UNKNOWN.  The last error is a thread-local string.
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstring>
 #include <memory>
 #include <new>
@@ -15,6 +16,7 @@
 
 #include "../../include/vesper_b200.h"
 #include "ivf_pq_gpu.hpp"
+#include "kmeans_gpu.hpp"
 
 using vesper::index::IvfPqIndex;
 using vesper::index::IvfPqSearchParams;
@@ -389,6 +391,96 @@ VESPER_C_API vesper_status_t vesper_ivfpq_load(vesper_index_t* index, const char
         index->ivfpq = std::make_unique<IvfPqIndex>(std::move(*r));
         return VESPER_OK;
     });
+}
+
+VESPER_C_API void vesper_kmeans_params_init(vesper_kmeans_params_t* p) {
+    if (!p) return;
+    std::memset(p, 0, sizeof(*p));
+    p->struct_size = sizeof(*p);
+    p->k = 256;
+    p->max_iter = 25;
+    p->epsilon = 1e-4f;
+    p->seed = 42;
+    p->algorithm = VESPER_KMEANS_ELKAN;
+}
+
+}  // extern "C"
+
+namespace {
+// Shared body of vesper_kmeans_fit / _fit_device: on_device says where data and the
+// outputs live.  Checks follow kmeans_cluster (src/index/kmeans.cpp:141-151).
+vesper_status_t kmeans_fit(const float* data, size_t n, size_t dim, const vesper_kmeans_params_t* p,
+                           float* out_c, uint32_t* out_a, vesper_kmeans_result_t* out_r, bool on_device) {
+    if (!data || !p || !out_c || dim == 0 || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < sizeof(vesper_kmeans_params_t) || p->algorithm > VESPER_KMEANS_LLOYD)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    if (n < p->k) {
+        set_error("Not enough data points for k clusters");
+        return VESPER_ERROR_INVALID_PARAM;
+    }
+    if (p->k == 0) {
+        set_error("k must be > 0");
+        return VESPER_ERROR_INVALID_PARAM;
+    }
+    if (dim > (size_t)INT32_MAX) return VESPER_ERROR_INVALID_PARAM;
+    return guarded("kmeans", [&] {
+        const auto t0 = std::chrono::steady_clock::now();
+        cudaStream_t st = nullptr;
+        vgpu::check(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "cudaStreamCreate");
+        struct StreamOwner {
+            cudaStream_t s;
+            ~StreamOwner() { cudaStreamSynchronize(s); cudaStreamDestroy(s); }
+        } owner{st};
+        vgpu::DeviceBuffer<float> x_own, c_own;
+        vgpu::DeviceBuffer<uint32_t> a_own;
+        const float* x = data;
+        float* c = out_c;
+        uint32_t* a = out_a;
+        if (!on_device) {
+            x_own.resize(n * dim);
+            vgpu::check(cudaMemcpyAsync(x_own.data(), data, n * dim * sizeof(float), cudaMemcpyHostToDevice, st),
+                        "h2d");
+            x = x_own.data();
+            c_own.resize((size_t)p->k * dim);
+            c = c_own.data();
+        }
+        if (!on_device || !out_a) {
+            a_own.resize(n);
+            a = a_own.data();
+        }
+        vgpu::KmeansEngine eng(st);
+        const auto r = eng.fit(x, n, (int)dim, p->k, p->max_iter, p->epsilon, p->seed,
+                               p->algorithm == VESPER_KMEANS_ELKAN, c, a);
+        if (!on_device) {
+            vgpu::check(cudaMemcpyAsync(out_c, c, (size_t)p->k * dim * sizeof(float), cudaMemcpyDeviceToHost, st),
+                        "d2h");
+            if (out_a)
+                vgpu::check(cudaMemcpyAsync(out_a, a, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
+        }
+        vgpu::check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        if (out_r) {
+            out_r->iterations = r.iterations;
+            out_r->inertia = r.inertia;
+            out_r->time_sec = std::chrono::duration<float>(std::chrono::steady_clock::now() - t0).count();
+        }
+        return VESPER_OK;
+    });
+}
+}  // namespace
+
+extern "C" {
+
+VESPER_C_API vesper_status_t vesper_kmeans_fit(const float* data, size_t n, size_t dim,
+                                               const vesper_kmeans_params_t* params, float* out_centroids,
+                                               uint32_t* out_assignments, vesper_kmeans_result_t* out_result) {
+    return kmeans_fit(data, n, dim, params, out_centroids, out_assignments, out_result, false);
+}
+
+VESPER_C_API vesper_status_t vesper_kmeans_fit_device(const float* d_data, size_t n, size_t dim,
+                                                      const vesper_kmeans_params_t* params, float* d_out_centroids,
+                                                      uint32_t* d_out_assignments, vesper_kmeans_result_t* out_result) {
+    return kmeans_fit(d_data, n, dim, params, d_out_centroids, d_out_assignments, out_result, true);
 }
 
 VESPER_C_API int vesper_b200_device_count(void) {
