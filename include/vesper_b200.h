@@ -116,8 +116,16 @@ typedef struct vesper_ivfpq_timings_s {
   float total_ms;
   uint64_t scanned_entries; /* sum over queries of the probed lists' sizes */
   uint32_t kernel_launches; /* kernels launched by the call */
-  uint32_t scan_variant;    /* 1 exact per-(query, list) tables, 2 per-query tables, 3 blocked layout */
+  uint32_t scan_variant;    /* 1 exact per-(query, list) tables, 2 per-query tables, 3 blocked layout,
+                               4 tensor-core list scan (bf16 screen + exact FAST refine) */
   uint32_t coarse_variant;  /* 1 CUDA-core exact distances, 2 tensor-core screen + exact refine */
+  float list_kernel_ms;     /* variant 4: device time of the tensor-core screening kernel */
+  uint64_t list_candidates; /* variant 4: (query, entry) pairs the screen kept */
+  uint32_t list_fallback_queries; /* variant 4: queries scanned by the blocked scan instead */
+  float list_threshold_ms;  /* variant 4: nearest-list scan that gives the screen thresholds */
+  float list_prep_ms;       /* variant 4: bf16 queries, pair grouping by list, unit table */
+  float list_refine_ms;     /* variant 4: exact FAST re-scoring of the kept pairs */
+  float list_fallback_ms;   /* variant 4: blocked scan of queries whose candidates overflowed */
 } vesper_ivfpq_timings_t;
 VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index,
                                                            vesper_ivfpq_timings_t* out);

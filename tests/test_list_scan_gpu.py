@@ -1,0 +1,96 @@
+"""Tensor-core list scan (FAST mode, VGPU_SCAN=tc) against the blocked scan.
+
+The list scan screens (query, entry) pairs with bf16 tcgen05 products and re-scores the
+survivors with the blocked scan's own arithmetic and scan positions, so its results
+must equal the blocked scan's bit for bit: ids, distances and counts.  The cases cover
+every supported sub-vector width (dim / m = 4, 8, 16), both accumulator widths (N = 128
+for dim <= 512, N = 64 above), OPQ rotations, ragged 128-entry tiles, queries whose
+nearest list holds fewer than k entries (not screened), candidate-list overflow (the
+blocked-scan fallback), and exact ties (duplicated vectors).
+"""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _index():
+    from vesper_db_b200 import IvfPqIndex
+    return IvfPqIndex()
+
+
+def _search(idx, q, k, npb, scan):
+    old = os.environ.get("VGPU_SCAN")
+    os.environ["VGPU_SCAN"] = scan
+    try:
+        out = idx.search_batch(q, k, npb)
+        variant = idx.last_timings()["scan_variant"]
+    finally:
+        if old is None:
+            del os.environ["VGPU_SCAN"]
+        else:
+            os.environ["VGPU_SCAN"] = old
+    return out, variant
+
+
+def _build(rng, dim, m, nlist, n, rot, sigma=0.3, dup=0):
+    cent = rng.standard_normal((nlist, dim)).astype(np.float32)
+    cb = (0.3 * rng.standard_normal((m * 256, dim // m))).astype(np.float32)
+    R = np.linalg.qr(rng.standard_normal((dim, dim)))[0].astype(np.float32) if rot else None
+    base = (cent[rng.integers(0, nlist, n)] + sigma * rng.standard_normal((n, dim))).astype(np.float32)
+    if dup:
+        base[-dup:] = base[:dup]
+    idx = _index()
+    idx.set_model(cent, cb, R)
+    idx.add(np.arange(n, dtype=np.uint64) * 7 + 3, base)
+    return idx, cent
+
+
+CASES = [
+    # dim, m, nlist, n, nq, rot, searches (k, nprobe)
+    (128, 16, 64, 40000, 300, False, [(10, 8), (100, 16), (1, 2)]),
+    (128, 32, 64, 40000, 300, True, [(10, 8), (50, 33)]),
+    (256, 16, 32, 30000, 200, True, [(10, 6), (100, 12)]),
+    (768, 96, 48, 20000, 130, True, [(10, 8), (100, 20)]),
+    (512, 64, 40, 20000, 150, False, [(20, 10)]),
+]
+
+
+@pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES)
+def test_list_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches):
+    rng = np.random.default_rng(dim + m + nlist)
+    idx, cent = _build(rng, dim, m, nlist, n, rot)
+    q = (cent[rng.integers(0, nlist, nq)] + 0.3 * rng.standard_normal((nq, dim))).astype(np.float32)
+    for k, npb in searches:
+        (bi, bd, bn), vb = _search(idx, q, k, npb, "blocked")
+        (ti, td, tn), vt = _search(idx, q, k, npb, "tc")
+        assert vb == 3 and vt == 4
+        assert np.array_equal(bn, tn)
+        assert np.array_equal(bd, td)
+        assert np.array_equal(bi, ti)
+
+
+def test_small_home_lists_and_overflow():
+    """Many lists smaller than k (those queries skip the screen), and k large enough that
+    some candidate lists overflow (the blocked scan takes those queries over)."""
+    rng = np.random.default_rng(77)
+    dim, m = 128, 16
+    idx, cent = _build(rng, dim, m, 300, 12000, True, sigma=0.05)
+    q = (cent[rng.integers(0, 300, 200)] + 0.05 * rng.standard_normal((200, dim))).astype(np.float32)
+    for k, npb in [(100, 10), (1000, 40), (64, 300)]:
+        (bi, bd, bn), _ = _search(idx, q, k, npb, "blocked")
+        (ti, td, tn), vt = _search(idx, q, k, npb, "tc")
+        assert vt == 4
+        assert np.array_equal(bn, tn) and np.array_equal(bd, td) and np.array_equal(bi, ti)
+
+
+def test_exact_ties_keep_scan_order():
+    rng = np.random.default_rng(5)
+    idx, cent = _build(rng, 128, 16, 32, 20000, False, dup=6000)
+    q = (cent[rng.integers(0, 32, 256)] + 0.3 * rng.standard_normal((256, 128))).astype(np.float32)
+    for k, npb in [(10, 4), (200, 8)]:
+        (bi, bd, bn), _ = _search(idx, q, k, npb, "blocked")
+        (ti, td, tn), _ = _search(idx, q, k, npb, "tc")
+        assert np.array_equal(bn, tn) and np.array_equal(bd, td) and np.array_equal(bi, ti)

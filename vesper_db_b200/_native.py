@@ -75,7 +75,10 @@ class Timings(C.Structure):
     _fields_ = [("coarse_ms", C.c_float), ("select_ms", C.c_float), ("rotate_ms", C.c_float),
                 ("scan_ms", C.c_float), ("merge_ms", C.c_float), ("total_ms", C.c_float),
                 ("scanned_entries", C.c_uint64), ("kernel_launches", C.c_uint32),
-                ("scan_variant", C.c_uint32), ("coarse_variant", C.c_uint32)]
+                ("scan_variant", C.c_uint32), ("coarse_variant", C.c_uint32),
+                ("list_kernel_ms", C.c_float), ("list_candidates", C.c_uint64),
+                ("list_fallback_queries", C.c_uint32), ("list_threshold_ms", C.c_float),
+                ("list_prep_ms", C.c_float), ("list_refine_ms", C.c_float), ("list_fallback_ms", C.c_float)]
 
 
 class KmeansParams(C.Structure):

@@ -33,6 +33,7 @@ using vgpu::DeviceBuffer;
 namespace {
 
 constexpr size_t kDistBudget = size_t(512) << 20;  // bytes per distance-matrix chunk
+constexpr int kListScanCap = 2048;                   // screened candidates kept per query
 
 auto fail(error_code c, std::string msg, std::string comp = "ivf_pq") {
     return std::unexpected(error{c, std::move(msg), std::move(comp)});
@@ -129,6 +130,11 @@ public:
     DeviceBuffer<uint64_t> d_blk_off;
     DeviceBuffer<uint8_t> d_bcodes;
     DeviceBuffer<float> d_bvterm;
+    // Tensor-core list scan: bf16 codebooks, per-entry decoded norms, batch scratch.
+    DeviceBuffer<uint16_t> d_cbb;
+    DeviceBuffer<float> d_xnorm;
+    mutable vgpu::TlWork tlw;
+    mutable DeviceBuffer<float> w_pbase;
 
     double t_assign_ms = 0, t_encode_ms = 0, t_lists_ms = 0;
     mutable SearchTimings timings;
@@ -178,12 +184,14 @@ public:
         has_blocks = false;
         d_bcodes.release();
         d_bvterm.release();
+        d_xnorm.release();
     }
 
     void rebuild_blocks() {
         has_blocks = false;
         d_bcodes.release();
         d_bvterm.release();
+        d_xnorm.release();
         if (!vgpu::scan_blocked_supported((int)m(), (int)ksub)) return;
         std::vector<uint64_t> boff(nlist() + 1, 0);
         for (uint32_t l = 0; l < nlist(); ++l) boff[l + 1] = boff[l] + (h_offs[l + 1] - h_offs[l] + 127) / 128;
@@ -194,8 +202,28 @@ public:
         d_bvterm.resize(std::max<uint64_t>(nb, 1) * 128);
         if (nb) vgpu::launch_build_blocks(d_codes.data(), d_vterm.data(), d_offs.data(), d_blk_off.data(), (int)m(),
                                           (int)nlist(), d_bcodes.data(), d_bvterm.data(), st);
+        if (vgpu::tc_list_scan_supported((int)dim, (int)m(), (int)ksub)) {
+            // Tensor-core list scan: bf16 codebooks and per-entry decoded norms.
+            d_cbb.resize((size_t)m() * ksub * dsub);
+            vgpu::launch_codebook_bf16(d_cb.data(), (long long)d_cbb.size(), d_cbb.data(), st);
+            d_xnorm.resize(std::max<size_t>(n_vectors, 1));
+            vgpu::launch_entry_norms(d_codes.data(), (long long)n_vectors, d_cb.data(), (int)m(), (int)dsub,
+                                     d_xnorm.data(), st);
+        }
         sync(st);
         has_blocks = true;
+    }
+
+    // FAST-scan kernel for this call: the tensor-core list scan where the shapes allow
+    // it and the batch scans enough entries per query to amortise its set-up, else the
+    // blocked scan.  VGPU_SCAN=tc / blocked overrides the choice.
+    bool use_list_scan(size_t nq, uint32_t np) const {
+        if (!has_blocks || np < 2 || !vgpu::tc_list_scan_supported((int)dim, (int)m(), (int)ksub)) return false;
+        const char* v = std::getenv("VGPU_SCAN");
+        if (v && std::string(v) == "tc") return true;
+        if (v && std::string(v) == "blocked") return false;
+        const double per_query = (double)n_vectors / std::max<uint32_t>(nlist(), 1) * np;
+        return per_query >= 4096.0 && nq >= 256;
     }
 
     void recompute_vterms() {
@@ -668,6 +696,13 @@ public:
         } else {
             w_rq.reserve(qc * dim);
             w_T.reserve(qc * (size_t)m() * ksub);
+            w_pbase.reserve(qc * np);
+        }
+        const bool list_scan = !exact && use_list_scan(nq, np);
+        if (list_scan) {
+            tlw.reserve((long long)qc, (int)np, (int)nlist(), (int)dim, (int)k, kListScanCap, n_vectors);
+            vgpu::check(cudaMemsetAsync(tlw.stats.data(), 0, 2 * sizeof(unsigned long long), st), "memset");
+            reset_err();
         }
         SearchTimings tm;
         w_scanned.reserve(1);
@@ -739,11 +774,24 @@ public:
                 if (has_blocks) {
                     vgpu::launch_lut_blocked(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)dsub,
                                              w_T.data(), st);
+                    vgpu::launch_probe_base(rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
+                                            has_rot ? d_rc.data() : nullptr, (int)np, w_pbase.data(), st);
                     cudaEventRecord(ev[3], st);
-                    vgpu::launch_scan_blocked(w_T.data(), rq, (long long)nc, (int)dim, w_probe.data(),
-                                              w_probe_d.data(), has_rot ? d_rc.data() : nullptr, (int)np, (int)m(),
-                                              d_offs.data(), d_blk_off.data(), d_bcodes.data(), d_bvterm.data(),
-                                              d_ids.data(), (int)k, oid, od, on, st);
+                    if (list_scan) {
+                        vgpu::TlScanArgs a{};
+                        a.T = w_T.data(); a.rq = rq; a.pbase = w_pbase.data(); a.probe = w_probe.data();
+                        a.nq = (long long)nc; a.nprobe = (int)np; a.nlist = (int)nlist(); a.dim = (int)dim;
+                        a.m = (int)m(); a.k = (int)k; a.offs = d_offs.data(); a.codes = d_codes.data();
+                        a.vterm = d_vterm.data(); a.xnorm = d_xnorm.data(); a.cbb = d_cbb.data();
+                        a.blk_off = d_blk_off.data(); a.bcodes = d_bcodes.data(); a.bvterm = d_bvterm.data();
+                        a.ids = d_ids.data(); a.out_ids = oid; a.out_d = od; a.out_n = on; a.err = d_err.data();
+                        vgpu::launch_tc_list_scan(a, tlw, st);
+                    } else {
+                        vgpu::launch_scan_blocked(w_T.data(), (long long)nc, w_pbase.data(), w_probe.data(), (int)np,
+                                                  (int)np, (int)m(), d_offs.data(), d_blk_off.data(),
+                                                  d_bcodes.data(), d_bvterm.data(), d_ids.data(), (int)k, oid, od,
+                                                  on, nullptr, 0, st);
+                    }
                 } else {
                     vgpu::launch_lut_fast(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)ksub, (int)dsub,
                                           w_T.data(), st);
@@ -756,8 +804,9 @@ public:
                 cudaEventRecord(ev[4], st);
             }
             cudaEventRecord(ev[5], st);
-            tm.kernel_launches += 3 + (exact ? 2 : 2) + (has_rot ? 1 : 0) + (tc ? 1 : 0);
-            tm.scan_variant = exact ? 1u : (has_blocks ? 3u : 2u);
+            tm.kernel_launches += 3 + (exact ? 2 : 2) + (has_rot ? 1 : 0) + (tc ? 1 : 0) +
+                                  (!exact && has_blocks ? 1 : 0) + (list_scan ? 12 : 0);
+            tm.scan_variant = exact ? 1u : list_scan ? 4u : (has_blocks ? 3u : 2u);
             tm.coarse_variant = tc ? 2u : 1u;
             if (!on_device) {
                 d2h(out_ids + q0 * k, oid, nc * k, st);
@@ -765,7 +814,7 @@ public:
                 if (out_n) d2h(out_n + q0, on, nc, st);
             }
             sync(st);
-            if (tc) check_err();
+            if (tc || list_scan) check_err();
             float a = 0;
             cudaEventElapsedTime(&a, ev[0], ev[1]); tm.coarse_ms += a;
             cudaEventElapsedTime(&a, ev[1], ev[2]); tm.select_ms += a;
@@ -773,6 +822,20 @@ public:
             cudaEventElapsedTime(&a, ev[3], ev[4]); tm.scan_ms += a;
             cudaEventElapsedTime(&a, ev[4], ev[5]); tm.merge_ms += a;
             cudaEventElapsedTime(&a, ev[0], ev[5]); tm.total_ms += a;
+            if (list_scan) {
+                cudaEventElapsedTime(&a, tlw.ev[0], tlw.ev[1]); tm.list_threshold_ms += a;
+                cudaEventElapsedTime(&a, tlw.ev[1], tlw.ev[2]); tm.list_prep_ms += a;
+                cudaEventElapsedTime(&a, tlw.ev[2], tlw.ev[3]); tm.list_kernel_ms += a;
+                cudaEventElapsedTime(&a, tlw.ev[3], tlw.ev[4]); tm.list_refine_ms += a;
+                cudaEventElapsedTime(&a, tlw.ev[4], tlw.ev[5]); tm.list_fallback_ms += a;
+            }
+        }
+        if (list_scan) {
+            unsigned long long s2[2] = {0, 0};
+            d2h(s2, tlw.stats.data(), 2, st);
+            sync(st);
+            tm.list_candidates = s2[0];
+            tm.list_fallback_queries = (uint32_t)s2[1];
         }
         unsigned long long scanned = 0;
         d2h(&scanned, w_scanned.data(), 1, st);
@@ -937,7 +1000,8 @@ auto IvfPqIndex::get_stats() const noexcept -> Stats {
     s.code_size = I.params.m;
     s.memory_bytes = sizeof(Impl) + I.d_cent.bytes() + I.d_cb.bytes() + I.d_rot.bytes() + I.d_rotT.bytes() +
                      I.d_rc.bytes() + I.d_offs.bytes() + I.d_ids.bytes() + I.d_codes.bytes() + I.d_vterm.bytes() +
-                     I.d_blk_off.bytes() + I.d_bcodes.bytes() + I.d_bvterm.bytes();
+                     I.d_blk_off.bytes() + I.d_bcodes.bytes() + I.d_bvterm.bytes() + I.d_cbb.bytes() +
+                     I.d_xnorm.bytes();
     s.avg_list_size = I.n_vectors > 0 && I.params.nlist ? (float)I.n_vectors / (float)I.params.nlist : 0.0f;
     s.timings_enabled = I.params.verbose || I.params.timings_enabled || env_flag("VESPER_TIMING");
     if (s.timings_enabled) { s.t_assign_ms = I.t_assign_ms; s.t_encode_ms = I.t_encode_ms; s.t_lists_ms = I.t_lists_ms; }

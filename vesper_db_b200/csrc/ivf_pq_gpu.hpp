@@ -107,8 +107,16 @@ struct SearchTimings {
     float coarse_ms{0}, select_ms{0}, rotate_ms{0}, scan_ms{0}, merge_ms{0}, total_ms{0};
     std::uint64_t scanned_entries{0};   // sum over queries of the probed lists' sizes
     std::uint32_t kernel_launches{0};   // kernels this library launched for the call
-    std::uint32_t scan_variant{0};      // 1 exact per-list LUT, 2 per-query LUT, 3 blocked per-query LUT
+    std::uint32_t scan_variant{0};      // 1 exact per-list LUT, 2 per-query LUT, 3 blocked per-query LUT,
+                                        // 4 tensor-core list scan + refine
     std::uint32_t coarse_variant{0};    // 1 CUDA-core exact distances, 2 tensor-core screen + exact refine
+    float list_kernel_ms{0};            // variant 4: device time of the tensor-core screening kernel
+    std::uint64_t list_candidates{0};   // variant 4: pairs kept by the screen (refined)
+    std::uint32_t list_fallback_queries{0};  // variant 4: queries handed to the blocked scan
+    float list_threshold_ms{0};         // variant 4: nearest-list scan giving the thresholds
+    float list_prep_ms{0};              // variant 4: bf16 queries, pair grouping, unit table
+    float list_refine_ms{0};            // variant 4: exact re-scoring of the kept pairs
+    float list_fallback_ms{0};          // variant 4: blocked scan of overflowed queries
 };
 
 class IvfPqIndex {

@@ -1013,25 +1013,25 @@ constexpr int FB_PF = 8;                      // 16-byte code segments a lane ke
 
 template <int MC, int G>
 __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
-    const float* __restrict__ T, const float* __restrict__ rq, int dim,
-    const uint32_t* __restrict__ probe, const float* __restrict__ probe_d, const float* __restrict__ rc,
-    int nprobe, const uint64_t* __restrict__ offs, const uint64_t* __restrict__ blk_off,
+    const float* __restrict__ T, const float* __restrict__ pbase, const uint32_t* __restrict__ probe,
+    int nprobe, int nscan, const uint64_t* __restrict__ offs, const uint64_t* __restrict__ blk_off,
     const uint8_t* __restrict__ bcodes, const float* __restrict__ bvterm, const uint64_t* __restrict__ ids,
     int k, int kp2, int bp2, uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
-    uint32_t* __restrict__ out_n) {
+    uint32_t* __restrict__ out_n, const uint32_t* __restrict__ only_over, uint32_t over_cap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int m = MC;
     float* lut = reinterpret_cast<float*>(smem_raw);                                   // [m*256]
     unsigned long long* buf = reinterpret_cast<unsigned long long*>(lut + m * 256);     // [bp2]
     unsigned long long* top = buf + bp2;                                               // [kp2]
-    uint32_t* eprefix = reinterpret_cast<uint32_t*>(top + kp2);                         // [nprobe+1]
-    uint32_t* bprefix = eprefix + (nprobe + 1);                                        // [nprobe+1]
-    float* base = reinterpret_cast<float*>(bprefix + (nprobe + 1));                     // [nprobe]
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(top + kp2);                         // [nscan+1]
+    uint32_t* bprefix = eprefix + (nscan + 1);                                         // [nscan+1]
+    float* base = reinterpret_cast<float*>(bprefix + (nscan + 1));                      // [nscan]
     __shared__ uint32_t cnt;
     __shared__ int have;
     __shared__ unsigned long long tau;
 
     const long long q = blockIdx.x;
+    if (only_over && only_over[q] <= over_cap) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     {
         const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * 256);
@@ -1041,36 +1041,20 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
     // Per-probe prefixes (entries, blocks) and base terms.
     if (threadIdx.x == 0) {
         uint32_t ep = 0, bp = 0;
-        for (int t = 0; t < nprobe; ++t) {
+        for (int t = 0; t < nscan; ++t) {
             const uint32_t l = probe[q * nprobe + t];
             eprefix[t] = ep;
             bprefix[t] = bp;
             ep += (uint32_t)(offs[l + 1] - offs[l]);
             bp += (uint32_t)(blk_off[l + 1] - blk_off[l]);
         }
-        eprefix[nprobe] = ep;
-        bprefix[nprobe] = bp;
+        eprefix[nscan] = ep;
+        bprefix[nscan] = bp;
         cnt = 0; have = 0; tau = ~0ull;
     }
-    for (int t = warp; t < nprobe; t += FB_WARPS) {
-        const long long pr = q * nprobe + t;
-        float b;
-        if (rc) {
-            const float* cl = rc + (long long)probe[pr] * dim;
-            const float* qv = rq + q * dim;
-            float acc = 0.0f;
-            for (int d = lane; d < dim; d += 32) {
-                const float df = qv[d] - cl[d];
-                acc = fmaf(df, df, acc);
-            }
-            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            b = acc;
-        } else {
-            b = probe_d[pr];
-        }
-        if (lane == 0) base[t] = b;
-    }
+    for (int t = threadIdx.x; t < nscan; t += FB_NT) base[t] = pbase[q * nprobe + t];
     __syncthreads();
+    (void)lane;
 
     auto merge = [&]() {
         const int c = (int)cnt, h = have;
@@ -1086,11 +1070,11 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
         __syncthreads();
     };
 
-    const uint32_t NB = bprefix[nprobe];
+    const uint32_t NB = bprefix[nscan];
     for (uint32_t r0 = 0; r0 < NB; r0 += FB_WARPS) {
         const uint32_t bi = r0 + warp;
         if (bi < NB) {
-            int lo = 0, hi = nprobe;  // largest t with bprefix[t] <= bi
+            int lo = 0, hi = nscan;  // largest t with bprefix[t] <= bi
             while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (bprefix[mid] <= bi) lo = mid; else hi = mid; }
             const uint32_t l = probe[q * nprobe + lo];
             const uint32_t b = bi - bprefix[lo];
@@ -1150,7 +1134,7 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
         if (i < h) {
             const unsigned long long key = top[i];
             const uint32_t sq = (uint32_t)(key & 0xffffffffull);
-            int lo = 0, hi = nprobe;
+            int lo = 0, hi = nscan;
             while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (eprefix[mid] <= sq) lo = mid; else hi = mid; }
             const uint32_t l = probe[q * nprobe + lo];
             out_ids[q * k + i] = ids[offs[l] + (sq - eprefix[lo])];
@@ -1163,28 +1147,67 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
     if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)h;
 }
 
+// Base term of every (query, probe) pair: ||Rq - R c_l||^2 (lane-strided fp32 FMAs
+// and a butterfly sum, one warp per pair) when rotated centroids are given, else the
+// coarse distance.  Shared by the blocked scan and the tensor-core list scan so both
+// see the same value.
+__global__ void probe_base_kernel(const float* __restrict__ rq, int dim, const uint32_t* __restrict__ probe,
+                                  const float* __restrict__ probe_d, const float* __restrict__ rc, int nprobe,
+                                  long long npairs, float* __restrict__ pbase) {
+    const int lane = threadIdx.x & 31;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long pr = w; pr < npairs; pr += nw) {
+        float b;
+        if (rc) {
+            const float* cl = rc + (long long)probe[pr] * dim;
+            const float* qv = rq + (pr / nprobe) * dim;
+            float acc = 0.0f;
+            for (int d = lane; d < dim; d += 32) {
+                const float df = qv[d] - cl[d];
+                acc = fmaf(df, df, acc);
+            }
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            b = acc;
+        } else {
+            b = probe_d[pr];
+        }
+        if (lane == 0) pbase[pr] = b;
+    }
+}
+
+void launch_probe_base(const float* rq, long long nq, int dim, const uint32_t* probe, const float* probe_d,
+                       const float* rc, int nprobe, float* pbase, cudaStream_t st) {
+    const long long npairs = nq * nprobe;
+    if (npairs <= 0) return;
+    const int blocks = (int)std::min<long long>((npairs * 32 + 255) / 256, 148LL * 32);
+    probe_base_kernel<<<blocks, 256, 0, st>>>(rq, dim, probe, probe_d, rc, nprobe, npairs, pbase);
+    VGPU_LAUNCH("probe_base_kernel");
+}
+
 bool scan_blocked_supported(int m, int ksub) {
     return ksub == 256 && (m == 16 || m == 32 || m == 64 || m == 96 || m == 128);
 }
 
-void launch_scan_blocked(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
-                         const float* probe_d, const float* rc, int nprobe, int m, const uint64_t* offs,
-                         const uint64_t* blk_off, const uint8_t* bcodes, const float* bvterm, const uint64_t* ids,
-                         int k, uint64_t* out_ids, float* out_d, uint32_t* out_n, cudaStream_t st) {
+void launch_scan_blocked(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
+                         int nscan, int m, const uint64_t* offs, const uint64_t* blk_off, const uint8_t* bcodes,
+                         const float* bvterm, const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
+                         uint32_t* out_n, const uint32_t* only_over, uint32_t over_cap, cudaStream_t st) {
     if (nq <= 0) return;
+    if (nscan < 1 || nscan > nprobe) throw CudaError("scan_blocked: nscan must be in [1, nprobe]");
     if (k > kMaxK) throw CudaError("scan_blocked: k exceeds the supported maximum");
     const int kp2 = next_pow2(k < 2 ? 2 : k);
     const int bp2 = next_pow2(FB_CB + kp2);
     const size_t smem = (size_t)m * 256 * sizeof(float) + (size_t)(bp2 + kp2) * sizeof(unsigned long long) +
-                        (size_t)(nprobe + 1) * 8 + (size_t)nprobe * 4;
+                        (size_t)(nscan + 1) * 8 + (size_t)nscan * 4;
     if (smem > 227 * 1024) throw CudaError("scan_blocked: lookup table does not fit in shared memory");
 #define VGPU_SB(MCV, GV)                                                                          \
     do {                                                                                          \
         VGPU_CHECK(cudaFuncSetAttribute(scan_blocked_kernel<MCV, GV>,                             \
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         scan_blocked_kernel<MCV, GV><<<(unsigned)nq, FB_NT, smem, st>>>(                          \
-            T, rq, dim, probe, probe_d, rc, nprobe, offs, blk_off, bcodes, bvterm, ids, k, kp2,   \
-            bp2, out_ids, out_d, out_n);                                                          \
+            T, pbase, probe, nprobe, nscan, offs, blk_off, bcodes, bvterm, ids, k, kp2, bp2,      \
+            out_ids, out_d, out_n, only_over, over_cap);                                          \
     } while (0)
     if (m == 16) VGPU_SB(16, 16);
     else if (m == 32) VGPU_SB(32, 32);

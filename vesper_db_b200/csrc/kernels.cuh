@@ -75,10 +75,16 @@ void launch_build_blocks(const uint8_t* codes, const float* vterm, const uint64_
                          int m, int nlist, uint8_t* bcodes, float* bvterm, cudaStream_t st);
 void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb, int m, int dsub, float* T,
                         cudaStream_t st);
-void launch_scan_blocked(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
-                         const float* probe_d, const float* rc, int nprobe, int m, const uint64_t* offs,
-                         const uint64_t* blk_off, const uint8_t* bcodes, const float* bvterm, const uint64_t* ids,
-                         int k, uint64_t* out_ids, float* out_d, uint32_t* out_n, cudaStream_t st);
+// Base term of each (query, probe) pair for the FAST scans: ||Rq - R c_l||^2 when rc
+// (rotated centroids) is given, else probe_d.
+void launch_probe_base(const float* rq, long long nq, int dim, const uint32_t* probe, const float* probe_d,
+                       const float* rc, int nprobe, float* pbase, cudaStream_t st);
+// Blocked FAST scan of the first nscan of each query's nprobe probes.  With only_over,
+// a query is processed only when only_over[q] > over_cap (the others are left as is).
+void launch_scan_blocked(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
+                         int nscan, int m, const uint64_t* offs, const uint64_t* blk_off, const uint8_t* bcodes,
+                         const float* bvterm, const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
+                         uint32_t* out_n, const uint32_t* only_over, uint32_t over_cap, cudaStream_t st);
 
 // u(x) = sum_s ( ||y_s,c_s||^2 + 2 <(R c_l)_s, y_s,c_s> ) for every CSR entry, with
 // rc = rotated centroids [nlist x dim]; accumulated in fp64, rounded once.

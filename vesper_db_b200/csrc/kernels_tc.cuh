@@ -21,3 +21,71 @@ void launch_screen_select(const float* Dt, long long n_rows, long long ldd, int 
                           uint32_t* out_idx, float* out_val, int* err, cudaStream_t st);
 
 }  // namespace vgpu
+
+namespace vgpu {
+
+// ---------------------------------------------------------------------------------
+// List-major tensor-core FAST scan (tc_scan.cu).
+// ---------------------------------------------------------------------------------
+// Shapes the kernel handles: 256 codes per sub-space, dim a multiple of 64 up to 768,
+// dim / m in {4, 8, 16}, and an m the blocked scan supports (it provides the
+// thresholds and handles overflowed queries).
+bool tc_list_scan_supported(int dim, int m, int ksub);
+
+// Per-batch scratch, grown on demand and reused.  bf16 arrays are held as uint16_t.
+struct TlWork {
+    DeviceBuffer<uint16_t> rqb, qperm;
+    DeviceBuffer<float> rqn, tau, p1_d;
+    DeviceBuffer<uint64_t> p1_ids;
+    DeviceBuffer<uint32_t> p1_n, cnt, cursor, seg_off, units, unit_off, unit_list, seg_meta, cand_cnt, counter;
+    DeviceBuffer<unsigned long long> cand;
+    DeviceBuffer<unsigned char> scan_tmp;
+    // stats[0] += candidates refined, stats[1] += queries left to the blocked scan
+    // (zeroed by the caller); ev brackets the screening kernel of the last launch.
+    DeviceBuffer<unsigned long long> stats;
+    // ev[0..5]: start, threshold scan done, batch prep done, screen done, refine done,
+    // fallback done (of the last launch)
+    cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    int cap = 0;
+    void reserve(long long nq, int nprobe, int nlist, int dim, int k, int cap, size_t n_vectors);
+    TlWork() = default;
+    TlWork(const TlWork&) = delete;
+    TlWork& operator=(const TlWork&) = delete;
+    ~TlWork() {
+        for (auto& e : ev)
+            if (e) cudaEventDestroy(e);
+    }
+};
+
+struct TlScanArgs {
+    const float* T;          // blocked lookup tables [nq x m x 256]
+    const float* rq;         // rotated queries [nq x dim]
+    const float* pbase;      // [nq x nprobe] (launch_probe_base)
+    const uint32_t* probe;   // [nq x nprobe]
+    long long nq;
+    int nprobe, nlist, dim, m, k;
+    const uint64_t* offs;    // CSR list offsets
+    const uint8_t* codes;    // CSR codes
+    const float* vterm;      // CSR per-entry terms
+    const float* xnorm;      // CSR per-entry decoded norms
+    const uint16_t* cbb;     // bf16 codebooks [m x 256 x dsub]
+    const uint64_t* blk_off; // blocked copy (threshold scan and overflow fallback)
+    const uint8_t* bcodes;
+    const float* bvterm;
+    const uint64_t* ids;
+    uint64_t* out_ids;
+    float* out_d;
+    uint32_t* out_n;
+    int* err;
+};
+
+// FAST search results identical to launch_scan_blocked over all nprobe probes.
+void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st);
+// out[i] = bf16(cb[i]).
+void launch_codebook_bf16(const float* cb, long long n, uint16_t* out, cudaStream_t st);
+// xnorm[e] = ||decoded entry e|| (rounded up), for the screen's error bound.
+void launch_entry_norms(const uint8_t* codes, long long n, const float* cb, int m, int dsub, float* xnorm,
+                        cudaStream_t st);
+void launch_query_prep(const float* rq, long long nq, int dim, uint16_t* rqb, float* rqn, cudaStream_t st);
+
+}  // namespace vgpu

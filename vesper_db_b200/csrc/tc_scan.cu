@@ -1,0 +1,892 @@
+// List-major tensor-core PQ scan (FAST search): screen every (query, entry) pair of a
+// query batch with tcgen05 bf16 products, keep the pairs that can still be in a query's
+// top k, and re-score only those with the FAST lookup-table arithmetic.
+//
+// The FAST distance of entry x of list l for query q is
+//     d = (base(q,l) + u(x)) + sum_s T_q[s][c_s(x)],   T_q[s][c] = -2 <(Rq)_s, y_s,c>,
+// and sum_s T_q[s][c_s(x)] = -2 <Rq, xhat> with xhat the decoded (rotated-space)
+// residual.  The screen computes S = <bf16(Rq), bf16(xhat)> on the tensor cores, so
+//     approx = (base + u) - 2 S,   |approx - d| <= slack(q, x)
+// with the bound below.  A pair is kept when approx - slack <= tau(q), where tau(q) is
+// an upper bound of q's k-th FAST distance (its k-th distance over its nearest list).
+// Every entry whose FAST distance is <= tau(q) is therefore kept, the refine computes
+// its FAST distance and scan position exactly as the blocked scan does, and the k
+// smallest (distance, position) keys are the blocked scan's result, bit for bit.
+//
+// Work layout.  The (query, probe) pairs of the batch are grouped by list.  A unit is
+// (list, 128-entry tile, group of up to QG x N queries).  A persistent CTA per SM takes
+// units from a global counter:
+//   * warps 0-7 decode the tile's 128 entries (codes -> bf16 codebook rows) straight
+//     into tensor memory (A operand, 128 lanes x dim/2 columns);
+//   * warps 4-7 stream the queries' bf16 rows (B operand, N x 64 per stage, 128-byte
+//     swizzle) through an S-stage shared-memory ring with cp.async;
+//   * one thread of warp 8 issues tcgen05.mma.kind::f16 (M = 128, N, K = 16, A from
+//     TMEM) into one of two TMEM accumulators;
+//   * warps 0-3 read the accumulator (thread = entry row), apply the keep rule and
+//     append survivors to per-query candidate lists.
+// Every wait is bounded; on timeout the kernel records an error code, stops issuing
+// work at the next unit boundary, drains its tensor-core work and frees its TMEM.
+#include <cub/cub.cuh>
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cfloat>
+
+#include "kernels.cuh"
+#include "kernels_tc.cuh"
+#include "select.cuh"
+#include "tc_common.cuh"
+
+namespace vgpu {
+
+CUtensorMap make_tile_map_bf16(const void* base, long long rows, int dim, int box_rows);
+
+namespace {
+constexpr int TL_M = 128;          // entries per tile (TMEM lanes)
+constexpr int TL_THREADS = 224;    // 7 warps: 0-3 decode + epilogue, 4 TMA, 5 MMA, 6 scheduler
+constexpr int TL_QG = 1024;        // query chunks per unit (a unit is normally a whole list tile)
+constexpr float kSlackMul = 0.03125f;           // 2^-5: bf16 products + tensor-core accumulation
+constexpr float kSlackAbs = 9.5367431640625e-07f;  // 2^-20: fp32 rounding of both formulas
+
+// Instruction descriptor for kind::f16: D f32, A and B bf16, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TL_M >> 4) << 24);
+}
+
+// tcgen05.mma (A from shared memory / from TMEM) and tcgen05.commit, issued by one
+// elected lane of a converged warp.
+__device__ __forceinline__ void mma_bf16_ss_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_bf16_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void commit_elect(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+        ::"r"(tc::smem_u32(bar))
+        : "memory");
+}
+
+// OR of `v` over the 128 epilogue threads (named barrier 1); also a barrier for them.
+__device__ __forceinline__ bool group_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+// A box of 64 bf16 columns x 128 rows at (x, y) of the map's matrix, 128B-swizzled.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+struct UnitInfo {
+    uint32_t list, tile, pair_begin, pair_end, n_chunks, list_len, valid;
+    unsigned long long entry_base;
+};
+
+}  // namespace
+
+struct TlParams {
+    const __nv_bfloat16* rqb;   // [nq x dim] rotated queries, bf16
+    const float* rqn;           // [nq] ||Rq||
+    const float* pbase;         // [nq x nprobe]
+    const float* tau;           // [nq] upper bound of the k-th FAST distance (-FLT_MAX: no screen)
+    const uint32_t* probe;      // [nq x nprobe]
+    const uint64_t* offs;       // [nlist + 1]
+    const uint8_t* codes;       // [n_vectors x m]
+    const float* vterm;         // [n_vectors]
+    const float* xnorm;         // [n_vectors] ||xhat||
+    const __nv_bfloat16* cbb;   // [m x 256 x dsub] codebooks, bf16
+    const uint32_t* seg_off;    // [nlist + 1] pair segments per list
+    const uint32_t* unit_list;  // [total units] list of each unit
+    const uint4* seg_meta;      // [nq x nprobe] grouped by list: {q << 10 | probe, base, tau, ||Rq||}
+    const uint32_t* unit_off;   // [nlist + 1]
+    uint32_t* unit_counter;
+    unsigned long long* cand;   // [nq x cap] (probe << 32 | position)
+    uint32_t* cand_cnt;         // [nq]
+    int* err;
+    int nlist, nprobe, dim, m, k, cap;
+};
+
+// 64 bf16 of dims [64 kc, 64 kc + 64) of the decoded entry whose codes start at crow
+// (shared memory).
+template <int DS>
+__device__ __forceinline__ void decode_kchunk_smem(uint32_t (&v)[32], const uint8_t* crow,
+                                                   const __nv_bfloat16* __restrict__ cbb, int kc, bool valid) {
+    constexpr int SPK = 64 / DS;  // sub-spaces per 64-dim chunk
+    if (!valid) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0u;
+        return;
+    }
+    const int s0 = kc * SPK;
+    uint32_t cw[(SPK + 3) / 4];
+#pragma unroll
+    for (int w = 0; w < (SPK + 3) / 4; ++w) cw[w] = reinterpret_cast<const uint32_t*>(crow + s0)[w];
+#pragma unroll
+    for (int i = 0; i < SPK; ++i) {
+        const uint32_t code = (cw[i >> 2] >> ((i & 3) * 8)) & 0xffu;
+        const __nv_bfloat16* y = cbb + ((size_t)(s0 + i) * 256 + code) * DS;
+        if constexpr (DS == 4) {
+            const uint2 t = __ldg(reinterpret_cast<const uint2*>(y));
+            v[2 * i] = t.x; v[2 * i + 1] = t.y;
+        } else if constexpr (DS == 8) {
+            const uint4 t = __ldg(reinterpret_cast<const uint4*>(y));
+            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+        } else {
+            const uint4 t0 = __ldg(reinterpret_cast<const uint4*>(y));
+            const uint4 t1 = __ldg(reinterpret_cast<const uint4*>(y) + 1);
+            v[8 * i] = t0.x; v[8 * i + 1] = t0.y; v[8 * i + 2] = t0.z; v[8 * i + 3] = t0.w;
+            v[8 * i + 4] = t1.x; v[8 * i + 5] = t1.y; v[8 * i + 6] = t1.z; v[8 * i + 7] = t1.w;
+        }
+    }
+}
+
+// Decode DB consecutive 64-dim chunks (kc0 .. kc0+DB-1, those < KC) of one entry into TMEM
+// columns [32 kc, 32 kc + 32) of this thread's lane.  crow: the entry's codes (shared
+// memory); all codebook gathers of the batch are issued before the first store.
+// Chunks kc < KT go to this thread's TMEM lane; chunks kc >= KT go to row `row` of the
+// 128B-swizzled shared-memory tile a_smem (16 KB per 64-dim chunk).
+template <int DS, int DB>
+__device__ __forceinline__ void decode_batch(uint32_t tlane, unsigned char* a_smem, int row, const uint8_t* crow,
+                                             const __nv_bfloat16* __restrict__ cbb, int kc0, int KC, int KT,
+                                             bool valid) {
+    uint32_t v[DB][32];
+#pragma unroll
+    for (int b = 0; b < DB; ++b)
+        if (kc0 + b < KC) decode_kchunk_smem<DS>(v[b], crow, cbb, kc0 + b, valid);
+#pragma unroll
+    for (int b = 0; b < DB; ++b) {
+        const int kc = kc0 + b;
+        if (kc < KT) {
+            tc::tmem_st32(tlane + (uint32_t)(kc * 32), v[b]);
+        } else if (kc < KC) {
+            unsigned char* atom = a_smem + (size_t)(kc - KT) * (TL_M * 128);
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(atom + tc::sw128_offset(row, c)) =
+                    make_uint4(v[b][4 * c], v[b][4 * c + 1], v[b][4 * c + 2], v[b][4 * c + 3]);
+        }
+    }
+}
+
+template <int N, int S, int DS>
+__global__ void __launch_bounds__(TL_THREADS, 1) tc_list_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                     const TlParams P) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int STAGE_BYTES = N * 128;
+    constexpr uint32_t kDcol = 512u - 2u * N;  // two accumulators at the top of TMEM
+    const int KC = P.dim / 64;
+    // The first KT 64-dim chunks of the tile live in TMEM (columns [0, 32 KT)), the
+    // rest in a shared-memory tile after the B ring.
+    const int KT = min(KC, (int)(kDcol / 32));
+    unsigned char* a_smem = smem + S * STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(a_smem + (KC - KT) * (TL_M * 128));
+    uint64_t* empty = full + S;
+    uint64_t* accf = empty + S;
+    uint64_t* acce = accf + 2;
+    uint64_t* ufull = acce + 2;   // unit ring: scheduler -> roles
+    uint64_t* uempty = ufull + 2; // unit ring: roles -> scheduler
+    uint64_t* afull = uempty + 2; // decoded tile in TMEM -> MMA
+    uint64_t* drain = afull + 1;
+    uint4* meta = reinterpret_cast<uint4*>(drain + 1);    // [2][N] column metadata (16-byte aligned)
+    float2* mtest = reinterpret_cast<float2*>(meta + 2 * N);      // [2][N] (||Rq||, keep threshold)
+    UnitInfo* units = reinterpret_cast<UnitInfo*>(mtest + 2 * N);  // [2]
+    unsigned char* ucodes = reinterpret_cast<unsigned char*>(units + 2);  // [2][128 * m], 16-byte aligned
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ucodes + 2 * TL_M * P.m);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr uint32_t kIdesc = idesc_bf16(N);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&accf[b], 1);
+            tc::mbar_init(&acce[b], 128);
+            tc::mbar_init(&ufull[b], 1);
+            tc::mbar_init(&uempty[b], 6);  // TMA warp + MMA + 4 decoder warps
+        }
+        tc::mbar_init(afull, 128);
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::mbar_init_fence();
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         tc::smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    auto fail = [&](int code) {
+        *abort_flag = 1;
+        atomicExch(P.err, code);
+    };
+
+    if (warp == 6) {
+        // ---- scheduler: unit info and the tile's codes into a 2-slot ring.
+        const uint32_t total = P.unit_off[P.nlist];
+        for (uint32_t it = 0;; ++it) {
+            const uint32_t slot = it & 1;
+            if (it >= 2 && !tc::mbar_wait(&uempty[slot], ((it >> 1) - 1) & 1)) { fail(21); break; }
+            UnitInfo ui{};
+            uint32_t u = total;
+            if (lane == 0 && !*abort_flag) u = atomicAdd(P.unit_counter, 1u);
+            u = __shfl_sync(0xffffffffu, u, 0);
+            if (u < total) {
+                const uint32_t l = P.unit_list[u];
+                const uint32_t r = u - P.unit_off[l];
+                const uint32_t s0 = P.seg_off[l], s1 = P.seg_off[l + 1];
+                const uint64_t o0 = P.offs[l], o1 = P.offs[l + 1];
+                const uint32_t nqg = (s1 - s0 + N * TL_QG - 1) / (N * TL_QG);
+                ui.list = l;
+                ui.tile = r / nqg;
+                ui.pair_begin = s0 + (r % nqg) * (uint32_t)(N * TL_QG);
+                ui.pair_end = min(s1, ui.pair_begin + (uint32_t)(N * TL_QG));
+                ui.n_chunks = (ui.pair_end - ui.pair_begin + N - 1) / N;
+                ui.list_len = (uint32_t)(o1 - o0);
+                ui.entry_base = o0 + (unsigned long long)ui.tile * TL_M;
+                ui.valid = 1;
+                // the tile's codes are contiguous in the CSR array: rows * m bytes
+                const uint32_t rows = min((uint32_t)TL_M, ui.list_len - ui.tile * TL_M);
+                const uint32_t n16 = rows * (uint32_t)P.m / 16;
+                const unsigned char* src = P.codes + ui.entry_base * (unsigned long long)P.m;
+                const uint32_t dst = tc::smem_u32(ucodes + slot * TL_M * P.m);
+                for (uint32_t i = lane; i < n16; i += 32) cp_async16(dst + i * 16, src + (size_t)i * 16);
+                cp_async_commit();
+                cp_async_wait<0>();
+            }
+            if (lane == 0) units[slot] = ui;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&ufull[slot]);
+            if (!ui.valid) break;
+        }
+    } else if (warp == 4) {
+        // ---- TMA producer: the chunk's 128 query rows are consecutive rows of the
+        // list-ordered query matrix, so each stage is one 128 x 64 tile load.
+        uint32_t it_prod = 0;
+        if (lane == 0) {
+            for (uint32_t it = 0; !*abort_flag; ++it) {
+                const uint32_t slot = it & 1;
+                if (!tc::mbar_wait(&ufull[slot], (it >> 1) & 1)) { fail(22); break; }
+                const UnitInfo ui = units[slot];
+                tc::mbar_arrive(&uempty[slot]);
+                if (!ui.valid) break;
+                bool ok = true;
+                for (uint32_t c = 0; c < ui.n_chunks && ok; ++c) {
+                    const int y = (int)(ui.pair_begin + c * N);
+                    for (int kc = 0; kc < KC; ++kc) {
+                        const uint32_t stage = it_prod % S;
+                        if (it_prod >= (uint32_t)S && !tc::mbar_wait(&empty[stage], ((it_prod / S) - 1) & 1)) {
+                            fail(11);
+                            ok = false;
+                            break;
+                        }
+                        tc::mbar_expect_tx(&full[stage], (uint32_t)STAGE_BYTES);
+                        tma_load_2d(tc::smem_u32(smem + stage * STAGE_BYTES), &qmap, kc * 64, y, &full[stage]);
+                        ++it_prod;
+                    }
+                }
+            }
+            // Every load issued has landed before the CTA can exit (normally the MMA
+            // already waited for each of them).
+            for (uint32_t i = it_prod > (uint32_t)S ? it_prod - S : 0; i < it_prod; ++i)
+                if (!tc::mbar_wait(&full[i % S], (i / S) & 1)) { fail(16); break; }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ---- MMA issuer: the whole warp runs the loop (uniform control flow keeps the
+        // descriptors in uniform registers); one elected lane issues each tcgen05 op.
+        uint32_t it_mma = 0, cg_mma = 0;
+        auto wwait = [&](uint64_t* bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity));
+        };
+        for (uint32_t it = 0; !*abort_flag; ++it) {
+            const uint32_t slot = it & 1;
+            if (!wwait(&ufull[slot], (it >> 1) & 1)) { if (lane == 0) fail(23); break; }
+            const uint32_t nch = units[slot].n_chunks;
+            const uint32_t valid = units[slot].valid;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&uempty[slot]);
+            if (!valid) break;
+            if (!wwait(afull, it & 1)) { if (lane == 0) fail(24); break; }
+            tc::fence_after_sync();
+            bool ok = true;
+            for (uint32_t c = 0; c < nch && ok; ++c) {
+                const uint32_t buf = cg_mma & 1;
+                if (cg_mma >= 2 && !wwait(&acce[buf], ((cg_mma >> 1) - 1) & 1)) {
+                    if (lane == 0) fail(12);
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t dcol = tmem + kDcol + buf * (uint32_t)N;
+                for (int kc = 0; kc < KC; ++kc) {
+                    const uint32_t stage = it_mma % S;
+                    if (!wwait(&full[stage], (it_mma / S) & 1)) {
+                        if (lane == 0) fail(13);
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_u32(smem + stage * STAGE_BYTES));
+                    if (kc < KT) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)  // K = 16 bf16 = 32 bytes per MMA
+                            mma_bf16_ts_elect(dcol, tmem + (uint32_t)(kc * 32 + kk * 8), bd + (uint64_t)(kk * 2),
+                                              kIdesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        const uint64_t ad =
+                            tc::sw128_kmajor_desc(tc::smem_u32(a_smem + (size_t)(kc - KT) * (TL_M * 128)));
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_bf16_ss_elect(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), kIdesc,
+                                              (kc > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    commit_elect(&empty[stage]);
+                    ++it_mma;
+                }
+                commit_elect(&accf[buf]);
+                ++cg_mma;
+            }
+            if (!ok) break;
+        }
+        // Every tensor-core operation issued has completed before TMEM is freed.
+        commit_elect(drain);
+        if (!wwait(drain, 0) && lane == 0) atomicExch(P.err, 15);
+    } else if (warp < 4) {
+        // ---- decoders + epilogue (warps 0-3): thread = entry row of the tile.
+        const int row = tid;
+        const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint4 pad = make_uint4(0xffffffffu, 0u, 0u, 0u);
+        uint32_t cg_epi = 0;
+        for (uint32_t it = 0;; ++it) {
+            const uint32_t slot = it & 1;
+            const bool got = !*abort_flag && tc::mbar_wait(&ufull[slot], (it >> 1) & 1);
+            if (group_any(!got)) {
+                if (!got && !*abort_flag) fail(25);
+                break;
+            }
+            const UnitInfo ui = units[slot];
+            if (!ui.valid) break;
+            const uint32_t pb = ui.pair_begin, pe = ui.pair_end, nch = ui.n_chunks;
+            const uint32_t e0 = ui.tile * TL_M;
+            const bool vrow = e0 + (uint32_t)row < ui.list_len;
+            const float u = vrow ? P.vterm[ui.entry_base + row] : 0.0f;
+            const float xn = vrow ? P.xnorm[ui.entry_base + row] : 0.0f;
+            uint4 next = pad;
+            if (tid < N && pb + (uint32_t)tid < pe) next = P.seg_meta[pb + tid];
+            // Decode the tile into TMEM.  This group waited for the previous unit's last
+            // accumulator, so the MMAs that read the previous tile have completed.
+            tc::fence_after_sync();
+            const uint8_t* crow = ucodes + slot * TL_M * P.m + row * P.m;
+            for (int kc0 = 0; kc0 < KC; kc0 += 3)
+                decode_batch<DS, 3>(tlane, a_smem, row, crow, P.cbb, kc0, KC, KT, vrow);
+            tc::tmem_st_wait();
+            tc::fence_proxy_async_smem();  // the shared-memory part is read by the tensor core
+            tc::fence_before_sync();
+            tc::mbar_arrive(afull);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&uempty[slot]);
+
+            // Keep rule approx - slack <= tau, rearranged as
+            //   -2 S - sx ||Rq||  <=  T_col + W_row,
+            //   T_col = tau - base + 2^-20 (|base| + |tau|),  W_row = 2^-20 |u| - u,
+            // (the extra 2^-20 |tau| covers the rounding of the rearrangement).
+            const float sx = (kSlackMul + 2.0f * kSlackAbs) * xn;
+            const float wrow = kSlackAbs * fabsf(u) - u;
+            const uint32_t pos = e0 + (uint32_t)row;
+            bool stop = false;
+            for (uint32_t c = 0; c < nch; ++c) {
+                const uint32_t buf = cg_epi & 1;
+                uint4* bm = meta + buf * N;
+                float2* bt = mtest + buf * N;
+                if (tid < N) {
+                    bm[tid] = next;
+                    const float bj = __uint_as_float(next.y), tq = __uint_as_float(next.z);
+                    bt[tid] = next.x == 0xffffffffu
+                                  ? make_float2(0.0f, -FLT_MAX)
+                                  : make_float2(__uint_as_float(next.w),
+                                                (tq - bj) + kSlackAbs * (fabsf(bj) + fabsf(tq)));
+                    const uint32_t pi = pb + (c + 1) * N + (uint32_t)tid;
+                    next = (c + 1 < nch && pi < pe) ? P.seg_meta[pi] : pad;
+                }
+                // One decision for the whole group (the named barrier also publishes the
+                // column metadata written above).
+                const bool ok = !*abort_flag && tc::mbar_wait(&accf[buf], (cg_epi >> 1) & 1);
+                if (group_any(!ok)) {
+                    if (!ok && !*abort_flag) fail(14);
+                    stop = true;
+                    break;
+                }
+                tc::fence_after_sync();
+#pragma unroll
+                for (int h = 0; h < N / 32; ++h) {
+                    uint32_t acc[32];
+                    tc::tmem_ld32(tlane + kDcol + buf * (uint32_t)N + h * 32, acc);
+                    tc::tmem_ld_wait();
+                    if (h == N / 32 - 1) {
+                        tc::fence_before_sync();
+                        tc::mbar_arrive(&acce[buf]);
+                    }
+                    uint32_t mask = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float2 t = bt[h * 32 + j];
+                        const float lhs = fmaf(-sx, t.x, -2.0f * __uint_as_float(acc[j]));
+                        mask |= (lhs <= t.y + wrow) ? (1u << j) : 0u;
+                    }
+                    if (!vrow) mask = 0;
+                    while (mask) {
+                        const int j = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const uint32_t qt = bm[h * 32 + j].x;
+                        const uint32_t q = qt >> 10;
+                        const uint32_t slot2 = atomicAdd(&P.cand_cnt[q], 1u);
+                        if (slot2 < (uint32_t)P.cap)
+                            P.cand[(size_t)q * P.cap + slot2] = ((unsigned long long)(qt & 1023u) << 32) | pos;
+                    }
+                }
+                ++cg_epi;
+            }
+            if (stop) break;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 5)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+}
+
+// ---------------------------------------------------------------------------------
+// Batch preparation: bf16 queries and norms, pair grouping by list, unit counts.
+// ---------------------------------------------------------------------------------
+__global__ void query_prep_kernel(const float* __restrict__ rq, long long nq, int dim, __nv_bfloat16* __restrict__ rqb,
+                                  float* __restrict__ rqn) {
+    const int lane = threadIdx.x & 31;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long q = w; q < nq; q += nw) {
+        float s = 0.0f;
+        for (int d = lane; d < dim; d += 32) {
+            const float v = rq[q * dim + d];
+            rqb[q * dim + d] = __float2bfloat16_rn(v);
+            s = fmaf(v, v, s);
+        }
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) rqn[q] = sqrtf(s) * 1.0000005f;
+    }
+}
+
+// tau[q] = k-th FAST distance over q's nearest list; a query whose nearest list has
+// fewer than k entries is not screened (tau = -FLT_MAX) and is marked as overflowed so
+// that the blocked scan handles it.
+__global__ void tau_prep_kernel(const float* __restrict__ p1_d, const uint32_t* __restrict__ p1_n, long long nq,
+                                int k, int cap, float* __restrict__ tau, uint32_t* __restrict__ cand_cnt) {
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
+        const bool full = p1_n[q] == (uint32_t)k;
+        tau[q] = full ? p1_d[q * k + k - 1] : -FLT_MAX;
+        cand_cnt[q] = full ? 0u : (uint32_t)cap + 1u;
+    }
+}
+
+// qperm[i] = rqb[q(i)]: the bf16 query rows in the list-grouped pair order (one warp
+// per row, 16-byte copies).
+__global__ void qperm_kernel(const uint4* __restrict__ seg_meta, long long npairs, const uint4* __restrict__ rqb,
+                             int row16, uint4* __restrict__ qperm) {
+    const int lane = threadIdx.x & 31;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long i = w; i < npairs; i += nw) {
+        const uint32_t q = __ldg(&seg_meta[i].x) >> 10;
+        for (int c = lane; c < row16; c += 32) qperm[i * row16 + c] = __ldg(&rqb[(long long)q * row16 + c]);
+    }
+}
+
+__global__ void cand_stats_kernel(const uint32_t* __restrict__ cand_cnt, long long nq, uint32_t cap,
+                                  unsigned long long* __restrict__ stats) {
+    unsigned long long c = 0, f = 0;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
+        const uint32_t n = cand_cnt[q];
+        if (n > cap) ++f; else c += n;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        c += __shfl_xor_sync(0xffffffffu, c, o);
+        f += __shfl_xor_sync(0xffffffffu, f, o);
+    }
+    if ((threadIdx.x & 31) == 0 && (c | f)) {
+        atomicAdd(&stats[0], c);
+        atomicAdd(&stats[1], f);
+    }
+}
+
+__global__ void pair_hist_kernel(const uint32_t* __restrict__ probe, long long npairs, uint32_t* __restrict__ cnt) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npairs;
+         i += (long long)gridDim.x * blockDim.x)
+        atomicAdd(&cnt[probe[i]], 1u);
+}
+
+// Pairs grouped by list, each with the metadata the screen's epilogue needs:
+// {q << 10 | probe index, base term, tau(q), ||Rq||}.
+__global__ void pair_scatter_kernel(const uint32_t* __restrict__ probe, long long npairs, int nprobe,
+                                    const uint32_t* __restrict__ seg_off, uint32_t* __restrict__ cursor,
+                                    const float* __restrict__ pbase, const float* __restrict__ tau,
+                                    const float* __restrict__ rqn, uint4* __restrict__ seg_meta) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npairs;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint32_t l = probe[i];
+        const uint32_t q = (uint32_t)(i / nprobe), t = (uint32_t)(i - (long long)q * nprobe);
+        seg_meta[seg_off[l] + atomicAdd(&cursor[l], 1u)] =
+            make_uint4((q << 10) | t, __float_as_uint(pbase[i]), __float_as_uint(tau[q]), __float_as_uint(rqn[q]));
+    }
+}
+
+// unit_list[u] = the list unit u belongs to (unit_off[l] <= u < unit_off[l + 1]).
+__global__ void unit_fill_kernel(const uint32_t* __restrict__ unit_off, int nlist, uint32_t* __restrict__ unit_list) {
+    const uint32_t total = unit_off[nlist];
+    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total; u += gridDim.x * blockDim.x) {
+        int lo = 0, hi = nlist;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (unit_off[mid] <= u) lo = mid; else hi = mid;
+        }
+        unit_list[u] = (uint32_t)lo;
+    }
+}
+
+__global__ void unit_count_kernel(const uint32_t* __restrict__ cnt, const uint64_t* __restrict__ offs, int nlist,
+                                  int n_cols, uint32_t* __restrict__ units) {
+    const int l = blockIdx.x * blockDim.x + threadIdx.x;
+    if (l > nlist) return;
+    if (l == nlist) { units[l] = 0; return; }
+    const uint32_t c = cnt[l];
+    const uint64_t L = offs[l + 1] - offs[l];
+    units[l] = (c == 0 || L == 0) ? 0u
+                                  : (uint32_t)((L + TL_M - 1) / TL_M) *
+                                        ((c + (uint32_t)(n_cols * TL_QG) - 1) / (uint32_t)(n_cols * TL_QG));
+}
+
+// ---------------------------------------------------------------------------------
+// Refine: exact FAST distances of the candidates (the blocked scan's arithmetic and
+// scan positions), then the k smallest keys.  Queries whose candidate list overflowed
+// are left to the blocked scan.
+// ---------------------------------------------------------------------------------
+template <int MC, int G>
+__global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict__ T, const uint32_t* __restrict__ probe,
+                                                        int nprobe, const float* __restrict__ pbase,
+                                                        const uint64_t* __restrict__ offs,
+                                                        const uint8_t* __restrict__ codes,
+                                                        const float* __restrict__ vterm,
+                                                        const uint64_t* __restrict__ ids,
+                                                        const unsigned long long* __restrict__ cand,
+                                                        const uint32_t* __restrict__ cand_cnt, int cap, int k,
+                                                        uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
+                                                        uint32_t* __restrict__ out_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    constexpr int m = MC;
+    float* lut = reinterpret_cast<float*>(smem_raw);                                  // [m * 256]
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(lut + m * 256);  // [next_pow2(cap)]
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(keys + next_pow2(cap));           // [nprobe + 1]
+    const long long q = blockIdx.x;
+    const uint32_t n = cand_cnt[q];
+    if (n > (uint32_t)cap) return;
+    {
+        const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * 256);
+        float4* dst = reinterpret_cast<float4*>(lut);
+        for (int i = threadIdx.x; i < m * 64; i += 256) dst[i] = __ldg(src + i);
+    }
+    if (threadIdx.x == 0) {
+        uint32_t ep = 0;
+        for (int t = 0; t < nprobe; ++t) {
+            const uint32_t l = probe[q * nprobe + t];
+            eprefix[t] = ep;
+            ep += (uint32_t)(offs[l + 1] - offs[l]);
+        }
+        eprefix[nprobe] = ep;
+    }
+    __syncthreads();
+    const int p2 = next_pow2(n < 2 ? 2 : (int)n);
+    for (int i = threadIdx.x; i < p2; i += 256) {
+        unsigned long long key = ~0ull;
+        if (i < (int)n) {
+            const unsigned long long c = cand[q * cap + i];
+            const uint32_t t = (uint32_t)(c >> 32), p = (uint32_t)c;
+            const uint32_t l = probe[q * nprobe + t];
+            const uint64_t e = offs[l] + p;
+            const uint8_t* cr = codes + e * m;
+            const int lane = (int)((p & 127u) >> 2);
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int r = 0; r < m; ++r) {
+                const int g = r / G, s_lo = (lane + r) & (G - 1);
+                acc += lut[(g * 256 + cr[g * G + s_lo]) * G + s_lo];
+            }
+            const float dist = (pbase[q * nprobe + t] + vterm[e]) + acc;
+            key = ((unsigned long long)float_key(dist) << 32) | (eprefix[t] + p);
+        }
+        keys[i] = key;
+    }
+    bitonic_sort_u64<256>(keys, p2);
+    const int h = (int)n < k ? (int)n : k;
+    for (int i = threadIdx.x; i < k; i += 256) {
+        if (i < h) {
+            const unsigned long long key = keys[i];
+            const uint32_t sq = (uint32_t)(key & 0xffffffffull);
+            int lo = 0, hi = nprobe;
+            while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (eprefix[mid] <= sq) lo = mid; else hi = mid; }
+            const uint32_t l = probe[q * nprobe + lo];
+            out_ids[q * k + i] = ids[offs[l] + (sq - eprefix[lo])];
+            out_d[q * k + i] = key_float((uint32_t)(key >> 32));
+        } else {
+            out_ids[q * k + i] = 0;
+            out_d[q * k + i] = h > 0 ? key_float((uint32_t)(keys[h - 1] >> 32)) : 0.0f;
+        }
+    }
+    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)h;
+}
+
+// ---------------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------------
+namespace {
+// One accumulator is 128 queries wide; with two of them 256 TMEM columns remain for the
+// tile, so dims beyond 512 go to a shared-memory tile and the B ring shrinks.
+template <int S>
+size_t tl_smem(int dim, int m) {
+    constexpr int N = 128;
+    const int kc = dim / 64, ks = kc > 8 ? kc - 8 : 0;
+    return 1024 + (size_t)S * N * 128 + (size_t)ks * TL_M * 128 + (2 * S + 10) * 8 + 2 * N * 16 + 2 * N * 8 +
+           2 * sizeof(UnitInfo) + 2 * (size_t)TL_M * m + 16;
+}
+}  // namespace
+
+bool tc_list_scan_supported(int dim, int m, int ksub) {
+    const int dsub = m > 0 ? dim / m : 0;
+    return ksub == 256 && dim % 64 == 0 && dim >= 64 && dim <= 768 && dim % m == 0 &&
+           (dsub == 4 || dsub == 8 || dsub == 16) && scan_blocked_supported(m, ksub);
+}
+
+void launch_query_prep(const float* rq, long long nq, int dim, uint16_t* rqb, float* rqn, cudaStream_t st) {
+    if (nq <= 0) return;
+    const int blocks = (int)std::min<long long>((nq * 32 + 255) / 256, 148LL * 16);
+    query_prep_kernel<<<blocks, 256, 0, st>>>(rq, nq, dim, reinterpret_cast<__nv_bfloat16*>(rqb), rqn);
+    VGPU_LAUNCH("query_prep_kernel");
+}
+
+void TlWork::reserve(long long nq, int nprobe, int nlist, int dim, int k, int cap_, size_t n_vectors) {
+    const long long np = nq * nprobe;
+    // units <= (query groups per list) x (128-entry tiles over all lists)
+    const size_t groups = (size_t)((nq + 128LL * TL_QG - 1) / (128LL * TL_QG));
+    unit_list.reserve(groups * (n_vectors / TL_M + (size_t)nlist + 1));
+    rqb.reserve((size_t)nq * dim);
+    tau.reserve(nq);
+    rqn.reserve(nq);
+    cnt.reserve(nlist + 1);
+    cursor.reserve(nlist + 1);
+    seg_off.reserve(nlist + 1);
+    units.reserve(nlist + 1);
+    unit_off.reserve(nlist + 1);
+    seg_meta.reserve((size_t)np * 4);
+    qperm.reserve((size_t)np * dim);
+    cand.reserve((size_t)nq * cap_);
+    cand_cnt.reserve(nq);
+    counter.reserve(1);
+    stats.reserve(2);
+    for (auto& e : ev)
+        if (!e) check(cudaEventCreate(&e), "cudaEventCreate");
+    p1_ids.reserve((size_t)nq * k);
+    p1_d.reserve((size_t)nq * k);
+    p1_n.reserve(nq);
+    cap = cap_;
+    size_t need = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, need, cnt.data(), seg_off.data(), nlist + 1);
+    scan_tmp.reserve(need + 256);
+}
+
+void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
+    const long long npairs = a.nq * a.nprobe;
+    if (a.nq <= 0 || npairs <= 0) return;
+    if (!tc_list_scan_supported(a.dim, a.m, 256)) throw CudaError("tc_list_scan: unsupported shape");
+    if (a.k > kMaxK) throw CudaError("tc_list_scan: k exceeds the supported maximum");
+    if (npairs > 0xffffffffLL || a.nq > (1LL << 22) || a.nprobe > 1024)
+        throw CudaError("tc_list_scan: batch too large (at most 2^22 queries and 1024 probes)");
+    constexpr int N = 128;
+    const int dsub = a.dim / a.m;
+
+    check(cudaEventRecord(w.ev[0], st), "cudaEventRecord");
+    // Threshold source: FAST top-k over each query's nearest list.
+    launch_scan_blocked(a.T, a.nq, a.pbase, a.probe, a.nprobe, 1, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm, a.ids,
+                        a.k, w.p1_ids.data(), w.p1_d.data(), w.p1_n.data(), nullptr, 0, st);
+    check(cudaEventRecord(w.ev[1], st), "cudaEventRecord");
+    launch_query_prep(a.rq, a.nq, a.dim, w.rqb.data(), w.rqn.data(), st);
+    tau_prep_kernel<<<(int)std::min<long long>((a.nq + 255) / 256, 148LL * 4), 256, 0, st>>>(
+        w.p1_d.data(), w.p1_n.data(), a.nq, a.k, w.cap, w.tau.data(), w.cand_cnt.data());
+    VGPU_LAUNCH("tau_prep_kernel");
+
+    // Pairs grouped by list; units per list.
+    check(cudaMemsetAsync(w.cnt.data(), 0, sizeof(uint32_t) * (a.nlist + 1), st), "memset");
+    check(cudaMemsetAsync(w.cursor.data(), 0, sizeof(uint32_t) * (a.nlist + 1), st), "memset");
+    const int gb = (int)std::min<long long>((npairs + 255) / 256, 148LL * 8);
+    pair_hist_kernel<<<gb, 256, 0, st>>>(a.probe, npairs, w.cnt.data());
+    VGPU_LAUNCH("pair_hist_kernel");
+    size_t tmp = w.scan_tmp.size();
+    check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.cnt.data(), w.seg_off.data(), a.nlist + 1, st),
+          "cub::DeviceScan::ExclusiveSum(seg_off)");
+    pair_scatter_kernel<<<gb, 256, 0, st>>>(a.probe, npairs, a.nprobe, w.seg_off.data(), w.cursor.data(), a.pbase,
+                                            w.tau.data(), w.rqn.data(), reinterpret_cast<uint4*>(w.seg_meta.data()));
+    VGPU_LAUNCH("pair_scatter_kernel");
+    unit_count_kernel<<<(a.nlist + 1 + 255) / 256, 256, 0, st>>>(w.cnt.data(), a.offs, a.nlist, N, w.units.data());
+    VGPU_LAUNCH("unit_count_kernel");
+    tmp = w.scan_tmp.size();
+    check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.units.data(), w.unit_off.data(), a.nlist + 1, st),
+          "cub::DeviceScan::ExclusiveSum(unit_off)");
+    unit_fill_kernel<<<148 * 4, 256, 0, st>>>(w.unit_off.data(), a.nlist, w.unit_list.data());
+    VGPU_LAUNCH("unit_fill_kernel");
+    check(cudaMemsetAsync(w.counter.data(), 0, sizeof(uint32_t), st), "memset");
+
+    TlParams P;
+    P.rqb = reinterpret_cast<const __nv_bfloat16*>(w.rqb.data()); P.rqn = w.rqn.data(); P.pbase = a.pbase;
+    P.tau = w.tau.data();
+    P.probe = a.probe; P.offs = a.offs; P.codes = a.codes; P.vterm = a.vterm; P.xnorm = a.xnorm;
+    P.cbb = reinterpret_cast<const __nv_bfloat16*>(a.cbb);
+    P.seg_off = w.seg_off.data(); P.seg_meta = reinterpret_cast<const uint4*>(w.seg_meta.data());
+    P.unit_off = w.unit_off.data(); P.unit_list = w.unit_list.data();
+    P.unit_counter = w.counter.data(); P.cand = w.cand.data(); P.cand_cnt = w.cand_cnt.data(); P.err = a.err;
+    P.nlist = a.nlist; P.nprobe = a.nprobe; P.dim = a.dim; P.m = a.m; P.k = a.k; P.cap = w.cap;
+
+    int dev = 0, sms = 148;
+    check(cudaGetDevice(&dev), "cudaGetDevice");
+    check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+    qperm_kernel<<<148 * 16, 256, 0, st>>>(reinterpret_cast<const uint4*>(w.seg_meta.data()), npairs,
+                                           reinterpret_cast<const uint4*>(w.rqb.data()), a.dim / 8,
+                                           reinterpret_cast<uint4*>(w.qperm.data()));
+    VGPU_LAUNCH("qperm_kernel");
+    const CUtensorMap qmap = make_tile_map_bf16(w.qperm.data(), npairs, a.dim, 128);
+    check(cudaEventRecord(w.ev[2], st), "cudaEventRecord");
+#define VGPU_TL(SV, DSV)                                                                                 \
+    do {                                                                                                 \
+        const size_t smem = tl_smem<SV>(a.dim, a.m);                                                     \
+        if (smem > 227 * 1024) throw CudaError("tc_list_scan: shared-memory layout too large");          \
+        check(cudaFuncSetAttribute(tc_list_scan_kernel<N, SV, DSV>,                                      \
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),             \
+              "cudaFuncSetAttribute(tc_list_scan)");                                                     \
+        tc_list_scan_kernel<N, SV, DSV><<<sms, TL_THREADS, smem, st>>>(qmap, P);                               \
+    } while (0)
+    if (a.dim > 512) {  // part of the tile in shared memory: 8 B stages
+        if (dsub == 4) VGPU_TL(8, 4); else if (dsub == 8) VGPU_TL(8, 8); else VGPU_TL(8, 16);
+    } else {
+        if (dsub == 4) VGPU_TL(10, 4); else if (dsub == 8) VGPU_TL(10, 8); else VGPU_TL(10, 16);
+    }
+#undef VGPU_TL
+    VGPU_LAUNCH("tc_list_scan_kernel");
+    check(cudaEventRecord(w.ev[3], st), "cudaEventRecord");
+
+    // Refine the candidates; overflowed queries fall back to the blocked scan.
+    const size_t rsmem = (size_t)a.m * 256 * 4 + (size_t)next_pow2(w.cap) * 8 + (size_t)(a.nprobe + 1) * 4;
+    if (rsmem > 227 * 1024) throw CudaError("tc_list_scan: refine buffers do not fit in shared memory");
+#define VGPU_RF(MCV, GV)                                                                                    \
+    do {                                                                                                    \
+        check(cudaFuncSetAttribute(tl_refine_kernel<MCV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)rsmem),                                                             \
+              "cudaFuncSetAttribute(tl_refine)");                                                           \
+        tl_refine_kernel<MCV, GV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                      \
+            a.T, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids, w.cand.data(),               \
+            w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n);                                    \
+    } while (0)
+    if (a.m == 16) VGPU_RF(16, 16);
+    else if (a.m == 32) VGPU_RF(32, 32);
+    else if (a.m == 64) VGPU_RF(64, 32);
+    else if (a.m == 96) VGPU_RF(96, 32);
+    else VGPU_RF(128, 32);
+#undef VGPU_RF
+    VGPU_LAUNCH("tl_refine_kernel");
+    check(cudaEventRecord(w.ev[4], st), "cudaEventRecord");
+    launch_scan_blocked(a.T, a.nq, a.pbase, a.probe, a.nprobe, a.nprobe, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm,
+                        a.ids, a.k, a.out_ids, a.out_d, a.out_n, w.cand_cnt.data(), (uint32_t)w.cap, st);
+    check(cudaEventRecord(w.ev[5], st), "cudaEventRecord");
+    cand_stats_kernel<<<(int)std::min<long long>((a.nq + 255) / 256, 148LL * 4), 256, 0, st>>>(
+        w.cand_cnt.data(), a.nq, (uint32_t)w.cap, w.stats.data());
+    VGPU_LAUNCH("cand_stats_kernel");
+}
+
+// ---------------------------------------------------------------------------------
+// Per-index preparation: bf16 codebooks and per-entry decoded norms.
+// ---------------------------------------------------------------------------------
+__global__ void codebook_bf16_kernel(const float* __restrict__ cb, long long n, __nv_bfloat16* __restrict__ out) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = __float2bfloat16_rn(cb[i]);
+}
+
+void launch_codebook_bf16(const float* cb, long long n, uint16_t* out, cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 8);
+    codebook_bf16_kernel<<<blocks, 256, 0, st>>>(cb, n, reinterpret_cast<__nv_bfloat16*>(out));
+    VGPU_LAUNCH("codebook_bf16_kernel");
+}
+
+// xnorm[e] = ||xhat_e|| = sqrt(sum_s ||y_s,c_s||^2) (fp64 sum, rounded up slightly).
+__global__ void entry_norm_kernel(const uint8_t* __restrict__ codes, long long n, const float* __restrict__ cb, int m,
+                                  int dsub, float* __restrict__ xnorm) {
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+        double s = 0.0;
+        for (int j = 0; j < m; ++j) {
+            const float* y = cb + ((long long)j * 256 + codes[e * m + j]) * dsub;
+            for (int t = 0; t < dsub; ++t) s += (double)y[t] * y[t];
+        }
+        xnorm[e] = (float)(sqrt(s) * (1.0 + 1e-6));
+    }
+}
+
+void launch_entry_norms(const uint8_t* codes, long long n, const float* cb, int m, int dsub, float* xnorm,
+                        cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+    entry_norm_kernel<<<blocks, 256, 0, st>>>(codes, n, cb, m, dsub, xnorm);
+    VGPU_LAUNCH("entry_norm_kernel");
+}
+
+}  // namespace vgpu

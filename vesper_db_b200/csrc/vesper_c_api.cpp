@@ -327,6 +327,13 @@ VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t*
     out->kernel_launches = t.kernel_launches;
     out->scan_variant = t.scan_variant;
     out->coarse_variant = t.coarse_variant;
+    out->list_kernel_ms = t.list_kernel_ms;
+    out->list_candidates = t.list_candidates;
+    out->list_fallback_queries = t.list_fallback_queries;
+    out->list_threshold_ms = t.list_threshold_ms;
+    out->list_prep_ms = t.list_prep_ms;
+    out->list_refine_ms = t.list_refine_ms;
+    out->list_fallback_ms = t.list_fallback_ms;
     return VESPER_OK;
 }
 
