@@ -72,6 +72,20 @@ def test_list_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches):
         assert np.array_equal(bi, ti)
 
 
+@pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES[:2])
+def test_split_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches):
+    """The blocked scan with each query's blocks split over several CTAs and merged
+    (used for the list scan's thresholds and overflow fallback) is bit-identical."""
+    rng = np.random.default_rng(dim + m + nlist)
+    idx, cent = _build(rng, dim, m, nlist, n, rot)
+    q = (cent[rng.integers(0, nlist, nq)] + 0.3 * rng.standard_normal((nq, dim))).astype(np.float32)
+    for k, npb in searches + [(1000, 40)]:
+        (bi, bd, bn), _ = _search(idx, q, k, npb, "blocked")
+        (si, sd, sn), vs = _search(idx, q, k, npb, "split")
+        assert vs == 3
+        assert np.array_equal(bn, sn) and np.array_equal(bd, sd) and np.array_equal(bi, si)
+
+
 def test_small_home_lists_and_overflow():
     """Many lists smaller than k (those queries skip the screen), and k large enough that
     some candidate lists overflow (the blocked scan takes those queries over)."""

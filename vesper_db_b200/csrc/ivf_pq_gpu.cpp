@@ -214,6 +214,12 @@ public:
         has_blocks = true;
     }
 
+    // VGPU_SCAN=split: the blocked scan with each query's blocks spread over several CTAs.
+    static bool use_split_scan() {
+        const char* v = std::getenv("VGPU_SCAN");
+        return v && std::string(v) == "split";
+    }
+
     // FAST-scan kernel for this call: the tensor-core list scan where the shapes allow
     // it and the batch scans enough entries per query to amortise its set-up, else the
     // blocked scan.  VGPU_SCAN=tc / blocked overrides the choice.
@@ -221,7 +227,7 @@ public:
         if (!has_blocks || np < 2 || !vgpu::tc_list_scan_supported((int)dim, (int)m(), (int)ksub)) return false;
         const char* v = std::getenv("VGPU_SCAN");
         if (v && std::string(v) == "tc") return true;
-        if (v && std::string(v) == "blocked") return false;
+        if (v && (std::string(v) == "blocked" || std::string(v) == "split")) return false;
         const double per_query = (double)n_vectors / std::max<uint32_t>(nlist(), 1) * np;
         return per_query >= 4096.0 && nq >= 256;
     }
@@ -699,6 +705,7 @@ public:
             w_pbase.reserve(qc * np);
         }
         const bool list_scan = !exact && use_list_scan(nq, np);
+        const bool split_scan = !exact && !list_scan && has_blocks && use_split_scan();
         if (list_scan) {
             tlw.reserve((long long)qc, (int)np, (int)nlist(), (int)dim, (int)k, kListScanCap, n_vectors);
             vgpu::check(cudaMemsetAsync(tlw.stats.data(), 0, 2 * sizeof(unsigned long long), st), "memset");
@@ -786,6 +793,11 @@ public:
                         a.blk_off = d_blk_off.data(); a.bcodes = d_bcodes.data(); a.bvterm = d_bvterm.data();
                         a.ids = d_ids.data(); a.out_ids = oid; a.out_d = od; a.out_n = on; a.err = d_err.data();
                         vgpu::launch_tc_list_scan(a, tlw, st);
+                    } else if (split_scan) {
+                        vgpu::launch_scan_blocked_split(w_T.data(), (long long)nc, w_pbase.data(), w_probe.data(),
+                                                        (int)np, (int)np, (int)m(), d_offs.data(), d_blk_off.data(),
+                                                        d_bcodes.data(), d_bvterm.data(), d_ids.data(), (int)k, oid,
+                                                        od, on, nullptr, 0, tlw.split, st);
                     } else {
                         vgpu::launch_scan_blocked(w_T.data(), (long long)nc, w_pbase.data(), w_probe.data(), (int)np,
                                                   (int)np, (int)m(), d_offs.data(), d_blk_off.data(),

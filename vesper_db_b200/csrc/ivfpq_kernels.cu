@@ -8,6 +8,8 @@
 // The fast scan (lut_fast_kernel + scan_fast2_kernel) regroups the ADC algebra so the table is
 // built once per query instead of once per (query, list); its distances agree with
 // the exact ones to fp32 rounding.
+#include <cub/cub.cuh>
+
 #include <cfloat>
 
 #include "kernels.cuh"
@@ -962,32 +964,42 @@ void launch_build_blocks(const uint8_t* codes, const float* vterm, const uint64_
 }
 
 // Tables in the blocked order, T[q][(g*256 + c)*G + s_lo] = -2 <(Rq)_s, y_sc>.
+// A CTA owns one sub-space group g and 64 codes: it stages those codes' sub-vectors
+// of the group's G sub-spaces in shared memory once, then for each of its queries
+// writes the 64 x G contiguous table entries (thread e -> code e / G, sub-space e % G).
+namespace {
+constexpr int LB_C = 64;    // codes per CTA
+constexpr int LB_Q = 64;    // queries per CTA
+}
+
 __global__ void __launch_bounds__(256) lut_blocked_kernel(const float* __restrict__ rq, long long nq, int dim,
                                                           const float* __restrict__ cb, int m, int dsub, int G,
                                                           float* __restrict__ T) {
     extern __shared__ __align__(16) float sm[];
-    float* Yt = sm;                      // [dsub][256]
-    float* Q = sm + (size_t)dsub * 256;  // [32][dsub]
-    const int s = blockIdx.y;
-    const long long q0 = (long long)blockIdx.x * 32;
-    const float* y = cb + (long long)s * 256 * dsub;
-    for (int e = threadIdx.x; e < 256 * dsub; e += blockDim.x) {
-        const int j = e / dsub, t = e % dsub;
-        Yt[t * 256 + j] = y[e];
+    float* ys = sm;                                 // [LB_C][dsub][G]
+    float* qs = ys + (size_t)LB_C * dsub * G;       // [dsub][G]
+    const int g = blockIdx.y, c0 = blockIdx.z * LB_C;
+    for (int e = threadIdx.x; e < LB_C * dsub * G; e += blockDim.x) {
+        const int s_lo = e % G, t = (e / G) % dsub, c = e / (G * dsub);
+        ys[e] = cb[((long long)(g * G + s_lo) * 256 + c0 + c) * dsub + t];
     }
-    for (int e = threadIdx.x; e < 32 * dsub; e += blockDim.x) {
-        const int qi = e / dsub, t = e % dsub;
-        Q[e] = (q0 + qi < nq) ? rq[(q0 + qi) * dim + (long long)s * dsub + t] : 0.0f;
-    }
-    __syncthreads();
+    const long long qb = (long long)blockIdx.x * LB_Q;
+    const long long qe = min(nq, qb + LB_Q);
     const long long row = (long long)m * 256;
-    const int g = s / G, s_lo = s % G;
-    for (int e = threadIdx.x; e < 32 * 256; e += blockDim.x) {
-        const int qi = e / 256, j = e % 256;
-        if (q0 + qi >= nq) continue;
-        float acc = 0.0f;
-        for (int t = 0; t < dsub; ++t) acc = fmaf(Q[qi * dsub + t], Yt[t * 256 + j], acc);
-        T[(q0 + qi) * row + ((long long)g * 256 + j) * G + s_lo] = -2.0f * acc;
+    for (long long q = qb; q < qe; ++q) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < dsub * G; e += blockDim.x) {
+            const int s_lo = e % G, t = e / G;
+            qs[e] = rq[q * dim + (long long)(g * G + s_lo) * dsub + t];
+        }
+        __syncthreads();
+        float* dst = T + q * row + ((long long)g * 256 + c0) * G;
+        for (int e = threadIdx.x; e < LB_C * G; e += blockDim.x) {
+            const int c = e / G, s_lo = e % G;
+            float acc = 0.0f;
+            for (int t = 0; t < dsub; ++t) acc = fmaf(qs[t * G + s_lo], ys[(c * dsub + t) * G + s_lo], acc);
+            dst[e] = -2.0f * acc;
+        }
     }
 }
 
@@ -995,10 +1007,10 @@ void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb,
                         cudaStream_t st) {
     if (nq <= 0) return;
     const int G = scan_group(m);
-    const size_t smem = ((size_t)dsub * 256 + 32 * (size_t)dsub) * sizeof(float);
-    if (smem > 200 * 1024) throw CudaError("lut_blocked: sub-space codebook too large for shared memory");
+    const size_t smem = ((size_t)LB_C * dsub * G + (size_t)dsub * G) * sizeof(float);
+    if (smem > 200 * 1024) throw CudaError("lut_blocked: sub-space codebook slice too large for shared memory");
     VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid(ceil_div(nq, 32), m);
+    dim3 grid(ceil_div(nq, LB_Q), m / G, 256 / LB_C);
     lut_blocked_kernel<<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, dsub, G, T);
     VGPU_LAUNCH("lut_blocked_kernel");
 }
@@ -1017,7 +1029,8 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
     int nprobe, int nscan, const uint64_t* __restrict__ offs, const uint64_t* __restrict__ blk_off,
     const uint8_t* __restrict__ bcodes, const float* __restrict__ bvterm, const uint64_t* __restrict__ ids,
     int k, int kp2, int bp2, uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
-    uint32_t* __restrict__ out_n, const uint32_t* __restrict__ only_over, uint32_t over_cap) {
+    uint32_t* __restrict__ out_n, const uint32_t* __restrict__ only_over, uint32_t over_cap,
+    const uint4* __restrict__ items, unsigned long long* __restrict__ part_keys) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int m = MC;
     float* lut = reinterpret_cast<float*>(smem_raw);                                   // [m*256]
@@ -1030,8 +1043,10 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
     __shared__ int have;
     __shared__ unsigned long long tau;
 
-    const long long q = blockIdx.x;
-    if (only_over && only_over[q] <= over_cap) return;
+    // Split mode (items != nullptr): this CTA scans blocks [b_begin, b_end) of query
+    // items[blockIdx.x].x and writes its k smallest keys to part_keys.
+    const long long q = items ? (long long)items[blockIdx.x].x : (long long)blockIdx.x;
+    if (!items && only_over && only_over[q] <= over_cap) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     {
         const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * 256);
@@ -1070,8 +1085,9 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
         __syncthreads();
     };
 
-    const uint32_t NB = bprefix[nscan];
-    for (uint32_t r0 = 0; r0 < NB; r0 += FB_WARPS) {
+    const uint32_t NB = items ? min(items[blockIdx.x].z, bprefix[nscan]) : bprefix[nscan];
+    const uint32_t B0 = items ? items[blockIdx.x].y : 0u;
+    for (uint32_t r0 = B0; r0 < NB; r0 += FB_WARPS) {
         const uint32_t bi = r0 + warp;
         if (bi < NB) {
             int lo = 0, hi = nscan;  // largest t with bprefix[t] <= bi
@@ -1130,6 +1146,10 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
         if (cnt > 0) merge();
     }
     const int h = have;
+    if (part_keys) {
+        for (int i = threadIdx.x; i < k; i += FB_NT) part_keys[(long long)blockIdx.x * k + i] = i < h ? top[i] : ~0ull;
+        return;
+    }
     for (int i = threadIdx.x; i < k; i += FB_NT) {
         if (i < h) {
             const unsigned long long key = top[i];
@@ -1189,10 +1209,13 @@ bool scan_blocked_supported(int m, int ksub) {
     return ksub == 256 && (m == 16 || m == 32 || m == 64 || m == 96 || m == 128);
 }
 
-void launch_scan_blocked(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
-                         int nscan, int m, const uint64_t* offs, const uint64_t* blk_off, const uint8_t* bcodes,
-                         const float* bvterm, const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
-                         uint32_t* out_n, const uint32_t* only_over, uint32_t over_cap, cudaStream_t st) {
+namespace {
+void scan_blocked_impl(const float* T, long long grid, const float* pbase, const uint32_t* probe, int nprobe,
+                       int nscan, int m, const uint64_t* offs, const uint64_t* blk_off, const uint8_t* bcodes,
+                       const float* bvterm, const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
+                       uint32_t* out_n, const uint32_t* only_over, uint32_t over_cap, const uint4* items,
+                       unsigned long long* part_keys, cudaStream_t st) {
+    const long long nq = grid;
     if (nq <= 0) return;
     if (nscan < 1 || nscan > nprobe) throw CudaError("scan_blocked: nscan must be in [1, nprobe]");
     if (k > kMaxK) throw CudaError("scan_blocked: k exceeds the supported maximum");
@@ -1207,7 +1230,7 @@ void launch_scan_blocked(const float* T, long long nq, const float* pbase, const
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
         scan_blocked_kernel<MCV, GV><<<(unsigned)nq, FB_NT, smem, st>>>(                          \
             T, pbase, probe, nprobe, nscan, offs, blk_off, bcodes, bvterm, ids, k, kp2, bp2,      \
-            out_ids, out_d, out_n, only_over, over_cap);                                          \
+            out_ids, out_d, out_n, only_over, over_cap, items, part_keys);                        \
     } while (0)
     if (m == 16) VGPU_SB(16, 16);
     else if (m == 32) VGPU_SB(32, 32);
@@ -1217,6 +1240,154 @@ void launch_scan_blocked(const float* T, long long nq, const float* pbase, const
     else throw CudaError("scan_blocked: unsupported m");
 #undef VGPU_SB
     VGPU_LAUNCH("scan_blocked_kernel");
+}
+}  // namespace
+
+void launch_scan_blocked(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
+                         int nscan, int m, const uint64_t* offs, const uint64_t* blk_off, const uint8_t* bcodes,
+                         const float* bvterm, const uint64_t* ids, int k, uint64_t* out_ids, float* out_d,
+                         uint32_t* out_n, const uint32_t* only_over, uint32_t over_cap, cudaStream_t st) {
+    scan_blocked_impl(T, nq, pbase, probe, nprobe, nscan, m, offs, blk_off, bcodes, bvterm, ids, k, out_ids, out_d,
+                      out_n, only_over, over_cap, nullptr, nullptr, st);
+}
+
+// ---------------------------------------------------------------------------------
+// Split blocked scan: a query's blocks are cut into parts of at most SPLIT_BLOCKS
+// blocks, each scanned by its own CTA (keys = (distance, scan position), so the
+// merge reproduces the single-CTA result exactly).
+// ---------------------------------------------------------------------------------
+namespace {
+constexpr uint32_t SPLIT_BLOCKS = 64;   // 128-entry blocks per part
+constexpr int SPLIT_MAX_KEYS = 8192;    // keys merged per query (parts x next_pow2(k))
+}
+
+__global__ void split_count_kernel(const uint32_t* __restrict__ probe, int nprobe, int nscan,
+                                   const uint64_t* __restrict__ blk_off, long long nq,
+                                   const uint32_t* __restrict__ only_over, uint32_t over_cap, uint32_t max_parts,
+                                   uint32_t* __restrict__ parts, uint32_t* __restrict__ nblocks) {
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
+        uint32_t nb = 0;
+        for (int t = 0; t < nscan; ++t) {
+            const uint32_t l = probe[q * nprobe + t];
+            nb += (uint32_t)(blk_off[l + 1] - blk_off[l]);
+        }
+        const bool run = !only_over || only_over[q] > over_cap;
+        const uint32_t p = (nb + SPLIT_BLOCKS - 1) / SPLIT_BLOCKS;
+        parts[q] = run ? max(1u, min(p, max_parts)) : 0u;
+        nblocks[q] = nb;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) parts[nq] = 0;
+}
+
+__global__ void split_fill_kernel(const uint32_t* __restrict__ parts, const uint32_t* __restrict__ part_off,
+                                  const uint32_t* __restrict__ nblocks, long long nq, uint4* __restrict__ items) {
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
+        const uint32_t np = parts[q];
+        if (np == 0) continue;
+        const uint32_t nb = nblocks[q];
+        const uint32_t per = (nb + np - 1) / np;
+        for (uint32_t i = 0; i < np; ++i)
+            items[part_off[q] + i] = make_uint4((uint32_t)q, i * per, min(nb, (i + 1) * per), 0u);
+    }
+}
+
+// Per query: the k smallest of its parts' keys, written like the unsplit scan.
+__global__ void __launch_bounds__(256) split_merge_kernel(
+    const unsigned long long* __restrict__ part_keys, const uint32_t* __restrict__ parts,
+    const uint32_t* __restrict__ part_off, const uint32_t* __restrict__ probe, int nprobe, int nscan,
+    const uint64_t* __restrict__ offs, const uint64_t* __restrict__ ids, int k, uint64_t* __restrict__ out_ids,
+    float* __restrict__ out_d, uint32_t* __restrict__ out_n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);    // [SPLIT_MAX_KEYS]
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(keys + SPLIT_MAX_KEYS);          // [nscan + 1]
+    const long long q = blockIdx.x;
+    const uint32_t np = parts[q];
+    if (np == 0) return;
+    const int n = (int)np * k;
+    const int p2 = next_pow2(n < 2 ? 2 : n);
+    const unsigned long long* src = part_keys + (long long)part_off[q] * k;
+    for (int i = threadIdx.x; i < p2; i += 256) keys[i] = i < n ? src[i] : ~0ull;
+    if (threadIdx.x == 0) {
+        uint32_t ep = 0;
+        for (int t = 0; t < nscan; ++t) {
+            const uint32_t l = probe[q * nprobe + t];
+            eprefix[t] = ep;
+            ep += (uint32_t)(offs[l + 1] - offs[l]);
+        }
+        eprefix[nscan] = ep;
+    }
+    bitonic_sort_u64<256>(keys, p2);
+    __shared__ int h_s;
+    if (threadIdx.x == 0) {
+        int h = 0;
+        while (h < k && h < n && keys[h] != ~0ull) ++h;
+        h_s = h;
+    }
+    __syncthreads();
+    const int h = h_s;
+    for (int i = threadIdx.x; i < k; i += 256) {
+        if (i < h) {
+            const unsigned long long key = keys[i];
+            const uint32_t sq = (uint32_t)(key & 0xffffffffull);
+            int lo = 0, hi = nscan;
+            while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (eprefix[mid] <= sq) lo = mid; else hi = mid; }
+            const uint32_t l = probe[q * nprobe + lo];
+            out_ids[q * k + i] = ids[offs[l] + (sq - eprefix[lo])];
+            out_d[q * k + i] = key_float((uint32_t)(key >> 32));
+        } else {
+            out_ids[q * k + i] = 0;
+            out_d[q * k + i] = h > 0 ? key_float((uint32_t)(keys[h - 1] >> 32)) : 0.0f;
+        }
+    }
+    if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)h;
+}
+
+void SplitWork::reserve(long long nq) {
+    parts.reserve(nq + 1);
+    part_off.reserve(nq + 1);
+    nblocks.reserve(nq);
+    size_t need = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, need, parts.data(), part_off.data(), (int)(nq + 1));
+    scan_tmp.reserve(need + 256);
+    if (!host_total) check(cudaMallocHost(&host_total, sizeof(uint32_t)), "cudaMallocHost");
+}
+
+SplitWork::~SplitWork() {
+    if (host_total) cudaFreeHost(host_total);
+}
+
+void launch_scan_blocked_split(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
+                               int nscan, int m, const uint64_t* offs, const uint64_t* blk_off,
+                               const uint8_t* bcodes, const float* bvterm, const uint64_t* ids, int k,
+                               uint64_t* out_ids, float* out_d, uint32_t* out_n, const uint32_t* only_over,
+                               uint32_t over_cap, SplitWork& w, cudaStream_t st) {
+    if (nq <= 0) return;
+    if (k > kMaxK) throw CudaError("scan_blocked_split: k exceeds the supported maximum");
+    w.reserve(nq);
+    const uint32_t max_parts = (uint32_t)std::max(1, SPLIT_MAX_KEYS / k);
+    const int gb = (int)std::min<long long>((nq + 255) / 256, 148LL * 4);
+    split_count_kernel<<<gb, 256, 0, st>>>(probe, nprobe, nscan, blk_off, nq, only_over, over_cap, max_parts,
+                                           w.parts.data(), w.nblocks.data());
+    VGPU_LAUNCH("split_count_kernel");
+    size_t tmp = w.scan_tmp.size();
+    check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.parts.data(), w.part_off.data(), (int)(nq + 1), st),
+          "cub::DeviceScan::ExclusiveSum(split parts)");
+    check(cudaMemcpyAsync(w.host_total, w.part_off.data() + nq, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
+    check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    const uint32_t total = *w.host_total;
+    if (total == 0) return;
+    w.items.reserve(total);
+    w.part_keys.reserve((size_t)total * k);
+    split_fill_kernel<<<gb, 256, 0, st>>>(w.parts.data(), w.part_off.data(), w.nblocks.data(), nq, w.items.data());
+    VGPU_LAUNCH("split_fill_kernel");
+    scan_blocked_impl(T, total, pbase, probe, nprobe, nscan, m, offs, blk_off, bcodes, bvterm, ids, k, nullptr, nullptr,
+                      nullptr, nullptr, 0, w.items.data(), w.part_keys.data(), st);
+    const size_t smem = (size_t)SPLIT_MAX_KEYS * 8 + (size_t)(nscan + 1) * 4;
+    check(cudaFuncSetAttribute(split_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+          "cudaFuncSetAttribute(split_merge)");
+    split_merge_kernel<<<(unsigned)nq, 256, smem, st>>>(w.part_keys.data(), w.parts.data(), w.part_off.data(), probe,
+                                                        nprobe, nscan, offs, ids, k, out_ids, out_d, out_n);
+    VGPU_LAUNCH("split_merge_kernel");
 }
 
 }  // namespace vgpu

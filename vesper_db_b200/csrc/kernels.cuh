@@ -79,6 +79,27 @@ void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb,
 // (rotated centroids) is given, else probe_d.
 void launch_probe_base(const float* rq, long long nq, int dim, const uint32_t* probe, const float* probe_d,
                        const float* rc, int nprobe, float* pbase, cudaStream_t st);
+// Scratch of the split blocked scan (grown on demand).
+struct SplitWork {
+    DeviceBuffer<uint32_t> parts, part_off, nblocks;
+    DeviceBuffer<uint4> items;
+    DeviceBuffer<unsigned long long> part_keys;
+    DeviceBuffer<unsigned char> scan_tmp;
+    uint32_t* host_total = nullptr;   // pinned
+    void reserve(long long nq);
+    SplitWork() = default;
+    SplitWork(const SplitWork&) = delete;
+    SplitWork& operator=(const SplitWork&) = delete;
+    ~SplitWork();
+};
+// launch_scan_blocked with each query's blocks split over several CTAs (parts of 64
+// blocks, at most 8192 / k parts) and merged: the same results, without a single CTA
+// scanning a very long probe set.  Synchronizes the stream once (number of parts).
+void launch_scan_blocked_split(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
+                               int nscan, int m, const uint64_t* offs, const uint64_t* blk_off,
+                               const uint8_t* bcodes, const float* bvterm, const uint64_t* ids, int k,
+                               uint64_t* out_ids, float* out_d, uint32_t* out_n, const uint32_t* only_over,
+                               uint32_t over_cap, SplitWork& w, cudaStream_t st);
 // Blocked FAST scan of the first nscan of each query's nprobe probes.  With only_over,
 // a query is processed only when only_over[q] > over_cap (the others are left as is).
 void launch_scan_blocked(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,

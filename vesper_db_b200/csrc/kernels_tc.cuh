@@ -2,6 +2,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace vgpu {
 
@@ -46,6 +47,7 @@ struct TlWork {
     // ev[0..5]: start, threshold scan done, batch prep done, screen done, refine done,
     // fallback done (of the last launch)
     cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    SplitWork split;  // threshold scan and overflow fallback
     int cap = 0;
     void reserve(long long nq, int nprobe, int nlist, int dim, int k, int cap, size_t n_vectors);
     TlWork() = default;

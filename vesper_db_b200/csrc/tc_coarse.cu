@@ -264,7 +264,8 @@ void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStre
 // ---------------------------------------------------------------------------------
 namespace {
 constexpr int SS_NT = 256;
-constexpr int SS_CAP = 4096;   // candidates refined per pass
+constexpr int SS_CAP = 1024;   // columns per candidate chunk (at most this many candidates)
+constexpr int SS_SMEM_KEYS = 16384;  // rows up to this width keep their upper-bound keys in shared memory
 
 // Screening error bound.  tf32 truncation of both operands (relative 2^-10 each), fp32
 // accumulation over dim products, fp32 rounding of the epilogue and of the norms, and
@@ -284,11 +285,13 @@ __device__ __forceinline__ float warp_l2_group(const float* __restrict__ x, cons
     const int lane = threadIdx.x & 31, l = lane & 7;
     const int simd_end = dim & ~7;
     float acc = 0.0f;
-    if (active)
+    if (active) {
+#pragma unroll 8
         for (int t = l; t < simd_end; t += 8) {
             const float d = __fsub_rn(x[t], c[t]);
             acc = __fmaf_rn(d, d, acc);
         }
+    }
     const float a4 = __shfl_down_sync(0xffffffffu, acc, 4, 8);
     const float s = __fadd_rn(a4, acc);
     const float s1 = __shfl_down_sync(0xffffffffu, s, 1, 8);
@@ -304,14 +307,11 @@ __device__ __forceinline__ float warp_l2_group(const float* __restrict__ x, cons
 }
 
 struct ScreenSmem {
-    float exact[SS_CAP + kMaxK];
-    uint32_t idx[SS_CAP + kMaxK];
-    unsigned long long sortb[8192];   // >= next_pow2(SS_CAP + kMaxK)
-    uint32_t warp_tmp[33];
+    unsigned long long keys[4096];   // (exact key << 32 | index): carried winners + a chunk's candidates
+    uint32_t cidx[SS_CAP];           // the chunk's candidate indices (in arrival order)
     uint32_t hist[256];
     uint32_t remaining, thresh, count;
     float keep_val;
-    SelectSmem sel;
 };
 }  // namespace
 
@@ -327,18 +327,71 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
     const float rn = xn[row];
     const int kk = k < nc ? k : nc;
     const uint32_t kc = keep ? keep[row] : 0xffffffffu;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) S.keep_val = FLT_MAX;
+    (void)err;
+    // Upper-bound keys computed once into shared memory when the row fits.
+    uint32_t* ukeys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(ScreenSmem));
+    const bool cached = nc <= SS_SMEM_KEYS;
+    float eps_max = 0.0f;
+    if (cached) {
+        // 8 columns per thread in flight at a time
+        for (int c0 = threadIdx.x; c0 < nc; c0 += 8 * SS_NT) {
+            float dt[8], cv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * SS_NT;
+                dt[u] = c < nc ? drow[c] : 0.0f;
+                cv[u] = c < nc ? cn[c] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * SS_NT;
+                if (c < nc) {
+                    const float e = screen_eps(rn, cv[u], dt[u], dim);
+                    ukeys[c] = float_key(dt[u] + e);
+                    eps_max = fmaxf(eps_max, e);
+                }
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) eps_max = fmaxf(eps_max, __shfl_xor_sync(0xffffffffu, eps_max, o));
+        if (lane == 0) S.hist[warp] = __float_as_uint(eps_max);
+        __syncthreads();
+        eps_max = 0.0f;
+        for (int w = 0; w < SS_NT / 32; ++w) eps_max = fmaxf(eps_max, __uint_as_float(S.hist[w]));
+        __syncthreads();
+    }
 
-    // 1) U* = kk-th smallest upper bound (4-pass radix select on order-preserving keys).
+    // 1) U* = kk-th smallest upper bound (4-pass radix select on order-preserving keys;
+    //    histogram updates aggregated per warp, since the keys of one row share most
+    //    of their leading bits).
     uint32_t prefix = 0, mask = 0;
     if (threadIdx.x == 0) S.remaining = (uint32_t)kk;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = threadIdx.x; i < 256; i += SS_NT) S.hist[i] = 0;
         __syncthreads();
-        for (int c = threadIdx.x; c < nc; c += SS_NT) {
-            const float dt = drow[c];
-            const uint32_t key = float_key(dt + screen_eps(rn, cn[c], dt, dim));
-            if ((key & mask) == prefix) atomicAdd(&S.hist[(key >> shift) & 255u], 1u);
+        for (int c0 = 0; c0 < nc; c0 += SS_NT) {
+            const int c = c0 + threadIdx.x;
+            uint32_t key = 0;
+            bool part = false;
+            if (c < nc) {
+                if (cached) {
+                    key = ukeys[c];
+                } else {
+                    const float dt = drow[c];
+                    key = float_key(dt + screen_eps(rn, cn[c], dt, dim));
+                }
+                part = (key & mask) == prefix;
+            }
+            // lanes sharing the first participating lane's bin add once, the rest alone
+            const unsigned act = __ballot_sync(0xffffffffu, part);
+            if (act) {
+                const uint32_t bin = (key >> shift) & 255u;
+                const uint32_t bin0 = __shfl_sync(0xffffffffu, bin, __ffs(act) - 1);
+                const unsigned same = __ballot_sync(0xffffffffu, part && bin == bin0);
+                if (lane == __ffs(act) - 1) atomicAdd(&S.hist[bin0], (uint32_t)__popc(same));
+                if (part && bin != bin0) atomicAdd(&S.hist[bin], 1u);
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -353,70 +406,79 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
         __syncthreads();
     }
     const float ustar = key_float(prefix);
+    // With cached keys, a column can only be a candidate (lower bound <= U*) if its
+    // upper bound is <= U* + 2 max eps (+ a rounding margin).
+    const uint32_t ukey_cut = float_key(ustar + 2.0f * eps_max + fabsf(ustar) * 1e-6f + 1e-30f);
 
-    // 2) Candidates in index order (lower bound <= U*), refined exactly, selected with a
-    //    running top-kk by (exact distance, index).
-    int carry = 0;
-    int base = 0;
-    while (base < nc) {
-        // gather up to SS_CAP candidates after the carried ones
+    // 2) Column chunks of SS_CAP: candidates (lower bound <= U*) refined exactly, then
+    //    the kk smallest (exact distance, index) of carried winners + candidates.
+    // With cached keys, count the candidate superset first: when it fits, one chunk
+    // spans the whole row.
+    int chunk = SS_CAP;
+    if (cached) {
         if (threadIdx.x == 0) S.count = 0;
         __syncthreads();
-        int c0 = base;
-        for (; c0 < nc; c0 += SS_NT) {
+        uint32_t mine = 0;
+        for (int c = threadIdx.x; c < nc; c += SS_NT) mine += ukeys[c] <= ukey_cut ? 1u : 0u;
+        for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+        if (lane == 0 && mine) atomicAdd(&S.count, mine);
+        __syncthreads();
+        if (S.count <= (uint32_t)SS_CAP) chunk = nc;
+        __syncthreads();
+    }
+    int carry = 0;
+    for (int cb = 0; cb < nc; cb += chunk) {
+        const int ce = min(nc, cb + chunk);
+        if (threadIdx.x == 0) S.count = 0;
+        __syncthreads();
+        for (int c0 = cb; c0 < ce; c0 += SS_NT) {
             const int c = c0 + threadIdx.x;
             bool cand = false;
-            if (c < nc) {
+            if (c < ce && (!cached || ukeys[c] <= ukey_cut)) {
                 const float dt = drow[c];
                 cand = (dt - screen_eps(rn, cn[c], dt, dim)) <= ustar;
             }
-            uint32_t tot;
-            const uint32_t r = block_rank<SS_NT>(cand, S.warp_tmp, &tot);
-            const uint32_t cur = S.count;
-            if (cand && cur + r < (uint32_t)SS_CAP) S.idx[carry + cur + r] = (uint32_t)c;
-            __syncthreads();
-            if (threadIdx.x == 0) S.count = cur + tot;
-            __syncthreads();
-            if (S.count >= (uint32_t)(SS_CAP - SS_NT)) { c0 += SS_NT; break; }
-        }
-        base = c0;
-        const int nnew = (int)min(S.count, (uint32_t)SS_CAP);
-        if (S.count > (uint32_t)SS_CAP && threadIdx.x == 0) atomicExch(err, 10);
-        // exact distances for the new candidates: 4 per warp per step
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int b0 = warp * 4; b0 < nnew; b0 += (SS_NT / 32) * 4) {
-            const int ci = b0 + (lane >> 3);
-            const bool act = ci < nnew;
-            const uint32_t c = act ? S.idx[carry + ci] : 0u;
-            const float v = warp_l2_group(xr, cent + (long long)c * dim, dim, act);
-            if (act && (lane & 7) == 0) {
-                S.exact[carry + ci] = v;
-                if (c == kc) S.keep_val = v;
+            const unsigned bal = __ballot_sync(0xffffffffu, cand);
+            if (bal) {
+                uint32_t base = 0;
+                if (lane == 0) base = atomicAdd(&S.count, (uint32_t)__popc(bal));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (cand) S.cidx[base + __popc(bal & ((1u << lane) - 1u))] = (uint32_t)c;
             }
         }
         __syncthreads();
-        const int n = carry + nnew;
-        const int got = block_select_k<SS_NT>(S.exact, n, kk, S.sortb, S.sel);
-        // compact the winners to the front (positions are into exact/idx)
-        for (int i = threadIdx.x; i < got; i += SS_NT) {
-            const uint32_t pos = (uint32_t)(S.sortb[i] & 0xffffffffull);
-            S.sortb[i] = ((unsigned long long)float_key(S.exact[pos]) << 32) | S.idx[pos];
+        const int nnew = (int)S.count;
+        // exact distances, 4 candidates per warp per step
+        for (int b0 = warp * 4; b0 < nnew; b0 += (SS_NT / 32) * 4) {
+            const int ci = b0 + (lane >> 3);
+            const bool act = ci < nnew;
+            const uint32_t c = act ? S.cidx[ci] : 0u;
+            const float v = warp_l2_group(xr, cent + (long long)c * dim, dim, act);
+            if (act && (lane & 7) == 0) {
+                S.keys[carry + ci] = ((unsigned long long)float_key(v) << 32) | c;
+                if (c == kc) S.keep_val = v;
+            }
         }
+        const int total = carry + nnew;
+        const int p2 = next_pow2(total < 2 ? 2 : total);
         __syncthreads();
-        for (int i = threadIdx.x; i < got; i += SS_NT) {
-            S.exact[i] = key_float((uint32_t)(S.sortb[i] >> 32));
-            S.idx[i] = (uint32_t)(S.sortb[i] & 0xffffffffull);
-        }
-        __syncthreads();
-        carry = got;
+        for (int i = total + threadIdx.x; i < p2; i += SS_NT) S.keys[i] = ~0ull;
+        bitonic_sort_u64<SS_NT>(S.keys, p2);
+        carry = total < kk ? total : kk;
     }
     // 3) Output in (exact distance, index) order; with `keep`, a tie with the current
     //    assignment keeps it.
-    if (threadIdx.x == 0 && keep && carry >= 1 && S.keep_val == S.exact[0]) S.idx[0] = kc;
     __syncthreads();
     for (int i = threadIdx.x; i < k; i += SS_NT) {
-        out_idx[row * k + i] = i < carry ? S.idx[i] : 0u;
-        if (out_val) out_val[row * k + i] = i < carry ? S.exact[i] : FLT_MAX;
+        uint32_t id = 0u;
+        float v = FLT_MAX;
+        if (i < carry) {
+            id = (uint32_t)(S.keys[i] & 0xffffffffull);
+            v = key_float((uint32_t)(S.keys[i] >> 32));
+            if (i == 0 && keep && S.keep_val == v) id = kc;
+        }
+        out_idx[row * k + i] = id;
+        if (out_val) out_val[row * k + i] = v;
     }
 }
 
@@ -425,13 +487,9 @@ void launch_screen_select(const float* Dt, long long n_rows, long long ldd, int 
                           uint32_t* out_idx, float* out_val, int* err, cudaStream_t st) {
     if (n_rows <= 0) return;
     if (k > kMaxK) throw CudaError("screen_select: k exceeds the supported maximum");
-    const size_t smem = sizeof(ScreenSmem);
-    static bool attr = false;
-    if (!attr) {
-        check(cudaFuncSetAttribute(screen_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-              "cudaFuncSetAttribute(screen_select)");
-        attr = true;
-    }
+    const size_t smem = sizeof(ScreenSmem) + (nc <= SS_SMEM_KEYS ? (size_t)nc * sizeof(uint32_t) : 0);
+    check(cudaFuncSetAttribute(screen_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+          "cudaFuncSetAttribute(screen_select)");
     screen_select_kernel<<<(unsigned)n_rows, SS_NT, smem, st>>>(Dt, ldd, nc, x, dim, cent, xn, cn, k, keep, out_idx,
                                                                  out_val, err);
     check(cudaGetLastError(), "screen_select_kernel");

@@ -759,8 +759,8 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
 
     check(cudaEventRecord(w.ev[0], st), "cudaEventRecord");
     // Threshold source: FAST top-k over each query's nearest list.
-    launch_scan_blocked(a.T, a.nq, a.pbase, a.probe, a.nprobe, 1, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm, a.ids,
-                        a.k, w.p1_ids.data(), w.p1_d.data(), w.p1_n.data(), nullptr, 0, st);
+    launch_scan_blocked_split(a.T, a.nq, a.pbase, a.probe, a.nprobe, 1, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm,
+                              a.ids, a.k, w.p1_ids.data(), w.p1_d.data(), w.p1_n.data(), nullptr, 0, w.split, st);
     check(cudaEventRecord(w.ev[1], st), "cudaEventRecord");
     launch_query_prep(a.rq, a.nq, a.dim, w.rqb.data(), w.rqn.data(), st);
     tau_prep_kernel<<<(int)std::min<long long>((a.nq + 255) / 256, 148LL * 4), 256, 0, st>>>(
@@ -845,8 +845,9 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
 #undef VGPU_RF
     VGPU_LAUNCH("tl_refine_kernel");
     check(cudaEventRecord(w.ev[4], st), "cudaEventRecord");
-    launch_scan_blocked(a.T, a.nq, a.pbase, a.probe, a.nprobe, a.nprobe, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm,
-                        a.ids, a.k, a.out_ids, a.out_d, a.out_n, w.cand_cnt.data(), (uint32_t)w.cap, st);
+    launch_scan_blocked_split(a.T, a.nq, a.pbase, a.probe, a.nprobe, a.nprobe, a.m, a.offs, a.blk_off, a.bcodes,
+                              a.bvterm, a.ids, a.k, a.out_ids, a.out_d, a.out_n, w.cand_cnt.data(), (uint32_t)w.cap,
+                              w.split, st);
     check(cudaEventRecord(w.ev[5], st), "cudaEventRecord");
     cand_stats_kernel<<<(int)std::min<long long>((a.nq + 255) / 256, 148LL * 4), 256, 0, st>>>(
         w.cand_cnt.data(), a.nq, (uint32_t)w.cap, w.stats.data());
