@@ -21,17 +21,23 @@ def _index():
     return IvfPqIndex()
 
 
-def _search(idx, q, k, npb, scan):
-    old = os.environ.get("VGPU_SCAN")
-    os.environ["VGPU_SCAN"] = scan
+def _search(idx, q, k, npb, scan, threshold=None):
+    env = {"VGPU_SCAN": scan, "VGPU_LIST_THRESHOLD": threshold}
+    old = {key: os.environ.get(key) for key in env}
+    for key, val in env.items():
+        if val is None:
+            os.environ.pop(key, None)
+        else:
+            os.environ[key] = val
     try:
         out = idx.search_batch(q, k, npb)
         variant = idx.last_timings()["scan_variant"]
     finally:
-        if old is None:
-            del os.environ["VGPU_SCAN"]
-        else:
-            os.environ["VGPU_SCAN"] = old
+        for key, val in old.items():
+            if val is None:
+                os.environ.pop(key, None)
+            else:
+                os.environ[key] = val
     return out, variant
 
 
@@ -55,17 +61,21 @@ CASES = [
     (256, 16, 32, 30000, 200, True, [(10, 6), (100, 12)]),
     (768, 96, 48, 20000, 130, True, [(10, 8), (100, 20)]),
     (512, 64, 40, 20000, 150, False, [(20, 10)]),
+    (128, 16, 6, 90000, 300, True, [(10, 3), (100, 5)]),   # nearest lists > 8192 entries
 ]
 
 
+@pytest.mark.parametrize("threshold", [None, "tc"])
 @pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES)
-def test_list_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches):
+def test_list_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches, threshold):
+    """threshold None: long nearest lists get their threshold from the tensor-core
+    pass, short ones from the blocked scan; "tc": every query from the tensor cores."""
     rng = np.random.default_rng(dim + m + nlist)
     idx, cent = _build(rng, dim, m, nlist, n, rot)
     q = (cent[rng.integers(0, nlist, nq)] + 0.3 * rng.standard_normal((nq, dim))).astype(np.float32)
     for k, npb in searches:
         (bi, bd, bn), vb = _search(idx, q, k, npb, "blocked")
-        (ti, td, tn), vt = _search(idx, q, k, npb, "tc")
+        (ti, td, tn), vt = _search(idx, q, k, npb, "tc", threshold)
         assert vb == 3 and vt == 4
         assert np.array_equal(bn, tn)
         assert np.array_equal(bd, td)

@@ -39,6 +39,9 @@ struct TlWork {
     DeviceBuffer<float> rqn, tau, p1_d;
     DeviceBuffer<uint64_t> p1_ids;
     DeviceBuffer<uint32_t> p1_n, cnt, cursor, seg_off, units, unit_off, unit_list, seg_meta, cand_cnt, counter;
+    DeviceBuffer<uint32_t> p0, mcount, mins_off, run_lut;   // threshold pass over long nearest lists
+    DeviceBuffer<float> pbase0, mins;
+    uint32_t* host_u32 = nullptr;                            // pinned
     DeviceBuffer<unsigned long long> cand;
     DeviceBuffer<unsigned char> scan_tmp;
     // stats[0] += candidates refined, stats[1] += queries left to the blocked scan
@@ -56,6 +59,7 @@ struct TlWork {
     ~TlWork() {
         for (auto& e : ev)
             if (e) cudaEventDestroy(e);
+        if (host_u32) cudaFreeHost(host_u32);
     }
 };
 

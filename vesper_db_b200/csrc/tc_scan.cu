@@ -31,6 +31,8 @@
 #include <cuda_bf16.h>
 
 #include <cfloat>
+#include <cstdlib>
+#include <string>
 
 #include "kernels.cuh"
 #include "kernels_tc.cuh"
@@ -43,6 +45,7 @@ CUtensorMap make_tile_map_bf16(const void* base, long long rows, int dim, int bo
 
 namespace {
 constexpr int TL_M = 128;          // entries per tile (TMEM lanes)
+constexpr uint32_t kSkipPair = 0xffffffffu;  // probe entry left out of a pair grouping
 constexpr int TL_THREADS = 224;    // 7 warps: 0-3 decode + epilogue, 4 TMA, 5 MMA, 6 scheduler
 constexpr int TL_QG = 1024;        // query chunks per unit (a unit is normally a whole list tile)
 constexpr float kSlackMul = 0.03125f;           // 2^-5: bf16 products + tensor-core accumulation
@@ -138,6 +141,8 @@ struct TlParams {
     const uint32_t* unit_off;   // [nlist + 1]
     uint32_t* unit_counter;
     unsigned long long* cand;   // [nq x cap] (probe << 32 | position)
+    float* mins;                // threshold pass: per (query, tile, warp) minimum upper bound (else null)
+    const uint32_t* mins_off;   // [nq] first slot of each query's minima
     uint32_t* cand_cnt;         // [nq]
     int* err;
     int nlist, nprobe, dim, m, k, cap;
@@ -472,6 +477,28 @@ __global__ void __launch_bounds__(TL_THREADS, 1) tc_list_scan_kernel(const __gri
                         tc::fence_before_sync();
                         tc::mbar_arrive(&acce[buf]);
                     }
+                    if (P.mins) {
+                        // Threshold pass: lane j records, for column h*32+j, the smallest
+                        // upper bound (approx + slack) among this warp's 32 rows.
+                        float mine = FLT_MAX;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const uint4 md = bm[h * 32 + j];
+                            const float bj = __uint_as_float(md.y);
+                            float ub = FLT_MAX;
+                            if (vrow) {
+                                const float approx = fmaf(-2.0f, __uint_as_float(acc[j]), bj + u);
+                                ub = approx + fmaf(sx, __uint_as_float(md.w), kSlackAbs * (fabsf(bj) + fabsf(u)));
+                            }
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) ub = fminf(ub, __shfl_xor_sync(0xffffffffu, ub, o));
+                            if (lane == j) mine = ub;
+                        }
+                        const uint32_t qt = bm[h * 32 + lane].x;
+                        if (qt != 0xffffffffu)
+                            P.mins[P.mins_off[qt >> 10] + ui.tile * 4 + warp] = mine;
+                        continue;
+                    }
                     uint32_t mask = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -522,28 +549,86 @@ __global__ void query_prep_kernel(const float* __restrict__ rq, long long nq, in
     }
 }
 
-// tau[q] = k-th FAST distance over q's nearest list; a query whose nearest list has
-// fewer than k entries is not screened (tau = -FLT_MAX) and is marked as overflowed so
-// that the blocked scan handles it.
-__global__ void tau_prep_kernel(const float* __restrict__ p1_d, const uint32_t* __restrict__ p1_n, long long nq,
-                                int k, int cap, float* __restrict__ tau, uint32_t* __restrict__ cand_cnt) {
+// Per query: nearest-list size L0; queries with L0 > small_max (and k <= 256) get their
+// threshold from the tensor-core pass over that list (pair kept in p0, 4 minima per
+// 128-entry tile), the others from the blocked scan (run flag).
+__global__ void home_split_kernel(const uint32_t* __restrict__ probe, int nprobe, const float* __restrict__ pbase,
+                                  const uint64_t* __restrict__ offs, long long nq, uint32_t small_max, int big_ok,
+                                  uint32_t* __restrict__ p0, float* __restrict__ pbase0, uint32_t* __restrict__ mcount,
+                                  uint32_t* __restrict__ run_lut) {
     for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
-        const bool full = p1_n[q] == (uint32_t)k;
-        tau[q] = full ? p1_d[q * k + k - 1] : -FLT_MAX;
-        cand_cnt[q] = full ? 0u : (uint32_t)cap + 1u;
+        const uint32_t l = probe[q * nprobe];
+        const uint64_t L0 = offs[l + 1] - offs[l];
+        const bool big = big_ok && L0 > small_max;
+        p0[q] = big ? l : kSkipPair;
+        pbase0[q] = pbase[q * nprobe];
+        mcount[q] = big ? (uint32_t)(4 * ((L0 + 127) / 128)) : 0u;
+        run_lut[q] = big ? 0u : 1u;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) mcount[nq] = 0;
+}
+
+// tau[q] = k-th smallest of the query's minima (radix select on order-preserving keys,
+// one CTA per query with minima).
+__global__ void __launch_bounds__(256) minima_select_kernel(const float* __restrict__ mins,
+                                                            const uint32_t* __restrict__ mins_off,
+                                                            const uint32_t* __restrict__ mcount, int k,
+                                                            float* __restrict__ tau) {
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t remaining, thresh;
+    const long long q = blockIdx.x;
+    const uint32_t n = mcount[q];
+    if (n == 0) return;
+    const float* v = mins + mins_off[q];
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0, mask = 0;
+    if (threadIdx.x == 0) remaining = (uint32_t)min((uint32_t)k, n);
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += 256) hist[i] = 0;
+        __syncthreads();
+        for (uint32_t c0 = 0; c0 < n; c0 += 256) {
+            const uint32_t c = c0 + threadIdx.x;
+            uint32_t key = 0;
+            bool part = false;
+            if (c < n) {
+                key = float_key(v[c]);
+                part = (key & mask) == prefix;
+            }
+            const unsigned act = __ballot_sync(0xffffffffu, part);
+            if (act) {
+                const uint32_t bin = (key >> shift) & 255u;
+                const uint32_t bin0 = __shfl_sync(0xffffffffu, bin, __ffs(act) - 1);
+                const unsigned same = __ballot_sync(0xffffffffu, part && bin == bin0);
+                if (lane == __ffs(act) - 1) atomicAdd(&hist[bin0], (uint32_t)__popc(same));
+                if (part && bin != bin0) atomicAdd(&hist[bin], 1u);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t rem = remaining, acc = 0, b = 0;
+            for (; b < 256; ++b) { const uint32_t h = hist[b]; if (acc + h >= rem) break; acc += h; }
+            remaining = rem - acc;
+            thresh = b;
+        }
+        __syncthreads();
+        prefix |= thresh << shift;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    // fewer than k finite minima: no usable threshold
+    if (threadIdx.x == 0) {
+        const float t = key_float(prefix);
+        tau[q] = (n >= (uint32_t)k && t < FLT_MAX) ? t : -FLT_MAX;
     }
 }
 
-// qperm[i] = rqb[q(i)]: the bf16 query rows in the list-grouped pair order (one warp
-// per row, 16-byte copies).
-__global__ void qperm_kernel(const uint4* __restrict__ seg_meta, long long npairs, const uint4* __restrict__ rqb,
-                             int row16, uint4* __restrict__ qperm) {
-    const int lane = threadIdx.x & 31;
-    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
-    for (long long i = w; i < npairs; i += nw) {
-        const uint32_t q = __ldg(&seg_meta[i].x) >> 10;
-        for (int c = lane; c < row16; c += 32) qperm[i * row16 + c] = __ldg(&rqb[(long long)q * row16 + c]);
+// tau from the blocked scan for the queries it ran on (run_lut), overflow marks.
+__global__ void tau_merge_kernel(const float* __restrict__ p1_d, const uint32_t* __restrict__ p1_n,
+                                 const uint32_t* __restrict__ run_lut, long long nq, int k, int cap,
+                                 float* __restrict__ tau, uint32_t* __restrict__ cand_cnt) {
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
+        if (run_lut[q]) tau[q] = p1_n[q] == (uint32_t)k ? p1_d[q * k + k - 1] : -FLT_MAX;
+        cand_cnt[q] = tau[q] > -FLT_MAX ? 0u : (uint32_t)cap + 1u;
     }
 }
 
@@ -564,10 +649,24 @@ __global__ void cand_stats_kernel(const uint32_t* __restrict__ cand_cnt, long lo
     }
 }
 
+// qperm[i] = rqb[q(i)]: the bf16 query rows in the list-grouped pair order (one warp
+// per row, 16-byte copies); *total = number of grouped pairs.
+__global__ void qperm_kernel(const uint4* __restrict__ seg_meta, const uint32_t* __restrict__ total,
+                             const uint4* __restrict__ rqb, int row16, uint4* __restrict__ qperm) {
+    const long long npairs = *total;
+    const int lane = threadIdx.x & 31;
+    const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long i = w; i < npairs; i += nw) {
+        const uint32_t q = __ldg(&seg_meta[i].x) >> 10;
+        for (int c = lane; c < row16; c += 32) qperm[i * row16 + c] = __ldg(&rqb[(long long)q * row16 + c]);
+    }
+}
+
 __global__ void pair_hist_kernel(const uint32_t* __restrict__ probe, long long npairs, uint32_t* __restrict__ cnt) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npairs;
          i += (long long)gridDim.x * blockDim.x)
-        atomicAdd(&cnt[probe[i]], 1u);
+        if (probe[i] != kSkipPair) atomicAdd(&cnt[probe[i]], 1u);
 }
 
 // Pairs grouped by list, each with the metadata the screen's epilogue needs:
@@ -579,6 +678,7 @@ __global__ void pair_scatter_kernel(const uint32_t* __restrict__ probe, long lon
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npairs;
          i += (long long)gridDim.x * blockDim.x) {
         const uint32_t l = probe[i];
+        if (l == kSkipPair) continue;
         const uint32_t q = (uint32_t)(i / nprobe), t = (uint32_t)(i - (long long)q * nprobe);
         seg_meta[seg_off[l] + atomicAdd(&cursor[l], 1u)] =
             make_uint4((q << 10) | t, __float_as_uint(pbase[i]), __float_as_uint(tau[q]), __float_as_uint(rqn[q]));
@@ -731,6 +831,12 @@ void TlWork::reserve(long long nq, int nprobe, int nlist, int dim, int k, int ca
     units.reserve(nlist + 1);
     unit_off.reserve(nlist + 1);
     seg_meta.reserve((size_t)np * 4);
+    p0.reserve(nq);
+    pbase0.reserve(nq);
+    mcount.reserve(nq + 1);
+    mins_off.reserve(nq + 1);
+    run_lut.reserve(nq);
+    if (!host_u32) check(cudaMallocHost(&host_u32, sizeof(uint32_t)), "cudaMallocHost");
     qperm.reserve((size_t)np * dim);
     cand.reserve((size_t)nq * cap_);
     cand_cnt.reserve(nq);
@@ -742,41 +848,30 @@ void TlWork::reserve(long long nq, int nprobe, int nlist, int dim, int k, int ca
     p1_d.reserve((size_t)nq * k);
     p1_n.reserve(nq);
     cap = cap_;
-    size_t need = 0;
+    size_t need = 0, need2 = 0;
     cub::DeviceScan::ExclusiveSum(nullptr, need, cnt.data(), seg_off.data(), nlist + 1);
-    scan_tmp.reserve(need + 256);
+    cub::DeviceScan::ExclusiveSum(nullptr, need2, mcount.data(), mins_off.data(), (int)(nq + 1));
+    scan_tmp.reserve(std::max(need, need2) + 256);
 }
 
-void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
-    const long long npairs = a.nq * a.nprobe;
-    if (a.nq <= 0 || npairs <= 0) return;
-    if (!tc_list_scan_supported(a.dim, a.m, 256)) throw CudaError("tc_list_scan: unsupported shape");
-    if (a.k > kMaxK) throw CudaError("tc_list_scan: k exceeds the supported maximum");
-    if (npairs > 0xffffffffLL || a.nq > (1LL << 22) || a.nprobe > 1024)
-        throw CudaError("tc_list_scan: batch too large (at most 2^22 queries and 1024 probes)");
+namespace {
+constexpr uint32_t kSmallHome = 8192;  // nearest lists up to this size get the blocked-scan threshold
+
+// Group the pairs of probe [nq x np] (kSkipPair entries left out) by list with their
+// epilogue metadata, build the unit table, and gather the list-ordered bf16 query rows.
+void group_pairs(const TlScanArgs& a, TlWork& w, const uint32_t* probe, int np, const float* pbase,
+                 cudaStream_t st) {
     constexpr int N = 128;
-    const int dsub = a.dim / a.m;
-
-    check(cudaEventRecord(w.ev[0], st), "cudaEventRecord");
-    // Threshold source: FAST top-k over each query's nearest list.
-    launch_scan_blocked_split(a.T, a.nq, a.pbase, a.probe, a.nprobe, 1, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm,
-                              a.ids, a.k, w.p1_ids.data(), w.p1_d.data(), w.p1_n.data(), nullptr, 0, w.split, st);
-    check(cudaEventRecord(w.ev[1], st), "cudaEventRecord");
-    launch_query_prep(a.rq, a.nq, a.dim, w.rqb.data(), w.rqn.data(), st);
-    tau_prep_kernel<<<(int)std::min<long long>((a.nq + 255) / 256, 148LL * 4), 256, 0, st>>>(
-        w.p1_d.data(), w.p1_n.data(), a.nq, a.k, w.cap, w.tau.data(), w.cand_cnt.data());
-    VGPU_LAUNCH("tau_prep_kernel");
-
-    // Pairs grouped by list; units per list.
+    const long long npairs = a.nq * np;
     check(cudaMemsetAsync(w.cnt.data(), 0, sizeof(uint32_t) * (a.nlist + 1), st), "memset");
     check(cudaMemsetAsync(w.cursor.data(), 0, sizeof(uint32_t) * (a.nlist + 1), st), "memset");
     const int gb = (int)std::min<long long>((npairs + 255) / 256, 148LL * 8);
-    pair_hist_kernel<<<gb, 256, 0, st>>>(a.probe, npairs, w.cnt.data());
+    pair_hist_kernel<<<gb, 256, 0, st>>>(probe, npairs, w.cnt.data());
     VGPU_LAUNCH("pair_hist_kernel");
     size_t tmp = w.scan_tmp.size();
     check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.cnt.data(), w.seg_off.data(), a.nlist + 1, st),
           "cub::DeviceScan::ExclusiveSum(seg_off)");
-    pair_scatter_kernel<<<gb, 256, 0, st>>>(a.probe, npairs, a.nprobe, w.seg_off.data(), w.cursor.data(), a.pbase,
+    pair_scatter_kernel<<<gb, 256, 0, st>>>(probe, npairs, np, w.seg_off.data(), w.cursor.data(), pbase,
                                             w.tau.data(), w.rqn.data(), reinterpret_cast<uint4*>(w.seg_meta.data()));
     VGPU_LAUNCH("pair_scatter_kernel");
     unit_count_kernel<<<(a.nlist + 1 + 255) / 256, 256, 0, st>>>(w.cnt.data(), a.offs, a.nlist, N, w.units.data());
@@ -787,7 +882,17 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     unit_fill_kernel<<<148 * 4, 256, 0, st>>>(w.unit_off.data(), a.nlist, w.unit_list.data());
     VGPU_LAUNCH("unit_fill_kernel");
     check(cudaMemsetAsync(w.counter.data(), 0, sizeof(uint32_t), st), "memset");
+    qperm_kernel<<<148 * 16, 256, 0, st>>>(reinterpret_cast<const uint4*>(w.seg_meta.data()),
+                                           w.seg_off.data() + a.nlist, reinterpret_cast<const uint4*>(w.rqb.data()),
+                                           a.dim / 8, reinterpret_cast<uint4*>(w.qperm.data()));
+    VGPU_LAUNCH("qperm_kernel");
+}
 
+// One launch of the screening kernel over the grouped pairs (mins != null: threshold pass).
+void screen_pass(const TlScanArgs& a, TlWork& w, long long npairs, int np, float* mins, const uint32_t* mins_off,
+                 cudaStream_t st) {
+    constexpr int N = 128;
+    const int dsub = a.dim / a.m;
     TlParams P;
     P.rqb = reinterpret_cast<const __nv_bfloat16*>(w.rqb.data()); P.rqn = w.rqn.data(); P.pbase = a.pbase;
     P.tau = w.tau.data();
@@ -796,17 +901,12 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     P.seg_off = w.seg_off.data(); P.seg_meta = reinterpret_cast<const uint4*>(w.seg_meta.data());
     P.unit_off = w.unit_off.data(); P.unit_list = w.unit_list.data();
     P.unit_counter = w.counter.data(); P.cand = w.cand.data(); P.cand_cnt = w.cand_cnt.data(); P.err = a.err;
-    P.nlist = a.nlist; P.nprobe = a.nprobe; P.dim = a.dim; P.m = a.m; P.k = a.k; P.cap = w.cap;
-
+    P.mins = mins; P.mins_off = mins_off;
+    P.nlist = a.nlist; P.nprobe = np; P.dim = a.dim; P.m = a.m; P.k = a.k; P.cap = w.cap;
     int dev = 0, sms = 148;
     check(cudaGetDevice(&dev), "cudaGetDevice");
     check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
-    qperm_kernel<<<148 * 16, 256, 0, st>>>(reinterpret_cast<const uint4*>(w.seg_meta.data()), npairs,
-                                           reinterpret_cast<const uint4*>(w.rqb.data()), a.dim / 8,
-                                           reinterpret_cast<uint4*>(w.qperm.data()));
-    VGPU_LAUNCH("qperm_kernel");
     const CUtensorMap qmap = make_tile_map_bf16(w.qperm.data(), npairs, a.dim, 128);
-    check(cudaEventRecord(w.ev[2], st), "cudaEventRecord");
 #define VGPU_TL(SV, DSV)                                                                                 \
     do {                                                                                                 \
         const size_t smem = tl_smem<SV>(a.dim, a.m);                                                     \
@@ -814,7 +914,7 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
         check(cudaFuncSetAttribute(tc_list_scan_kernel<N, SV, DSV>,                                      \
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),             \
               "cudaFuncSetAttribute(tc_list_scan)");                                                     \
-        tc_list_scan_kernel<N, SV, DSV><<<sms, TL_THREADS, smem, st>>>(qmap, P);                               \
+        tc_list_scan_kernel<N, SV, DSV><<<sms, TL_THREADS, smem, st>>>(qmap, P);                         \
     } while (0)
     if (a.dim > 512) {  // part of the tile in shared memory: 8 B stages
         if (dsub == 4) VGPU_TL(8, 4); else if (dsub == 8) VGPU_TL(8, 8); else VGPU_TL(8, 16);
@@ -823,6 +923,58 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     }
 #undef VGPU_TL
     VGPU_LAUNCH("tc_list_scan_kernel");
+}
+}  // namespace
+
+void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
+    const long long npairs = a.nq * a.nprobe;
+    if (a.nq <= 0 || npairs <= 0) return;
+    if (!tc_list_scan_supported(a.dim, a.m, 256)) throw CudaError("tc_list_scan: unsupported shape");
+    if (a.k > kMaxK) throw CudaError("tc_list_scan: k exceeds the supported maximum");
+    if (npairs > 0xffffffffLL || a.nq > (1LL << 22) || a.nprobe > 1024)
+        throw CudaError("tc_list_scan: batch too large (at most 2^22 queries and 1024 probes)");
+
+    check(cudaEventRecord(w.ev[0], st), "cudaEventRecord");
+    launch_query_prep(a.rq, a.nq, a.dim, w.rqb.data(), w.rqn.data(), st);
+    // Thresholds.  A query whose nearest list is long gets tau from a tensor-core pass
+    // over that list: the k-th smallest of per-warp minima of the pairs' proven upper
+    // bounds (k distinct entries, so an upper bound of its k-th FAST distance).  The
+    // others take the k-th FAST distance over their nearest list (blocked scan).
+    const int gq = (int)std::min<long long>((a.nq + 255) / 256, 148LL * 4);
+    // VGPU_LIST_THRESHOLD=tc / lut forces one threshold source for every query.
+    uint32_t small_max = kSmallHome;
+    if (const char* v = std::getenv("VGPU_LIST_THRESHOLD")) {
+        if (std::string(v) == "tc") small_max = 0;
+        if (std::string(v) == "lut") small_max = 0xffffffffu;
+    }
+    home_split_kernel<<<gq, 256, 0, st>>>(a.probe, a.nprobe, a.pbase, a.offs, a.nq, small_max, a.k <= 256 ? 1 : 0,
+                                          w.p0.data(), w.pbase0.data(), w.mcount.data(), w.run_lut.data());
+    VGPU_LAUNCH("home_split_kernel");
+    size_t tmp = w.scan_tmp.size();
+    check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.mcount.data(), w.mins_off.data(), (int)(a.nq + 1), st),
+          "cub::DeviceScan::ExclusiveSum(mins_off)");
+    check(cudaMemcpyAsync(w.host_u32, w.mins_off.data() + a.nq, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
+    launch_scan_blocked_split(a.T, a.nq, a.pbase, a.probe, a.nprobe, 1, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm,
+                              a.ids, a.k, w.p1_ids.data(), w.p1_d.data(), w.p1_n.data(), w.run_lut.data(), 0u,
+                              w.split, st);  // synchronizes the stream: host_u32 is ready
+    const uint32_t n_mins = *w.host_u32;
+    if (n_mins > 0) {
+        w.mins.reserve(n_mins);
+        group_pairs(a, w, w.p0.data(), 1, w.pbase0.data(), st);
+        screen_pass(a, w, a.nq, 1, w.mins.data(), w.mins_off.data(), st);
+        minima_select_kernel<<<(unsigned)a.nq, 256, 0, st>>>(w.mins.data(), w.mins_off.data(), w.mcount.data(), a.k,
+                                                             w.tau.data());
+        VGPU_LAUNCH("minima_select_kernel");
+    }
+    tau_merge_kernel<<<gq, 256, 0, st>>>(w.p1_d.data(), w.p1_n.data(), w.run_lut.data(), a.nq, a.k, w.cap,
+                                         w.tau.data(), w.cand_cnt.data());
+    VGPU_LAUNCH("tau_merge_kernel");
+    check(cudaEventRecord(w.ev[1], st), "cudaEventRecord");
+
+    // Pairs grouped by list; units per list; list-ordered query rows.
+    group_pairs(a, w, a.probe, a.nprobe, a.pbase, st);
+    check(cudaEventRecord(w.ev[2], st), "cudaEventRecord");
+    screen_pass(a, w, npairs, a.nprobe, nullptr, nullptr, st);
     check(cudaEventRecord(w.ev[3], st), "cudaEventRecord");
 
     // Refine the candidates; overflowed queries fall back to the blocked scan.
