@@ -229,7 +229,7 @@ public:
         if (v && std::string(v) == "tc") return true;
         if (v && (std::string(v) == "blocked" || std::string(v) == "split")) return false;
         const double per_query = (double)n_vectors / std::max<uint32_t>(nlist(), 1) * np;
-        return per_query >= 4096.0 && nq >= 256;
+        return per_query >= 1024.0 && nq >= 256;
     }
 
     void recompute_vterms() {
