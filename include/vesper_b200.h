@@ -189,6 +189,47 @@ VESPER_C_API vesper_status_t vesper_kmeans_fit_device(const float* d_data, size_
                                                       const vesper_kmeans_params_t* params, float* d_out_centroids,
                                                       uint32_t* d_out_assignments, vesper_kmeans_result_t* out_result);
 
+/* ---------------------------------------------------------------------------------
+ * Exact flat top-k: find_nearest_centroids_batch_fused
+ * (include/vesper/kernels/batch_distances.hpp:338-456), which the reference calls from
+ * C++ only.  For each of nq queries the k_eff = min(k, n_base) best base vectors:
+ *   VESPER_FLAT_L2  squared L2 (avx2_l2_sq lane order), smallest first;
+ *   VESPER_FLAT_IP  inner product (avx2_inner_product lane order), largest first;
+ * equal scores go to the smaller index.  Row q of out_indices / out_scores holds k
+ * entries; entries k_eff..k-1 (only when k > n_base) are index 0xffffffff with score
+ * FLT_MAX (L2) or -FLT_MAX (IP) -- the reference leaves them undefined.
+ * Limits: k <= 1024, dim a multiple of 4 and >= 32, n_base < 2^31.
+ * ------------------------------------------------------------------------------- */
+typedef enum vesper_flat_op_e { VESPER_FLAT_L2 = 0, VESPER_FLAT_IP = 1 } vesper_flat_op_t;
+
+typedef struct vesper_flat_timings_s {
+  float total_ms;          /* device time of the call (norms to results) */
+  float norms_ms;          /* row norms */
+  float sample_ms;         /* pass 1 (screen + exact top-k over a strided sample); the
+                              whole search when single_pass */
+  float filter_ms;         /* pass 2 tensor-core screen over the whole base */
+  float refine_ms;         /* pass 2 exact re-scoring and selection */
+  float fallback_ms;       /* queries whose kept-column list overflowed */
+  uint64_t candidates;     /* kept columns, all queries (pass 2) */
+  uint32_t overflow_queries;
+  uint32_t sample_stride;
+  uint32_t single_pass;    /* 1: base small enough for one screen + select */
+} vesper_flat_timings_t;
+
+/* queries [nq x dim], base [n_base x dim] host; outputs [nq x k] host. */
+VESPER_C_API vesper_status_t vesper_flat_topk(vesper_flat_op_t op, const float* queries, size_t nq,
+                                              const float* base, size_t n_base, size_t dim, uint32_t k,
+                                              uint32_t* out_indices, float* out_scores);
+
+/* Same with all arrays in device memory of the current device (16-byte aligned); the
+ * outputs are complete when the call returns. */
+VESPER_C_API vesper_status_t vesper_flat_topk_device(vesper_flat_op_t op, const float* d_queries, size_t nq,
+                                                     const float* d_base, size_t n_base, size_t dim, uint32_t k,
+                                                     uint32_t* d_out_indices, float* d_out_scores);
+
+/* Stage times of this thread's last vesper_flat_topk[_device] call. */
+VESPER_C_API vesper_status_t vesper_flat_get_last_timings(vesper_flat_timings_t* out);
+
 /* Number of CUDA devices visible to the library. */
 VESPER_C_API int vesper_b200_device_count(void);
 

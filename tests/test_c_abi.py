@@ -92,6 +92,32 @@ def test_kmeans_params_and_precondition_errors():
     assert lib.vesper_kmeans_fit_device(None, 10, 4, C.byref(p), None, None, None) == N.VESPER_ERROR_INVALID_PARAM
 
 
+def test_flat_topk_precondition_errors():
+    """The reference returns early on n_base, nq or k == 0 (batch_distances.hpp:349-350);
+    unsupported shapes and operators are rejected before any device work."""
+    import numpy as np
+    lib = N.load()
+    f32, u32 = C.POINTER(C.c_float), C.POINTER(C.c_uint32)
+    q = np.zeros((3, 32), np.float32)
+    b = np.zeros((10, 32), np.float32)
+    i = np.zeros((3, 2000), np.uint32)
+    s = np.zeros((3, 2000), np.float32)
+    qp, bp, ip, sp = q.ctypes.data_as(f32), b.ctypes.data_as(f32), i.ctypes.data_as(u32), s.ctypes.data_as(f32)
+    assert lib.vesper_flat_topk(N.FLAT_L2, qp, 0, bp, 10, 32, 5, ip, sp) == N.VESPER_OK
+    assert lib.vesper_flat_topk(N.FLAT_IP, qp, 3, bp, 0, 32, 5, ip, sp) == N.VESPER_OK
+    assert lib.vesper_flat_topk(N.FLAT_IP, qp, 3, bp, 10, 32, 0, ip, sp) == N.VESPER_OK
+    assert lib.vesper_flat_topk(7, qp, 3, bp, 10, 32, 5, ip, sp) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_flat_topk(N.FLAT_L2, None, 3, bp, 10, 32, 5, ip, sp) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_flat_topk(N.FLAT_L2, qp, 3, bp, 10, 32, 1025, ip, sp) == N.VESPER_ERROR_INVALID_PARAM
+    assert b"unsupported shape" in lib.vesper_get_last_error()
+    assert lib.vesper_flat_topk(N.FLAT_L2, qp, 3, bp, 10, 30, 5, ip, sp) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_flat_topk_device(N.FLAT_L2, None, 3, None, 10, 32, 5, None, None) == \
+        N.VESPER_ERROR_INVALID_PARAM
+    t = N.FlatTimings()
+    assert lib.vesper_flat_get_last_timings(C.byref(t)) == N.VESPER_OK
+    assert lib.vesper_flat_get_last_timings(None) == N.VESPER_ERROR_INVALID_PARAM
+
+
 def test_missing_library_fails_loudly(tmp_path):
     N_mod = N
     saved = N_mod._lib

@@ -1,0 +1,129 @@
+"""Exact flat top-k (find_nearest_centroids_batch_fused) on the GPU against the oracle.
+
+The GPU path screens every (query, base) pair with tf32 tensor-core products and
+re-scores, in the reference's lane order, every column the proven screening bound cannot
+rule out, so indices and scores must equal the oracle's bit for bit.  Cases: both
+operators; the single-pass path (base <= 65536 rows) and the two-pass path (strided
+sample threshold + filter + refine); k = 1, 10, 100, 300 (the larger kept-column
+capacity); unit-norm 768-d data shaped like the 1M x 768 inner-product workload;
+exact ties (duplicated rows); lists that overflow their capacity (the single-pass
+fallback); k > n_base (padding); and the device-pointer entry point.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _flat(op, q, base, k):
+    from vesper_db_b200 import flat_topk
+    return flat_topk(op, q, base, k)
+
+
+def _timings():
+    from vesper_db_b200.flat import last_timings
+    return last_timings()
+
+
+def _check_equal(op, q, base, k, oracle, single=None):
+    gi, gs = _flat(op, q, base, k)
+    t = _timings()
+    if single is not None:
+        assert t["single_pass"] == (1 if single else 0)
+    ke = min(k, base.shape[0])
+    oi, os_ = oracle.flat_topk(op, q, base, k)
+    assert np.array_equal(gi[:, :ke], oi[:, :ke])
+    assert np.array_equal(gs[:, :ke], os_[:, :ke])
+    return t
+
+
+@pytest.mark.parametrize("op", [0, 1])
+@pytest.mark.parametrize("dim,nb,nq,k", [(128, 5000, 200, 10), (40, 3000, 17, 25), (768, 20000, 64, 100),
+                                         (96, 65536, 100, 1)])
+def test_single_pass(op, dim, nb, nq, k, oracle):
+    rng = np.random.default_rng(dim + nb + op)
+    base = rng.standard_normal((nb, dim)).astype(np.float32)
+    q = rng.standard_normal((nq, dim)).astype(np.float32)
+    _check_equal(op, q, base, k, oracle, single=True)
+
+
+@pytest.mark.parametrize("op", [0, 1])
+@pytest.mark.parametrize("dim,nb,nq,k", [(128, 200000, 300, 100), (64, 150000, 200, 10), (128, 120000, 80, 300)])
+def test_two_pass(op, dim, nb, nq, k, oracle):
+    rng = np.random.default_rng(dim + nb + op + k)
+    base = rng.standard_normal((nb, dim)).astype(np.float32)
+    q = rng.standard_normal((nq, dim)).astype(np.float32)
+    t = _check_equal(op, q, base, k, oracle, single=False)
+    assert t["overflow_queries"] == 0
+    assert t["candidates"] >= nq * k
+
+
+def test_unit_norm_inner_product_768(oracle):
+    """The 1M x 768 inner-product workload's distribution (N(0,1) rows, L2-normalised)
+    at 200k rows."""
+    rng = np.random.default_rng(2024)
+    base = rng.standard_normal((200000, 768)).astype(np.float32)
+    base /= np.linalg.norm(base, axis=1, keepdims=True)
+    q = rng.standard_normal((48, 768)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    t = _check_equal(1, q, base, 100, oracle, single=False)
+    assert t["overflow_queries"] == 0
+
+
+@pytest.mark.parametrize("op", [0, 1])
+def test_ties_go_to_the_smaller_index(op, oracle):
+    rng = np.random.default_rng(11 + op)
+    uniq = rng.standard_normal((30000, 64)).astype(np.float32)
+    base = np.concatenate([uniq, uniq[:25000], uniq[:25000]])   # every row of the head three times
+    perm = rng.permutation(base.shape[0])
+    base = base[perm]
+    q = rng.standard_normal((100, 64)).astype(np.float32)
+    _check_equal(op, q, base, 50, oracle, single=False)
+    _check_equal(op, q, base[:40000], 50, oracle, single=True)
+
+
+@pytest.mark.parametrize("op", [0, 1])
+def test_overflow_uses_single_pass(op, oracle):
+    """Eight distinct rows repeated 12500 times: every column ties with thousands of
+    others, the kept-column lists overflow, and the single-pass fallback answers."""
+    rng = np.random.default_rng(3 + op)
+    uniq = rng.standard_normal((8, 32)).astype(np.float32)
+    base = np.tile(uniq, (12500, 1))
+    q = rng.standard_normal((6, 32)).astype(np.float32)
+    t = _check_equal(op, q, base, 20, oracle, single=False)
+    assert t["overflow_queries"] == 6
+
+
+@pytest.mark.parametrize("op", [0, 1])
+def test_k_larger_than_base(op, oracle):
+    rng = np.random.default_rng(9)
+    base = rng.standard_normal((50, 32)).astype(np.float32)
+    q = rng.standard_normal((7, 32)).astype(np.float32)
+    gi, gs = _flat(op, q, base, 100)
+    oi, os_ = oracle.flat_topk(op, q, base, 100)
+    assert np.array_equal(gi[:, :50], oi[:, :50]) and np.array_equal(gs[:, :50], os_[:, :50])
+    assert np.all(gi[:, 50:] == 0xFFFFFFFF)
+    assert np.all(gs[:, 50:] == (np.float32(np.finfo(np.float32).max) * (1 if op == 0 else -1)))
+
+
+def test_device_entry_point(oracle):
+    import torch
+    from vesper_db_b200 import flat_topk_device
+    rng = np.random.default_rng(21)
+    base = rng.standard_normal((100000, 128)).astype(np.float32)
+    q = rng.standard_normal((64, 128)).astype(np.float32)
+    db, dq = torch.from_numpy(base).cuda(), torch.from_numpy(q).cuda()
+    idx = torch.empty((64, 10), dtype=torch.int32, device="cuda")
+    sc = torch.empty((64, 10), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    flat_topk_device(1, dq.data_ptr(), 64, db.data_ptr(), 100000, 128, 10, idx.data_ptr(), sc.data_ptr())
+    oi, os_ = oracle.flat_topk(1, q, base, 10)
+    assert np.array_equal(idx.cpu().numpy().view(np.uint32), oi)
+    assert np.array_equal(sc.cpu().numpy(), os_)
+
+
+def test_empty_inputs_write_nothing():
+    from vesper_db_b200 import flat_topk
+    base = np.ones((10, 32), np.float32)
+    i, s = flat_topk(0, np.zeros((0, 32), np.float32), base, 5)
+    assert i.shape == (0, 5)

@@ -35,10 +35,14 @@ EXPORTED = [
     "vesper_ivfpq_train_ex_device", "vesper_ivfpq_add_device",
     "vesper_ivfpq_search_batch_device_noalloc",
     "vesper_kmeans_params_init", "vesper_kmeans_fit", "vesper_kmeans_fit_device",
+    "vesper_flat_topk", "vesper_flat_topk_device", "vesper_flat_get_last_timings",
 ]
 
 KMEANS_ELKAN = 0
 KMEANS_LLOYD = 1
+
+FLAT_L2 = 0
+FLAT_IP = 1
 
 
 class TrainParams(C.Structure):
@@ -88,6 +92,13 @@ class KmeansParams(C.Structure):
 
 class KmeansResult(C.Structure):
     _fields_ = [("iterations", C.c_uint32), ("inertia", C.c_float), ("time_sec", C.c_float)]
+
+
+class FlatTimings(C.Structure):
+    _fields_ = [("total_ms", C.c_float), ("norms_ms", C.c_float), ("sample_ms", C.c_float),
+                ("filter_ms", C.c_float), ("refine_ms", C.c_float), ("fallback_ms", C.c_float),
+                ("candidates", C.c_uint64), ("overflow_queries", C.c_uint32), ("sample_stride", C.c_uint32),
+                ("single_pass", C.c_uint32)]
 
 
 _lib = None
@@ -149,6 +160,11 @@ def load(path: str = LIB_PATH) -> C.CDLL:
                                        C.POINTER(KmeansResult)]),
             "vesper_kmeans_fit_device": (st, [vp, C.c_size_t, C.c_size_t, C.POINTER(KmeansParams), vp, vp,
                                               C.POINTER(KmeansResult)]),
+            "vesper_flat_topk": (st, [C.c_int, f32p, C.c_size_t, f32p, C.c_size_t, C.c_size_t, C.c_uint32,
+                                      u32p, f32p]),
+            "vesper_flat_topk_device": (st, [C.c_int, vp, C.c_size_t, vp, C.c_size_t, C.c_size_t, C.c_uint32,
+                                             vp, vp]),
+            "vesper_flat_get_last_timings": (st, [C.POINTER(FlatTimings)]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

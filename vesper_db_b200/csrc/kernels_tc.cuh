@@ -12,6 +12,42 @@ bool tc_screen_supported(int dim);
 // err receives a nonzero code if a bounded wait timed out.
 void launch_tc_screen(const float* x, long long nx, const float* c, int nc, int dim, const float* xn,
                       const float* cn, float* Dt, long long ldd, int* err, cudaStream_t st);
+// ip: Dt = -2 <x_i, c_j> instead (inner-product screen).  c_stride: row stride of c in
+// elements (0 = dim), e.g. to screen a strided sample of a base set.
+void launch_tc_screen_op(bool ip, const float* x, long long nx, const float* c, long long nc, long long c_stride,
+                         int dim, const float* xn, const float* cn, float* Dt, long long ldd, int* err,
+                         cudaStream_t st);
+// Flat top-k filter: the same screen without storing it; column j of row i is appended
+// to cand[i * cap + ...] as {j + col_off, screen value bits} (count in cand_cnt[i],
+// which may exceed cap) when its lower bound is <= tau[i] (L2: distance; ip: -2 *
+// inner product).
+void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, int dim, const float* xn,
+                      const float* cn, const float* tau, uint32_t col_off, uint2* cand, uint32_t* cand_cnt, int cap,
+                      int* err, cudaStream_t st);
+// Exact flat top-k (flat_topk.cu).  Stage times of the last call, in ms.
+struct FlatStats {
+    float total_ms = 0, norms_ms = 0, sample_ms = 0, filter_ms = 0, refine_ms = 0, fallback_ms = 0;
+    unsigned long long candidates = 0;  // kept columns over all queries (pass 2)
+    uint32_t overflow_queries = 0;      // queries redone by the single-pass path
+    int sample_stride = 0, cap = 0, single_pass = 0;
+};
+struct FlatWork {
+    DeviceBuffer<float> xn, cn, cs, tau, dt, s_val, oq, oxn, o_val;
+    DeviceBuffer<uint32_t> s_idx, cand_cnt, over, o_idx;
+    DeviceBuffer<uint2> cand;
+    DeviceBuffer<int> err;
+    cudaEvent_t ev[7] = {};
+    FlatStats last;
+    FlatWork() = default;
+    FlatWork(const FlatWork&) = delete;
+    FlatWork& operator=(const FlatWork&) = delete;
+    ~FlatWork();
+};
+// ip: inner product (largest first), else squared L2 (smallest first).  q, base: device
+// rows (16-byte aligned); out_idx/out_score: device [nq x k].  Synchronous on st.
+void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
+                      uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st);
+
 // out[i] = ||x_i||^2 (fp64 accumulation).
 void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st);
 // Per row: exact k nearest centroids (reference-order distances, ties to the lowest
@@ -20,6 +56,11 @@ void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStre
 void launch_screen_select(const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
                           const float* cent, const float* xn, const float* cn, int k, const uint32_t* keep,
                           uint32_t* out_idx, float* out_val, int* err, cudaStream_t st);
+// The same for L2 or inner-product screens (ip: exact reference-order inner products,
+// larger first); column j is row j * cent_ld of cent.
+void launch_screen_select_op(bool ip, const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
+                             const float* cent, long long cent_ld, const float* xn, const float* cn, int k,
+                             uint32_t* out_idx, float* out_val, int* err, cudaStream_t st);
 
 }  // namespace vgpu
 

@@ -27,6 +27,7 @@
 #include "kernels_tc.cuh"
 #include "select.cuh"
 #include "tc_common.cuh"
+#include "tc_screen.cuh"
 
 namespace vgpu {
 namespace {
@@ -74,11 +75,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 }  // namespace
 
+// MODE 0: Dt = ||x||^2 + ||c||^2 - 2S (L2 screen), 1: Dt = -2S (inner-product screen),
+// 2 / 3: the same values are not stored; column c of row r is appended to the row's
+// candidate list when its lower bound (value - eps) is <= tau[r] (flat top-k filter).
+template <int MODE>
 __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant__ CUtensorMap map_x,
                                                            const __grid_constant__ CUtensorMap map_c, int nx,
                                                            int nc, int dim, const float* __restrict__ xn,
                                                            const float* __restrict__ cn, float* __restrict__ Dt,
-                                                           long long ldd, int* __restrict__ err) {
+                                                           long long ldd, int* __restrict__ err,
+                                                           const float* __restrict__ tau,
+                                                           uint2* __restrict__ cand, uint32_t* __restrict__ cand_cnt,
+                                                           int cap, uint32_t col_off, int qfast) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -88,7 +96,9 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
     __shared__ int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    // qfast: consecutive CTAs share a column tile (columns streamed from HBM once while
+    // the row tiles stay in L2); otherwise they share a row tile.
+    const int m0 = (qfast ? blockIdx.x : blockIdx.y) * BM, n0 = (qfast ? blockIdx.y : blockIdx.x) * BN;
     const int kt = (dim + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -147,11 +157,38 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
             uint32_t r[32];
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(ch * 32), r);
             if (row < nx) {
-                float* out = Dt + (long long)row * ldd + n0 + ch * 32;
+                if constexpr (MODE <= 1) {
+                    float* out = Dt + (long long)row * ldd + n0 + ch * 32;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int col = n0 + ch * 32 + j;
-                    if (col < nc) out[j] = (rn + cn[col]) - 2.0f * __uint_as_float(r[j]);
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = n0 + ch * 32 + j;
+                        if (col < nc)
+                            out[j] = MODE == 0 ? (rn + cn[col]) - 2.0f * __uint_as_float(r[j])
+                                               : -2.0f * __uint_as_float(r[j]);
+                    }
+                } else {
+                    const float t = tau[row];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = n0 + ch * 32 + j;
+                        if (col < nc) {
+                            const float c2 = cn[col];
+                            float dt, e;
+                            if constexpr (MODE == 2) {
+                                dt = (rn + c2) - 2.0f * __uint_as_float(r[j]);
+                                e = screen_eps(rn, c2, dt, dim);
+                            } else {
+                                dt = -2.0f * __uint_as_float(r[j]);
+                                e = screen_eps_ip(rn, c2, dim);
+                            }
+                            if (dt - e <= t) {
+                                const uint32_t slot = atomicAdd(&cand_cnt[row], 1u);
+                                if (slot < (uint32_t)cap)
+                                    cand[(long long)row * cap + slot] = make_uint2((uint32_t)col + col_off,
+                                                                                   __float_as_uint(dt));
+                            }
+                        }
+                    }
                 }
             }
         }
@@ -184,10 +221,10 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-CUtensorMap make_map(const float* base, long long rows, int dim, int box_rows) {
+CUtensorMap make_map(const float* base, long long rows, int dim, int box_rows, long long row_stride = 0) {
     CUtensorMap m;
     const cuuint64_t gdim[2] = {(cuuint64_t)dim, (cuuint64_t)rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)dim * sizeof(float)};
+    const cuuint64_t gstride[1] = {(cuuint64_t)(row_stride ? row_stride : dim) * sizeof(float)};
     const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     const cuuint32_t estride[2] = {1, 1};
     const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride,
@@ -218,23 +255,51 @@ bool tc_screen_supported(int dim) {
     return dim % 4 == 0 && dim >= 32;
 }
 
-void launch_tc_screen(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
-                      float* Dt, long long ldd, int* err, cudaStream_t st) {
+namespace {
+template <int MODE>
+void tc_screen_launch(const float* x, long long nx, const float* c, long long nc, long long c_stride, int dim,
+                      const float* xn, const float* cn, float* Dt, long long ldd, int* err, const float* tau,
+                      uint2* cand, uint32_t* cand_cnt, int cap, uint32_t col_off, cudaStream_t st) {
     if (nx <= 0 || nc <= 0) return;
     if (!tc_screen_supported(dim)) throw CudaError("tc_screen: dim must be a multiple of 4 and >= 32");
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
         throw CudaError("tc_screen: operands must be 16-byte aligned");
+    if (nc > 0x7fffffffLL) throw CudaError("tc_screen: too many columns");
     const CUtensorMap mx = make_map(x, nx, dim, BM);
-    const CUtensorMap mc = make_map(c, nc, dim, BN);
-    static bool attr = false;
-    if (!attr) {
-        check(cudaFuncSetAttribute(tc_screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
-              "cudaFuncSetAttribute(tc_screen)");
-        attr = true;
-    }
-    dim3 grid(ceil_div(nc, BN), ceil_div(nx, BM));
-    tc_screen_kernel<<<grid, 128, SMEM_BYTES, st>>>(mx, mc, (int)nx, nc, dim, xn, cn, Dt, ldd, err);
+    const CUtensorMap mc = make_map(c, nc, dim, BN, c_stride);
+    check(cudaFuncSetAttribute(tc_screen_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+          "cudaFuncSetAttribute(tc_screen)");
+    // Columns larger than a quarter of L2 are streamed once, row tiles fastest.
+    const long long row_bytes = (long long)dim * sizeof(float);
+    const int qfast = (nc * row_bytes > (32LL << 20) && ceil_div(nc, BN) <= 65535) ? 1 : 0;
+    if (!qfast && ceil_div(nx, BM) > 65535) throw CudaError("tc_screen: too many rows for one launch");
+    dim3 grid = qfast ? dim3((unsigned)ceil_div(nx, BM), (unsigned)ceil_div(nc, BN))
+                      : dim3((unsigned)ceil_div(nc, BN), (unsigned)ceil_div(nx, BM));
+    tc_screen_kernel<MODE><<<grid, 128, SMEM_BYTES, st>>>(mx, mc, (int)nx, (int)nc, dim, xn, cn, Dt, ldd, err, tau,
+                                                          cand, cand_cnt, cap, col_off, qfast);
     check(cudaGetLastError(), "tc_screen_kernel");
+}
+}  // namespace
+
+void launch_tc_screen(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
+                      float* Dt, long long ldd, int* err, cudaStream_t st) {
+    tc_screen_launch<0>(x, nx, c, nc, 0, dim, xn, cn, Dt, ldd, err, nullptr, nullptr, nullptr, 0, 0, st);
+}
+
+void launch_tc_screen_op(bool ip, const float* x, long long nx, const float* c, long long nc, long long c_stride,
+                         int dim, const float* xn, const float* cn, float* Dt, long long ldd, int* err,
+                         cudaStream_t st) {
+    if (ip)
+        tc_screen_launch<1>(x, nx, c, nc, c_stride, dim, xn, cn, Dt, ldd, err, nullptr, nullptr, nullptr, 0, 0, st);
+    else
+        tc_screen_launch<0>(x, nx, c, nc, c_stride, dim, xn, cn, Dt, ldd, err, nullptr, nullptr, nullptr, 0, 0, st);
+}
+
+void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, int dim, const float* xn,
+                      const float* cn, const float* tau, uint32_t col_off, uint2* cand, uint32_t* cand_cnt, int cap,
+                      int* err, cudaStream_t st) {
+    if (ip) tc_screen_launch<3>(x, nx, c, nc, 0, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off, st);
+    else tc_screen_launch<2>(x, nx, c, nc, 0, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off, st);
 }
 
 // ---------------------------------------------------------------------------------
@@ -267,45 +332,6 @@ constexpr int SS_NT = 256;
 constexpr int SS_CAP = 1024;   // columns per candidate chunk (at most this many candidates)
 constexpr int SS_SMEM_KEYS = 16384;  // rows up to this width keep their upper-bound keys in shared memory
 
-// Screening error bound.  tf32 truncation of both operands (relative 2^-10 each), fp32
-// accumulation over dim products, fp32 rounding of the epilogue and of the norms, and
-// the reference-order rounding of d_ref; times a safety factor of 2.
-__device__ __forceinline__ float screen_eps(float xn, float cn, float dt, int dim) {
-    const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;   // 2^-9 + (dim+8) 2^-23
-    const float xc = sqrtf(xn * cn);
-    const float e = 2.0f * a * xc + 2.384e-7f * (xn + cn + 2.0f * xc) +
-                    (float)(dim / 8 + 8) * 1.1920929e-7f * fabsf(dt);
-    return 2.0f * e + 1e-30f;
-}
-
-// Exact l2 for up to 4 candidates per warp: lane group g = lane / 8 takes candidate g,
-// lane (lane % 8) plays AVX2 lane l, then an 8-lane hsum in the reference order.
-__device__ __forceinline__ float warp_l2_group(const float* __restrict__ x, const float* __restrict__ c, int dim,
-                                               bool active) {
-    const int lane = threadIdx.x & 31, l = lane & 7;
-    const int simd_end = dim & ~7;
-    float acc = 0.0f;
-    if (active) {
-#pragma unroll 8
-        for (int t = l; t < simd_end; t += 8) {
-            const float d = __fsub_rn(x[t], c[t]);
-            acc = __fmaf_rn(d, d, acc);
-        }
-    }
-    const float a4 = __shfl_down_sync(0xffffffffu, acc, 4, 8);
-    const float s = __fadd_rn(a4, acc);
-    const float s1 = __shfl_down_sync(0xffffffffu, s, 1, 8);
-    const float s2 = __shfl_down_sync(0xffffffffu, s, 2, 8);
-    const float s3 = __shfl_down_sync(0xffffffffu, s, 3, 8);
-    float r = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
-    if (active)
-        for (int t = simd_end; t < dim; ++t) {
-            const float d = __fsub_rn(x[t], c[t]);
-            r = __fadd_rn(r, __fmul_rn(d, d));
-        }
-    return r;  // valid in lane l == 0 of each group
-}
-
 struct ScreenSmem {
     unsigned long long keys[4096];   // (exact key << 32 | index): carried winners + a chunk's candidates
     uint32_t cidx[SS_CAP];           // the chunk's candidate indices (in arrival order)
@@ -315,10 +341,14 @@ struct ScreenSmem {
 };
 }  // namespace
 
+// IP: Dt holds -2 S (inner-product screen); the exact score is the reference-order
+// inner product, larger first (ties to the lower index); out_val receives it.
+// Column c of the screen is row c * cent_ld of cent.
+template <bool IP>
 __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
     const float* __restrict__ Dt, long long ldd, int nc, const float* __restrict__ x, int dim,
-    const float* __restrict__ cent, const float* __restrict__ xn, const float* __restrict__ cn, int k,
-    const uint32_t* __restrict__ keep, uint32_t* __restrict__ out_idx, float* __restrict__ out_val, int* err) {
+    const float* __restrict__ cent, long long cent_ld, const float* __restrict__ xn, const float* __restrict__ cn,
+    int k, const uint32_t* __restrict__ keep, uint32_t* __restrict__ out_idx, float* __restrict__ out_val, int* err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ScreenSmem& S = *reinterpret_cast<ScreenSmem*>(smem_raw);
     const long long row = blockIdx.x;
@@ -348,7 +378,7 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
             for (int u = 0; u < 8; ++u) {
                 const int c = c0 + u * SS_NT;
                 if (c < nc) {
-                    const float e = screen_eps(rn, cv[u], dt[u], dim);
+                    const float e = IP ? screen_eps_ip(rn, cv[u], dim) : screen_eps(rn, cv[u], dt[u], dim);
                     ukeys[c] = float_key(dt[u] + e);
                     eps_max = fmaxf(eps_max, e);
                 }
@@ -379,7 +409,7 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
                     key = ukeys[c];
                 } else {
                     const float dt = drow[c];
-                    key = float_key(dt + screen_eps(rn, cn[c], dt, dim));
+                    key = float_key(dt + (IP ? screen_eps_ip(rn, cn[c], dim) : screen_eps(rn, cn[c], dt, dim)));
                 }
                 part = (key & mask) == prefix;
             }
@@ -436,7 +466,7 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
             bool cand = false;
             if (c < ce && (!cached || ukeys[c] <= ukey_cut)) {
                 const float dt = drow[c];
-                cand = (dt - screen_eps(rn, cn[c], dt, dim)) <= ustar;
+                cand = (dt - (IP ? screen_eps_ip(rn, cn[c], dim) : screen_eps(rn, cn[c], dt, dim))) <= ustar;
             }
             const unsigned bal = __ballot_sync(0xffffffffu, cand);
             if (bal) {
@@ -453,9 +483,12 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
             const int ci = b0 + (lane >> 3);
             const bool act = ci < nnew;
             const uint32_t c = act ? S.cidx[ci] : 0u;
-            const float v = warp_l2_group(xr, cent + (long long)c * dim, dim, act);
+            const float* crow = cent + (long long)c * cent_ld;
+            const float v = IP ? warp_ip_group(xr, crow, dim, act) : warp_l2_group(xr, crow, dim, act);
             if (act && (lane & 7) == 0) {
-                S.keys[carry + ci] = ((unsigned long long)float_key(v) << 32) | c;
+                // inner products order by -v (zero canonicalised so -0 and +0 tie)
+                const float ordv = IP ? (v == 0.0f ? 0.0f : -v) : v;
+                S.keys[carry + ci] = ((unsigned long long)float_key(ordv) << 32) | c;
                 if (c == kc) S.keep_val = v;
             }
         }
@@ -475,24 +508,45 @@ __global__ void __launch_bounds__(SS_NT) screen_select_kernel(
         if (i < carry) {
             id = (uint32_t)(S.keys[i] & 0xffffffffull);
             v = key_float((uint32_t)(S.keys[i] >> 32));
+            if (IP) v = v == 0.0f ? 0.0f : -v;
             if (i == 0 && keep && S.keep_val == v) id = kc;
+        } else if (IP) {
+            v = -FLT_MAX;
         }
         out_idx[row * k + i] = id;
         if (out_val) out_val[row * k + i] = v;
     }
 }
 
-void launch_screen_select(const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
-                          const float* cent, const float* xn, const float* cn, int k, const uint32_t* keep,
-                          uint32_t* out_idx, float* out_val, int* err, cudaStream_t st) {
+namespace {
+template <bool IP>
+void screen_select_launch(const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
+                          const float* cent, long long cent_ld, const float* xn, const float* cn, int k,
+                          const uint32_t* keep, uint32_t* out_idx, float* out_val, int* err, cudaStream_t st) {
     if (n_rows <= 0) return;
     if (k > kMaxK) throw CudaError("screen_select: k exceeds the supported maximum");
     const size_t smem = sizeof(ScreenSmem) + (nc <= SS_SMEM_KEYS ? (size_t)nc * sizeof(uint32_t) : 0);
-    check(cudaFuncSetAttribute(screen_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+    check(cudaFuncSetAttribute(screen_select_kernel<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
           "cudaFuncSetAttribute(screen_select)");
-    screen_select_kernel<<<(unsigned)n_rows, SS_NT, smem, st>>>(Dt, ldd, nc, x, dim, cent, xn, cn, k, keep, out_idx,
-                                                                 out_val, err);
+    screen_select_kernel<IP><<<(unsigned)n_rows, SS_NT, smem, st>>>(Dt, ldd, nc, x, dim, cent, cent_ld, xn, cn, k,
+                                                                    keep, out_idx, out_val, err);
     check(cudaGetLastError(), "screen_select_kernel");
+}
+}  // namespace
+
+void launch_screen_select(const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
+                          const float* cent, const float* xn, const float* cn, int k, const uint32_t* keep,
+                          uint32_t* out_idx, float* out_val, int* err, cudaStream_t st) {
+    screen_select_launch<false>(Dt, n_rows, ldd, nc, x, dim, cent, dim, xn, cn, k, keep, out_idx, out_val, err, st);
+}
+
+void launch_screen_select_op(bool ip, const float* Dt, long long n_rows, long long ldd, int nc, const float* x, int dim,
+                             const float* cent, long long cent_ld, const float* xn, const float* cn, int k,
+                             uint32_t* out_idx, float* out_val, int* err, cudaStream_t st) {
+    if (ip) screen_select_launch<true>(Dt, n_rows, ldd, nc, x, dim, cent, cent_ld, xn, cn, k, nullptr, out_idx,
+                                       out_val, err, st);
+    else screen_select_launch<false>(Dt, n_rows, ldd, nc, x, dim, cent, cent_ld, xn, cn, k, nullptr, out_idx,
+                                     out_val, err, st);
 }
 
 }  // namespace vgpu

@@ -16,6 +16,7 @@
 
 #include "../../include/vesper_b200.h"
 #include "ivf_pq_gpu.hpp"
+#include "kernels_tc.cuh"
 #include "kmeans_gpu.hpp"
 
 using vesper::index::IvfPqIndex;
@@ -488,6 +489,114 @@ VESPER_C_API vesper_status_t vesper_kmeans_fit_device(const float* d_data, size_
                                                       const vesper_kmeans_params_t* params, float* d_out_centroids,
                                                       uint32_t* d_out_assignments, vesper_kmeans_result_t* out_result) {
     return kmeans_fit(d_data, n, dim, params, d_out_centroids, d_out_assignments, out_result, true);
+}
+
+}  // extern "C"
+
+namespace {
+// Per-thread flat top-k context on the current device: stream + reusable scratch.
+struct FlatCtx {
+    int device = -1;
+    cudaStream_t st = nullptr;
+    std::unique_ptr<vgpu::FlatWork> w;
+    ~FlatCtx() {
+        w.reset();
+        if (st) cudaStreamDestroy(st);
+    }
+};
+thread_local FlatCtx g_flat;
+
+FlatCtx& flat_ctx() {
+    int dev = 0;
+    vgpu::check(cudaGetDevice(&dev), "cudaGetDevice");
+    if (g_flat.device != dev) {
+        g_flat.w.reset();
+        if (g_flat.st) cudaStreamDestroy(g_flat.st);
+        g_flat.st = nullptr;
+        g_flat.device = dev;
+        vgpu::check(cudaStreamCreateWithFlags(&g_flat.st, cudaStreamNonBlocking), "cudaStreamCreate");
+        g_flat.w = std::make_unique<vgpu::FlatWork>();
+    }
+    return g_flat;
+}
+
+// Shared body of vesper_flat_topk / _device; the checks mirror the reference's early
+// return (n_base, nq or k == 0 -> nothing written).
+vesper_status_t flat_topk(vesper_flat_op_t op, const float* q, size_t nq, const float* base, size_t nb, size_t dim,
+                          uint32_t k, uint32_t* out_i, float* out_s, bool on_device) {
+    if (op != VESPER_FLAT_L2 && op != VESPER_FLAT_IP) return VESPER_ERROR_INVALID_PARAM;
+    if (nq == 0 || nb == 0 || k == 0) return VESPER_OK;
+    if (!q || !base || !out_i || !out_s || dim == 0) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    if (k > 1024 || dim % 4 != 0 || dim < 32 || dim > (size_t)INT32_MAX || nb > (size_t)INT32_MAX ||
+        nq > (size_t)INT32_MAX) {
+        set_error("flat_topk: unsupported shape (k <= 1024, dim % 4 == 0, dim >= 32, n_base < 2^31)");
+        return VESPER_ERROR_INVALID_PARAM;
+    }
+    return guarded("flat_topk", [&] {
+        FlatCtx& ctx = flat_ctx();
+        cudaStream_t st = ctx.st;
+        vgpu::DeviceBuffer<float> q_own, b_own, s_own;
+        vgpu::DeviceBuffer<uint32_t> i_own;
+        const float* dq = q;
+        const float* db = base;
+        uint32_t* di = out_i;
+        float* ds = out_s;
+        if (!on_device) {
+            q_own.resize(nq * dim);
+            b_own.resize(nb * dim);
+            i_own.resize(nq * k);
+            s_own.resize(nq * k);
+            vgpu::check(cudaMemcpyAsync(q_own.data(), q, nq * dim * sizeof(float), cudaMemcpyHostToDevice, st), "h2d");
+            vgpu::check(cudaMemcpyAsync(b_own.data(), base, nb * dim * sizeof(float), cudaMemcpyHostToDevice, st),
+                        "h2d");
+            dq = q_own.data();
+            db = b_own.data();
+            di = i_own.data();
+            ds = s_own.data();
+        }
+        vgpu::launch_flat_topk(op == VESPER_FLAT_IP, dq, (long long)nq, db, (long long)nb, (int)dim, (int)k, di, ds,
+                               *ctx.w, st);
+        if (!on_device) {
+            vgpu::check(cudaMemcpyAsync(out_i, di, nq * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
+            vgpu::check(cudaMemcpyAsync(out_s, ds, nq * k * sizeof(float), cudaMemcpyDeviceToHost, st), "d2h");
+        }
+        vgpu::check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        return VESPER_OK;
+    });
+}
+}  // namespace
+
+extern "C" {
+
+VESPER_C_API vesper_status_t vesper_flat_topk(vesper_flat_op_t op, const float* queries, size_t nq,
+                                              const float* base, size_t n_base, size_t dim, uint32_t k,
+                                              uint32_t* out_indices, float* out_scores) {
+    return flat_topk(op, queries, nq, base, n_base, dim, k, out_indices, out_scores, false);
+}
+
+VESPER_C_API vesper_status_t vesper_flat_topk_device(vesper_flat_op_t op, const float* d_queries, size_t nq,
+                                                     const float* d_base, size_t n_base, size_t dim, uint32_t k,
+                                                     uint32_t* d_out_indices, float* d_out_scores) {
+    return flat_topk(op, d_queries, nq, d_base, n_base, dim, k, d_out_indices, d_out_scores, true);
+}
+
+VESPER_C_API vesper_status_t vesper_flat_get_last_timings(vesper_flat_timings_t* out) {
+    if (!out) return VESPER_ERROR_INVALID_PARAM;
+    std::memset(out, 0, sizeof(*out));
+    if (!g_flat.w) return VESPER_OK;
+    const vgpu::FlatStats& s = g_flat.w->last;
+    out->total_ms = s.total_ms;
+    out->norms_ms = s.norms_ms;
+    out->sample_ms = s.sample_ms;
+    out->filter_ms = s.filter_ms;
+    out->refine_ms = s.refine_ms;
+    out->fallback_ms = s.fallback_ms;
+    out->candidates = s.candidates;
+    out->overflow_queries = s.overflow_queries;
+    out->sample_stride = (uint32_t)s.sample_stride;
+    out->single_pass = (uint32_t)s.single_pass;
+    return VESPER_OK;
 }
 
 VESPER_C_API int vesper_b200_device_count(void) {
