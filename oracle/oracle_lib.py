@@ -55,6 +55,9 @@ class Oracle:
                                     _u32p, _u8p]
         L.orc_ivfpq_search_batch.argtypes = [_f32p, _sz, _f32p, _u32, _sz, C.c_void_p, _f32p, _u32,
                                              _u32, _u64p, _u64p, _u8p, _u32, _u32, _u64p, _f32p, _u32p]
+        L.orc_ivfpq_search_batch_ex.argtypes = [_f32p, _sz, _f32p, _u32, _sz, C.c_void_p, _f32p, _u32,
+                                                _u32, _u64p, _u64p, _u8p, _u32, _u32, _u32, C.c_int, _u32,
+                                                _u64p, _f32p, _u32p]
         L.orc_flat_topk.argtypes = [C.c_int, _f32p, _sz, _f32p, _u32, _sz, _u32, _u32p, _f32p]
         L.orc_kmeanspp_init.argtypes = [_f32p, _sz, _sz, _u32, _u32, _f32p, _u32p]
         L.orc_lloyd_assign.restype = C.c_float
@@ -141,7 +144,8 @@ class Oracle:
                                None if Rp is None else Rp.ctypes.data, cb, m, ksub, assign, codes)
         return assign, codes
 
-    def ivfpq_search(self, q, c, R, cb, m, list_offsets, ids, codes, k, nprobe):
+    def ivfpq_search(self, q, c, R, cb, m, list_offsets, ids, codes, k, nprobe, cand_k=0, rerank=False,
+                     rerank_k=0):
         q, c, cb = _f32(q), _f32(c), _f32(cb)
         ksub = cb.shape[0] // m
         nq = q.shape[0]
@@ -149,10 +153,11 @@ class Oracle:
         out_d = np.zeros((nq, k), np.float32)
         counts = np.zeros(nq, np.uint32)
         Rp = None if R is None else _f32(R)
-        self.lib.orc_ivfpq_search_batch(
+        self.lib.orc_ivfpq_search_batch_ex(
             q, nq, c, c.shape[0], q.shape[1], None if Rp is None else Rp.ctypes.data, cb, m, ksub,
             np.ascontiguousarray(list_offsets, np.uint64), np.ascontiguousarray(ids, np.uint64),
-            np.ascontiguousarray(codes, np.uint8), k, nprobe, out_ids, out_d, counts)
+            np.ascontiguousarray(codes, np.uint8), k, nprobe, cand_k, int(rerank), rerank_k, out_ids, out_d,
+            counts)
         return out_ids, out_d, counts
 
     def flat_topk(self, op, q, base, k):
@@ -244,6 +249,9 @@ class Reference:
         L.rb_ivfpq_add.argtypes = [C.c_void_p, _u64p, _f32p, _sz]
         L.rb_ivfpq_search_batch.restype = C.c_int
         L.rb_ivfpq_search_batch.argtypes = [C.c_void_p, _f32p, _sz, _u32, _u32, _u64p, _f32p, _u32p]
+        L.rb_ivfpq_search_batch_ex.restype = C.c_int
+        L.rb_ivfpq_search_batch_ex.argtypes = [C.c_void_p, _f32p, _sz, _u32, _u32, _u32, C.c_int, _u32, _u64p,
+                                               _f32p, _u32p]
         L.rb_ivfpq_save.restype = C.c_int
         L.rb_ivfpq_save.argtypes = [C.c_void_p, C.c_char_p]
         L.rb_ivfpq_load.restype = C.c_int
@@ -399,13 +407,17 @@ class RefIvfPq:
         if rc != 0:
             raise ValueError(self.ref.error())
 
-    def search(self, q, k, nprobe):
+    def search(self, q, k, nprobe, cand_k=0, rerank=False, rerank_k=0):
         q = _f32(q)
         nq = q.shape[0]
         ids = np.zeros((nq, k), np.uint64)
         d = np.zeros((nq, k), np.float32)
         counts = np.zeros(nq, np.uint32)
-        rc = self.ref.lib.rb_ivfpq_search_batch(self.h, q, nq, k, nprobe, ids, d, counts)
+        if cand_k or rerank or rerank_k:
+            rc = self.ref.lib.rb_ivfpq_search_batch_ex(self.h, q, nq, k, nprobe, cand_k, int(rerank), rerank_k,
+                                                       ids, d, counts)
+        else:
+            rc = self.ref.lib.rb_ivfpq_search_batch(self.h, q, nq, k, nprobe, ids, d, counts)
         if rc != 0:
             raise ValueError(self.ref.error())
         return ids, d, counts

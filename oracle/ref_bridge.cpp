@@ -100,6 +100,31 @@ int rb_ivfpq_search_batch(void* h, const float* queries, size_t nq, uint32_t k,
     } catch (const std::exception& e) { set_err(e.what()); return 5; }
 }
 
+// The same with the search parameters the C ABI hides (ivf_pq.hpp:109-117): candidate
+// pool cand_k and the opt-in exact rerank of the pool's head (use_exact_rerank,
+// rerank_k).  At most k results per query are copied out.
+int rb_ivfpq_search_batch_ex(void* h, const float* queries, size_t nq, uint32_t k,
+                             uint32_t nprobe, uint32_t cand_k, int use_exact_rerank,
+                             uint32_t rerank_k, uint64_t* out_ids, float* out_d,
+                             uint32_t* out_counts) {
+    IvfPqSearchParams sp; sp.k = k; sp.nprobe = nprobe; sp.cand_k = cand_k;
+    sp.use_exact_rerank = use_exact_rerank != 0; sp.rerank_k = rerank_k;
+    try {
+        auto r = static_cast<RbIndex*>(h)->idx.search_batch(queries, nq, sp);
+        if (!r) { set_err(r.error().message); return 2; }
+        for (size_t q = 0; q < nq; ++q) {
+            const auto& v = (*r)[q];
+            const size_t take = v.size() < k ? v.size() : k;
+            out_counts[q] = static_cast<uint32_t>(take);
+            for (size_t i = 0; i < take; ++i) {
+                out_ids[q * k + i] = v[i].first;
+                out_d[q * k + i] = v[i].second;
+            }
+        }
+        return 0;
+    } catch (const std::exception& e) { set_err(e.what()); return 5; }
+}
+
 int rb_ivfpq_save(void* h, const char* dir) {
     auto r = static_cast<RbIndex*>(h)->idx.save(std::string(dir));
     if (!r) { set_err(r.error().message); return 4; }

@@ -144,16 +144,67 @@ inline float adc_one(const float* lut, const uint8_t* code, uint32_t m, uint32_t
     return d;
 }
 
+// Exact rerank of the head of a search result (src/index/ivf_pq.cpp:3995-4091): each
+// candidate's entry is the first one in list order holding its id; the vector is
+// rebuilt as centroid + apply_rotation_T(decode(code)) (rounded adds), its squared
+// distance to q summed sequentially with rounded products and adds; the head is
+// re-sorted by that distance (std::sort in the reference: order among exact ties is
+// unspecified; stable here) and the result trimmed to k.
+void rerank_one(const float* q, const float* c, size_t dim, const float* R, const float* cb,
+                uint32_t m, uint32_t ksub, uint32_t nlist, const uint64_t* offs, const uint64_t* ids,
+                const uint8_t* codes, size_t head, std::vector<std::pair<uint64_t, float>>& res) {
+    const size_t dsub = dim / m;
+    std::vector<float> rc(dim), ro(dim);
+    for (size_t i = 0; i < head; ++i) {
+        const uint64_t id = res[i].first;
+        uint64_t e = offs[nlist];
+        for (uint64_t j = 0; j < offs[nlist]; ++j)
+            if (ids[j] == id) { e = j; break; }
+        if (e == offs[nlist]) continue;
+        const uint32_t l = static_cast<uint32_t>(std::upper_bound(offs, offs + nlist + 1, e) - offs - 1);
+        for (uint32_t s = 0; s < m; ++s) {
+            const float* cw = cb + (size_t(s) * ksub + codes[e * m + s]) * dsub;
+            std::copy(cw, cw + dsub, rc.begin() + size_t(s) * dsub);
+        }
+        const float* res_v = rc.data();
+        if (R) {
+            // apply_rotation_T (src/index/ivf_pq.cpp:5369-5390)
+            for (size_t j = 0; j < dim; ++j) {
+                float sum = 0.0f;
+                for (size_t t = 0; t < dim; ++t) {
+                    const float p = rc[t] * R[j * dim + t];
+                    sum = sum + p;
+                }
+                ro[j] = sum;
+            }
+            res_v = ro.data();
+        }
+        const float* cl = c + size_t(l) * dim;
+        float dist = 0.0f;
+        for (size_t d = 0; d < dim; ++d) {
+            const float rec = cl[d] + res_v[d];
+            const float diff = q[d] - rec;
+            const float p = diff * diff;
+            dist = dist + p;
+        }
+        res[i].second = dist;
+    }
+    std::stable_sort(res.begin(), res.begin() + head,
+                     [](const auto& a, const auto& b) { return a.second < b.second; });
+}
+
 uint32_t search_one(const float* q, const float* c, uint32_t nlist, size_t dim, const float* R,
                     const float* cb, uint32_t m, uint32_t ksub, const uint64_t* offs,
                     const uint64_t* ids, const uint8_t* codes, uint32_t k, uint32_t nprobe,
-                    uint64_t* out_ids, float* out_d) {
-    // Impl::search (src/index/ivf_pq.cpp:3491-4094) with cand_k=0 and no rerank:
-    // pool_k = k; TopKBuffer for pool_k <= 64, else a max-heap of (dist, id).
+                    uint32_t cand_k, bool rerank, uint32_t rerank_k, uint64_t* out_ids, float* out_d) {
+    // Impl::search (src/index/ivf_pq.cpp:3491-4094).  Candidate pool (:3544-3552):
+    // pool_k = max(k, cand_k or k), with rerank also >= rerank_k or max(3k, 1000);
+    // TopKBuffer for pool_k <= 64, else a max-heap of (dist, id).
     std::vector<std::pair<float, uint32_t>> probe;
     coarse_probe_one(q, c, nlist, dim, nprobe, probe);
     const size_t dsub = dim / m;
-    const size_t pool_k = k;
+    size_t pool_k = std::max<uint32_t>(k, cand_k > 0 ? cand_k : k);
+    if (rerank) pool_k = std::max<size_t>(pool_k, rerank_k > 0 ? rerank_k : std::max<uint32_t>(k * 3, 1000));
     const bool heapless = pool_k <= 64;
     TopKBuffer topk(pool_k);
     std::priority_queue<std::pair<float, uint64_t>> heap;
@@ -183,6 +234,10 @@ uint32_t search_one(const float* q, const float* c, uint32_t nlist, size_t dim, 
     } else {
         while (!heap.empty()) { res.emplace_back(heap.top().second, heap.top().first); heap.pop(); }
         std::reverse(res.begin(), res.end());
+    }
+    if (rerank && !res.empty()) {
+        const size_t head = std::min<size_t>(rerank_k > 0 ? rerank_k : pool_k, res.size());
+        rerank_one(q, c, dim, R, cb, m, ksub, nlist, offs, ids, codes, head, res);
     }
     const uint32_t take = static_cast<uint32_t>(std::min<size_t>(res.size(), k));
     for (uint32_t i = 0; i < take; ++i) { out_ids[i] = res[i].first; out_d[i] = res[i].second; }
@@ -346,8 +401,8 @@ uint32_t orc_ivfpq_search(const float* q, const float* c, uint32_t nlist, size_t
                           const uint64_t* list_offsets, const uint64_t* ids,
                           const uint8_t* codes, uint32_t k, uint32_t nprobe, uint64_t* out_ids,
                           float* out_d) {
-    return search_one(q, c, nlist, dim, R, cb, m, ksub, list_offsets, ids, codes, k, nprobe,
-                      out_ids, out_d);
+    return search_one(q, c, nlist, dim, R, cb, m, ksub, list_offsets, ids, codes, k, nprobe, 0, false,
+                      0, out_ids, out_d);
 }
 
 // Impl::search_batch (src/index/ivf_pq.cpp:4096-4113): independent per-query searches.
@@ -356,10 +411,23 @@ void orc_ivfpq_search_batch(const float* q, size_t nq, const float* c, uint32_t 
                             uint32_t ksub, const uint64_t* list_offsets, const uint64_t* ids,
                             const uint8_t* codes, uint32_t k, uint32_t nprobe, uint64_t* out_ids,
                             float* out_d, uint32_t* out_counts) {
+    orc_ivfpq_search_batch_ex(q, nq, c, nlist, dim, R, cb, m, ksub, list_offsets, ids, codes, k, nprobe, 0, 0,
+                              0, out_ids, out_d, out_counts);
+}
+
+// With the candidate pool and the exact rerank (IvfPqSearchParams::cand_k,
+// use_exact_rerank, rerank_k; include/vesper/index/ivf_pq.hpp:109-117).
+void orc_ivfpq_search_batch_ex(const float* q, size_t nq, const float* c, uint32_t nlist,
+                               size_t dim, const float* R, const float* cb, uint32_t m,
+                               uint32_t ksub, const uint64_t* list_offsets, const uint64_t* ids,
+                               const uint8_t* codes, uint32_t k, uint32_t nprobe, uint32_t cand_k,
+                               int rerank, uint32_t rerank_k, uint64_t* out_ids, float* out_d,
+                               uint32_t* out_counts) {
 #pragma omp parallel for schedule(dynamic, 4)
     for (long long i = 0; i < (long long)nq; ++i)
         out_counts[i] = search_one(q + size_t(i) * dim, c, nlist, dim, R, cb, m, ksub, list_offsets,
-                                   ids, codes, k, nprobe, out_ids + size_t(i) * k, out_d + size_t(i) * k);
+                                   ids, codes, k, nprobe, cand_k, rerank != 0, rerank_k,
+                                   out_ids + size_t(i) * k, out_d + size_t(i) * k);
 }
 
 // find_nearest_centroids_batch_fused (include/vesper/kernels/batch_distances.hpp:338-456):

@@ -49,6 +49,13 @@ void orc_ivfpq_search_batch(const float* q, size_t nq, const float* c, uint32_t 
                             const uint8_t* codes, uint32_t k, uint32_t nprobe, uint64_t* out_ids,
                             float* out_d, uint32_t* out_counts);
 
+void orc_ivfpq_search_batch_ex(const float* q, size_t nq, const float* c, uint32_t nlist,
+                               size_t dim, const float* R, const float* cb, uint32_t m,
+                               uint32_t ksub, const uint64_t* list_offsets, const uint64_t* ids,
+                               const uint8_t* codes, uint32_t k, uint32_t nprobe, uint32_t cand_k,
+                               int rerank, uint32_t rerank_k, uint64_t* out_ids, float* out_d,
+                               uint32_t* out_counts);
+
 void orc_flat_topk(int op, const float* q, size_t nq, const float* base, uint32_t nb,
                    size_t dim, uint32_t k, uint32_t* out_idx, float* out_score);
 

@@ -14,6 +14,8 @@ Outputs (all small, committed):
   ivfpq_<case>.npz      the base vectors and queries used, and the reference's
                         search results for several (k, nprobe)
   kmeans_small.npz      reference k-means++ / Elkan / Lloyd / PQ-train outputs
+  ivfpq_<case>_rerank.npz  the reference's searches with the exact rerank on the saved
+                           indexes (`--rerank-only` regenerates just these)
 """
 from __future__ import annotations
 
@@ -81,6 +83,26 @@ def make_ivfpq(ref: Reference):
         print("wrote", name)
 
 
+# (k, nprobe, cand_k, rerank_k) searches with the exact rerank on
+RERANK_SEARCHES = [(10, 8, 0, 0), (5, 16, 0, 20), (10, 4, 50, 30), (3, 64, 0, 2), (20, 8, 100, 0)]
+
+
+def make_rerank(ref: Reference):
+    """The reference's exact rerank (IvfPqSearchParams::use_exact_rerank) on the saved
+    golden indexes: ivfpq_<case>_rerank.npz."""
+    for (name, *_rest) in CASES:
+        data = np.load(os.path.join(HERE, f"ivfpq_{name}.npz"))
+        idx = ref.ivfpq()
+        idx.load(os.path.join(HERE, f"ivfpq_{name}"))
+        res = {}
+        for k, npb, ck, rk in RERANK_SEARCHES:
+            ids, dist, cnt = idx.search(data["queries"], k, npb, cand_k=ck, rerank=True, rerank_k=rk)
+            tag = f"{k}_{npb}_{ck}_{rk}"
+            res[f"ids_{tag}"], res[f"d_{tag}"], res[f"n_{tag}"] = ids, dist, cnt
+        np.savez_compressed(os.path.join(HERE, f"ivfpq_{name}_rerank.npz"), **res)
+        print("wrote", name, "rerank")
+
+
 def make_kmeans(ref: Reference):
     x = mixture(3000, 16, 60, 0.05, 21)
     kpp = ref.kmeanspp_init(x, 48, 42)
@@ -98,8 +120,11 @@ def make_kmeans(ref: Reference):
 
 
 if __name__ == "__main__":
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    ref_root = args[0] if args else "/root/reference"
     convert_fixtures(ref_root)
     ref = Reference()
-    make_ivfpq(ref)
-    make_kmeans(ref)
+    if "--rerank-only" not in sys.argv:
+        make_ivfpq(ref)
+        make_kmeans(ref)
+    make_rerank(ref)

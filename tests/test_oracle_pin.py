@@ -53,6 +53,26 @@ def test_golden_search(oracle, name):
         assert np.array_equal(d, data[f"d_{k}_{npb}"]), (name, k, npb)
 
 
+RERANK_SEARCHES = [(10, 8, 0, 0), (5, 16, 0, 20), (10, 4, 50, 30), (3, 64, 0, 2), (20, 8, 100, 0)]
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_golden_rerank(oracle, name):
+    """The reference's exact rerank (use_exact_rerank, rerank_k, cand_k) on its own saved
+    index.  The reference re-sorts with std::sort, so the order among exactly equal
+    distances is unspecified: distances must match position by position and the ids
+    everywhere except inside a tie group cut by k."""
+    from conftest import assert_topk_equivalent
+    f, _, data = golden_case(name)
+    rr = np.load(os.path.join(GOLDEN, f"ivfpq_{name}_rerank.npz"))
+    for k, npb, ck, rk in RERANK_SEARCHES:
+        tag = f"{k}_{npb}_{ck}_{rk}"
+        ids, d, cnt = oracle.ivfpq_search(data["queries"], f["centroids"], f["rotation"], f["codebooks"], f["m"],
+                                          f["list_offsets"], f["ids"], f["codes"], k, npb, cand_k=ck, rerank=True,
+                                          rerank_k=rk)
+        assert_topk_equivalent(ids, d, cnt, rr[f"ids_{tag}"], rr[f"d_{tag}"], rr[f"n_{tag}"], 0.0)
+
+
 @pytest.mark.parametrize("name", CASES)
 def test_golden_add(oracle, name):
     """Coarse assignment, list order and PQ codes of the reference's add()."""
