@@ -70,7 +70,14 @@ typedef struct vesper_ivfpq_search_params_ex_s {
   uint32_t k;              /* at most 1024 */
   uint32_t nprobe;         /* clamped to nlist, at most 1024 */
   uint32_t mode;           /* vesper_search_mode_t */
+  /* IvfPqSearchParams (include/vesper/index/ivf_pq.hpp:109-117); read only when
+   * struct_size covers them (callers built against the shorter struct get 0s). */
+  uint32_t cand_k;           /* ADC candidate pool; 0 = k (matters only with the rerank) */
+  uint32_t use_exact_rerank; /* 1: re-score the pool's head exactly (ivf_pq.cpp:3995-4091) */
+  uint32_t rerank_k;         /* head size; 0 = the whole pool of max(k, cand_k, max(3k, 1000)) */
 } vesper_ivfpq_search_params_ex_t;
+/* struct_size of callers that predate cand_k / use_exact_rerank / rerank_k. */
+#define VESPER_IVFPQ_SEARCH_PARAMS_EX_V1_SIZE (sizeof(size_t) + 3 * sizeof(uint32_t))
 
 /* vesper_ivfpq_search_batch with a search mode; out_counts (may be NULL) receives the
  * number of real results per query (the rest of each row is padding). */
@@ -126,6 +133,7 @@ typedef struct vesper_ivfpq_timings_s {
   float list_prep_ms;       /* variant 4: bf16 queries, pair grouping by list, unit table */
   float list_refine_ms;     /* variant 4: exact FAST re-scoring of the kept pairs */
   float list_fallback_ms;   /* variant 4: blocked scan of queries whose candidates overflowed */
+  float rerank_ms;          /* exact rerank of the candidate pool (use_exact_rerank) */
 } vesper_ivfpq_timings_t;
 VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index,
                                                            vesper_ivfpq_timings_t* out);

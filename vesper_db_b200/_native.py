@@ -72,7 +72,8 @@ class TrainReport(C.Structure):
 
 class SearchParamsEx(C.Structure):
     _fields_ = [("struct_size", C.c_size_t), ("k", C.c_uint32), ("nprobe", C.c_uint32),
-                ("mode", C.c_uint32)]
+                ("mode", C.c_uint32), ("cand_k", C.c_uint32), ("use_exact_rerank", C.c_uint32),
+                ("rerank_k", C.c_uint32)]
 
 
 class Timings(C.Structure):
@@ -82,7 +83,8 @@ class Timings(C.Structure):
                 ("scan_variant", C.c_uint32), ("coarse_variant", C.c_uint32),
                 ("list_kernel_ms", C.c_float), ("list_candidates", C.c_uint64),
                 ("list_fallback_queries", C.c_uint32), ("list_threshold_ms", C.c_float),
-                ("list_prep_ms", C.c_float), ("list_refine_ms", C.c_float), ("list_fallback_ms", C.c_float)]
+                ("list_prep_ms", C.c_float), ("list_refine_ms", C.c_float), ("list_fallback_ms", C.c_float),
+                ("rerank_ms", C.c_float)]
 
 
 class KmeansParams(C.Structure):

@@ -146,6 +146,12 @@ public:
     mutable DeviceBuffer<unsigned long long> w_scanned;
     mutable Pinned pin_a, pin_b, pin_c;
     mutable std::unique_ptr<vgpu::KmeansEngine> kme;
+    // Exact rerank: id -> first entry map (rebuilt after the lists change) and scratch.
+    mutable bool id_map_ok = false;
+    mutable DeviceBuffer<uint64_t> d_sid, w_pool_ids;
+    mutable DeviceBuffer<uint32_t> d_sent, w_iota, w_pool_n, w_rr_ent, w_rr_lst;
+    mutable DeviceBuffer<unsigned char> w_cub;
+    mutable DeviceBuffer<float> w_pool_d, w_rr_q, w_rr_dec, w_rr_rot, w_rr_exact;
 
     uint32_t nlist() const { return params.nlist; }
     uint32_t m() const { return params.m; }
@@ -181,6 +187,7 @@ public:
         d_codes.release();
         d_vterm.release();
         n_vectors = 0;
+        id_map_ok = false;
         has_blocks = false;
         d_bcodes.release();
         d_bvterm.release();
@@ -188,6 +195,7 @@ public:
     }
 
     void rebuild_blocks() {
+        id_map_ok = false;
         has_blocks = false;
         d_bcodes.release();
         d_bvterm.release();
@@ -655,6 +663,126 @@ public:
     std::expected<void, error> search_flat(const float* queries, size_t nq, const IvfPqSearchParams& sp,
                                            uint64_t* out_ids, float* out_d, uint32_t* out_n,
                                            bool on_device) const {
+        // VESPER_IVFPQ_RERANK=1 forces the rerank as in the reference (ivf_pq.cpp:3543).
+        if (sp.use_exact_rerank || env_flag("VESPER_IVFPQ_RERANK"))
+            return search_rerank(queries, nq, sp, out_ids, out_d, out_n, on_device);
+        return search_adc(queries, nq, sp, out_ids, out_d, out_n, on_device);
+    }
+
+    // ------------------------------------------------------------------ exact rerank
+    // Impl::search with use_exact_rerank (src/index/ivf_pq.cpp:3544-3552, 3995-4091):
+    // the ADC pool of pool_k = max(k, cand_k or k, rerank_k or max(3k, 1000)) candidates,
+    // then the first min(rerank_k or pool_k, pool size) re-scored exactly and re-sorted.
+    std::expected<void, error> search_rerank(const float* queries, size_t nq, const IvfPqSearchParams& sp,
+                                             uint64_t* out_ids, float* out_d, uint32_t* out_n,
+                                             bool on_device) const {
+        if (!trained) return fail(error_code::precondition_failed, "Index must be trained before searching");
+        if (sp.k == 0) return fail(error_code::invalid_argument, "k must be > 0");
+        if (nq == 0) return {};
+        const uint32_t k = sp.k;
+        size_t pool = std::max<uint32_t>(k, sp.cand_k > 0 ? sp.cand_k : k);
+        pool = std::max<size_t>(pool, sp.rerank_k > 0 ? sp.rerank_k : std::max<uint32_t>(k * 3, 1000));
+        if (pool > (size_t)vgpu::kMaxK)
+            return fail(error_code::unsupported, "the rerank candidate pool (" + std::to_string(pool) +
+                                                     " = max(k, cand_k, rerank_k or max(3k, 1000))) exceeds 1024, "
+                                                     "the GPU path's limit");
+        const int head_cap = sp.rerank_k > 0 ? (int)sp.rerank_k : (int)pool;
+        IvfPqSearchParams ap = sp;
+        ap.k = (uint32_t)pool;
+        ap.cand_k = 0;
+        ap.use_exact_rerank = false;
+        ap.rerank_k = 0;
+        const size_t per_q = has_rot ? 2 * pool * dim * sizeof(float) : 0;
+        size_t qc = std::min<size_t>(nq, 16384);
+        if (per_q) qc = std::min(qc, std::max<size_t>(1, kDistBudget / per_q));
+        SearchTimings acc;
+        float rerank_ms = 0.0f;
+        for (size_t q0 = 0; q0 < nq; q0 += qc) {
+            const size_t nc = std::min(qc, nq - q0);
+            const float* dq = queries + q0 * dim;
+            if (!on_device) {
+                std::lock_guard<std::mutex> lock(mu);
+                w_rr_q.reserve(qc * dim);
+                h2d(w_rr_q.data(), queries + q0 * dim, nc * dim, st);
+                dq = w_rr_q.data();
+            }
+            {
+                std::lock_guard<std::mutex> lock(mu);
+                w_pool_ids.reserve(qc * pool);
+                w_pool_d.reserve(qc * pool);
+                w_pool_n.reserve(qc);
+            }
+            auto r = search_adc(dq, nc, ap, w_pool_ids.data(), w_pool_d.data(), w_pool_n.data(), true);
+            if (!r) return r;
+            std::lock_guard<std::mutex> lock(mu);
+            acc.coarse_ms += timings.coarse_ms; acc.select_ms += timings.select_ms;
+            acc.rotate_ms += timings.rotate_ms; acc.scan_ms += timings.scan_ms; acc.merge_ms += timings.merge_ms;
+            acc.total_ms += timings.total_ms; acc.scanned_entries += timings.scanned_entries;
+            acc.kernel_launches += timings.kernel_launches + 3 + (has_rot ? 1 : 0);
+            acc.scan_variant = timings.scan_variant; acc.coarse_variant = timings.coarse_variant;
+            acc.list_kernel_ms += timings.list_kernel_ms; acc.list_candidates += timings.list_candidates;
+            acc.list_fallback_queries += timings.list_fallback_queries;
+            acc.list_threshold_ms += timings.list_threshold_ms; acc.list_prep_ms += timings.list_prep_ms;
+            acc.list_refine_ms += timings.list_refine_ms; acc.list_fallback_ms += timings.list_fallback_ms;
+            if (!id_map_ok) {
+                d_sid.reserve(std::max<size_t>(n_vectors, 1));
+                d_sent.reserve(std::max<size_t>(n_vectors, 1));
+                vgpu::launch_id_map_build(d_ids.data(), (long long)n_vectors, d_sid.data(), d_sent.data(), w_iota,
+                                          w_cub, st);
+                id_map_ok = true;
+                acc.kernel_launches += 3;
+            }
+            w_rr_ent.reserve(qc * pool);
+            w_rr_lst.reserve(qc * pool);
+            w_rr_exact.reserve(qc * pool);
+            if (has_rot) {
+                w_rr_dec.reserve(qc * pool * dim);
+                w_rr_rot.reserve(qc * pool * dim);
+            }
+            uint64_t* oid = out_ids + q0 * k;
+            float* od = out_d + q0 * k;
+            uint32_t* on = out_n ? out_n + q0 : nullptr;
+            if (!on_device) {
+                w_out_ids.reserve(qc * k);
+                w_out_d.reserve(qc * k);
+                w_out_n.reserve(qc);
+                oid = w_out_ids.data();
+                od = w_out_d.data();
+                on = w_out_n.data();
+            }
+            cudaEventRecord(ev[0], st);
+            vgpu::RerankArgs a{};
+            a.q = dq; a.pool_ids = w_pool_ids.data(); a.pool_d = w_pool_d.data(); a.pool_n = w_pool_n.data();
+            a.nq = (long long)nc; a.P = (int)pool; a.head_cap = head_cap; a.k = (int)k;
+            a.sid = d_sid.data(); a.sent = d_sent.data(); a.n = (long long)n_vectors;
+            a.offs = d_offs.data(); a.nlist = (int)nlist(); a.codes = d_codes.data();
+            a.m = (int)m(); a.ksub = (int)ksub; a.dsub = (int)dsub; a.cb = d_cb.data(); a.cent = d_cent.data();
+            a.rotT = has_rot ? d_rotT.data() : nullptr;
+            a.ent = w_rr_ent.data(); a.lst = w_rr_lst.data();
+            a.dec = has_rot ? w_rr_dec.data() : nullptr; a.rot_out = has_rot ? w_rr_rot.data() : nullptr;
+            a.exact_d = w_rr_exact.data(); a.out_ids = oid; a.out_d = od; a.out_n = on;
+            vgpu::launch_rerank(a, st);
+            cudaEventRecord(ev[1], st);
+            if (!on_device) {
+                d2h(out_ids + q0 * k, oid, nc * k, st);
+                d2h(out_d + q0 * k, od, nc * k, st);
+                if (out_n) d2h(out_n + q0, on, nc, st);
+            }
+            sync(st);
+            float t = 0.0f;
+            cudaEventElapsedTime(&t, ev[0], ev[1]);
+            rerank_ms += t;
+        }
+        std::lock_guard<std::mutex> lock(mu);
+        acc.rerank_ms = rerank_ms;
+        acc.total_ms += rerank_ms;
+        timings = acc;
+        return {};
+    }
+
+    std::expected<void, error> search_adc(const float* queries, size_t nq, const IvfPqSearchParams& sp,
+                                          uint64_t* out_ids, float* out_d, uint32_t* out_n,
+                                          bool on_device) const {
         if (!trained) return fail(error_code::precondition_failed, "Index must be trained before searching");
         if (sp.k == 0) return fail(error_code::invalid_argument, "k must be > 0");
         if (sp.k > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "k above 1024 is not supported by the GPU path");

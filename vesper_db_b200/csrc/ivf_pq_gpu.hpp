@@ -117,6 +117,7 @@ struct SearchTimings {
     float list_prep_ms{0};              // variant 4: bf16 queries, pair grouping, unit table
     float list_refine_ms{0};            // variant 4: exact re-scoring of the kept pairs
     float list_fallback_ms{0};          // variant 4: blocked scan of overflowed queries
+    float rerank_ms{0};                 // exact rerank of the candidate pool (use_exact_rerank)
 };
 
 class IvfPqIndex {

@@ -144,4 +144,38 @@ void launch_segment_mean(const float* x, int dim, const uint32_t* order, const u
 void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,
                         cudaStream_t st);
 
+// ----------------------------------------------------------------------- exact rerank (rerank.cu)
+void launch_iota(uint32_t* out, long long n, cudaStream_t st);
+// sorted_ids / sorted_entry: the ids of the n entries in ascending order with their
+// entry index, equal ids in entry order (id -> first entry holding it).
+void launch_id_map_build(const uint64_t* ids, long long n, uint64_t* sorted_ids, uint32_t* sorted_entry,
+                         DeviceBuffer<uint32_t>& iota, DeviceBuffer<unsigned char>& tmp, cudaStream_t st);
+struct RerankArgs {
+    const float* q;                  // [nq x dim] queries
+    const uint64_t* pool_ids;        // [nq x P] ADC pool, ascending ADC distance
+    const float* pool_d;             // [nq x P]
+    const uint32_t* pool_n;          // [nq] pool sizes
+    long long nq;
+    int P, head_cap, k;              // head = min(pool_n, head_cap) candidates are reranked
+    const uint64_t* sid;             // id map
+    const uint32_t* sent;
+    long long n;
+    const uint64_t* offs;            // [nlist + 1]
+    int nlist;
+    const uint8_t* codes;            // [n x m]
+    int m, ksub, dsub;
+    const float* cb;                 // [m x ksub x dsub]
+    const float* cent;               // [nlist x dim]
+    const float* rotT;               // R transposed, or null without a rotation
+    uint32_t* ent;                   // [nq x P] scratch
+    uint32_t* lst;                   // [nq x P] scratch
+    float* dec;                      // [nq x P x dim] scratch (rotation only)
+    float* rot_out;                  // [nq x P x dim] scratch (rotation only)
+    float* exact_d;                  // [nq x P] scratch
+    uint64_t* out_ids;               // [nq x k]
+    float* out_d;                    // [nq x k]
+    uint32_t* out_n;                 // [nq] or null
+};
+void launch_rerank(const RerankArgs& a, cudaStream_t st);
+
 }  // namespace vgpu

@@ -239,10 +239,25 @@ VESPER_C_API vesper_status_t vesper_ivfpq_add(vesper_index_t* index, const uint6
     });
 }
 
+// The fields of vesper_ivfpq_search_params_ex_t the caller's struct_size covers.
+static IvfPqSearchParams ex_params(const vesper_ivfpq_search_params_ex_t* p) {
+    IvfPqSearchParams sp;
+    sp.k = p->k;
+    sp.nprobe = p->nprobe;
+    sp.mode = p->mode == VESPER_SEARCH_EXACT ? SearchMode::Exact : SearchMode::Fast;
+    if (p->struct_size >= sizeof(vesper_ivfpq_search_params_ex_t)) {
+        sp.cand_k = p->cand_k;
+        sp.use_exact_rerank = p->use_exact_rerank != 0;
+        sp.rerank_k = p->rerank_k;
+    }
+    return sp;
+}
+
 static vesper_status_t do_search(const vesper_index_t* index, const float* q, size_t nq, uint32_t k,
                                  uint32_t nprobe, uint32_t mode, uint64_t* ids, float* d, uint32_t* counts,
-                                 bool on_device) {
+                                 bool on_device, const vesper_ivfpq_search_params_ex_t* ex = nullptr) {
     IvfPqSearchParams sp;
+    if (ex) sp = ex_params(ex);
     sp.k = k;
     sp.nprobe = nprobe;
     sp.mode = mode == VESPER_SEARCH_EXACT ? SearchMode::Exact : SearchMode::Fast;
@@ -280,30 +295,31 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_ex(const vesper_index_t* 
                                                           uint64_t* out_ids, float* out_d, uint32_t* out_counts) {
     if (!index || !index->ivfpq || !queries || !p || !out_ids || !out_d || nq == 0)
         return VESPER_ERROR_INVALID_PARAM;
-    if (p->struct_size < sizeof(vesper_ivfpq_search_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < VESPER_IVFPQ_SEARCH_PARAMS_EX_V1_SIZE) return VESPER_ERROR_INVALID_PARAM;
     clear_error();
-    return do_search(index, queries, nq, p->k, p->nprobe, p->mode, out_ids, out_d, out_counts, false);
+    return do_search(index, queries, nq, p->k, p->nprobe, p->mode, out_ids, out_d, out_counts, false, p);
 }
 
 VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device(const vesper_index_t* index, const float* d_q,
                                                               size_t nq, const vesper_ivfpq_search_params_ex_t* p,
                                                               uint64_t* d_ids, float* d_d, uint32_t* d_counts) {
     if (!index || !index->ivfpq || !d_q || !p || !d_ids || !d_d || nq == 0) return VESPER_ERROR_INVALID_PARAM;
-    if (p->struct_size < sizeof(vesper_ivfpq_search_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < VESPER_IVFPQ_SEARCH_PARAMS_EX_V1_SIZE) return VESPER_ERROR_INVALID_PARAM;
     clear_error();
-    return do_search(index, d_q, nq, p->k, p->nprobe, p->mode, d_ids, d_d, d_counts, true);
+    return do_search(index, d_q, nq, p->k, p->nprobe, p->mode, d_ids, d_d, d_counts, true, p);
 }
 
 VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_noalloc(
     const vesper_index_t* index, const float* d_q, size_t nq, const vesper_ivfpq_search_params_ex_t* p,
     uint64_t* d_ids, float* d_d, uint32_t* d_counts) {
     if (!index || !index->ivfpq || !d_q || !p || !d_ids || !d_d || nq == 0) return VESPER_ERROR_INVALID_PARAM;
-    if (p->struct_size < sizeof(vesper_ivfpq_search_params_ex_t)) return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < VESPER_IVFPQ_SEARCH_PARAMS_EX_V1_SIZE) return VESPER_ERROR_INVALID_PARAM;
     clear_error();
-    IvfPqSearchParams sp;
-    sp.k = p->k;
-    sp.nprobe = p->nprobe;
-    sp.mode = p->mode == VESPER_SEARCH_EXACT ? SearchMode::Exact : SearchMode::Fast;
+    const IvfPqSearchParams sp = ex_params(p);
+    if (sp.use_exact_rerank) {
+        set_error("the allocation-free search does not support the exact rerank");
+        return VESPER_ERROR_INVALID_PARAM;
+    }
     return guarded("search_noalloc", [&] {
         auto r = index->ivfpq->search_batch_device_noalloc(d_q, nq, sp, d_ids, d_d, d_counts);
         if (!r) {
@@ -335,6 +351,7 @@ VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t*
     out->list_prep_ms = t.list_prep_ms;
     out->list_refine_ms = t.list_refine_ms;
     out->list_fallback_ms = t.list_fallback_ms;
+    out->rerank_ms = t.rerank_ms;
     return VESPER_OK;
 }
 

@@ -131,14 +131,17 @@ class IvfPqIndex:
         self._keep = (c, cb, R)
 
     # ------------------------------------------------------------------ search
-    def search_batch(self, queries, k: int, nprobe: int, mode: int = N.SEARCH_FAST):
-        """Returns (ids [nq, k] uint64, distances [nq, k] float32, counts [nq] uint32)."""
+    def search_batch(self, queries, k: int, nprobe: int, mode: int = N.SEARCH_FAST, cand_k: int = 0,
+                     use_exact_rerank: bool = False, rerank_k: int = 0):
+        """Returns (ids [nq, k] uint64, distances [nq, k] float32, counts [nq] uint32).
+        cand_k / use_exact_rerank / rerank_k are IvfPqSearchParams' fields
+        (include/vesper/index/ivf_pq.hpp:109-117)."""
         q = _f32(queries)
         nq = q.shape[0]
         ids = np.zeros((nq, k), np.uint64)
         d = np.zeros((nq, k), np.float32)
         cnt = np.zeros(nq, np.uint32)
-        p = N.SearchParamsEx(C.sizeof(N.SearchParamsEx), k, nprobe, mode)
+        p = N.SearchParamsEx(C.sizeof(N.SearchParamsEx), k, nprobe, mode, cand_k, int(use_exact_rerank), rerank_k)
         _check(self._lib, self._lib.vesper_ivfpq_search_batch_ex(
             self._h, _ptr(q, C.c_float), nq, C.byref(p), _ptr(ids, C.c_uint64), _ptr(d, C.c_float),
             _ptr(cnt, C.c_uint32)))
@@ -165,9 +168,10 @@ class IvfPqIndex:
         return ids, d
 
     def search_batch_device(self, q_ptr: int, nq: int, k: int, nprobe: int, ids_ptr: int, d_ptr: int,
-                            counts_ptr: int = 0, mode: int = N.SEARCH_FAST):
+                            counts_ptr: int = 0, mode: int = N.SEARCH_FAST, cand_k: int = 0,
+                            use_exact_rerank: bool = False, rerank_k: int = 0):
         """Device-resident search: all pointers are device addresses (e.g. torch data_ptr())."""
-        p = N.SearchParamsEx(C.sizeof(N.SearchParamsEx), k, nprobe, mode)
+        p = N.SearchParamsEx(C.sizeof(N.SearchParamsEx), k, nprobe, mode, cand_k, int(use_exact_rerank), rerank_k)
         _check(self._lib, self._lib.vesper_ivfpq_search_batch_device(
             self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(ids_ptr), C.c_void_p(d_ptr),
             C.c_void_p(counts_ptr) if counts_ptr else None))
