@@ -3,9 +3,9 @@
 The GPU path screens every (query, base) pair with tf32 tensor-core products and
 re-scores, in the reference's lane order, every column the proven screening bound cannot
 rule out, so indices and scores must equal the oracle's bit for bit.  Cases: both
-operators; the single-pass path (base <= 65536 rows) and the two-pass path (strided
-sample threshold + filter + refine); k = 1, 10, 100, 300 (the larger kept-column
-capacity); unit-norm 768-d data shaped like the 1M x 768 inner-product workload;
+operators; the single-pass path (base <= 16384 rows) and the two-pass path (threshold
+from a strided sample, itself searched recursively, then filter + refine); k = 1, 10,
+100, 300 and 1024 (the larger kept-column capacity); unit-norm 768-d data shaped like the 1M x 768 inner-product workload;
 exact ties (duplicated rows); lists that overflow their capacity (the single-pass
 fallback); k > n_base (padding); and the device-pointer entry point.
 """
@@ -38,8 +38,8 @@ def _check_equal(op, q, base, k, oracle, single=None):
 
 
 @pytest.mark.parametrize("op", [0, 1])
-@pytest.mark.parametrize("dim,nb,nq,k", [(128, 5000, 200, 10), (40, 3000, 17, 25), (768, 20000, 64, 100),
-                                         (96, 65536, 100, 1)])
+@pytest.mark.parametrize("dim,nb,nq,k", [(128, 5000, 200, 10), (40, 3000, 17, 25), (768, 16000, 64, 100),
+                                         (96, 16384, 100, 1)])
 def test_single_pass(op, dim, nb, nq, k, oracle):
     rng = np.random.default_rng(dim + nb + op)
     base = rng.standard_normal((nb, dim)).astype(np.float32)
@@ -48,7 +48,8 @@ def test_single_pass(op, dim, nb, nq, k, oracle):
 
 
 @pytest.mark.parametrize("op", [0, 1])
-@pytest.mark.parametrize("dim,nb,nq,k", [(128, 200000, 300, 100), (64, 150000, 200, 10), (128, 120000, 80, 300)])
+@pytest.mark.parametrize("dim,nb,nq,k", [(128, 200000, 300, 100), (64, 150000, 200, 10), (128, 120000, 80, 300),
+                                         (96, 65536, 100, 1), (32, 20000, 50, 1024)])
 def test_two_pass(op, dim, nb, nq, k, oracle):
     rng = np.random.default_rng(dim + nb + op + k)
     base = rng.standard_normal((nb, dim)).astype(np.float32)
@@ -79,16 +80,16 @@ def test_ties_go_to_the_smaller_index(op, oracle):
     base = base[perm]
     q = rng.standard_normal((100, 64)).astype(np.float32)
     _check_equal(op, q, base, 50, oracle, single=False)
-    _check_equal(op, q, base[:40000], 50, oracle, single=True)
+    _check_equal(op, q, base[:12000], 50, oracle, single=True)
 
 
 @pytest.mark.parametrize("op", [0, 1])
 def test_overflow_uses_single_pass(op, oracle):
-    """Eight distinct rows repeated 12500 times: every column ties with thousands of
-    others, the kept-column lists overflow, and the single-pass fallback answers."""
+    """Four distinct rows repeated 25000 times: every column ties with 24999 others, the
+    kept-column lists overflow their 4096 slots, and the single-screen fallback answers."""
     rng = np.random.default_rng(3 + op)
-    uniq = rng.standard_normal((8, 32)).astype(np.float32)
-    base = np.tile(uniq, (12500, 1))
+    uniq = rng.standard_normal((4, 32)).astype(np.float32)
+    base = np.tile(uniq, (25000, 1))
     q = rng.standard_normal((6, 32)).astype(np.float32)
     t = _check_equal(op, q, base, 20, oracle, single=False)
     assert t["overflow_queries"] == 6

@@ -4,19 +4,20 @@
 // reference's AVX2 lane order (kernels/backends/avx2.hpp:76-154), ties to the smaller
 // index (:362-369), k_eff = min(k, N).
 //
-// Small bases (N <= 65536): one tf32 tensor-core screen of every (query, base) pair and
+// Small bases (N <= 16384): one tf32 tensor-core screen of every (query, base) pair and
 // the exact band refine of screen_select (the coarse quantizer's path).
 // Larger bases, two passes over tensor-core screens:
-//   1. the screen + exact refine over a strided sample of the base gives each query the
-//      exact k_eff-th best score of the sample, tau -- no worse than the k_eff-th best of
-//      the whole base, so every member of the true top-k scores at least as well as tau;
+//   1. the exact top-k of a strided sample of the base (every 16th row, computed the
+//      same way, recursively) gives each query the exact k_eff-th best score of the
+//      sample, tau -- no worse than the k_eff-th best of the whole base, so every member
+//      of the true top-k scores at least as well as tau;
 //   2. the screen over the whole base keeps the columns whose proven bound can reach tau
 //      (tc_screen_kernel filter modes, column tiles streamed from HBM once), then
 //      flat_refine_kernel takes U* = the k_eff-th smallest upper bound among them,
 //      re-scores exactly every kept column whose lower bound is <= U*, and selects by
 //      (score, index).
-// A query whose kept-column list overflows its capacity is redone by the single-pass
-// path, which handles any number of columns.
+// A query whose kept-column list overflows its capacity is redone by one full screen,
+// which handles any number of columns.
 #include <algorithm>
 #include <cfloat>
 #include <vector>
@@ -29,9 +30,10 @@
 namespace vgpu {
 namespace {
 constexpr int FR_NT = 256;
-constexpr long long FLAT_SINGLE = 65536;        // bases up to this size take the single-pass path
+constexpr long long FLAT_SINGLE = 16384;        // views up to this size take one screen (shared-memory select)
+constexpr long long FLAT_STRIDE = 16;           // sample stride of the threshold pass
 constexpr size_t SCREEN_BUDGET = size_t(512) << 20;  // bytes of screen values per query chunk
-constexpr long long FILTER_ROWS = 16384;        // queries per filter chunk (kept-column lists)
+constexpr long long FILTER_ROWS = 8192;         // queries per filter chunk (kept-column lists)
 constexpr long long FILTER_COLS = 65535LL * 256;  // columns per filter launch (grid.y limit)
 
 // Ordering key: ascending (score, index) for L2, (-score, index) for inner products
@@ -55,17 +57,21 @@ __device__ __forceinline__ float eps_of(float rn, float cn, float dt, int dim) {
 
 // One CTA per query: kept columns -> U* -> exact band -> the k_eff best.  Queries whose
 // list overflowed are recorded in `over` (global row ids) and left to the caller.
+// Shared memory: u64[cap] (the upper-bound keys as u32 first, later the exact keys)
+// and u32[cap] (the band's positions).
 template <bool IP>
 __global__ void __launch_bounds__(FR_NT) flat_refine_kernel(const float* __restrict__ q, const float* __restrict__ base,
-                                                            int dim, const float* __restrict__ xn,
+                                                            long long ld, int dim, const float* __restrict__ xn,
                                                             const float* __restrict__ cn, const uint2* __restrict__ cand,
                                                             const uint32_t* __restrict__ cand_cnt, int cap, int k,
                                                             int ke, long long row0, uint32_t* __restrict__ out_idx,
                                                             float* __restrict__ out_score, uint32_t* __restrict__ over,
                                                             uint32_t* __restrict__ n_over) {
-    extern __shared__ __align__(16) unsigned long long keys[];  // [next_pow2(cap)]
-    uint32_t* band = reinterpret_cast<uint32_t*>(keys + next_pow2(cap));  // [cap]
-    __shared__ uint32_t s_band;
+    extern __shared__ __align__(16) unsigned long long keys[];         // [cap]
+    uint32_t* ukey = reinterpret_cast<uint32_t*>(keys);               // [cap], aliases keys
+    uint32_t* band = reinterpret_cast<uint32_t*>(keys + cap);         // [cap]
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_band, s_rem, s_bin;
     const long long row = blockIdx.x;
     const uint32_t n_all = cand_cnt[row];
     if (n_all > (uint32_t)cap) {
@@ -78,21 +84,49 @@ __global__ void __launch_bounds__(FR_NT) flat_refine_kernel(const float* __restr
     const float rn = xn[row];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // 1) U* = the ke-th smallest upper bound among the kept columns.
-    const int p2 = next_pow2(n < 2 ? 2 : n);
-    for (int i = threadIdx.x; i < p2; i += FR_NT) {
-        unsigned long long key = ~0ull;
-        if (i < n) {
-            const uint2 e = cr[i];
-            const float dt = __uint_as_float(e.y);
-            key = ((unsigned long long)float_key(dt + eps_of<IP>(rn, cn[e.x], dt, dim)) << 32) | (uint32_t)i;
-        }
-        keys[i] = key;
+    // 1) U* = the ke-th smallest upper bound among the kept columns (4-pass radix
+    //    select on order-preserving keys; histogram updates aggregated per warp).
+    for (int i = threadIdx.x; i < n; i += FR_NT) {
+        const uint2 e = cr[i];
+        const float dt = __uint_as_float(e.y);
+        ukey[i] = float_key(dt + eps_of<IP>(rn, cn[e.x], dt, dim));
     }
-    if (threadIdx.x == 0) s_band = 0;
-    bitonic_sort_u64<FR_NT>(keys, p2);
     const bool take_all = n < ke;
-    const float ustar = take_all ? FLT_MAX : key_float((uint32_t)(keys[ke - 1] >> 32));
+    uint32_t prefix = 0, mask = 0;
+    if (threadIdx.x == 0) { s_rem = (uint32_t)ke; s_band = 0; }
+    if (!take_all) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = threadIdx.x; i < 256; i += FR_NT) hist[i] = 0;
+            __syncthreads();
+            for (int i0 = 0; i0 < n; i0 += FR_NT) {
+                const int i = i0 + threadIdx.x;
+                const uint32_t key = i < n ? ukey[i] : 0u;
+                const bool part = i < n && (key & mask) == prefix;
+                const unsigned act = __ballot_sync(0xffffffffu, part);
+                if (act) {
+                    const int lead = __ffs(act) - 1;
+                    const uint32_t bin = (key >> shift) & 255u;
+                    const uint32_t bin0 = __shfl_sync(0xffffffffu, bin, lead);
+                    const unsigned same = __ballot_sync(0xffffffffu, part && bin == bin0);
+                    if (lane == lead) atomicAdd(&hist[bin0], (uint32_t)__popc(same));
+                    if (part && bin != bin0) atomicAdd(&hist[bin], 1u);
+                }
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                uint32_t rem = s_rem, acc = 0, b = 0;
+                for (; b < 256; ++b) { const uint32_t h = hist[b]; if (acc + h >= rem) break; acc += h; }
+                s_rem = rem - acc;
+                s_bin = b;
+            }
+            __syncthreads();
+            prefix |= s_bin << shift;
+            mask |= 255u << shift;
+        }
+    } else {
+        __syncthreads();
+    }
+    const float ustar = take_all ? FLT_MAX : key_float(prefix);
 
     // 2) The band: every kept column whose lower bound is <= U*.
     for (int i0 = 0; i0 < n; i0 += FR_NT) {
@@ -119,7 +153,7 @@ __global__ void __launch_bounds__(FR_NT) flat_refine_kernel(const float* __restr
         const int bi = b0 + (lane >> 3);
         const bool act = bi < nb;
         const uint32_t c = act ? cr[band[bi]].x : 0u;
-        const float* crow = base + (long long)c * dim;
+        const float* crow = base + (long long)c * ld;
         const float v = IP ? warp_ip_group(xr, crow, dim, act) : warp_l2_group(xr, crow, dim, act);
         if (act && (lane & 7) == 0) keys[bi] = order_key<IP>(v, c);
     }
@@ -205,15 +239,136 @@ void exact_rows(bool ip, const float* x, long long nx, const float* xn, const fl
 }
 
 template <bool IP>
-void refine_launch(const float* q, const float* base, int dim, const float* xn, const float* cn, const uint2* cand,
-                   const uint32_t* cnt, int cap, long long nrows, int k, int ke, long long row0, uint32_t* out_idx,
-                   float* out_score, uint32_t* over, uint32_t* n_over, cudaStream_t st) {
-    const size_t smem = (size_t)next_pow2(cap) * 8 + (size_t)cap * 4;
+void refine_launch(const float* q, const float* base, long long ld, int dim, const float* xn, const float* cn,
+                   const uint2* cand, const uint32_t* cnt, int cap, long long nrows, int k, int ke, long long row0,
+                   uint32_t* out_idx, float* out_score, uint32_t* over, uint32_t* n_over, cudaStream_t st) {
+    const size_t smem = (size_t)cap * 12;  // cap is a power of two
     check(cudaFuncSetAttribute(flat_refine_kernel<IP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
           "cudaFuncSetAttribute(flat_refine)");
-    flat_refine_kernel<IP><<<(unsigned)nrows, FR_NT, smem, st>>>(q, base, dim, xn, cn, cand, cnt, cap, k, ke, row0,
-                                                                out_idx, out_score, over, n_over);
+    flat_refine_kernel<IP><<<(unsigned)nrows, FR_NT, smem, st>>>(q, base, ld, dim, xn, cn, cand, cnt, cap, k, ke,
+                                                                row0, out_idx, out_score, over, n_over);
     check(cudaGetLastError(), "flat_refine_kernel");
+}
+
+// A view of the base: row j at base + j * ld, with its squared norms and their roots.
+struct View {
+    const float* base;
+    long long n, ld;
+    const float* cn;
+    const float* cs;
+};
+
+// Exact top-k of every query against the view (indices local to the view).  Views
+// that fit screen_select's shared-memory path take one screen; larger ones get their
+// threshold from the exact top-k of a strided sample of themselves (recursively), then
+// one filtering screen and the refine.  `stats` (top level only) receives stage times.
+void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, const View& v, int k,
+               uint32_t* out_idx, float* out_val, FlatWork& w, int depth, FlatStats* stats, cudaStream_t st) {
+    const int ke = (int)std::min<long long>(k, v.n);
+    if (v.n <= FLAT_SINGLE || depth + 1 >= FlatWork::kLevels) {
+        exact_rows(ip, q, nq, xn, v.base, v.n, v.ld, v.cn, dim, k, out_idx, out_val, w, st);
+        if (stats) stats->single_pass = 1;
+        return;
+    }
+    // The sample's k-th best is about the (k * stride)-th best of the view, so about
+    // k * stride columns survive the filter: stride <= cap / (2k).
+    const int cap = k <= 128 ? 4096 : 16384;
+    long long stride = std::min<long long>(FLAT_STRIDE, std::max(1, cap / (2 * k)));
+    while (stride > 1 && (v.n + stride - 1) / stride < ke) stride >>= 1;
+    if (stride < 2) {
+        exact_rows(ip, q, nq, xn, v.base, v.n, v.ld, v.cn, dim, k, out_idx, out_val, w, st);
+        if (stats) stats->single_pass = 1;
+        return;
+    }
+    FlatWork::Level& L = w.level[depth];
+    const long long ns = (v.n + stride - 1) / stride;
+    L.cn.reserve(ns);
+    L.cs.reserve(ns);
+    L.s_idx.reserve((size_t)nq * k);
+    L.s_val.reserve((size_t)nq * k);
+    gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cn, ns, stride, L.cn.data());
+    check(cudaGetLastError(), "gather_stride_kernel");
+    gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cs, ns, stride, L.cs.data());
+    check(cudaGetLastError(), "gather_stride_kernel");
+    if (stats) check(cudaEventRecord(w.ev[1], st), "event");
+    const View sample{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
+    view_topk(ip, q, nq, xn, dim, sample, k, L.s_idx.data(), L.s_val.data(), w, depth + 1, nullptr, st);
+    w.tau.reserve(nq);
+    flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(L.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
+    check(cudaGetLastError(), "flat_tau_kernel");
+    if (stats) check(cudaEventRecord(w.ev[2], st), "event");
+
+    // filter the whole view, refine the kept columns
+    const long long qc = std::min(nq, FILTER_ROWS);
+    w.cand.reserve((size_t)qc * cap);
+    w.cand_cnt.reserve(nq);
+    w.over.reserve(nq + 1);
+    check(cudaMemsetAsync(w.cand_cnt.data(), 0, (size_t)nq * sizeof(uint32_t), st), "memset");
+    check(cudaMemsetAsync(w.over.data() + nq, 0, sizeof(uint32_t), st), "memset");
+    float filter_ms = 0.0f, refine_ms = 0.0f;
+    for (long long q0 = 0; q0 < nq; q0 += qc) {
+        const long long n = std::min(qc, nq - q0);
+        if (stats) check(cudaEventRecord(w.ev[3], st), "event");
+        for (long long c0 = 0; c0 < v.n; c0 += FILTER_COLS)
+            launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, std::min(FILTER_COLS, v.n - c0), v.ld, dim,
+                             xn + q0, v.cn + c0, v.cs + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(),
+                             w.cand_cnt.data() + q0, cap, w.err.data(), st);
+        if (stats) check(cudaEventRecord(w.ev[4], st), "event");
+        if (ip)
+            refine_launch<true>(q + q0 * dim, v.base, v.ld, dim, xn + q0, v.cn, w.cand.data(), w.cand_cnt.data() + q0,
+                                cap, n, k, ke, q0, out_idx + q0 * k, out_val + q0 * k, w.over.data(),
+                                w.over.data() + nq, st);
+        else
+            refine_launch<false>(q + q0 * dim, v.base, v.ld, dim, xn + q0, v.cn, w.cand.data(),
+                                 w.cand_cnt.data() + q0, cap, n, k, ke, q0, out_idx + q0 * k, out_val + q0 * k,
+                                 w.over.data(), w.over.data() + nq, st);
+        if (stats) {
+            check(cudaEventRecord(w.ev[5], st), "event");
+            check(cudaEventSynchronize(w.ev[5]), "cudaEventSynchronize");
+            float a = 0.0f, b = 0.0f;
+            check(cudaEventElapsedTime(&a, w.ev[3], w.ev[4]), "elapsed");
+            check(cudaEventElapsedTime(&b, w.ev[4], w.ev[5]), "elapsed");
+            filter_ms += a;
+            refine_ms += b;
+        }
+    }
+    uint32_t n_over = 0;
+    check(cudaMemcpyAsync(&n_over, w.over.data() + nq, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
+    std::vector<uint32_t> cnt;
+    if (stats) {
+        cnt.resize((size_t)nq);
+        check(cudaMemcpyAsync(cnt.data(), w.cand_cnt.data(), (size_t)nq * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                              st),
+              "d2h");
+    }
+    check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    if (stats) {
+        for (uint32_t c : cnt) stats->candidates += std::min<uint32_t>(c, (uint32_t)cap);
+        stats->filter_ms = filter_ms;
+        stats->refine_ms = refine_ms;
+        stats->sample_stride = (int)stride;
+        stats->cap = cap;
+        stats->overflow_queries = n_over;
+    }
+    if (n_over) {
+        // one screen over the view for the queries whose lists overflowed
+        w.oq.reserve((size_t)n_over * dim);
+        w.oxn.reserve(n_over);
+        w.o_idx.reserve((size_t)n_over * k);
+        w.o_val.reserve((size_t)n_over * k);
+        w.o_rows.reserve(n_over);
+        check(cudaMemcpyAsync(w.o_rows.data(), w.over.data(), n_over * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st),
+              "d2d");
+        gather_rows_kernel<<<std::min<uint32_t>(n_over, 4096), 256, 0, st>>>(q, xn, w.o_rows.data(), (int)n_over, dim,
+                                                                             w.oq.data(), w.oxn.data());
+        check(cudaGetLastError(), "gather_rows_kernel");
+        exact_rows(ip, w.oq.data(), n_over, w.oxn.data(), v.base, v.n, v.ld, v.cn, dim, k, w.o_idx.data(),
+                   w.o_val.data(), w, st);
+        scatter_rows_kernel<<<std::min<uint32_t>(n_over, 4096), 128, 0, st>>>(w.o_idx.data(), w.o_val.data(),
+                                                                              w.o_rows.data(), (int)n_over, k, out_idx,
+                                                                              out_val);
+        check(cudaGetLastError(), "scatter_rows_kernel");
+    }
 }
 }  // namespace
 
@@ -237,115 +392,40 @@ void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, 
     w.err.reserve(1);
     w.xn.reserve(nq);
     w.cn.reserve(nb);
+    w.csq.reserve(nb);
     check(cudaMemsetAsync(w.err.data(), 0, sizeof(int), st), "memset");
     check(cudaEventRecord(w.ev[0], st), "event");
     launch_row_norms(q, nq, dim, w.xn.data(), st);
     launch_row_norms(base, nb, dim, w.cn.data(), st);
-    uint32_t n_over = 0;
-    if (nb <= FLAT_SINGLE) {
-        check(cudaEventRecord(w.ev[1], st), "event");
-        exact_rows(ip, q, nq, w.xn.data(), base, nb, dim, w.cn.data(), dim, k, out_idx, out_score, w, st);
-        if (k > ke) {
-            pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
-            check(cudaGetLastError(), "pad_topk_kernel");
-        }
-        check(cudaEventRecord(w.ev[2], st), "event");
-        w.last.single_pass = 1;
-    } else {
-        // Capacity of the kept-column lists and sample stride: the sample's k-th best is
-        // about the (k * stride)-th best of the base, so about k * stride columns survive.
-        const int cap = k <= 256 ? 4096 : 16384;
-        long long stride = 16;
-        while (stride > 1 && (long long)k * stride * 4 > cap) stride >>= 1;
-        while (stride > 1 && (nb + stride - 1) / stride < ke) stride >>= 1;
-        const long long ns = (nb + stride - 1) / stride;
-        w.cs.reserve(ns);
-        w.s_idx.reserve((size_t)nq * k);
-        w.s_val.reserve((size_t)nq * k);
-        w.tau.reserve(nq);
-        gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(w.cn.data(), ns, stride, w.cs.data());
-        check(cudaGetLastError(), "gather_stride_kernel");
-        check(cudaEventRecord(w.ev[1], st), "event");
-        // pass 1: exact top-ke of the sample
-        exact_rows(ip, q, nq, w.xn.data(), base, ns, stride * dim, w.cs.data(), dim, k, w.s_idx.data(),
-                   w.s_val.data(), w, st);
-        flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(w.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
-        check(cudaGetLastError(), "flat_tau_kernel");
-        check(cudaEventRecord(w.ev[2], st), "event");
-        // pass 2: filter the whole base, refine the kept columns
-        const long long qc = std::min(nq, FILTER_ROWS);
-        w.cand.reserve((size_t)qc * cap);
-        w.cand_cnt.reserve(nq);
-        w.over.reserve(nq + 1);
-        check(cudaMemsetAsync(w.cand_cnt.data(), 0, (size_t)nq * sizeof(uint32_t), st), "memset");
-        check(cudaMemsetAsync(w.over.data() + nq, 0, sizeof(uint32_t), st), "memset");
-        float filter_ms = 0.0f, refine_ms = 0.0f;
-        for (long long q0 = 0; q0 < nq; q0 += qc) {
-            const long long n = std::min(qc, nq - q0);
-            check(cudaEventRecord(w.ev[3], st), "event");
-            for (long long c0 = 0; c0 < nb; c0 += FILTER_COLS)
-                launch_tc_filter(ip, q + q0 * dim, n, base + c0 * dim, std::min(FILTER_COLS, nb - c0), dim,
-                                 w.xn.data() + q0, w.cn.data() + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(),
-                                 w.cand_cnt.data() + q0, cap, w.err.data(), st);
-            check(cudaEventRecord(w.ev[4], st), "event");
-            if (ip)
-                refine_launch<true>(q + q0 * dim, base, dim, w.xn.data() + q0, w.cn.data(), w.cand.data(),
-                                    w.cand_cnt.data() + q0, cap, n, k, ke, q0, out_idx + q0 * k, out_score + q0 * k,
-                                    w.over.data(), w.over.data() + nq, st);
-            else
-                refine_launch<false>(q + q0 * dim, base, dim, w.xn.data() + q0, w.cn.data(), w.cand.data(),
-                                     w.cand_cnt.data() + q0, cap, n, k, ke, q0, out_idx + q0 * k, out_score + q0 * k,
-                                     w.over.data(), w.over.data() + nq, st);
-            check(cudaEventRecord(w.ev[5], st), "event");
-            check(cudaEventSynchronize(w.ev[5]), "cudaEventSynchronize");
-            float a = 0.0f, b = 0.0f;
-            check(cudaEventElapsedTime(&a, w.ev[3], w.ev[4]), "elapsed");
-            check(cudaEventElapsedTime(&b, w.ev[4], w.ev[5]), "elapsed");
-            filter_ms += a;
-            refine_ms += b;
-        }
-        check(cudaMemcpyAsync(&n_over, w.over.data() + nq, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
-        std::vector<uint32_t> cnt((size_t)nq);
-        check(cudaMemcpyAsync(cnt.data(), w.cand_cnt.data(), (size_t)nq * sizeof(uint32_t), cudaMemcpyDeviceToHost, st),
-              "d2h");
-        check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-        for (uint32_t c : cnt) w.last.candidates += std::min<uint32_t>(c, (uint32_t)cap);
-        w.last.filter_ms = filter_ms;
-        w.last.refine_ms = refine_ms;
-        w.last.sample_stride = (int)stride;
-        w.last.cap = cap;
-        if (n_over) {
-            // the single-pass path for the queries whose lists overflowed
-            w.oq.reserve((size_t)n_over * dim);
-            w.oxn.reserve(n_over);
-            w.o_idx.reserve((size_t)n_over * k);
-            w.o_val.reserve((size_t)n_over * k);
-            gather_rows_kernel<<<std::min<uint32_t>(n_over, 4096), 256, 0, st>>>(q, w.xn.data(), w.over.data(),
-                                                                                 (int)n_over, dim, w.oq.data(),
-                                                                                 w.oxn.data());
-            check(cudaGetLastError(), "gather_rows_kernel");
-            exact_rows(ip, w.oq.data(), n_over, w.oxn.data(), base, nb, dim, w.cn.data(), dim, k, w.o_idx.data(),
-                       w.o_val.data(), w, st);
-            scatter_rows_kernel<<<std::min<uint32_t>(n_over, 4096), 128, 0, st>>>(
-                w.o_idx.data(), w.o_val.data(), w.over.data(), (int)n_over, k, out_idx, out_score);
-            check(cudaGetLastError(), "scatter_rows_kernel");
-        }
+    launch_sqrt(w.cn.data(), nb, w.csq.data(), st);
+    check(cudaEventRecord(w.ev[1], st), "event");
+    check(cudaEventRecord(w.ev[2], st), "event");
+    FlatStats stats;
+    const View v{base, nb, dim, w.cn.data(), w.csq.data()};
+    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st);
+    if (k > ke) {
+        pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
+        check(cudaGetLastError(), "pad_topk_kernel");
     }
     check(cudaEventRecord(w.ev[6], st), "event");
     int e = 0;
     check(cudaMemcpyAsync(&e, w.err.data(), sizeof(int), cudaMemcpyDeviceToHost, st), "d2h");
     check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     if (e) throw CudaError("flat_topk: tensor-core screen wait expired (code " + std::to_string(e) + ")");
-    w.last.overflow_queries = n_over;
     float t = 0.0f;
     check(cudaEventElapsedTime(&t, w.ev[0], w.ev[6]), "elapsed");
-    w.last.total_ms = t;
+    stats.total_ms = t;
     check(cudaEventElapsedTime(&t, w.ev[0], w.ev[1]), "elapsed");
-    w.last.norms_ms = t;
-    check(cudaEventElapsedTime(&t, w.ev[1], w.ev[2]), "elapsed");
-    w.last.sample_ms = t;  // single pass: the whole screen + select
-    w.last.fallback_ms =
-        std::max(0.0f, w.last.total_ms - w.last.norms_ms - w.last.sample_ms - w.last.filter_ms - w.last.refine_ms);
+    stats.norms_ms = t;
+    if (stats.single_pass) {
+        stats.sample_ms = stats.total_ms - stats.norms_ms;  // the whole screen + select
+    } else {
+        check(cudaEventElapsedTime(&t, w.ev[1], w.ev[2]), "elapsed");
+        stats.sample_ms = t;
+        stats.fallback_ms = std::max(0.0f, stats.total_ms - stats.norms_ms - stats.sample_ms - stats.filter_ms -
+                                               stats.refine_ms);
+    }
+    w.last = stats;
 }
 
 }  // namespace vgpu

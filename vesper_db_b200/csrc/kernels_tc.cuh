@@ -21,9 +21,13 @@ void launch_tc_screen_op(bool ip, const float* x, long long nx, const float* c, 
 // to cand[i * cap + ...] as {j + col_off, screen value bits} (count in cand_cnt[i],
 // which may exceed cap) when its lower bound is <= tau[i] (L2: distance; ip: -2 *
 // inner product).
-void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, int dim, const float* xn,
-                      const float* cn, const float* tau, uint32_t col_off, uint2* cand, uint32_t* cand_cnt, int cap,
-                      int* err, cudaStream_t st);
+// cs: sqrt(cn), precomputed.
+// c_stride: row stride of c in elements (0 = dim).
+void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, long long c_stride,
+                      int dim, const float* xn, const float* cn, const float* cs, const float* tau, uint32_t col_off,
+                      uint2* cand, uint32_t* cand_cnt, int cap, int* err, cudaStream_t st);
+// out[i] = sqrt(in[i]).
+void launch_sqrt(const float* in, long long n, float* out, cudaStream_t st);
 // Exact flat top-k (flat_topk.cu).  Stage times of the last call, in ms.
 struct FlatStats {
     float total_ms = 0, norms_ms = 0, sample_ms = 0, filter_ms = 0, refine_ms = 0, fallback_ms = 0;
@@ -32,8 +36,13 @@ struct FlatStats {
     int sample_stride = 0, cap = 0, single_pass = 0;
 };
 struct FlatWork {
-    DeviceBuffer<float> xn, cn, cs, tau, dt, s_val, oq, oxn, o_val;
-    DeviceBuffer<uint32_t> s_idx, cand_cnt, over, o_idx;
+    static constexpr int kLevels = 4;   // sample levels of the threshold recursion
+    struct Level {
+        DeviceBuffer<float> cn, cs, s_val;
+        DeviceBuffer<uint32_t> s_idx;
+    } level[kLevels];
+    DeviceBuffer<float> xn, cn, csq, tau, dt, oq, oxn, o_val;
+    DeviceBuffer<uint32_t> cand_cnt, over, o_idx, o_rows;
     DeviceBuffer<uint2> cand;
     DeviceBuffer<int> err;
     cudaEvent_t ev[7] = {};

@@ -86,7 +86,8 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
                                                            long long ldd, int* __restrict__ err,
                                                            const float* __restrict__ tau,
                                                            uint2* __restrict__ cand, uint32_t* __restrict__ cand_cnt,
-                                                           int cap, uint32_t col_off, int qfast) {
+                                                           int cap, uint32_t col_off, int qfast,
+                                                           const float* __restrict__ cs) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
     uint64_t* accum = empty + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
     __shared__ int s_fail;
+    __shared__ float s_cn[BN], s_cs[BN];  // filter modes: the tile's column norms and their square roots
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // qfast: consecutive CTAs share a column tile (columns streamed from HBM once while
@@ -101,6 +103,13 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
     const int m0 = (qfast ? blockIdx.x : blockIdx.y) * BM, n0 = (qfast ? blockIdx.y : blockIdx.x) * BN;
     const int kt = (dim + BK - 1) / BK;
 
+    if constexpr (MODE >= 2) {
+        for (int j = threadIdx.x; j < BN; j += blockDim.x) {
+            const int col = n0 + j;
+            s_cn[j] = col < nc ? cn[col] : 0.0f;
+            s_cs[j] = col < nc ? cs[col] : 0.0f;
+        }
+    }
     if (threadIdx.x == 0) {
         s_fail = 0;
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -153,11 +162,12 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
     if (s_fail == 0) {
         const int row = m0 + warp * 32 + lane;
         const float rn = row < nx ? xn[row] : 0.0f;
-        for (int ch = 0; ch < BN / 32; ++ch) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(ch * 32), r);
-            if (row < nx) {
-                if constexpr (MODE <= 1) {
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        if constexpr (MODE <= 1) {
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                uint32_t r[32];
+                tmem_ld32(trow + (uint32_t)(ch * 32), r);
+                if (row < nx) {
                     float* out = Dt + (long long)row * ldd + n0 + ch * 32;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -166,29 +176,73 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
                             out[j] = MODE == 0 ? (rn + cn[col]) - 2.0f * __uint_as_float(r[j])
                                                : -2.0f * __uint_as_float(r[j]);
                     }
+                }
+            }
+        } else {
+            // Keep column c when value - eps <= tau (screen_eps / screen_eps_ip with
+            // sqrt(xn * cn) taken as sqrt(xn) * sqrt(cn); the bounds' factor-2 margin
+            // covers the extra rounding), rearranged so that no division or square root
+            // runs per element.  Two passes over the accumulator: keep masks first, then
+            // one slot reservation per row and the appends, so that each row waits for
+            // one returning atomic per tile instead of one per kept column.
+            const float t = row < nx ? tau[row] : -FLT_MAX;
+            const float xs = sqrtf(rn);
+            const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;
+            const float rr = (float)(dim / 8 + 8) * 1.1920929e-7f;
+            // IP: keep iff S >= -t/2 - w sqrt(cn), w = 2 (a + rr + 2.4e-7) sqrt(xn) (+2^-10)
+            const float w_ip = 2.0f * (a + rr + 2.4e-7f) * xs * 1.0009765625f;
+            const float t_ip = -0.5f * t;
+            auto screen_value = [&](float S, int cj) -> float {
+                if constexpr (MODE == 2) return (rn + s_cn[cj]) - 2.0f * S;
+                else return -2.0f * S;
+            };
+            auto keep_of = [&](float S, int cj) -> bool {
+                if constexpr (MODE == 2) {
+                    const float c2 = s_cn[cj];
+                    const float xc = xs * s_cs[cj];
+                    const float dt = (rn + c2) - 2.0f * S;
+                    const float e = 4.0f * a * xc + 4.768e-7f * (rn + c2 + 2.0f * xc) + 2.0f * rr * fabsf(dt);
+                    return dt - 1.0009765625f * e <= t;
                 } else {
-                    const float t = tau[row];
+                    return S >= fmaf(-w_ip, s_cs[cj], t_ip);
+                }
+            };
+            uint32_t mask[BN / 32];
+            uint32_t total = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int col = n0 + ch * 32 + j;
-                        if (col < nc) {
-                            const float c2 = cn[col];
-                            float dt, e;
-                            if constexpr (MODE == 2) {
-                                dt = (rn + c2) - 2.0f * __uint_as_float(r[j]);
-                                e = screen_eps(rn, c2, dt, dim);
-                            } else {
-                                dt = -2.0f * __uint_as_float(r[j]);
-                                e = screen_eps_ip(rn, c2, dim);
-                            }
-                            if (dt - e <= t) {
-                                const uint32_t slot = atomicAdd(&cand_cnt[row], 1u);
-                                if (slot < (uint32_t)cap)
-                                    cand[(long long)row * cap + slot] = make_uint2((uint32_t)col + col_off,
-                                                                                   __float_as_uint(dt));
-                            }
-                        }
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                uint32_t r[32];
+                tmem_ld32(trow + (uint32_t)(ch * 32), r);
+                uint32_t mk = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int cj = ch * 32 + j;
+                    if (keep_of(__uint_as_float(r[j]), cj) && n0 + cj < nc) mk |= 1u << j;
+                }
+                mask[ch] = row < nx ? mk : 0u;
+                total += __popc(mask[ch]);
+            }
+            uint32_t slot = 0;
+            if (total) slot = atomicAdd(&cand_cnt[row], total);
+            uint2* dst = cand + (long long)row * cap;
+#pragma unroll
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                if (!__any_sync(0xffffffffu, mask[ch] != 0u)) continue;
+                uint32_t r[32];
+                tmem_ld32(trow + (uint32_t)(ch * 32), r);
+                uint32_t mk = mask[ch];
+                while (mk) {
+                    const int j = __ffs(mk) - 1;
+                    mk &= mk - 1u;
+                    const int cj = ch * 32 + j;
+                    if (slot < (uint32_t)cap) {
+                        // r[] is indexed by a run-time j here; pick it with a small select
+                        float S = 0.0f;
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) S = (u == j) ? __uint_as_float(r[u]) : S;
+                        dst[slot] = make_uint2((uint32_t)(n0 + cj) + col_off, __float_as_uint(screen_value(S, cj)));
                     }
+                    ++slot;
                 }
             }
         }
@@ -259,7 +313,8 @@ namespace {
 template <int MODE>
 void tc_screen_launch(const float* x, long long nx, const float* c, long long nc, long long c_stride, int dim,
                       const float* xn, const float* cn, float* Dt, long long ldd, int* err, const float* tau,
-                      uint2* cand, uint32_t* cand_cnt, int cap, uint32_t col_off, cudaStream_t st) {
+                      uint2* cand, uint32_t* cand_cnt, int cap, uint32_t col_off, cudaStream_t st,
+                      const float* cs = nullptr) {
     if (nx <= 0 || nc <= 0) return;
     if (!tc_screen_supported(dim)) throw CudaError("tc_screen: dim must be a multiple of 4 and >= 32");
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
@@ -276,7 +331,7 @@ void tc_screen_launch(const float* x, long long nx, const float* c, long long nc
     dim3 grid = qfast ? dim3((unsigned)ceil_div(nx, BM), (unsigned)ceil_div(nc, BN))
                       : dim3((unsigned)ceil_div(nc, BN), (unsigned)ceil_div(nx, BM));
     tc_screen_kernel<MODE><<<grid, 128, SMEM_BYTES, st>>>(mx, mc, (int)nx, (int)nc, dim, xn, cn, Dt, ldd, err, tau,
-                                                          cand, cand_cnt, cap, col_off, qfast);
+                                                          cand, cand_cnt, cap, col_off, qfast, cs);
     check(cudaGetLastError(), "tc_screen_kernel");
 }
 }  // namespace
@@ -295,11 +350,27 @@ void launch_tc_screen_op(bool ip, const float* x, long long nx, const float* c, 
         tc_screen_launch<0>(x, nx, c, nc, c_stride, dim, xn, cn, Dt, ldd, err, nullptr, nullptr, nullptr, 0, 0, st);
 }
 
-void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, int dim, const float* xn,
-                      const float* cn, const float* tau, uint32_t col_off, uint2* cand, uint32_t* cand_cnt, int cap,
-                      int* err, cudaStream_t st) {
-    if (ip) tc_screen_launch<3>(x, nx, c, nc, 0, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off, st);
-    else tc_screen_launch<2>(x, nx, c, nc, 0, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off, st);
+void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, long long c_stride,
+                      int dim, const float* xn, const float* cn, const float* cs, const float* tau, uint32_t col_off,
+                      uint2* cand, uint32_t* cand_cnt, int cap, int* err, cudaStream_t st) {
+    if (ip)
+        tc_screen_launch<3>(x, nx, c, nc, c_stride, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off,
+                            st, cs);
+    else
+        tc_screen_launch<2>(x, nx, c, nc, c_stride, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off,
+                            st, cs);
+}
+
+__global__ void sqrt_kernel(const float* __restrict__ in, long long n, float* __restrict__ out) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = sqrtf(in[i]);
+}
+
+void launch_sqrt(const float* in, long long n, float* out, cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+    sqrt_kernel<<<blocks, 256, 0, st>>>(in, n, out);
+    check(cudaGetLastError(), "sqrt_kernel");
 }
 
 // ---------------------------------------------------------------------------------
