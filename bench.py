@@ -1,5 +1,8 @@
 """Benchmark: IVF-PQ search QPS at matched recall@10, 10k-query batch (B200).
 
+(`--workload flat` measures the exact flat top-k instead: 1M x 768 unit vectors, inner
+product, k = 100, 10k queries; see main_flat.)
+
 Workload (the IVF-PQ configuration with a 10k-query batch): N = 10,000,000 base vectors,
 d = 768 fp32, from a seeded mixture of 50,000 anisotropic Gaussians (centres ~U[-1,1],
 per-centre per-dim sigma ~U[0.01, 0.2]); OPQ rotation 768x768; nlist = 16,384;
@@ -57,6 +60,7 @@ SCAN_KERNELS = {1: "scan_exact_kernel", 2: "scan_fast2_kernel", 3: "scan_blocked
                 4: "tc_list_scan_kernel"}
 COARSE_KERNELS = {1: "l2_dist_kernel (CUDA cores)", 2: "tc_screen_kernel (tcgen05 tf32) + screen_select_kernel"}
 METRIC = "QPS at matched recall@10 (IVF-PQ, 10k-query batch) at 1/2/4/8 B200 vs CPU ref"
+LIST_SCAN_BYTES_PER_PAIR = (662.9e6 + 8.7e6) / 6.65e9   # ncu, main-pass launch on the 4M-vector case
 WORKLOAD = ("IVF-PQ+OPQ search: N=10,000,000 x d=768 fp32 (mixture of 50,000 anisotropic Gaussians, "
             "sigma~U[0.01,0.2]), nlist=16384, m=96x8 bits, OPQ 768x768, 10,000 queries, k=10, L2, nprobe=32")
 
@@ -69,6 +73,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "flat"],
+                    help="ivfpq: the IVF-PQ+OPQ search (default); flat: exact flat top-k, 1M x 768 IP, k=100")
     return ap.parse_args()
 
 
@@ -193,9 +199,223 @@ def reference_cpu_search(index_dir, queries_np, nprobe, seconds):
             "ids": np.concatenate(ids_all), "cores": os.cpu_count()}
 
 
+# ------------------------------------------------------------------------------- flat top-k
+FLAT_N, FLAT_NQ, FLAT_K, FLAT_CHUNK = 1_000_000, 10_000, 100, 125_000
+FLAT_FILTER_BYTES_PER_ROW = (929.28e6 + 39.77e6) / 300_000   # ncu, filter launch over a 300k-row base
+FLAT_METRIC = "QPS, exact flat top-k (inner product, k=100), 10k-query batch"
+FLAT_WORKLOAD = ("Exact brute-force k-NN (flat index): N=1,000,000 x d=768 fp32 ~N(0,1) then L2-normalised, "
+                 "10,000 queries from the same distribution, inner product, k=100")
+
+
+def flat_rows(torch, dev, n, seed, out=None):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn((n, DIM), device=dev, generator=g, out=out)
+    x /= x.norm(dim=1, keepdim=True)
+    return x
+
+
+def reference_flat(base_np, q_np, seconds, batch=8):
+    """Time the reference's find_nearest_centroids_batch_fused (OpenMP over all host
+    threads) on query batches until `seconds` of search have run; the base sits in the
+    reference's AlignedCentroidBuffer (filled once, untimed)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle_lib import REF_SO, Reference
+    fb = Reference(REF_SO).flat_buffer(base_np)
+    fb.topk(1, q_np[:2], FLAT_K)  # warm-up
+    done, el, ids, scores = 0, 0.0, [], []
+    while done < q_np.shape[0] and (el < seconds or done == 0):
+        qb = q_np[done:done + batch]
+        t = time.perf_counter()
+        i, sc = fb.topk(1, qb, FLAT_K)
+        el += time.perf_counter() - t
+        ids.append(i)
+        scores.append(sc)
+        done += qb.shape[0]
+    import numpy as np
+    return done / el, done, el, np.concatenate(ids), np.concatenate(scores)
+
+
+def main_flat(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 and args.impl == "ours":
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    shard_world = world if args.impl == "ours" else 1
+    from vesper_db_b200.shard import chunks_of, merge_topk
+    my_chunks = chunks_of(rank if args.impl == "ours" else 0, shard_world, FLAT_N // FLAT_CHUNK)
+    n_local = len(my_chunks) * FLAT_CHUNK
+    base = torch.empty((n_local, DIM), device=dev)
+    for j, c in enumerate(my_chunks):
+        flat_rows(torch, dev, FLAT_CHUNK, 7000 + c, out=base[j * FLAT_CHUNK:(j + 1) * FLAT_CHUNK])
+    queries = flat_rows(torch, dev, FLAT_NQ, 6999)
+    torch.cuda.synchronize()
+    q_np = queries.cpu().numpy()
+    peaks, peak_kind = measured_peaks()
+    cfg = {"workload": FLAT_WORKLOAD, "n_base": FLAT_N, "nq": FLAT_NQ, "k": FLAT_K, "op": "inner_product",
+           "parallelism": f"vector-sharded x{world}" if world > 1 else "single GPU",
+           "l2_policy": "inputs larger than L2 (3.07 GB base streamed per pass)"}
+    if args.impl == "reference":
+        per = max(1.0, args.cpu_seconds / max(1, args.steps))
+        base_np = base.cpu().numpy()
+        vals, nq_done = [], 0
+        for s in range(args.warmup + args.steps):
+            v, n, el, _, _ = reference_flat(base_np, q_np[(s * 64) % FLAT_NQ:], per)
+            if s >= args.warmup:
+                vals.append(v)
+                nq_done += n
+        v = sorted(vals)[len(vals) // 2]
+        print(json.dumps({"impl": "reference", "metric": FLAT_METRIC, "value": v, "unit": "queries/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": 1e3 * FLAT_NQ / v, "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), normalised)",
+                          "config": cfg,
+                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": os.cpu_count(),
+                                           "kind": "reference",
+                                           "sample": f"{nq_done} queries over {args.steps} steps (~{per:.0f} s "
+                                                     f"each), OpenMP over all host threads"},
+                          "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return 0
+
+    from vesper_db_b200 import flat_topk_device
+    from vesper_db_b200.flat import last_timings
+    import ctypes as C
+    from vesper_db_b200 import _native as N
+    out_i = torch.empty((FLAT_NQ, FLAT_K), dtype=torch.int32, device=dev)
+    out_s = torch.empty((FLAT_NQ, FLAT_K), dtype=torch.float32, device=dev)
+    chunk0 = torch.tensor([my_chunks[j] * FLAT_CHUNK for j in range(len(my_chunks))], device=dev)
+
+    def one_step():
+        flat_topk_device(1, queries.data_ptr(), FLAT_NQ, base.data_ptr(), n_local, DIM, FLAT_K, out_i.data_ptr(),
+                         out_s.data_ptr())
+        if world > 1:
+            # local row -> global id, then the merge (scores negated: merge_topk keeps smallest)
+            loc = out_i.long()
+            gid = chunk0[loc // FLAT_CHUNK] + loc % FLAT_CHUNK
+            d, i = merge_topk(-out_s, gid, FLAT_K)
+            return -d, i
+        return out_s, out_i.long()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        one_step()
+    barrier()
+    filt, stages, launches = [], [], 0
+    with ClockSampler(local) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        ev0.record()
+        for _ in range(args.steps):
+            res_s, res_i = one_step()
+            t = last_timings()
+            filt.append(t["filter_ms"])
+            stages.append(t)
+            launches += t["kernel_launches"]
+        ev1.record()
+        barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    if world > 1:
+        tt = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_total = float(tt.item())
+    qps = FLAT_NQ * args.steps / (ms_total / 1e3)
+
+    # e2e: vesper_flat_topk with host buffers (queries and base copied in, results out)
+    lib = N.load()
+    base_h = torch.empty((n_local, DIM), dtype=torch.float32, pin_memory=True)
+    base_h.copy_(base)
+    q_h = torch.empty((FLAT_NQ, DIM), dtype=torch.float32, pin_memory=True)
+    q_h.copy_(queries)
+    i_h = torch.empty((FLAT_NQ, FLAT_K), dtype=torch.int32, pin_memory=True)
+    s_h = torch.empty((FLAT_NQ, FLAT_K), dtype=torch.float32, pin_memory=True)
+    f32p, u32p = C.POINTER(C.c_float), C.POINTER(C.c_uint32)
+    e2e = []
+    for s in range(args.warmup + args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record()
+        st = lib.vesper_flat_topk(1, C.cast(q_h.data_ptr(), f32p), FLAT_NQ, C.cast(base_h.data_ptr(), f32p),
+                                  n_local, DIM, FLAT_K, C.cast(i_h.data_ptr(), u32p), C.cast(s_h.data_ptr(), f32p))
+        if st != 0:
+            raise RuntimeError(lib.vesper_get_last_error().decode())
+        e1.record()
+        barrier()
+        if s >= args.warmup:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_ms = sum(e2e) / len(e2e)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+
+    fk = sum(filt) / len(filt)
+    flop_launches = 2.0 * n_local * DIM * FLAT_NQ
+    achieved = flop_launches / (fk / 1e3) / 1e12
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    avg = {k2: sum(t[k2] for t in stages) / len(stages) for k2 in stages[0] if k2.endswith("_ms")}
+    out = {
+        "metric": FLAT_METRIC, "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), L2-normalised, generated on device)",
+        "config": cfg,
+        "e2e": {"value": FLAT_NQ / (e2e_ms / 1e3), "unit": "queries/s",
+                "h2d_bytes_per_step": (n_local + FLAT_NQ) * DIM * 4, "d2h_bytes_per_step": FLAT_NQ * FLAT_K * 8,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "tc_screen_kernel filter mode (tcgen05 kind::tf32)",
+                     "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
+                     "peak_source": f"{peak_kind} bf16 dense burst / 2 (tf32 dense rate)",
+                     # DRAM bytes of one filter launch, from the ncu capture in
+                     # profiles/tc_screen_kernel_filter_300kx768_nq2048.md (969 MB for a 300,000-row
+                     # base), scaled by base rows: the base is streamed once per launch.
+                     "traffic": FLAT_FILTER_BYTES_PER_ROW * n_local,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 300k-row case, "
+                                       "scaled by base rows (one level-0 filter launch per step)",
+                     "algorithmic_flop_per_step": flop_launches, "kernel_ms_per_step": fk},
+        "stage_ms": avg,
+        "candidates_per_query": stages[-1]["candidates"] / FLAT_NQ,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            base_np = base.cpu().numpy()
+            v, n, el, rid, rsc = reference_flat(base_np, q_np, args.cpu_seconds)
+            gi = res_i[:n].cpu().numpy().astype(np.uint32)
+            gs = res_s[:n].cpu().numpy()
+            out["cpu_baseline"] = {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",
+                                   "sample": f"first {n} queries of the batch ({el:.1f} s of search), "
+                                             f"find_nearest_centroids_batch_fused, OpenMP over all host threads"}
+            out["parity_vs_reference"] = {"queries": int(n), "indices_equal": bool(np.array_equal(gi, rid)),
+                                          "scores_equal": bool(np.array_equal(gs, rsc))}
+        except Exception as e:
+            out["cpu_baseline"] = {"value": None, "unit": "queries/s", "cores": os.cpu_count(),
+                                   "kind": "reference", "sample": f"unavailable: {e}"}
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # ------------------------------------------------------------------------------- main
 def main():
     args = parse()
+    if args.workload == "flat":
+        return main_flat(args)
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -405,7 +625,13 @@ def main():
         roofline = {"bound": "tensor", "kernel": "tc_list_scan_kernel (tcgen05 kind::f16, bf16, A in TMEM)",
                     "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                     "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} (bf16 dense, burst)",
-                    "traffic": None, "algorithmic_flop_per_search": flop, "kernel_ms_per_search": lk,
+                    # DRAM bytes per launch: profiles/tc_list_scan_kernel_4Mx768_nq8192.md measured
+                    # 671.6 MB for 6.65e9 (query, entry) pairs on the 4M-vector case; scaled by the
+                    # pairs of one launch here (codes of each probed tile are read once per batch).
+                    "traffic": LIST_SCAN_BYTES_PER_PAIR * entries / -(-NQ // QUERY_CHUNK),
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4M-vector case, "
+                                      "scaled by (query, entry) pairs per launch",
+                    "algorithmic_flop_per_search": flop, "kernel_ms_per_search": lk,
                     "launches_per_search": -(-NQ // QUERY_CHUNK),
                     "scan_stage_ms": scan_avg,
                     "scan_stage_code_GBps": code_bytes / (scan_avg / 1e3) / 1e9,

@@ -222,6 +222,7 @@ typedef struct vesper_flat_timings_s {
   uint32_t overflow_queries;
   uint32_t sample_stride;
   uint32_t single_pass;    /* 1: base small enough for one screen + select */
+  uint32_t kernel_launches; /* kernels the call launched */
 } vesper_flat_timings_t;
 
 /* queries [nq x dim], base [n_base x dim] host; outputs [nq x k] host. */

@@ -249,6 +249,10 @@ class Reference:
         L.rb_ivfpq_add.argtypes = [C.c_void_p, _u64p, _f32p, _sz]
         L.rb_ivfpq_search_batch.restype = C.c_int
         L.rb_ivfpq_search_batch.argtypes = [C.c_void_p, _f32p, _sz, _u32, _u32, _u64p, _f32p, _u32p]
+        L.rb_flat_buffer_create.restype = C.c_void_p
+        L.rb_flat_buffer_create.argtypes = [_f32p, _u32, _sz]
+        L.rb_flat_buffer_destroy.argtypes = [C.c_void_p]
+        L.rb_flat_topk_buffer.argtypes = [C.c_int, _f32p, _sz, C.c_void_p, _u32, _u32p, _f32p]
         L.rb_ivfpq_search_batch_ex.restype = C.c_int
         L.rb_ivfpq_search_batch_ex.argtypes = [C.c_void_p, _f32p, _sz, _u32, _u32, _u32, C.c_int, _u32, _u64p,
                                                _f32p, _u32p]
@@ -330,11 +334,35 @@ class Reference:
         self.lib.rb_flat_topk(op, q, q.shape[0], base, base.shape[0], q.shape[1], k, idx, sc)
         return idx, sc
 
+    def flat_buffer(self, base):
+        """The base copied once into the reference's AlignedCentroidBuffer; returns an
+        object whose topk(op, q, k) runs find_nearest_centroids_batch_fused on it."""
+        return RefFlatBuffer(self, base)
+
     def pq(self, m, nbits):
         return RefPq(self, m, nbits)
 
     def ivfpq(self):
         return RefIvfPq(self)
+
+
+class RefFlatBuffer:
+    def __init__(self, ref: Reference, base):
+        base = _f32(base)
+        self.ref, self.nb = ref, base.shape[0]
+        self.h = ref.lib.rb_flat_buffer_create(base, base.shape[0], base.shape[1])
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.rb_flat_buffer_destroy(self.h)
+            self.h = None
+
+    def topk(self, op, q, k):
+        q = _f32(q)
+        idx = np.zeros((q.shape[0], k), np.uint32)
+        sc = np.zeros((q.shape[0], k), np.float32)
+        self.ref.lib.rb_flat_topk_buffer(op, q, q.shape[0], self.h, k, idx, sc)
+        return idx, sc
 
 
 class RefPq:

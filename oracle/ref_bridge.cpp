@@ -251,4 +251,19 @@ void rb_flat_topk(int op, const float* queries, size_t nq, const float* base, ui
         k, out_idx, out_score);
 }
 
+// The same search over a base held in the reference's AlignedCentroidBuffer across
+// calls (the copy into it is not part of a timed search).
+void* rb_flat_buffer_create(const float* base, uint32_t nb, size_t dim) {
+    auto* buf = new AlignedCentroidBuffer(nb, dim);
+    for (uint32_t i = 0; i < nb; ++i) std::memcpy((*buf)[i], base + (size_t)i * dim, dim * 4);
+    return buf;
+}
+void rb_flat_buffer_destroy(void* h) { delete static_cast<AlignedCentroidBuffer*>(h); }
+void rb_flat_topk_buffer(int op, const float* queries, size_t nq, void* h, uint32_t k, uint32_t* out_idx,
+                         float* out_score) {
+    kernels::find_nearest_centroids_batch_fused(
+        op == 0 ? kernels::DistanceOp::L2 : kernels::DistanceOp::InnerProduct, queries, nq,
+        *static_cast<AlignedCentroidBuffer*>(h), k, out_idx, out_score);
+}
+
 }  // extern "C"

@@ -100,7 +100,7 @@ class FlatTimings(C.Structure):
     _fields_ = [("total_ms", C.c_float), ("norms_ms", C.c_float), ("sample_ms", C.c_float),
                 ("filter_ms", C.c_float), ("refine_ms", C.c_float), ("fallback_ms", C.c_float),
                 ("candidates", C.c_uint64), ("overflow_queries", C.c_uint32), ("sample_stride", C.c_uint32),
-                ("single_pass", C.c_uint32)]
+                ("single_pass", C.c_uint32), ("kernel_launches", C.c_uint32)]
 
 
 _lib = None

@@ -33,7 +33,7 @@ constexpr int FR_NT = 256;
 constexpr long long FLAT_SINGLE = 16384;        // views up to this size take one screen (shared-memory select)
 constexpr long long FLAT_STRIDE = 16;           // sample stride of the threshold pass
 constexpr size_t SCREEN_BUDGET = size_t(512) << 20;  // bytes of screen values per query chunk
-constexpr long long FILTER_ROWS = 8192;         // queries per filter chunk (kept-column lists)
+constexpr size_t CAND_BUDGET = size_t(1) << 30;  // bytes of kept-column lists per filter chunk
 constexpr long long FILTER_COLS = 65535LL * 256;  // columns per filter launch (grid.y limit)
 
 // Ordering key: ascending (score, index) for L2, (-score, index) for inner products
@@ -235,6 +235,7 @@ void exact_rows(bool ip, const float* x, long long nx, const float* xn, const fl
         launch_tc_screen_op(ip, x + q0 * dim, n, c, nc, c_ld, dim, xn + q0, cn, w.dt.data(), nc, w.err.data(), st);
         launch_screen_select_op(ip, w.dt.data(), n, nc, (int)nc, x + q0 * dim, dim, c, c_ld, xn + q0, cn, k,
                                 out_idx + q0 * k, out_val + q0 * k, w.err.data(), st);
+        w.launches += 2;
     }
 }
 
@@ -249,6 +250,7 @@ void refine_launch(const float* q, const float* base, long long ld, int dim, con
                                                                 row0, out_idx, out_score, over, n_over);
     check(cudaGetLastError(), "flat_refine_kernel");
 }
+
 
 // A view of the base: row j at base + j * ld, with its squared norms and their roots.
 struct View {
@@ -290,16 +292,18 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     check(cudaGetLastError(), "gather_stride_kernel");
     gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cs, ns, stride, L.cs.data());
     check(cudaGetLastError(), "gather_stride_kernel");
+    w.launches += 2;
     if (stats) check(cudaEventRecord(w.ev[1], st), "event");
     const View sample{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
     view_topk(ip, q, nq, xn, dim, sample, k, L.s_idx.data(), L.s_val.data(), w, depth + 1, nullptr, st);
     w.tau.reserve(nq);
     flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(L.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
     check(cudaGetLastError(), "flat_tau_kernel");
+    ++w.launches;
     if (stats) check(cudaEventRecord(w.ev[2], st), "event");
 
     // filter the whole view, refine the kept columns
-    const long long qc = std::min(nq, FILTER_ROWS);
+    const long long qc = std::min<long long>(nq, (long long)(CAND_BUDGET / ((size_t)cap * sizeof(uint2))));
     w.cand.reserve((size_t)qc * cap);
     w.cand_cnt.reserve(nq);
     w.over.reserve(nq + 1);
@@ -309,11 +313,12 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     for (long long q0 = 0; q0 < nq; q0 += qc) {
         const long long n = std::min(qc, nq - q0);
         if (stats) check(cudaEventRecord(w.ev[3], st), "event");
-        for (long long c0 = 0; c0 < v.n; c0 += FILTER_COLS)
+        for (long long c0 = 0; c0 < v.n; c0 += FILTER_COLS, ++w.launches)
             launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, std::min(FILTER_COLS, v.n - c0), v.ld, dim,
                              xn + q0, v.cn + c0, v.cs + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(),
                              w.cand_cnt.data() + q0, cap, w.err.data(), st);
         if (stats) check(cudaEventRecord(w.ev[4], st), "event");
+        ++w.launches;
         if (ip)
             refine_launch<true>(q + q0 * dim, v.base, v.ld, dim, xn + q0, v.cn, w.cand.data(), w.cand_cnt.data() + q0,
                                 cap, n, k, ke, q0, out_idx + q0 * k, out_val + q0 * k, w.over.data(),
@@ -368,6 +373,7 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
                                                                               w.o_rows.data(), (int)n_over, k, out_idx,
                                                                               out_val);
         check(cudaGetLastError(), "scatter_rows_kernel");
+        w.launches += 2;
     }
 }
 }  // namespace
@@ -398,6 +404,7 @@ void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, 
     launch_row_norms(q, nq, dim, w.xn.data(), st);
     launch_row_norms(base, nb, dim, w.cn.data(), st);
     launch_sqrt(w.cn.data(), nb, w.csq.data(), st);
+    w.launches = 3;
     check(cudaEventRecord(w.ev[1], st), "event");
     check(cudaEventRecord(w.ev[2], st), "event");
     FlatStats stats;
@@ -406,6 +413,7 @@ void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, 
     if (k > ke) {
         pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
         check(cudaGetLastError(), "pad_topk_kernel");
+        ++w.launches;
     }
     check(cudaEventRecord(w.ev[6], st), "event");
     int e = 0;
@@ -425,6 +433,7 @@ void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, 
         stats.fallback_ms = std::max(0.0f, stats.total_ms - stats.norms_ms - stats.sample_ms - stats.filter_ms -
                                                stats.refine_ms);
     }
+    stats.launches = (uint32_t)w.launches;
     w.last = stats;
 }
 

@@ -34,6 +34,7 @@ struct FlatStats {
     unsigned long long candidates = 0;  // kept columns over all queries (pass 2)
     uint32_t overflow_queries = 0;      // queries redone by the single-pass path
     int sample_stride = 0, cap = 0, single_pass = 0;
+    uint32_t launches = 0;              // kernels launched by the call
 };
 struct FlatWork {
     static constexpr int kLevels = 4;   // sample levels of the threshold recursion
@@ -47,6 +48,7 @@ struct FlatWork {
     DeviceBuffer<int> err;
     cudaEvent_t ev[7] = {};
     FlatStats last;
+    int launches = 0;
     FlatWork() = default;
     FlatWork(const FlatWork&) = delete;
     FlatWork& operator=(const FlatWork&) = delete;

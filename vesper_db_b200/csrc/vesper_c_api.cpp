@@ -613,6 +613,7 @@ VESPER_C_API vesper_status_t vesper_flat_get_last_timings(vesper_flat_timings_t*
     out->overflow_queries = s.overflow_queries;
     out->sample_stride = (uint32_t)s.sample_stride;
     out->single_pass = (uint32_t)s.single_pass;
+    out->kernel_launches = s.launches;
     return VESPER_OK;
 }
 
