@@ -21,8 +21,8 @@ def _index():
     return IvfPqIndex()
 
 
-def _search(idx, q, k, npb, scan, threshold=None):
-    env = {"VGPU_SCAN": scan, "VGPU_LIST_THRESHOLD": threshold}
+def _search(idx, q, k, npb, scan, threshold=None, cta=None):
+    env = {"VGPU_SCAN": scan, "VGPU_LIST_THRESHOLD": threshold, "VGPU_LIST_CTA": cta}
     old = {key: os.environ.get(key) for key in env}
     for key, val in env.items():
         if val is None:
@@ -80,6 +80,21 @@ def test_list_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches, thre
         assert np.array_equal(bn, tn)
         assert np.array_equal(bd, td)
         assert np.array_equal(bi, ti)
+
+
+@pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES)
+def test_cta_pair_screen_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches):
+    """The screen on CTA pairs (tcgen05 cta_group::2, M = 256: two tiles per unit, the
+    query tile split between the two SMs) keeps the same pairs: bit-identical results."""
+    rng = np.random.default_rng(dim + m + nlist)
+    idx, cent = _build(rng, dim, m, nlist, n, rot)
+    q = (cent[rng.integers(0, nlist, nq)] + 0.3 * rng.standard_normal((nq, dim))).astype(np.float32)
+    for k, npb in searches:
+        (bi, bd, bn), _ = _search(idx, q, k, npb, "blocked")
+        for threshold in (None, "tc"):
+            (ti, td, tn), vt = _search(idx, q, k, npb, "tc", threshold, cta="2")
+            assert vt == 4
+            assert np.array_equal(bn, tn) and np.array_equal(bd, td) and np.array_equal(bi, ti)
 
 
 @pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES[:2])

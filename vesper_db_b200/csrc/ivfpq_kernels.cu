@@ -1258,13 +1258,15 @@ void launch_scan_blocked(const float* T, long long nq, const float* pbase, const
 // ---------------------------------------------------------------------------------
 namespace {
 constexpr uint32_t SPLIT_BLOCKS = 64;   // 128-entry blocks per part
+constexpr uint32_t SPLIT_BLOCKS_OVER = 64;  // ... when only overflowed queries run (smaller parts measured slower)
 constexpr int SPLIT_MAX_KEYS = 8192;    // keys merged per query (parts x next_pow2(k))
 }
 
 __global__ void split_count_kernel(const uint32_t* __restrict__ probe, int nprobe, int nscan,
                                    const uint64_t* __restrict__ blk_off, long long nq,
                                    const uint32_t* __restrict__ only_over, uint32_t over_cap, uint32_t max_parts,
-                                   uint32_t* __restrict__ parts, uint32_t* __restrict__ nblocks) {
+                                   uint32_t blocks_per_part, uint32_t* __restrict__ parts,
+                                   uint32_t* __restrict__ nblocks) {
     for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
         uint32_t nb = 0;
         for (int t = 0; t < nscan; ++t) {
@@ -1272,7 +1274,7 @@ __global__ void split_count_kernel(const uint32_t* __restrict__ probe, int nprob
             nb += (uint32_t)(blk_off[l + 1] - blk_off[l]);
         }
         const bool run = !only_over || only_over[q] > over_cap;
-        const uint32_t p = (nb + SPLIT_BLOCKS - 1) / SPLIT_BLOCKS;
+        const uint32_t p = (nb + blocks_per_part - 1) / blocks_per_part;
         parts[q] = run ? max(1u, min(p, max_parts)) : 0u;
         nblocks[q] = nb;
     }
@@ -1367,7 +1369,8 @@ void launch_scan_blocked_split(const float* T, long long nq, const float* pbase,
     const uint32_t max_parts = (uint32_t)std::max(1, SPLIT_MAX_KEYS / k);
     const int gb = (int)std::min<long long>((nq + 255) / 256, 148LL * 4);
     split_count_kernel<<<gb, 256, 0, st>>>(probe, nprobe, nscan, blk_off, nq, only_over, over_cap, max_parts,
-                                           w.parts.data(), w.nblocks.data());
+                                           only_over ? SPLIT_BLOCKS_OVER : SPLIT_BLOCKS, w.parts.data(),
+                                           w.nblocks.data());
     VGPU_LAUNCH("split_count_kernel");
     size_t tmp = w.scan_tmp.size();
     check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.parts.data(), w.part_off.data(), (int)(nq + 1), st),

@@ -104,6 +104,7 @@ struct TlWork {
     cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     SplitWork split;  // threshold scan and overflow fallback
     int cap = 0;
+    bool pairs = false;  // screen on CTA pairs (tcgen05 cta_group::2) instead of single CTAs
     void reserve(long long nq, int nprobe, int nlist, int dim, int k, int cap, size_t n_vectors);
     TlWork() = default;
     TlWork(const TlWork&) = delete;

@@ -530,6 +530,420 @@ __global__ void __launch_bounds__(TL_THREADS, 1) tc_list_scan_kernel(const __gri
 }
 
 // ---------------------------------------------------------------------------------
+// The same screen on CTA pairs (clusters of two, tcgen05 cta_group::2).  A unit covers
+// two consecutive 128-entry tiles of a list; CTA r of the pair decodes tile 2p + r into
+// its own tensor memory (rows 128 r .. 128 r + 127 of an M = 256 A operand) and streams
+// half of each chunk's N query rows (N/2 rows per stage) into its own shared memory.
+// The pair's leader (rank 0) issues tcgen05.mma.cta_group::2 M = 256: each SM reads only
+// its half of the query tile, halving the shared-memory traffic per MMA, and each CTA's
+// tensor memory receives the accumulator rows of its own tile.  Roles as in the
+// single-CTA kernel; in addition the leader's scheduler picks the units and publishes
+// them to the peer, the peer's TMA loads complete on the leader's stage barriers, the
+// leader's commits arrive on the barriers of both CTAs, and the peer's decoders and
+// epilogue arrive on the leader's barriers.
+// ---------------------------------------------------------------------------------
+namespace {
+__device__ __forceinline__ void mma2_ss_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma2_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Commit of this thread's earlier tcgen05 operations to the mbarrier at cluster address
+// caddr (this CTA's or the peer's).
+__device__ __forceinline__ void commit2_elect(uint32_t caddr) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+        ::"r"(caddr)
+        : "memory");
+}
+// A box of 64 bf16 columns x (N/2) rows into this CTA's shared memory; the bytes complete
+// on the mbarrier at cluster address mbar (the pair leader's stage barrier).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
+        : "memory");
+}
+// Arrive on a barrier of the pair leader (local arrive on the leader itself).
+__device__ __forceinline__ void arrive_leader(uint64_t* bar, bool leader) {
+    if (leader) tc::mbar_arrive(bar);
+    else tc::mbar_arrive_cluster(tc::peer_addr(bar, 0));
+}
+}  // namespace
+
+template <int N, int S, int DS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TL_THREADS, 1)
+    tc_list_scan2_kernel(const __grid_constant__ CUtensorMap qmap, const TlParams P) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int HN = N / 2;                 // query rows per CTA per chunk
+    constexpr int STAGE_BYTES = HN * 128;
+    constexpr uint32_t kDcol = 512u - 2u * N;
+    const int KC = P.dim / 64;
+    const int KT = min(KC, (int)(kDcol / 32));
+    unsigned char* a_smem = smem + S * STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(a_smem + (KC - KT) * (TL_M * 128));
+    uint64_t* empty = full + S;
+    uint64_t* accf = empty + S;
+    uint64_t* acce = accf + 2;
+    uint64_t* ufull = acce + 2;
+    uint64_t* uempty = ufull + 2;
+    uint64_t* uann = uempty + 2;   // peer: unit published by the leader's scheduler
+    uint64_t* ureq = uann + 2;     // leader: the peer released a unit slot
+    uint64_t* afull = ureq + 2;
+    uint64_t* drain = afull + 1;
+    uint4* meta = reinterpret_cast<uint4*>(drain + 1);
+    float2* mtest = reinterpret_cast<float2*>(meta + 2 * N);
+    UnitInfo* units = reinterpret_cast<UnitInfo*>(mtest + 2 * N);
+    unsigned char* ucodes = reinterpret_cast<unsigned char*>(units + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ucodes + 2 * TL_M * P.m);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = tc::cluster_rank();
+    const bool leader = rank == 0;
+    constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (16u << 24);  // M 256
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&accf[b], 1);
+            tc::mbar_init(&acce[b], 2 * 128);
+            tc::mbar_init(&ufull[b], 1);
+            tc::mbar_init(&uempty[b], 6);  // TMA warp + MMA warp + 4 decoder warps
+            tc::mbar_init(&uann[b], 1);
+            tc::mbar_init(&ureq[b], 1);
+        }
+        tc::mbar_init(afull, 2 * 128);
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::mbar_init_fence();
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         tc::smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::cluster_sync();  // the peer's barriers exist before anything arrives on them
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t peer = rank ^ 1u;
+
+    auto fail = [&](int code) {
+        *abort_flag = 1;
+        tc::st_cluster_u32(tc::peer_addr((const void*)abort_flag, peer), 1u);
+        atomicExch(P.err, code);
+    };
+
+    if (warp == 6) {
+        // ---- scheduler.  The leader takes units from the global counter and publishes
+        // each to the peer (unit slot copy + arrive on the peer's uann); each CTA then
+        // prefetches the codes of its own tile.
+        const uint32_t total = P.unit_off[P.nlist];
+        for (uint32_t it = 0;; ++it) {
+            const uint32_t slot = it & 1;
+            UnitInfo ui{};
+            if (leader) {
+                if (it >= 2) {
+                    const bool ok = tc::mbar_wait(&uempty[slot], ((it >> 1) - 1) & 1) &&
+                                    tc::mbar_wait_cluster(&ureq[slot], ((it >> 1) - 1) & 1);
+                    if (!__all_sync(0xffffffffu, ok)) { if (lane == 0) fail(31); break; }
+                }
+                uint32_t u = total;
+                if (lane == 0 && !*abort_flag) u = atomicAdd(P.unit_counter, 1u);
+                u = __shfl_sync(0xffffffffu, u, 0);
+                if (u < total) {
+                    const uint32_t l = P.unit_list[u];
+                    const uint32_t r = u - P.unit_off[l];
+                    const uint32_t s0 = P.seg_off[l], s1 = P.seg_off[l + 1];
+                    const uint64_t o0 = P.offs[l], o1 = P.offs[l + 1];
+                    const uint32_t nqg = (s1 - s0 + N * TL_QG - 1) / (N * TL_QG);
+                    ui.list = l;
+                    ui.tile = r / nqg;  // tile pair
+                    ui.pair_begin = s0 + (r % nqg) * (uint32_t)(N * TL_QG);
+                    ui.pair_end = min(s1, ui.pair_begin + (uint32_t)(N * TL_QG));
+                    ui.n_chunks = (ui.pair_end - ui.pair_begin + N - 1) / N;
+                    ui.list_len = (uint32_t)(o1 - o0);
+                    ui.entry_base = o0;
+                    ui.valid = 1;
+                }
+                // publish to the peer's slot, then signal it
+                if (lane == 0) {
+                    const uint32_t* w = reinterpret_cast<const uint32_t*>(&ui);
+                    const uint32_t dst = tc::peer_addr(&units[slot], peer);
+                    for (int i = 0; i < (int)(sizeof(UnitInfo) / 4); ++i) tc::st_cluster_u32(dst + 4 * i, w[i]);
+                    tc::mbar_arrive_cluster(tc::peer_addr(&uann[slot], peer));
+                }
+            } else {
+                if (it >= 2) {
+                    const bool ok = tc::mbar_wait(&uempty[slot], ((it >> 1) - 1) & 1);
+                    if (!__all_sync(0xffffffffu, ok)) { if (lane == 0) fail(32); break; }
+                    if (lane == 0) tc::mbar_arrive_cluster(tc::peer_addr(&ureq[slot], peer));
+                }
+                if (!__all_sync(0xffffffffu, tc::mbar_wait_cluster(&uann[slot], (it >> 1) & 1))) {
+                    if (lane == 0) fail(33);
+                    break;
+                }
+                ui = units[slot];
+            }
+            if (ui.valid) {
+                // this CTA's tile of the pair: codes contiguous in the CSR array
+                const uint32_t tile = 2 * ui.tile + rank;
+                const uint32_t e0 = tile * TL_M;
+                const uint32_t rows = e0 < ui.list_len ? min((uint32_t)TL_M, ui.list_len - e0) : 0u;
+                const uint32_t n16 = rows * (uint32_t)P.m / 16;
+                const unsigned char* src = P.codes + (ui.entry_base + e0) * (unsigned long long)P.m;
+                const uint32_t dst = tc::smem_u32(ucodes + slot * TL_M * P.m);
+                for (uint32_t i = lane; i < n16; i += 32) cp_async16(dst + i * 16, src + (size_t)i * 16);
+                cp_async_commit();
+                cp_async_wait<0>();
+            }
+            if (leader && lane == 0) units[slot] = ui;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&ufull[slot]);
+            if (!ui.valid) break;
+        }
+    } else if (warp == 4) {
+        // ---- TMA producer: this CTA's N/2 query rows of each chunk, one 64 x N/2 tile
+        // load per stage; the bytes complete on the leader's stage barrier.
+        uint32_t it_prod = 0;
+        if (lane == 0) {
+            for (uint32_t it = 0; !*abort_flag; ++it) {
+                const uint32_t slot = it & 1;
+                if (!tc::mbar_wait(&ufull[slot], (it >> 1) & 1)) { fail(22); break; }
+                const UnitInfo ui = units[slot];
+                tc::mbar_arrive(&uempty[slot]);
+                if (!ui.valid) break;
+                bool ok = true;
+                for (uint32_t c = 0; c < ui.n_chunks && ok; ++c) {
+                    const int y = (int)(ui.pair_begin + c * N + rank * HN);
+                    for (int kc = 0; kc < KC; ++kc) {
+                        const uint32_t stage = it_prod % S;
+                        if (it_prod >= (uint32_t)S && !tc::mbar_wait(&empty[stage], ((it_prod / S) - 1) & 1)) {
+                            fail(11);
+                            ok = false;
+                            break;
+                        }
+                        if (leader) tc::mbar_expect_tx(&full[stage], 2u * STAGE_BYTES);
+                        tma_load_2d_pair(tc::smem_u32(smem + stage * STAGE_BYTES), &qmap, kc * 64, y,
+                                         leader ? tc::smem_u32(&full[stage]) : tc::peer_addr(&full[stage], 0));
+                        ++it_prod;
+                    }
+                }
+            }
+            // The leader's last stages have landed (both halves) before the pair can exit.
+            if (leader)
+                for (uint32_t i = it_prod > (uint32_t)S ? it_prod - S : 0; i < it_prod; ++i)
+                    if (!tc::mbar_wait(&full[i % S], (i / S) & 1)) { fail(16); break; }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ---- MMA issuer (leader only); the peer's warp follows the unit ring.
+        uint32_t it_mma = 0, cg_mma = 0;
+        auto wwait = [&](uint64_t* bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, tc::mbar_wait_cluster(bar, parity));
+        };
+        for (uint32_t it = 0; !*abort_flag; ++it) {
+            const uint32_t slot = it & 1;
+            if (!wwait(&ufull[slot], (it >> 1) & 1)) { if (lane == 0) fail(23); break; }
+            const uint32_t nch = units[slot].n_chunks;
+            const uint32_t valid = units[slot].valid;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&uempty[slot]);
+            if (!valid) break;
+            if (!leader) continue;
+            if (!wwait(afull, it & 1)) { if (lane == 0) fail(24); break; }
+            tc::fence_after_sync();
+            bool ok = true;
+            for (uint32_t c = 0; c < nch && ok; ++c) {
+                const uint32_t buf = cg_mma & 1;
+                if (cg_mma >= 2 && !wwait(&acce[buf], ((cg_mma >> 1) - 1) & 1)) {
+                    if (lane == 0) fail(12);
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t dcol = tmem + kDcol + buf * (uint32_t)N;
+                for (int kc = 0; kc < KC; ++kc) {
+                    const uint32_t stage = it_mma % S;
+                    if (!wwait(&full[stage], (it_mma / S) & 1)) {
+                        if (lane == 0) fail(13);
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint64_t bd = tc::sw128_kmajor_desc(tc::smem_u32(smem + stage * STAGE_BYTES));
+                    if (kc < KT) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma2_ts_elect(dcol, tmem + (uint32_t)(kc * 32 + kk * 8), bd + (uint64_t)(kk * 2), kIdesc,
+                                          (kc > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        const uint64_t ad =
+                            tc::sw128_kmajor_desc(tc::smem_u32(a_smem + (size_t)(kc - KT) * (TL_M * 128)));
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma2_ss_elect(dcol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), kIdesc,
+                                          (kc > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    commit2_elect(tc::smem_u32(&empty[stage]));
+                    commit2_elect(tc::peer_addr(&empty[stage], 1));
+                    ++it_mma;
+                }
+                commit2_elect(tc::smem_u32(&accf[buf]));
+                commit2_elect(tc::peer_addr(&accf[buf], 1));
+                ++cg_mma;
+            }
+            if (!ok) break;
+        }
+        if (leader) {
+            // Every tensor-core operation issued has completed before TMEM is freed.
+            commit2_elect(tc::smem_u32(drain));
+            if (!wwait(drain, 0) && lane == 0) atomicExch(P.err, 15);
+        }
+    } else if (warp < 4) {
+        // ---- decoders + epilogue (warps 0-3): thread = entry row of this CTA's tile.
+        const int row = tid;
+        const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint4 pad = make_uint4(0xffffffffu, 0u, 0u, 0u);
+        uint32_t cg_epi = 0;
+        for (uint32_t it = 0;; ++it) {
+            const uint32_t slot = it & 1;
+            const bool got = !*abort_flag && tc::mbar_wait(&ufull[slot], (it >> 1) & 1);
+            if (group_any(!got)) {
+                if (!got && !*abort_flag) fail(25);
+                break;
+            }
+            const UnitInfo ui = units[slot];
+            if (!ui.valid) break;
+            const uint32_t pb = ui.pair_begin, pe = ui.pair_end, nch = ui.n_chunks;
+            const uint32_t tile = 2 * ui.tile + rank;
+            const uint32_t e0 = tile * TL_M;
+            const bool vrow = e0 + (uint32_t)row < ui.list_len;
+            const unsigned long long ebase = ui.entry_base + e0;
+            const float u = vrow ? P.vterm[ebase + row] : 0.0f;
+            const float xn = vrow ? P.xnorm[ebase + row] : 0.0f;
+            uint4 next = pad;
+            if (tid < N && pb + (uint32_t)tid < pe) next = P.seg_meta[pb + tid];
+            tc::fence_after_sync();
+            const uint8_t* crow = ucodes + slot * TL_M * P.m + row * P.m;
+            for (int kc0 = 0; kc0 < KC; kc0 += 3)
+                decode_batch<DS, 3>(tlane, a_smem, row, crow, P.cbb, kc0, KC, KT, vrow);
+            tc::tmem_st_wait();
+            tc::fence_proxy_async_smem();
+            tc::fence_before_sync();
+            arrive_leader(afull, leader);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&uempty[slot]);
+
+            const float sx = (kSlackMul + 2.0f * kSlackAbs) * xn;
+            const float wrow = kSlackAbs * fabsf(u) - u;
+            const uint32_t pos = e0 + (uint32_t)row;
+            bool stop = false;
+            for (uint32_t c = 0; c < nch; ++c) {
+                const uint32_t buf = cg_epi & 1;
+                uint4* bm = meta + buf * N;
+                float2* bt = mtest + buf * N;
+                if (tid < N) {
+                    bm[tid] = next;
+                    const float bj = __uint_as_float(next.y), tq = __uint_as_float(next.z);
+                    bt[tid] = next.x == 0xffffffffu
+                                  ? make_float2(0.0f, -FLT_MAX)
+                                  : make_float2(__uint_as_float(next.w),
+                                                (tq - bj) + kSlackAbs * (fabsf(bj) + fabsf(tq)));
+                    const uint32_t pi = pb + (c + 1) * N + (uint32_t)tid;
+                    next = (c + 1 < nch && pi < pe) ? P.seg_meta[pi] : pad;
+                }
+                const bool ok = !*abort_flag && tc::mbar_wait_cluster(&accf[buf], (cg_epi >> 1) & 1);
+                if (group_any(!ok)) {
+                    if (!ok && !*abort_flag) fail(14);
+                    stop = true;
+                    break;
+                }
+                tc::fence_after_sync();
+#pragma unroll
+                for (int h = 0; h < N / 32; ++h) {
+                    uint32_t acc[32];
+                    tc::tmem_ld32(tlane + kDcol + buf * (uint32_t)N + h * 32, acc);
+                    tc::tmem_ld_wait();
+                    if (h == N / 32 - 1) {
+                        tc::fence_before_sync();
+                        arrive_leader(&acce[buf], leader);
+                    }
+                    if (P.mins) {
+                        float mine = FLT_MAX;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const uint4 md = bm[h * 32 + j];
+                            const float bj = __uint_as_float(md.y);
+                            float ub = FLT_MAX;
+                            if (vrow) {
+                                const float approx = fmaf(-2.0f, __uint_as_float(acc[j]), bj + u);
+                                ub = approx + fmaf(sx, __uint_as_float(md.w), kSlackAbs * (fabsf(bj) + fabsf(u)));
+                            }
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) ub = fminf(ub, __shfl_xor_sync(0xffffffffu, ub, o));
+                            if (lane == j) mine = ub;
+                        }
+                        const uint32_t qt = bm[h * 32 + lane].x;
+                        if (qt != 0xffffffffu && e0 < ui.list_len)
+                            P.mins[P.mins_off[qt >> 10] + tile * 4 + warp] = mine;
+                        continue;
+                    }
+                    uint32_t mask = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float2 t = bt[h * 32 + j];
+                        const float lhs = fmaf(-sx, t.x, -2.0f * __uint_as_float(acc[j]));
+                        mask |= (lhs <= t.y + wrow) ? (1u << j) : 0u;
+                    }
+                    if (!vrow) mask = 0;
+                    while (mask) {
+                        const int j = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const uint32_t qt = bm[h * 32 + j].x;
+                        const uint32_t q = qt >> 10;
+                        const uint32_t slot2 = atomicAdd(&P.cand_cnt[q], 1u);
+                        if (slot2 < (uint32_t)P.cap)
+                            P.cand[(size_t)q * P.cap + slot2] = ((unsigned long long)(qt & 1023u) << 32) | pos;
+                    }
+                }
+                ++cg_epi;
+            }
+            if (stop) break;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::cluster_sync();  // neither CTA frees its TMEM or exits while the pair still works
+    tc::fence_after_sync();
+    if (warp == 5)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+}
+
+// ---------------------------------------------------------------------------------
 // Batch preparation: bf16 queries and norms, pair grouping by list, unit counts.
 // ---------------------------------------------------------------------------------
 __global__ void query_prep_kernel(const float* __restrict__ rq, long long nq, int dim, __nv_bfloat16* __restrict__ rqb,
@@ -698,15 +1112,16 @@ __global__ void unit_fill_kernel(const uint32_t* __restrict__ unit_off, int nlis
     }
 }
 
+// unit_rows: entries per unit (128 for single CTAs, 256 for CTA pairs).
 __global__ void unit_count_kernel(const uint32_t* __restrict__ cnt, const uint64_t* __restrict__ offs, int nlist,
-                                  int n_cols, uint32_t* __restrict__ units) {
+                                  int n_cols, int unit_rows, uint32_t* __restrict__ units) {
     const int l = blockIdx.x * blockDim.x + threadIdx.x;
     if (l > nlist) return;
     if (l == nlist) { units[l] = 0; return; }
     const uint32_t c = cnt[l];
     const uint64_t L = offs[l + 1] - offs[l];
     units[l] = (c == 0 || L == 0) ? 0u
-                                  : (uint32_t)((L + TL_M - 1) / TL_M) *
+                                  : (uint32_t)((L + unit_rows - 1) / unit_rows) *
                                         ((c + (uint32_t)(n_cols * TL_QG) - 1) / (uint32_t)(n_cols * TL_QG));
 }
 
@@ -795,11 +1210,18 @@ __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict_
 namespace {
 // One accumulator is 128 queries wide; with two of them 256 TMEM columns remain for the
 // tile, so dims beyond 512 go to a shared-memory tile and the B ring shrinks.
-template <int S>
+template <int S, int N>
 size_t tl_smem(int dim, int m) {
+    const int kt = (512 - 2 * N) / 32, kc = dim / 64, ks = kc > kt ? kc - kt : 0;  // 32 TMEM columns per 64 dims
+    return 1024 + (size_t)S * N * 128 + (size_t)ks * TL_M * 128 + (2 * S + 10) * 8 + 2 * N * 16 + 2 * N * 8 +
+           2 * sizeof(UnitInfo) + 2 * (size_t)TL_M * m + 16;
+}
+// CTA-pair kernel: stages of N/2 query rows, four more unit-ring barriers.
+template <int S>
+size_t tl_smem2(int dim, int m) {
     constexpr int N = 128;
     const int kc = dim / 64, ks = kc > 8 ? kc - 8 : 0;
-    return 1024 + (size_t)S * N * 128 + (size_t)ks * TL_M * 128 + (2 * S + 10) * 8 + 2 * N * 16 + 2 * N * 8 +
+    return 1024 + (size_t)S * (N / 2) * 128 + (size_t)ks * TL_M * 128 + (2 * S + 14) * 8 + 2 * N * 16 + 2 * N * 8 +
            2 * sizeof(UnitInfo) + 2 * (size_t)TL_M * m + 16;
 }
 }  // namespace
@@ -874,7 +1296,8 @@ void group_pairs(const TlScanArgs& a, TlWork& w, const uint32_t* probe, int np, 
     pair_scatter_kernel<<<gb, 256, 0, st>>>(probe, npairs, np, w.seg_off.data(), w.cursor.data(), pbase,
                                             w.tau.data(), w.rqn.data(), reinterpret_cast<uint4*>(w.seg_meta.data()));
     VGPU_LAUNCH("pair_scatter_kernel");
-    unit_count_kernel<<<(a.nlist + 1 + 255) / 256, 256, 0, st>>>(w.cnt.data(), a.offs, a.nlist, N, w.units.data());
+    unit_count_kernel<<<(a.nlist + 1 + 255) / 256, 256, 0, st>>>(w.cnt.data(), a.offs, a.nlist, N,
+                                                                 TL_M * (w.pairs ? 2 : 1), w.units.data());
     VGPU_LAUNCH("unit_count_kernel");
     tmp = w.scan_tmp.size();
     check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.units.data(), w.unit_off.data(), a.nlist + 1, st),
@@ -906,20 +1329,51 @@ void screen_pass(const TlScanArgs& a, TlWork& w, long long npairs, int np, float
     int dev = 0, sms = 148;
     check(cudaGetDevice(&dev), "cudaGetDevice");
     check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
-    const CUtensorMap qmap = make_tile_map_bf16(w.qperm.data(), npairs, a.dim, 128);
-#define VGPU_TL(SV, DSV)                                                                                 \
+    if (w.pairs) {
+        const CUtensorMap qmap2 = make_tile_map_bf16(w.qperm.data(), npairs, a.dim, N / 2);
+#define VGPU_TL2(SV, DSV)                                                                                \
     do {                                                                                                 \
-        const size_t smem = tl_smem<SV>(a.dim, a.m);                                                     \
+        const size_t smem = tl_smem2<SV>(a.dim, a.m);                                                    \
         if (smem > 227 * 1024) throw CudaError("tc_list_scan: shared-memory layout too large");          \
-        check(cudaFuncSetAttribute(tc_list_scan_kernel<N, SV, DSV>,                                      \
+        check(cudaFuncSetAttribute(tc_list_scan2_kernel<N, SV, DSV>,                                     \
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),             \
+              "cudaFuncSetAttribute(tc_list_scan2)");                                                    \
+        cudaLaunchConfig_t cfg = {};                                                                     \
+        cfg.blockDim = dim3(TL_THREADS);                                                                 \
+        cfg.dynamicSmemBytes = smem;                                                                     \
+        cfg.stream = st;                                                                                 \
+        cfg.gridDim = dim3(2 * (sms / 2));                                                               \
+        int clusters = 0;                                                                                \
+        check(cudaOccupancyMaxActiveClusters(&clusters, tc_list_scan2_kernel<N, SV, DSV>, &cfg),        \
+              "cudaOccupancyMaxActiveClusters");                                                         \
+        if (clusters < 1) throw CudaError("tc_list_scan: no CTA pair fits on an SM pair");               \
+        tc_list_scan2_kernel<N, SV, DSV><<<2 * std::min(clusters, sms / 2), TL_THREADS, smem, st>>>(qmap2, P); \
+    } while (0)
+        if (a.dim > 512 && tl_smem2<16>(a.dim, a.m) > 227 * 1024) {
+            if (dsub == 4) VGPU_TL2(12, 4); else if (dsub == 8) VGPU_TL2(12, 8); else VGPU_TL2(12, 16);
+        } else if (a.dim > 512) {
+            if (dsub == 4) VGPU_TL2(16, 4); else if (dsub == 8) VGPU_TL2(16, 8); else VGPU_TL2(16, 16);
+        } else {
+            if (dsub == 4) VGPU_TL2(16, 4); else if (dsub == 8) VGPU_TL2(16, 8); else VGPU_TL2(16, 16);
+        }
+#undef VGPU_TL2
+        VGPU_LAUNCH("tc_list_scan2_kernel");
+        return;
+    }
+    const CUtensorMap qmap = make_tile_map_bf16(w.qperm.data(), npairs, a.dim, N);
+#define VGPU_TL(NV, SV, DSV)                                                                             \
+    do {                                                                                                 \
+        const size_t smem = tl_smem<SV, NV>(a.dim, a.m);                                                 \
+        if (smem > 227 * 1024) throw CudaError("tc_list_scan: shared-memory layout too large");          \
+        check(cudaFuncSetAttribute(tc_list_scan_kernel<NV, SV, DSV>,                                     \
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),             \
               "cudaFuncSetAttribute(tc_list_scan)");                                                     \
-        tc_list_scan_kernel<N, SV, DSV><<<sms, TL_THREADS, smem, st>>>(qmap, P);                         \
+        tc_list_scan_kernel<NV, SV, DSV><<<sms, TL_THREADS, smem, st>>>(qmap, P);                        \
     } while (0)
     if (a.dim > 512) {  // part of the tile in shared memory: 8 B stages
-        if (dsub == 4) VGPU_TL(8, 4); else if (dsub == 8) VGPU_TL(8, 8); else VGPU_TL(8, 16);
+        if (dsub == 4) VGPU_TL(128, 8, 4); else if (dsub == 8) VGPU_TL(128, 8, 8); else VGPU_TL(128, 8, 16);
     } else {
-        if (dsub == 4) VGPU_TL(10, 4); else if (dsub == 8) VGPU_TL(10, 8); else VGPU_TL(10, 16);
+        if (dsub == 4) VGPU_TL(128, 10, 4); else if (dsub == 8) VGPU_TL(128, 10, 8); else VGPU_TL(128, 10, 16);
     }
 #undef VGPU_TL
     VGPU_LAUNCH("tc_list_scan_kernel");
@@ -934,6 +1388,11 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     if (npairs > 0xffffffffLL || a.nq > (1LL << 22) || a.nprobe > 1024)
         throw CudaError("tc_list_scan: batch too large (at most 2^22 queries and 1024 probes)");
 
+    // VGPU_LIST_CTA=2 selects the CTA-pair screen (M = 256); default single CTAs (the
+    // pair kernel halves the query bytes each SM streams but measures slower: its stage
+    // recycling crosses the pair twice per stage).
+    w.pairs = false;
+    if (const char* v = std::getenv("VGPU_LIST_CTA")) w.pairs = std::string(v) == "2";
     check(cudaEventRecord(w.ev[0], st), "cudaEventRecord");
     launch_query_prep(a.rq, a.nq, a.dim, w.rqb.data(), w.rqn.data(), st);
     // Thresholds.  A query whose nearest list is long gets tau from a tensor-core pass
