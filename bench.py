@@ -23,8 +23,9 @@ reference's IvfPqIndex::load reads).
 
 Multi-GPU (torchrun, one rank per GPU): the base set is sharded by vector (rank r
 holds base chunks r, r+W, ...); every rank trains the same model on the same training
-sample, searches all queries over its shard, and the per-rank top-k are merged with an
-NCCL all_gather.
+sample; each rank probes 1/W of the query batch (the coarse stage is identical on every
+shard) and the probe lists are all-gathered over NCCL; every rank then searches all
+queries over its shard, and the per-rank top-k are merged with an NCCL all_gather.
 """
 from __future__ import annotations
 
@@ -432,7 +433,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
 
     from vesper_db_b200 import IvfPqIndex
-    from vesper_db_b200.shard import chunks_of, merge_topk
+    from vesper_db_b200.shard import chunks_of, merge_topk, probed_search
     t_build0 = time.perf_counter()
     centres, sigmas = gen_centres(torch, dev)
     queries = synth.gen_queries(torch, dev, centres, sigmas, NQ)
@@ -528,9 +529,16 @@ def main():
 
     slot = torch.arange(K, device=dev)[None, :]
 
+    # Multi-GPU: each rank probes 1/world of the batch (the coarse stage is the same on
+    # every shard) and the probe lists are all-gathered before the shard searches.
+    probe_bufs = {}
+
     def one_search(nprobe):
-        index.search_batch_device(queries.data_ptr(), NQ, K, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
-                                  out_n.data_ptr())
+        if world > 1 and NQ % world == 0:
+            probed_search(index, queries, K, nprobe, NLIST, out_ids, out_d, out_n, probe_bufs)
+        else:
+            index.search_batch_device(queries.data_ptr(), NQ, K, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
+                                      out_n.data_ptr())
         if world > 1:
             # padded slots (fewer than k results on this shard) must not win the merge
             d = torch.where(slot < out_n[:, None], out_d, torch.full_like(out_d, float("inf")))

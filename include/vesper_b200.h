@@ -113,6 +113,24 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_noalloc(const vesp
                                                                       uint64_t* d_out_ids, float* d_out_distances,
                                                                       uint32_t* d_out_counts);
 
+/* The coarse stage alone: for each query the min(nprobe, nlist) nearest lists in the
+ * search's probe order (d_probe uint32 [nq x np]) and their distances (d_probe_d float
+ * [nq x np]); device pointers on the index's GPU.  No counterpart in the reference: with
+ * vesper_ivfpq_search_batch_device_probed it lets several indexes that share a query
+ * batch (one per GPU, each holding a shard of the base set) probe a slice of the batch
+ * each and exchange the lists, instead of every GPU probing every query. */
+VESPER_C_API vesper_status_t vesper_ivfpq_probe_device(const vesper_index_t* index, const float* d_queries,
+                                                       size_t nq, uint32_t nprobe, uint32_t* d_probe,
+                                                       float* d_probe_d);
+
+/* vesper_ivfpq_search_batch_device with the probe lists given (as
+ * vesper_ivfpq_probe_device writes them, for the same nprobe); results are those of the
+ * plain call.  The exact rerank is not available here. */
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
+    const vesper_index_t* index, const float* d_queries, size_t nq, const vesper_ivfpq_search_params_ex_t* params,
+    const uint32_t* d_probe, const float* d_probe_d, uint64_t* d_out_ids, float* d_out_distances,
+    uint32_t* d_out_counts);
+
 /* Device time per stage of the last search call (CUDA events, milliseconds). */
 typedef struct vesper_ivfpq_timings_s {
   float coarse_ms;   /* query-centroid distances */

@@ -73,3 +73,74 @@ def test_sharded_merge_equals_single_index(tmp_path, name, k, nprobe):
     ref_ids, ref_d, ref_n = data[f"ids_{k}_{nprobe}"], data[f"d_{k}_{nprobe}"], data[f"n_{k}_{nprobe}"]
     cnt = np.isfinite(got["d"]).sum(1).astype(np.uint32)
     assert_topk_equivalent(got["ids"], got["d"], cnt, ref_ids, ref_d, ref_n, 0.0)
+
+
+class _FakeProbeIndex:
+    """Stands in for the GPU index on CPU tensors: probe lists are a fixed function of
+    the query row, and the probed search records the probe lists it was handed."""
+
+    def __init__(self, nlist):
+        self.nlist = nlist
+
+    @staticmethod
+    def _view(ptr, shape, dtype):
+        import ctypes as C
+        ct = {np.int32: C.c_int32, np.float32: C.c_float, np.int64: C.c_int64}[dtype]
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(ct)), shape=shape)
+
+    def probe_device(self, q_ptr, nq, nprobe, probe_ptr, probe_d_ptr):
+        q = self._view(q_ptr, (nq, 4), np.float32)
+        pr = self._view(probe_ptr, (nq, nprobe), np.int32)
+        pd = self._view(probe_d_ptr, (nq, nprobe), np.float32)
+        for i in range(nq):
+            base = int(q[i, 0])
+            pr[i] = [(base * 7 + j) % self.nlist for j in range(nprobe)]
+            pd[i] = q[i, 0] + np.arange(nprobe, dtype=np.float32)
+
+    def search_batch_device_probed(self, q_ptr, nq, k, nprobe, probe_ptr, probe_d_ptr, ids_ptr, d_ptr,
+                                   counts_ptr=0, mode=0):
+        pr = self._view(probe_ptr, (nq, nprobe), np.int32)
+        pd = self._view(probe_d_ptr, (nq, nprobe), np.float32)
+        ids = self._view(ids_ptr, (nq, k), np.int64)
+        d = self._view(d_ptr, (nq, k), np.float32)
+        ids[:, :] = pr[:, :k]
+        d[:, :] = pd[:, :k]
+
+
+def _probe_worker(rank, world, port, out_path):
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from vesper_db_b200.shard import probed_search
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        nq, k, nprobe = 12, 3, 5
+        q = torch.zeros((nq, 4), dtype=torch.float32)
+        q[:, 0] = torch.arange(nq, dtype=torch.float32) * 3
+        ids = torch.zeros((nq, k), dtype=torch.int64)
+        d = torch.zeros((nq, k), dtype=torch.float32)
+        n = torch.zeros(nq, dtype=torch.int32)
+        probed_search(_FakeProbeIndex(64), q, k, nprobe, 64, ids, d, n, {})
+        np.savez(f"{out_path}.{rank}", ids=ids.numpy(), d=d.numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_probed_search_gathers_every_slice(tmp_path):
+    """Two ranks each probe half of the batch; both must search the full batch with the
+    probe lists a single rank would have computed."""
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "probe")
+    mp.start_processes(_probe_worker, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    fake = _FakeProbeIndex(64)
+    exp_ids = np.array([[(int(i * 3) * 7 + j) % 64 for j in range(3)] for i in range(12)])
+    exp_d = np.array([[i * 3 + j for j in range(3)] for i in range(12)], np.float32)
+    for r in range(2):
+        got = np.load(f"{out}.{r}.npz")
+        assert np.array_equal(got["ids"], exp_ids) and np.array_equal(got["d"], exp_d)
+    del fake

@@ -36,6 +36,7 @@ EXPORTED = [
     "vesper_ivfpq_search_batch_device_noalloc",
     "vesper_kmeans_params_init", "vesper_kmeans_fit", "vesper_kmeans_fit_device",
     "vesper_flat_topk", "vesper_flat_topk_device", "vesper_flat_get_last_timings",
+    "vesper_ivfpq_probe_device", "vesper_ivfpq_search_batch_device_probed",
 ]
 
 KMEANS_ELKAN = 0
@@ -167,6 +168,9 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_flat_topk_device": (st, [C.c_int, vp, C.c_size_t, vp, C.c_size_t, C.c_size_t, C.c_uint32,
                                              vp, vp]),
             "vesper_flat_get_last_timings": (st, [C.POINTER(FlatTimings)]),
+            "vesper_ivfpq_probe_device": (st, [vp, vp, C.c_size_t, C.c_uint32, vp, vp]),
+            "vesper_ivfpq_search_batch_device_probed": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx), vp, vp,
+                                                             vp, vp, vp]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

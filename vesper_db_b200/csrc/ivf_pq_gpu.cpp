@@ -780,9 +780,12 @@ public:
         return {};
     }
 
+    // ext_probe / ext_probe_d (device, [nq x min(nprobe, nlist)]): probe lists computed
+    // elsewhere (probe_device, e.g. by another rank); the coarse stage is skipped.
     std::expected<void, error> search_adc(const float* queries, size_t nq, const IvfPqSearchParams& sp,
                                           uint64_t* out_ids, float* out_d, uint32_t* out_n,
-                                          bool on_device) const {
+                                          bool on_device, const uint32_t* ext_probe = nullptr,
+                                          const float* ext_probe_d = nullptr) const {
         if (!trained) return fail(error_code::precondition_failed, "Index must be trained before searching");
         if (sp.k == 0) return fail(error_code::invalid_argument, "k must be > 0");
         if (sp.k > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "k above 1024 is not supported by the GPU path");
@@ -860,9 +863,13 @@ public:
                 od = w_out_d.data();
                 on = w_out_n.data();
             }
-            const bool tc = vgpu::use_tensor_cores(dq, d_cent.data(), (int)dim, nlist());
+            const bool tc = !ext_probe && vgpu::use_tensor_cores(dq, d_cent.data(), (int)dim, nlist());
+            const uint32_t* probe = ext_probe ? ext_probe + q0 * np : w_probe.data();
+            const float* probe_d = ext_probe ? ext_probe_d + q0 * np : w_probe_d.data();
             cudaEventRecord(ev[0], st);
-            if (tc) {
+            if (ext_probe) {
+                // probe lists given
+            } else if (tc) {
                 w_xn.reserve(qc);
                 reset_err();
                 vgpu::launch_row_norms(dq, (long long)nc, (int)dim, w_xn.data(), st);
@@ -873,7 +880,9 @@ public:
                                      (long long)nlist(), st);
             }
             cudaEventRecord(ev[1], st);
-            if (tc) {
+            if (ext_probe) {
+                // probe lists given
+            } else if (tc) {
                 vgpu::launch_screen_select(w_D.data(), (long long)nc, (long long)nlist(), (int)nlist(), dq, (int)dim,
                                            d_cent.data(), w_xn.data(), d_cn.data(), (int)np, nullptr, w_probe.data(),
                                            w_probe_d.data(), d_err.data(), st);
@@ -882,24 +891,24 @@ public:
                                       w_probe.data(), w_probe_d.data(), st);
             }
             cudaEventRecord(ev[2], st);
-            vgpu::launch_probe_sizes(w_probe.data(), (long long)(nc * np), d_offs.data(), w_scanned.data(), st);
+            vgpu::launch_probe_sizes(probe, (long long)(nc * np), d_offs.data(), w_scanned.data(), st);
             if (exact) {
                 const float* rres = nullptr;
                 if (has_rot) {
                     std::vector<uint32_t> pq(nc * np);
                     for (size_t i = 0; i < nc * np; ++i) pq[i] = (uint32_t)(i / np);
                     h2d(w_pair_q.data(), pq.data(), pq.size(), st);
-                    vgpu::launch_residual_rotate(dq, w_pair_q.data(), d_cent.data(), w_probe.data(),
+                    vgpu::launch_residual_rotate(dq, w_pair_q.data(), d_cent.data(), probe,
                                                  (long long)(nc * np), (int)dim, d_rot.data(), w_rres.data(), st);
                     rres = w_rres.data();
                 }
                 cudaEventRecord(ev[3], st);
-                vgpu::launch_scan_exact(dq, (long long)nc, (int)dim, d_cent.data(), rres, w_probe.data(), (int)np,
+                vgpu::launch_scan_exact(dq, (long long)nc, (int)dim, d_cent.data(), rres, probe, (int)np,
                                         d_cb.data(), (int)m(), (int)ksub, (int)dsub, d_offs.data(), d_codes.data(),
                                         (int)k, w_cand_d.data(), w_cand_pos.data(), w_cand_n.data(), st);
                 cudaEventRecord(ev[4], st);
                 vgpu::launch_merge(w_cand_d.data(), w_cand_pos.data(), w_cand_n.data(), (long long)nc, (int)np,
-                                   (int)k, w_probe.data(), d_offs.data(), d_ids.data(), oid, od, on, st);
+                                   (int)k, probe, d_offs.data(), d_ids.data(), oid, od, on, st);
             } else {
                 const float* rq = dq;
                 if (has_rot) {
@@ -909,12 +918,12 @@ public:
                 if (has_blocks) {
                     vgpu::launch_lut_blocked(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)dsub,
                                              w_T.data(), st);
-                    vgpu::launch_probe_base(rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
+                    vgpu::launch_probe_base(rq, (long long)nc, (int)dim, probe, probe_d,
                                             has_rot ? d_rc.data() : nullptr, (int)np, w_pbase.data(), st);
                     cudaEventRecord(ev[3], st);
                     if (list_scan) {
                         vgpu::TlScanArgs a{};
-                        a.T = w_T.data(); a.rq = rq; a.pbase = w_pbase.data(); a.probe = w_probe.data();
+                        a.T = w_T.data(); a.rq = rq; a.pbase = w_pbase.data(); a.probe = probe;
                         a.nq = (long long)nc; a.nprobe = (int)np; a.nlist = (int)nlist(); a.dim = (int)dim;
                         a.m = (int)m(); a.k = (int)k; a.offs = d_offs.data(); a.codes = d_codes.data();
                         a.vterm = d_vterm.data(); a.xnorm = d_xnorm.data(); a.cbb = d_cbb.data();
@@ -922,12 +931,12 @@ public:
                         a.ids = d_ids.data(); a.out_ids = oid; a.out_d = od; a.out_n = on; a.err = d_err.data();
                         vgpu::launch_tc_list_scan(a, tlw, st);
                     } else if (split_scan) {
-                        vgpu::launch_scan_blocked_split(w_T.data(), (long long)nc, w_pbase.data(), w_probe.data(),
+                        vgpu::launch_scan_blocked_split(w_T.data(), (long long)nc, w_pbase.data(), probe,
                                                         (int)np, (int)np, (int)m(), d_offs.data(), d_blk_off.data(),
                                                         d_bcodes.data(), d_bvterm.data(), d_ids.data(), (int)k, oid,
                                                         od, on, nullptr, 0, tlw.split, st);
                     } else {
-                        vgpu::launch_scan_blocked(w_T.data(), (long long)nc, w_pbase.data(), w_probe.data(), (int)np,
+                        vgpu::launch_scan_blocked(w_T.data(), (long long)nc, w_pbase.data(), probe, (int)np,
                                                   (int)np, (int)m(), d_offs.data(), d_blk_off.data(),
                                                   d_bcodes.data(), d_bvterm.data(), d_ids.data(), (int)k, oid, od,
                                                   on, nullptr, 0, st);
@@ -936,7 +945,7 @@ public:
                     vgpu::launch_lut_fast(rq, (long long)nc, (int)dim, d_cb.data(), (int)m(), (int)ksub, (int)dsub,
                                           w_T.data(), st);
                     cudaEventRecord(ev[3], st);
-                    vgpu::launch_scan_fast2(w_T.data(), rq, (long long)nc, (int)dim, w_probe.data(), w_probe_d.data(),
+                    vgpu::launch_scan_fast2(w_T.data(), rq, (long long)nc, (int)dim, probe, probe_d,
                                             has_rot ? d_rc.data() : nullptr, (int)np, (int)m(), (int)ksub,
                                             d_offs.data(), d_codes.data(), d_vterm.data(), d_ids.data(), (int)k,
                                             oid, od, on, st);
@@ -944,7 +953,7 @@ public:
                 cudaEventRecord(ev[4], st);
             }
             cudaEventRecord(ev[5], st);
-            tm.kernel_launches += 3 + (exact ? 2 : 2) + (has_rot ? 1 : 0) + (tc ? 1 : 0) +
+            tm.kernel_launches += (ext_probe ? 1 : 3) + (exact ? 2 : 2) + (has_rot ? 1 : 0) + (tc ? 1 : 0) +
                                   (!exact && has_blocks ? 1 : 0) + (list_scan ? 12 : 0);
             tm.scan_variant = exact ? 1u : list_scan ? 4u : (has_blocks ? 3u : 2u);
             tm.coarse_variant = tc ? 2u : 1u;
@@ -982,6 +991,45 @@ public:
         sync(st);
         tm.scanned_entries = scanned;
         timings = tm;
+        return {};
+    }
+
+    // ------------------------------------------------------------------ coarse stage only
+    // The probe lists of search_adc's coarse stage (tensor-core screen + exact refine,
+    // or CUDA-core distances): d_probe / d_probe_d [nq x min(nprobe, nlist)].
+    std::expected<void, error> probe_only(const float* dq_all, size_t nq, uint32_t nprobe, uint32_t* d_probe,
+                                          float* d_probe_d) const {
+        if (!trained) return fail(error_code::precondition_failed, "Index must be trained before searching");
+        const uint32_t np = std::min(nprobe, nlist());
+        if (nq == 0 || np == 0) return {};
+        if (np > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "nprobe above 1024 is not supported by the GPU path");
+        std::lock_guard<std::mutex> lock(mu);
+        const size_t qc = std::min(nq, std::max<size_t>(1, kDistBudget / (sizeof(float) * (size_t)nlist())));
+        w_D.reserve(qc * nlist());
+        for (size_t q0 = 0; q0 < nq; q0 += qc) {
+            const size_t nc = std::min(qc, nq - q0);
+            const float* dq = dq_all + q0 * dim;
+            uint32_t* probe = d_probe + q0 * np;
+            float* probe_d = d_probe_d + q0 * np;
+            if (vgpu::use_tensor_cores(dq, d_cent.data(), (int)dim, nlist())) {
+                w_xn.reserve(qc);
+                reset_err();
+                vgpu::launch_row_norms(dq, (long long)nc, (int)dim, w_xn.data(), st);
+                vgpu::launch_tc_screen(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, w_xn.data(),
+                                       d_cn.data(), w_D.data(), (long long)nlist(), d_err.data(), st);
+                vgpu::launch_screen_select(w_D.data(), (long long)nc, (long long)nlist(), (int)nlist(), dq, (int)dim,
+                                           d_cent.data(), w_xn.data(), d_cn.data(), (int)np, nullptr, probe, probe_d,
+                                           d_err.data(), st);
+                sync(st);
+                check_err();
+            } else {
+                vgpu::launch_l2_dist(dq, (long long)nc, d_cent.data(), (int)nlist(), (int)dim, w_D.data(),
+                                     (long long)nlist(), st);
+                vgpu::launch_row_topk(w_D.data(), (long long)nc, (int)nlist(), (long long)nlist(), (int)np, probe,
+                                      probe_d, st);
+            }
+        }
+        sync(st);
         return {};
     }
 
@@ -1090,6 +1138,31 @@ auto IvfPqIndex::search_batch_flat(const float* queries, std::size_t n_queries,
     DeviceGuard g(impl_->dev);
     try {
         return impl_->search_flat(queries, n_queries, params, out_ids, out_dist, out_counts, on_device);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    }
+}
+
+auto IvfPqIndex::probe_device(const float* d_queries, std::size_t n_queries, std::uint32_t nprobe,
+                              std::uint32_t* d_probe, float* d_probe_d) const -> std::expected<void, core::error> {
+    DeviceGuard g(impl_->dev);
+    try {
+        return impl_->probe_only(d_queries, n_queries, nprobe, d_probe, d_probe_d);
+    } catch (const vgpu::CudaError& e) {
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+    }
+}
+
+auto IvfPqIndex::search_batch_device_probed(const float* d_queries, std::size_t n_queries,
+                                            const IvfPqSearchParams& params, const std::uint32_t* d_probe,
+                                            const float* d_probe_d, std::uint64_t* d_out_ids, float* d_out_dist,
+                                            std::uint32_t* d_out_counts) const -> std::expected<void, core::error> {
+    DeviceGuard g(impl_->dev);
+    if (params.use_exact_rerank)
+        return fail(error_code::unsupported, "the search with given probe lists does not support the exact rerank");
+    try {
+        return impl_->search_adc(d_queries, n_queries, params, d_out_ids, d_out_dist, d_out_counts, true, d_probe,
+                                 d_probe_d);
     } catch (const vgpu::CudaError& e) {
         return fail(error_code::internal, e.what(), "ivf_pq.cuda");
     }

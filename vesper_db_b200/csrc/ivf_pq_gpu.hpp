@@ -151,6 +151,18 @@ public:
                            float* out_dist, std::uint32_t* out_counts, bool on_device) const
         -> std::expected<void, core::error>;
 
+    // The coarse stage alone: the nprobe nearest lists of each query (device arrays
+    // [nq x min(nprobe, nlist)], the probe order of search).  With
+    // search_batch_device_probed, ranks that share a query batch can each probe a slice
+    // of it and exchange the lists instead of all probing every query.
+    auto probe_device(const float* d_queries, std::size_t n_queries, std::uint32_t nprobe, std::uint32_t* d_probe,
+                      float* d_probe_d) const -> std::expected<void, core::error>;
+    // Device search with the probe lists given (as probe_device writes them).
+    auto search_batch_device_probed(const float* d_queries, std::size_t n_queries, const IvfPqSearchParams& params,
+                                    const std::uint32_t* d_probe, const float* d_probe_d, std::uint64_t* d_out_ids,
+                                    float* d_out_dist, std::uint32_t* d_out_counts) const
+        -> std::expected<void, core::error>;
+
     // FAST-mode device search that allocates nothing: its temporary buffers come from
     // a fixed 64 MiB device array (noalloc_search.cu) instead of cudaMalloc.
     auto search_batch_device_noalloc(const float* d_queries, std::size_t n_queries,

@@ -330,6 +330,38 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_noalloc(
     });
 }
 
+VESPER_C_API vesper_status_t vesper_ivfpq_probe_device(const vesper_index_t* index, const float* d_q, size_t nq,
+                                                       uint32_t nprobe, uint32_t* d_probe, float* d_probe_d) {
+    if (!index || !index->ivfpq || !d_q || !d_probe || !d_probe_d || nq == 0) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("probe", [&] {
+        auto r = index->ivfpq->probe_device(d_q, nq, nprobe, d_probe, d_probe_d);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
+    const vesper_index_t* index, const float* d_q, size_t nq, const vesper_ivfpq_search_params_ex_t* p,
+    const uint32_t* d_probe, const float* d_probe_d, uint64_t* d_ids, float* d_d, uint32_t* d_counts) {
+    if (!index || !index->ivfpq || !d_q || !p || !d_probe || !d_probe_d || !d_ids || !d_d || nq == 0)
+        return VESPER_ERROR_INVALID_PARAM;
+    if (p->struct_size < VESPER_IVFPQ_SEARCH_PARAMS_EX_V1_SIZE) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    const IvfPqSearchParams sp = ex_params(p);
+    return guarded("search_probed", [&] {
+        auto r = index->ivfpq->search_batch_device_probed(d_q, nq, sp, d_probe, d_probe_d, d_ids, d_d, d_counts);
+        if (!r) {
+            set_error(r.error().message);
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        return VESPER_OK;
+    });
+}
+
 VESPER_C_API vesper_status_t vesper_ivfpq_get_last_timings(const vesper_index_t* index, vesper_ivfpq_timings_t* out) {
     if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
     clear_error();

@@ -176,6 +176,21 @@ class IvfPqIndex:
             self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(ids_ptr), C.c_void_p(d_ptr),
             C.c_void_p(counts_ptr) if counts_ptr else None))
 
+    def probe_device(self, q_ptr: int, nq: int, nprobe: int, probe_ptr: int, probe_d_ptr: int):
+        """The coarse stage alone: probe lists uint32 [nq, min(nprobe, nlist)] and their
+        distances float32 (device addresses)."""
+        _check(self._lib, self._lib.vesper_ivfpq_probe_device(self._h, C.c_void_p(q_ptr), nq, nprobe,
+                                                              C.c_void_p(probe_ptr), C.c_void_p(probe_d_ptr)))
+
+    def search_batch_device_probed(self, q_ptr: int, nq: int, k: int, nprobe: int, probe_ptr: int,
+                                   probe_d_ptr: int, ids_ptr: int, d_ptr: int, counts_ptr: int = 0,
+                                   mode: int = N.SEARCH_FAST):
+        """search_batch_device with the probe lists given (as probe_device writes them)."""
+        p = N.SearchParamsEx(C.sizeof(N.SearchParamsEx), k, nprobe, mode, 0, 0, 0)
+        _check(self._lib, self._lib.vesper_ivfpq_search_batch_device_probed(
+            self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(probe_ptr), C.c_void_p(probe_d_ptr),
+            C.c_void_p(ids_ptr), C.c_void_p(d_ptr), C.c_void_p(counts_ptr) if counts_ptr else None))
+
     def search_batch_device_noalloc(self, q_ptr: int, nq: int, k: int, nprobe: int, ids_ptr: int, d_ptr: int,
                                     counts_ptr: int = 0):
         """Like search_batch_device (FAST mode) but allocating nothing: temporaries live in
