@@ -964,12 +964,13 @@ void launch_build_blocks(const uint8_t* codes, const float* vterm, const uint64_
 }
 
 // Tables in the blocked order, T[q][(g*256 + c)*G + s_lo] = -2 <(Rq)_s, y_sc>.
-// A CTA owns one sub-space group g and 64 codes: it stages those codes' sub-vectors
-// of the group's G sub-spaces in shared memory once, then for each of its queries
-// writes the 64 x G contiguous table entries (thread e -> code e / G, sub-space e % G).
+// A CTA owns one sub-space group g, 64 codes and 32 queries: it stages those codes'
+// sub-vectors and the queries' slices of the group's G sub-spaces in shared memory once,
+// then writes each query's 64 x G contiguous table entries (thread e -> query, code,
+// sub-space), with no barrier between queries.
 namespace {
 constexpr int LB_C = 64;    // codes per CTA
-constexpr int LB_Q = 64;    // queries per CTA
+constexpr int LB_Q = 32;    // queries per CTA
 }
 
 __global__ void __launch_bounds__(256) lut_blocked_kernel(const float* __restrict__ rq, long long nq, int dim,
@@ -977,29 +978,28 @@ __global__ void __launch_bounds__(256) lut_blocked_kernel(const float* __restric
                                                           float* __restrict__ T) {
     extern __shared__ __align__(16) float sm[];
     float* ys = sm;                                 // [LB_C][dsub][G]
-    float* qs = ys + (size_t)LB_C * dsub * G;       // [dsub][G]
+    float* qs = ys + (size_t)LB_C * dsub * G;       // [LB_Q][dsub][G]
     const int g = blockIdx.y, c0 = blockIdx.z * LB_C;
     for (int e = threadIdx.x; e < LB_C * dsub * G; e += blockDim.x) {
         const int s_lo = e % G, t = (e / G) % dsub, c = e / (G * dsub);
         ys[e] = cb[((long long)(g * G + s_lo) * 256 + c0 + c) * dsub + t];
     }
+    // every query's slice of the group's sub-spaces at once (coalesced: t fastest)
     const long long qb = (long long)blockIdx.x * LB_Q;
-    const long long qe = min(nq, qb + LB_Q);
+    const int nqq = (int)min((long long)LB_Q, nq - qb);
+    for (int e = threadIdx.x; e < nqq * dsub * G; e += blockDim.x) {
+        const int qi = e / (dsub * G), r = e % (dsub * G), t = r % dsub, s_lo = r / dsub;
+        qs[(qi * dsub + t) * G + s_lo] = rq[(qb + qi) * dim + (long long)g * G * dsub + r];
+    }
+    __syncthreads();
     const long long row = (long long)m * 256;
-    for (long long q = qb; q < qe; ++q) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < dsub * G; e += blockDim.x) {
-            const int s_lo = e % G, t = e / G;
-            qs[e] = rq[q * dim + (long long)(g * G + s_lo) * dsub + t];
-        }
-        __syncthreads();
-        float* dst = T + q * row + ((long long)g * 256 + c0) * G;
-        for (int e = threadIdx.x; e < LB_C * G; e += blockDim.x) {
-            const int c = e / G, s_lo = e % G;
-            float acc = 0.0f;
-            for (int t = 0; t < dsub; ++t) acc = fmaf(qs[t * G + s_lo], ys[(c * dsub + t) * G + s_lo], acc);
-            dst[e] = -2.0f * acc;
-        }
+    const int per_q = LB_C * G;
+    for (int e = threadIdx.x; e < nqq * per_q; e += blockDim.x) {
+        const int qi = e / per_q, r = e % per_q, c = r / G, s_lo = r % G;
+        float acc = 0.0f;
+        for (int t = 0; t < dsub; ++t)
+            acc = fmaf(qs[(qi * dsub + t) * G + s_lo], ys[(c * dsub + t) * G + s_lo], acc);
+        T[(qb + qi) * row + ((long long)g * 256 + c0) * G + r] = -2.0f * acc;
     }
 }
 
@@ -1007,7 +1007,7 @@ void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb,
                         cudaStream_t st) {
     if (nq <= 0) return;
     const int G = scan_group(m);
-    const size_t smem = ((size_t)LB_C * dsub * G + (size_t)dsub * G) * sizeof(float);
+    const size_t smem = ((size_t)LB_C * dsub * G + (size_t)LB_Q * dsub * G) * sizeof(float);
     if (smem > 200 * 1024) throw CudaError("lut_blocked: sub-space codebook slice too large for shared memory");
     VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(ceil_div(nq, LB_Q), m / G, 256 / LB_C);
