@@ -160,6 +160,75 @@ class Oracle:
             counts)
         return out_ids, out_d, counts
 
+    # ---- the rest of IvfPqIndex's API (src/index/ivf_pq.cpp:4997-5321, 5392-5541) on a
+    # CSR index (list_offsets, ids, codes in list order), restated with the primitives above.
+    @staticmethod
+    def find_entry(ids, vid):
+        """The first entry in list order holding vid (the reference's linear search), or None."""
+        hit = np.flatnonzero(np.asarray(ids, np.uint64) == np.uint64(vid))
+        return int(hit[0]) if hit.size else None
+
+    @staticmethod
+    def list_of(list_offsets, e):
+        return int(np.searchsorted(np.asarray(list_offsets, np.uint64), np.uint64(e), side="right") - 1)
+
+    def reconstruct_entries(self, centroids, R, cb, m, lists, codes):
+        """centroid + apply_rotation_T(decode(code)) (reconstruct, ivf_pq.cpp:5064-5117)."""
+        res = self.pq_decode(codes, cb, m)
+        if R is not None:
+            res = self.rotate_T(res, R)
+        return (_f32(centroids)[np.asarray(lists)] + res).astype(np.float32)
+
+    def reassign(self, centroids, R, cb, m, list_offsets, ids, codes, vid, new_cluster):
+        """reassign_vector (ivf_pq.cpp:5226-5321): remove the entry, re-encode the
+        reconstructed vector against the new centroid, append it to the new list."""
+        offs = np.asarray(list_offsets, np.uint64).astype(np.int64)
+        ids = np.asarray(ids, np.uint64)
+        codes = np.ascontiguousarray(codes, np.uint8)
+        e = self.find_entry(ids, vid)
+        lo = self.list_of(offs, e)
+        vec = self.reconstruct_entries(centroids, R, cb, m, [lo], codes[e:e + 1])
+        r = (vec - _f32(centroids)[new_cluster:new_cluster + 1]).astype(np.float32)
+        if R is not None:
+            r = self.rotate(r, R)
+        code = self.pq_encode(r, cb, m)
+        keep = np.ones(ids.shape[0], bool)
+        keep[e] = False
+        nl = offs.shape[0] - 1
+        new_ids, new_codes, new_offs = [], [], [0]
+        for l in range(nl):
+            sl = slice(offs[l], offs[l + 1])
+            li, lc = ids[sl][keep[sl]], codes[sl][keep[sl]]
+            if l == new_cluster:
+                li = np.concatenate([li, np.array([vid], np.uint64)])
+                lc = np.concatenate([lc, code])
+            new_ids.append(li)
+            new_codes.append(lc)
+            new_offs.append(new_offs[-1] + li.shape[0])
+        return (np.array(new_offs, np.uint64), np.concatenate(new_ids),
+                np.concatenate(new_codes).reshape(-1, m))
+
+    def centroid_rank(self, q, centroids, cluster):
+        """debug_explain_centroid_rank: 1 + #centroids strictly closer than the target's."""
+        d = np.array([self.l2_sq(q, c) for c in _f32(centroids)], np.float32)
+        return int(np.sum(d < d[cluster])) + 1
+
+    def adc_all(self, q, centroids, R, cb, m, list_offsets, codes):
+        """The exact ADC distance of q to every entry (its list's table, reference order)."""
+        offs = np.asarray(list_offsets, np.uint64).astype(np.int64)
+        codes = np.ascontiguousarray(codes, np.uint8)
+        out = np.zeros(codes.shape[0], np.float32)
+        for l in range(offs.shape[0] - 1):
+            if offs[l + 1] == offs[l]:
+                continue
+            r = (_f32(q)[None, :] - _f32(centroids)[l:l + 1]).astype(np.float32)
+            if R is not None:
+                r = self.rotate(r, R)
+            lut = self.pq_lut(r[0], cb, m)
+            for e in range(offs[l], offs[l + 1]):
+                out[e] = self.adc(lut, codes[e])
+        return out
+
     def flat_topk(self, op, q, base, k):
         q, base = _f32(q), _f32(base)
         idx = np.zeros((q.shape[0], k), np.uint32)
@@ -249,6 +318,18 @@ class Reference:
         L.rb_ivfpq_add.argtypes = [C.c_void_p, _u64p, _f32p, _sz]
         L.rb_ivfpq_search_batch.restype = C.c_int
         L.rb_ivfpq_search_batch.argtypes = [C.c_void_p, _f32p, _sz, _u32, _u32, _u64p, _f32p, _u32p]
+        for name, args in {
+                "rb_ivfpq_reconstruct": [C.c_void_p, C.c_uint64, _f32p],
+                "rb_ivfpq_reconstruct_cluster": [C.c_void_p, _u32, _u64p, _f32p, _sz, C.POINTER(C.c_size_t)],
+                "rb_ivfpq_get_cluster_assignment": [C.c_void_p, C.c_uint64, C.POINTER(C.c_uint32)],
+                "rb_ivfpq_update_cluster_centroid": [C.c_void_p, _u32, _f32p],
+                "rb_ivfpq_reassign_vector": [C.c_void_p, C.c_uint64, _u32],
+                "rb_ivfpq_debug_centroid_rank": [C.c_void_p, _f32p, C.c_uint64, C.POINTER(C.c_uint64),
+                                                 C.POINTER(C.c_uint32)],
+                "rb_ivfpq_debug_adc_rank": [C.c_void_p, _f32p, C.c_uint64, C.POINTER(C.c_uint64),
+                                            C.POINTER(C.c_float)]}.items():
+            getattr(L, name).restype = C.c_int
+            getattr(L, name).argtypes = args
         L.rb_flat_buffer_create.restype = C.c_void_p
         L.rb_flat_buffer_create.argtypes = [_f32p, _u32, _sz]
         L.rb_flat_buffer_destroy.argtypes = [C.c_void_p]
@@ -449,6 +530,39 @@ class RefIvfPq:
         if rc != 0:
             raise ValueError(self.ref.error())
         return ids, d, counts
+
+    def reconstruct(self, vid, dim):
+        out = np.zeros(dim, np.float32)
+        rc = self.ref.lib.rb_ivfpq_reconstruct(self.h, vid, out)
+        return rc, out
+
+    def reconstruct_cluster(self, cluster, dim, cap=1 << 20):
+        ids = np.zeros(cap, np.uint64)
+        vec = np.zeros(cap * dim, np.float32)
+        n = C.c_size_t(0)
+        rc = self.ref.lib.rb_ivfpq_reconstruct_cluster(self.h, cluster, ids, vec, cap, C.byref(n))
+        return rc, ids[:n.value], vec[:n.value * dim].reshape(n.value, dim)
+
+    def get_cluster_assignment(self, vid):
+        out = C.c_uint32(0)
+        rc = self.ref.lib.rb_ivfpq_get_cluster_assignment(self.h, vid, C.byref(out))
+        return rc, out.value
+
+    def update_cluster_centroid(self, cluster, c):
+        return self.ref.lib.rb_ivfpq_update_cluster_centroid(self.h, cluster, _f32(c))
+
+    def reassign_vector(self, vid, cluster):
+        return self.ref.lib.rb_ivfpq_reassign_vector(self.h, vid, cluster)
+
+    def debug_centroid_rank(self, q, vid):
+        rank, cl = C.c_uint64(0), C.c_uint32(0)
+        rc = self.ref.lib.rb_ivfpq_debug_centroid_rank(self.h, _f32(q), vid, C.byref(rank), C.byref(cl))
+        return rc, rank.value, cl.value
+
+    def debug_adc_rank(self, q, vid):
+        rank, d = C.c_uint64(0), C.c_float(0)
+        rc = self.ref.lib.rb_ivfpq_debug_adc_rank(self.h, _f32(q), vid, C.byref(rank), C.byref(d))
+        return rc, rank.value, d.value
 
     def save(self, directory):
         if self.ref.lib.rb_ivfpq_save(self.h, directory.encode()) != 0:

@@ -125,6 +125,60 @@ int rb_ivfpq_search_batch_ex(void* h, const float* queries, size_t nq, uint32_t 
     } catch (const std::exception& e) { set_err(e.what()); return 5; }
 }
 
+// The rest of IvfPqIndex's API (ivf_pq.hpp:252-386).  Each returns 0 or the reference's
+// error code number (core::error_code) and writes its outputs.
+static int code_of(const core::error& e) { set_err(e.message); return static_cast<int>(e.code); }
+
+int rb_ivfpq_reconstruct(void* h, uint64_t id, float* out) {
+    auto r = static_cast<RbIndex*>(h)->idx.reconstruct(id);
+    if (!r) return code_of(r.error());
+    std::memcpy(out, r->data(), r->size() * sizeof(float));
+    return 0;
+}
+// out_ids / out_vec must hold the cluster's entries; *n receives their count.
+int rb_ivfpq_reconstruct_cluster(void* h, uint32_t cluster, uint64_t* out_ids, float* out_vec, size_t cap,
+                                 size_t* n) {
+    std::vector<uint64_t> ids;
+    std::vector<float> vec;
+    auto r = static_cast<RbIndex*>(h)->idx.reconstruct_cluster(cluster, ids, vec);
+    if (!r) return code_of(r.error());
+    *n = ids.size();
+    if (ids.size() > cap) return -1;
+    std::memcpy(out_ids, ids.data(), ids.size() * 8);
+    std::memcpy(out_vec, vec.data(), vec.size() * 4);
+    return 0;
+}
+int rb_ivfpq_get_cluster_assignment(void* h, uint64_t id, uint32_t* out) {
+    auto r = static_cast<RbIndex*>(h)->idx.get_cluster_assignment(id);
+    if (!r) return code_of(r.error());
+    *out = *r;
+    return 0;
+}
+int rb_ivfpq_update_cluster_centroid(void* h, uint32_t cluster, const float* c) {
+    auto r = static_cast<RbIndex*>(h)->idx.update_cluster_centroid(cluster, c);
+    if (!r) return code_of(r.error());
+    return 0;
+}
+int rb_ivfpq_reassign_vector(void* h, uint64_t id, uint32_t cluster) {
+    auto r = static_cast<RbIndex*>(h)->idx.reassign_vector(id, cluster);
+    if (!r) return code_of(r.error());
+    return 0;
+}
+int rb_ivfpq_debug_centroid_rank(void* h, const float* q, uint64_t id, uint64_t* rank, uint32_t* cluster) {
+    auto r = static_cast<RbIndex*>(h)->idx.debug_explain_centroid_rank(q, id);
+    if (!r) return code_of(r.error());
+    *rank = r->first;
+    *cluster = r->second;
+    return 0;
+}
+int rb_ivfpq_debug_adc_rank(void* h, const float* q, uint64_t id, uint64_t* rank, float* dist) {
+    auto r = static_cast<RbIndex*>(h)->idx.debug_explain_adc_rank(q, id);
+    if (!r) return code_of(r.error());
+    *rank = r->first;
+    *dist = r->second;
+    return 0;
+}
+
 int rb_ivfpq_save(void* h, const char* dir) {
     auto r = static_cast<RbIndex*>(h)->idx.save(std::string(dir));
     if (!r) { set_err(r.error().message); return 4; }

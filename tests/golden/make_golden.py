@@ -16,6 +16,10 @@ Outputs (all small, committed):
   kmeans_small.npz      reference k-means++ / Elkan / Lloyd / PQ-train outputs
   ivfpq_<case>_rerank.npz  the reference's searches with the exact rerank on the saved
                            indexes (`--rerank-only` regenerates just these)
+  ivfpq_<case>_api.npz     reconstruct / reconstruct_cluster / get_cluster_assignment /
+                           debug rank explanations, and update_cluster_centroid +
+                           reassign_vector with the index they leave (ivfpq_<case>_api/)
+                           (`--api-only` regenerates just these)
 """
 from __future__ import annotations
 
@@ -103,6 +107,57 @@ def make_rerank(ref: Reference):
         print("wrote", name, "rerank")
 
 
+def make_api(ref: Reference):
+    """The rest of IvfPqIndex's API on the saved golden indexes (ivfpq_<case>_api.npz):
+    reconstruct / get_cluster_assignment of some ids (including a missing one),
+    reconstruct_cluster of a few clusters, the debug rank explanations (which need
+    VESPER_IVFPQ_DEBUG=1), then update_cluster_centroid + reassign_vector, saved again
+    (ivfpq_<case>_api/ivfpq.bin)."""
+    os.environ["VESPER_IVFPQ_DEBUG"] = "1"
+    for (name, d, nlist, *_rest) in CASES:
+        data = np.load(os.path.join(HERE, f"ivfpq_{name}.npz"))
+        idx = ref.ivfpq()
+        idx.load(os.path.join(HERE, f"ivfpq_{name}"))
+        nb = data["base"].shape[0]
+        ids = (np.array([0, 1, 5, nb // 2, nb - 1], dtype=np.uint64) * 3 + 7).tolist() + [2]  # 2: not an id
+        res = {"ids": np.array(ids, np.uint64)}
+        rec, rc_rec, asg, rc_asg = [], [], [], []
+        for vid in ids:
+            rc, v = idx.reconstruct(vid, d)
+            rec.append(v); rc_rec.append(rc)
+            rc, a = idx.get_cluster_assignment(vid)
+            asg.append(a); rc_asg.append(rc)
+        res.update(reconstruct=np.array(rec), reconstruct_rc=np.array(rc_rec), assign=np.array(asg, np.uint32),
+                   assign_rc=np.array(rc_asg))
+        for c in (0, nlist // 2, nlist - 1):
+            rc, cids, vec = idx.reconstruct_cluster(c, d)
+            res[f"cluster_{c}_ids"], res[f"cluster_{c}_vec"], res[f"cluster_{c}_rc"] = cids, vec, rc
+        rc, _, _ = idx.reconstruct_cluster(nlist, d)
+        res["cluster_bad_rc"] = rc
+        q = data["queries"][:4]
+        cr, ar = [], []
+        for i, vid in enumerate(ids[:4]):
+            rc, rank, cl = idx.debug_centroid_rank(q[i], vid)
+            cr.append((rc, rank, cl))
+            rc, rank, dist = idx.debug_adc_rank(q[i], vid)
+            ar.append((rc, rank, dist))
+        res["centroid_rank"] = np.array(cr, np.float64)
+        res["adc_rank"] = np.array(ar, np.float64)
+        # mutations: a centroid moved, then three vectors reassigned
+        g = np.random.default_rng(5)
+        newc = g.standard_normal(d).astype(np.float32)
+        res["update_cluster"], res["update_centroid"] = np.uint32(1), newc
+        res["update_rc"] = idx.update_cluster_centroid(1, newc)
+        moves = [(ids[0], nlist - 1), (ids[2], 0), (ids[3], 1)]
+        res["moves"] = np.array(moves, np.uint64)
+        res["move_rc"] = np.array([idx.reassign_vector(v, c) for v, c in moves])
+        out = os.path.join(HERE, f"ivfpq_{name}_api")
+        shutil.rmtree(out, ignore_errors=True)
+        idx.save(out)
+        np.savez_compressed(os.path.join(HERE, f"ivfpq_{name}_api.npz"), **res)
+        print("wrote", name, "api")
+
+
 def make_kmeans(ref: Reference):
     x = mixture(3000, 16, 60, 0.05, 21)
     kpp = ref.kmeanspp_init(x, 48, 42)
@@ -124,7 +179,9 @@ if __name__ == "__main__":
     ref_root = args[0] if args else "/root/reference"
     convert_fixtures(ref_root)
     ref = Reference()
-    if "--rerank-only" not in sys.argv:
+    if "--rerank-only" not in sys.argv and "--api-only" not in sys.argv:
         make_ivfpq(ref)
         make_kmeans(ref)
-    make_rerank(ref)
+    if "--api-only" not in sys.argv:
+        make_rerank(ref)
+    make_api(ref)

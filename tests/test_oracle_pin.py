@@ -74,6 +74,51 @@ def test_golden_rerank(oracle, name):
 
 
 @pytest.mark.parametrize("name", CASES)
+def test_golden_index_api(oracle, name):
+    """reconstruct / get_cluster_assignment / reconstruct_cluster / debug ranks, and the
+    index left by update_cluster_centroid + reassign_vector, against the reference."""
+    from oracle_lib import read_ivfpq_v10
+    f, _, data = golden_case(name)
+    g = np.load(os.path.join(GOLDEN, f"ivfpq_{name}_api.npz"))
+    cent, R, cb, m = f["centroids"], f["rotation"], f["codebooks"], f["m"]
+    offs, ids, codes = f["list_offsets"], f["ids"], f["codes"]
+    for i, vid in enumerate(g["ids"]):
+        e = oracle.find_entry(ids, vid)
+        if e is None:
+            assert g["reconstruct_rc"][i] == 6001 and g["assign_rc"][i] == 6001
+            continue
+        l = oracle.list_of(offs, e)
+        assert g["assign"][i] == l
+        v = oracle.reconstruct_entries(cent, R, cb, m, [l], codes[e:e + 1])[0]
+        assert np.array_equal(v, g["reconstruct"][i])
+    nlist = cent.shape[0]
+    for c in (0, nlist // 2, nlist - 1):
+        sl = slice(int(offs[c]), int(offs[c + 1]))
+        assert np.array_equal(ids[sl], g[f"cluster_{c}_ids"])
+        v = oracle.reconstruct_entries(cent, R, cb, m, [c] * (sl.stop - sl.start), codes[sl])
+        assert np.array_equal(v.reshape(-1, cent.shape[1]), g[f"cluster_{c}_vec"].reshape(-1, cent.shape[1]))
+    q = data["queries"][:4]
+    for i in range(4):
+        vid = g["ids"][i]
+        e = oracle.find_entry(ids, vid)
+        l = oracle.list_of(offs, e)
+        rc, rank, cl = g["centroid_rank"][i]
+        assert rc == 0 and cl == l and rank == oracle.centroid_rank(q[i], cent, l)
+        adc = oracle.adc_all(q[i], cent, R, cb, m, offs, codes)
+        rc, rank, dist = g["adc_rank"][i]
+        assert rc == 0 and np.float32(dist) == adc[e] and rank == int(np.sum(adc < adc[e])) + 1
+    # mutations
+    cent2 = cent.copy()
+    cent2[int(g["update_cluster"])] = g["update_centroid"]
+    for vid, c in g["moves"]:
+        offs, ids, codes = oracle.reassign(cent2, R, cb, m, offs, ids, codes, vid, int(c))
+    f2 = read_ivfpq_v10(os.path.join(GOLDEN, f"ivfpq_{name}_api", "ivfpq.bin"))
+    assert np.array_equal(f2["centroids"], cent2)
+    assert np.array_equal(f2["list_offsets"], offs)
+    assert np.array_equal(f2["ids"], ids) and np.array_equal(f2["codes"], codes)
+
+
+@pytest.mark.parametrize("name", CASES)
 def test_golden_add(oracle, name):
     """Coarse assignment, list order and PQ codes of the reference's add()."""
     f, model, data = golden_case(name)
