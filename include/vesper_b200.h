@@ -131,6 +131,42 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
     const uint32_t* d_probe, const float* d_probe_d, uint64_t* d_out_ids, float* d_out_distances,
     uint32_t* d_out_counts);
 
+/* ---------------------------------------------------------------------------------
+ * The rest of IvfPqIndex's API (include/vesper/index/ivf_pq.hpp:252-386), which the
+ * reference reaches from C++ only.  Vectors are rebuilt exactly as the reference does:
+ * centroid + apply_rotation_T(decode(code)); an id held by several entries resolves to
+ * the first one in list order.  Errors: VESPER_ERROR_NOT_TRAINED before training,
+ * VESPER_ERROR_INVALID_PARAM with the reference's message otherwise ("Vector ID not
+ * found", "Cluster ID out of range", ...).
+ * ------------------------------------------------------------------------------- */
+VESPER_C_API vesper_status_t vesper_ivfpq_reconstruct(const vesper_index_t* index, uint64_t id,
+                                                      float* out_vector /* [dim] */);
+/* Entries of a cluster in list order: *out_count receives their number; ids and vectors
+ * are written when capacity (entries) suffices, else VESPER_ERROR_INVALID_PARAM. */
+VESPER_C_API vesper_status_t vesper_ivfpq_reconstruct_cluster(const vesper_index_t* index, uint32_t cluster_id,
+                                                              uint64_t* out_ids, float* out_vectors,
+                                                              size_t capacity, size_t* out_count);
+VESPER_C_API vesper_status_t vesper_ivfpq_get_cluster_assignment(const vesper_index_t* index, uint64_t id,
+                                                                 uint32_t* out_cluster);
+VESPER_C_API vesper_status_t vesper_ivfpq_get_cluster_centroid(const vesper_index_t* index, uint32_t cluster_id,
+                                                               float* out_centroid /* [dim] */);
+VESPER_C_API vesper_status_t vesper_ivfpq_update_cluster_centroid(vesper_index_t* index, uint32_t cluster_id,
+                                                                  const float* centroid /* [dim] */);
+VESPER_C_API vesper_status_t vesper_ivfpq_reassign_vector(vesper_index_t* index, uint64_t id, uint32_t new_cluster);
+/* compact_inverted_list: removes the cluster's entries whose id, cut to 32 bits, is in
+ * deleted_ids (the reference takes a roaring bitmap of 32-bit ids). */
+VESPER_C_API vesper_status_t vesper_ivfpq_compact_inverted_list(vesper_index_t* index, uint32_t cluster_id,
+                                                                const uint32_t* deleted_ids, size_t n_deleted,
+                                                                size_t* out_removed);
+/* debug_explain_centroid_rank / debug_explain_adc_rank (VESPER_IVFPQ_DEBUG=1 required, as
+ * in the reference): rank = 1 + the number of centroids (entries) strictly closer. */
+VESPER_C_API vesper_status_t vesper_ivfpq_debug_explain_centroid_rank(const vesper_index_t* index,
+                                                                      const float* query, uint64_t target_id,
+                                                                      uint64_t* out_rank, uint32_t* out_cluster);
+VESPER_C_API vesper_status_t vesper_ivfpq_debug_explain_adc_rank(const vesper_index_t* index, const float* query,
+                                                                 uint64_t target_id, uint64_t* out_rank,
+                                                                 float* out_distance);
+
 /* Device time per stage of the last search call (CUDA events, milliseconds). */
 typedef struct vesper_ivfpq_timings_s {
   float coarse_ms;   /* query-centroid distances */

@@ -37,6 +37,10 @@ EXPORTED = [
     "vesper_kmeans_params_init", "vesper_kmeans_fit", "vesper_kmeans_fit_device",
     "vesper_flat_topk", "vesper_flat_topk_device", "vesper_flat_get_last_timings",
     "vesper_ivfpq_probe_device", "vesper_ivfpq_search_batch_device_probed",
+    "vesper_ivfpq_reconstruct", "vesper_ivfpq_reconstruct_cluster", "vesper_ivfpq_get_cluster_assignment",
+    "vesper_ivfpq_get_cluster_centroid", "vesper_ivfpq_update_cluster_centroid", "vesper_ivfpq_reassign_vector",
+    "vesper_ivfpq_compact_inverted_list", "vesper_ivfpq_debug_explain_centroid_rank",
+    "vesper_ivfpq_debug_explain_adc_rank",
 ]
 
 KMEANS_ELKAN = 0
@@ -171,6 +175,16 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_ivfpq_probe_device": (st, [vp, vp, C.c_size_t, C.c_uint32, vp, vp]),
             "vesper_ivfpq_search_batch_device_probed": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx), vp, vp,
                                                              vp, vp, vp]),
+            "vesper_ivfpq_reconstruct": (st, [vp, C.c_uint64, f32p]),
+            "vesper_ivfpq_reconstruct_cluster": (st, [vp, C.c_uint32, u64p, f32p, C.c_size_t,
+                                                      C.POINTER(C.c_size_t)]),
+            "vesper_ivfpq_get_cluster_assignment": (st, [vp, C.c_uint64, u32p]),
+            "vesper_ivfpq_get_cluster_centroid": (st, [vp, C.c_uint32, f32p]),
+            "vesper_ivfpq_update_cluster_centroid": (st, [vp, C.c_uint32, f32p]),
+            "vesper_ivfpq_reassign_vector": (st, [vp, C.c_uint64, C.c_uint32]),
+            "vesper_ivfpq_compact_inverted_list": (st, [vp, C.c_uint32, u32p, C.c_size_t, C.POINTER(C.c_size_t)]),
+            "vesper_ivfpq_debug_explain_centroid_rank": (st, [vp, f32p, C.c_uint64, u64p, u32p]),
+            "vesper_ivfpq_debug_explain_adc_rank": (st, [vp, f32p, C.c_uint64, u64p, f32p]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

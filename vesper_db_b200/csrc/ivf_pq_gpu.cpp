@@ -152,6 +152,9 @@ public:
     mutable DeviceBuffer<uint32_t> d_sent, w_iota, w_pool_n, w_rr_ent, w_rr_lst;
     mutable DeviceBuffer<unsigned char> w_cub;
     mutable DeviceBuffer<float> w_pool_d, w_rr_q, w_rr_dec, w_rr_rot, w_rr_exact;
+    mutable DeviceBuffer<float> w_rc_dec, w_rc_rot;
+    mutable DeviceBuffer<uint32_t> w_lookup;
+    mutable DeviceBuffer<unsigned long long> w_count;
 
     uint32_t nlist() const { return params.nlist; }
     uint32_t m() const { return params.m; }
@@ -724,14 +727,8 @@ public:
             acc.list_fallback_queries += timings.list_fallback_queries;
             acc.list_threshold_ms += timings.list_threshold_ms; acc.list_prep_ms += timings.list_prep_ms;
             acc.list_refine_ms += timings.list_refine_ms; acc.list_fallback_ms += timings.list_fallback_ms;
-            if (!id_map_ok) {
-                d_sid.reserve(std::max<size_t>(n_vectors, 1));
-                d_sent.reserve(std::max<size_t>(n_vectors, 1));
-                vgpu::launch_id_map_build(d_ids.data(), (long long)n_vectors, d_sid.data(), d_sent.data(), w_iota,
-                                          w_cub, st);
-                id_map_ok = true;
-                acc.kernel_launches += 3;
-            }
+            if (!id_map_ok) acc.kernel_launches += 3;
+            ensure_id_map();
             w_rr_ent.reserve(qc * pool);
             w_rr_lst.reserve(qc * pool);
             w_rr_exact.reserve(qc * pool);
@@ -782,6 +779,233 @@ public:
 
     // ext_probe / ext_probe_d (device, [nq x min(nprobe, nlist)]): probe lists computed
     // elsewhere (probe_device, e.g. by another rank); the coarse stage is skipped.
+    // id -> first entry in list order (stable radix sort of the ids); caller holds mu.
+    void ensure_id_map() const {
+        if (id_map_ok) return;
+        d_sid.reserve(std::max<size_t>(n_vectors, 1));
+        d_sent.reserve(std::max<size_t>(n_vectors, 1));
+        vgpu::launch_id_map_build(d_ids.data(), (long long)n_vectors, d_sid.data(), d_sent.data(), w_iota, w_cub, st);
+        id_map_ok = true;
+    }
+
+    // ------------------------------------------------------------------ maintenance / inspection
+    // (src/index/ivf_pq.cpp:4997-5541).  Caller holds mu.
+    // The first entry holding id and its list; false if absent.
+    bool find_entry(uint64_t id, uint32_t& e, uint32_t& l) const {
+        if (n_vectors == 0) return false;
+        ensure_id_map();
+        w_lookup.reserve(2);
+        vgpu::launch_id_lookup(d_sid.data(), d_sent.data(), (long long)n_vectors, id, d_offs.data(), (int)nlist(),
+                               w_lookup.data(), st);
+        uint32_t h[2] = {0, 0};
+        d2h(h, w_lookup.data(), 2, st);
+        sync(st);
+        e = h[0];
+        l = h[1];
+        return e != 0xffffffffu;
+    }
+
+    // Rebuild n entries (device entries/lists, or the range e0.. of one list) into d_out.
+    void reconstruct_rows(const uint32_t* entries, uint64_t e0, const uint32_t* lists, uint32_t list0, size_t n,
+                          float* d_out) const {
+        w_rc_dec.reserve(std::max<size_t>(n * dim, 1));
+        if (has_rot) w_rc_rot.reserve(std::max<size_t>(n * dim, 1));
+        vgpu::launch_reconstruct_rows(entries, e0, lists, list0, (long long)n, d_codes.data(), (int)m(), (int)ksub,
+                                      (int)dsub, d_cb.data(), d_cent.data(), has_rot ? d_rotT.data() : nullptr,
+                                      w_rc_dec.data(), has_rot ? w_rc_rot.data() : nullptr, d_out, st);
+    }
+
+    std::expected<std::vector<float>, error> reconstruct(uint64_t id) const {
+        if (!trained) return fail(error_code::precondition_failed, "Index not trained");
+        std::lock_guard<std::mutex> lock(mu);
+        uint32_t e = 0, l = 0;
+        if (!find_entry(id, e, l)) return fail(error_code::not_found, "Vector ID not found");
+        DeviceBuffer<float> out(dim);
+        reconstruct_rows(nullptr, e, nullptr, l, 1, out.data());
+        std::vector<float> h(dim);
+        d2h(h.data(), out.data(), dim, st);
+        sync(st);
+        return h;
+    }
+
+    std::expected<void, error> reconstruct_cluster(uint32_t c, std::vector<uint64_t>& ids,
+                                                   std::vector<float>& vectors) const {
+        if (!trained) return fail(error_code::precondition_failed, "Index not trained");
+        if (c >= nlist()) return fail(error_code::precondition_failed, "Invalid cluster ID");
+        std::lock_guard<std::mutex> lock(mu);
+        ids.clear();
+        vectors.clear();
+        const uint64_t e0 = h_offs[c], n = h_offs[c + 1] - e0;
+        if (n == 0) return {};
+        ids.resize(n);
+        vectors.resize(n * dim);
+        DeviceBuffer<float> out(n * dim);
+        reconstruct_rows(nullptr, e0, nullptr, c, n, out.data());
+        d2h(ids.data(), d_ids.data() + e0, n, st);
+        d2h(vectors.data(), out.data(), n * dim, st);
+        sync(st);
+        return {};
+    }
+
+    std::expected<uint32_t, error> cluster_assignment(uint64_t id) const {
+        if (!trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.get_cluster_assignment");
+        std::lock_guard<std::mutex> lock(mu);
+        uint32_t e = 0, l = 0;
+        if (!find_entry(id, e, l)) return fail(error_code::not_found, "Vector ID not found", "ivf_pq.get_cluster_assignment");
+        return l;
+    }
+
+    std::expected<void, error> update_centroid(uint32_t c, const float* centroid) {
+        if (!trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.update_cluster_centroid");
+        if (c >= nlist()) return fail(error_code::out_of_range, "Cluster ID out of range", "ivf_pq.update_cluster_centroid");
+        if (!centroid) return fail(error_code::invalid_argument, "Null centroid pointer", "ivf_pq.update_cluster_centroid");
+        std::lock_guard<std::mutex> lock(mu);
+        std::copy(centroid, centroid + dim, h_cent.begin() + (size_t)c * dim);
+        // the centroid and what the search derives from it: its norm, its rotation, and
+        // the per-entry terms of the fast scan
+        h2d(d_cent.data() + (size_t)c * dim, h_cent.data() + (size_t)c * dim, dim, st);
+        vgpu::launch_row_norms(d_cent.data() + (size_t)c * dim, 1, (int)dim, d_cn.data() + c, st);
+        if (has_rot)
+            vgpu::launch_rotate_fast(d_cent.data() + (size_t)c * dim, 1, (int)dim, d_rot.data(),
+                                     d_rc.data() + (size_t)c * dim, st);
+        else
+            d2d(d_rc.data() + (size_t)c * dim, d_cent.data() + (size_t)c * dim, dim, st);
+        recompute_vterms();
+        rebuild_blocks();
+        sync(st);
+        return {};
+    }
+
+    // Move entries so that the new order is `order` (old entry index per new position,
+    // 0xffffffff = the single new entry taken from new_code / new_id); h_offs_new: the
+    // new list offsets.  Codes, ids and everything derived from them are rebuilt.
+    void relayout(const std::vector<uint32_t>& order, const std::vector<uint64_t>& h_offs_new,
+                  const uint8_t* d_new_code, uint64_t new_id) {
+        const size_t n = order.size();
+        DeviceBuffer<uint32_t> d_order(std::max<size_t>(n, 1));
+        h2d(d_order.data(), order.data(), n, st);
+        DeviceBuffer<uint8_t> codes2(std::max<size_t>(n * m(), 1));
+        DeviceBuffer<uint64_t> ids2(std::max<size_t>(n, 1));
+        vgpu::launch_gather_entries(d_order.data(), (long long)n, d_codes.data(), d_ids.data(), (int)m(), d_new_code,
+                                    new_id, codes2.data(), ids2.data(), st);
+        sync(st);  // the old arrays are released below
+        d_codes = std::move(codes2);
+        d_ids = std::move(ids2);
+        h_offs = h_offs_new;
+        h2d(d_offs.data(), h_offs.data(), h_offs.size(), st);
+        n_vectors = n;
+        recompute_vterms();
+        rebuild_blocks();
+        id_map_ok = false;
+        sync(st);
+    }
+
+    std::expected<void, error> reassign(uint64_t id, uint32_t nc) {
+        if (!trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.reassign_vector");
+        if (nc >= nlist()) return fail(error_code::out_of_range, "New cluster ID out of range", "ivf_pq.reassign_vector");
+        std::lock_guard<std::mutex> lock(mu);
+        uint32_t e = 0, lo = 0;
+        if (!find_entry(id, e, lo)) return fail(error_code::not_found, "Vector ID not found", "ivf_pq.reassign_vector");
+        // the stored vector rebuilt, its residual to the new centroid (rotated), encoded
+        DeviceBuffer<float> vec(dim), res(dim);
+        DeviceBuffer<uint32_t> d_nc(1);
+        DeviceBuffer<uint8_t> code(m());
+        reconstruct_rows(nullptr, e, nullptr, lo, 1, vec.data());
+        h2d(d_nc.data(), &nc, 1, st);
+        vgpu::launch_residual_rotate(vec.data(), nullptr, d_cent.data(), d_nc.data(), 1, (int)dim,
+                                     has_rot ? d_rot.data() : nullptr, res.data(), st);
+        vgpu::launch_pq_encode(res.data(), 1, (int)m(), (int)ksub, (int)dsub, d_cb.data(), code.data(), st);
+        // new order: entry e removed, the new entry appended to list nc
+        std::vector<uint32_t> order;
+        order.reserve(n_vectors);
+        std::vector<uint64_t> offs2(nlist() + 1, 0);
+        for (uint32_t l = 0; l < nlist(); ++l) {
+            for (uint64_t i = h_offs[l]; i < h_offs[l + 1]; ++i)
+                if (i != e) order.push_back((uint32_t)i);
+            if (l == nc) order.push_back(0xffffffffu);
+            offs2[l + 1] = order.size();
+        }
+        relayout(order, offs2, code.data(), id);
+        return {};
+    }
+
+    std::expected<size_t, error> compact_list(uint32_t c, const uint32_t* deleted, size_t n_del) {
+        if (!trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.compact_inverted_list");
+        if (c >= nlist()) return fail(error_code::out_of_range, "Cluster ID out of range", "ivf_pq.compact_inverted_list");
+        std::lock_guard<std::mutex> lock(mu);
+        const uint64_t e0 = h_offs[c], n = h_offs[c + 1] - e0;
+        if (n == 0 || n_del == 0 || !deleted) return (size_t)0;
+        std::vector<uint64_t> lid(n);
+        d2h(lid.data(), d_ids.data() + e0, n, st);
+        sync(st);
+        std::vector<uint32_t> del(deleted, deleted + n_del);
+        std::sort(del.begin(), del.end());
+        std::vector<uint32_t> order;
+        order.reserve(n_vectors);
+        std::vector<uint64_t> offs2(nlist() + 1, 0);
+        size_t removed = 0;
+        for (uint32_t l = 0; l < nlist(); ++l) {
+            for (uint64_t i = h_offs[l]; i < h_offs[l + 1]; ++i) {
+                if (l == c && std::binary_search(del.begin(), del.end(), static_cast<uint32_t>(lid[i - e0]))) {
+                    ++removed;
+                    continue;
+                }
+                order.push_back((uint32_t)i);
+            }
+            offs2[l + 1] = order.size();
+        }
+        if (removed) relayout(order, offs2, nullptr, 0);
+        return removed;
+    }
+
+    std::expected<std::pair<size_t, uint32_t>, error> centroid_rank(const float* query, uint64_t id) const {
+        if (!env_flag("VESPER_IVFPQ_DEBUG"))
+            return fail(error_code::precondition_failed, "debug_explain_centroid_rank requires VESPER_IVFPQ_DEBUG=1");
+        if (!trained || n_vectors == 0) return fail(error_code::precondition_failed, "Index must be trained and non-empty");
+        std::lock_guard<std::mutex> lock(mu);
+        uint32_t e = 0, l = 0;
+        if (!find_entry(id, e, l)) return fail(error_code::not_found, "Target ID not found in index");
+        DeviceBuffer<float> q(dim), d(nlist());
+        h2d(q.data(), query, dim, st);
+        vgpu::launch_l2_dist(q.data(), 1, d_cent.data(), (int)nlist(), (int)dim, d.data(), (long long)nlist(), st);
+        w_count.reserve(1);
+        vgpu::check(cudaMemsetAsync(w_count.data(), 0, sizeof(unsigned long long), st), "memset");
+        vgpu::launch_count_less(d.data(), (long long)nlist(), (long long)l, w_count.data(), st);
+        unsigned long long cnt = 0;
+        d2h(&cnt, w_count.data(), 1, st);
+        sync(st);
+        return std::make_pair((size_t)cnt + 1, l);
+    }
+
+    std::expected<std::pair<size_t, float>, error> adc_rank(const float* query, uint64_t id) const {
+        if (!env_flag("VESPER_IVFPQ_DEBUG"))
+            return fail(error_code::precondition_failed, "debug_explain_adc_rank requires VESPER_IVFPQ_DEBUG=1");
+        if (!trained || n_vectors == 0) return fail(error_code::precondition_failed, "Index must be trained and non-empty");
+        std::lock_guard<std::mutex> lock(mu);
+        uint32_t e = 0, l = 0;
+        if (!find_entry(id, e, l)) return fail(error_code::not_found, "Target ID not found in index");
+        // every list's (rotated) query residual in the search's exact order, then every
+        // entry's exact ADC distance
+        DeviceBuffer<float> q(dim), rres((size_t)nlist() * dim), adc(n_vectors);
+        DeviceBuffer<uint32_t> qidx(nlist()), lidx(nlist());
+        h2d(q.data(), query, dim, st);
+        vgpu::check(cudaMemsetAsync(qidx.data(), 0, nlist() * sizeof(uint32_t), st), "memset");
+        vgpu::launch_iota(lidx.data(), nlist(), st);
+        vgpu::launch_residual_rotate(q.data(), qidx.data(), d_cent.data(), lidx.data(), nlist(), (int)dim,
+                                     has_rot ? d_rot.data() : nullptr, rres.data(), st);
+        vgpu::launch_adc_all(rres.data(), (int)dim, (int)nlist(), d_cb.data(), (int)m(), (int)ksub, (int)dsub,
+                             d_offs.data(), d_codes.data(), adc.data(), st);
+        w_count.reserve(1);
+        vgpu::check(cudaMemsetAsync(w_count.data(), 0, sizeof(unsigned long long), st), "memset");
+        vgpu::launch_count_less(adc.data(), (long long)n_vectors, (long long)e, w_count.data(), st);
+        unsigned long long cnt = 0;
+        float dist = 0.0f;
+        d2h(&cnt, w_count.data(), 1, st);
+        d2h(&dist, adc.data() + e, 1, st);
+        sync(st);
+        return std::make_pair((size_t)cnt + 1, dist);
+    }
+
     std::expected<void, error> search_adc(const float* queries, size_t nq, const IvfPqSearchParams& sp,
                                           uint64_t* out_ids, float* out_d, uint32_t* out_n,
                                           bool on_device, const uint32_t* ext_probe = nullptr,
@@ -1225,6 +1449,61 @@ auto IvfPqIndex::is_trained() const noexcept -> bool { return impl_->trained; }
 auto IvfPqIndex::dimension() const noexcept -> std::size_t { return impl_->dim; }
 auto IvfPqIndex::last_search_timings() const -> SearchTimings { return impl_->timings; }
 auto IvfPqIndex::params() const -> IvfPqTrainParams { return impl_->params; }
+
+#define VGPU_GUARDED(expr)                                      \
+    DeviceGuard g(impl_->dev);                                  \
+    try {                                                       \
+        return expr;                                            \
+    } catch (const vgpu::CudaError& e) {                        \
+        return fail(error_code::internal, e.what(), "ivf_pq.cuda"); \
+    }
+
+auto IvfPqIndex::reconstruct_cluster(std::uint32_t cluster_id, std::vector<std::uint64_t>& ids,
+                                     std::vector<float>& vectors) const -> std::expected<void, core::error> {
+    VGPU_GUARDED(impl_->reconstruct_cluster(cluster_id, ids, vectors))
+}
+auto IvfPqIndex::reconstruct(std::uint64_t id) const -> std::expected<std::vector<float>, core::error> {
+    VGPU_GUARDED(impl_->reconstruct(id))
+}
+auto IvfPqIndex::get_num_clusters() const -> std::expected<std::uint32_t, core::error> {
+    if (!impl_->trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.get_num_clusters");
+    return impl_->nlist();
+}
+auto IvfPqIndex::get_dimension() const -> std::expected<std::size_t, core::error> {
+    if (!impl_->trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.get_dimension");
+    return impl_->dim;
+}
+auto IvfPqIndex::get_cluster_assignment(std::uint64_t id) const -> std::expected<std::uint32_t, core::error> {
+    VGPU_GUARDED(impl_->cluster_assignment(id))
+}
+auto IvfPqIndex::get_cluster_centroid(std::uint32_t cluster_id) const
+    -> std::expected<std::vector<float>, core::error> {
+    if (!impl_->trained) return fail(error_code::not_initialized, "Index not trained", "ivf_pq.get_cluster_centroid");
+    if (cluster_id >= impl_->nlist())
+        return fail(error_code::out_of_range, "Cluster ID out of range", "ivf_pq.get_cluster_centroid");
+    const float* c = impl_->h_cent.data() + (size_t)cluster_id * impl_->dim;
+    return std::vector<float>(c, c + impl_->dim);
+}
+auto IvfPqIndex::update_cluster_centroid(std::uint32_t cluster_id, const float* centroid)
+    -> std::expected<void, core::error> {
+    VGPU_GUARDED(impl_->update_centroid(cluster_id, centroid))
+}
+auto IvfPqIndex::reassign_vector(std::uint64_t id, std::uint32_t new_cluster) -> std::expected<void, core::error> {
+    VGPU_GUARDED(impl_->reassign(id, new_cluster))
+}
+auto IvfPqIndex::compact_inverted_list(std::uint32_t cluster_id, const std::uint32_t* deleted_ids,
+                                       std::size_t n_deleted) -> std::expected<std::size_t, core::error> {
+    VGPU_GUARDED(impl_->compact_list(cluster_id, deleted_ids, n_deleted))
+}
+auto IvfPqIndex::debug_explain_centroid_rank(const float* query, std::uint64_t target_id) const
+    -> std::expected<std::pair<std::size_t, std::uint32_t>, core::error> {
+    VGPU_GUARDED(impl_->centroid_rank(query, target_id))
+}
+auto IvfPqIndex::debug_explain_adc_rank(const float* query, std::uint64_t target_id) const
+    -> std::expected<std::pair<std::size_t, float>, core::error> {
+    VGPU_GUARDED(impl_->adc_rank(query, target_id))
+}
+#undef VGPU_GUARDED
 
 auto IvfPqIndex::clear() -> void {
     DeviceGuard g(impl_->dev);

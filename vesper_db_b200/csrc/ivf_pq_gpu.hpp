@@ -35,6 +35,7 @@ enum class error_code : std::uint32_t {
     not_found = 6001,
     internal = 9001,
     invalid_argument = 9002,
+    not_initialized = 9003,
     out_of_range = 9004,
     unsupported = 9005,
 };
@@ -169,6 +170,33 @@ public:
                                      const IvfPqSearchParams& params, std::uint64_t* d_out_ids,
                                      float* d_out_dist, std::uint32_t* d_out_counts) const
         -> std::expected<void, core::error>;
+
+    // The rest of the reference's index API (include/vesper/index/ivf_pq.hpp:252-386).
+    // Vectors are rebuilt exactly as the reference does: centroid + apply_rotation_T(decode).
+    // An id held by several entries resolves to the first in list order.
+    auto reconstruct_cluster(std::uint32_t cluster_id, std::vector<std::uint64_t>& ids,
+                             std::vector<float>& vectors) const -> std::expected<void, core::error>;
+    auto reconstruct(std::uint64_t id) const -> std::expected<std::vector<float>, core::error>;
+    auto get_vector(std::uint64_t id) const -> std::expected<std::vector<float>, core::error> {
+        return reconstruct(id);
+    }
+    auto get_num_clusters() const -> std::expected<std::uint32_t, core::error>;
+    auto get_dimension() const -> std::expected<std::size_t, core::error>;
+    auto get_cluster_assignment(std::uint64_t id) const -> std::expected<std::uint32_t, core::error>;
+    auto get_cluster_centroid(std::uint32_t cluster_id) const -> std::expected<std::vector<float>, core::error>;
+    auto update_cluster_centroid(std::uint32_t cluster_id, const float* centroid)
+        -> std::expected<void, core::error>;
+    auto reassign_vector(std::uint64_t id, std::uint32_t new_cluster) -> std::expected<void, core::error>;
+    // compact_inverted_list with the deleted ids given as a 32-bit id set (the reference
+    // takes a roaring bitmap and tests static_cast<uint32_t>(id)); returns the number removed.
+    auto compact_inverted_list(std::uint32_t cluster_id, const std::uint32_t* deleted_ids, std::size_t n_deleted)
+        -> std::expected<std::size_t, core::error>;
+    // Require VESPER_IVFPQ_DEBUG=1 like the reference.  (rank, assigned cluster) and
+    // (rank, exact ADC distance); ranks are 1 + the number of strictly smaller values.
+    auto debug_explain_centroid_rank(const float* query, std::uint64_t target_id) const
+        -> std::expected<std::pair<std::size_t, std::uint32_t>, core::error>;
+    auto debug_explain_adc_rank(const float* query, std::uint64_t target_id) const
+        -> std::expected<std::pair<std::size_t, float>, core::error>;
 
     void set_metadata_json(std::string_view json);
     auto get_metadata_json() const -> std::string;

@@ -178,4 +178,24 @@ struct RerankArgs {
 };
 void launch_rerank(const RerankArgs& a, cudaStream_t st);
 
+// ----------------------------------------------------------------------- index maintenance (index_ops.cu)
+// out[i] = cent[list(i)] + rotT-rotated decode(codes[entry(i)]) in the reference's order;
+// entry(i) = entries ? entries[i] : e0 + i, list(i) = lists ? lists[i] : list0; rotT may be
+// null (no rotation).  tmp_dec / tmp_rot: [n x dim] scratch.
+void launch_reconstruct_rows(const uint32_t* entries, unsigned long long e0, const uint32_t* lists, uint32_t list0,
+                             long long n, const uint8_t* codes, int m, int ksub, int dsub, const float* cb,
+                             const float* cent, const float* rotT, float* tmp_dec, float* tmp_rot, float* out,
+                             cudaStream_t st);
+// adc[e] = exact ADC distance of entry e from its list's table built from rres[list].
+void launch_adc_all(const float* rres, int dim, int nlist, const float* cb, int m, int ksub, int dsub,
+                    const uint64_t* offs, const uint8_t* codes, float* adc, cudaStream_t st);
+void launch_count_less(const float* v, long long n, long long target, unsigned long long* count, cudaStream_t st);
+// codes2 / ids2 in the new entry order (order[i] = old entry, 0xffffffff = the new entry).
+void launch_gather_entries(const uint32_t* order, long long n, const uint8_t* codes, const uint64_t* ids, int m,
+                           const uint8_t* new_code, uint64_t new_id, uint8_t* codes2, uint64_t* ids2,
+                           cudaStream_t st);
+// out[0] = first entry holding id (0xffffffff if none), out[1] = its list.
+void launch_id_lookup(const uint64_t* sid, const uint32_t* sent, long long n, uint64_t id, const uint64_t* offs,
+                      int nlist, uint32_t* out, cudaStream_t st);
+
 }  // namespace vgpu

@@ -13,6 +13,7 @@
 #include <memory>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/vesper_b200.h"
 #include "ivf_pq_gpu.hpp"
@@ -359,6 +360,129 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
             return VESPER_ERROR_INVALID_PARAM;
         }
         return VESPER_OK;
+    });
+}
+
+}  // extern "C"
+
+namespace {
+// Status of an index-API result: not trained -> NOT_TRAINED, other errors -> INVALID_PARAM
+// with the message.
+template <class R>
+vesper_status_t api_status(const R& r) {
+    if (r) return VESPER_OK;
+    set_error(r.error().message);
+    using vesper::core::error_code;
+    return r.error().code == error_code::not_initialized || r.error().message == "Index not trained"
+               ? VESPER_ERROR_NOT_TRAINED
+               : (r.error().code == error_code::internal ? VESPER_ERROR_INTERNAL : VESPER_ERROR_INVALID_PARAM);
+}
+}  // namespace
+
+extern "C" {
+
+VESPER_C_API vesper_status_t vesper_ivfpq_reconstruct(const vesper_index_t* index, uint64_t id, float* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("reconstruct", [&] {
+        auto r = index->ivfpq->reconstruct(id);
+        if (r) std::memcpy(out, r->data(), r->size() * sizeof(float));
+        return api_status(r);
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_reconstruct_cluster(const vesper_index_t* index, uint32_t cluster_id,
+                                                              uint64_t* out_ids, float* out_vectors, size_t capacity,
+                                                              size_t* out_count) {
+    if (!index || !index->ivfpq || !out_count) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("reconstruct_cluster", [&] {
+        std::vector<uint64_t> ids;
+        std::vector<float> vec;
+        auto r = index->ivfpq->reconstruct_cluster(cluster_id, ids, vec);
+        if (!r) return api_status(r);
+        *out_count = ids.size();
+        if (ids.size() > capacity || (!ids.empty() && (!out_ids || !out_vectors))) {
+            set_error("reconstruct_cluster: output capacity too small");
+            return VESPER_ERROR_INVALID_PARAM;
+        }
+        if (!ids.empty()) {
+            std::memcpy(out_ids, ids.data(), ids.size() * sizeof(uint64_t));
+            std::memcpy(out_vectors, vec.data(), vec.size() * sizeof(float));
+        }
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_cluster_assignment(const vesper_index_t* index, uint64_t id,
+                                                                 uint32_t* out_cluster) {
+    if (!index || !index->ivfpq || !out_cluster) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("get_cluster_assignment", [&] {
+        auto r = index->ivfpq->get_cluster_assignment(id);
+        if (r) *out_cluster = *r;
+        return api_status(r);
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_get_cluster_centroid(const vesper_index_t* index, uint32_t cluster_id,
+                                                               float* out) {
+    if (!index || !index->ivfpq || !out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("get_cluster_centroid", [&] {
+        auto r = index->ivfpq->get_cluster_centroid(cluster_id);
+        if (r) std::memcpy(out, r->data(), r->size() * sizeof(float));
+        return api_status(r);
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_update_cluster_centroid(vesper_index_t* index, uint32_t cluster_id,
+                                                                  const float* centroid) {
+    if (!index || !index->ivfpq) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("update_cluster_centroid",
+                   [&] { return api_status(index->ivfpq->update_cluster_centroid(cluster_id, centroid)); });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_reassign_vector(vesper_index_t* index, uint64_t id, uint32_t new_cluster) {
+    if (!index || !index->ivfpq) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("reassign_vector", [&] { return api_status(index->ivfpq->reassign_vector(id, new_cluster)); });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_compact_inverted_list(vesper_index_t* index, uint32_t cluster_id,
+                                                                const uint32_t* deleted_ids, size_t n_deleted,
+                                                                size_t* out_removed) {
+    if (!index || !index->ivfpq || (n_deleted && !deleted_ids)) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("compact_inverted_list", [&] {
+        auto r = index->ivfpq->compact_inverted_list(cluster_id, deleted_ids, n_deleted);
+        if (r && out_removed) *out_removed = *r;
+        return api_status(r);
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_debug_explain_centroid_rank(const vesper_index_t* index, const float* query,
+                                                                      uint64_t target_id, uint64_t* out_rank,
+                                                                      uint32_t* out_cluster) {
+    if (!index || !index->ivfpq || !query || !out_rank || !out_cluster) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("debug_explain_centroid_rank", [&] {
+        auto r = index->ivfpq->debug_explain_centroid_rank(query, target_id);
+        if (r) { *out_rank = r->first; *out_cluster = r->second; }
+        return api_status(r);
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_ivfpq_debug_explain_adc_rank(const vesper_index_t* index, const float* query,
+                                                                 uint64_t target_id, uint64_t* out_rank,
+                                                                 float* out_distance) {
+    if (!index || !index->ivfpq || !query || !out_rank || !out_distance) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("debug_explain_adc_rank", [&] {
+        auto r = index->ivfpq->debug_explain_adc_rank(query, target_id);
+        if (r) { *out_rank = r->first; *out_distance = r->second; }
+        return api_status(r);
     });
 }
 

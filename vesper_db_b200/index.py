@@ -191,6 +191,66 @@ class IvfPqIndex:
             self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(probe_ptr), C.c_void_p(probe_d_ptr),
             C.c_void_p(ids_ptr), C.c_void_p(d_ptr), C.c_void_p(counts_ptr) if counts_ptr else None))
 
+    # ------------------------------------------------------------------ the rest of the index API
+    # (IvfPqIndex::reconstruct & co., include/vesper/index/ivf_pq.hpp:252-386)
+    def reconstruct(self, vid: int) -> np.ndarray:
+        out = np.zeros(self.dimension(), np.float32)
+        _check(self._lib, self._lib.vesper_ivfpq_reconstruct(self._h, vid, _ptr(out, C.c_float)))
+        return out
+
+    get_vector = reconstruct
+
+    def reconstruct_cluster(self, cluster_id: int):
+        """(ids uint64 [n], vectors float32 [n, dim]) of the cluster, list order."""
+        n = C.c_size_t(0)
+        st = self._lib.vesper_ivfpq_reconstruct_cluster(self._h, cluster_id, None, None, 0, C.byref(n))
+        if st != N.VESPER_OK and n.value == 0:
+            _check(self._lib, st)  # an error other than the capacity probe
+        dim = self.dimension()
+        ids = np.zeros(max(1, n.value), np.uint64)
+        vec = np.zeros(max(1, n.value) * dim, np.float32)
+        _check(self._lib, self._lib.vesper_ivfpq_reconstruct_cluster(self._h, cluster_id, _ptr(ids, C.c_uint64),
+                                                                     _ptr(vec, C.c_float), ids.shape[0], C.byref(n)))
+        return ids[:n.value], vec[:n.value * dim].reshape(n.value, dim)
+
+    def get_cluster_assignment(self, vid: int) -> int:
+        out = C.c_uint32(0)
+        _check(self._lib, self._lib.vesper_ivfpq_get_cluster_assignment(self._h, vid, C.byref(out)))
+        return out.value
+
+    def get_cluster_centroid(self, cluster_id: int) -> np.ndarray:
+        out = np.zeros(self.dimension(), np.float32)
+        _check(self._lib, self._lib.vesper_ivfpq_get_cluster_centroid(self._h, cluster_id, _ptr(out, C.c_float)))
+        return out
+
+    def update_cluster_centroid(self, cluster_id: int, centroid):
+        c = _f32(centroid)
+        _check(self._lib, self._lib.vesper_ivfpq_update_cluster_centroid(self._h, cluster_id, _ptr(c, C.c_float)))
+
+    def reassign_vector(self, vid: int, new_cluster: int):
+        _check(self._lib, self._lib.vesper_ivfpq_reassign_vector(self._h, vid, new_cluster))
+
+    def compact_inverted_list(self, cluster_id: int, deleted_ids) -> int:
+        d = np.ascontiguousarray(deleted_ids, np.uint32)
+        out = C.c_size_t(0)
+        _check(self._lib, self._lib.vesper_ivfpq_compact_inverted_list(self._h, cluster_id, _ptr(d, C.c_uint32),
+                                                                       d.shape[0], C.byref(out)))
+        return out.value
+
+    def debug_explain_centroid_rank(self, query, vid: int):
+        q = _f32(query).reshape(-1)
+        rank, cl = C.c_uint64(0), C.c_uint32(0)
+        _check(self._lib, self._lib.vesper_ivfpq_debug_explain_centroid_rank(self._h, _ptr(q, C.c_float), vid,
+                                                                             C.byref(rank), C.byref(cl)))
+        return rank.value, cl.value
+
+    def debug_explain_adc_rank(self, query, vid: int):
+        q = _f32(query).reshape(-1)
+        rank, d = C.c_uint64(0), C.c_float(0)
+        _check(self._lib, self._lib.vesper_ivfpq_debug_explain_adc_rank(self._h, _ptr(q, C.c_float), vid,
+                                                                        C.byref(rank), C.byref(d)))
+        return rank.value, d.value
+
     def search_batch_device_noalloc(self, q_ptr: int, nq: int, k: int, nprobe: int, ids_ptr: int, d_ptr: int,
                                     counts_ptr: int = 0):
         """Like search_batch_device (FAST mode) but allocating nothing: temporaries live in
