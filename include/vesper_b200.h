@@ -216,8 +216,8 @@ VESPER_C_API vesper_status_t vesper_ivfpq_get_lists(const vesper_index_t* index,
  *          the inertia the loop stopped at (the reference's return value);
  *   LLOYD  one run of kmeans_cluster (n_redo = 1): lowest index wins a tie, fp64 sum /
  *          count, and after the loop one more mean update and the inertia of the final
- *          assignment (an fp64 sum of per-point distances; the reference sums it in a
- *          float running total, which differs by that total's rounding).
+ *          assignment, the reference's float running total over every (point,
+ *          dimension) term in order.
  * Errors as the reference: k == 0 or n < k -> VESPER_ERROR_INVALID_PARAM with its message. */
 typedef enum vesper_kmeans_algorithm_e { VESPER_KMEANS_ELKAN = 0, VESPER_KMEANS_LLOYD = 1 } vesper_kmeans_algorithm_t;
 
@@ -250,6 +250,62 @@ VESPER_C_API vesper_status_t vesper_kmeans_fit(const float* data, size_t n, size
 VESPER_C_API vesper_status_t vesper_kmeans_fit_device(const float* d_data, size_t n, size_t dim,
                                                       const vesper_kmeans_params_t* params, float* d_out_centroids,
                                                       uint32_t* d_out_assignments, vesper_kmeans_result_t* out_result);
+
+/* k-means over points sharded across GPUs (one process per GPU).  The building blocks
+ * of the fit above, for a driver that owns the collectives (vesper_db_b200.shard
+ * .kmeans_fit_sharded runs them over torch.distributed / NCCL).  Points are split into
+ * contiguous shards in point order; centroids are replicated.  Per iteration every
+ * shard assigns its own points (vesper_kmeans_shard_assign), the per-point distances
+ * are gathered for the fp64 inertia in point order, and the mean update runs as a
+ * chain in shard order: each shard continues the (sum, Kahan compensation, count)
+ * state the previous shard left (vesper_kmeans_shard_accumulate, state [k x dim] f64,
+ * [k x dim] f64, [k] u64, zero before the first shard) and the last one turns it into
+ * centroids (vesper_kmeans_shard_finish), which are then broadcast.  The chain keeps
+ * the reference's sums in point order, so the sharded fit equals the one-GPU fit bit
+ * for bit.  k-means++ draws use vesper_kmeanspp_sampler_* on the gathered D^2 vector.
+ * All pointers but the sampler's d2 are device memory of the handle's device; every
+ * call's outputs are complete when it returns, and its inputs must be complete when
+ * it starts. */
+typedef struct vesper_kmeans_shard_s vesper_kmeans_shard_t;
+
+/* A handle on the calling thread's current device (own stream and scratch). */
+VESPER_C_API vesper_status_t vesper_kmeans_shard_create(vesper_kmeans_shard_t** out);
+VESPER_C_API void vesper_kmeans_shard_destroy(vesper_kmeans_shard_t* shard);
+/* Nearest centroid of each of the n rows of x (reference lane order; the lowest index
+ * wins a tie, or, with keep_on_tie, the current d_assign entry does).  d_min_dist may
+ * be NULL. */
+VESPER_C_API vesper_status_t vesper_kmeans_shard_assign(vesper_kmeans_shard_t* shard, const float* d_x, size_t n,
+                                                        size_t dim, const float* d_centroids, uint32_t k,
+                                                        int keep_on_tie, uint32_t* d_assign, float* d_min_dist);
+/* k-means++ D^2 refresh: d_min_dist[i] = min(d_min_dist[i], l2(x_i, centroid)). */
+VESPER_C_API vesper_status_t vesper_kmeans_shard_pp_update(vesper_kmeans_shard_t* shard, const float* d_x, size_t n,
+                                                           size_t dim, const float* d_centroid, float* d_min_dist);
+/* This shard's part of the mean update (algorithm: ELKAN = Kahan, LLOYD = plain sum). */
+VESPER_C_API vesper_status_t vesper_kmeans_shard_accumulate(vesper_kmeans_shard_t* shard, const float* d_x, size_t n,
+                                                            size_t dim, const uint32_t* d_assign, uint32_t k,
+                                                            uint32_t algorithm, double* d_sum, double* d_comp,
+                                                            uint64_t* d_count);
+/* Centroids from the final state; a cluster with count 0 keeps its centroid. */
+VESPER_C_API vesper_status_t vesper_kmeans_shard_finish(vesper_kmeans_shard_t* shard, const double* d_sum,
+                                                        const uint64_t* d_count, uint32_t k, size_t dim,
+                                                        uint32_t algorithm, float* d_centroids);
+/* LLOYD's final inertia (kmeans.cpp:230-241), a float running total over every
+ * (point, dimension) term (x - c)^2 in point order: *inout_total (host) is continued
+ * over this shard's points.  Start from 0 on the first shard and pass the total along
+ * in shard order. */
+VESPER_C_API vesper_status_t vesper_kmeans_shard_running_inertia(vesper_kmeans_shard_t* shard, const float* d_x,
+                                                                 size_t n, size_t dim, const float* d_centroids,
+                                                                 const uint32_t* d_assign, float* inout_total);
+
+/* The k-means++ draws of kmeans_plusplus_init (src/index/kmeans.cpp:45-89) for n points:
+ * create returns the first row; next takes the D^2 value of every point (host, n
+ * floats, point order) and returns the next row. */
+typedef struct vesper_kmeanspp_sampler_s vesper_kmeanspp_sampler_t;
+VESPER_C_API vesper_status_t vesper_kmeanspp_sampler_create(uint32_t seed, size_t n, vesper_kmeanspp_sampler_t** out,
+                                                            size_t* first_index);
+VESPER_C_API vesper_status_t vesper_kmeanspp_sampler_next(vesper_kmeanspp_sampler_t* sampler, const float* d2,
+                                                          size_t* index);
+VESPER_C_API void vesper_kmeanspp_sampler_destroy(vesper_kmeanspp_sampler_t* sampler);
 
 /* ---------------------------------------------------------------------------------
  * Exact flat top-k: find_nearest_centroids_batch_fused

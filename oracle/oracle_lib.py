@@ -341,6 +341,10 @@ class Reference:
         L.rb_ivfpq_save.argtypes = [C.c_void_p, C.c_char_p]
         L.rb_ivfpq_load.restype = C.c_int
         L.rb_ivfpq_load.argtypes = [C.c_void_p, C.c_char_p]
+        L.rb_ivfpq_set_metadata_json.restype = None
+        L.rb_ivfpq_set_metadata_json.argtypes = [C.c_void_p, C.c_char_p]
+        L.rb_ivfpq_get_metadata_json.restype = C.c_size_t
+        L.rb_ivfpq_get_metadata_json.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
         L.rb_kmeanspp_init.argtypes = [_f32p, _sz, _sz, _u32, _u32, _f32p]
         for fn in ("rb_kmeans_elkan", "rb_kmeans_lloyd"):
             getattr(L, fn).restype = C.c_int
@@ -572,37 +576,25 @@ class RefIvfPq:
         if self.ref.lib.rb_ivfpq_load(self.h, directory.encode()) != 0:
             raise IOError(self.ref.error())
 
+    def set_metadata_json(self, js: str):
+        self.ref.lib.rb_ivfpq_set_metadata_json(self.h, js.encode())
 
-def read_ivfpq_v10(path: str) -> dict:
-    """Parse an ``ivfpq.bin`` v1.0 file (the layout IvfPqIndex::save writes,
-    src/index/ivf_pq.cpp:4412-4490) into arrays: centroids, codebooks [m*ksub, dsub],
-    rotation or None, and the inverted lists as CSR (list_offsets, ids, codes) in
-    list order, entries in file order.  Verifies the FNV-1a-64 trailer."""
-    raw = open(path, "rb").read()
-    if raw[:8] != b"IVFPQv10":
-        raise ValueError("not a v1.0 IVF-PQ file")
+    def get_metadata_json(self) -> str:
+        n = self.ref.lib.rb_ivfpq_get_metadata_json(self.h, None, 0)
+        buf = C.create_string_buffer(n + 1)
+        self.ref.lib.rb_ivfpq_get_metadata_json(self.h, buf, n + 1)
+        return buf.value.decode()
+
+
+def _fnv1a64(data: bytes) -> int:
     h = 1469598103934665603
-    body = raw[:-12]
-    arr = np.frombuffer(body, np.uint8)
-    # FNV-1a 64 over the body (vectorised in chunks would be faster; files here are small)
-    for b in arr.tobytes():
+    for b in data:
         h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
-    if raw[-12:-8] != b"CHKS" or int.from_bytes(raw[-8:], "little") != h:
-        raise ValueError("checksum mismatch")
-    off = 8
-    ver_major, ver_minor = np.frombuffer(raw, np.uint16, 2, off); off += 4
-    flags, dim, nlist, m, nbits, dsub = np.frombuffer(raw, np.uint32, 6, off); off += 24
-    nvec = int(np.frombuffer(raw, np.uint64, 1, off)[0]); off += 8
-    code_size = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4
-    off += 8  # build timestamp
-    meta_len = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4 + meta_len
-    dim, nlist, m, nbits, dsub = int(dim), int(nlist), int(m), int(nbits), int(dsub)
-    cent = np.frombuffer(raw, np.float32, nlist * dim, off).reshape(nlist, dim).copy(); off += nlist * dim * 4
-    ksub = 1 << nbits
-    cb = np.frombuffer(raw, np.float32, m * ksub * dsub, off).reshape(m * ksub, dsub).copy(); off += cb.nbytes
-    R = None
-    if flags & 1:
-        R = np.frombuffer(raw, np.float32, dim * dim, off).reshape(dim, dim).copy(); off += R.nbytes
+    return h
+
+
+def _parse_lists(raw: bytes, off: int, m: int):
+    """[lists_count u32][per list: size u64, size x (id u64, m code bytes)] -> CSR."""
     lists_count = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4
     offs = np.zeros(lists_count + 1, np.uint64)
     ids, codes = [], []
@@ -612,7 +604,70 @@ def read_ivfpq_v10(path: str) -> dict:
         ids.append(rec[:, :8].copy().view(np.uint64).reshape(-1))
         codes.append(rec[:, 8:].copy())
         offs[li + 1] = offs[li] + sz
-    return dict(dim=dim, nlist=nlist, m=m, nbits=nbits, dsub=dsub, nvec=nvec, flags=int(flags),
-                centroids=cent, codebooks=cb, rotation=R, list_offsets=offs,
-                ids=np.concatenate(ids) if ids else np.zeros(0, np.uint64),
-                codes=np.concatenate(codes) if codes else np.zeros((0, m), np.uint8))
+    return off, offs, (np.concatenate(ids) if ids else np.zeros(0, np.uint64)), \
+        (np.concatenate(codes) if codes else np.zeros((0, m), np.uint8))
+
+
+def read_ivfpq(path: str) -> dict:
+    """Parse an ``ivfpq.bin`` file as IvfPqIndex::save writes it (src/index/ivf_pq.cpp:
+    4270-4491), v1.0 monolithic or v1.1 sectioned (uncompressed sections), into arrays:
+    centroids, codebooks [m*ksub, dsub], rotation or None, metadata (str), and the
+    inverted lists as CSR (list_offsets, ids, codes) in list order, entries in file
+    order.  Verifies the FNV-1a-64 trailer and, for v1.1, every section checksum;
+    `sections` lists the v1.1 section types in file order."""
+    raw = open(path, "rb").read()
+    magic = raw[:8]
+    if magic not in (b"IVFPQv10", b"IVFPQv11"):
+        raise ValueError("not an IVF-PQ file")
+    v11 = magic == b"IVFPQv11"
+    if raw[-12:-8] != b"CHKS" or int.from_bytes(raw[-8:], "little") != _fnv1a64(raw[:-12]):
+        raise ValueError("checksum mismatch")
+    off = 8
+    ver_major, ver_minor = np.frombuffer(raw, np.uint16, 2, off); off += 4
+    flags, dim, nlist, m, nbits, dsub = np.frombuffer(raw, np.uint32, 6, off); off += 24
+    nvec = int(np.frombuffer(raw, np.uint64, 1, off)[0]); off += 8
+    code_size = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4
+    off += 8  # build timestamp
+    meta_len = int(np.frombuffer(raw, np.uint32, 1, off)[0]); off += 4
+    meta = raw[off:off + meta_len].decode(); off += meta_len
+    dim, nlist, m, nbits, dsub = int(dim), int(nlist), int(m), int(nbits), int(dsub)
+    ksub = 1 << nbits
+    R = None
+    sections = []
+    if v11:
+        end = len(raw) - 12
+        payloads = {}
+        while off + 28 <= end:
+            typ = int(np.frombuffer(raw, np.uint32, 1, off)[0])
+            unc, comp, shash = (int(v) for v in np.frombuffer(raw, np.uint64, 3, off + 4))
+            off += 28
+            if comp != unc:
+                raise ValueError("compressed section")
+            data = raw[off:off + comp]; off += comp
+            if _fnv1a64(data) != shash:
+                raise ValueError("section checksum mismatch")
+            sections.append(typ)
+            payloads[typ] = data
+        cent = np.frombuffer(payloads[1], np.float32).reshape(nlist, dim).copy()
+        cb = np.frombuffer(payloads[2], np.float32).reshape(m * ksub, dsub).copy()
+        if 4 in payloads:
+            R = np.frombuffer(payloads[4], np.float32).reshape(dim, dim).copy()
+        if 5 in payloads:
+            meta = payloads[5].decode()
+        _, offs, ids, codes = _parse_lists(payloads[3], 0, m)
+    else:
+        cent = np.frombuffer(raw, np.float32, nlist * dim, off).reshape(nlist, dim).copy(); off += nlist * dim * 4
+        cb = np.frombuffer(raw, np.float32, m * ksub * dsub, off).reshape(m * ksub, dsub).copy(); off += cb.nbytes
+        if flags & 1:
+            R = np.frombuffer(raw, np.float32, dim * dim, off).reshape(dim, dim).copy(); off += R.nbytes
+        _, offs, ids, codes = _parse_lists(raw, off, m)
+    return dict(version=(int(ver_major), int(ver_minor)), dim=dim, nlist=nlist, m=m, nbits=nbits, dsub=dsub,
+                nvec=nvec, flags=int(flags), code_size=code_size, centroids=cent, codebooks=cb, rotation=R,
+                metadata=meta, sections=sections, list_offsets=offs, ids=ids, codes=codes)
+
+
+def read_ivfpq_v10(path: str) -> dict:
+    """read_ivfpq restricted to v1.0 files."""
+    if open(path, "rb").read(8) != b"IVFPQv10":
+        raise ValueError("not a v1.0 IVF-PQ file")
+    return read_ivfpq(path)

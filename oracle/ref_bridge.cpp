@@ -185,6 +185,18 @@ int rb_ivfpq_save(void* h, const char* dir) {
     return 0;
 }
 
+void rb_ivfpq_set_metadata_json(void* h, const char* js) { static_cast<RbIndex*>(h)->idx.set_metadata_json(js); }
+// Copies up to cap-1 bytes (NUL-terminated) and returns the full length.
+size_t rb_ivfpq_get_metadata_json(void* h, char* out, size_t cap) {
+    const std::string s = static_cast<RbIndex*>(h)->idx.get_metadata_json();
+    if (out && cap) {
+        const size_t n = std::min(cap - 1, s.size());
+        std::memcpy(out, s.data(), n);
+        out[n] = 0;
+    }
+    return s.size();
+}
+
 int rb_ivfpq_load(void* h, const char* dir) {
     auto r = IvfPqIndex::load(std::string(dir));
     if (!r) { set_err(r.error().message); return 4; }

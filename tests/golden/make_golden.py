@@ -20,6 +20,10 @@ Outputs (all small, committed):
                            debug rank explanations, and update_cluster_centroid +
                            reassign_vector with the index they leave (ivfpq_<case>_api/)
                            (`--api-only` regenerates just these)
+  ivfpq_<case>_v11/ivfpq.bin  the golden index re-saved by the reference in the v1.1
+                              sectioned layout (VESPER_IVFPQ_SAVE_V11=1), one case with
+                              JSON metadata; ivfpq_v11.json records the metadata and the
+                              reference's answers to invalid metadata (`--v11-only`)
 """
 from __future__ import annotations
 
@@ -158,6 +162,46 @@ def make_api(ref: Reference):
         print("wrote", name, "api")
 
 
+V11_CASES = [("plain_d32_m8", '{"name": "golden", "tags": ["a", "b"], "n": 2000, "nested": {"x": [1.5e3, null, true]}}'),
+             ("opq_d32_m4", "")]
+BAD_METADATA = ['{"a": 1', '{"a": 1} x', '[' * 65 + ']' * 65, '{"a": "\\q"}']
+
+
+def make_v11(ref: Reference):
+    """The golden indexes re-saved by the reference with VESPER_IVFPQ_SAVE_V11=1."""
+    os.environ["VESPER_IVFPQ_SAVE_V11"] = "1"
+    rec = {"metadata": {}, "bad_metadata": []}
+    try:
+        for name, meta in V11_CASES:
+            idx = ref.ivfpq()
+            idx.load(os.path.join(HERE, f"ivfpq_{name}"))
+            if meta:
+                idx.set_metadata_json(meta)
+            out = os.path.join(HERE, f"ivfpq_{name}_v11")
+            shutil.rmtree(out, ignore_errors=True)
+            idx.save(out)
+            back = ref.ivfpq()
+            back.load(out)
+            assert back.get_metadata_json() == meta
+            rec["metadata"][name] = meta
+            print("wrote", name, "v11")
+        with __import__("tempfile").TemporaryDirectory() as td:
+            for bad in BAD_METADATA:
+                idx = ref.ivfpq()
+                idx.load(os.path.join(HERE, f"ivfpq_{V11_CASES[0][0]}"))
+                idx.set_metadata_json(bad)
+                try:
+                    idx.save(td)
+                    msg = ""
+                except IOError as e:
+                    msg = str(e)
+                rec["bad_metadata"].append([bad, msg])
+    finally:
+        os.environ.pop("VESPER_IVFPQ_SAVE_V11", None)
+    with open(os.path.join(HERE, "ivfpq_v11.json"), "w") as f:
+        json.dump(rec, f, indent=1)
+
+
 def make_kmeans(ref: Reference):
     x = mixture(3000, 16, 60, 0.05, 21)
     kpp = ref.kmeanspp_init(x, 48, 42)
@@ -179,9 +223,13 @@ if __name__ == "__main__":
     ref_root = args[0] if args else "/root/reference"
     convert_fixtures(ref_root)
     ref = Reference()
-    if "--rerank-only" not in sys.argv and "--api-only" not in sys.argv:
+    only = [a for a in sys.argv if a.endswith("-only")]
+    if not only:
         make_ivfpq(ref)
         make_kmeans(ref)
-    if "--api-only" not in sys.argv:
+    if not only or "--rerank-only" in only:
         make_rerank(ref)
-    make_api(ref)
+    if not only or "--api-only" in only:
+        make_api(ref)
+    if not only or "--v11-only" in only:
+        make_v11(ref)

@@ -213,3 +213,23 @@ def test_oracle_vs_reference_random(oracle, reference):
         i1, s1 = oracle.flat_topk(op, q, base, 25)
         i2, s2 = reference.flat_topk(op, q, base, 25)
         assert np.array_equal(i1, i2) and np.array_equal(s1, s2)
+
+
+@pytest.mark.parametrize("name", ["plain_d32_m8", "opq_d32_m4"])
+def test_golden_v11_file(name):
+    """The reference's v1.1 sectioned file of a golden index holds the same model and
+    lists as its v1.0 file, in sections 1, 2, [4 OPQ], [5 metadata], 3, each with a
+    matching FNV-1a checksum (src/index/ivf_pq.cpp:4270-4413)."""
+    from oracle_lib import read_ivfpq
+    f, _, _ = golden_case(name)
+    g = read_ivfpq(os.path.join(GOLDEN, f"ivfpq_{name}_v11", "ivfpq.bin"))
+    meta = json.load(open(os.path.join(GOLDEN, "ivfpq_v11.json")))["metadata"][name]
+    assert g["version"] == (1, 1)
+    for key in ("centroids", "codebooks", "list_offsets", "ids", "codes"):
+        assert np.array_equal(g[key], f[key]), key
+    assert (g["rotation"] is None) == (f["rotation"] is None)
+    if f["rotation"] is not None:
+        assert np.array_equal(g["rotation"], f["rotation"])
+    expect = [1, 2] + ([4] if f["rotation"] is not None else []) + ([5] if meta else []) + [3]
+    assert g["sections"] == expect
+    assert g["metadata"] == meta

@@ -41,6 +41,10 @@ EXPORTED = [
     "vesper_ivfpq_get_cluster_centroid", "vesper_ivfpq_update_cluster_centroid", "vesper_ivfpq_reassign_vector",
     "vesper_ivfpq_compact_inverted_list", "vesper_ivfpq_debug_explain_centroid_rank",
     "vesper_ivfpq_debug_explain_adc_rank",
+    "vesper_kmeans_shard_create", "vesper_kmeans_shard_destroy", "vesper_kmeans_shard_assign",
+    "vesper_kmeans_shard_pp_update", "vesper_kmeans_shard_accumulate", "vesper_kmeans_shard_finish",
+    "vesper_kmeans_shard_running_inertia", "vesper_kmeanspp_sampler_create", "vesper_kmeanspp_sampler_next",
+    "vesper_kmeanspp_sampler_destroy",
 ]
 
 KMEANS_ELKAN = 0
@@ -185,6 +189,18 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_ivfpq_compact_inverted_list": (st, [vp, C.c_uint32, u32p, C.c_size_t, C.POINTER(C.c_size_t)]),
             "vesper_ivfpq_debug_explain_centroid_rank": (st, [vp, f32p, C.c_uint64, u64p, u32p]),
             "vesper_ivfpq_debug_explain_adc_rank": (st, [vp, f32p, C.c_uint64, u64p, f32p]),
+            "vesper_kmeans_shard_create": (st, [C.POINTER(vp)]),
+            "vesper_kmeans_shard_destroy": (None, [vp]),
+            "vesper_kmeans_shard_assign": (st, [vp, vp, C.c_size_t, C.c_size_t, vp, C.c_uint32, C.c_int, vp, vp]),
+            "vesper_kmeans_shard_pp_update": (st, [vp, vp, C.c_size_t, C.c_size_t, vp, vp]),
+            "vesper_kmeans_shard_accumulate": (st, [vp, vp, C.c_size_t, C.c_size_t, vp, C.c_uint32, C.c_uint32, vp,
+                                                    vp, vp]),
+            "vesper_kmeans_shard_finish": (st, [vp, vp, vp, C.c_uint32, C.c_size_t, C.c_uint32, vp]),
+            "vesper_kmeans_shard_running_inertia": (st, [vp, vp, C.c_size_t, C.c_size_t, vp, vp,
+                                                         C.POINTER(C.c_float)]),
+            "vesper_kmeanspp_sampler_create": (st, [C.c_uint32, C.c_size_t, C.POINTER(vp), C.POINTER(C.c_size_t)]),
+            "vesper_kmeanspp_sampler_next": (st, [vp, f32p, C.POINTER(C.c_size_t)]),
+            "vesper_kmeanspp_sampler_destroy": (None, [vp]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cctype>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -1577,71 +1578,237 @@ struct Fnv {
         for (size_t i = 0; i < n; ++i) { h ^= b[i]; h *= 1099511628211ull; }
     }
 };
-}  // namespace
+
 
 // IvfPqIndex::save v1.0 layout (src/index/ivf_pq.cpp:4412-4490): magic, version,
 // flags, dims, centroids, codebooks, optional R, lists as (id, code) entries, FNV-1a
 // trailer.  The directory is created; the file is <path>/ivfpq.bin.
+// Byte offsets of each list's size field inside the inverted-list section (after the
+// u32 list count) for list sizes offs.
+std::vector<uint64_t> list_byte_offsets(const std::vector<uint64_t>& offs, uint32_t m) {
+    const size_t nlist = offs.size() - 1;
+    std::vector<uint64_t> lb(nlist + 1);
+    uint64_t p = 4;
+    for (size_t l = 0; l < nlist; ++l) {
+        lb[l] = p;
+        p += 8 + (offs[l + 1] - offs[l]) * (8 + (uint64_t)m);
+    }
+    lb[nlist] = p;
+    return lb;
+}
+
+// Metadata JSON check used by the v1.1 writer and reader (validate_json_structure,
+// src/index/ivf_pq.cpp:113-160): well-formed UTF-8, one JSON value by the RFC 8259
+// grammar with nothing after it, nesting depth <= 64 and at most 4096 object keys.
+class JsonCheck {
+public:
+    explicit JsonCheck(std::string_view s) : s_(s) {}
+    // empty string = valid, else the reason
+    std::string run() {
+        if (!utf8_ok()) return "Metadata JSON is not valid UTF-8";
+        ws();
+        if (!value()) return "Metadata JSON is structurally invalid";
+        ws();
+        if (i_ != s_.size()) return "Trailing characters after JSON";
+        return {};
+    }
+
+private:
+    std::string_view s_;
+    size_t i_ = 0, depth_ = 0, keys_ = 0;
+
+    bool utf8_ok() const {
+        const auto* p = reinterpret_cast<const uint8_t*>(s_.data());
+        const size_t n = s_.size();
+        for (size_t i = 0; i < n;) {
+            const uint8_t c = p[i];
+            int len = c < 0x80 ? 1 : (c >> 5) == 6 ? 2 : (c >> 4) == 14 ? 3 : (c >> 3) == 30 ? 4 : 0;
+            if (len == 0 || i + len > n) return false;
+            uint32_t cp = len == 1 ? c : len == 2 ? (c & 0x1f) : len == 3 ? (c & 0x0f) : (c & 0x07);
+            for (int k = 1; k < len; ++k) {
+                if ((p[i + k] & 0xc0) != 0x80) return false;
+                cp = (cp << 6) | (p[i + k] & 0x3f);
+            }
+            static constexpr uint32_t kMin[5] = {0, 0, 0x80, 0x800, 0x10000};
+            if (cp < kMin[len] || cp > 0x10ffff || (cp >= 0xd800 && cp <= 0xdfff)) return false;
+            i += len;
+        }
+        return true;
+    }
+    bool more() const { return i_ < s_.size(); }
+    void ws() {
+        while (more() && (s_[i_] == ' ' || s_[i_] == '\n' || s_[i_] == '\r' || s_[i_] == '\t')) ++i_;
+    }
+    bool lit(std::string_view w) {
+        if (s_.substr(i_, w.size()) != w) return false;
+        i_ += w.size();
+        return true;
+    }
+    static bool digit(char c) { return c >= '0' && c <= '9'; }
+    bool digits() {
+        const size_t b = i_;
+        while (more() && digit(s_[i_])) ++i_;
+        return i_ > b;
+    }
+    bool number() {
+        if (more() && s_[i_] == '-') ++i_;
+        if (!more()) return false;
+        if (s_[i_] == '0') ++i_;
+        else if (!digits()) return false;
+        if (more() && s_[i_] == '.') { ++i_; if (!digits()) return false; }
+        if (more() && (s_[i_] == 'e' || s_[i_] == 'E')) {
+            ++i_;
+            if (more() && (s_[i_] == '+' || s_[i_] == '-')) ++i_;
+            if (!digits()) return false;
+        }
+        return true;
+    }
+    bool string() {
+        if (!more() || s_[i_] != '"') return false;
+        ++i_;
+        while (more()) {
+            const char c = s_[i_++];
+            if (c == '"') return true;
+            if (c != '\\') continue;
+            if (!more()) return false;
+            const char e = s_[i_++];
+            if (e == 'u') {
+                for (int k = 0; k < 4; ++k, ++i_)
+                    if (!more() || !std::isxdigit(static_cast<unsigned char>(s_[i_]))) return false;
+            } else if (std::string_view("\"\\/bfnrt").find(e) == std::string_view::npos) {
+                return false;
+            }
+        }
+        return false;
+    }
+    // '[' or '{' already current; close = ']' or '}'
+    bool container(char close, bool object) {
+        ++i_;
+        if (++depth_ > 64) return false;
+        ws();
+        if (more() && s_[i_] == close) { ++i_; --depth_; return true; }
+        while (more()) {
+            if (object) {
+                if (!string() || ++keys_ > 4096) return false;
+                ws();
+                if (!more() || s_[i_] != ':') return false;
+                ++i_;
+            }
+            if (!value()) return false;
+            ws();
+            if (!more()) return false;
+            if (s_[i_] == ',') { ++i_; ws(); continue; }
+            if (s_[i_] == close) { ++i_; --depth_; return true; }
+            return false;
+        }
+        return false;
+    }
+    bool value() {
+        ws();
+        if (!more()) return false;
+        switch (s_[i_]) {
+            case '"': return string();
+            case '{': return container('}', true);
+            case '[': return container(']', false);
+            case 't': return lit("true");
+            case 'f': return lit("false");
+            case 'n': return lit("null");
+            default: return number();
+        }
+    }
+};
+}  // namespace
+
+// IvfPqIndex::save (src/index/ivf_pq.cpp:4241-4491): the v1.0 monolithic layout, or the
+// v1.1 sectioned layout with VESPER_IVFPQ_SAVE_V11=1 (sections stored uncompressed:
+// compressed size = uncompressed size).  The inverted-list section is packed on the device.
 auto IvfPqIndex::save(const std::string& path) const -> std::expected<void, core::error> {
     namespace fs = std::filesystem;
     const auto& I = *impl_;
     if (!I.trained) return fail(error_code::internal, "PQ not trained", "ivf_pq.save");
+    const bool v11 = env_flag("VESPER_IVFPQ_SAVE_V11");
+    if (v11 && !I.metadata_json.empty()) {
+        if (I.metadata_json.size() > 64u * 1024u)
+            return fail(error_code::config_invalid, "Metadata JSON too large (limit 64 KiB)", "ivf_pq.save");
+        const std::string why = JsonCheck(I.metadata_json).run();
+        if (!why.empty()) return fail(error_code::config_invalid, "Metadata JSON invalid: " + why, "ivf_pq.save");
+    }
     std::error_code fec;
     fs::create_directories(path, fec);
     if (fec) return fail(error_code::io_failed, "Failed to create directory: " + path, "ivf_pq.save");
     const std::string file_path = path + "/ivfpq.bin";
     std::ofstream f(file_path, std::ios::binary);
     if (!f) return fail(error_code::io_failed, "Failed to open file for writing: " + file_path, "ivf_pq.save");
-    std::vector<uint64_t> ids = list_ids();
-    std::vector<uint8_t> codes = list_codes();
+    const uint32_t dim = (uint32_t)I.dim, nlist = I.params.nlist, m = I.params.m, nbits = I.params.nbits,
+                   dsub = (uint32_t)I.dsub, code_size = m;
+    // the inverted-list section, packed on the device
+    const std::vector<uint64_t> lb = list_byte_offsets(I.h_offs, m);
+    std::vector<uint8_t> inv(lb[nlist]);
+    std::memcpy(inv.data(), &nlist, 4);
+    {
+        DeviceGuard g(I.dev);
+        try {
+            vgpu::DeviceBuffer<uint64_t> d_lb(nlist + 1);
+            vgpu::DeviceBuffer<uint8_t> d_raw(inv.size());
+            h2d(d_lb.data(), lb.data(), lb.size(), I.st);
+            vgpu::launch_pack_lists(I.d_ids.data(), I.d_codes.data(), I.d_offs.data(), (int)nlist, (int)m,
+                                    d_lb.data(), d_raw.data(), I.st);
+            d2h(inv.data() + 4, d_raw.data() + 4, inv.size() - 4, I.st);
+            sync(I.st);
+        } catch (const vgpu::CudaError& e) {
+            return fail(error_code::internal, e.what(), "ivf_pq.cuda");
+        }
+    }
     Fnv fnv;
-    std::vector<char> buf;
-    buf.reserve(1 << 20);
     auto put = [&](const void* p, size_t n) {
         fnv.update(p, n);
-        const char* c = static_cast<const char*>(p);
-        buf.insert(buf.end(), c, c + n);
-        if (buf.size() > (8u << 20)) { f.write(buf.data(), (std::streamsize)buf.size()); buf.clear(); }
+        f.write(static_cast<const char*>(p), (std::streamsize)n);
     };
-    const char magic[8] = {'I', 'V', 'F', 'P', 'Q', 'v', '1', '0'};
+    const char magic[8] = {'I', 'V', 'F', 'P', 'Q', 'v', '1', v11 ? '1' : '0'};
     put(magic, 8);
-    const uint16_t vmaj = 1, vmin = 0;
+    const uint16_t vmaj = 1, vmin = v11 ? 1 : 0;
     put(&vmaj, 2);
     put(&vmin, 2);
     const uint32_t flags = (I.params.use_opq && I.has_rot) ? 1u : 0u;
     put(&flags, 4);
-    const uint32_t dim = (uint32_t)I.dim, nlist = I.params.nlist, m = I.params.m, nbits = I.params.nbits,
-                   dsub = (uint32_t)I.dsub, code_size = m;
     const uint64_t nvec = I.n_vectors;
     const uint64_t ts = (uint64_t)std::chrono::system_clock::to_time_t(std::chrono::system_clock::now());
     put(&dim, 4); put(&nlist, 4); put(&m, 4); put(&nbits, 4); put(&dsub, 4);
     put(&nvec, 8); put(&code_size, 4); put(&ts, 8);
     const uint32_t meta_len = 0;
     put(&meta_len, 4);
-    put(I.h_cent.data(), I.h_cent.size() * 4);
-    put(I.h_cb.data(), I.h_cb.size() * 4);
-    if (flags & 1u) put(I.h_rot.data(), I.h_rot.size() * 4);
-    put(&nlist, 4);
-    for (uint32_t l = 0; l < nlist; ++l) {
-        const uint64_t b = I.h_offs[l], e = I.h_offs[l + 1];
-        const uint64_t sz = e - b;
-        put(&sz, 8);
-        for (uint64_t j = b; j < e; ++j) {
-            put(&ids[j], 8);
-            put(codes.data() + j * m, m);
-        }
+    if (v11) {
+        // section header: type u32, uncompressed u64, stored u64, FNV-1a of the payload u64
+        auto section = [&](uint32_t type, const void* data, uint64_t bytes) {
+            Fnv sh;
+            sh.update(data, bytes);
+            put(&type, 4); put(&bytes, 8); put(&bytes, 8); put(&sh.h, 8);
+            if (bytes) put(data, bytes);
+        };
+        section(1, I.h_cent.data(), I.h_cent.size() * 4);
+        section(2, I.h_cb.data(), I.h_cb.size() * 4);
+        if (flags & 1u) section(4, I.h_rot.data(), I.h_rot.size() * 4);
+        if (!I.metadata_json.empty()) section(5, I.metadata_json.data(), I.metadata_json.size());
+        section(3, inv.data(), inv.size());
+    } else {
+        put(I.h_cent.data(), I.h_cent.size() * 4);
+        put(I.h_cb.data(), I.h_cb.size() * 4);
+        if (flags & 1u) put(I.h_rot.data(), I.h_rot.size() * 4);
+        put(inv.data(), inv.size());
     }
     const char tail[4] = {'C', 'H', 'K', 'S'};
-    buf.insert(buf.end(), tail, tail + 4);
-    const char* hp = reinterpret_cast<const char*>(&fnv.h);
-    buf.insert(buf.end(), hp, hp + 8);
-    f.write(buf.data(), (std::streamsize)buf.size());
+    f.write(tail, 4);
+    f.write(reinterpret_cast<const char*>(&fnv.h), 8);
     if (!f) return fail(error_code::io_failed, "Failed writing " + file_path, "ivf_pq.save");
     return {};
 }
 
-// IvfPqIndex::load for the v1.0 layout (src/index/ivf_pq.cpp:4493-4966, monolithic
-// branch): every field is validated and the FNV-1a trailer must match.
+// IvfPqIndex::load (src/index/ivf_pq.cpp:4493-4966): v1.0 monolithic or v1.1 sectioned.
+// Sections are checked as the reference's mapped-file reader checks them (4565-4690):
+// every section's FNV-1a checksum, including unknown types, which are then skipped; a
+// compressed section is refused (this build has no Zstandard).  The file checksum is
+// verified first, and the inverted-list section is uploaded once and unpacked on the
+// device.
 auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core::error> {
     const std::string file_path = path + "/ivfpq.bin";
     std::ifstream f(file_path, std::ios::binary);
@@ -1653,8 +1820,17 @@ auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core
     std::vector<char> raw((size_t)fsize);
     f.read(raw.data(), fsize);
     if (f.gcount() != fsize) return fail(error_code::io_failed, "Failed reading file", "ivf_pq.load");
-    size_t off = 0;
     const size_t body_end = (size_t)fsize - 12;
+    if (std::memcmp(raw.data() + body_end, "CHKS", 4) != 0)
+        return fail(error_code::config_invalid, "Missing checksum trailer", "ivf_pq.load");
+    uint64_t chk = 0;
+    std::memcpy(&chk, raw.data() + body_end + 4, 8);
+    {
+        Fnv fnv;
+        fnv.update(raw.data(), body_end);
+        if (chk != fnv.h) return fail(error_code::config_invalid, "Checksum mismatch", "ivf_pq.load");
+    }
+    size_t off = 0;
     auto get = [&](void* p, size_t n) -> bool {
         if (off + n > body_end) return false;
         std::memcpy(p, raw.data() + off, n);
@@ -1663,9 +1839,8 @@ auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core
     };
     char magic[8];
     if (!get(magic, 8)) return fail(error_code::io_failed, "Failed reading magic", "ivf_pq.load");
-    if (std::string_view(magic, 8) == std::string_view("IVFPQv11", 8))
-        return fail(error_code::unsupported, "v1.1 sectioned files are not supported by this loader", "ivf_pq.load");
-    if (std::string_view(magic, 8) != std::string_view("IVFPQv10", 8))
+    const bool v11 = std::string_view(magic, 8) == std::string_view("IVFPQv11", 8);
+    if (!v11 && std::string_view(magic, 8) != std::string_view("IVFPQv10", 8))
         return fail(error_code::config_invalid, "Magic mismatch", "ivf_pq.load");
     uint16_t vmaj = 0, vmin = 0;
     if (!get(&vmaj, 2) || !get(&vmin, 2)) return fail(error_code::io_failed, "Failed reading version", "ivf_pq.load");
@@ -1680,39 +1855,109 @@ auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core
     if (meta_len > 64u * 1024u) return fail(error_code::config_invalid, "Metadata too large", "ivf_pq.load");
     std::string meta(meta_len, '\0');
     if (meta_len && !get(meta.data(), meta_len)) return fail(error_code::io_failed, "Failed reading metadata", "ivf_pq.load");
+    if (meta_len) {
+        const std::string why = JsonCheck(meta).run();
+        if (!why.empty()) return fail(error_code::config_invalid, "Metadata JSON invalid (header): " + why, "ivf_pq.load");
+    }
     const uint32_t ksub = 1u << nbits;
     std::vector<float> cent((size_t)nlist * dim), cb((size_t)m * ksub * dsub), rot;
-    if (!get(cent.data(), cent.size() * 4)) return fail(error_code::io_failed, "Failed reading centroid row", "ivf_pq.load");
-    if (!get(cb.data(), cb.size() * 4)) return fail(error_code::io_failed, "Failed reading PQ codebooks", "ivf_pq.load");
-    if (flags & 1u) {
-        rot.resize((size_t)dim * dim);
-        if (!get(rot.data(), rot.size() * 4)) return fail(error_code::io_failed, "Failed reading OPQ rotation", "ivf_pq.load");
-    }
-    uint32_t lists_count = 0;
-    if (!get(&lists_count, 4)) return fail(error_code::io_failed, "Failed reading lists_count", "ivf_pq.load");
-    if (lists_count != nlist) return fail(error_code::config_invalid, "lists_count mismatch", "ivf_pq.load");
-    std::vector<uint64_t> offs(nlist + 1, 0), ids;
-    std::vector<uint8_t> codes;
-    for (uint32_t l = 0; l < nlist; ++l) {
-        uint64_t sz = 0;
-        if (!get(&sz, 8)) return fail(error_code::io_failed, "Failed reading list size", "ivf_pq.load");
-        if (sz > (body_end - off) / (8 + (uint64_t)m)) return fail(error_code::io_failed, "Failed reading id", "ivf_pq.load");
-        offs[l + 1] = offs[l] + sz;
-        const size_t base = ids.size();
-        ids.resize(base + sz);
-        codes.resize((base + sz) * m);
-        for (uint64_t j = 0; j < sz; ++j) {
-            get(&ids[base + j], 8);
-            get(codes.data() + (base + j) * m, m);
+    size_t inv_off = 0, inv_len = 0;
+    bool have_cent = false, have_cb = false, have_inv = false;
+    if (v11) {
+        while (off < body_end) {
+            uint32_t type = 0;
+            uint64_t unc = 0, comp = 0, shash = 0;
+            if (!get(&type, 4) || !get(&unc, 8) || !get(&comp, 8) || !get(&shash, 8)) break;
+            if (comp > body_end - off) return fail(error_code::io_failed, "Failed reading section payload", "ivf_pq.load");
+            const char* payload = raw.data() + off;
+            off += comp;
+            if (unc == 0 && comp == 0) continue;
+            if (comp != unc && unc != 0)
+                return fail(error_code::config_invalid, "Decompression failed (compressed sections need Zstandard)",
+                            "ivf_pq.load");
+            if (unc) {
+                Fnv sh;
+                sh.update(payload, unc);
+                if (sh.h != shash) return fail(error_code::config_invalid, "Section checksum mismatch", "ivf_pq.load");
+            }
+            switch (type) {
+                case 1:
+                    if (unc != cent.size() * 4) return fail(error_code::config_invalid, "Centroids size mismatch", "ivf_pq.load");
+                    std::memcpy(cent.data(), payload, unc);
+                    have_cent = true;
+                    break;
+                case 2:
+                    if (unc != cb.size() * 4) return fail(error_code::config_invalid, "Codebooks size mismatch", "ivf_pq.load");
+                    std::memcpy(cb.data(), payload, unc);
+                    have_cb = true;
+                    break;
+                case 4:
+                    if (unc != (uint64_t)dim * dim * 4) return fail(error_code::config_invalid, "OPQ size mismatch", "ivf_pq.load");
+                    rot.resize((size_t)dim * dim);
+                    std::memcpy(rot.data(), payload, unc);
+                    flags |= 1u;
+                    break;
+                case 5: {
+                    if (unc > 64u * 1024u) return fail(error_code::config_invalid, "Metadata too large", "ivf_pq.load");
+                    std::string sec(payload, unc);
+                    const std::string why = JsonCheck(sec).run();
+                    if (!why.empty())
+                        return fail(error_code::config_invalid, "Metadata JSON invalid (section): " + why, "ivf_pq.load");
+                    meta = std::move(sec);
+                    break;
+                }
+                case 3:
+                    inv_off = (size_t)(payload - raw.data());
+                    inv_len = unc;
+                    have_inv = true;
+                    break;
+                default:
+                    break;  // unknown sections are skipped
+            }
         }
+        if (!have_cent || !have_cb) return fail(error_code::config_invalid, "Missing centroid or codebook section", "ivf_pq.load");
+    } else {
+        if (!get(cent.data(), cent.size() * 4)) return fail(error_code::io_failed, "Failed reading centroid row", "ivf_pq.load");
+        if (!get(cb.data(), cb.size() * 4)) return fail(error_code::io_failed, "Failed reading PQ codebooks", "ivf_pq.load");
+        if (flags & 1u) {
+            rot.resize((size_t)dim * dim);
+            if (!get(rot.data(), rot.size() * 4)) return fail(error_code::io_failed, "Failed reading OPQ rotation", "ivf_pq.load");
+        }
+        inv_off = off;
+        inv_len = body_end - off;
+        have_inv = true;
     }
-    if (std::memcmp(raw.data() + body_end, "CHKS", 4) != 0)
-        return fail(error_code::config_invalid, "Missing checksum trailer", "ivf_pq.load");
-    uint64_t chk = 0;
-    std::memcpy(&chk, raw.data() + body_end + 4, 8);
-    Fnv fnv;
-    fnv.update(raw.data(), off);
-    if (off != body_end || chk != fnv.h) return fail(error_code::config_invalid, "Checksum mismatch", "ivf_pq.load");
+    // list sizes from the inverted-list section's headers (error texts: v1.1 section
+    // parser, src/index/ivf_pq.cpp:4839-4857; v1.0 stream reader, 4939-4949)
+    std::vector<uint64_t> offs(nlist + 1, 0), lb(nlist + 1, 0);
+    if (have_inv) {
+        const char* q = raw.data() + inv_off;
+        const uint64_t rec = 8 + (uint64_t)m;
+        uint32_t lists_count = 0;
+        if (inv_len < 4)
+            return v11 ? fail(error_code::config_invalid, "Inverted too small", "ivf_pq.load")
+                       : fail(error_code::io_failed, "Failed reading lists_count", "ivf_pq.load");
+        std::memcpy(&lists_count, q, 4);
+        if (lists_count != nlist) return fail(error_code::config_invalid, "lists_count mismatch", "ivf_pq.load");
+        uint64_t p = 4;
+        for (uint32_t l = 0; l < nlist; ++l) {
+            uint64_t sz = 0;
+            if (inv_len - p < 8)
+                return v11 ? fail(error_code::config_invalid, "List header truncated", "ivf_pq.load")
+                           : fail(error_code::io_failed, "Failed reading list size", "ivf_pq.load");
+            std::memcpy(&sz, q + p, 8);
+            if (sz > (inv_len - p - 8) / rec)
+                return v11 ? fail(error_code::config_invalid, "Entry truncated", "ivf_pq.load")
+                           : fail(error_code::io_failed, "Failed reading id", "ivf_pq.load");
+            lb[l] = p;
+            offs[l + 1] = offs[l] + sz;
+            p += 8 + sz * rec;
+        }
+        if (p != inv_len)
+            return fail(error_code::config_invalid, v11 ? "Inverted section extra bytes" : "Missing checksum trailer",
+                        "ivf_pq.load");
+    }
+    const uint64_t n_entries = offs[nlist];
 
     IvfPqIndex index;
     auto r = index.set_model(dim, nlist, m, nbits, cent.data(), cb.data(), rot.empty() ? nullptr : rot.data());
@@ -1721,14 +1966,22 @@ auto IvfPqIndex::load(const std::string& path) -> std::expected<IvfPqIndex, core
     DeviceGuard g(I.dev);
     try {
         I.params.use_opq = (flags & 1u) != 0;
+        I.metadata_json = meta;
         I.h_offs = offs;
-        I.n_vectors = ids.size();
+        I.n_vectors = n_entries;
         I.d_offs.resize(nlist + 1);
         h2d(I.d_offs.data(), offs.data(), offs.size(), I.st);
-        I.d_ids.resize(std::max<size_t>(ids.size(), 1));
-        h2d(I.d_ids.data(), ids.data(), ids.size(), I.st);
-        I.d_codes.resize(std::max<size_t>(codes.size(), 1));
-        h2d(I.d_codes.data(), codes.data(), codes.size(), I.st);
+        I.d_ids.resize(std::max<size_t>(n_entries, 1));
+        I.d_codes.resize(std::max<size_t>(n_entries * m, 1));
+        if (n_entries) {
+            vgpu::DeviceBuffer<uint8_t> d_raw(inv_len);
+            vgpu::DeviceBuffer<uint64_t> d_lb(nlist + 1);
+            h2d(d_raw.data(), reinterpret_cast<const uint8_t*>(raw.data() + inv_off), inv_len, I.st);
+            h2d(d_lb.data(), lb.data(), lb.size(), I.st);
+            vgpu::launch_unpack_lists(d_raw.data(), d_lb.data(), I.d_offs.data(), (int)nlist, (int)m, I.d_ids.data(),
+                                      I.d_codes.data(), I.st);
+            sync(I.st);
+        }
         I.recompute_vterms();
         I.rebuild_blocks();
         sync(I.st);

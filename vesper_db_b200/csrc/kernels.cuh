@@ -140,6 +140,20 @@ void launch_kpp_update(const float* x, long long n, int dim, const float* c, flo
 // keep their centroid.
 void launch_segment_mean(const float* x, int dim, const uint32_t* order, const uint32_t* seg,
                          int k, int kahan, float* centroids, cudaStream_t st);
+// The M-step split over point shards held by different GPUs: each shard continues the
+// per-(cluster, dimension) running sums (sum, and the Kahan compensation when kahan=1)
+// over its own points in order, starting from the state the previous shard left, and
+// adds its cluster sizes to count; finish turns the state into centroids exactly as
+// launch_segment_mean does.  Running the shards in point order reproduces
+// launch_segment_mean over the whole set bit for bit.
+void launch_segment_accumulate(const float* x, int dim, const uint32_t* order, const uint32_t* seg, int k,
+                               int kahan, double* sum, double* comp, unsigned long long* count, cudaStream_t st);
+void launch_finish_means(const double* sum, const unsigned long long* count, int k, int dim, int kahan,
+                         float* centroids, cudaStream_t st);
+// *total = *total + sum over points i in order, dims d in order, of (x_id - c_{a_i}d)^2,
+// one rounded float add per term (kmeans_cluster's final inertia).
+void launch_ordered_sq_sum(const float* x, const float* c, const uint32_t* assign, long long n, int dim,
+                           float* total, cudaStream_t st);
 // out[i] = l2(x_i, c[assign[i]]) in reference order.
 void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,
                         cudaStream_t st);
@@ -190,6 +204,12 @@ void launch_reconstruct_rows(const uint32_t* entries, unsigned long long e0, con
 void launch_adc_all(const float* rres, int dim, int nlist, const float* cb, int m, int ksub, int dsub,
                     const uint64_t* offs, const uint8_t* codes, float* adc, cudaStream_t st);
 void launch_count_less(const float* v, long long n, long long target, unsigned long long* count, cudaStream_t st);
+// The index files' inverted-list section <-> CSR (lists_io.cu).  list_byte[l]: offset
+// of list l's size field in raw (after the u32 list count).
+void launch_unpack_lists(const uint8_t* raw, const uint64_t* list_byte, const uint64_t* offs, int nlist, int m,
+                         uint64_t* ids, uint8_t* codes, cudaStream_t st);
+void launch_pack_lists(const uint64_t* ids, const uint8_t* codes, const uint64_t* offs, int nlist, int m,
+                       const uint64_t* list_byte, uint8_t* raw, cudaStream_t st);
 // codes2 / ids2 in the new entry order (order[i] = old entry, 0xffffffff = the new entry).
 void launch_gather_entries(const uint32_t* order, long long n, const uint8_t* codes, const uint64_t* ids, int m,
                            const uint8_t* new_code, uint64_t new_id, uint8_t* codes2, uint64_t* ids2,

@@ -85,37 +85,73 @@ void KmeansEngine::assign(const float* d_x, size_t n, int d, const float* d_c, u
     }
 }
 
-// The D^2 vector comes from the GPU; the fp64 prefix sum, the draws and lower_bound
-// run on the host with the reference's std::mt19937 and libstdc++ distributions.
-void KmeansEngine::kmeanspp(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c) {
-    std::mt19937 gen(seed);
+KmeansPPSampler::KmeansPPSampler(uint32_t seed, size_t n) : gen_(seed), n_(n), cum_(n) {
     std::uniform_int_distribution<size_t> first(0, n - 1);
-    size_t idx = first(gen);
+    first_ = first(gen_);
+}
+
+size_t KmeansPPSampler::next(const float* d2) {
+    cum_[0] = d2[0];
+    for (size_t i = 1; i < n_; ++i) cum_[i] = cum_[i - 1] + d2[i];
+    std::uniform_real_distribution<double> sd(0.0, cum_.back());
+    const double target = sd(gen_);
+    return (size_t)(std::lower_bound(cum_.begin(), cum_.end(), target) - cum_.begin());
+}
+
+// The D^2 vector comes from the GPU; the draws run on the host (KmeansPPSampler).
+void KmeansEngine::kmeanspp(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c) {
+    KmeansPPSampler sampler(seed, n);
+    size_t idx = sampler.first();
     check(cudaMemcpyAsync(d_c, d_x + idx * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, st_), "d2d");
     kpp_.reserve(n);
     launch_fill(kpp_.data(), (long long)n, std::numeric_limits<float>::max(), st_);
     float* h = pinned(n);
-    std::vector<double> cum(n);
     for (uint32_t c = 1; c < k; ++c) {
         launch_kpp_update(d_x, (long long)n, d, d_c + (size_t)(c - 1) * d, kpp_.data(), st_);
         check(cudaMemcpyAsync(h, kpp_.data(), n * sizeof(float), cudaMemcpyDeviceToHost, st_), "d2h");
         check(cudaStreamSynchronize(st_), "sync");
-        cum[0] = h[0];
-        for (size_t i = 1; i < n; ++i) cum[i] = cum[i - 1] + h[i];
-        std::uniform_real_distribution<double> sd(0.0, cum.back());
-        const double target = sd(gen);
-        idx = (size_t)(std::lower_bound(cum.begin(), cum.end(), target) - cum.begin());
+        idx = sampler.next(h);
         check(cudaMemcpyAsync(d_c + (size_t)c * d, d_x + idx * d, sizeof(float) * d, cudaMemcpyDeviceToDevice, st_),
               "d2d");
     }
 }
+
+void KmeansEngine::accumulate(const float* d_x, size_t n, int d, const uint32_t* d_assign, uint32_t k, bool kahan,
+                              double* sum, double* comp, unsigned long long* count) {
+    if (n == 0) return;
+    order_.reserve(n);
+    seg_.reserve(k + 1);
+    group_by_key(d_assign, (long long)n, (int)k, order_.data(), seg_.data(), gw_, st_);
+    launch_segment_accumulate(d_x, d, order_.data(), seg_.data(), (int)k, kahan ? 1 : 0, sum, comp, count, st_);
+}
+
+void KmeansEngine::finish_means(const double* sum, const unsigned long long* count, uint32_t k, int d, bool kahan,
+                                float* d_c) {
+    launch_finish_means(sum, count, (int)k, d, kahan ? 1 : 0, d_c, st_);
+}
+
+void KmeansEngine::pp_update(const float* d_x, size_t n, int d, const float* d_crow, float* d_mind) {
+    launch_kpp_update(d_x, (long long)n, d, d_crow, d_mind, st_);
+}
+
+void KmeansEngine::running_inertia(const float* d_x, size_t n, int d, const float* d_c, const uint32_t* d_assign,
+                                   float* total) {
+    mind_.reserve(1);
+    check(cudaMemcpyAsync(mind_.data(), total, sizeof(float), cudaMemcpyHostToDevice, st_), "h2d");
+    launch_ordered_sq_sum(d_x, d_c, d_assign, (long long)n, d, mind_.data(), st_);
+    check(cudaMemcpyAsync(total, mind_.data(), sizeof(float), cudaMemcpyDeviceToHost, st_), "d2h");
+    check(cudaStreamSynchronize(st_), "sync");
+}
+
+void KmeansEngine::sync() { check(cudaStreamSynchronize(st_), "sync"); }
 
 // Elkan (KmeansElkan::cluster): exact E-step with the keep-on-tie rule (Elkan prunes
 // only provably farther centroids), convergence test on the fp64-summed inertia
 // before the M-step, Kahan M-step in point order; returns the last converged-from
 // inertia and the iteration count, as the reference does.
 // Lloyd (kmeans_cluster): lowest-index E-step, the same test, fp64 sum / count
-// M-step; after the loop one more M-step and the inertia of the final assignment.
+// M-step; after the loop one more M-step and the inertia of the final assignment as the
+// reference's float running total over every term.
 KmeansResultGpu KmeansEngine::fit(const float* d_x, size_t n, int d, uint32_t k, uint32_t max_iter, float eps,
                                   uint32_t seed, bool elkan, float* d_c, uint32_t* d_assign) {
     kmeanspp(d_x, n, d, k, seed, d_c);
@@ -141,8 +177,9 @@ KmeansResultGpu KmeansEngine::fit(const float* d_x, size_t n, int d, uint32_t k,
     } else {
         group_by_key(d_assign, (long long)n, (int)k, order_.data(), seg_.data(), gw_, st_);
         launch_segment_mean(d_x, d, order_.data(), seg_.data(), (int)k, 0, d_c, st_);
-        launch_assigned_l2(d_x, d_c, d_assign, (long long)n, d, mind_.data(), st_);
-        r.inertia = (float)ordered_sum(mind_.data(), n);
+        float total = 0.0f;
+        running_inertia(d_x, n, d, d_c, d_assign, &total);
+        r.inertia = total;
     }
     check(cudaStreamSynchronize(st_), "sync");
     return r;

@@ -6,6 +6,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <random>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels_train.cuh"
@@ -16,6 +18,23 @@ namespace vgpu {
 // unless the shapes or the pointer alignment rule it out, or VGPU_COARSE=exact asks
 // for the CUDA-core kernels; both give the same (exact) result.
 bool use_tensor_cores(const float* x, const float* c, int d, uint32_t k);
+
+// The draws of kmeans_plusplus_init (src/index/kmeans.cpp:45-89) on the host: the
+// reference's std::mt19937(seed), uniform_int_distribution<size_t> for the first row,
+// then per further centroid an fp64 running prefix sum of the D^2 vector in point
+// order, one uniform_real_distribution<double>(0, total) draw and lower_bound.
+class KmeansPPSampler {
+public:
+    KmeansPPSampler(uint32_t seed, size_t n);
+    size_t first() const { return first_; }
+    // d2: the current D^2 value of every point (host, n floats, point order).
+    size_t next(const float* d2);
+
+private:
+    std::mt19937 gen_;
+    size_t n_, first_;
+    std::vector<double> cum_;
+};
 
 struct KmeansResultGpu {
     uint32_t iterations = 0;
@@ -45,6 +64,18 @@ public:
 
     // Sum of a device float array in index order, in fp64.
     double ordered_sum(const float* d, size_t n);
+
+    // One shard's part of the M-step (launch_segment_accumulate): the points of x
+    // [n x d] grouped by d_assign, sums continued from (sum, comp), sizes added to count.
+    void accumulate(const float* d_x, size_t n, int d, const uint32_t* d_assign, uint32_t k, bool kahan,
+                    double* sum, double* comp, unsigned long long* count);
+    void finish_means(const double* sum, const unsigned long long* count, uint32_t k, int d, bool kahan,
+                      float* d_c);
+    void pp_update(const float* d_x, size_t n, int d, const float* d_crow, float* d_mind);
+    // *total (host) continued by kmeans_cluster's final float running inertia over the
+    // points of x in order (launch_ordered_sq_sum).
+    void running_inertia(const float* d_x, size_t n, int d, const float* d_c, const uint32_t* d_assign, float* total);
+    void sync();
 
 private:
     cudaStream_t st_;

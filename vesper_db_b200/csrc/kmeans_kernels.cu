@@ -96,6 +96,61 @@ void launch_segment_mean(const float* x, int dim, const uint32_t* order, const u
     VGPU_LAUNCH("segment_mean_kernel");
 }
 
+// One CTA per cluster, one thread per dimension: the loop of segment_mean_kernel,
+// resumed from and saved to (sum, comp).
+__global__ void segment_accumulate_kernel(const float* __restrict__ x, int dim, const uint32_t* __restrict__ order,
+                                          const uint32_t* __restrict__ seg, int kahan, double* __restrict__ sum,
+                                          double* __restrict__ comp, unsigned long long* __restrict__ count) {
+    const int c = blockIdx.x;
+    const uint32_t b = seg[c], e = seg[c + 1];
+    if (b == e) return;
+    if (threadIdx.x == 0) count[c] += e - b;
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+        const long long o = (long long)c * dim + d;
+        double s = sum[o];
+        if (kahan) {
+            double cp = comp[o];
+            for (uint32_t j = b; j < e; ++j) {
+                const double y = (double)x[(long long)order[j] * dim + d] - cp;
+                const double t = s + y;
+                cp = (t - s) - y;
+                s = t;
+            }
+            comp[o] = cp;
+        } else {
+            for (uint32_t j = b; j < e; ++j) s += (double)x[(long long)order[j] * dim + d];
+        }
+        sum[o] = s;
+    }
+}
+
+__global__ void finish_means_kernel(const double* __restrict__ sum, const unsigned long long* __restrict__ count,
+                                    long long total, int dim, int kahan, float* __restrict__ centroids) {
+    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const unsigned long long n = count[t / dim];
+        if (n == 0) continue;  // empty cluster keeps its centroid
+        centroids[t] = kahan ? (float)(sum[t] * (1.0 / (double)n)) : (float)(sum[t] / (double)n);
+    }
+}
+
+void launch_segment_accumulate(const float* x, int dim, const uint32_t* order, const uint32_t* seg, int k,
+                               int kahan, double* sum, double* comp, unsigned long long* count, cudaStream_t st) {
+    if (k <= 0) return;
+    const int threads = dim >= 256 ? 256 : ((dim + 31) / 32) * 32;
+    segment_accumulate_kernel<<<k, threads, 0, st>>>(x, dim, order, seg, kahan, sum, comp, count);
+    VGPU_LAUNCH("segment_accumulate_kernel");
+}
+
+void launch_finish_means(const double* sum, const unsigned long long* count, int k, int dim, int kahan,
+                         float* centroids, cudaStream_t st) {
+    const long long total = (long long)k * dim;
+    if (total <= 0) return;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    finish_means_kernel<<<blocks, 256, 0, st>>>(sum, count, total, dim, kahan, centroids);
+    VGPU_LAUNCH("finish_means_kernel");
+}
+
 }  // namespace vgpu
 
 namespace vgpu {
@@ -131,6 +186,44 @@ __global__ void assigned_l2_kernel(const float* __restrict__ x, const float* __r
             out[i] = r;
         }
     }
+}
+
+// The final inertia of kmeans_cluster (src/index/kmeans.cpp:230-241): ONE float running
+// total over every (point, dimension) term in point-major order, t += (x - c)^2 with the
+// subtraction, the square and the add each rounded.  A running float sum has no
+// reassociation, so one thread adds; the CTA's other threads compute the next chunk of
+// terms into shared memory.  *total holds the starting value and receives the result.
+constexpr int OSQ_CHUNK = 8192;
+__global__ void __launch_bounds__(1024) ordered_sq_sum_kernel(const float* __restrict__ x, const float* __restrict__ c,
+                                                              const uint32_t* __restrict__ assign, long long n,
+                                                              int dim, float* __restrict__ total) {
+    __shared__ float terms[OSQ_CHUNK];
+    const long long count = n * dim;
+    float acc = *total;
+    for (long long t0 = 0; t0 < count; t0 += OSQ_CHUNK) {
+        const int len = (int)(count - t0 < OSQ_CHUNK ? count - t0 : (long long)OSQ_CHUNK);
+        for (int j = threadIdx.x; j < len; j += blockDim.x) {
+            const long long t = t0 + j;
+            const long long i = t / dim;
+            const int d = (int)(t - i * dim);
+            const float diff = __fsub_rn(x[t], c[(long long)assign[i] * dim + d]);
+            terms[j] = __fmul_rn(diff, diff);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+#pragma unroll 16
+            for (int j = 0; j < len; ++j) acc = __fadd_rn(acc, terms[j]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *total = acc;
+}
+
+void launch_ordered_sq_sum(const float* x, const float* c, const uint32_t* assign, long long n, int dim,
+                           float* total, cudaStream_t st) {
+    if (n <= 0) return;
+    ordered_sq_sum_kernel<<<1, 1024, 0, st>>>(x, c, assign, n, dim, total);
+    VGPU_LAUNCH("ordered_sq_sum_kernel");
 }
 
 void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,

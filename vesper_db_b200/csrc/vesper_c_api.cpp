@@ -666,6 +666,130 @@ VESPER_C_API vesper_status_t vesper_kmeans_fit_device(const float* d_data, size_
 
 }  // extern "C"
 
+struct vesper_kmeans_shard_s {
+    cudaStream_t st = nullptr;
+    std::unique_ptr<vgpu::KmeansEngine> eng;
+    ~vesper_kmeans_shard_s() {
+        eng.reset();
+        if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
+    }
+};
+
+struct vesper_kmeanspp_sampler_s {
+    vgpu::KmeansPPSampler s;
+};
+
+extern "C" {
+
+VESPER_C_API vesper_status_t vesper_kmeans_shard_create(vesper_kmeans_shard_t** out) {
+    if (!out) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    *out = nullptr;
+    return guarded("kmeans_shard_create", [&] {
+        auto h = std::make_unique<vesper_kmeans_shard_s>();
+        vgpu::check(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "cudaStreamCreate");
+        h->eng = std::make_unique<vgpu::KmeansEngine>(h->st);
+        *out = h.release();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API void vesper_kmeans_shard_destroy(vesper_kmeans_shard_t* shard) { delete shard; }
+
+VESPER_C_API vesper_status_t vesper_kmeans_shard_assign(vesper_kmeans_shard_t* shard, const float* d_x, size_t n,
+                                                        size_t dim, const float* d_centroids, uint32_t k,
+                                                        int keep_on_tie, uint32_t* d_assign, float* d_min_dist) {
+    if (!shard || (n && (!d_x || !d_assign)) || !d_centroids || k == 0 || dim == 0 || dim > (size_t)INT32_MAX)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("kmeans_shard_assign", [&] {
+        if (n) shard->eng->assign(d_x, n, (int)dim, d_centroids, k, d_assign, d_min_dist, keep_on_tie != 0);
+        shard->eng->sync();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_kmeans_shard_pp_update(vesper_kmeans_shard_t* shard, const float* d_x, size_t n,
+                                                           size_t dim, const float* d_centroid, float* d_min_dist) {
+    if (!shard || (n && (!d_x || !d_min_dist)) || !d_centroid || dim == 0 || dim > (size_t)INT32_MAX)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("kmeans_shard_pp_update", [&] {
+        shard->eng->pp_update(d_x, n, (int)dim, d_centroid, d_min_dist);
+        shard->eng->sync();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_kmeans_shard_accumulate(vesper_kmeans_shard_t* shard, const float* d_x, size_t n,
+                                                            size_t dim, const uint32_t* d_assign, uint32_t k,
+                                                            uint32_t algorithm, double* d_sum, double* d_comp,
+                                                            uint64_t* d_count) {
+    if (!shard || (n && (!d_x || !d_assign)) || !d_sum || !d_comp || !d_count || k == 0 || dim == 0 ||
+        dim > (size_t)INT32_MAX || algorithm > VESPER_KMEANS_LLOYD)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("kmeans_shard_accumulate", [&] {
+        shard->eng->accumulate(d_x, n, (int)dim, d_assign, k, algorithm == VESPER_KMEANS_ELKAN, d_sum, d_comp,
+                               reinterpret_cast<unsigned long long*>(d_count));
+        shard->eng->sync();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_kmeans_shard_finish(vesper_kmeans_shard_t* shard, const double* d_sum,
+                                                        const uint64_t* d_count, uint32_t k, size_t dim,
+                                                        uint32_t algorithm, float* d_centroids) {
+    if (!shard || !d_sum || !d_count || !d_centroids || k == 0 || dim == 0 || dim > (size_t)INT32_MAX ||
+        algorithm > VESPER_KMEANS_LLOYD)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("kmeans_shard_finish", [&] {
+        shard->eng->finish_means(d_sum, reinterpret_cast<const unsigned long long*>(d_count), k, (int)dim,
+                                 algorithm == VESPER_KMEANS_ELKAN, d_centroids);
+        shard->eng->sync();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_kmeans_shard_running_inertia(vesper_kmeans_shard_t* shard, const float* d_x,
+                                                                 size_t n, size_t dim, const float* d_centroids,
+                                                                 const uint32_t* d_assign, float* inout_total) {
+    if (!shard || (n && (!d_x || !d_assign)) || !d_centroids || !inout_total || dim == 0 || dim > (size_t)INT32_MAX)
+        return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("kmeans_shard_running_inertia", [&] {
+        if (n) shard->eng->running_inertia(d_x, n, (int)dim, d_centroids, d_assign, inout_total);
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_kmeanspp_sampler_create(uint32_t seed, size_t n, vesper_kmeanspp_sampler_t** out,
+                                                            size_t* first_index) {
+    if (!out || !first_index || n == 0) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    *out = nullptr;
+    return guarded("kmeanspp_sampler_create", [&] {
+        *out = new vesper_kmeanspp_sampler_s{vgpu::KmeansPPSampler(seed, n)};
+        *first_index = (*out)->s.first();
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API vesper_status_t vesper_kmeanspp_sampler_next(vesper_kmeanspp_sampler_t* sampler, const float* d2,
+                                                          size_t* index) {
+    if (!sampler || !d2 || !index) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("kmeanspp_sampler_next", [&] {
+        *index = sampler->s.next(d2);
+        return VESPER_OK;
+    });
+}
+
+VESPER_C_API void vesper_kmeanspp_sampler_destroy(vesper_kmeanspp_sampler_t* sampler) { delete sampler; }
+
+}  // extern "C"
+
 namespace {
 // Per-thread flat top-k context on the current device: stream + reusable scratch.
 struct FlatCtx {

@@ -74,3 +74,259 @@ def probed_search(index, queries, k: int, nprobe: int, nlist: int, out_ids, out_
         torch.cuda.current_stream(probe.device).synchronize()
     index.search_batch_device_probed(queries.data_ptr(), nq, k, nprobe, probe.data_ptr(), probe_d.data_ptr(),
                                      out_ids.data_ptr(), out_d.data_ptr(), out_n.data_ptr(), mode=mode)
+
+
+# ------------------------------------------------------------------ sharded k-means
+class KmeansPPSampler:
+    """The k-means++ draws of kmeans_plusplus_init (src/index/kmeans.cpp:45-89) for n
+    points (vesper_kmeanspp_sampler_*): `first` is the first row; `next(d2)` takes the
+    D^2 value of every point (float32, point order) and returns the next row."""
+
+    def __init__(self, seed: int, n: int):
+        import ctypes as C
+
+        from . import _native as N
+        from .index import _check
+        self._lib = N.load()
+        self._h = C.c_void_p()
+        first = C.c_size_t(0)
+        _check(self._lib, self._lib.vesper_kmeanspp_sampler_create(seed, n, C.byref(self._h), C.byref(first)))
+        self.first = int(first.value)
+        self.n = n
+
+    def next(self, d2) -> int:
+        import ctypes as C
+
+        import numpy as np
+
+        from .index import _check
+        h = np.ascontiguousarray(d2, dtype=np.float32)
+        if h.shape != (self.n,):
+            raise ValueError("KmeansPPSampler.next: d2 must hold one value per point")
+        idx = C.c_size_t(0)
+        _check(self._lib, self._lib.vesper_kmeanspp_sampler_next(
+            self._h, h.ctypes.data_as(C.POINTER(C.c_float)), C.byref(idx)))
+        return int(idx.value)
+
+    def close(self):
+        if self._h:
+            self._lib.vesper_kmeanspp_sampler_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+class GpuKmeansOps:
+    """The per-shard k-means steps on this process's current GPU
+    (vesper_kmeans_shard_* in libvesper_c.so).  Tensors are CUDA tensors; assignments
+    are int32 tensors holding the uint32 cluster ids, counts int64 holding uint64."""
+
+    def __init__(self):
+        import ctypes as C
+
+        from . import _native as N
+        from .index import _check
+        self._lib = N.load()
+        self._h = C.c_void_p()
+        _check(self._lib, self._lib.vesper_kmeans_shard_create(C.byref(self._h)))
+
+    @staticmethod
+    def _ready(t):
+        # the library runs on its own stream: finish what torch queued on the inputs
+        import torch
+        if t.is_cuda:
+            torch.cuda.current_stream(t.device).synchronize()
+
+    def _call(self, fn, *args):
+        from .index import _check
+        _check(self._lib, getattr(self._lib, fn)(self._h, *args))
+
+    def assign(self, x, c, keep, a, mind):
+        self._ready(x)
+        self._call("vesper_kmeans_shard_assign", x.data_ptr(), x.shape[0], x.shape[1], c.data_ptr(), c.shape[0],
+                   int(bool(keep)), a.data_ptr(), mind.data_ptr())
+
+    def pp_update(self, x, crow, mind):
+        self._ready(x)
+        self._call("vesper_kmeans_shard_pp_update", x.data_ptr(), x.shape[0], x.shape[1], crow.data_ptr(),
+                   mind.data_ptr())
+
+    def accumulate(self, x, a, k, algorithm, s, comp, count):
+        self._ready(x)
+        self._call("vesper_kmeans_shard_accumulate", x.data_ptr(), x.shape[0], x.shape[1], a.data_ptr(), k,
+                   algorithm, s.data_ptr(), comp.data_ptr(), count.data_ptr())
+
+    def finish(self, s, count, algorithm, c):
+        self._ready(s)
+        self._call("vesper_kmeans_shard_finish", s.data_ptr(), count.data_ptr(), c.shape[0], c.shape[1], algorithm,
+                   c.data_ptr())
+
+    def running_inertia(self, x, c, a, total: float) -> float:
+        import ctypes as C
+        self._ready(x)
+        t = C.c_float(total)
+        self._call("vesper_kmeans_shard_running_inertia", x.data_ptr(), x.shape[0], x.shape[1], c.data_ptr(),
+                   a.data_ptr(), C.byref(t))
+        return t.value
+
+    @staticmethod
+    def sampler(seed: int, n: int):
+        return KmeansPPSampler(seed, n)
+
+    def close(self):
+        if self._h:
+            self._lib.vesper_kmeans_shard_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+def kmeans_fit_sharded(shards, k: int, max_iter: int = 25, epsilon: float = 1e-4, seed: int = 42,
+                       algorithm: int = 0, group=None, ops=None):
+    """k-means over points sharded across processes (one per GPU), equal bit for bit to
+    the one-GPU fit (vesper_kmeans_fit_device) over the concatenation of every rank's
+    shards in rank order.
+
+    `shards`: this rank's [n_i, dim] float32 tensors, in point order (several per rank
+    are allowed).  algorithm 0 = Elkan (KmeansElkan::cluster,
+    src/index/kmeans_elkan.cpp:293-430), 1 = Lloyd (kmeans_cluster, src/index/kmeans.cpp:
+    137-252, one run).  Centroids are replicated; per iteration each rank assigns its own
+    points, the per-point distances are all-gathered for the fp64 inertia in point order,
+    and the mean update is a chain in rank order (each rank continues the per-cluster
+    running sums the previous rank sent it, the last rank finishes the means and
+    broadcasts them), which keeps the reference's point-order sums exact.  k-means++
+    gathers the D^2 vector per centroid and draws on every rank with the same sampler.
+    Lloyd's final inertia, a float running total over every term, travels the same chain.
+
+    Returns (centroids [k, dim] tensor, [assignments per shard], iterations, inertia)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    if ops is None:
+        ops = GpuKmeansOps()
+    on = dist.is_available() and dist.is_initialized()
+    world = dist.get_world_size(group) if on else 1
+    rank = dist.get_rank(group) if on else 0
+    dev = shards[0].device
+    d = int(shards[0].shape[1])
+    n_local = sum(int(s.shape[0]) for s in shards)
+    if world > 1:
+        t = torch.tensor([n_local], dtype=torch.int64, device=dev)
+        allt = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allt, t, group=group)
+        rank_n = [int(v.item()) for v in allt]
+    else:
+        rank_n = [n_local]
+    n = sum(rank_n)
+    if k == 0:
+        raise ValueError("k must be > 0")
+    if n < k:
+        raise ValueError("Not enough data points for k clusters")
+    base = sum(rank_n[:rank])
+    elkan = algorithm == 0
+
+    def src(r):
+        return dist.get_global_rank(group, r) if group is not None else r
+
+    def gather_host(parts):
+        local = torch.cat(parts) if len(parts) > 1 else parts[0]
+        if world == 1:
+            return local.cpu().numpy()
+        m = max(rank_n)
+        buf = torch.zeros(m, dtype=local.dtype, device=dev)
+        buf[:n_local] = local
+        out = torch.empty(world * m, dtype=local.dtype, device=dev)
+        dist.all_gather_into_tensor(out, buf, group=group)
+        h = out.cpu().numpy()
+        return np.concatenate([h[r * m:r * m + rank_n[r]] for r in range(world)])
+
+    def fetch_row(gidx, row):
+        owner = int(np.searchsorted(np.cumsum(rank_n), gidx, side="right"))
+        if owner == rank:
+            i = gidx - base
+            for s in shards:
+                if i < s.shape[0]:
+                    row.copy_(s[i])
+                    break
+                i -= s.shape[0]
+        if world > 1:
+            dist.broadcast(row, src=src(owner), group=group)
+
+    # k-means++ (kmeans.cpp:45-89)
+    cent = torch.empty((k, d), dtype=torch.float32, device=dev)
+    sampler = ops.sampler(seed, n)
+    fetch_row(sampler.first, cent[0])
+    mind = [torch.full((s.shape[0],), float(np.finfo(np.float32).max), dtype=torch.float32, device=dev)
+            for s in shards]
+    for c in range(1, k):
+        for s, md in zip(shards, mind):
+            ops.pp_update(s, cent[c - 1], md)
+        fetch_row(sampler.next(gather_host(mind)), cent[c])
+    sampler.close()
+
+    asg = [torch.zeros(s.shape[0], dtype=torch.int32, device=dev) for s in shards]
+    dst = [torch.empty(s.shape[0], dtype=torch.float32, device=dev) for s in shards]
+
+    def estep(keep):
+        for s, a, md in zip(shards, asg, dst):
+            ops.assign(s, cent, keep, a, md)
+
+    def inertia():
+        h = gather_host(dst).astype(np.float64)
+        return np.float32(np.cumsum(h)[-1]) if h.size else np.float32(0.0)
+
+    def mstep():
+        sm = torch.zeros((k, d), dtype=torch.float64, device=dev)
+        comp = torch.zeros((k, d), dtype=torch.float64, device=dev)
+        cnt = torch.zeros(k, dtype=torch.int64, device=dev)
+        if world > 1 and rank > 0:
+            for t_ in (sm, comp, cnt):
+                dist.recv(t_, src=src(rank - 1), group=group)
+        for s, a in zip(shards, asg):
+            ops.accumulate(s, a, k, algorithm, sm, comp, cnt)
+        if rank < world - 1:
+            for t_ in (sm, comp, cnt):
+                dist.send(t_, dst=src(rank + 1), group=group)
+        else:
+            ops.finish(sm, cnt, algorithm, cent)
+        if world > 1:
+            dist.broadcast(cent, src=src(world - 1), group=group)
+
+    eps = np.float32(epsilon)
+    tiny = np.float32(1e-10)
+    prev = np.float32(np.finfo(np.float32).max)
+    if elkan:
+        estep(False)
+    it = 0
+    while it < max_iter:
+        if not elkan or it > 0:
+            estep(elkan)
+        cur = inertia()
+        change = np.float32(abs(np.float32(prev - cur))) / np.float32(prev + tiny)
+        if change < eps:
+            break
+        prev = cur
+        mstep()
+        it += 1
+    if elkan:
+        result_inertia = float(prev)
+    else:
+        # kmeans.cpp:230-241: one float running total over every term, in point order,
+        # passed along the ranks like the mean-update state
+        mstep()
+        tot = torch.zeros(1, dtype=torch.float32, device=dev)
+        if world > 1 and rank > 0:
+            dist.recv(tot, src=src(rank - 1), group=group)
+        run = float(tot.item())
+        for s, a in zip(shards, asg):
+            run = ops.running_inertia(s, cent, a, run)
+        tot.fill_(run)
+        if rank < world - 1:
+            dist.send(tot, dst=src(rank + 1), group=group)
+        if world > 1:
+            dist.broadcast(tot, src=src(world - 1), group=group)
+        result_inertia = float(tot.item())
+    return cent, asg, it, result_inertia
