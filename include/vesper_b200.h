@@ -352,6 +352,12 @@ VESPER_C_API vesper_status_t vesper_flat_get_last_timings(vesper_flat_timings_t*
 /* Number of CUDA devices visible to the library. */
 VESPER_C_API int vesper_b200_device_count(void);
 
+/* ---------------------------------------------------------------------------------
+ * IndexManager (include/vesper_manager.h): the search mode its IVF-PQ searches use,
+ * VESPER_SEARCH_FAST (default) or VESPER_SEARCH_EXACT (the reference's arithmetic). */
+typedef struct vesper_manager_t vesper_manager_t;
+VESPER_C_API vesper_status_t vesper_mgr_set_search_mode(vesper_manager_t* mgr, uint32_t mode);
+
 #ifdef __cplusplus
 }
 #endif

@@ -160,6 +160,56 @@ class Oracle:
             counts)
         return out_ids, out_d, counts
 
+    def manager_search(self, q, c, R, cb, m, list_offsets, ids, codes, k, nprobe, deleted=(), total_deleted=0,
+                       use_exact_rerank=False, rerank_k=0, rerank_alpha=2.0, ceiling=2000,
+                       filter_by_distance=False):
+        """IndexManager::search (src/index/index_manager.cpp:344-585) over an IVF-PQ index
+        only: nprobe 0 -> 8; with the exact rerank, cand_k = rerank_k or
+        ceil(max(k, alpha * k * log2(1 + nprobe))) capped by the ceiling (:414-436); the
+        tombstone filter on (uint32)id -- or, with filter_by_distance, on the truncated
+        distance, which is what the reference's TombstoneManager::filter_results reads
+        for (id, distance) pairs (tombstone_manager.hpp:150-170); rows left short re-searched
+        with k * factor * 1.5, factor = 1 + 1.25 * total_deleted / 100000
+        (tombstone_manager.cpp:345-351), at most two nested re-searches; truncated to k.
+        Returns per query a list of (id, distance)."""
+        import math
+        nprobe = nprobe if nprobe > 0 else 8
+        dead = set(int(x) & 0xFFFFFFFF for x in deleted)
+        factor = np.float32(1.0 + (total_deleted / 100000.0) * 1.25)
+
+        def level(rows, kk, depth):
+            # a re-search is a new search() call: the heuristic sees its larger k
+            cand_k = 0
+            if use_exact_rerank:
+                if rerank_k > 0:
+                    cand_k = rerank_k
+                else:
+                    h = max(float(kk), float(np.float32(rerank_alpha)) * float(kk) * math.log2(1.0 + nprobe))
+                    cand_k = int(math.ceil(h))
+                    if ceiling > 0:
+                        cand_k = min(cand_k, ceiling)
+            rr_k = rerank_k if rerank_k > 0 else cand_k
+            rid, rd, rcnt = self.ivfpq_search(q[rows], c, R, cb, m, list_offsets, ids, codes, kk, nprobe,
+                                              cand_k=cand_k, rerank=use_exact_rerank, rerank_k=rr_k)
+            res = []
+            for i in range(len(rows)):
+                keep = []
+                for j in range(int(rcnt[i])):
+                    key = int(np.float32(rd[i, j])) & 0xFFFFFFFF if filter_by_distance else int(rid[i, j]) & 0xFFFFFFFF
+                    if key not in dead:
+                        keep.append((int(rid[i, j]), float(rd[i, j])))
+                res.append(keep)
+            short = [i for i in range(len(rows)) if len(res[i]) < kk]
+            if short and factor > np.float32(1.0) and depth < 2:
+                k2 = int(np.float32(np.float32(kk) * factor) * np.float32(1.5))
+                again = level([rows[i] for i in short], k2, depth + 1)
+                for j, i in enumerate(short):
+                    if len(again[j]) >= kk:
+                        res[i] = again[j]
+            return [r[:kk] for r in res]
+
+        return level(list(range(q.shape[0])), k, 0)
+
     # ---- the rest of IvfPqIndex's API (src/index/ivf_pq.cpp:4997-5321, 5392-5541) on a
     # CSR index (list_offsets, ids, codes in list order), restated with the primitives above.
     @staticmethod

@@ -3,6 +3,8 @@ import ctypes as C
 import os
 import re
 
+import numpy as np
+
 import pytest
 
 from conftest import ROOT
@@ -11,7 +13,7 @@ from vesper_db_b200 import _native as N
 
 def declared_symbols():
     names = set()
-    for h in ("vesper.h", "vesper_b200.h"):
+    for h in ("vesper.h", "vesper_b200.h", "vesper_manager.h"):
         text = open(os.path.join(ROOT, "include", h)).read()
         for mt in re.finditer(r"VESPER_C_API\s+[\w\s\*]+?\b(vesper_\w+)\s*\(", text):
             names.add(mt.group(1))
@@ -37,6 +39,73 @@ def test_reference_symbols_present():
     lib = N.load()
     for name in ref:
         assert hasattr(lib, name)
+
+
+def test_manager_symbols_present():
+    # The reference's IndexManager C ABI (include/vesper/c/vesper_manager.h:79-117).
+    ref = ["vesper_mgr_create", "vesper_mgr_destroy", "vesper_mgr_build", "vesper_mgr_add_batch",
+           "vesper_mgr_update", "vesper_mgr_update_batch", "vesper_mgr_remove", "vesper_mgr_remove_batch",
+           "vesper_mgr_search", "vesper_mgr_search_batch", "vesper_mgr_save", "vesper_mgr_load",
+           "vesper_mgr_memory_usage", "vesper_mgr_disk_usage", "vesper_mgr_set_memory_budget_mb",
+           "vesper_mgr_get_memory_budget_mb", "vesper_mgr_get_stats"]
+    lib = N.load()
+    for name in ref:
+        assert hasattr(lib, name)
+
+
+def test_manager_host_logic_without_index():
+    """Entry points that need no GPU index: create, budget, stats, removal bookkeeping,
+    search refusal, and a save/load round trip of the manifest and tombstones (the
+    manager holds no IVF-PQ index, so nothing touches a device)."""
+    import ctypes as C
+    import tempfile
+    lib = N.load()
+    h = C.c_void_p()
+    assert lib.vesper_mgr_create(0, C.byref(h)) == N.VESPER_ERROR_INVALID_PARAM
+    assert lib.vesper_mgr_create(16, C.byref(h)) == N.VESPER_OK
+    try:
+        mb = C.c_uint32(0)
+        assert lib.vesper_mgr_get_memory_budget_mb(h, C.byref(mb)) == N.VESPER_OK and mb.value == 1024
+        assert lib.vesper_mgr_set_memory_budget_mb(h, 77) == N.VESPER_OK
+        lib.vesper_mgr_get_memory_budget_mb(h, C.byref(mb))
+        assert mb.value == 77
+        cnt = C.c_size_t(5)
+        assert lib.vesper_mgr_get_stats(h, None, None, C.byref(cnt)) == N.VESPER_OK and cnt.value == 0
+        for vid in (3, 70000, 2**32 + 5, 123456789):
+            assert lib.vesper_mgr_remove(h, vid) == N.VESPER_OK
+        assert lib.vesper_mgr_remove(h, 3) == N.VESPER_ERROR_INVALID_PARAM
+        assert b"already marked" in lib.vesper_get_last_error()
+        # 5000 ids in one 64K block: a bitset container
+        ids = np.arange(200000, 205000, dtype=np.uint64)
+        assert lib.vesper_mgr_remove_batch(h, ids.ctypes.data_as(C.POINTER(C.c_uint64)), ids.size) == N.VESPER_OK
+        q = np.zeros(16, np.float32)
+        qc = N.QueryConfig()
+        qc.k = 5
+        out_i = np.zeros(5, np.uint64)
+        out_d = np.zeros(5, np.float32)
+        rc = lib.vesper_mgr_search(h, q.ctypes.data_as(C.POINTER(C.c_float)), C.byref(qc),
+                                   out_i.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                   out_d.ctypes.data_as(C.POINTER(C.c_float)))
+        assert rc == N.VESPER_ERROR_INVALID_PARAM and b"No suitable index" in lib.vesper_get_last_error()
+        with tempfile.TemporaryDirectory() as td:
+            assert lib.vesper_mgr_save(h, td.encode()) == N.VESPER_OK
+            raw = open(os.path.join(td, "index_manager.manifest"), "rb").read()
+            # u32 version, u64 dim, u64 total, u64 budget, bool, i32 strategy, i32 type,
+            # u64 budget, u64 cache, 3 x u32 hnsw, 3 x u32 ivf, u32 + f32 + u32 vamana, 3 x bool
+            assert len(raw) == 4 + 8 * 3 + 1 + 4 + 4 + 8 + 8 + 12 + 12 + 12 + 3
+            assert int.from_bytes(raw[4:12], "little") == 16 and int.from_bytes(raw[20:28], "little") == 77
+            h2 = C.c_void_p()
+            assert lib.vesper_mgr_create(4, C.byref(h2)) == N.VESPER_OK
+            try:
+                assert lib.vesper_mgr_load(h2, td.encode()) == N.VESPER_OK
+                # the tombstones came back: removing any of them again is refused
+                for vid in (3, 70000, 5, 123456789, 200000, 204999):
+                    assert lib.vesper_mgr_remove(h2, vid) == N.VESPER_ERROR_INVALID_PARAM, vid
+                assert lib.vesper_mgr_remove(h2, 205000) == N.VESPER_OK
+            finally:
+                lib.vesper_mgr_destroy(h2)
+    finally:
+        lib.vesper_mgr_destroy(h)
 
 
 def test_null_argument_semantics():

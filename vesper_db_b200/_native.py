@@ -45,7 +45,19 @@ EXPORTED = [
     "vesper_kmeans_shard_pp_update", "vesper_kmeans_shard_accumulate", "vesper_kmeans_shard_finish",
     "vesper_kmeans_shard_running_inertia", "vesper_kmeanspp_sampler_create", "vesper_kmeanspp_sampler_next",
     "vesper_kmeanspp_sampler_destroy",
+    "vesper_mgr_create", "vesper_mgr_destroy", "vesper_mgr_build", "vesper_mgr_add_batch", "vesper_mgr_update",
+    "vesper_mgr_update_batch", "vesper_mgr_remove", "vesper_mgr_remove_batch", "vesper_mgr_search",
+    "vesper_mgr_search_batch", "vesper_mgr_save", "vesper_mgr_load", "vesper_mgr_memory_usage",
+    "vesper_mgr_disk_usage", "vesper_mgr_set_memory_budget_mb", "vesper_mgr_get_memory_budget_mb",
+    "vesper_mgr_get_stats", "vesper_mgr_set_search_mode",
 ]
+
+INDEX_HNSW = 0
+INDEX_IVF_PQ = 1
+INDEX_DISKANN = 2
+SELECT_AUTO = 0
+SELECT_MANUAL = 1
+SELECT_HYBRID = 2
 
 KMEANS_ELKAN = 0
 KMEANS_LLOYD = 1
@@ -56,6 +68,33 @@ FLAT_IP = 1
 
 class TrainParams(C.Structure):
     _fields_ = [("nlist", C.c_uint32), ("m", C.c_uint32), ("nbits", C.c_uint32)]
+
+
+class HnswBuildParams(C.Structure):
+    _fields_ = [("M", C.c_uint32), ("ef_construction", C.c_uint32), ("seed", C.c_uint32)]
+
+
+class VamanaBuildParams(C.Structure):
+    _fields_ = [("degree", C.c_uint32), ("L", C.c_uint32), ("alpha", C.c_float)]
+
+
+class ManagerBuildConfig(C.Structure):
+    _fields_ = [("type", C.c_int), ("strategy", C.c_int), ("ivf", TrainParams), ("hnsw", HnswBuildParams),
+                ("vamana", VamanaBuildParams)]
+
+
+class QueryConfig(C.Structure):
+    _fields_ = [("k", C.c_uint32), ("epsilon", C.c_float), ("ef_search", C.c_uint32), ("nprobe", C.c_uint32),
+                ("l_search", C.c_uint32), ("use_exact_rerank", C.c_int), ("rerank_k", C.c_uint32),
+                ("rerank_alpha", C.c_float), ("rerank_cand_ceiling", C.c_uint32), ("use_query_planner", C.c_int),
+                ("has_preferred_index", C.c_int), ("preferred_index", C.c_int), ("has_filter", C.c_int),
+                ("filter_json", C.c_char_p)]
+
+
+class IndexStats(C.Structure):
+    _fields_ = [("type", C.c_int), ("num_vectors", C.c_size_t), ("memory_usage_bytes", C.c_size_t),
+                ("disk_usage_bytes", C.c_size_t), ("build_time_seconds", C.c_float),
+                ("avg_query_time_ms", C.c_float), ("measured_recall", C.c_float), ("query_count", C.c_uint64)]
 
 
 class SearchParams(C.Structure):
@@ -201,6 +240,24 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_kmeanspp_sampler_create": (st, [C.c_uint32, C.c_size_t, C.POINTER(vp), C.POINTER(C.c_size_t)]),
             "vesper_kmeanspp_sampler_next": (st, [vp, f32p, C.POINTER(C.c_size_t)]),
             "vesper_kmeanspp_sampler_destroy": (None, [vp]),
+            "vesper_mgr_create": (st, [C.c_size_t, C.POINTER(vp)]),
+            "vesper_mgr_destroy": (st, [vp]),
+            "vesper_mgr_build": (st, [vp, f32p, C.c_size_t, C.POINTER(ManagerBuildConfig)]),
+            "vesper_mgr_add_batch": (st, [vp, u64p, f32p, C.c_size_t]),
+            "vesper_mgr_update": (st, [vp, C.c_uint64, f32p]),
+            "vesper_mgr_update_batch": (st, [vp, u64p, f32p, C.c_size_t]),
+            "vesper_mgr_remove": (st, [vp, C.c_uint64]),
+            "vesper_mgr_remove_batch": (st, [vp, u64p, C.c_size_t]),
+            "vesper_mgr_search": (st, [vp, f32p, C.POINTER(QueryConfig), u64p, f32p]),
+            "vesper_mgr_search_batch": (st, [vp, f32p, C.c_size_t, C.POINTER(QueryConfig), u64p, f32p]),
+            "vesper_mgr_save": (st, [vp, C.c_char_p]),
+            "vesper_mgr_load": (st, [vp, C.c_char_p]),
+            "vesper_mgr_memory_usage": (st, [vp, C.POINTER(C.c_size_t)]),
+            "vesper_mgr_disk_usage": (st, [vp, C.POINTER(C.c_size_t)]),
+            "vesper_mgr_set_memory_budget_mb": (st, [vp, C.c_uint32]),
+            "vesper_mgr_get_memory_budget_mb": (st, [vp, C.POINTER(C.c_uint32)]),
+            "vesper_mgr_get_stats": (st, [vp, C.POINTER(IndexStats), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+            "vesper_mgr_set_search_mode": (st, [vp, C.c_uint32]),
         }
         for name, (res, args) in proto.items():
             fn = getattr(L, name)

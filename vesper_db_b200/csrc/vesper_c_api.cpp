@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/vesper_b200.h"
+#include "c_error.hpp"
 #include "ivf_pq_gpu.hpp"
 #include "kernels_tc.cuh"
 #include "kmeans_gpu.hpp"
@@ -33,8 +34,17 @@ struct vesper_index_t {
 
 namespace {
 thread_local std::string g_last_error;
+}  // namespace
+
+namespace vesper_c {
 void set_error(const std::string& s) { g_last_error = s; }
 void clear_error() { g_last_error.clear(); }
+}  // namespace vesper_c
+
+using vesper_c::clear_error;
+using vesper_c::set_error;
+
+namespace {
 
 template <class F>
 vesper_status_t guarded(const char* what, F&& f) {
