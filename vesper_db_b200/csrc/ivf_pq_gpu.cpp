@@ -34,6 +34,10 @@ using vgpu::DeviceBuffer;
 namespace {
 
 constexpr size_t kDistBudget = size_t(512) << 20;  // bytes per distance-matrix chunk
+// Search batches are chunked by their coarse distance matrix; one chunk per batch keeps
+// every probed list's codes streamed once and its queries in full tiles (a 10k-query
+// batch at nlist 16384 is 655 MB).
+constexpr size_t kSearchDistBudget = size_t(1) << 30;
 constexpr int kListScanCap = 2048;                   // screened candidates kept per query
 
 auto fail(error_code c, std::string msg, std::string comp = "ivf_pq") {
@@ -1035,7 +1039,7 @@ public:
         const uint32_t k = sp.k;
         const bool exact = sp.mode == SearchMode::Exact;
         // Chunk queries so the coarse distance tile and the exact-path buffers stay bounded.
-        size_t qc = std::max<size_t>(1, kDistBudget / (sizeof(float) * (size_t)nlist()));
+        size_t qc = std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist()));
         if (exact && has_rot) qc = std::min(qc, std::max<size_t>(1, kDistBudget / (sizeof(float) * np * dim)));
         qc = std::min(qc, nq);
         w_D.reserve(qc * nlist());
@@ -1229,7 +1233,7 @@ public:
         if (nq == 0 || np == 0) return {};
         if (np > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "nprobe above 1024 is not supported by the GPU path");
         std::lock_guard<std::mutex> lock(mu);
-        const size_t qc = std::min(nq, std::max<size_t>(1, kDistBudget / (sizeof(float) * (size_t)nlist())));
+        const size_t qc = std::min(nq, std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist())));
         w_D.reserve(qc * nlist());
         for (size_t q0 = 0; q0 < nq; q0 += qc) {
             const size_t nc = std::min(qc, nq - q0);

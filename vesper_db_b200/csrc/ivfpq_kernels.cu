@@ -1265,7 +1265,7 @@ constexpr int SPLIT_MAX_KEYS = 8192;    // keys merged per query (parts x next_p
 __global__ void split_count_kernel(const uint32_t* __restrict__ probe, int nprobe, int nscan,
                                    const uint64_t* __restrict__ blk_off, long long nq,
                                    const uint32_t* __restrict__ only_over, uint32_t over_cap, uint32_t max_parts,
-                                   uint32_t blocks_per_part, uint32_t* __restrict__ parts,
+                                   uint32_t blocks_per_part, uint32_t max_blocks, uint32_t* __restrict__ parts,
                                    uint32_t* __restrict__ nblocks) {
     for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
         uint32_t nb = 0;
@@ -1273,6 +1273,7 @@ __global__ void split_count_kernel(const uint32_t* __restrict__ probe, int nprob
             const uint32_t l = probe[q * nprobe + t];
             nb += (uint32_t)(blk_off[l + 1] - blk_off[l]);
         }
+        nb = min(nb, max_blocks);
         const bool run = !only_over || only_over[q] > over_cap;
         const uint32_t p = (nb + blocks_per_part - 1) / blocks_per_part;
         parts[q] = run ? max(1u, min(p, max_parts)) : 0u;
@@ -1362,15 +1363,15 @@ void launch_scan_blocked_split(const float* T, long long nq, const float* pbase,
                                int nscan, int m, const uint64_t* offs, const uint64_t* blk_off,
                                const uint8_t* bcodes, const float* bvterm, const uint64_t* ids, int k,
                                uint64_t* out_ids, float* out_d, uint32_t* out_n, const uint32_t* only_over,
-                               uint32_t over_cap, SplitWork& w, cudaStream_t st) {
+                               uint32_t over_cap, SplitWork& w, cudaStream_t st, uint32_t max_blocks) {
     if (nq <= 0) return;
     if (k > kMaxK) throw CudaError("scan_blocked_split: k exceeds the supported maximum");
     w.reserve(nq);
     const uint32_t max_parts = (uint32_t)std::max(1, SPLIT_MAX_KEYS / k);
     const int gb = (int)std::min<long long>((nq + 255) / 256, 148LL * 4);
     split_count_kernel<<<gb, 256, 0, st>>>(probe, nprobe, nscan, blk_off, nq, only_over, over_cap, max_parts,
-                                           only_over ? SPLIT_BLOCKS_OVER : SPLIT_BLOCKS, w.parts.data(),
-                                           w.nblocks.data());
+                                           only_over ? SPLIT_BLOCKS_OVER : SPLIT_BLOCKS, max_blocks,
+                                           w.parts.data(), w.nblocks.data());
     VGPU_LAUNCH("split_count_kernel");
     size_t tmp = w.scan_tmp.size();
     check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.parts.data(), w.part_off.data(), (int)(nq + 1), st),

@@ -95,11 +95,12 @@ struct SplitWork {
 // launch_scan_blocked with each query's blocks split over several CTAs (parts of 64
 // blocks, at most 8192 / k parts) and merged: the same results, without a single CTA
 // scanning a very long probe set.  Synchronizes the stream once (number of parts).
+// max_blocks: only the first max_blocks 128-entry blocks of each query's probe set.
 void launch_scan_blocked_split(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,
                                int nscan, int m, const uint64_t* offs, const uint64_t* blk_off,
                                const uint8_t* bcodes, const float* bvterm, const uint64_t* ids, int k,
                                uint64_t* out_ids, float* out_d, uint32_t* out_n, const uint32_t* only_over,
-                               uint32_t over_cap, SplitWork& w, cudaStream_t st);
+                               uint32_t over_cap, SplitWork& w, cudaStream_t st, uint32_t max_blocks = 0xffffffffu);
 // Blocked FAST scan of the first nscan of each query's nprobe probes.  With only_over,
 // a query is processed only when only_over[q] > over_cap (the others are left as is).
 void launch_scan_blocked(const float* T, long long nq, const float* pbase, const uint32_t* probe, int nprobe,

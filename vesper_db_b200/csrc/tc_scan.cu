@@ -1413,9 +1413,15 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.mcount.data(), w.mins_off.data(), (int)(a.nq + 1), st),
           "cub::DeviceScan::ExclusiveSum(mins_off)");
     check(cudaMemcpyAsync(w.host_u32, w.mins_off.data() + a.nq, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
+    // Any k entries of the nearest list bound the k-th distance; scanning a prefix of the
+    // list trades a looser tau for a cheaper threshold pass (VGPU_LIST_HOME_BLOCKS caps it
+    // in 128-entry blocks, at least enough blocks to hold k entries).
+    uint32_t home_blocks = 0xffffffffu;
+    if (const char* v = std::getenv("VGPU_LIST_HOME_BLOCKS"))
+        home_blocks = std::max<uint32_t>((uint32_t)std::strtoul(v, nullptr, 10), (uint32_t)((a.k + 127) / 128));
     launch_scan_blocked_split(a.T, a.nq, a.pbase, a.probe, a.nprobe, 1, a.m, a.offs, a.blk_off, a.bcodes, a.bvterm,
                               a.ids, a.k, w.p1_ids.data(), w.p1_d.data(), w.p1_n.data(), w.run_lut.data(), 0u,
-                              w.split, st);  // synchronizes the stream: host_u32 is ready
+                              w.split, st, home_blocks);  // synchronizes the stream: host_u32 is ready
     const uint32_t n_mins = *w.host_u32;
     if (n_mins > 0) {
         w.mins.reserve(n_mins);
