@@ -133,3 +133,21 @@ def test_exact_ties_keep_scan_order():
         (bi, bd, bn), _ = _search(idx, q, k, npb, "blocked")
         (ti, td, tn), _ = _search(idx, q, k, npb, "tc")
         assert np.array_equal(bn, tn) and np.array_equal(bd, td) and np.array_equal(bi, ti)
+
+
+@pytest.mark.parametrize("dim,m", [(128, 16), (128, 32), (256, 64), (64, 16), (96, 24), (256, 16), (64, 32), (256, 32)])
+def test_register_lut_equals_generic_lut(dim, m):
+    """The register-resident table kernel (thread-fixed entries) writes the same tables
+    as the generic one: FAST searches through both are bit-identical (dsub = dim / m in
+    {2, 4, 8, 16}, sub-space groups of 4 to 32)."""
+    rng = np.random.default_rng(dim + m)
+    idx, cent = _build(rng, dim, m, 32, 6000, True)
+    q = (cent[rng.integers(0, 32, 70)] + 0.3 * rng.standard_normal((70, dim))).astype(np.float32)
+    a, _ = _search(idx, q, 10, 4, "blocked")
+    os.environ["VGPU_LUT_GENERIC"] = "1"
+    try:
+        b, _ = _search(idx, q, 10, 4, "blocked")
+    finally:
+        os.environ.pop("VGPU_LUT_GENERIC", None)
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y)

@@ -38,7 +38,7 @@ constexpr size_t kDistBudget = size_t(512) << 20;  // bytes per distance-matrix 
 // every probed list's codes streamed once and its queries in full tiles (a 10k-query
 // batch at nlist 16384 is 655 MB).
 constexpr size_t kSearchDistBudget = size_t(1) << 30;
-constexpr int kListScanCap = 2048;                   // screened candidates kept per query
+constexpr int kListScanCap = 4096;                   // screened candidates kept per query (2048: more overflow fallbacks, 8192: no faster)
 
 auto fail(error_code c, std::string msg, std::string comp = "ivf_pq") {
     return std::unexpected(error{c, std::move(msg), std::move(comp)});
@@ -1067,7 +1067,9 @@ public:
         const bool list_scan = !exact && use_list_scan(nq, np);
         const bool split_scan = !exact && !list_scan && has_blocks && use_split_scan();
         if (list_scan) {
-            tlw.reserve((long long)qc, (int)np, (int)nlist(), (int)dim, (int)k, kListScanCap, n_vectors);
+            int cap = kListScanCap;
+            if (const char* v = std::getenv("VGPU_LIST_CAP")) cap = std::clamp(std::atoi(v), 256, 16384);
+            tlw.reserve((long long)qc, (int)np, (int)nlist(), (int)dim, (int)k, cap, n_vectors);
             vgpu::check(cudaMemsetAsync(tlw.stats.data(), 0, 2 * sizeof(unsigned long long), st), "memset");
             reset_err();
         }

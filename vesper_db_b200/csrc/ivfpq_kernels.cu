@@ -12,6 +12,8 @@
 
 #include <cfloat>
 
+#include <cstdlib>
+
 #include "kernels.cuh"
 #include "select.cuh"
 
@@ -1003,10 +1005,93 @@ __global__ void __launch_bounds__(256) lut_blocked_kernel(const float* __restric
     }
 }
 
+// The same tables with each thread's entries fixed: thread x owns entries r = x + 256 j
+// (j < R = G / 4) of every query, which share the sub-space s_lo = x % G, so it keeps
+// their codebook sub-vectors in registers, reads one query slice per query from shared
+// memory, and writes R coalesced entries per query.  No integer division per entry;
+// the store of T is the bound.  Same arithmetic, same order as lut_blocked_kernel.
+template <int DSUB, int R>
+__global__ void __launch_bounds__(256) lut_blocked_reg_kernel(const float* __restrict__ rq, long long nq, int dim,
+                                                              const float* __restrict__ cb, int m, int G,
+                                                              float* __restrict__ T) {
+    extern __shared__ __align__(16) float qs[];     // [LB_Q][DSUB][G]
+    const int g = blockIdx.y, c0 = blockIdx.z * LB_C;
+    const long long qb = (long long)blockIdx.x * LB_Q;
+    const int nqq = (int)min((long long)LB_Q, nq - qb);
+    for (int e = threadIdx.x; e < nqq * DSUB * G; e += blockDim.x) {
+        const int qi = e / (DSUB * G), r = e % (DSUB * G), t = r % DSUB, s_lo = r / DSUB;
+        qs[(qi * DSUB + t) * G + s_lo] = rq[(qb + qi) * dim + (long long)g * G * DSUB + r];
+    }
+    const int s_lo = threadIdx.x % G;
+    float y[R][DSUB];
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        const int c = (threadIdx.x + 256 * j) / G;
+        const float* src = cb + ((long long)(g * G + s_lo) * 256 + c0 + c) * DSUB;
+#pragma unroll
+        for (int t = 0; t < DSUB; ++t) y[j][t] = src[t];
+    }
+    __syncthreads();
+    const long long row = (long long)m * 256;
+    float* Tb = T + qb * row + ((long long)g * 256 + c0) * G + threadIdx.x;
+    for (int qi = 0; qi < nqq; ++qi) {
+        float qv[DSUB];
+#pragma unroll
+        for (int t = 0; t < DSUB; ++t) qv[t] = qs[(qi * DSUB + t) * G + s_lo];
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int t = 0; t < DSUB; ++t) acc = fmaf(qv[t], y[j][t], acc);
+            Tb[qi * row + 256 * j] = -2.0f * acc;
+        }
+    }
+}
+
+namespace {
+template <int DSUB, int R>
+bool lut_reg_launch(const float* rq, long long nq, int dim, const float* cb, int m, int G, float* T, cudaStream_t st) {
+    const size_t smem = (size_t)LB_Q * DSUB * G * sizeof(float);
+    VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_reg_kernel<DSUB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem));
+    dim3 grid(ceil_div(nq, LB_Q), m / G, 256 / LB_C);
+    lut_blocked_reg_kernel<DSUB, R><<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, G, T);
+    VGPU_LAUNCH("lut_blocked_reg_kernel");
+    return true;
+}
+
+template <int DSUB>
+bool lut_reg_dispatch(const float* rq, long long nq, int dim, const float* cb, int m, int G, float* T,
+                      cudaStream_t st) {
+    const int R = LB_C * G / 256;
+    if (R * DSUB > 64) return false;
+    switch (R) {
+        case 1: return lut_reg_launch<DSUB, 1>(rq, nq, dim, cb, m, G, T, st);
+        case 2: return lut_reg_launch<DSUB, 2>(rq, nq, dim, cb, m, G, T, st);
+        case 4: return lut_reg_launch<DSUB, 4>(rq, nq, dim, cb, m, G, T, st);
+        case 8:
+            if constexpr (DSUB <= 8) return lut_reg_launch<DSUB, 8>(rq, nq, dim, cb, m, G, T, st);
+            return false;
+        default: return false;
+    }
+}
+}  // namespace
+
 void launch_lut_blocked(const float* rq, long long nq, int dim, const float* cb, int m, int dsub, float* T,
                         cudaStream_t st) {
     if (nq <= 0) return;
     const int G = scan_group(m);
+    if (G > 0 && 256 % G == 0 && !std::getenv("VGPU_LUT_GENERIC")) {
+        bool done = false;
+        switch (dsub) {
+            case 2: done = lut_reg_dispatch<2>(rq, nq, dim, cb, m, G, T, st); break;
+            case 4: done = lut_reg_dispatch<4>(rq, nq, dim, cb, m, G, T, st); break;
+            case 8: done = lut_reg_dispatch<8>(rq, nq, dim, cb, m, G, T, st); break;
+            case 16: done = lut_reg_dispatch<16>(rq, nq, dim, cb, m, G, T, st); break;
+            default: break;
+        }
+        if (done) return;
+    }
     const size_t smem = ((size_t)LB_C * dsub * G + (size_t)LB_Q * dsub * G) * sizeof(float);
     if (smem > 200 * 1024) throw CudaError("lut_blocked: sub-space codebook slice too large for shared memory");
     VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
