@@ -168,6 +168,7 @@ def _nccl_worker(rank, world, port, out_path, algorithm):
         dist.destroy_process_group()
 
 
+@pytest.mark.timeout(600)
 @pytest.mark.parametrize("algorithm", [0, 1])
 def test_two_gpu_sharded_fit_equals_single_gpu(tmp_path, algorithm):
     import torch
