@@ -252,6 +252,40 @@ void refine_launch(const float* q, const float* base, long long ld, int dim, con
 }
 
 
+// Sample stride of a view of n rows at top-k k: the sample's k-th best is about the
+// (k * stride)-th best of the view, so about k * stride columns survive the filter:
+// stride <= cap / (2k).  Below 2 the view is screened in one pass.
+long long flat_sample_stride(long long n, int k) {
+    const int cap = k <= 128 ? 4096 : 16384;
+    const long long ke = std::min<long long>(k, n);
+    long long stride = std::min<long long>(FLAT_STRIDE, std::max(1, cap / (2 * k)));
+    while (stride > 1 && (n + stride - 1) / stride < ke) stride >>= 1;
+    return stride;
+}
+
+// A base arriving from host memory in chunks (launch_flat_topk_host): rows [0, normed)
+// have landed as far as the compute stream knows and have their norms.
+struct Feed {
+    const float* base;
+    long long nb, chunk;
+    int dim;
+    float* cn;
+    float* cs;
+    cudaEvent_t sample;
+    const std::vector<cudaEvent_t>* ev;
+    long long normed = 0;
+    void ready(long long upto, cudaStream_t st, int& launches) {
+        while (normed < upto) {
+            const long long i = normed / chunk, r1 = std::min(nb, (i + 1) * chunk);
+            check(cudaStreamWaitEvent(st, (*ev)[(size_t)i], 0), "cudaStreamWaitEvent");
+            launch_row_norms(base + normed * dim, r1 - normed, dim, cn + normed, st);
+            launch_sqrt(cn + normed, r1 - normed, cs + normed, st);
+            launches += 2;
+            normed = r1;
+        }
+    }
+};
+
 // A view of the base: row j at base + j * ld, with its squared norms and their roots.
 struct View {
     const float* base;
@@ -265,19 +299,13 @@ struct View {
 // threshold from the exact top-k of a strided sample of themselves (recursively), then
 // one filtering screen and the refine.  `stats` (top level only) receives stage times.
 void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, const View& v, int k,
-               uint32_t* out_idx, float* out_val, FlatWork& w, int depth, FlatStats* stats, cudaStream_t st) {
+               uint32_t* out_idx, float* out_val, FlatWork& w, int depth, FlatStats* stats, cudaStream_t st,
+               Feed* feed = nullptr) {
     const int ke = (int)std::min<long long>(k, v.n);
-    if (v.n <= FLAT_SINGLE || depth + 1 >= FlatWork::kLevels) {
-        exact_rows(ip, q, nq, xn, v.base, v.n, v.ld, v.cn, dim, k, out_idx, out_val, w, st);
-        if (stats) stats->single_pass = 1;
-        return;
-    }
-    // The sample's k-th best is about the (k * stride)-th best of the view, so about
-    // k * stride columns survive the filter: stride <= cap / (2k).
     const int cap = k <= 128 ? 4096 : 16384;
-    long long stride = std::min<long long>(FLAT_STRIDE, std::max(1, cap / (2 * k)));
-    while (stride > 1 && (v.n + stride - 1) / stride < ke) stride >>= 1;
-    if (stride < 2) {
+    const long long stride = flat_sample_stride(v.n, k);
+    if (v.n <= FLAT_SINGLE || depth + 1 >= FlatWork::kLevels || stride < 2) {
+        if (feed) feed->ready(v.n, st, w.launches);
         exact_rows(ip, q, nq, xn, v.base, v.n, v.ld, v.cn, dim, k, out_idx, out_val, w, st);
         if (stats) stats->single_pass = 1;
         return;
@@ -288,10 +316,18 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     L.cs.reserve(ns);
     L.s_idx.reserve((size_t)nq * k);
     L.s_val.reserve((size_t)nq * k);
-    gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cn, ns, stride, L.cn.data());
-    check(cudaGetLastError(), "gather_stride_kernel");
-    gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cs, ns, stride, L.cs.data());
-    check(cudaGetLastError(), "gather_stride_kernel");
+    if (feed) {
+        // the sample rows were copied first: their norms straight from the strided rows
+        // (the same arithmetic as the full-base norms they would be gathered from)
+        check(cudaStreamWaitEvent(st, feed->sample, 0), "cudaStreamWaitEvent");
+        launch_row_norms(v.base, ns, dim, L.cn.data(), st, v.ld * stride);
+        launch_sqrt(L.cn.data(), ns, L.cs.data(), st);
+    } else {
+        gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cn, ns, stride, L.cn.data());
+        check(cudaGetLastError(), "gather_stride_kernel");
+        gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cs, ns, stride, L.cs.data());
+        check(cudaGetLastError(), "gather_stride_kernel");
+    }
     w.launches += 2;
     if (stats) check(cudaEventRecord(w.ev[1], st), "event");
     const View sample{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
@@ -313,10 +349,14 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     for (long long q0 = 0; q0 < nq; q0 += qc) {
         const long long n = std::min(qc, nq - q0);
         if (stats) check(cudaEventRecord(w.ev[3], st), "event");
-        for (long long c0 = 0; c0 < v.n; c0 += FILTER_COLS, ++w.launches)
-            launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, std::min(FILTER_COLS, v.n - c0), v.ld, dim,
+        // with a feed, one launch per copied chunk, each after its chunk lands
+        const long long step = feed ? std::min(FILTER_COLS, feed->chunk) : FILTER_COLS;
+        for (long long c0 = 0; c0 < v.n; c0 += step, ++w.launches) {
+            if (feed) feed->ready(std::min(v.n, c0 + step), st, w.launches);
+            launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, std::min(step, v.n - c0), v.ld, dim,
                              xn + q0, v.cn + c0, v.cs + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(),
                              w.cand_cnt.data() + q0, cap, w.err.data(), st);
+        }
         if (stats) check(cudaEventRecord(w.ev[4], st), "event");
         ++w.launches;
         if (ip)
@@ -381,17 +421,17 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
 FlatWork::~FlatWork() {
     for (auto& e : ev)
         if (e) cudaEventDestroy(e);
+    for (auto& e : chunk_ev) cudaEventDestroy(e);
+    if (sample_ev) cudaEventDestroy(sample_ev);
+    if (copy_st) {
+        cudaStreamSynchronize(copy_st);
+        cudaStreamDestroy(copy_st);
+    }
 }
 
-void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
-                      uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st) {
-    w.last = FlatStats{};
-    if (nq <= 0 || nb <= 0 || k <= 0) return;
-    if (k > kMaxK) throw CudaError("flat_topk: k exceeds the supported maximum (1024)");
-    if (!tc_screen_supported(dim)) throw CudaError("flat_topk: dim must be a multiple of 4 and >= 32");
-    if (nb > 0x7fffffffLL) throw CudaError("flat_topk: at most 2^31 - 1 base vectors");
-    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(base)) & 15)
-        throw CudaError("flat_topk: queries and base must be 16-byte aligned");
+namespace {
+void flat_topk_body(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
+                    uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st, Feed* feed) {
     if (!w.ev[0])
         for (auto& e : w.ev) check(cudaEventCreate(&e), "cudaEventCreate");
     const int ke = (int)std::min<long long>(k, nb);
@@ -402,14 +442,20 @@ void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, 
     check(cudaMemsetAsync(w.err.data(), 0, sizeof(int), st), "memset");
     check(cudaEventRecord(w.ev[0], st), "event");
     launch_row_norms(q, nq, dim, w.xn.data(), st);
-    launch_row_norms(base, nb, dim, w.cn.data(), st);
-    launch_sqrt(w.cn.data(), nb, w.csq.data(), st);
-    w.launches = 3;
+    w.launches = 1;
+    if (feed) {
+        feed->cn = w.cn.data();
+        feed->cs = w.csq.data();
+    } else {
+        launch_row_norms(base, nb, dim, w.cn.data(), st);
+        launch_sqrt(w.cn.data(), nb, w.csq.data(), st);
+        w.launches += 2;
+    }
     check(cudaEventRecord(w.ev[1], st), "event");
     check(cudaEventRecord(w.ev[2], st), "event");
     FlatStats stats;
     const View v{base, nb, dim, w.cn.data(), w.csq.data()};
-    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st);
+    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st, feed);
     if (k > ke) {
         pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
         check(cudaGetLastError(), "pad_topk_kernel");
@@ -435,6 +481,73 @@ void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, 
     }
     stats.launches = (uint32_t)w.launches;
     w.last = stats;
+}
+
+void check_flat_args(const float* q, const float* base, long long nb, int dim, int k) {
+    if (k > kMaxK) throw CudaError("flat_topk: k exceeds the supported maximum (1024)");
+    if (!tc_screen_supported(dim)) throw CudaError("flat_topk: dim must be a multiple of 4 and >= 32");
+    if (nb > 0x7fffffffLL) throw CudaError("flat_topk: at most 2^31 - 1 base vectors");
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(base)) & 15)
+        throw CudaError("flat_topk: queries and base must be 16-byte aligned");
+}
+}  // namespace
+
+void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
+                      uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st) {
+    w.last = FlatStats{};
+    if (nq <= 0 || nb <= 0 || k <= 0) return;
+    check_flat_args(q, base, nb, dim, k);
+    flat_topk_body(ip, q, nq, base, nb, dim, k, out_idx, out_score, w, st, nullptr);
+}
+
+void launch_flat_topk_host(bool ip, const float* q, long long nq, const float* host_base, float* dev_base,
+                           long long nb, int dim, int k, uint32_t* out_idx, float* out_score, FlatWork& w,
+                           cudaStream_t st) {
+    w.last = FlatStats{};
+    if (nq <= 0 || nb <= 0 || k <= 0) return;
+    check_flat_args(q, dev_base, nb, dim, k);
+    const size_t row = (size_t)dim * sizeof(float);
+    const long long stride = flat_sample_stride(nb, k);
+    if (nb <= FLAT_SINGLE || stride < 2) {
+        // one screen over the whole base: nothing to overlap
+        check(cudaMemcpyAsync(dev_base, host_base, (size_t)nb * row, cudaMemcpyHostToDevice, st), "h2d");
+        flat_topk_body(ip, q, nq, dev_base, nb, dim, k, out_idx, out_score, w, st, nullptr);
+        return;
+    }
+    constexpr int kChunks = 8;
+    const long long chunk = ((nb + kChunks - 1) / kChunks + 255) / 256 * 256;
+    const long long n_chunks = (nb + chunk - 1) / chunk;
+    if (!w.copy_st) {
+        check(cudaStreamCreateWithFlags(&w.copy_st, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaEventCreateWithFlags(&w.sample_ev, cudaEventDisableTiming), "cudaEventCreate");
+    }
+    while ((long long)w.chunk_ev.size() < n_chunks) {
+        cudaEvent_t e = nullptr;
+        check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        w.chunk_ev.push_back(e);
+    }
+    // The copies must not outlive this call's use of dev_base, whatever happens.
+    struct CopyDone {
+        cudaStream_t s;
+        ~CopyDone() { cudaStreamSynchronize(s); }
+    } done{w.copy_st};
+    // order the copies after the caller's earlier work on st
+    check(cudaEventRecord(w.sample_ev, st), "cudaEventRecord");
+    check(cudaStreamWaitEvent(w.copy_st, w.sample_ev, 0), "cudaStreamWaitEvent");
+    const long long ns = (nb + stride - 1) / stride;
+    check(cudaMemcpy2DAsync(dev_base, (size_t)stride * row, host_base, (size_t)stride * row, row, (size_t)ns,
+                            cudaMemcpyHostToDevice, w.copy_st),
+          "h2d (sample rows)");
+    check(cudaEventRecord(w.sample_ev, w.copy_st), "cudaEventRecord");
+    for (long long i = 0; i < n_chunks; ++i) {
+        const long long r0 = i * chunk, r1 = std::min(nb, r0 + chunk);
+        check(cudaMemcpyAsync(dev_base + r0 * dim, host_base + r0 * dim, (size_t)(r1 - r0) * row,
+                              cudaMemcpyHostToDevice, w.copy_st),
+              "h2d (chunk)");
+        check(cudaEventRecord(w.chunk_ev[(size_t)i], w.copy_st), "cudaEventRecord");
+    }
+    Feed feed{dev_base, nb, chunk, dim, nullptr, nullptr, w.sample_ev, &w.chunk_ev};
+    flat_topk_body(ip, q, nq, dev_base, nb, dim, k, out_idx, out_score, w, st, &feed);
 }
 
 }  // namespace vgpu

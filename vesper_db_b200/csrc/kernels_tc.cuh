@@ -1,6 +1,8 @@
 // Tensor-core screening + exact refine for nearest-centroid search (tc_coarse.cu).
 #pragma once
 
+#include <vector>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -47,6 +49,10 @@ struct FlatWork {
     DeviceBuffer<uint2> cand;
     DeviceBuffer<int> err;
     cudaEvent_t ev[7] = {};
+    // host-resident base: copy stream, sample-rows event, per-chunk events
+    cudaStream_t copy_st = nullptr;
+    cudaEvent_t sample_ev = nullptr;
+    std::vector<cudaEvent_t> chunk_ev;
     FlatStats last;
     int launches = 0;
     FlatWork() = default;
@@ -58,9 +64,16 @@ struct FlatWork {
 // rows (16-byte aligned); out_idx/out_score: device [nq x k].  Synchronous on st.
 void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
                       uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st);
+// The same with the base in host memory (pinned for the copy to overlap): `dev_base`
+// [nb x dim] receives it.  The threshold pass's sample rows are copied first; the rest
+// arrives in chunks on a second stream while the sample pass runs, and each chunk is
+// filtered as soon as it lands.  Results are those of launch_flat_topk on the copied base.
+void launch_flat_topk_host(bool ip, const float* q, long long nq, const float* host_base, float* dev_base,
+                           long long nb, int dim, int k, uint32_t* out_idx, float* out_score, FlatWork& w,
+                           cudaStream_t st);
 
-// out[i] = ||x_i||^2 (fp64 accumulation).
-void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st);
+// out[i] = ||x_i||^2 (fp64 accumulation); row i at x + i * ld (ld = dim by default).
+void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st, long long ld = 0);
 // Per row: exact k nearest centroids (reference-order distances, ties to the lowest
 // index; `keep` applies Elkan's keep-on-tie rule to the nearest).  Dt from
 // launch_tc_screen bounds which centroids need the exact recomputation.

@@ -376,22 +376,23 @@ void launch_sqrt(const float* in, long long n, float* out, cudaStream_t st) {
 // ---------------------------------------------------------------------------------
 // Row norms (fp64 accumulate, one rounding) for the screen.
 // ---------------------------------------------------------------------------------
-__global__ void row_norms_kernel(const float* __restrict__ x, long long n, int dim, float* __restrict__ out) {
+__global__ void row_norms_kernel(const float* __restrict__ x, long long n, int dim, long long ld,
+                                 float* __restrict__ out) {
     const int lane = threadIdx.x & 31;
     const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
     for (long long i = warp; i < n; i += nw) {
         double s = 0.0;
-        for (int d = lane; d < dim; d += 32) { const double v = x[i * dim + d]; s += v * v; }
+        for (int d = lane; d < dim; d += 32) { const double v = x[i * ld + d]; s += v * v; }
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
         if (lane == 0) out[i] = (float)s;
     }
 }
 
-void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st) {
+void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st, long long ld) {
     if (n <= 0) return;
     const int blocks = (int)std::min<long long>((n * 32 + 255) / 256, 148LL * 32);
-    row_norms_kernel<<<blocks, 256, 0, st>>>(x, n, dim, out);
+    row_norms_kernel<<<blocks, 256, 0, st>>>(x, n, dim, ld > 0 ? ld : dim, out);
     check(cudaGetLastError(), "row_norms_kernel");
 }
 

@@ -855,15 +855,16 @@ vesper_status_t flat_topk(vesper_flat_op_t op, const float* q, size_t nq, const 
             i_own.resize(nq * k);
             s_own.resize(nq * k);
             vgpu::check(cudaMemcpyAsync(q_own.data(), q, nq * dim * sizeof(float), cudaMemcpyHostToDevice, st), "h2d");
-            vgpu::check(cudaMemcpyAsync(b_own.data(), base, nb * dim * sizeof(float), cudaMemcpyHostToDevice, st),
-                        "h2d");
             dq = q_own.data();
-            db = b_own.data();
             di = i_own.data();
             ds = s_own.data();
+            // the base's copy overlaps the threshold pass and the filter
+            vgpu::launch_flat_topk_host(op == VESPER_FLAT_IP, dq, (long long)nq, base, b_own.data(), (long long)nb,
+                                        (int)dim, (int)k, di, ds, *ctx.w, st);
+        } else {
+            vgpu::launch_flat_topk(op == VESPER_FLAT_IP, dq, (long long)nq, db, (long long)nb, (int)dim, (int)k, di,
+                                   ds, *ctx.w, st);
         }
-        vgpu::launch_flat_topk(op == VESPER_FLAT_IP, dq, (long long)nq, db, (long long)nb, (int)dim, (int)k, di, ds,
-                               *ctx.w, st);
         if (!on_device) {
             vgpu::check(cudaMemcpyAsync(out_i, di, nq * k * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "d2h");
             vgpu::check(cudaMemcpyAsync(out_s, ds, nq * k * sizeof(float), cudaMemcpyDeviceToHost, st), "d2h");
