@@ -271,6 +271,7 @@ struct Feed {
     int dim;
     float* cn;
     float* cs;
+    const float* sample_rows;   // every stride-th base row, contiguous, copied first
     cudaEvent_t sample;
     const std::vector<cudaEvent_t>* ev;
     long long normed = 0;
@@ -317,10 +318,11 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     L.s_idx.reserve((size_t)nq * k);
     L.s_val.reserve((size_t)nq * k);
     if (feed) {
-        // the sample rows were copied first: their norms straight from the strided rows
+        // the sample rows were copied first, into their own buffer (so the chunk copies
+        // never write rows the sample pass reads); their norms come straight from them
         // (the same arithmetic as the full-base norms they would be gathered from)
         check(cudaStreamWaitEvent(st, feed->sample, 0), "cudaStreamWaitEvent");
-        launch_row_norms(v.base, ns, dim, L.cn.data(), st, v.ld * stride);
+        launch_row_norms(feed->sample_rows, ns, dim, L.cn.data(), st);
         launch_sqrt(L.cn.data(), ns, L.cs.data(), st);
     } else {
         gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cn, ns, stride, L.cn.data());
@@ -330,7 +332,8 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     }
     w.launches += 2;
     if (stats) check(cudaEventRecord(w.ev[1], st), "event");
-    const View sample{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
+    const View sample = feed ? View{feed->sample_rows, ns, (long long)dim, L.cn.data(), L.cs.data()}
+                             : View{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
     view_topk(ip, q, nq, xn, dim, sample, k, L.s_idx.data(), L.s_val.data(), w, depth + 1, nullptr, st);
     w.tau.reserve(nq);
     flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(L.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
@@ -535,7 +538,8 @@ void launch_flat_topk_host(bool ip, const float* q, long long nq, const float* h
     check(cudaEventRecord(w.sample_ev, st), "cudaEventRecord");
     check(cudaStreamWaitEvent(w.copy_st, w.sample_ev, 0), "cudaStreamWaitEvent");
     const long long ns = (nb + stride - 1) / stride;
-    check(cudaMemcpy2DAsync(dev_base, (size_t)stride * row, host_base, (size_t)stride * row, row, (size_t)ns,
+    w.sample_rows.reserve((size_t)ns * dim);
+    check(cudaMemcpy2DAsync(w.sample_rows.data(), row, host_base, (size_t)stride * row, row, (size_t)ns,
                             cudaMemcpyHostToDevice, w.copy_st),
           "h2d (sample rows)");
     check(cudaEventRecord(w.sample_ev, w.copy_st), "cudaEventRecord");
@@ -546,7 +550,7 @@ void launch_flat_topk_host(bool ip, const float* q, long long nq, const float* h
               "h2d (chunk)");
         check(cudaEventRecord(w.chunk_ev[(size_t)i], w.copy_st), "cudaEventRecord");
     }
-    Feed feed{dev_base, nb, chunk, dim, nullptr, nullptr, w.sample_ev, &w.chunk_ev};
+    Feed feed{dev_base, nb, chunk, dim, nullptr, nullptr, w.sample_rows.data(), w.sample_ev, &w.chunk_ev};
     flat_topk_body(ip, q, nq, dev_base, nb, dim, k, out_idx, out_score, w, st, &feed);
 }
 

@@ -52,6 +52,7 @@ struct FlatWork {
     // host-resident base: copy stream, sample-rows event, per-chunk events
     cudaStream_t copy_st = nullptr;
     cudaEvent_t sample_ev = nullptr;
+    DeviceBuffer<float> sample_rows;   // the threshold pass's rows, copied apart from the base
     std::vector<cudaEvent_t> chunk_ev;
     FlatStats last;
     int launches = 0;
