@@ -128,3 +128,34 @@ def test_empty_inputs_write_nothing():
     base = np.ones((10, 32), np.float32)
     i, s = flat_topk(0, np.zeros((0, 32), np.float32), base, 5)
     assert i.shape == (0, 5)
+
+
+@pytest.mark.parametrize("op", [0, 1])
+def test_pinned_host_base_equals_device_base(op):
+    """With the base in pinned host memory the copy runs in chunks on a second stream
+    while the threshold pass and the per-chunk filters run; results must equal the
+    device-resident call's bit for bit (two calls, so the reused copy stream and sample
+    buffer are exercised)."""
+    import ctypes as C
+
+    import torch
+    from vesper_db_b200 import _native as N
+    from vesper_db_b200 import flat_topk_device
+    lib = N.load()
+    rng = np.random.default_rng(40 + op)
+    for nb, dim, nq, k in [(300000, 128, 96, 100), (120000, 64, 50, 10)]:
+        base = torch.from_numpy(rng.standard_normal((nb, dim)).astype(np.float32)).pin_memory()
+        q = torch.from_numpy(rng.standard_normal((nq, dim)).astype(np.float32)).pin_memory()
+        hi = np.zeros((nq, k), np.uint32)
+        hs = np.zeros((nq, k), np.float32)
+        f32p = C.POINTER(C.c_float)
+        st = lib.vesper_flat_topk(op, C.cast(q.data_ptr(), f32p), nq, C.cast(base.data_ptr(), f32p), nb, dim, k,
+                                  hi.ctypes.data_as(C.POINTER(C.c_uint32)), hs.ctypes.data_as(f32p))
+        assert st == N.VESPER_OK
+        db, dq = base.cuda(), q.cuda()
+        di = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+        ds = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        flat_topk_device(op, dq.data_ptr(), nq, db.data_ptr(), nb, dim, k, di.data_ptr(), ds.data_ptr())
+        assert np.array_equal(di.cpu().numpy().view(np.uint32), hi)
+        assert np.array_equal(ds.cpu().numpy(), hs)
