@@ -155,9 +155,6 @@ void launch_finish_means(const double* sum, const unsigned long long* count, int
 // one rounded float add per term (kmeans_cluster's final inertia).
 void launch_ordered_sq_sum(const float* x, const float* c, const uint32_t* assign, long long n, int dim,
                            float* total, cudaStream_t st);
-// out[i] = l2(x_i, c[assign[i]]) in reference order.
-void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,
-                        cudaStream_t st);
 
 // ----------------------------------------------------------------------- exact rerank (rerank.cu)
 void launch_iota(uint32_t* out, long long n, cudaStream_t st);

@@ -152,86 +152,3 @@ void launch_finish_means(const double* sum, const unsigned long long* count, int
 }
 
 }  // namespace vgpu
-
-namespace vgpu {
-
-// out[i] = l2_ref(x_i, c[assign[i]]) (one warp per row, lanes 0..7 run the 8 chains).
-__global__ void assigned_l2_kernel(const float* __restrict__ x, const float* __restrict__ c,
-                                   const uint32_t* __restrict__ assign, long long n, int dim,
-                                   float* __restrict__ out) {
-    const int lane = threadIdx.x & 31;
-    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
-    const int simd_end = dim & ~7;
-    for (long long i = warp; i < n; i += nw) {
-        const float* p = x + i * dim;
-        const float* q = c + (long long)assign[i] * dim;
-        float acc = 0.0f;
-        if (lane < 8)
-            for (int t = lane; t < simd_end; t += 8) {
-                const float d = __fsub_rn(p[t], q[t]);
-                acc = __fmaf_rn(d, d, acc);
-            }
-        const float a4 = __shfl_down_sync(0xffffffffu, acc, 4);
-        const float s = __fadd_rn(a4, acc);
-        const float s1 = __shfl_down_sync(0xffffffffu, s, 1);
-        const float s2 = __shfl_down_sync(0xffffffffu, s, 2);
-        const float s3 = __shfl_down_sync(0xffffffffu, s, 3);
-        if (lane == 0) {
-            float r = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
-            for (int t = simd_end; t < dim; ++t) {
-                const float d = __fsub_rn(p[t], q[t]);
-                r = __fadd_rn(r, __fmul_rn(d, d));
-            }
-            out[i] = r;
-        }
-    }
-}
-
-// The final inertia of kmeans_cluster (src/index/kmeans.cpp:230-241): ONE float running
-// total over every (point, dimension) term in point-major order, t += (x - c)^2 with the
-// subtraction, the square and the add each rounded.  A running float sum has no
-// reassociation, so one thread adds; the CTA's other threads compute the next chunk of
-// terms into shared memory.  *total holds the starting value and receives the result.
-constexpr int OSQ_CHUNK = 8192;
-__global__ void __launch_bounds__(1024) ordered_sq_sum_kernel(const float* __restrict__ x, const float* __restrict__ c,
-                                                              const uint32_t* __restrict__ assign, long long n,
-                                                              int dim, float* __restrict__ total) {
-    __shared__ float terms[OSQ_CHUNK];
-    const long long count = n * dim;
-    float acc = *total;
-    for (long long t0 = 0; t0 < count; t0 += OSQ_CHUNK) {
-        const int len = (int)(count - t0 < OSQ_CHUNK ? count - t0 : (long long)OSQ_CHUNK);
-        for (int j = threadIdx.x; j < len; j += blockDim.x) {
-            const long long t = t0 + j;
-            const long long i = t / dim;
-            const int d = (int)(t - i * dim);
-            const float diff = __fsub_rn(x[t], c[(long long)assign[i] * dim + d]);
-            terms[j] = __fmul_rn(diff, diff);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-#pragma unroll 16
-            for (int j = 0; j < len; ++j) acc = __fadd_rn(acc, terms[j]);
-        }
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) *total = acc;
-}
-
-void launch_ordered_sq_sum(const float* x, const float* c, const uint32_t* assign, long long n, int dim,
-                           float* total, cudaStream_t st) {
-    if (n <= 0) return;
-    ordered_sq_sum_kernel<<<1, 1024, 0, st>>>(x, c, assign, n, dim, total);
-    VGPU_LAUNCH("ordered_sq_sum_kernel");
-}
-
-void launch_assigned_l2(const float* x, const float* c, const uint32_t* assign, long long n, int dim, float* out,
-                        cudaStream_t st) {
-    if (n <= 0) return;
-    const int blocks = (int)std::min<long long>((n * 32 + 255) / 256, 148LL * 64);
-    assigned_l2_kernel<<<blocks, 256, 0, st>>>(x, c, assign, n, dim, out);
-    VGPU_LAUNCH("assigned_l2_kernel");
-}
-
-}  // namespace vgpu
