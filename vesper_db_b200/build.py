@@ -72,7 +72,7 @@ def build(verbose: bool = False) -> str:
             changed = True
         objs.append(obj)
     if changed or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-cudart", "static",
+        _run([NVCC, "-shared", "-Xlinker", "--no-undefined", "-gencode", "arch=compute_100a,code=sm_100a", "-cudart", "static",
               "-o", LIB, *objs, "-lpthread", "-ldl", "-lrt"])
     return LIB
 

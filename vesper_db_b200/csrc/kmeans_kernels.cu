@@ -152,3 +152,46 @@ void launch_finish_means(const double* sum, const unsigned long long* count, int
 }
 
 }  // namespace vgpu
+
+namespace vgpu {
+
+// The final inertia of kmeans_cluster (src/index/kmeans.cpp:230-241): ONE float running
+// total over every (point, dimension) term in point-major order, t += (x - c)^2 with the
+// subtraction, the square and the add each rounded.  A running float sum has no
+// reassociation, so one thread adds; the CTA's other threads compute the next chunk of
+// terms into shared memory.  *total holds the starting value and receives the result.
+constexpr int OSQ_CHUNK = 8192;
+__global__ void __launch_bounds__(1024) ordered_sq_sum_kernel(const float* __restrict__ x, const float* __restrict__ c,
+                                                              const uint32_t* __restrict__ assign, long long n,
+                                                              int dim, float* __restrict__ total) {
+    __shared__ float terms[OSQ_CHUNK];
+    const long long count = n * dim;
+    float acc = *total;
+    for (long long t0 = 0; t0 < count; t0 += OSQ_CHUNK) {
+        const int len = (int)(count - t0 < OSQ_CHUNK ? count - t0 : (long long)OSQ_CHUNK);
+        for (int j = threadIdx.x; j < len; j += blockDim.x) {
+            const long long t = t0 + j;
+            const long long i = t / dim;
+            const int d = (int)(t - i * dim);
+            const float diff = __fsub_rn(x[t], c[(long long)assign[i] * dim + d]);
+            terms[j] = __fmul_rn(diff, diff);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+#pragma unroll 16
+            for (int j = 0; j < len; ++j) acc = __fadd_rn(acc, terms[j]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *total = acc;
+}
+
+void launch_ordered_sq_sum(const float* x, const float* c, const uint32_t* assign, long long n, int dim,
+                           float* total, cudaStream_t st) {
+    if (n <= 0) return;
+    ordered_sq_sum_kernel<<<1, 1024, 0, st>>>(x, c, assign, n, dim, total);
+    VGPU_LAUNCH("ordered_sq_sum_kernel");
+}
+
+
+}  // namespace vgpu
