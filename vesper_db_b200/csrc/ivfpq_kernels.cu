@@ -1048,6 +1048,59 @@ __global__ void __launch_bounds__(256) lut_blocked_reg_kernel(const float* __res
     }
 }
 
+// The same with 16-byte accesses, for groups of 16 or 32 sub-spaces (R = G / 4 >= 4
+// entries per thread): thread x owns the quads of entries r = 4 (x + 256 h) + e, which
+// share a code and four consecutive sub-spaces, so a query's slice is read as DSUB
+// float4 loads and each quad is written with one float4 store.  Same arithmetic, same
+// order per entry.
+template <int DSUB, int R>
+__global__ void __launch_bounds__(256) lut_blocked_vec_kernel(const float* __restrict__ rq, long long nq, int dim,
+                                                              const float* __restrict__ cb, int m, int G,
+                                                              float* __restrict__ T) {
+    extern __shared__ __align__(16) float qs[];     // [LB_Q][DSUB][G]
+    constexpr int H = R / 4;                        // quads per thread
+    const int g = blockIdx.y, c0 = blockIdx.z * LB_C;
+    const long long qb = (long long)blockIdx.x * LB_Q;
+    const int nqq = (int)min((long long)LB_Q, nq - qb);
+    for (int e = threadIdx.x; e < nqq * DSUB * G; e += blockDim.x) {
+        const int qi = e / (DSUB * G), r = e % (DSUB * G), t = r % DSUB, s_lo = r / DSUB;
+        qs[(qi * DSUB + t) * G + s_lo] = rq[(qb + qi) * dim + (long long)g * G * DSUB + r];
+    }
+    const int s0 = (4 * threadIdx.x) % G;           // the same for every quad of the thread
+    float y[H][4][DSUB];
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+        const int c = 4 * (threadIdx.x + 256 * h) / G;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float* src = cb + ((long long)(g * G + s0 + e) * 256 + c0 + c) * DSUB;
+#pragma unroll
+            for (int t = 0; t < DSUB; ++t) y[h][e][t] = src[t];
+        }
+    }
+    __syncthreads();
+    const long long row = (long long)m * 256;
+    float* Tb = T + qb * row + ((long long)g * 256 + c0) * G + 4 * threadIdx.x;
+    for (int qi = 0; qi < nqq; ++qi) {
+        float4 qv[DSUB];
+#pragma unroll
+        for (int t = 0; t < DSUB; ++t) qv[t] = *reinterpret_cast<const float4*>(&qs[(qi * DSUB + t) * G + s0]);
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+            for (int t = 0; t < DSUB; ++t) {
+                a0 = fmaf(qv[t].x, y[h][0][t], a0);
+                a1 = fmaf(qv[t].y, y[h][1][t], a1);
+                a2 = fmaf(qv[t].z, y[h][2][t], a2);
+                a3 = fmaf(qv[t].w, y[h][3][t], a3);
+            }
+            *reinterpret_cast<float4*>(Tb + qi * row + 1024 * h) =
+                make_float4(-2.0f * a0, -2.0f * a1, -2.0f * a2, -2.0f * a3);
+        }
+    }
+}
+
 namespace {
 template <int DSUB, int R>
 bool lut_reg_launch(const float* rq, long long nq, int dim, const float* cb, int m, int G, float* T, cudaStream_t st) {
@@ -1055,6 +1108,15 @@ bool lut_reg_launch(const float* rq, long long nq, int dim, const float* cb, int
     VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_reg_kernel<DSUB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem));
     dim3 grid(ceil_div(nq, LB_Q), m / G, 256 / LB_C);
+    if constexpr (R >= 4) {
+        if (!std::getenv("VGPU_LUT_SCALAR")) {
+            VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_vec_kernel<DSUB, R>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            lut_blocked_vec_kernel<DSUB, R><<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, G, T);
+            VGPU_LAUNCH("lut_blocked_vec_kernel");
+            return true;
+        }
+    }
     lut_blocked_reg_kernel<DSUB, R><<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, G, T);
     VGPU_LAUNCH("lut_blocked_reg_kernel");
     return true;
