@@ -13,13 +13,20 @@ A step is one search of the 10k-query batch at nprobe = 32 through
 vesper_ivfpq_search_batch_device (inputs resident in HBM).  `e2e` is the same
 search through vesper_ivfpq_search_batch with host buffers (the reference's C call).
 The index is trained (k-means++ -> k-means, OPQ, PQ) and filled on the GPU by this
-library before timing; the training set is the first N_TRAIN base vectors.
+library before timing; the training set is the first N_TRAIN = 200,000 base vectors
+(the reference IndexManager's subsample size).  The bench line states the shape of the
+lists (`config.list_stats`: sizes, skew, entries probed per query).
+
+One GPU, rank 0: the cpu_baseline leg runs the reference's search_batch on 256 queries
+strided across the batch at nprobe 8/32/128; `recall_matched` gives its recall@10 beside
+the GPU's on exactly those queries, and `parity_vs_reference` compares the GPU's ids and
+distances with the reference's (ids equal outside 1e-4 ties, distance error).
 
 --impl reference times the reference's own CPU search (oracle/_ref/libvesper_ref.so,
-the reference IVF-PQ sources compiled with their own flags) on the host cores, on a
-bounded sample of the same query batch, against the same index (built on the GPU by
-this library and handed over through the reference's v1.0 file format, which the
-reference's IvfPqIndex::load reads).
+the reference IVF-PQ sources compiled with their own flags) on every host CPU (OpenMP
+thread count set explicitly: torchrun exports OMP_NUM_THREADS=1), one query slice per
+step, against the same index (built on the GPU by this library and handed over through
+the reference's v1.0 file format, which the reference's IvfPqIndex::load reads).
 
 Multi-GPU (torchrun, one rank per GPU): the base set is sharded by vector (rank r
 holds base chunks r, r+W, ...); every rank trains the same model on the same training
@@ -48,22 +55,32 @@ N_BASE = 10_000_000
 DIM = 768
 N_CENTRES = 50_000
 NLIST = 16_384
-QUERY_CHUNK = (512 << 20) // (4 * NLIST)  # queries per engine pass: 512 MiB of coarse distances
+SEARCH_QUERY_CHUNK = (1 << 30) // (4 * NLIST)  # queries per engine pass: 1 GiB of coarse distances
 M = 96
 NBITS = 8
 NQ = 10_000
 K = 10
 NPROBE = 32
 SWEEP = (8, 32, 128)
-N_TRAIN = 131_072
+SWEEP_PASSES = 5
+# Training sample: min(n, 200,000), the subsample the reference's IndexManager trains its
+# IVF-PQ index on (src/index/index_manager.cpp:1712).
+N_TRAIN = 200_000
+CPU_SAMPLE = 256          # queries the reference searches per nprobe in the cpu_baseline leg
 CHUNK = 125_000           # base rows per generator chunk (80 chunks; divisible by 1/2/4/8)
 SCAN_KERNELS = {1: "scan_exact_kernel", 2: "scan_fast2_kernel", 3: "scan_blocked_kernel",
                 4: "tc_list_scan_kernel"}
 COARSE_KERNELS = {1: "l2_dist_kernel (CUDA cores)", 2: "tc_screen_kernel (tcgen05 tf32) + screen_select_kernel"}
 METRIC = "QPS at matched recall@10 (IVF-PQ, 10k-query batch) at 1/2/4/8 B200 vs CPU ref"
 LIST_SCAN_BYTES_PER_PAIR = (662.9e6 + 8.7e6) / 6.65e9   # ncu, main-pass launch on the 4M-vector case
-WORKLOAD = ("IVF-PQ+OPQ search: N=10,000,000 x d=768 fp32 (mixture of 50,000 anisotropic Gaussians, "
-            "sigma~U[0.01,0.2]), nlist=16384, m=96x8 bits, OPQ 768x768, 10,000 queries, k=10, L2, nprobe=32")
+
+
+def workload_name():
+    return (f"IVF-PQ+OPQ search: N={N_BASE:,} x d=768 fp32 (mixture of 50,000 anisotropic Gaussians, "
+            f"sigma~U[0.01,0.2]), nlist=16384, m=96x8 bits, OPQ 768x768, {NQ:,} queries, k=10, L2, nprobe=32")
+
+
+WORKLOAD = workload_name()
 
 
 def parse():
@@ -76,7 +93,25 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "flat"],
                     help="ivfpq: the IVF-PQ+OPQ search (default); flat: exact flat top-k, 1M x 768 IP, k=100")
-    return ap.parse_args()
+    # Smaller cases of the same workload, for profiler captures (the defaults are the
+    # benchmark's sizes; a line measured with either flag names its sizes in config).
+    ap.add_argument("--n-base", type=int, default=0, help="base vectors (multiple of the 125,000-row chunk)")
+    ap.add_argument("--nq", type=int, default=0, help="queries in the batch")
+    ap.add_argument("--scan", default="auto", choices=["auto", "tc", "blocked"],
+                    help="FAST scan kernel: the engine's choice, the tensor-core list scan or the blocked scan")
+    args = ap.parse_args()
+    global N_BASE, NQ, WORKLOAD, FLAT_N, FLAT_NQ
+    if args.workload == "flat":
+        FLAT_N = max(FLAT_CHUNK, args.n_base // FLAT_CHUNK * FLAT_CHUNK) if args.n_base else FLAT_N
+        FLAT_NQ = args.nq or FLAT_NQ
+    else:
+        if args.n_base:
+            N_BASE = max(CHUNK, args.n_base // CHUNK * CHUNK)
+        NQ = args.nq or NQ
+        WORKLOAD = workload_name()
+    if args.scan != "auto":
+        os.environ["VGPU_SCAN"] = args.scan
+    return args
 
 
 # ------------------------------------------------------------------------------- data
@@ -176,28 +211,58 @@ def recall_at(ids, gt_ids, k):
     return hits / (ids.shape[0] * k)
 
 
-def reference_cpu_search(index_dir, queries_np, nprobe, seconds):
-    """Time the reference's own IvfPqIndex::search_batch (OpenMP over all host cores)."""
+def _oracle_lib():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    from oracle_lib import REF_SO, Reference
-    ref = Reference(REF_SO)
-    idx = ref.ivfpq()
-    t0 = time.perf_counter()
-    idx.load(index_dir)
-    load_s = time.perf_counter() - t0
-    idx.search(queries_np[:64], K, nprobe)  # warm-up
-    done, elapsed, batch = 0, 0.0, 256
-    ids_all = []
-    while done < queries_np.shape[0] and elapsed < seconds:
-        qb = queries_np[done:done + batch]
-        t = time.perf_counter()
-        ids, _, _ = idx.search(qb, K, nprobe)
-        elapsed += time.perf_counter() - t
-        ids_all.append(ids)
-        done += qb.shape[0]
+    import oracle_lib
+    return oracle_lib
+
+
+def reference_threads():
+    """Use every host CPU this process may run on for the reference's OpenMP regions
+    (torchrun exports OMP_NUM_THREADS=1 to each rank) and describe the host."""
+    ol = _oracle_lib()
+    used = ol.set_omp_threads(ol.host_threads())
+    return used, ol.host_cpu()
+
+
+def topk_parity(ids, d, cnt, rids, rd, rcnt, rtol=1e-4):
+    """Compare two top-k results query by query: distances within rtol (relative, floor
+    1) position by position; an id that only one side returns must tie the reference's
+    k-th distance within that band.  Returns counts, not assertions."""
     import numpy as np
-    return {"qps": done / elapsed, "queries": done, "seconds": elapsed, "load_s": load_s,
-            "ids": np.concatenate(ids_all), "cores": os.cpu_count()}
+    nq = ids.shape[0]
+    bad_ids, bad_cnt, max_rel = 0, 0, 0.0
+    for q in range(nq):
+        n = int(rcnt[q])
+        if int(cnt[q]) != n:
+            bad_cnt += 1
+            continue
+        if n == 0:
+            continue
+        a, b = d[q, :n].astype(np.float64), rd[q, :n].astype(np.float64)
+        max_rel = max(max_rel, float((np.abs(a - b) / np.maximum(1.0, np.abs(b))).max()))
+        kth = b[n - 1]
+        band = rtol * max(1.0, abs(kth))
+        ia, ib = [int(i) for i in ids[q, :n]], [int(i) for i in rids[q, :n]]
+        sa, sb = set(ia), set(ib)
+        # an id only one side returns must tie the k-th distance within the band
+        if any(i not in sb and abs(x - kth) > band for i, x in zip(ia, a)) or \
+                any(i not in sa and abs(x - kth) > band for i, x in zip(ib, b)):
+            bad_ids += 1
+    return {"queries": int(nq), "count_mismatches": bad_cnt, "id_mismatches_outside_ties": bad_ids,
+            "max_rel_dist_err": max_rel, "rtol": rtol}
+
+
+def list_stats(index, n_queries, scanned_entries):
+    """Shape of the inverted lists this rank holds and of the probe work per query."""
+    import numpy as np
+    sizes = np.diff(index.list_offsets().astype(np.int64))
+    nz = sizes[sizes > 0]
+    return {"lists": int(sizes.size), "entries": int(sizes.sum()), "mean": float(sizes.mean()),
+            "max": int(sizes.max()), "p50": float(np.percentile(sizes, 50)), "p99": float(np.percentile(sizes, 99)),
+            "empty": int((sizes == 0).sum()), "max_over_mean": float(sizes.max() / max(sizes.mean(), 1e-9)),
+            "nonempty_min": int(nz.min()) if nz.size else 0,
+            "probed_entries_per_query": float(scanned_entries) / max(1, n_queries)}
 
 
 # ------------------------------------------------------------------------------- flat top-k
@@ -219,9 +284,9 @@ def reference_flat(base_np, q_np, seconds, batch=8):
     """Time the reference's find_nearest_centroids_batch_fused (OpenMP over all host
     threads) on query batches until `seconds` of search have run; the base sits in the
     reference's AlignedCentroidBuffer (filled once, untimed)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    from oracle_lib import REF_SO, Reference
-    fb = Reference(REF_SO).flat_buffer(base_np)
+    reference_threads()
+    ol = _oracle_lib()
+    fb = ol.Reference(ol.REF_SO).flat_buffer(base_np)
     fb.topk(1, q_np[:2], FLAT_K)  # warm-up
     done, el, ids, scores = 0, 0.0, [], []
     while done < q_np.shape[0] and (el < seconds or done == 0):
@@ -261,26 +326,27 @@ def main_flat(args):
     torch.cuda.synchronize()
     q_np = queries.cpu().numpy()
     peaks, peak_kind = measured_peaks()
-    cfg = {"workload": FLAT_WORKLOAD, "n_base": FLAT_N, "nq": FLAT_NQ, "k": FLAT_K, "op": "inner_product",
+    workload = FLAT_WORKLOAD.replace("N=1,000,000", f"N={FLAT_N:,}").replace("10,000 queries", f"{FLAT_NQ:,} queries")
+    cfg = {"workload": workload, "n_base": FLAT_N, "nq": FLAT_NQ, "k": FLAT_K, "op": "inner_product",
            "parallelism": f"vector-sharded x{world}" if world > 1 else "single GPU",
            "l2_policy": "inputs larger than L2 (3.07 GB base streamed per pass)"}
     if args.impl == "reference":
         per = max(1.0, args.cpu_seconds / max(1, args.steps))
         base_np = base.cpu().numpy()
-        vals, nq_done = [], 0
+        els, nq_done = [], 0
         for s in range(args.warmup + args.steps):
             v, n, el, _, _ = reference_flat(base_np, q_np[(s * 64) % FLAT_NQ:], per)
             if s >= args.warmup:
-                vals.append(v)
+                els.append(el)
                 nq_done += n
-        v = sorted(vals)[len(vals) // 2]
+        v = nq_done / sum(els)
         print(json.dumps({"impl": "reference", "metric": FLAT_METRIC, "value": v, "unit": "queries/s",
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                          "ms_per_step": 1e3 * FLAT_NQ / v, "higher_is_better": True, "scaling": "strong",
+                          "ms_per_step": 1e3 * sum(els) / len(els), "higher_is_better": True, "scaling": "strong",
                           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), normalised)",
                           "config": cfg,
-                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": os.cpu_count(),
-                                           "kind": "reference",
+                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": reference_threads()[0],
+                                           "host_cpu": reference_threads()[1], "kind": "reference",
                                            "sample": f"{nq_done} queries over {args.steps} steps (~{per:.0f} s "
                                                      f"each), OpenMP over all host threads"},
                           "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0,
@@ -396,7 +462,9 @@ def main_flat(args):
             v, n, el, rid, rsc = reference_flat(base_np, q_np, args.cpu_seconds)
             gi = res_i[:n].cpu().numpy().astype(np.uint32)
             gs = res_s[:n].cpu().numpy()
-            out["cpu_baseline"] = {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",
+            threads, cpu = reference_threads()
+            out["cpu_baseline"] = {"value": v, "unit": "queries/s", "cores": threads, "kind": "reference",
+                                   "host_cpu": cpu,
                                    "sample": f"first {n} queries of the batch ({el:.1f} s of search), "
                                              f"find_nearest_centroids_batch_fused, OpenMP over all host threads"}
             out["parity_vs_reference"] = {"queries": int(n), "indices_equal": bool(np.array_equal(gi, rid)),
@@ -413,27 +481,11 @@ def main_flat(args):
 
 
 # ------------------------------------------------------------------------------- main
-def main():
-    args = parse()
-    if args.workload == "flat":
-        return main_flat(args)
-    import numpy as np
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference" and rank != 0:
-        return 0
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1 and args.impl == "ours":
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-
+def build_ivfpq_workload(args, torch, dev, world, rank):
+    """Data, training and add of the IVF-PQ+OPQ workload on this rank's GPU (untimed),
+    plus the exact ground truth of the query batch."""
     from vesper_db_b200 import IvfPqIndex
-    from vesper_db_b200.shard import chunks_of, merge_topk, probed_search
+    from vesper_db_b200.shard import chunks_of, merge_topk
     t_build0 = time.perf_counter()
     centres, sigmas = gen_centres(torch, dev)
     queries = synth.gen_queries(torch, dev, centres, sigmas, NQ)
@@ -469,81 +521,148 @@ def main():
         gt_d, gt_i = merge_topk(gt_d, gt_i, K)
     del base, chunks
     torch.cuda.synchronize()
-    gt_np = gt_i.cpu().numpy()
-    q_np = queries.cpu().numpy()
+    build = {"data_s": t_data, "train_s": t_train, "add_s": t_add, "opq_kept": rep.opq_kept,
+             "err_unrot": rep.err_unrot, "err_opq": rep.err_opq}
+    return index, queries, gt_i.cpu().numpy(), build
 
-    if args.impl == "reference":
-        out = {"impl": "reference", "metric": METRIC, "unit": "queries/s", "higher_is_better": True,
-               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",
-               "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded mixture)",
-               "config": {"workload": WORKLOAD, "nprobe": NPROBE, "k": K, "nq": NQ, "n_train": N_TRAIN}}
-        tmp = tempfile.mkdtemp(prefix="vesper_ref_")
-        try:
-            index.save(tmp)
-            index.close()
-            sys.path.insert(0, os.path.join(ROOT, "oracle"))
-            from oracle_lib import REF_SO, Reference
-            ridx = Reference(REF_SO).ivfpq()
-            t0 = time.perf_counter()
-            ridx.load(tmp)
-            load_s = time.perf_counter() - t0
-            # Each step searches a disjoint 128-query slice block for ~cpu_seconds/steps.
-            per = max(1.0, args.cpu_seconds / max(1, args.steps))
-            step_qps, hits, nq_done, qpos = [], 0, 0, 0
-            for s in range(args.warmup + args.steps):
-                done, el = 0, 0.0
-                while (el < per or done == 0) and done < NQ:
-                    lo = qpos % NQ
-                    qb = q_np[lo:lo + 128]
-                    t = time.perf_counter()
-                    rid, _, _ = ridx.search(qb, K, NPROBE)
-                    el += time.perf_counter() - t
-                    if s >= args.warmup:
-                        g = gt_np[lo:lo + qb.shape[0]]
-                        hits += sum(len(set(a) & set(b)) for a, b in zip(rid.tolist(), g.tolist()))
-                        nq_done += qb.shape[0]
-                    done += qb.shape[0]
-                    qpos += qb.shape[0]
-                if s >= args.warmup:
-                    step_qps.append(done / el)
-            v = sorted(step_qps)[len(step_qps) // 2]
-            out.update({"value": v, "ms_per_step": 1e3 * NQ / v,
-                        "recall@10": hits / max(1, nq_done * K),
-                        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": os.cpu_count(),
-                                         "kind": "reference",
-                                         "sample": f"{nq_done} queries of the 10k batch over {args.steps} steps "
-                                                   f"(~{per:.0f} s each), nprobe={NPROBE}, k={K}, OpenMP over all "
-                                                   f"host threads; index load {load_s:.1f} s untimed"},
-                        "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0,
-                                "d2h_bytes_per_step": 0},
-                        "build": {"data_s": t_data, "train_s": t_train, "add_s": t_add}})
-        finally:
-            shutil.rmtree(tmp, ignore_errors=True)
-        print(json.dumps(out))
+
+def reference_arm(args, index, q_np, gt_np, build):
+    """--impl reference: the reference's own IvfPqIndex::search_batch (AVX2 build, OpenMP
+    over every host CPU) on the same index, handed over through its v1.0 file.  Each
+    step searches the next slice of the query batch; the value is the queries searched
+    over the summed step times."""
+    threads, cpu = reference_threads()
+    ol = _oracle_lib()
+    out = {"impl": "reference", "metric": METRIC, "unit": "queries/s", "higher_is_better": True,
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "scaling": "strong",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded mixture)",
+           "config": {"workload": WORKLOAD, "nlist": NLIST, "m": M, "nbits": NBITS, "nprobe": NPROBE, "k": K,
+                      "nq": NQ, "n_base": N_BASE, "n_train": N_TRAIN, "search_mode": "reference search_batch",
+                      "parallelism": "host CPU (OpenMP)"}}
+    tmp = tempfile.mkdtemp(prefix="vesper_ref_")
+    try:
+        index.save(tmp)
+        index.close()
+        ridx = ol.Reference(ol.REF_SO).ivfpq()
+        t0 = time.perf_counter()
+        ridx.load(tmp)
+        load_s = time.perf_counter() - t0
+        per_step = max(16, 4 * threads)   # one query slice per step, a few queries per thread
+        step_s, hits, nq_done, qpos = [], 0, 0, 0
+        for s in range(args.warmup + args.steps):
+            lo = qpos % NQ
+            qb = q_np[lo:lo + per_step]
+            t = time.perf_counter()
+            rid, _, _ = ridx.search(qb, K, NPROBE)
+            el = time.perf_counter() - t
+            qpos += qb.shape[0]
+            if s >= args.warmup:
+                step_s.append(el)
+                g = gt_np[lo:lo + qb.shape[0]]
+                hits += sum(len(set(a) & set(b)) for a, b in zip(rid.tolist(), g.tolist()))
+                nq_done += qb.shape[0]
+        v = nq_done / sum(step_s)
+        out.update({"value": v, "ms_per_step": 1e3 * sum(step_s) / len(step_s), "queries_per_step": per_step,
+                    "recall@10": hits / max(1, nq_done * K),
+                    "cpu_baseline": {"value": v, "unit": "queries/s", "cores": threads, "kind": "reference",
+                                     "host_cpu": cpu,
+                                     "sample": f"{nq_done} queries of the 10k batch, {per_step} per step over "
+                                               f"{args.steps} steps, nprobe={NPROBE}, k={K}, OpenMP on {threads} "
+                                               f"threads; index load {load_s:.1f} s untimed"},
+                    "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                    "build": build})
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    print(json.dumps(out))
+    return 0
+
+
+def cpu_leg(index, q_np, gt_np, gpu_results, seconds_hint):
+    """Rank 0 at N=1: the reference's search_batch on a strided sample of the batch at
+    every swept nprobe -- its QPS (the cpu_baseline at the headline nprobe), its recall
+    beside the GPU's on exactly the same queries, and the GPU results compared with the
+    reference's ids and distances."""
+    import numpy as np
+    threads, cpu = reference_threads()
+    ol = _oracle_lib()
+    sample = np.linspace(0, NQ - 1, CPU_SAMPLE).round().astype(np.int64)
+    qs = np.ascontiguousarray(q_np[sample])
+    tmp = tempfile.mkdtemp(prefix="vesper_cpu_")
+    try:
+        index.save(tmp)
+        ridx = ol.Reference(ol.REF_SO).ivfpq()
+        t0 = time.perf_counter()
+        ridx.load(tmp)
+        load_s = time.perf_counter() - t0
+        ridx.search(qs[:8], K, NPROBE)  # warm-up
+        matched, parity, qps = [], {}, {}
+        for npb in SWEEP:
+            t = time.perf_counter()
+            rid, rd, rcnt = ridx.search(qs, K, npb)
+            el = time.perf_counter() - t
+            qps[npb] = CPU_SAMPLE / el
+            gi, gd, gn = gpu_results[npb]
+            gi, gd, gn = gi[sample], gd[sample], gn[sample]
+            matched.append({"nprobe": npb, "queries": CPU_SAMPLE,
+                            "gpu": recall_at(gi, gt_np[sample], K), "cpu": recall_at(rid, gt_np[sample], K),
+                            "cpu_qps": qps[npb]})
+            parity[npb] = topk_parity(gi, gd, gn, rid, rd, rcnt)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    base = {"value": qps[NPROBE], "unit": "queries/s", "cores": threads, "kind": "reference", "host_cpu": cpu,
+            "sample": f"{CPU_SAMPLE} queries strided across the 10k batch, nprobe={NPROBE}, k={K}, reference "
+                      f"IvfPqIndex::search_batch with OpenMP on {threads} threads; index load {load_s:.1f} s untimed",
+            "recall@10": matched[SWEEP.index(NPROBE)]["cpu"]}
+    par = dict(parity[NPROBE])
+    par["by_nprobe"] = {str(k2): v for k2, v in parity.items()}
+    return base, matched, par
+
+
+def main():
+    args = parse()
+    if args.workload == "flat":
+        return main_flat(args)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and rank != 0:
         return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 and args.impl == "ours":
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from vesper_db_b200.shard import merge_topk, probed_search
+    index, queries, gt_np, build = build_ivfpq_workload(args, torch, dev, world, rank)
+    q_np = queries.cpu().numpy()
+    if args.impl == "reference":
+        return reference_arm(args, index, q_np, gt_np, build)
 
     # ------------------------------------------------------------------ our arm
     out_ids = torch.empty((NQ, K), dtype=torch.int64, device=dev)
     out_d = torch.empty((NQ, K), dtype=torch.float32, device=dev)
     out_n = torch.empty(NQ, dtype=torch.int32, device=dev)
-
     slot = torch.arange(K, device=dev)[None, :]
 
     # Multi-GPU: each rank probes 1/world of the batch (the coarse stage is the same on
     # every shard) and the probe lists are all-gathered before the shard searches.
     probe_bufs = {}
 
-    def one_search(nprobe):
-        if world > 1 and NQ % world == 0:
-            probed_search(index, queries, K, nprobe, NLIST, out_ids, out_d, out_n, probe_bufs)
-        else:
-            index.search_batch_device(queries.data_ptr(), NQ, K, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
-                                      out_n.data_ptr())
+    def one_search(q, nprobe):
         if world > 1:
+            probed_search(index, q, K, nprobe, NLIST, out_ids, out_d, out_n, probe_bufs)
             # padded slots (fewer than k results on this shard) must not win the merge
             d = torch.where(slot < out_n[:, None], out_d, torch.full_like(out_d, float("inf")))
-            return merge_topk(d, out_ids, K)
-        return out_d, out_ids
+            md, mi = merge_topk(d, out_ids, K)
+            return md, mi, torch.isfinite(md).sum(1)
+        index.search_batch_device(q.data_ptr(), NQ, K, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
+                                  out_n.data_ptr())
+        return out_d, out_ids, out_n
 
     def barrier():
         if world > 1:
@@ -551,20 +670,18 @@ def main():
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        one_search(NPROBE)
+        one_search(queries, NPROBE)
     barrier()
-    scan_ms, scanned, list_ms, launches = [], [], [], 0
+    steps_t, launches = [], 0
     with ClockSampler(local) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.nvtx.range_push("timed_search")
         ev0.record()
         for _ in range(args.steps):
-            res_d, res_i = one_search(NPROBE)
+            res_d, res_i, res_n = one_search(queries, NPROBE)
             t = index.last_timings()
-            scan_ms.append(t["scan_ms"])
-            scanned.append(t["scanned_entries"])
-            list_ms.append(t["list_kernel_ms"])
+            steps_t.append(t)
             launches += t["kernel_launches"]
         ev1.record()
         torch.cuda.nvtx.range_pop()
@@ -576,26 +693,40 @@ def main():
         ms_total = float(tt.item())
     ms_step = ms_total / args.steps
     qps = NQ * args.steps / (ms_total / 1e3)
-    timings = index.last_timings()
     recall = recall_at(res_i.cpu().numpy(), gt_np, K)
+    stage_ms = {k2: sum(t[k2] for t in steps_t) / len(steps_t) for k2 in steps_t[0] if k2.endswith("_ms")}
+    timings = steps_t[-1]
 
-    # nprobe sweep (one timed pass each) with recall
-    sweep = []
+    # nprobe sweep: SWEEP_PASSES timed passes per nprobe, recall of the last pass
+    sweep, gpu_results = [], {}
     for npb in SWEEP:
-        one_search(npb)
+        one_search(queries, npb)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        rd, ri = one_search(npb)
+        for _ in range(SWEEP_PASSES):
+            rd, ri, rn = one_search(queries, npb)
         e1.record()
         barrier()
-        sweep.append({"nprobe": npb, "qps": NQ / (e0.elapsed_time(e1) / 1e3),
-                      "recall@10": recall_at(ri.cpu().numpy(), gt_np, K)})
+        ms = e0.elapsed_time(e1) / SWEEP_PASSES
+        if world > 1:
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        ri_np = ri.cpu().numpy()
+        gpu_results[npb] = (ri_np, rd.cpu().numpy(), rn.cpu().numpy())
+        sweep.append({"nprobe": npb, "qps": NQ / (ms / 1e3), "passes": SWEEP_PASSES,
+                      "recall@10": recall_at(ri_np, gt_np, K),
+                      "stage_ms": {k2: v for k2, v in index.last_timings().items() if k2.endswith("_ms")}})
 
-    # e2e: the reference's C call with host buffers (H2D of queries, D2H of results inside)
+    # e2e: host query buffer in, host result out, every step.  One GPU: the reference's
+    # C call vesper_ivfpq_search_batch with host buffers (copies inside the library).
+    # Several GPUs: each rank copies the batch from pinned host memory, runs the sharded
+    # search (probe exchange, shard search, merge) and rank 0 reads the merged result.
     q_host = torch.empty((NQ, DIM), dtype=torch.float32, pin_memory=True)
     q_host.copy_(queries)
     q_host_np = q_host.numpy()
+    q_dev = torch.empty_like(queries)
     e2e_ms = []
     for s in range(args.warmup + args.steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -604,12 +735,11 @@ def main():
         if world == 1:
             index.search_batch_c(q_host_np, K, NPROBE)
         else:
-            # per-shard search through the C ABI with host buffers (counts mark the
-            # padding), then the merge across ranks and the merged result to the host
-            hid, hd, hcnt = index.search_batch(q_host_np, K, NPROBE)
-            hd = np.where(np.arange(K)[None, :] < hcnt[:, None], hd, np.inf).astype(np.float32)
-            md, mi = merge_topk(torch.from_numpy(hd).to(dev), torch.from_numpy(hid.astype(np.int64)).to(dev), K)
-            mi.cpu()
+            q_dev.copy_(q_host, non_blocking=True)
+            torch.cuda.current_stream().synchronize()   # the library's stream does not wait on torch's
+            md, mi, _ = one_search(q_dev, NPROBE)
+            if rank == 0:
+                mi.cpu(), md.cpu()
         e1.record()
         barrier()
         if s >= args.warmup:
@@ -621,36 +751,39 @@ def main():
         e2e_step = float(tt.item())
 
     peaks, peak_kind = measured_peaks()
-    scan_avg = sum(scan_ms) / len(scan_ms)
-    entries = sum(scanned) / len(scanned)
+    entries = sum(t["scanned_entries"] for t in steps_t) / len(steps_t)
     code_bytes = entries * M
+    launches_per_search = -(-NQ // SEARCH_QUERY_CHUNK)
     if timings["scan_variant"] == 4:
         # Dominant kernel: the tcgen05 screen.  Algorithmic work = every (query, probed
-        # entry) pair's dim-long product, 2 * dim FLOP each; one launch per query chunk.
-        lk = sum(list_ms) / len(list_ms)
+        # entry) pair's dim-long product, 2 * dim FLOP each.
+        lk = stage_ms["list_kernel_ms"]
         flop = 2.0 * DIM * entries
         achieved = flop / (lk / 1e3) / 1e12
         roofline = {"bound": "tensor", "kernel": "tc_list_scan_kernel (tcgen05 kind::f16, bf16, A in TMEM)",
                     "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                     "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} (bf16 dense, burst)",
-                    # DRAM bytes per launch: profiles/tc_list_scan_kernel_4Mx768_nq8192.md measured
-                    # 671.6 MB for 6.65e9 (query, entry) pairs on the 4M-vector case; scaled by the
-                    # pairs of one launch here (codes of each probed tile are read once per batch).
-                    "traffic": LIST_SCAN_BYTES_PER_PAIR * entries / -(-NQ // QUERY_CHUNK),
+                    # DRAM bytes per launch: the ncu capture of one main-pass launch on the
+                    # 4M-vector case (671.6 MB for 6.65e9 (query, entry) pairs), scaled by
+                    # the pairs of one launch here (codes of each probed tile are read once
+                    # per batch).
+                    "traffic": LIST_SCAN_BYTES_PER_PAIR * entries / launches_per_search,
                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4M-vector case, "
                                       "scaled by (query, entry) pairs per launch",
                     "algorithmic_flop_per_search": flop, "kernel_ms_per_search": lk,
-                    "launches_per_search": -(-NQ // QUERY_CHUNK),
-                    "scan_stage_ms": scan_avg,
-                    "scan_stage_code_GBps": code_bytes / (scan_avg / 1e3) / 1e9,
+                    "launches_per_search": launches_per_search,
+                    "scan_stage_ms": stage_ms["scan_ms"],
+                    "scan_stage_code_GBps": code_bytes / (stage_ms["scan_ms"] / 1e3) / 1e9,
                     "candidates_refined": timings["list_candidates"],
                     "fallback_queries": timings["list_fallback_queries"]}
     else:
-        achieved = code_bytes / (scan_avg / 1e3) / 1e9
+        achieved = code_bytes / (stage_ms["scan_ms"] / 1e3) / 1e9
         roofline = {"bound": "hbm", "kernel": SCAN_KERNELS.get(timings["scan_variant"], "?"), "achieved": achieved,
                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                     "peak_source": peak_kind, "traffic": None,
-                    "algorithmic_bytes_per_search": code_bytes, "scan_ms": scan_avg}
+                    "algorithmic_bytes_per_search": code_bytes, "scan_ms": stage_ms["scan_ms"]}
+    ls = list_stats(index, NQ, entries)
+    ls["probed_entries_per_query_at_mean_list_size"] = NPROBE * ls["mean"]
     out = {
         "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
@@ -658,33 +791,32 @@ def main():
         "config": {"workload": WORKLOAD, "nlist": NLIST, "m": M, "nbits": NBITS, "nprobe": NPROBE, "k": K,
                    "nq": NQ, "n_base": N_BASE, "n_train": N_TRAIN, "search_mode": "fast",
                    "parallelism": f"vector-sharded x{world}" if world > 1 else "single GPU",
-                   "l2_policy": "inputs larger than L2 (960 MB of PQ codes scanned per pass)"},
+                   "l2_policy": "inputs larger than L2 (960 MB of PQ codes scanned per pass)",
+                   "list_stats": ls},
         "recall@10": recall,
         "sweep": sweep,
         "e2e": {"value": NQ / (e2e_step / 1e3), "unit": "queries/s", "h2d_bytes_per_step": NQ * DIM * 4,
-                "d2h_bytes_per_step": NQ * K * 12, "ms_per_step": e2e_step},
+                "d2h_bytes_per_step": NQ * K * 12, "ms_per_step": e2e_step,
+                "path": "vesper_ivfpq_search_batch (host buffers)" if world == 1 else
+                        "per rank: pinned H2D of the batch, probe exchange, shard search, NCCL merge; "
+                        "rank 0 copies the merged result to the host"},
         "gpu_launches": launches,
         "roofline": roofline,
-        "stage_ms": {k2: v for k2, v in timings.items() if k2.endswith("_ms")},
+        "stage_ms": stage_ms,
+        "outside_engine_ms": ms_step - stage_ms["total_ms"],
         "coarse_kernel": COARSE_KERNELS.get(timings["coarse_variant"], "?"),
-        "build": {"data_s": t_data, "train_s": t_train, "add_s": t_add, "opq_kept": rep.opq_kept,
-                  "err_unrot": rep.err_unrot, "err_opq": rep.err_opq},
+        "build": build,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tmp = tempfile.mkdtemp(prefix="vesper_cpu_")
         try:
-            index.save(tmp)
-            r = reference_cpu_search(tmp, q_np, NPROBE, args.cpu_seconds)
-            out["cpu_baseline"] = {"value": r["qps"], "unit": "queries/s", "cores": r["cores"], "kind": "reference",
-                                   "sample": f"first {r['queries']} queries of the 10k batch, nprobe={NPROBE}, "
-                                             f"k={K} ({r['seconds']:.1f} s of search)",
-                                   "recall@10": recall_at(r["ids"], gt_np[:r["queries"]], K)}
+            base, matched, par = cpu_leg(index, q_np, gt_np, gpu_results, args.cpu_seconds)
+            out["cpu_baseline"] = base
+            out["recall_matched"] = matched
+            out["parity_vs_reference"] = par
         except Exception as e:  # the reference oracle may be absent on a machine without it
             out["cpu_baseline"] = {"value": None, "unit": "queries/s", "cores": os.cpu_count(),
                                    "kind": "reference", "sample": f"unavailable: {e}"}
-        finally:
-            shutil.rmtree(tmp, ignore_errors=True)
     if rank == 0:
         print(json.dumps(out))
     index.close()

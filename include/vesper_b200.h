@@ -106,7 +106,11 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device(const vesper_index
  * are serialized by a process-wide lock, because calls overlapping on the GPU would
  * race on it.  Queries are processed in chunks that fit; an index whose single query
  * would need more than 64 MiB of scratch (nlist * 4 + m * 2^nbits * 4 + ... bytes) is
- * rejected with VESPER_ERROR_INVALID_PARAM and a message, as is mode EXACT. */
+ * rejected with VESPER_ERROR_INVALID_PARAM and a message, as are mode EXACT and shapes
+ * whose lookup table or top-k buffer exceed the kernels' shared memory; such a call
+ * queues no GPU work.  The cached address belongs to the device's primary context:
+ * after cudaDeviceReset on that device the entry point must not be called again in the
+ * same process. */
 VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_noalloc(const vesper_index_t* index,
                                                                       const float* d_queries, size_t nq,
                                                                       const vesper_ivfpq_search_params_ex_t* params,

@@ -31,6 +31,55 @@ def _f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
+def host_threads() -> int:
+    """Host CPUs this process may run on (its affinity mask)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def set_omp_threads(n: int) -> int:
+    """Make the reference's OpenMP regions use n threads and return what OpenMP reports.
+
+    torch.distributed.run exports OMP_NUM_THREADS=1 to every rank; libgomp reads the
+    variable when it is first loaded, so the variable is set before any library that
+    links libgomp is opened, and omp_set_num_threads is called on the loaded copy too."""
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        gomp = C.CDLL("libgomp.so.1")
+        gomp.omp_set_num_threads(C.c_int(n))
+        gomp.omp_get_max_threads.restype = C.c_int
+        return int(gomp.omp_get_max_threads())
+    except OSError:
+        return n
+
+
+def host_cpu() -> dict:
+    """Model name, physical cores and logical CPUs of this host (from /proc/cpuinfo)."""
+    model, cores = None, set()
+    phys = core = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            key, _, val = line.partition(":")
+            key, val = key.strip(), val.strip()
+            if key == "model name" and model is None:
+                model = val
+            elif key == "physical id":
+                phys = val
+            elif key == "core id":
+                core = val
+            elif not key and phys is not None and core is not None:
+                cores.add((phys, core))
+                phys = core = None
+        if phys is not None and core is not None:
+            cores.add((phys, core))
+    except OSError:
+        pass
+    return {"model": model, "physical_cores": len(cores) or None, "logical_cpus": os.cpu_count(),
+            "affinity_cpus": host_threads()}
+
+
 class Oracle:
     """The restated reference arithmetic (bit-exact with the -ffp-contract=off build)."""
 

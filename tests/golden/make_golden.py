@@ -3,7 +3,7 @@
 Run where the reference sources are mounted and oracle/_ref is built
 (`make -C oracle`):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference source root>   # or VESPER_REFERENCE_DIR set
 
 Outputs (all small, committed):
   pq_lut_small.json     algorithms/fixtures/pq/pq_lut_small.json with its arithmetic
@@ -220,7 +220,9 @@ def make_kmeans(ref: Reference):
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    ref_root = args[0] if args else "/root/reference"
+    ref_root = args[0] if args else os.environ.get("VESPER_REFERENCE_DIR")
+    if not ref_root:
+        sys.exit("usage: make_golden.py <reference source root> (or set VESPER_REFERENCE_DIR)")
     convert_fixtures(ref_root)
     ref = Reference()
     only = [a for a in sys.argv if a.endswith("-only")]

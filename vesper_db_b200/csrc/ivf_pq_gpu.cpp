@@ -1287,6 +1287,12 @@ public:
                         "allocation-free search: one query needs " + std::to_string(per_q) +
                         " bytes of scratch, more than the fixed " + std::to_string(vgpu::kNoAllocScratchBytes) +
                         "-byte device buffer (nlist or m * 2^nbits too large)");
+        // Every launch limit is checked before anything is queued on the shared array, so
+        // a rejected call never leaves scratch work in flight behind the released lock.
+        if (!vgpu::lut_fast_fits((int)ksub, (int)dsub) || !vgpu::scan_fast2_fits((int)m(), (int)ksub, (int)sp.k, (int)np))
+            return fail(error_code::out_of_range,
+                        "allocation-free search: the per-query lookup table (m * 2^nbits floats) or the top-k "
+                        "merge buffer exceeds the shared memory of its kernels");
         std::lock_guard<std::mutex> call_lock(vgpu::noalloc_call_mutex());
         std::lock_guard<std::mutex> lock(mu);
         unsigned char* base = static_cast<unsigned char*>(vgpu::noalloc_scratch_device_address(dev));
@@ -1298,6 +1304,7 @@ public:
         float* rq = has_rot ? reinterpret_cast<float*>(p) : nullptr; p += has_rot ? al(qc * dim * 4) : 0;
         float* T = reinterpret_cast<float*>(p);
         const uint32_t k = sp.k;
+        try {
         for (size_t q0 = 0; q0 < nq; q0 += qc) {
             const size_t nc = std::min(qc, nq - q0);
             const float* dq = dq_all + q0 * dim;
@@ -1313,6 +1320,11 @@ public:
                                     (int)np, (int)m(), (int)ksub, d_offs.data(), d_codes.data(), d_vterm.data(),
                                     d_ids.data(), (int)k, out_ids + q0 * k, out_d + q0 * k,
                                     out_n ? out_n + q0 : nullptr, st);
+        }
+        } catch (...) {
+            // kernels already queued still use the array: drain them before the lock goes
+            cudaStreamSynchronize(st);
+            throw;
         }
         sync(st);
         return {};

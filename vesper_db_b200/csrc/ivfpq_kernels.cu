@@ -11,6 +11,7 @@
 #include <cub/cub.cuh>
 
 #include <cfloat>
+#include <cstdint>
 
 #include <cstdlib>
 
@@ -718,11 +719,17 @@ __global__ void __launch_bounds__(256) lut_fast_kernel(const float* __restrict__
     }
 }
 
+static size_t lut_fast_smem(int ksub, int dsub) {
+    return ((size_t)dsub * ksub + 32 * (size_t)dsub) * sizeof(float);
+}
+
+bool lut_fast_fits(int ksub, int dsub) { return lut_fast_smem(ksub, dsub) <= 200 * 1024; }
+
 void launch_lut_fast(const float* rq, long long nq, int dim, const float* cb, int m, int ksub, int dsub,
                      float* T, cudaStream_t st) {
     if (nq <= 0) return;
-    const size_t smem = ((size_t)dsub * ksub + 32 * (size_t)dsub) * sizeof(float);
-    if (smem > 200 * 1024) throw CudaError("lut_fast: sub-space codebook too large for shared memory");
+    const size_t smem = lut_fast_smem(ksub, dsub);
+    if (!lut_fast_fits(ksub, dsub)) throw CudaError("lut_fast: sub-space codebook too large for shared memory");
     VGPU_CHECK(cudaFuncSetAttribute(lut_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(ceil_div(nq, 32), m);
     lut_fast_kernel<<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, ksub, dsub, T);
@@ -882,6 +889,17 @@ __global__ void __launch_bounds__(FS_NT, 2) scan_fast2_kernel(
     if (threadIdx.x == 0 && out_n) out_n[q] = (uint32_t)h;
 }
 
+static size_t scan_fast2_smem(int m, int ksub, int k, int nprobe) {
+    const int kp2 = next_pow2(k < 2 ? 2 : k);
+    const int bp2 = next_pow2(FS_CB + kp2);
+    return (((size_t)m * ksub + 3) & ~(size_t)3) * sizeof(float) +
+           (size_t)(bp2 + kp2) * sizeof(unsigned long long) + (size_t)(nprobe + 1) * 4;
+}
+
+bool scan_fast2_fits(int m, int ksub, int k, int nprobe) {
+    return k >= 1 && k <= kMaxK && scan_fast2_smem(m, ksub, k, nprobe) <= 227 * 1024;
+}
+
 void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
                        const float* probe_d, const float* rc, int nprobe, int m, int ksub,
                        const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,
@@ -891,9 +909,9 @@ void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, c
     if (k > kMaxK) throw CudaError("scan_fast: k exceeds the supported maximum");
     const int kp2 = next_pow2(k < 2 ? 2 : k);
     const int bp2 = next_pow2(FS_CB + kp2);   // merge buffer: candidates + current top, padded
-    const size_t smem = (((size_t)m * ksub + 3) & ~(size_t)3) * sizeof(float) +
-                        (size_t)(bp2 + kp2) * sizeof(unsigned long long) + (size_t)(nprobe + 1) * 4;
-    if (smem > 227 * 1024) throw CudaError("scan_fast: lookup table does not fit in shared memory");
+    const size_t smem = scan_fast2_smem(m, ksub, k, nprobe);
+    if (!scan_fast2_fits(m, ksub, k, nprobe))
+        throw CudaError("scan_fast: lookup table does not fit in shared memory");
 #define VGPU_SF2(MCV)                                                                             \
     do {                                                                                          \
         VGPU_CHECK(cudaFuncSetAttribute(scan_fast2_kernel<MCV>,                                   \
@@ -1109,7 +1127,9 @@ bool lut_reg_launch(const float* rq, long long nq, int dim, const float* cb, int
                                     (int)smem));
     dim3 grid(ceil_div(nq, LB_Q), m / G, 256 / LB_C);
     if constexpr (R >= 4) {
-        if (!std::getenv("VGPU_LUT_SCALAR")) {
+        // float4 stores: every store offset is a multiple of 4 floats (row = m * 256,
+        // G a multiple of 4), so only the table's own address needs 16-byte alignment.
+        if (!std::getenv("VGPU_LUT_SCALAR") && reinterpret_cast<uintptr_t>(T) % 16 == 0) {
             VGPU_CHECK(cudaFuncSetAttribute(lut_blocked_vec_kernel<DSUB, R>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             lut_blocked_vec_kernel<DSUB, R><<<grid, 256, smem, st>>>(rq, nq, dim, cb, m, G, T);

@@ -62,6 +62,10 @@ void launch_merge(const float* cand_d, const uint32_t* cand_pos, const uint32_t*
 // with a running top-k filtered by the current k-th (distance, scan position) key.
 void launch_lut_fast(const float* rq, long long nq, int dim, const float* cb, int m, int ksub, int dsub,
                      float* T, cudaStream_t st);
+// Whether launch_lut_fast / launch_scan_fast2 accept these shapes (their shared-memory
+// and k limits); each launch throws CudaError when its check fails.
+bool lut_fast_fits(int ksub, int dsub);
+bool scan_fast2_fits(int m, int ksub, int k, int nprobe);
 void launch_scan_fast2(const float* T, const float* rq, long long nq, int dim, const uint32_t* probe,
                        const float* probe_d, const float* rc, int nprobe, int m, int ksub,
                        const uint64_t* list_offsets, const uint8_t* codes, const float* vterm,

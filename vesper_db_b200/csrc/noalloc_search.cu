@@ -16,7 +16,9 @@
 //     address; a kernel must never be handed it.  Its device address is looked up
 //     once per device with cudaGetSymbolAddress (with that device current) by the
 //     first allocation-free call on that device, and cached.  Make that first call
-//     before any stream capture.
+//     before any stream capture.  The cached address belongs to the device's primary
+//     context: once cudaDeviceReset has destroyed that context, the entry point must
+//     not be called again on the device in the same process.
 //   * Every call on a device shares the array and it keeps the last call's contents.
 //     Nothing in it has to start at zero: every byte a call reads is written earlier
 //     in the same call.  Calls that overlapped on the GPU would race on it, so the

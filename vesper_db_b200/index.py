@@ -281,6 +281,12 @@ class IvfPqIndex:
         _check(self._lib, self._lib.vesper_ivfpq_get_stats(self._h, C.byref(s)))
         return {f: getattr(s, f) for f, _ in N.Stats._fields_}
 
+    def list_offsets(self) -> np.ndarray:
+        """CSR offsets [nlist+1] of the inverted lists (list l holds entries offs[l]..offs[l+1])."""
+        offs = np.zeros(self.get_stats()["n_lists"] + 1, np.uint64)
+        _check(self._lib, self._lib.vesper_ivfpq_get_lists(self._h, _ptr(offs, C.c_uint64), None, None))
+        return offs
+
     def lists(self):
         """(offsets [nlist+1], ids [N], codes [N, m]) copied from the device."""
         st = self.get_stats()
