@@ -70,7 +70,8 @@ CPU_SAMPLE = 256          # queries the reference searches per nprobe in the cpu
 CHUNK = 125_000           # base rows per generator chunk (80 chunks; divisible by 1/2/4/8)
 SCAN_KERNELS = {1: "scan_exact_kernel", 2: "scan_fast2_kernel", 3: "scan_blocked_kernel",
                 4: "tc_list_scan_kernel"}
-COARSE_KERNELS = {1: "l2_dist_kernel (CUDA cores)", 2: "tc_screen_kernel (tcgen05 tf32) + screen_select_kernel"}
+COARSE_KERNELS = {1: "l2_dist_kernel (CUDA cores)", 2: "tc_screen_kernel (tcgen05 tf32) + screen_select_kernel",
+                  3: "sampled threshold + tc_screen_kernel filter (tcgen05 tf32) + flat_refine_kernel"}
 METRIC = "QPS at matched recall@10 (IVF-PQ, 10k-query batch) at 1/2/4/8 B200 vs CPU ref"
 LIST_SCAN_BYTES_PER_PAIR = (662.9e6 + 8.7e6) / 6.65e9   # ncu, main-pass launch on the 4M-vector case
 
@@ -91,8 +92,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "flat"],
-                    help="ivfpq: the IVF-PQ+OPQ search (default); flat: exact flat top-k, 1M x 768 IP, k=100")
+    ap.add_argument("--workload", default="ivfpq", choices=["ivfpq", "flat", "kmeans", "c5"],
+                    help="ivfpq: the IVF-PQ+OPQ search (default); flat: exact flat top-k, 1M x 768 IP, k=100; "
+                         "kmeans: Lloyd iterations, 2M x 128 points, k=16,384; c5: sharded IVF-PQ search, "
+                         "100M x 128, nlist 65,536, m 32, 100k queries, nprobe 64, k 100")
     # Smaller cases of the same workload, for profiler captures (the defaults are the
     # benchmark's sizes; a line measured with either flag names its sizes in config).
     ap.add_argument("--n-base", type=int, default=0, help="base vectors (multiple of the 125,000-row chunk)")
@@ -480,6 +483,541 @@ def main_flat(args):
     return 0
 
 
+# ------------------------------------------------------------------------------- k-means training
+KM_N, KM_DIM, KM_K, KM_CENTRES, KM_SIGMA, KM_ITERS = 2_000_000, 128, 16_384, 20_000, 0.05, 20
+KM_SEED = 42
+KM_PARITY_N, KM_PARITY_K = 200_000, 2_048     # the scaled run checked against the reference
+KM_CPU_SAMPLE = 100_000                        # points of the reference's timed Lloyd iteration
+KM_METRIC = "k-means Lloyd iterations/s (2,000,000 x 128 points, k=16,384)"
+KM_WORKLOAD = ("k-means training for the coarse quantizer: 2,000,000 x 128 fp32 from a seeded mixture of "
+               "20,000 isotropic Gaussians (sigma 0.05, centres ~U[-1,1]), k=16,384, Lloyd iterations from "
+               "k-means++ (seed 42)")
+
+
+def kmeans_launches_per_iteration():
+    """This library's kernels in one Lloyd iteration: the E-step's point norms, centroid
+    norms, their square roots, the column maxima and the fused tcgen05 arg-min; the
+    M-step's iota, segment boundaries, segmented sums and means (the grouping sort
+    between them is CUB's).  Rows left by a candidate-list overflow would add the filter
+    path's launches; none are expected on this data."""
+    return 5 + 4
+
+
+def main_kmeans(args):
+    """One step = one Lloyd iteration over the 2M points (src/index/kmeans.cpp:137-252):
+    E-step (tcgen05 tf32 screen + exact arg-min in the reference's lane order, lowest
+    index wins a tie), the convergence test's inertia (per-point minima summed in fp64
+    in point order on the host, as the engine's fit does), and the M-step (points
+    grouped by cluster, fp64 sums in point order / count).  The centroids come from the
+    library's k-means++ (the reference's draws); the whole 20-iteration fit through
+    vesper_kmeans_fit_device is timed once beside it."""
+    import numpy as np
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if rank != 0:
+        return 0   # k-means training runs on one GPU here (its sharded form is tested, not benched)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from vesper_db_b200 import _native as N
+    from vesper_db_b200.kmeans import kmeans_fit_device
+    from vesper_db_b200.shard import GpuKmeansOps
+    x = synth.gen_isotropic_mixture(torch, dev, KM_CENTRES, KM_DIM, KM_SIGMA, KM_N, 4242)
+    torch.cuda.synchronize()
+    cfg = {"workload": KM_WORKLOAD, "n": KM_N, "dim": KM_DIM, "k": KM_K, "algorithm": "lloyd",
+           "parallelism": "single GPU", "l2_policy": "inputs larger than L2 (1.02 GB of points per iteration)"}
+    out_common = {"unit": "iterations/s", "higher_is_better": True, "n_gpus": 1, "steps": args.steps,
+                  "warmup": args.warmup, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                  "data": "synthetic (seeded isotropic mixture generated on device)", "config": cfg}
+    if args.impl == "reference":
+        threads, cpu = reference_threads()
+        ol = _oracle_lib()
+        ref = ol.Reference(ol.REF_SO)
+        xs = x[:KM_CPU_SAMPLE].cpu().numpy()
+        c0 = x[torch.randperm(KM_N, device=dev, generator=torch.Generator(device=dev).manual_seed(7))[:KM_K]]
+        c0 = c0.cpu().numpy()
+        step_s = []
+        for s in range(args.warmup + args.steps):
+            t = time.perf_counter()
+            a, _ = ref.kmeans_assign(xs, c0)
+            ref.kmeans_update(xs, a, c0)
+            el = time.perf_counter() - t
+            if s >= args.warmup:
+                step_s.append(el * KM_N / KM_CPU_SAMPLE)
+        v = len(step_s) / sum(step_s)
+        print(json.dumps({"impl": "reference", "metric": KM_METRIC, "value": v, **out_common,
+                          "ms_per_step": 1e3 * sum(step_s) / len(step_s) * KM_CPU_SAMPLE / KM_N,
+                          "cpu_baseline": {"value": v, "unit": "iterations/s", "cores": threads, "kind": "reference",
+                                           "host_cpu": cpu,
+                                           "sample": f"kmeans_assign + kmeans_update (src/index/kmeans.cpp:91-135) "
+                                                     f"on {KM_CPU_SAMPLE:,} of the {KM_N:,} points per step, time "
+                                                     f"scaled by n (work is linear in n); OpenMP on {threads} threads"},
+                          "e2e": {"value": v, "unit": "iterations/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return 0
+
+    ops = GpuKmeansOps()
+    c = torch.empty((KM_K, KM_DIM), device=dev)
+    a = torch.empty(KM_N, dtype=torch.int32, device=dev)
+    mind = torch.empty(KM_N, device=dev)
+    s_sum = torch.empty((KM_K, KM_DIM), dtype=torch.float64, device=dev)
+    s_comp = torch.empty_like(s_sum)
+    s_cnt = torch.empty(KM_K, dtype=torch.int64, device=dev)
+
+    # The whole fit once: k-means++ + 20 Lloyd iterations (+ the final update and the
+    # reference's running-total inertia), through the library's device entry point.
+    t0 = time.perf_counter()
+    it, inertia = kmeans_fit_device(x.data_ptr(), KM_N, KM_DIM, KM_K, c.data_ptr(), a.data_ptr(), max_iter=KM_ITERS,
+                                    epsilon=0.0, seed=KM_SEED, algorithm=N.KMEANS_LLOYD)
+    fit_s = time.perf_counter() - t0
+    # Steps continue from the fitted centroids (the same work per iteration as any other).
+    host_mind = torch.empty(KM_N, dtype=torch.float32, pin_memory=True)
+
+    def one_iteration(xx):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        ops.assign(xx, c, False, a, mind)
+        ev[1].record()
+        host_mind.copy_(mind)
+        np.add.accumulate(host_mind.numpy().astype(np.float64))[-1]   # inertia in point order
+        ev[2].record()
+        s_sum.zero_(), s_comp.zero_(), s_cnt.zero_()
+        ops.accumulate(xx, a, KM_K, N.KMEANS_LLOYD, s_sum, s_comp, s_cnt)
+        ops.finish(s_sum, s_cnt, N.KMEANS_LLOYD, c)
+        ev[3].record()
+        return ev
+
+    for _ in range(args.warmup):
+        one_iteration(x)
+    torch.cuda.synchronize()
+    evs = []
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            evs.append(one_iteration(x))
+        e1.record()
+        torch.cuda.synchronize()
+    ms_total = e0.elapsed_time(e1)
+    e_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / len(evs)
+    inert_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / len(evs)
+    m_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / len(evs)
+
+    # e2e: the points copied from pinned host memory every step, the centroids read back.
+    x_host = torch.empty((KM_N, KM_DIM), dtype=torch.float32, pin_memory=True)
+    x_host.copy_(x)
+    x_dev = torch.empty_like(x)
+    c_host = torch.empty((KM_K, KM_DIM), dtype=torch.float32, pin_memory=True)
+    e2e = []
+    for s in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        x_dev.copy_(x_host, non_blocking=True)
+        one_iteration(x_dev)
+        c_host.copy_(c)
+        f1.record()
+        torch.cuda.synchronize()
+        if s >= args.warmup:
+            e2e.append(f0.elapsed_time(f1))
+    e2e_ms = sum(e2e) / len(e2e)
+
+    peaks, peak_kind = measured_peaks()
+    tf32 = peaks["bf16_tflops"] / 2.0
+    flop = 2.0 * KM_N * KM_K * KM_DIM
+    achieved = flop / (e_ms / 1e3) / 1e12
+    m_bytes = KM_N * KM_DIM * 4 + KM_N * 4
+    out = {"metric": KM_METRIC, "value": args.steps / (ms_total / 1e3), **out_common,
+           "ms_per_step": ms_total / args.steps,
+           "e2e": {"value": 1e3 / e2e_ms, "unit": "iterations/s", "h2d_bytes_per_step": KM_N * KM_DIM * 4,
+                   "d2h_bytes_per_step": KM_K * KM_DIM * 4 + KM_N * 4, "ms_per_step": e2e_ms},
+           "gpu_launches": args.steps * kmeans_launches_per_iteration(),
+           "roofline": {"bound": "tensor", "kernel": "E-step: tc_argmin_kernel (tcgen05 kind::tf32 screen fused "
+                                                     "with the arg-min and its exact refine)",
+                        "achieved": achieved, "peak": tf32, "unit": "TFLOP/s", "frac": achieved / tf32,
+                        "peak_source": f"{peak_kind} bf16 dense burst / 2 (tf32 dense rate)",
+                        "traffic": None, "algorithmic_flop_per_step": flop, "estep_ms": e_ms},
+           "stage_ms": {"estep_ms": e_ms, "inertia_ms": inert_ms, "mstep_ms": m_ms},
+           "mstep": {"algorithmic_bytes": m_bytes, "GBps": m_bytes / (m_ms / 1e3) / 1e9,
+                     "hbm_frac": m_bytes / (m_ms / 1e3) / 1e9 / peaks["hbm_gbs"]},
+           "fit": {"seconds": fit_s, "iterations": it, "inertia": inertia,
+                   "what": "vesper_kmeans_fit_device: k-means++ (16,384 host draws on GPU D^2) + 20 Lloyd "
+                           "iterations + final update and running-total inertia"},
+           "clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        out.update(kmeans_cpu_leg(torch, dev, x, c))
+    print(json.dumps(out))
+    ops.close()
+    return 0
+
+
+def kmeans_cpu_leg(torch, dev, x, c):
+    """The reference's Lloyd iteration (kmeans_assign + kmeans_update) on a sample of the
+    points with the GPU's current centroids, and the scaled fit (200,000 points, k=2,048,
+    20 iterations from k-means++) run by the library and by the reference, compared bit
+    for bit."""
+    import numpy as np
+    from vesper_db_b200.kmeans import kmeans_cluster
+    threads, cpu = reference_threads()
+    ol = _oracle_lib()
+    ref = ol.Reference(ol.REF_SO)
+    xs = x[:KM_CPU_SAMPLE].cpu().numpy()
+    cs = c.cpu().numpy()
+    t = time.perf_counter()
+    a_ref, _ = ref.kmeans_assign(xs, cs)
+    c_ref = ref.kmeans_update(xs, a_ref, cs)
+    el = time.perf_counter() - t
+    ops = __import__("vesper_db_b200.shard", fromlist=["GpuKmeansOps"]).GpuKmeansOps()
+    xs_d = x[:KM_CPU_SAMPLE].contiguous()
+    a_d = torch.empty(KM_CPU_SAMPLE, dtype=torch.int32, device=dev)
+    m_d = torch.empty(KM_CPU_SAMPLE, device=dev)
+    c_d = c.clone()
+    ops.assign(xs_d, c_d, False, a_d, m_d)
+    ss = torch.zeros((KM_K, KM_DIM), dtype=torch.float64, device=dev)
+    sc, sn = torch.zeros_like(ss), torch.zeros(KM_K, dtype=torch.int64, device=dev)
+    from vesper_db_b200 import _native as N
+    ops.accumulate(xs_d, a_d, KM_K, N.KMEANS_LLOYD, ss, sc, sn)
+    ops.finish(ss, sn, N.KMEANS_LLOYD, c_d)
+    ops.close()
+    same_step = {"points": KM_CPU_SAMPLE,
+                 "assignments_equal": bool(np.array_equal(a_d.cpu().numpy().view(np.uint32), a_ref)),
+                 "centroids_equal": bool(np.array_equal(c_d.cpu().numpy(), c_ref))}
+    # scaled fit, both sides from k-means++ with seed 42
+    xp = x[:KM_PARITY_N].cpu().numpy()
+    t = time.perf_counter()
+    g = kmeans_cluster(xp, KM_PARITY_K, max_iter=KM_ITERS, epsilon=0.0, seed=KM_SEED)
+    g_s = time.perf_counter() - t
+    t = time.perf_counter()
+    rc, ra, rit, rin = ref.kmeans_lloyd(xp, KM_PARITY_K, max_iter=KM_ITERS, eps=0.0, seed=KM_SEED)
+    r_s = time.perf_counter() - t
+    fit_parity = {"n": KM_PARITY_N, "k": KM_PARITY_K, "iterations": [g.iterations, rit],
+                  "assignments_equal": bool(np.array_equal(g.assignments, ra)),
+                  "centroids_equal": bool(np.array_equal(g.centroids, rc)),
+                  "inertia": [g.inertia, rin], "inertia_equal": g.inertia == rin,
+                  "gpu_fit_s_host_api": g_s, "reference_fit_s": r_s}
+    v = 1.0 / (el * KM_N / KM_CPU_SAMPLE)
+    return {"cpu_baseline": {"value": v, "unit": "iterations/s", "cores": threads, "kind": "reference",
+                             "host_cpu": cpu,
+                             "sample": f"one Lloyd iteration (kmeans_assign + kmeans_update, src/index/kmeans.cpp:"
+                                       f"91-135) on {KM_CPU_SAMPLE:,} points with the GPU's centroids, {el:.2f} s, "
+                                       f"scaled by n to the {KM_N:,} points"},
+            "parity_vs_reference": {"lloyd_iteration": same_step, "fit": fit_parity}}
+
+
+# ------------------------------------------------------------------------------- sharded 100M-vector search
+C5_N, C5_DIM, C5_CENTRES, C5_SIGMA = 100_000_000, 128, 200_000, 0.1
+C5_NLIST, C5_M, C5_NQ, C5_NPROBE, C5_K = 65_536, 32, 100_000, 64, 100
+C5_CHUNK = 6_250_000          # rows per generated chunk (16 chunks; divisible by 1/2/4/8)
+C5_TRAIN = 2_000_000          # training rows: the first rows of chunk 0, about 30 per list
+C5_GT_Q = 1_000               # queries with exact ground truth (strided across the batch)
+C5_CPU_Q = 128                # queries the reference searches in the cpu_baseline leg
+C5_METRIC = "QPS at recall@100 (IVF-PQ, 100M x 128, 100k-query batch) at 1/2/4/8 B200 vs CPU ref"
+C5_BASE_SEED, C5_QUERY_SEED = 9000, 5678
+
+
+def c5_workload():
+    return (f"Sharded IVF-PQ: N={C5_N:,} x d=128 fp32 from a seeded mixture of 200,000 isotropic Gaussians "
+            f"(sigma=0.1, centres ~U[-1,1]), nlist=65,536, m=32x8 bits (no OPQ), {C5_NQ:,} queries, nprobe=64, "
+            f"k=100, L2; database sharded by vector across the GPUs")
+
+
+def greedy_bins(sizes, bins):
+    """Greedy size-balanced bin packing of lists (largest first onto the lightest GPU):
+    the max/mean load a partition by list would have."""
+    import heapq
+    loads = [(0, b) for b in range(bins)]
+    heapq.heapify(loads)
+    for s in sorted((int(x) for x in sizes), reverse=True):
+        load, b = heapq.heappop(loads)
+        heapq.heappush(loads, (load + s, b))
+    mx = max(l for l, _ in loads)
+    return mx / (sum(int(x) for x in sizes) / bins)
+
+
+def main_c5(args):
+    """A step is one search of the 100k-query batch (nprobe 64, k 100) over the whole
+    100M-vector database: on one GPU the full index, on W GPUs a 1/W vector shard per
+    rank with the probe lists computed once per query across ranks and the per-rank
+    top-100 merged over NCCL.  The index is trained on the GPU (k-means++ and Elkan
+    k-means on 2,000,000 rows, PQ sub-quantizers) and filled chunk by chunk; nothing of
+    that is timed."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ours = args.impl == "ours"
+    if world > 1 and ours:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
+    from vesper_db_b200 import IvfPqIndex
+    from vesper_db_b200.shard import chunks_of, merge_topk, probed_search
+    shard_world = world if ours else 1
+    n_chunks = C5_N // C5_CHUNK
+    my_chunks = chunks_of(rank if ours else 0, shard_world, n_chunks)
+
+    def chunk_rows(c, out=None):
+        return synth.gen_isotropic_mixture(torch, dev, C5_CENTRES, C5_DIM, C5_SIGMA, C5_CHUNK, C5_BASE_SEED + c, out)
+
+    t0 = time.perf_counter()
+    queries = synth.gen_isotropic_mixture(torch, dev, C5_CENTRES, C5_DIM, C5_SIGMA, C5_NQ, C5_QUERY_SEED)
+    gt_rows = np.linspace(0, C5_NQ - 1, C5_GT_Q).round().astype(np.int64)
+    q_gt = queries[torch.from_numpy(gt_rows).to(dev)].contiguous()
+    index = IvfPqIndex()
+    train = chunk_rows(0)[:C5_TRAIN].contiguous()
+    torch.cuda.synchronize()
+    t_train0 = time.perf_counter()
+    index.train_device(train.data_ptr(), C5_TRAIN, C5_DIM, C5_NLIST, C5_M, 8, use_opq=False)
+    t_train = time.perf_counter() - t_train0
+    del train
+    buf = torch.empty((C5_CHUNK, C5_DIM), device=dev)
+    ids = torch.empty(C5_CHUNK, dtype=torch.int64, device=dev)
+    gt_d = torch.full((C5_GT_Q, C5_K), float("inf"), device=dev)
+    gt_i = torch.zeros((C5_GT_Q, C5_K), dtype=torch.int64, device=dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    qn = (q_gt * q_gt).sum(1, keepdim=True)
+    t_add = 0.0
+    for c in my_chunks:
+        chunk_rows(c, out=buf)
+        torch.arange(c * C5_CHUNK, (c + 1) * C5_CHUNK, out=ids)
+        torch.cuda.synchronize()
+        ta = time.perf_counter()
+        index.add_device(ids.data_ptr(), buf.data_ptr(), C5_CHUNK)
+        t_add += time.perf_counter() - ta
+        for s0 in range(0, C5_CHUNK, 500_000):   # exact fp32 ground truth of the sampled queries
+            x = buf[s0:s0 + 500_000]
+            dd = qn - 2.0 * (q_gt @ x.T) + (x * x).sum(1)[None, :]
+            v, i = torch.topk(dd, C5_K, dim=1, largest=False)
+            cd, ci = torch.cat([gt_d, v], 1), torch.cat([gt_i, i + c * C5_CHUNK + s0], 1)
+            gt_d, sel = torch.topk(cd, C5_K, dim=1, largest=False)
+            gt_i = torch.gather(ci, 1, sel)
+    del buf, ids
+    if world > 1 and ours:
+        gt_d, gt_i = merge_topk(gt_d, gt_i, C5_K)
+    gt_np = gt_i.cpu().numpy()
+    torch.cuda.synchronize()
+    build = {"setup_s": time.perf_counter() - t0, "train_s": t_train, "add_s": t_add}
+
+    # list shape: this rank's lists, and the global list sizes (summed over the shards)
+    local_sizes = np.diff(index.list_offsets().astype(np.int64))
+    sizes_t = torch.from_numpy(local_sizes).to(dev)
+    if world > 1 and ours:
+        dist.all_reduce(sizes_t)
+    sizes = sizes_t.cpu().numpy()
+    list_stats_c5 = {"lists": int(sizes.size), "mean": float(sizes.mean()), "max": int(sizes.max()),
+                     "p99": float(np.percentile(sizes, 99)), "empty": int((sizes == 0).sum()),
+                     "max_over_mean": float(sizes.max() / sizes.mean()),
+                     "list_partition_max_over_mean": {str(b): greedy_bins(sizes, b) for b in (2, 4, 8)}}
+
+    if args.impl == "reference":
+        return c5_reference_arm(args, index, queries.cpu().numpy(), gt_rows, gt_np, build, list_stats_c5)
+
+    out_ids = torch.empty((C5_NQ, C5_K), dtype=torch.int64, device=dev)
+    out_d = torch.empty((C5_NQ, C5_K), dtype=torch.float32, device=dev)
+    out_n = torch.empty(C5_NQ, dtype=torch.int32, device=dev)
+    slot = torch.arange(C5_K, device=dev)[None, :]
+    probe_bufs = {}
+
+    def one_search(q):
+        if world > 1:
+            probed_search(index, q, C5_K, C5_NPROBE, C5_NLIST, out_ids, out_d, out_n, probe_bufs)
+            d = torch.where(slot < out_n[:, None], out_d, torch.full_like(out_d, float("inf")))
+            md, mi = merge_topk(d, out_ids, C5_K)
+            return md, mi, torch.isfinite(md).sum(1)
+        index.search_batch_device(q.data_ptr(), C5_NQ, C5_K, C5_NPROBE, out_ids.data_ptr(), out_d.data_ptr(),
+                                  out_n.data_ptr())
+        return out_d, out_ids, out_n
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        one_search(queries)
+    barrier()
+    steps_t, launches = [], 0
+    with ClockSampler(local) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        ev0.record()
+        for _ in range(args.steps):
+            res_d, res_i, res_n = one_search(queries)
+            t = index.last_timings()
+            steps_t.append(t)
+            launches += t["kernel_launches"]
+        ev1.record()
+        barrier()
+    ms_total = ev0.elapsed_time(ev1)
+    if world > 1:
+        tt = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_total = float(tt.item())
+    ms_step = ms_total / args.steps
+    gi_all, gd_all, gn_all = res_i.cpu().numpy(), res_d.cpu().numpy(), res_n.cpu().numpy()
+    recall = recall_at(gi_all[gt_rows], gt_np, C5_K)
+    stage_ms = {k2: sum(t[k2] for t in steps_t) / len(steps_t) for k2 in steps_t[0] if k2.endswith("_ms")}
+    timings = steps_t[-1]
+
+    # e2e: pinned host queries in, merged results to the host, every step
+    q_host = torch.empty((C5_NQ, C5_DIM), dtype=torch.float32, pin_memory=True)
+    q_host.copy_(queries)
+    q_dev = torch.empty_like(queries)
+    e2e_ms = []
+    for s in range(args.warmup + args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record()
+        q_dev.copy_(q_host, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        md, mi, _ = one_search(q_dev)
+        if rank == 0:
+            mi.cpu(), md.cpu()
+        e1.record()
+        barrier()
+        if s >= args.warmup:
+            e2e_ms.append(e0.elapsed_time(e1))
+    e2e_step = sum(e2e_ms) / len(e2e_ms)
+    if world > 1:
+        tt = torch.tensor([e2e_step], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_step = float(tt.item())
+
+    peaks, peak_kind = measured_peaks()
+    entries = sum(t["scanned_entries"] for t in steps_t) / len(steps_t)
+    if timings["scan_variant"] == 4:
+        lk = stage_ms["list_kernel_ms"]
+        flop = 2.0 * C5_DIM * entries
+        achieved = flop / (lk / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "tc_list_scan_kernel (tcgen05 kind::f16, bf16, A in TMEM)",
+                    "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} (bf16 dense, burst)",
+                    "traffic": None, "algorithmic_flop_per_search": flop, "kernel_ms_per_search": lk,
+                    "scan_stage_code_GBps": entries * C5_M / (stage_ms["scan_ms"] / 1e3) / 1e9,
+                    "scan_stage_code_hbm_frac": entries * C5_M / (stage_ms["scan_ms"] / 1e3) / 1e9 / peaks["hbm_gbs"],
+                    "candidates_refined": timings["list_candidates"],
+                    "fallback_queries": timings["list_fallback_queries"]}
+    else:
+        achieved = entries * C5_M / (stage_ms["scan_ms"] / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": SCAN_KERNELS.get(timings["scan_variant"], "?"), "achieved": achieved,
+                    "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                    "peak_source": peak_kind, "traffic": None}
+    out = {"metric": C5_METRIC, "value": C5_NQ * args.steps / (ms_total / 1e3), "unit": "queries/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (seeded isotropic mixture generated on device)",
+           "config": {"workload": c5_workload(), "nlist": C5_NLIST, "m": C5_M, "nprobe": C5_NPROBE, "k": C5_K,
+                      "nq": C5_NQ, "n_base": C5_N, "n_train": C5_TRAIN,
+                      "parallelism": f"vector-sharded x{world}" if world > 1 else "single GPU",
+                      "l2_policy": "inputs larger than L2 (3.2 GB of PQ codes)", "list_stats": list_stats_c5,
+                      "probed_entries_per_query_per_rank": entries / C5_NQ},
+           "recall@100": recall, "recall_queries": C5_GT_Q,
+           "e2e": {"value": C5_NQ / (e2e_step / 1e3), "unit": "queries/s", "h2d_bytes_per_step": C5_NQ * C5_DIM * 4,
+                   "d2h_bytes_per_step": C5_NQ * C5_K * 12, "ms_per_step": e2e_step,
+                   "path": "pinned H2D of the batch, search (probe exchange, shard search, NCCL merge at N>1), "
+                           "rank 0 copies the merged result to the host"},
+           "gpu_launches": launches, "roofline": roofline, "stage_ms": stage_ms,
+           "outside_engine_ms": ms_step - stage_ms["total_ms"],
+           "coarse_kernel": COARSE_KERNELS.get(timings["coarse_variant"], "?"), "build": build,
+           "clocks": clk.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            out.update(c5_cpu_leg(index, queries.cpu().numpy(), gt_rows, gt_np, gi_all, gd_all, gn_all))
+        except Exception as e:
+            out["cpu_baseline"] = {"value": None, "unit": "queries/s", "cores": os.cpu_count(), "kind": "reference",
+                                   "sample": f"unavailable: {e}"}
+    if rank == 0:
+        print(json.dumps(out))
+    index.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def c5_reference_search(index):
+    """Save the GPU-built index as the reference's v1.0 file and load it into the
+    reference's IvfPqIndex (untimed); returns (reference index, load seconds, threads,
+    host description)."""
+    threads, cpu = reference_threads()
+    ol = _oracle_lib()
+    tmp = tempfile.mkdtemp(prefix="vesper_c5_")
+    try:
+        index.save(tmp)
+        ridx = ol.Reference(ol.REF_SO).ivfpq()
+        t0 = time.perf_counter()
+        ridx.load(tmp)
+        load_s = time.perf_counter() - t0
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    return ridx, load_s, threads, cpu
+
+
+def c5_cpu_leg(index, q_np, gt_rows, gt_np, gi_all, gd_all, gn_all):
+    """The reference's search_batch on C5_CPU_Q of the ground-truth queries: its QPS,
+    its recall@100 beside the GPU's on the same queries, and the GPU results compared
+    with the reference's ids and distances (the heap branch of its top-k, pool > 64)."""
+    import numpy as np
+    ridx, load_s, threads, cpu = c5_reference_search(index)
+    pick = np.linspace(0, C5_GT_Q - 1, C5_CPU_Q).round().astype(np.int64)
+    rows = gt_rows[pick]
+    qs = np.ascontiguousarray(q_np[rows])
+    ridx.search(qs[:4], C5_K, C5_NPROBE)
+    t = time.perf_counter()
+    rid, rd, rcnt = ridx.search(qs, C5_K, C5_NPROBE)
+    el = time.perf_counter() - t
+    par = topk_parity(gi_all[rows], gd_all[rows], gn_all[rows], rid, rd, rcnt)
+    return {"cpu_baseline": {"value": C5_CPU_Q / el, "unit": "queries/s", "cores": threads, "kind": "reference",
+                             "host_cpu": cpu,
+                             "sample": f"{C5_CPU_Q} queries of the batch, nprobe={C5_NPROBE}, k={C5_K}, reference "
+                                       f"IvfPqIndex::search_batch with OpenMP on {threads} threads, {el:.1f} s; "
+                                       f"v1.0 file load {load_s:.0f} s untimed"},
+            "recall_matched": [{"nprobe": C5_NPROBE, "queries": C5_CPU_Q, "gpu": recall_at(gi_all[rows], gt_np[pick], C5_K),
+                                "cpu": recall_at(rid, gt_np[pick], C5_K)}],
+            "parity_vs_reference": par}
+
+
+def c5_reference_arm(args, index, q_np, gt_rows, gt_np, build, list_stats_c5):
+    import numpy as np
+    ridx, load_s, threads, cpu = c5_reference_search(index)
+    index.close()
+    per_step = max(16, 2 * threads)
+    step_s, hits, done, qpos = [], 0, 0, 0
+    for s in range(args.warmup + args.steps):
+        rows = gt_rows[(np.arange(per_step) + qpos) % C5_GT_Q]
+        qpos += per_step
+        t = time.perf_counter()
+        rid, _, _ = ridx.search(np.ascontiguousarray(q_np[rows]), C5_K, C5_NPROBE)
+        el = time.perf_counter() - t
+        if s >= args.warmup:
+            step_s.append(el)
+            g = gt_np[(np.arange(per_step) + qpos - per_step) % C5_GT_Q]
+            hits += sum(len(set(a) & set(b)) for a, b in zip(rid.tolist(), g.tolist()))
+            done += per_step
+    v = done / sum(step_s)
+    print(json.dumps({"impl": "reference", "metric": C5_METRIC, "value": v, "unit": "queries/s",
+                      "higher_is_better": True, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": 1e3 * sum(step_s) / len(step_s), "queries_per_step": per_step,
+                      "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded mixture)",
+                      "config": {"workload": c5_workload(), "nprobe": C5_NPROBE, "k": C5_K, "nq": C5_NQ,
+                                 "list_stats": list_stats_c5},
+                      "recall@100": hits / max(1, done * C5_K),
+                      "cpu_baseline": {"value": v, "unit": "queries/s", "cores": threads, "kind": "reference",
+                                       "host_cpu": cpu,
+                                       "sample": f"{done} queries ({per_step} per step) of the batch, OpenMP on "
+                                                 f"{threads} threads; v1.0 file load {load_s:.0f} s untimed"},
+                      "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                      "build": build}))
+    return 0
+
+
 # ------------------------------------------------------------------------------- main
 def build_ivfpq_workload(args, torch, dev, world, rank):
     """Data, training and add of the IVF-PQ+OPQ workload on this rank's GPU (untimed),
@@ -622,6 +1160,10 @@ def main():
     args = parse()
     if args.workload == "flat":
         return main_flat(args)
+    if args.workload == "kmeans":
+        return main_kmeans(args)
+    if args.workload == "c5":
+        return main_c5(args)
     import numpy as np
     import torch
     import torch.distributed as dist

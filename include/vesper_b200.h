@@ -183,7 +183,7 @@ typedef struct vesper_ivfpq_timings_s {
   uint32_t kernel_launches; /* kernels launched by the call */
   uint32_t scan_variant;    /* 1 exact per-(query, list) tables, 2 per-query tables, 3 blocked layout,
                                4 tensor-core list scan (bf16 screen + exact FAST refine) */
-  uint32_t coarse_variant;  /* 1 CUDA-core exact distances, 2 tensor-core screen + exact refine */
+  uint32_t coarse_variant;  /* 1 CUDA-core exact distances, 2 tensor-core screen + exact refine, 3 tensor-core filter against a sampled threshold + exact refine */
   float list_kernel_ms;     /* variant 4: device time of the tensor-core screening kernel */
   uint64_t list_candidates; /* variant 4: (query, entry) pairs the screen kept */
   uint32_t list_fallback_queries; /* variant 4: queries scanned by the blocked scan instead */

@@ -47,9 +47,52 @@ def test_golden_elkan_and_lloyd():
     _check_lloyd_inertia(lo.inertia, float(g["lloyd_inertia"]))
 
 
-@pytest.mark.parametrize("n,d,k,iters", [(20000, 64, 256, 6), (12000, 128, 512, 4), (5000, 20, 100, 5)])
+def _with_kpp(mode, fn):
+    old = os.environ.get("VGPU_KPP")
+    os.environ["VGPU_KPP"] = mode
+    try:
+        return fn()
+    finally:
+        if old is None:
+            os.environ.pop("VGPU_KPP", None)
+        else:
+            os.environ["VGPU_KPP"] = old
+
+
+@pytest.mark.parametrize("n,d,k", [(60000, 64, 600), (30000, 20, 300), (4099, 128, 64)])
+def test_kmeanspp_device_draws_equal_host_draws(oracle, n, d, k):
+    """k-means++ with the prefix sums and the lower_bound on the device (the path large
+    n * k takes) picks the same rows as the host sampler and the oracle, which recompute
+    the reference's fp64 prefix sum in point order for every draw."""
+    from vesper_db_b200 import kmeans_cluster
+    x = _mixture(n, d, 2 * k, 0.05, 7 + d)
+    host = _with_kpp("host", lambda: kmeans_cluster(x, k, 2, 0.0, 42))
+    dev = _with_kpp("device", lambda: kmeans_cluster(x, k, 2, 0.0, 42))
+    c, a, it, inertia = oracle.kmeans_lloyd(x, k, 2, 0.0, 42)
+    for got in (host, dev):
+        assert np.array_equal(got.centroids, c)
+        assert np.array_equal(got.assignments, a)
+        assert got.iterations == it
+        _check_lloyd_inertia(got.inertia, inertia)
+
+
+def test_lloyd_zero_iterations_matches_reference(oracle, reference):
+    """max_iter = 0: no iteration runs; the final update reads the assignment vector as
+    the reference initialises it (all points in cluster 0)."""
+    from vesper_db_b200 import kmeans_cluster
+    x = _mixture(3000, 32, 60, 0.05, 5)
+    c, a, it, inertia = reference.kmeans_lloyd(x, 20, 0, 0.0, 42)
+    got = kmeans_cluster(x, 20, 0, 0.0, 42)
+    assert it == 0 and got.iterations == 0
+    assert np.array_equal(got.assignments, a)
+    assert np.array_equal(got.centroids, c)
+
+
+@pytest.mark.parametrize("n,d,k,iters", [(20000, 64, 256, 6), (12000, 128, 512, 4), (5000, 20, 100, 5),
+                                         (30000, 64, 2048, 3), (24000, 32, 4100, 2)])
 def test_lloyd_matches_oracle(oracle, n, d, k, iters):
-    """k >= 64 with d % 4 == 0 runs the tcgen05 screen; d = 20 the CUDA-core kernel."""
+    """k >= 64 with d % 4 == 0 runs the tcgen05 screen (k <= 1024: one screen of every
+    centroid; above: the filter against a sampled threshold); d = 20 the CUDA-core kernel."""
     from vesper_db_b200 import kmeans_cluster
     x = _mixture(n, d, 3 * k, 0.05, 31 + d)
     c, a, it, inertia = oracle.kmeans_lloyd(x, k, iters, 0.0, 42)
@@ -60,11 +103,16 @@ def test_lloyd_matches_oracle(oracle, n, d, k, iters):
     _check_lloyd_inertia(got.inertia, inertia)
 
 
-def test_elkan_matches_oracle_tensor_core_path(oracle):
+@pytest.mark.parametrize("n,d,k,dup", [(16000, 96, 300, False), (30000, 64, 2000, True)])
+def test_elkan_matches_oracle_tensor_core_path(oracle, n, d, k, dup):
+    """k = 2000 runs the filter path, with duplicated points so that centroids tie and
+    the keep-on-tie rule decides."""
     from vesper_db_b200 import kmeans_elkan
-    x = _mixture(16000, 96, 600, 0.08, 5)
-    c, a, it, inertia = oracle.kmeans_elkan(x, 300, 25, 1e-4, 42)
-    got = kmeans_elkan(x, 300, 25, 1e-4, 42)
+    x = _mixture(n, d, 2 * k, 0.08, 5)
+    if dup:
+        x[1::5] = x[0::5][: x[1::5].shape[0]]
+    c, a, it, inertia = oracle.kmeans_elkan(x, k, 25, 1e-4, 42)
+    got = kmeans_elkan(x, k, 25, 1e-4, 42)
     assert np.array_equal(got.assignments, a) and np.array_equal(got.centroids, c)
     assert got.iterations == it and np.float32(got.inertia) == np.float32(inertia)
 
@@ -192,3 +240,36 @@ def test_two_gpu_sharded_fit_equals_single_gpu(tmp_path, algorithm):
     assert int(r["it"]) == it and np.float32(r["inertia"]) == np.float32(inertia)
     assert np.array_equal(r["c"], dc.cpu().numpy())
     assert np.array_equal(r["a"], da.cpu().numpy())
+
+
+@pytest.mark.parametrize("keep", [False, True])
+def test_fused_argmin_ties_and_overflow(oracle, keep):
+    """The fused tensor-core arg-min (tc_argmin_kernel) against the oracle's exact
+    arg-min: five centroids repeated 20 more times give rows more exact ties than the
+    kernel's per-row candidate list holds (those rows take the overflow path), the rest
+    are ordinary; with keep_on_tie, a point whose current centroid ties its nearest
+    keeps it (KmeansElkan's rule), any other point moves to the lowest index."""
+    import torch
+
+    from vesper_db_b200.shard import GpuKmeansOps
+    rng = np.random.default_rng(3)
+    d, kb, n = 64, 200, 50000
+    base_c = rng.uniform(-1, 1, (kb, d)).astype(np.float32)
+    c = np.concatenate([base_c, np.repeat(base_c[:5], 20, axis=0)])
+    x = (base_c[rng.integers(0, kb, n)] + 0.05 * rng.standard_normal((n, d))).astype(np.float32)
+    ref = oracle.assign(x, c)
+    dup = ref < 5
+    assert dup.sum() > 500
+    init = np.where(dup, kb + 20 * ref.astype(np.int64) + 19, (ref.astype(np.int64) + 1) % kb).astype(np.uint32)
+    ops = GpuKmeansOps()
+    xt, ct = torch.from_numpy(x).cuda(), torch.from_numpy(c).cuda()
+    a = torch.from_numpy(init.view(np.int32).copy()).cuda()
+    m = torch.empty(n, dtype=torch.float32, device="cuda")
+    ops.assign(xt, ct, keep, a, m)
+    torch.cuda.synchronize()
+    got = a.cpu().numpy().view(np.uint32)
+    want = np.where(dup, init, ref) if keep else ref
+    assert np.array_equal(got, want)
+    dist = np.array([oracle.l2_sq(x[i], c[ref[i]]) for i in range(0, n, 97)], np.float32)
+    assert np.array_equal(m.cpu().numpy()[::97], dist)
+    ops.close()

@@ -301,11 +301,11 @@ struct View {
 // one filtering screen and the refine.  `stats` (top level only) receives stage times.
 void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, const View& v, int k,
                uint32_t* out_idx, float* out_val, FlatWork& w, int depth, FlatStats* stats, cudaStream_t st,
-               Feed* feed = nullptr) {
+               Feed* feed = nullptr, long long single_max = FLAT_SINGLE) {
     const int ke = (int)std::min<long long>(k, v.n);
     const int cap = k <= 128 ? 4096 : 16384;
     const long long stride = flat_sample_stride(v.n, k);
-    if (v.n <= FLAT_SINGLE || depth + 1 >= FlatWork::kLevels || stride < 2) {
+    if (v.n <= single_max || depth + 1 >= FlatWork::kLevels || stride < 2) {
         if (feed) feed->ready(v.n, st, w.launches);
         exact_rows(ip, q, nq, xn, v.base, v.n, v.ld, v.cn, dim, k, out_idx, out_val, w, st);
         if (stats) stats->single_pass = 1;
@@ -334,7 +334,8 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     if (stats) check(cudaEventRecord(w.ev[1], st), "event");
     const View sample = feed ? View{feed->sample_rows, ns, (long long)dim, L.cn.data(), L.cs.data()}
                              : View{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
-    view_topk(ip, q, nq, xn, dim, sample, k, L.s_idx.data(), L.s_val.data(), w, depth + 1, nullptr, st);
+    view_topk(ip, q, nq, xn, dim, sample, k, L.s_idx.data(), L.s_val.data(), w, depth + 1, nullptr, st, nullptr,
+              single_max);
     w.tau.reserve(nq);
     flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(L.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
     check(cudaGetLastError(), "flat_tau_kernel");
@@ -434,7 +435,8 @@ FlatWork::~FlatWork() {
 
 namespace {
 void flat_topk_body(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
-                    uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st, Feed* feed) {
+                    uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st, Feed* feed,
+                    long long single_max = FLAT_SINGLE) {
     if (!w.ev[0])
         for (auto& e : w.ev) check(cudaEventCreate(&e), "cudaEventCreate");
     const int ke = (int)std::min<long long>(k, nb);
@@ -458,7 +460,7 @@ void flat_topk_body(bool ip, const float* q, long long nq, const float* base, lo
     check(cudaEventRecord(w.ev[2], st), "event");
     FlatStats stats;
     const View v{base, nb, dim, w.cn.data(), w.csq.data()};
-    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st, feed);
+    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st, feed, single_max);
     if (k > ke) {
         pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
         check(cudaGetLastError(), "pad_topk_kernel");
@@ -494,6 +496,44 @@ void check_flat_args(const float* q, const float* base, long long nb, int dim, i
         throw CudaError("flat_topk: queries and base must be 16-byte aligned");
 }
 }  // namespace
+
+namespace {
+// Elkan's keep-on-tie rule on a top-1: where the current assignment's exact distance
+// (reference lane order) equals the nearest one, the current assignment stays.
+// Four rows per warp, eight lanes per row.
+__global__ void keep_on_tie_kernel(const float* __restrict__ x, long long n, int dim, const float* __restrict__ c,
+                                   const uint32_t* __restrict__ keep, uint32_t* __restrict__ idx,
+                                   const float* __restrict__ val) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp * 4; b < n; b += nw * 4) {   // warp-uniform trip count
+        const long long i = b + (lane >> 3);
+        const bool act = i < n;
+        const uint32_t kc = act ? keep[i] : 0u;
+        const float v = warp_l2_group(x + (act ? i : 0) * dim, c + (long long)kc * dim, dim, act);
+        if (act && (lane & 7) == 0 && kc != idx[i] && v == val[i]) idx[i] = kc;
+    }
+}
+}  // namespace
+
+// Views above this many columns take the sampled threshold and the filtering screen in
+// launch_exact_nearest (a one-pass screen writes and re-reads nx * nc screen values).
+constexpr long long kNearestSingle = 1024;
+
+void launch_exact_nearest(const float* x, long long nx, const float* c, long long nc, int dim, int k,
+                          const uint32_t* keep, uint32_t* out_idx, float* out_val, FlatWork& w, cudaStream_t st) {
+    w.last = FlatStats{};
+    if (nx <= 0 || nc <= 0 || k <= 0) return;
+    check_flat_args(x, c, nc, dim, k);
+    if (keep && k != 1) throw CudaError("exact_nearest: the keep-on-tie rule applies to k = 1");
+    flat_topk_body(false, x, nx, c, nc, dim, k, out_idx, out_val, w, st, nullptr, kNearestSingle);
+    if (keep) {
+        keep_on_tie_kernel<<<grid_for(nx * 8, 256), 256, 0, st>>>(x, nx, dim, c, keep, out_idx, out_val);
+        check(cudaGetLastError(), "keep_on_tie_kernel");
+        ++w.launches;
+    }
+}
 
 void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
                       uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st) {

@@ -38,6 +38,9 @@ constexpr size_t kDistBudget = size_t(512) << 20;  // bytes per distance-matrix 
 // every probed list's codes streamed once and its queries in full tiles (a 10k-query
 // batch at nlist 16384 is 655 MB).
 constexpr size_t kSearchDistBudget = size_t(1) << 30;
+// With the filtering probe (no distance matrix) a chunk is bounded by its per-query
+// tables instead: m * 2^nbits floats per query.
+constexpr size_t kSearchTableBudget = size_t(4) << 30;
 constexpr int kListScanCap = 4096;                   // screened candidates kept per query (2048: more overflow fallbacks, 8192: no faster)
 
 auto fail(error_code c, std::string msg, std::string comp = "ivf_pq") {
@@ -151,6 +154,7 @@ public:
     mutable DeviceBuffer<unsigned long long> w_scanned;
     mutable Pinned pin_a, pin_b, pin_c;
     mutable std::unique_ptr<vgpu::KmeansEngine> kme;
+    mutable vgpu::FlatWork w_flat;   // the coarse probe's sampled-threshold filter
     // Exact rerank: id -> first entry map (rebuilt after the lists change) and scratch.
     mutable bool id_map_ok = false;
     mutable DeviceBuffer<uint64_t> d_sid, w_pool_ids;
@@ -246,6 +250,13 @@ public:
         if (v && (std::string(v) == "blocked" || std::string(v) == "split")) return false;
         const double per_query = (double)n_vectors / std::max<uint32_t>(nlist(), 1) * np;
         return per_query >= 1024.0 && nq >= 256;
+    }
+
+    // The coarse probe's route for queries at dq: the tensor-core filter with the
+    // sampled threshold (launch_exact_nearest) unless the shapes rule the tensor cores
+    // out or VGPU_NEAREST=screen asks for the one-pass screen + screen_select.
+    bool filter_probe(const float* dq) const {
+        return vgpu::use_tensor_cores(dq, d_cent.data(), (int)dim, nlist()) && !vgpu::screen_all_columns();
     }
 
     void recompute_vterms() {
@@ -609,7 +620,12 @@ public:
         DeviceBuffer<uint32_t> assign(n);
         DeviceBuffer<uint8_t> new_codes(n * M);
         {
-            const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * std::max<size_t>(nlist(), dim))));
+            // Row chunks bounded by the residual buffer, and by the distance matrix when
+            // the assignment writes one (the fused tensor-core arg-min does not).
+            const bool fused = vgpu::use_tensor_cores(on_device ? data : d_cent.data(), d_cent.data(), (int)dim,
+                                                      nlist()) && !vgpu::screen_all_columns();
+            const size_t width = fused ? dim : std::max<size_t>(nlist(), dim);
+            const size_t rows = std::max<size_t>(1, std::min<size_t>(n, kDistBudget / (sizeof(float) * width)));
             DeviceBuffer<float> x(on_device ? 0 : rows * dim), res(rows * dim);
             for (size_t r0 = 0; r0 < n; r0 += rows) {
                 const size_t nr = std::min(rows, n - r0);
@@ -1038,11 +1054,16 @@ public:
         std::lock_guard<std::mutex> lock(mu);
         const uint32_t k = sp.k;
         const bool exact = sp.mode == SearchMode::Exact;
-        // Chunk queries so the coarse distance tile and the exact-path buffers stay bounded.
-        size_t qc = std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist()));
+        // Chunk queries so the coarse distance tile (when one is written), the tables and
+        // the exact-path buffers stay bounded.  Device queries keep their alignment per
+        // chunk (rows of dim floats, dim % 4 == 0 on the tensor-core path); host queries
+        // are copied into w_q.
+        const bool filt = !ext_probe && filter_probe(on_device ? queries : d_cent.data());  // w_q is cudaMalloc'd
+        size_t qc = filt ? std::max<size_t>(1, kSearchTableBudget / (sizeof(float) * (size_t)m() * ksub))
+                         : std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist()));
         if (exact && has_rot) qc = std::min(qc, std::max<size_t>(1, kDistBudget / (sizeof(float) * np * dim)));
         qc = std::min(qc, nq);
-        w_D.reserve(qc * nlist());
+        if (!filt && !ext_probe) w_D.reserve(qc * nlist());
         w_probe.reserve(qc * np);
         w_probe_d.reserve(qc * np);
         if (!on_device) {
@@ -1100,6 +1121,9 @@ public:
             cudaEventRecord(ev[0], st);
             if (ext_probe) {
                 // probe lists given
+            } else if (filt) {
+                vgpu::launch_exact_nearest(dq, (long long)nc, d_cent.data(), nlist(), (int)dim, (int)np, nullptr,
+                                           w_probe.data(), w_probe_d.data(), w_flat, st);
             } else if (tc) {
                 w_xn.reserve(qc);
                 reset_err();
@@ -1111,8 +1135,8 @@ public:
                                      (long long)nlist(), st);
             }
             cudaEventRecord(ev[1], st);
-            if (ext_probe) {
-                // probe lists given
+            if (ext_probe || filt) {
+                // probe lists given, or selected by the filter path
             } else if (tc) {
                 vgpu::launch_screen_select(w_D.data(), (long long)nc, (long long)nlist(), (int)nlist(), dq, (int)dim,
                                            d_cent.data(), w_xn.data(), d_cn.data(), (int)np, nullptr, w_probe.data(),
@@ -1184,17 +1208,18 @@ public:
                 cudaEventRecord(ev[4], st);
             }
             cudaEventRecord(ev[5], st);
-            tm.kernel_launches += (ext_probe ? 1 : 3) + (exact ? 2 : 2) + (has_rot ? 1 : 0) + (tc ? 1 : 0) +
-                                  (!exact && has_blocks ? 1 : 0) + (list_scan ? 12 : 0);
+            tm.kernel_launches += (ext_probe ? 1 : filt ? 1 + (uint32_t)w_flat.last.launches : 3) + (exact ? 2 : 2) +
+                                  (has_rot ? 1 : 0) + (tc && !filt ? 1 : 0) + (!exact && has_blocks ? 1 : 0) +
+                                  (list_scan ? 12 : 0);
             tm.scan_variant = exact ? 1u : list_scan ? 4u : (has_blocks ? 3u : 2u);
-            tm.coarse_variant = tc ? 2u : 1u;
+            tm.coarse_variant = filt ? 3u : tc ? 2u : 1u;
             if (!on_device) {
                 d2h(out_ids + q0 * k, oid, nc * k, st);
                 d2h(out_d + q0 * k, od, nc * k, st);
                 if (out_n) d2h(out_n + q0, on, nc, st);
             }
             sync(st);
-            if (tc || list_scan) check_err();
+            if ((tc && !filt) || list_scan) check_err();
             float a = 0;
             cudaEventElapsedTime(&a, ev[0], ev[1]); tm.coarse_ms += a;
             cudaEventElapsedTime(&a, ev[1], ev[2]); tm.select_ms += a;
@@ -1235,6 +1260,12 @@ public:
         if (nq == 0 || np == 0) return {};
         if (np > (uint32_t)vgpu::kMaxK) return fail(error_code::unsupported, "nprobe above 1024 is not supported by the GPU path");
         std::lock_guard<std::mutex> lock(mu);
+        if (filter_probe(dq_all)) {
+            vgpu::launch_exact_nearest(dq_all, (long long)nq, d_cent.data(), nlist(), (int)dim, (int)np, nullptr,
+                                       d_probe, d_probe_d, w_flat, st);
+            sync(st);
+            return {};
+        }
         const size_t qc = std::min(nq, std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist())));
         w_D.reserve(qc * nlist());
         for (size_t q0 = 0; q0 < nq; q0 += qc) {

@@ -110,7 +110,7 @@ struct SearchTimings {
     std::uint32_t kernel_launches{0};   // kernels this library launched for the call
     std::uint32_t scan_variant{0};      // 1 exact per-list LUT, 2 per-query LUT, 3 blocked per-query LUT,
                                         // 4 tensor-core list scan + refine
-    std::uint32_t coarse_variant{0};    // 1 CUDA-core exact distances, 2 tensor-core screen + exact refine
+    std::uint32_t coarse_variant{0};    // 1 CUDA-core exact distances, 2 tensor-core screen + exact refine, 3 sampled-threshold filter + exact refine
     float list_kernel_ms{0};            // variant 4: device time of the tensor-core screening kernel
     std::uint64_t list_candidates{0};   // variant 4: pairs kept by the screen (refined)
     std::uint32_t list_fallback_queries{0};  // variant 4: queries handed to the blocked scan

@@ -137,6 +137,14 @@ void launch_csr_scatter(const uint8_t* new_codes, const uint64_t* new_ids, const
 
 // ----------------------------------------------------------------------- k-means
 // k-means++ D^2 update: mind[i] = min(mind[i], l2(x_i, c)).
+// k-means++ draws on the device: refresh D^2 with centroid c and write per-block fp64
+// sums (kpp_blocks(n) of them), then pick the row whose running D^2 prefix first
+// reaches u[ci] * total and copy it into centroids row ci (kmeans_kernels.cu).
+long long kpp_blocks(long long n);
+void launch_kpp_update_sum(const float* x, long long n, int dim, const float* c, float* mind, double* block_sum,
+                           cudaStream_t st);
+void launch_kpp_pick(const float* x, long long n, int dim, const float* mind, const double* block_sum,
+                     const double* u, int ci, float* centroids, cudaStream_t st);
 void launch_kpp_update(const float* x, long long n, int dim, const float* c, float* mind,
                        cudaStream_t st);
 // Segmented M-step.  order: point indices grouped by cluster (ascending within a

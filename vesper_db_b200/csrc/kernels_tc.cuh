@@ -65,6 +65,14 @@ struct FlatWork {
 // rows (16-byte aligned); out_idx/out_score: device [nq x k].  Synchronous on st.
 void launch_flat_topk(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
                       uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st);
+// Exact k nearest rows of c [nc x dim] for every row of x [nx x dim] under squared L2
+// (reference lane order; ties to the lowest index): launch_flat_topk's sampled-threshold
+// filter path, which never writes an nx x nc matrix of screen values.  keep (device
+// [nx], may be null, k == 1 only): where the row's current centroid ties the nearest,
+// it stays (KmeansElkan::assign_with_bounds).  keep must not alias out_idx.  out_val
+// receives the exact distances.  Synchronous on st.
+void launch_exact_nearest(const float* x, long long nx, const float* c, long long nc, int dim, int k,
+                          const uint32_t* keep, uint32_t* out_idx, float* out_val, FlatWork& w, cudaStream_t st);
 // The same with the base in host memory (pinned for the copy to overlap): `dev_base`
 // [nb x dim] receives it.  The threshold pass's sample rows are copied first; the rest
 // arrives in chunks on a second stream while the sample pass runs, and each chunk is
@@ -73,6 +81,20 @@ void launch_flat_topk_host(bool ip, const float* q, long long nq, const float* h
                            long long nb, int dim, int k, uint32_t* out_idx, float* out_score, FlatWork& w,
                            cudaStream_t st);
 
+// Fused exact nearest centroid (k = 1) on the tensor cores (tc_argmin_kernel): x [nx x
+// dim] against c [nc x dim] with row norms xn, column norms cn, their square roots cs
+// and cmax = {max cn, max cs} (launch_col_max).  out_idx/out_val receive the reference
+// lane-order arg-min (ties to the lowest index; with keep, to keep[row] -- keep must not
+// alias out_idx).  Rows whose candidate list overflowed are appended to over[] with
+// *n_over counting them (zero it first); they are left for the caller.  err receives a
+// nonzero code if a bounded wait expired.
+bool tc_argmin_supported(int dim);
+void launch_col_max(const float* cn, const float* cs, int nc, float* cmax, cudaStream_t st);
+void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
+                      const float* cs, const float* cmax, const uint32_t* keep, uint32_t* out_idx, float* out_val,
+                      uint32_t* over, uint32_t* n_over, int* err, cudaStream_t st);
+void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const float* val, uint32_t* out_idx,
+                         float* out_val, cudaStream_t st);
 // out[i] = ||x_i||^2 (fp64 accumulation); row i at x + i * ld (ld = dim by default).
 void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st, long long ld = 0);
 // Per row: exact k nearest centroids (reference-order distances, ties to the lowest

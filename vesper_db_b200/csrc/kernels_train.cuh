@@ -45,6 +45,7 @@ void launch_row_l2(const float* a, const float* b, long long n, int dim, float* 
 void launch_transpose(const float* in, int d, float* out, cudaStream_t st);
 void launch_gather_rows(const float* x, int dim, const uint32_t* idx, long long n, float* out,
                         cudaStream_t st);
+void launch_gather_u32(const uint32_t* src, const uint32_t* idx, long long n, uint32_t* out, cudaStream_t st);
 void launch_d2f(const double* in, long long n, float* out, cudaStream_t st);
 
 }  // namespace vgpu

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "kernels_tc.cuh"
 #include "kernels_train.cuh"
 
 namespace vgpu {
@@ -18,6 +19,13 @@ namespace vgpu {
 // unless the shapes or the pointer alignment rule it out, or VGPU_COARSE=exact asks
 // for the CUDA-core kernels; both give the same (exact) result.
 bool use_tensor_cores(const float* x, const float* c, int d, uint32_t k);
+
+// Whether the tensor-core nearest-centroid search screens every (row, centroid) pair
+// into a distance matrix (VGPU_NEAREST=screen) instead of the sampled-threshold filter.
+bool screen_all_columns();
+
+// Whether k-means++ for n points and k centroids draws on the device (see kmeans_gpu.cpp).
+bool kmeanspp_on_device(size_t n, uint32_t k);
 
 // The draws of kmeans_plusplus_init (src/index/kmeans.cpp:45-89) on the host: the
 // reference's std::mt19937(seed), uniform_int_distribution<size_t> for the first row,
@@ -56,6 +64,8 @@ public:
 
     // kmeans_plusplus_init (src/index/kmeans.cpp:45-89): k rows of x copied into d_c.
     void kmeanspp(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c);
+    // The same draws with the D^2 prefix sums and the lower_bound on the device.
+    void kmeanspp_device(const float* d_x, size_t n, int d, uint32_t k, uint32_t seed, float* d_c);
 
     // KmeansElkan::cluster (src/index/kmeans_elkan.cpp:293-430) when elkan, else the
     // Lloyd loop of kmeans_cluster (src/index/kmeans.cpp:137-252, one run).
@@ -76,13 +86,19 @@ public:
     // points of x in order (launch_ordered_sq_sum).
     void running_inertia(const float* d_x, size_t n, int d, const float* d_c, const uint32_t* d_assign, float* total);
     void sync();
+    // Rows the last fused arg-min left to the filter path (candidate-list overflow).
+    uint32_t last_overflow() const { return last_overflow_; }
 
 private:
     cudaStream_t st_;
-    DeviceBuffer<float> D_, xn_, cn_, mind_, kpp_;
+    DeviceBuffer<float> D_, xn_, cn_, cs_, cmax_, mind_, kpp_, ox_, oval_;
+    DeviceBuffer<uint32_t> over_, oidx_, okeep_;
+    uint32_t last_overflow_ = 0;
+    DeviceBuffer<double> kpp_bsum_, kpp_u_;
     DeviceBuffer<int> err_;
-    DeviceBuffer<uint32_t> order_, seg_;
+    DeviceBuffer<uint32_t> order_, seg_, keep_;
     GroupWork gw_;
+    FlatWork flat_;
     void* pin_ = nullptr;
     size_t pin_bytes_ = 0;
     float* pinned(size_t n);

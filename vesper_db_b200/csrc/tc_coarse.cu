@@ -40,6 +40,7 @@ constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr uint32_t TMEM_COLS = 256;
 
 using tc::kSpinLimit;
+using tc::mbar_arrive;
 using tc::mbar_expect_tx;
 using tc::mbar_init;
 using tc::mbar_wait;
@@ -359,6 +360,314 @@ void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, lon
     else
         tc_screen_launch<2>(x, nx, c, nc, c_stride, dim, xn, cn, nullptr, 0, err, tau, cand, cand_cnt, cap, col_off,
                             st, cs);
+}
+
+// ---------------------------------------------------------------------------------
+// Fused nearest centroid (k = 1): tc_argmin_kernel.
+// One persistent CTA per 128-row block walks every 256-column centroid tile:
+//   warp 4 (one lane)  TMA producer of the 128x32 / 256x32 fp32 operand tiles (4-stage ring);
+//   warp 5 (one lane)  tcgen05.mma.kind::tf32 into two 256-column TMEM accumulators, so
+//                      the next tile's products run while the epilogue reads the last;
+//   warps 0..3         epilogue, thread = row: for every column the screen value
+//                      Dt = ||x||^2 + ||c||^2 - 2S and its proven error eps (the filter
+//                      modes' bound), a running minimum U of the upper bounds Dt + eps,
+//                      and the columns whose lower bound Dt - eps is <= U kept in a
+//                      per-row list of ARG_CAP (compacted against the current U when it
+//                      fills).
+// Then each warp re-scores its rows' surviving columns exactly (reference lane order)
+// and keeps the smallest (distance, index) -- the exact arg-min, ties to the lowest
+// index, or, with `keep`, to the current assignment (KmeansElkan's rule).  No screen
+// value ever reaches global memory.  A row whose list overflows is appended to `over`
+// for the caller to redo.  Every wait is bounded; on timeout the kernel records an
+// error code, stops, and frees its TMEM.
+// ---------------------------------------------------------------------------------
+namespace {
+constexpr int ARG_CAP = 16;
+constexpr int ARG_THREADS = 192;
+constexpr int ARG_SMEM = STAGES * STAGE_BYTES + 1024 + 256 + ARG_CAP * BM * 8;
+constexpr uint32_t ARG_TMEM_COLS = 512;
+}  // namespace
+
+__global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
+    const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_c, int nx, int nc, int dim,
+    const float* __restrict__ x, const float* __restrict__ cent, const float* __restrict__ xn,
+    const float* __restrict__ cn, const float* __restrict__ cs, const float* __restrict__ cmax,
+    const uint32_t* __restrict__ keep, uint32_t* __restrict__ out_idx, float* __restrict__ out_val,
+    uint32_t* __restrict__ over, uint32_t* __restrict__ n_over, int* __restrict__ err) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;     // [2]
+    uint64_t* acc_empty = acc_full + 2;      // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    // barriers in the first 256 bytes past the ring, then the candidate lists (the
+    // other 1024 bytes of ARG_SMEM's slack absorb the 1024-byte alignment of smem)
+    uint32_t* cand_col = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + 256);  // [ARG_CAP][BM]
+    float* cand_lb = reinterpret_cast<float*>(cand_col + ARG_CAP * BM);                         // [ARG_CAP][BM]
+    __shared__ int s_fail;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM;
+    const int kt = (dim + BK - 1) / BK;
+    const int ntiles = (nc + BN - 1) / BN;
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], 4); }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(ARG_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            // TMA producer: the same row tile with every column tile, K-slices in order.
+            int it = 0;
+            for (int j = 0; j < ntiles && !s_fail; ++j) {
+                for (int t = 0; t < kt; ++t, ++it) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { s_fail = 1; break; }
+                    unsigned char* a = smem + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_2d(a, &map_x, t * BK, m0, &full[s]);
+                    tma_load_2d(a + A_BYTES, &map_c, t * BK, j * BN, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            int it = 0;
+            for (int j = 0; j < ntiles && !s_fail; ++j) {
+                const int acc = j & 1;
+                if (j >= 2 && !mbar_wait(&acc_empty[acc], ((j >> 1) - 1) & 1)) { s_fail = 4; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t td = tmem + (uint32_t)(acc * BN);
+                bool ok = true;
+                for (int t = 0; t < kt; ++t, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1)) { s_fail = 2; ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
+                    const uint64_t ad = sw128_kmajor_desc(a), bd = sw128_kmajor_desc(a + A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk)
+                        mma_tf32(td, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), (t > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[acc]);
+            }
+        }
+    } else {
+        // Epilogue: thread (warp w < 4, lane l) owns row 32w + l.
+        const int r = warp * 32 + lane;
+        const int row = m0 + r;
+        const bool live = row < nx;
+        const float rn = live ? xn[row] : 0.0f;
+        const float xs = sqrtf(rn);
+        const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;
+        const float rr = (float)(dim / 8 + 8) * 1.1920929e-7f;
+        // e(col) <= E0 + 2.002 rr |dt| over every column (cmax = the largest ||c||^2 and
+        // ||c||), so dt > T = (U + E0)(1 + 4 rr) proves dt - e > U: most columns are
+        // dismissed on dt alone.  U >= 0 (an upper bound of an exact distance), so such
+        // a dt is positive.
+        const float c2max = cmax[0], csmax = cmax[1];
+        const float E0 = 1.0009765625f * (4.0f * a * xs * csmax + 4.768e-7f * (rn + c2max + 2.0f * xs * csmax));
+        const float tgrow = 1.0f + 4.0f * rr + 1e-5f;   // + slack for the fp32 rounding of this test
+        float U = FLT_MAX, T = FLT_MAX;
+        int cnt = 0;
+        bool overflow = false;
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        for (int j = 0; j < ntiles; ++j) {
+            const int acc = j & 1;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (j >> 1) & 1));
+            if (!got) { s_fail = 3; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int n0 = j * BN;
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                uint32_t v[32];
+                tmem_ld32(trow + (uint32_t)(acc * BN + ch * 32), v);
+                const int cb = n0 + ch * 32;
+                if (cb >= nc) continue;   // uniform: the last tile's padding columns
+                // Fast screen: one coalesced load of the chunk's column norms, broadcast
+                // by shuffle; a column passes when its screen value can reach T.
+                const int colL = cb + lane;
+                const float c2L = colL < nc ? __ldg(cn + colL) : FLT_MAX;
+                float dts[32];
+                uint32_t mask = 0;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const float c2 = __shfl_sync(0xffffffffu, c2L, jj);
+                    dts[jj] = (rn + c2) - 2.0f * __uint_as_float(v[jj]);
+                    mask |= (dts[jj] <= T ? 1u : 0u) << jj;
+                }
+                if (nc - cb < 32) mask &= (1u << (nc - cb)) - 1u;   // columns past nc never pass
+                if (!live) mask = 0;
+                // Slow path for the (few) passing columns: the exact bound and the list.
+                while (mask) {
+                    const int jj = __ffs(mask) - 1;
+                    mask &= mask - 1u;
+                    const int col = cb + jj;
+                    float dt = 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) dt = (u == jj) ? dts[u] : dt;
+                    const float c2 = __ldg(cn + col);
+                    const float xc = xs * __ldg(cs + col);
+                    const float e = 1.0009765625f *
+                                    (4.0f * a * xc + 4.768e-7f * (rn + c2 + 2.0f * xc) + 2.0f * rr * fabsf(dt));
+                    const float lb = dt - e;
+                    if (lb > U) continue;
+                    if (dt + e < U) {
+                        U = dt + e;
+                        T = (U + E0) * tgrow;
+                    }
+                    if (overflow) continue;
+                    if (cnt == ARG_CAP) {
+                        int w = 0;
+                        for (int i = 0; i < ARG_CAP; ++i) {
+                            const float l = cand_lb[i * BM + r];
+                            if (l <= U) {
+                                cand_lb[w * BM + r] = l;
+                                cand_col[w * BM + r] = cand_col[i * BM + r];
+                                ++w;
+                            }
+                        }
+                        cnt = w;
+                        if (cnt == ARG_CAP) { overflow = true; continue; }
+                    }
+                    cand_lb[cnt * BM + r] = lb;
+                    cand_col[cnt * BM + r] = (uint32_t)col;
+                    ++cnt;
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        // Exact refine, warp by warp: each of the warp's 32 rows in turn, four kept
+        // columns at a time (eight lanes each, the reference's lane order).
+        __syncwarp();
+        const int ccnt = overflow ? 0 : cnt;
+        const bool failed = __shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&s_fail), 0) != 0;
+        const uint32_t kc = (live && keep) ? keep[row] : 0xffffffffu;
+        for (int q = 0; q < 32; ++q) {
+            const int rq = warp * 32 + q;
+            const int rowq = m0 + rq;
+            const int nq_c = __shfl_sync(0xffffffffu, ccnt, q);
+            const float Uq = __shfl_sync(0xffffffffu, U, q);
+            const bool ovq = __shfl_sync(0xffffffffu, (int)overflow, q) != 0;
+            const uint32_t kcq = __shfl_sync(0xffffffffu, kc, q);
+            if (rowq >= nx || failed) continue;
+            if (ovq) {
+                if (lane == 0) over[atomicAdd(n_over, 1u)] = (uint32_t)rowq;
+                continue;
+            }
+            unsigned long long best = ~0ull;
+            float keep_v = FLT_MAX;
+            const float* xr = x + (long long)rowq * dim;
+            for (int b = 0; b < nq_c; b += 4) {
+                const int ci = b + (lane >> 3);
+                const bool act = ci < nq_c && cand_lb[ci * BM + rq] <= Uq;
+                const uint32_t col = act ? cand_col[ci * BM + rq] : 0u;
+                const float vv = warp_l2_group(xr, cent + (long long)col * dim, dim, act);
+                if (act && (lane & 7) == 0) {
+                    const unsigned long long key = ((unsigned long long)float_key(vv) << 32) | col;
+                    best = key < best ? key : best;
+                    if (col == kcq) keep_v = vv;
+                }
+            }
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
+                best = y < best ? y : best;
+                keep_v = fminf(keep_v, __shfl_xor_sync(0xffffffffu, keep_v, o));
+            }
+            if (lane == 0) {
+                uint32_t id = (uint32_t)(best & 0xffffffffull);
+                const float v = key_float((uint32_t)(best >> 32));
+                if (keep && kcq != id && keep_v == v) id = kcq;
+                out_idx[rowq] = id;
+                out_val[rowq] = v;
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && s_fail) atomicExch(err, s_fail);
+    if (warp == 5)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ARG_TMEM_COLS) : "memory");
+}
+
+namespace {
+// cmax[0] = max ||c||^2, cmax[1] = max ||c|| (non-negative floats order as their bits);
+// cmax must be zeroed first.
+__global__ void col_max_kernel(const float* __restrict__ cn, const float* __restrict__ cs, int nc,
+                               float* __restrict__ cmax) {
+    float a = 0.0f, b = 0.0f;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nc; i += gridDim.x * blockDim.x) {
+        a = fmaxf(a, cn[i]);
+        b = fmaxf(b, cs[i]);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(reinterpret_cast<unsigned int*>(cmax), __float_as_uint(a));
+        atomicMax(reinterpret_cast<unsigned int*>(cmax + 1), __float_as_uint(b));
+    }
+}
+
+__global__ void scatter_top1_kernel(const uint32_t* __restrict__ rows, int n, const uint32_t* __restrict__ idx,
+                                    const float* __restrict__ val, uint32_t* __restrict__ out_idx,
+                                    float* __restrict__ out_val) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        out_idx[rows[i]] = idx[i];
+        out_val[rows[i]] = val[i];
+    }
+}
+}  // namespace
+
+bool tc_argmin_supported(int dim) { return tc_screen_supported(dim); }
+
+void launch_col_max(const float* cn, const float* cs, int nc, float* cmax, cudaStream_t st) {
+    check(cudaMemsetAsync(cmax, 0, 2 * sizeof(float), st), "memset");
+    if (nc <= 0) return;
+    col_max_kernel<<<std::min(ceil_div(nc, 256), 148), 256, 0, st>>>(cn, cs, nc, cmax);
+    check(cudaGetLastError(), "col_max_kernel");
+}
+
+void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
+                      const float* cs, const float* cmax, const uint32_t* keep, uint32_t* out_idx, float* out_val,
+                      uint32_t* over, uint32_t* n_over, int* err, cudaStream_t st) {
+    if (nx <= 0 || nc <= 0) return;
+    if (!tc_screen_supported(dim)) throw CudaError("tc_argmin: dim must be a multiple of 4 and >= 32");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
+        throw CudaError("tc_argmin: operands must be 16-byte aligned");
+    if (nx > 0x7fffffffLL) throw CudaError("tc_argmin: too many rows");
+    const CUtensorMap mx = make_map(x, nx, dim, BM);
+    const CUtensorMap mc = make_map(c, nc, dim, BN);
+    check(cudaFuncSetAttribute(tc_argmin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ARG_SMEM),
+          "cudaFuncSetAttribute(tc_argmin)");
+    tc_argmin_kernel<<<(unsigned)ceil_div(nx, BM), ARG_THREADS, ARG_SMEM, st>>>(
+        mx, mc, (int)nx, nc, dim, x, c, xn, cn, cs, cmax, keep, out_idx, out_val, over, n_over, err);
+    check(cudaGetLastError(), "tc_argmin_kernel");
+}
+
+void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const float* val, uint32_t* out_idx,
+                         float* out_val, cudaStream_t st) {
+    if (n <= 0) return;
+    scatter_top1_kernel<<<std::min(ceil_div(n, 256), 148 * 8), 256, 0, st>>>(rows, n, idx, val, out_idx, out_val);
+    check(cudaGetLastError(), "scatter_top1_kernel");
 }
 
 __global__ void sqrt_kernel(const float* __restrict__ in, long long n, float* __restrict__ out) {

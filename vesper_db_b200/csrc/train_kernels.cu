@@ -347,6 +347,19 @@ void launch_gather_rows(const float* x, int dim, const uint32_t* idx, long long 
     VGPU_LAUNCH("gather_rows_kernel");
 }
 
+__global__ void gather_u32_kernel(const uint32_t* __restrict__ src, const uint32_t* __restrict__ idx, long long n,
+                                  uint32_t* __restrict__ out) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = src[idx[i]];
+}
+
+void launch_gather_u32(const uint32_t* src, const uint32_t* idx, long long n, uint32_t* out, cudaStream_t st) {
+    if (n <= 0) return;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 32);
+    gather_u32_kernel<<<blocks, 256, 0, st>>>(src, idx, n, out);
+    VGPU_LAUNCH("gather_u32_kernel");
+}
+
 __global__ void d2f_kernel(const double* __restrict__ in, long long n, float* __restrict__ out) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
