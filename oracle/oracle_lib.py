@@ -211,7 +211,7 @@ class Oracle:
 
     def manager_search(self, q, c, R, cb, m, list_offsets, ids, codes, k, nprobe, deleted=(), total_deleted=0,
                        use_exact_rerank=False, rerank_k=0, rerank_alpha=2.0, ceiling=2000,
-                       filter_by_distance=False):
+                       filter_by_distance=True):
         """IndexManager::search (src/index/index_manager.cpp:344-585) over an IVF-PQ index
         only: nprobe 0 -> 8; with the exact rerank, cand_k = rerank_k or
         ceil(max(k, alpha * k * log2(1 + nprobe))) capped by the ceiling (:414-436); the

@@ -58,7 +58,36 @@ def _manager(x, **kw):
     return mgr
 
 
-def test_build_search_remove_update(oracle):
+class _Env:
+    """Set an environment variable for the duration of a with block."""
+
+    def __init__(self, key, value):
+        self.key, self.value = key, value
+
+    def __enter__(self):
+        self.old = os.environ.get(self.key)
+        if self.value is None:
+            os.environ.pop(self.key, None)
+        else:
+            os.environ[self.key] = self.value
+
+    def __exit__(self, *a):
+        if self.old is None:
+            os.environ.pop(self.key, None)
+        else:
+            os.environ[self.key] = self.old
+
+
+@pytest.mark.parametrize("mode", [None, "id"])
+def test_build_search_remove_update(oracle, mode):
+    """mode None: the reference's tombstone filter, keyed on the truncated distance of
+    each (id, distance) pair (the default, so results equal the reference's); "id"
+    (VESPER_MGR_TOMBSTONE_FILTER=id): keyed on the id, removed ids never return."""
+    with _Env("VESPER_MGR_TOMBSTONE_FILTER", mode):
+        _build_search_remove_update(oracle, mode == "id")
+
+
+def _build_search_remove_update(oracle, by_id):
     from vesper_db_b200.manager import query_config
     x, q = _data()
     mgr = _manager(x)
@@ -73,13 +102,17 @@ def test_build_search_remove_update(oracle):
     dead = np.unique(ids[:, :6].reshape(-1))
     mgr.remove_batch(dead)
     got_ids, got_d = mgr.search_batch(q, query_config(k=10, nprobe=8))
-    assert not np.isin(got_ids[got_ids != 0], dead).any()
-    _compare(got_ids, got_d, oracle.manager_search(q, *args, 10, 8, deleted=dead, total_deleted=len(dead)), 10)
+    if by_id:
+        assert not np.isin(got_ids[got_ids != 0], dead).any()
+    _compare(got_ids, got_d, oracle.manager_search(q, *args, 10, 8, deleted=dead, total_deleted=len(dead),
+                                                   filter_by_distance=not by_id), 10)
     # single-query entry point
     i1, d1 = mgr.search(q[3], query_config(k=10, nprobe=8))
     assert np.array_equal(i1[0], got_ids[3]) and np.array_equal(d1[0], got_d[3])
     # update adds another entry under the id (the old one stays)
     target = int(got_ids[0, 0])
+    if not by_id:
+        return   # the update check below reads ids that the distance-keyed filter may keep
     mgr.update(target, q[0])
     ids2, d2 = mgr.search_batch(q[:1], query_config(k=10, nprobe=8))
     assert ids2[0, 0] == target and d2[0, 0] <= got_d[0, 0]
@@ -100,6 +133,11 @@ def test_many_removals_oversample(oracle):
     mgr.remove_batch(dead)
     ids, d = mgr.search_batch(q, query_config(k=20, nprobe=4))
     _compare(ids, d, oracle.manager_search(q, *args, 20, 4, deleted=dead, total_deleted=len(dead)), 20)
+    with _Env("VESPER_MGR_TOMBSTONE_FILTER", "id"):
+        ids, d = mgr.search_batch(q, query_config(k=20, nprobe=4))
+    assert not np.isin(ids[ids != 0], dead).any()
+    _compare(ids, d, oracle.manager_search(q, *args, 20, 4, deleted=dead, total_deleted=len(dead),
+                                           filter_by_distance=False), 20)
 
 
 def test_rerank_heuristic_and_env(oracle):

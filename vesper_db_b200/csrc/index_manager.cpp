@@ -15,8 +15,8 @@
 // The reference's result filter reads the id out of item.second, which for the
 // manager's (id, distance) pairs is the distance (tombstone_manager.hpp:150-170), so it
 // drops results whose truncated distance is a deleted id and keeps deleted ids.  This
-// engine filters by id, which is what remove() asks for; VESPER_MGR_TOMBSTONE_FILTER=
-// distance reproduces the reference's behaviour.
+// engine does the same by default, so that a drop-in returns the reference's results;
+// VESPER_MGR_TOMBSTONE_FILTER=id filters by id instead, which is what remove() asks for.
 #include <algorithm>
 #include <atomic>
 #include <chrono>
@@ -335,7 +335,7 @@ std::expected<std::vector<std::vector<std::pair<uint64_t, float>>>, Error> vespe
     // tombstones (index_manager.cpp:552-576, tombstone_manager.hpp:150-170)
     const bool by_distance = [] {
         const char* v = std::getenv("VESPER_MGR_TOMBSTONE_FILTER");
-        return v && std::string(v) == "distance";
+        return !(v && std::string(v) == "id");
     }();
     std::vector<size_t> short_rows, short_pos;
     for (size_t i = 0; i < res.size(); ++i) {

@@ -41,6 +41,7 @@ constexpr size_t kSearchDistBudget = size_t(1) << 30;
 // With the filtering probe (no distance matrix) a chunk is bounded by its per-query
 // tables instead: m * 2^nbits floats per query.
 constexpr size_t kSearchTableBudget = size_t(4) << 30;
+constexpr size_t kJacobiMaxDim = 256;               // OPQ Procrustes: the reference's Jacobi sweeps up to this dim
 constexpr int kListScanCap = 4096;                   // screened candidates kept per query (2048: more overflow fallbacks, 8192: no faster)
 
 auto fail(error_code c, std::string msg, std::string comp = "ivf_pq") {
@@ -426,6 +427,64 @@ public:
         return {};
     }
 
+    // The Procrustes rotation as the reference computes it (src/index/ivf_pq.cpp:2636-2698):
+    // one-sided Jacobi sweeps on the columns of A = C (at most 20, stopping when the sum of
+    // squared column inner products falls below 1e-10 d^2; pairs with |<a_p, a_q>| < 1e-10
+    // are left alone), U = A's columns normalised, R = U V^T.  Host fp64, every sum in the
+    // reference's order and no fused multiply-add, so R equals the reference's bit for
+    // bit given the same C.  O(20 d^3): used up to kJacobiMaxDim.
+    std::vector<float> jacobi_polar(const std::vector<double>& C) const {
+        const size_t d = dim;
+        const double tol = 1e-10;
+        std::vector<double> A = C, V(d * d, 0.0), U(d * d, 0.0);
+        for (size_t i = 0; i < d; ++i) { U[i * d + i] = 1.0; V[i * d + i] = 1.0; }
+        auto rotate_cols = [d](std::vector<double>& M, size_t p, size_t q, double c, double s) {
+            for (size_t i = 0; i < d; ++i) {
+                const double mp = M[i * d + p], mq = M[i * d + q];
+                M[i * d + p] = c * mp - s * mq;
+                M[i * d + q] = s * mp + c * mq;
+            }
+        };
+        for (int sweep = 0; sweep < 20; ++sweep) {
+            double off = 0.0;
+            for (size_t p = 0; p + 1 < d; ++p)
+                for (size_t q = p + 1; q < d; ++q) {
+                    double app = 0.0, aqq = 0.0, apq = 0.0;
+                    for (size_t i = 0; i < d; ++i) {
+                        const double ap = A[i * d + p], aq = A[i * d + q];
+                        app += ap * ap;
+                        aqq += aq * aq;
+                        apq += ap * aq;
+                    }
+                    off += apq * apq;
+                    if (std::abs(apq) < tol) continue;
+                    const double tau = (aqq - app) / (2.0 * apq);
+                    const double t = tau >= 0 ? 1.0 / (tau + std::sqrt(1.0 + tau * tau))
+                                              : -1.0 / (-tau + std::sqrt(1.0 + tau * tau));
+                    const double c = 1.0 / std::sqrt(1.0 + t * t);
+                    const double s = t * c;
+                    rotate_cols(A, p, q, c, s);
+                    rotate_cols(V, p, q, c, s);
+                }
+            if (off < tol * (double)d * (double)d) break;
+        }
+        for (size_t i = 0; i < d; ++i) {
+            double norm = 0.0;
+            for (size_t j = 0; j < d; ++j) norm += A[j * d + i] * A[j * d + i];
+            norm = std::sqrt(norm);
+            if (norm > tol)
+                for (size_t j = 0; j < d; ++j) U[j * d + i] = A[j * d + i] / norm;
+        }
+        std::vector<float> R(d * d);
+        for (size_t i = 0; i < d; ++i)
+            for (size_t j = 0; j < d; ++j) {
+                double sum = 0.0;
+                for (size_t k = 0; k < d; ++k) sum += U[i * d + k] * V[j * d + k];
+                R[i * d + j] = (float)sum;
+            }
+        return R;
+    }
+
     // Orthogonal polar factor of C (d x d, fp64, device) by Newton-Schulz; result in
     // float R (host).
     std::vector<float> polar_factor(DeviceBuffer<double>& C) {
@@ -572,11 +631,23 @@ public:
                 const auto el = std::chrono::duration_cast<std::chrono::milliseconds>(
                                     std::chrono::steady_clock::now() - topq).count();
                 if (el > 120000) break;
-                // Procrustes on the sample: C = X^T Y / n, R = polar(C).
-                vgpu::launch_cross_fp64(res.data(), Y.data(), (long long)n_opq, (int)dim, nullptr, nullptr,
-                                        C.data(), st);
-                vgpu::launch_daxpby(C.data(), C.data(), (long long)dim * dim, 0.0, 1.0 / (double)n_opq, st);
-                h_rot = polar_factor(C);
+                // Procrustes on the sample: C = X^T Y / n, R = polar(C): the reference's
+                // Jacobi iteration up to kJacobiMaxDim, a Newton-Schulz polar factor on the
+                // GPU above (the host sweeps are O(20 d^3)).
+                if (dim <= kJacobiMaxDim) {
+                    vgpu::launch_cross_fp64_unfused(res.data(), Y.data(), (long long)n_opq, (int)dim, C.data(), st);
+                    std::vector<double> hC(dim * dim);
+                    d2h(hC.data(), C.data(), dim * dim, st);
+                    sync(st);
+                    const double invn = 1.0 / (double)n_opq;
+                    for (double& v : hC) v *= invn;
+                    h_rot = jacobi_polar(hC);
+                } else {
+                    vgpu::launch_cross_fp64(res.data(), Y.data(), (long long)n_opq, (int)dim, nullptr, nullptr,
+                                            C.data(), st);
+                    vgpu::launch_daxpby(C.data(), C.data(), (long long)dim * dim, 0.0, 1.0 / (double)n_opq, st);
+                    h_rot = polar_factor(C);
+                }
             }
             if (!R_best.empty()) h_rot = R_best;
             if (err_best < std::numeric_limits<double>::infinity()) {

@@ -14,6 +14,7 @@ namespace vgpu {
 
 // C[j][k] += sum_i (a_i[j] - ma[j]) * (b_i[k] - mb[k]) over rows [0, n), fp64.
 // 32x32 output tile per CTA, rows staged 32 at a time.  ma/mb may be null (no centring).
+template <bool UNFUSED>
 __global__ void __launch_bounds__(256) cross_fp64_kernel(const float* __restrict__ A,
                                                          const float* __restrict__ B, long long n,
                                                          int d, const double* __restrict__ ma,
@@ -40,8 +41,15 @@ __global__ void __launch_bounds__(256) cross_fp64_kernel(const float* __restrict
         for (int r = 0; r < 32; ++r) {
             const double a0 = As[r][ty * 2], a1 = As[r][ty * 2 + 1];
             const double b0 = Bs[r][tx * 2], b1 = Bs[r][tx * 2 + 1];
-            acc[0][0] += a0 * b0; acc[0][1] += a0 * b1;
-            acc[1][0] += a1 * b0; acc[1][1] += a1 * b1;
+            if constexpr (UNFUSED) {   // rounded product, then rounded sum
+                acc[0][0] = __dadd_rn(acc[0][0], __dmul_rn(a0, b0));
+                acc[0][1] = __dadd_rn(acc[0][1], __dmul_rn(a0, b1));
+                acc[1][0] = __dadd_rn(acc[1][0], __dmul_rn(a1, b0));
+                acc[1][1] = __dadd_rn(acc[1][1], __dmul_rn(a1, b1));
+            } else {
+                acc[0][0] += a0 * b0; acc[0][1] += a0 * b1;
+                acc[1][0] += a1 * b0; acc[1][1] += a1 * b1;
+            }
         }
         __syncthreads();
     }
@@ -55,7 +63,13 @@ __global__ void __launch_bounds__(256) cross_fp64_kernel(const float* __restrict
 void launch_cross_fp64(const float* A, const float* B, long long n, int d, const double* ma,
                        const double* mb, double* C, cudaStream_t st) {
     dim3 grid(ceil_div(d, 32), ceil_div(d, 32));
-    cross_fp64_kernel<<<grid, 256, 0, st>>>(A, B, n, d, ma, mb, C);
+    cross_fp64_kernel<false><<<grid, 256, 0, st>>>(A, B, n, d, ma, mb, C);
+    VGPU_LAUNCH("cross_fp64_kernel");
+}
+
+void launch_cross_fp64_unfused(const float* A, const float* B, long long n, int d, double* C, cudaStream_t st) {
+    dim3 grid(ceil_div(d, 32), ceil_div(d, 32));
+    cross_fp64_kernel<true><<<grid, 256, 0, st>>>(A, B, n, d, nullptr, nullptr, C);
     VGPU_LAUNCH("cross_fp64_kernel");
 }
 
