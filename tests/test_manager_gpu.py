@@ -162,22 +162,33 @@ def test_rerank_heuristic_and_env(oracle):
     _compare(ids, d, oracle.manager_search(q, *args, 10, 8, use_exact_rerank=True, rerank_k=30), 10)
 
 
-def test_save_load_budget_and_refusals():
+def test_save_load_budget_and_refusals(oracle):
     from vesper_db_b200 import VesperError
     from vesper_db_b200 import _native as N
     from vesper_db_b200.manager import IndexManager, query_config
     x, q = _data(seed=9)
     mgr = _manager(x)
-    mgr.remove_batch(np.array([1, 2, 3, 70000], np.uint64))
-    a = mgr.search_batch(q, query_config(k=10, nprobe=8))
+    dead = np.array([1, 2, 3, 70000], np.uint64)
+    mgr.remove_batch(dead)
+    with _Env("VESPER_MGR_TOMBSTONE_FILTER", "id"):
+        a = mgr.search_batch(q, query_config(k=10, nprobe=8))
     with tempfile.TemporaryDirectory() as td:
         mgr.save(td)
         assert sorted(os.listdir(td)) == ["index_manager.manifest", "ivf_pq", "tombstones.bin"]
         m2 = IndexManager(7)
         m2.load(td)
         m2.set_search_mode(1)
-        b = m2.search_batch(q, query_config(k=10, nprobe=8))
+        # keyed on ids, the reloaded tombstones give the same results
+        with _Env("VESPER_MGR_TOMBSTONE_FILTER", "id"):
+            b = m2.search_batch(q, query_config(k=10, nprobe=8))
         assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+        # the reference's filter after a load: the tombstones are back but the deletion
+        # count restarts at zero (a loaded TombstoneManager's statistics start at zero),
+        # so no oversampled re-search runs
+        f = _model(m2)
+        args = (f["centroids"], f["rotation"], f["codebooks"], f["m"], f["list_offsets"], f["ids"], f["codes"])
+        got_ids, got_d = m2.search_batch(q, query_config(k=10, nprobe=8))
+        _compare(got_ids, got_d, oracle.manager_search(q, *args, 10, 8, deleted=dead, total_deleted=0), 10)
         with pytest.raises(VesperError, match="already marked"):
             m2.remove(2)
     # preferring an index this engine does not hold gives empty (padded) results

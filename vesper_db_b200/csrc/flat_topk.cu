@@ -20,6 +20,8 @@
 // which handles any number of columns.
 #include <algorithm>
 #include <cfloat>
+#include <cstdlib>
+#include <string>
 #include <vector>
 
 #include "kernels.cuh"
@@ -222,6 +224,16 @@ __global__ void pad_topk_kernel(long long nq, int k, int ke, bool ip, uint32_t* 
 }
 
 namespace {
+// The filter screen on the persistent pipeline (tc_filter_kernel) unless
+// VGPU_FILTER=tile asks for one CTA per 128 x 256 tile (tc_screen_kernel's filter modes).
+bool persistent_filter() {
+    static const bool on = [] {
+        const char* v = std::getenv("VGPU_FILTER");
+        return !(v && std::string(v) == "tile");
+    }();
+    return on;
+}
+
 int grid_for(long long n, int nt) { return (int)std::max<long long>(1, std::min<long long>((n + nt - 1) / nt, 148LL * 16)); }
 
 // Exact top-k of x rows against nc columns (row j of c at j * c_ld) through a full
@@ -357,9 +369,19 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
         const long long step = feed ? std::min(FILTER_COLS, feed->chunk) : FILTER_COLS;
         for (long long c0 = 0; c0 < v.n; c0 += step, ++w.launches) {
             if (feed) feed->ready(std::min(v.n, c0 + step), st, w.launches);
-            launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, std::min(step, v.n - c0), v.ld, dim,
-                             xn + q0, v.cn + c0, v.cs + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(),
-                             w.cand_cnt.data() + q0, cap, w.err.data(), st);
+            const long long nc = std::min(step, v.n - c0);
+            if (persistent_filter()) {
+                w.cmax.reserve(2);
+                launch_col_max(v.cn + c0, v.cs + c0, (int)nc, w.cmax.data(), st);
+                ++w.launches;
+                launch_tc_filter_persistent(ip, q + q0 * dim, n, v.base + c0 * v.ld, nc, v.ld, dim, xn + q0,
+                                            v.cn + c0, v.cs + c0, w.cmax.data(), w.tau.data() + q0, (uint32_t)c0,
+                                            w.cand.data(), w.cand_cnt.data() + q0, cap, w.err.data(), st);
+            } else {
+                launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, nc, v.ld, dim, xn + q0, v.cn + c0,
+                                 v.cs + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(), w.cand_cnt.data() + q0,
+                                 cap, w.err.data(), st);
+            }
         }
         if (stats) check(cudaEventRecord(w.ev[4], st), "event");
         ++w.launches;

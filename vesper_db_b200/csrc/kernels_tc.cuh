@@ -44,7 +44,7 @@ struct FlatWork {
         DeviceBuffer<float> cn, cs, s_val;
         DeviceBuffer<uint32_t> s_idx;
     } level[kLevels];
-    DeviceBuffer<float> xn, cn, csq, tau, dt, oq, oxn, o_val;
+    DeviceBuffer<float> xn, cn, csq, tau, dt, oq, oxn, o_val, cmax;
     DeviceBuffer<uint32_t> cand_cnt, over, o_idx, o_rows;
     DeviceBuffer<uint2> cand;
     DeviceBuffer<int> err;
@@ -95,6 +95,13 @@ void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int 
                       uint32_t* over, uint32_t* n_over, int* err, cudaStream_t st);
 void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const float* val, uint32_t* out_idx,
                          float* out_val, cudaStream_t st);
+// launch_tc_filter's keep rule on the persistent pipeline of tc_argmin_kernel (each CTA
+// walks a share of the column tiles for its 128 rows); cmax from launch_col_max over
+// the same columns' cn / cs.  Same outputs and semantics as launch_tc_filter.
+void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const float* c, long long nc,
+                                 long long c_stride, int dim, const float* xn, const float* cn, const float* cs,
+                                 const float* cmax, const float* tau, uint32_t col_off, uint2* cand,
+                                 uint32_t* cand_cnt, int cap, int* err, cudaStream_t st);
 // out[i] = ||x_i||^2 (fp64 accumulation); row i at x + i * ld (ld = dim by default).
 void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st, long long ld = 0);
 // Per row: exact k nearest centroids (reference-order distances, ties to the lowest

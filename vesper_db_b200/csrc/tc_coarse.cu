@@ -386,6 +386,51 @@ constexpr int ARG_CAP = 16;
 constexpr int ARG_THREADS = 192;
 constexpr int ARG_SMEM = STAGES * STAGE_BYTES + 1024 + 256 + ARG_CAP * BM * 8;
 constexpr uint32_t ARG_TMEM_COLS = 512;
+
+// The two pipeline roles of the persistent screens (tc_argmin_kernel, tc_filter_kernel),
+// each run by one lane.  Producer: the 128-row block at m0 with column tiles
+// jt0 .. jt0 + ntiles - 1, K-slices in order, through the STAGES-deep ring.  MMA: tile t
+// into TMEM accumulator t & 1 (256 columns each), after the epilogue has released the
+// accumulator's previous tile.  A failed (bounded) wait sets *fail and ends the role.
+__device__ __forceinline__ void screen_producer(unsigned char* smem, uint64_t* full, uint64_t* empty,
+                                                const CUtensorMap* map_x, const CUtensorMap* map_c, int m0,
+                                                int jt0, int ntiles, int kt, volatile int* fail) {
+    int it = 0;
+    for (int j = 0; j < ntiles && !*fail; ++j) {
+        for (int t = 0; t < kt; ++t, ++it) {
+            const int s = it % STAGES;
+            if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { *fail = 1; return; }
+            unsigned char* a = smem + s * STAGE_BYTES;
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(a, map_x, t * BK, m0, &full[s]);
+            tma_load_2d(a + A_BYTES, map_c, t * BK, (jt0 + j) * BN, &full[s]);
+        }
+    }
+}
+
+__device__ __forceinline__ void screen_mma(unsigned char* smem, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
+                                           uint64_t* acc_empty, uint32_t tmem, int ntiles, int kt,
+                                           volatile int* fail) {
+    int it = 0;
+    for (int j = 0; j < ntiles && !*fail; ++j) {
+        const int acc = j & 1;
+        if (j >= 2 && !mbar_wait(&acc_empty[acc], ((j >> 1) - 1) & 1)) { *fail = 4; return; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t td = tmem + (uint32_t)(acc * BN);
+        for (int t = 0; t < kt; ++t, ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&full[s], (it / STAGES) & 1)) { *fail = 2; return; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
+            const uint64_t ad = sw128_kmajor_desc(a), bd = sw128_kmajor_desc(a + A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk)
+                mma_tf32(td, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), (t > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[acc]);
+    }
+}
 }  // namespace
 
 __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
@@ -430,44 +475,9 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 4) {
-        if (lane == 0) {
-            // TMA producer: the same row tile with every column tile, K-slices in order.
-            int it = 0;
-            for (int j = 0; j < ntiles && !s_fail; ++j) {
-                for (int t = 0; t < kt; ++t, ++it) {
-                    const int s = it % STAGES;
-                    if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { s_fail = 1; break; }
-                    unsigned char* a = smem + s * STAGE_BYTES;
-                    mbar_expect_tx(&full[s], STAGE_BYTES);
-                    tma_load_2d(a, &map_x, t * BK, m0, &full[s]);
-                    tma_load_2d(a + A_BYTES, &map_c, t * BK, j * BN, &full[s]);
-                }
-            }
-        }
+        if (lane == 0) screen_producer(smem, full, empty, &map_x, &map_c, m0, 0, ntiles, kt, (volatile int*)&s_fail);
     } else if (warp == 5) {
-        if (lane == 0) {
-            int it = 0;
-            for (int j = 0; j < ntiles && !s_fail; ++j) {
-                const int acc = j & 1;
-                if (j >= 2 && !mbar_wait(&acc_empty[acc], ((j >> 1) - 1) & 1)) { s_fail = 4; break; }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t td = tmem + (uint32_t)(acc * BN);
-                bool ok = true;
-                for (int t = 0; t < kt; ++t, ++it) {
-                    const int s = it % STAGES;
-                    if (!mbar_wait(&full[s], (it / STAGES) & 1)) { s_fail = 2; ok = false; break; }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
-                    const uint64_t ad = sw128_kmajor_desc(a), bd = sw128_kmajor_desc(a + A_BYTES);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk)
-                        mma_tf32(td, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), (t > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(&empty[s]);
-                }
-                if (!ok) break;
-                mma_commit(&acc_full[acc]);
-            }
-        }
+        if (lane == 0) screen_mma(smem, full, empty, acc_full, acc_empty, tmem, ntiles, kt, (volatile int*)&s_fail);
     } else {
         // Epilogue: thread (warp w < 4, lane l) owns row 32w + l.
         const int r = warp * 32 + lane;
@@ -607,6 +617,167 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ARG_TMEM_COLS) : "memory");
 }
 
+// ---------------------------------------------------------------------------------
+// Persistent filter screen (flat top-k pass 2, the coarse probe's filter): the
+// pipeline of tc_argmin_kernel over the column tiles [jt0, jt0 + tiles) of blockIdx.y's
+// share, and the filter modes' keep rule: column c of row r is kept when its proven
+// lower bound can reach tau[r] (L2: Dt - eps <= tau; IP: -2 S' - eps <= tau, i.e.
+// S' >= -tau / 2 - w ||c||).  Kept columns are appended to the row's list (col +
+// col_off, screen value), one atomic reservation per row per tile; a row's count may
+// exceed cap (the refine treats that as an overflow).  Most columns are dismissed on a
+// column-independent bound first (L2: Dt > (tau + E0)(1 + 4 rr + 1e-5); IP: S' below
+// the threshold at the largest ||c||), the exact test runs only for the rest.
+// ---------------------------------------------------------------------------------
+template <bool IP>
+__global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
+    const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_c, int nx, int nc, int dim,
+    int tiles_per_cta, const float* __restrict__ xn, const float* __restrict__ cn, const float* __restrict__ cs,
+    const float* __restrict__ cmax, const float* __restrict__ tau, uint32_t col_off, uint2* __restrict__ cand,
+    uint32_t* __restrict__ cand_cnt, int cap, int* __restrict__ err) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    __shared__ int s_fail;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM;
+    const int kt = (dim + BK - 1) / BK;
+    const int all_tiles = (nc + BN - 1) / BN;
+    const int jt0 = blockIdx.y * tiles_per_cta;
+    const int ntiles = max(0, min(tiles_per_cta, all_tiles - jt0));
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int s2 = 0; s2 < STAGES; ++s2) { mbar_init(&full[s2], 1); mbar_init(&empty[s2], 1); }
+        for (int a2 = 0; a2 < 2; ++a2) { mbar_init(&acc_full[a2], 1); mbar_init(&acc_empty[a2], 4); }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(ARG_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) screen_producer(smem, full, empty, &map_x, &map_c, m0, jt0, ntiles, kt, (volatile int*)&s_fail);
+    } else if (warp == 5) {
+        if (lane == 0) screen_mma(smem, full, empty, acc_full, acc_empty, tmem, ntiles, kt, (volatile int*)&s_fail);
+    } else {
+        const int r = warp * 32 + lane;
+        const int row = m0 + r;
+        const bool live = row < nx;
+        const float rn = live ? xn[row] : 0.0f;
+        const float xs = sqrtf(rn);
+        const float t = live ? tau[row] : -FLT_MAX;
+        const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;
+        const float rr = (float)(dim / 8 + 8) * 1.1920929e-7f;
+        const float c2max = cmax[0], csmax = cmax[1];
+        // L2 fast bound (as in tc_argmin_kernel, with the fixed tau in place of U)
+        const float E0 = 1.0009765625f * (4.0f * a * xs * csmax + 4.768e-7f * (rn + c2max + 2.0f * xs * csmax));
+        const float T = (t + E0) * (1.0f + 4.0f * rr + 1e-5f);
+        // IP: keep iff S >= t_ip - w cs; below S_lo no column can be kept (w cs <= w csmax)
+        const float w_ip = 2.0f * (a + rr + 2.4e-7f) * xs * 1.0009765625f;
+        const float t_ip = -0.5f * t;
+        const float S_lo = fmaf(-w_ip, csmax, t_ip);
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        for (int j = 0; j < ntiles; ++j) {
+            const int acc = j & 1;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (j >> 1) & 1));
+            if (!got) { s_fail = 3; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int n0 = (jt0 + j) * BN;
+            uint32_t keepm[BN / 32];
+            uint32_t total = 0;
+#pragma unroll
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                uint32_t v[32];
+                tmem_ld32(trow + (uint32_t)(acc * BN + ch * 32), v);
+                keepm[ch] = 0u;
+                const int cb = n0 + ch * 32;
+                if (cb >= nc) continue;
+                const int colL = cb + lane;
+                uint32_t mask = 0;
+                if constexpr (IP) {
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) mask |= (__uint_as_float(v[jj]) >= S_lo ? 1u : 0u) << jj;
+                } else {
+                    const float c2L = colL < nc ? __ldg(cn + colL) : FLT_MAX;
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {
+                        const float c2 = __shfl_sync(0xffffffffu, c2L, jj);
+                        const float dt = (rn + c2) - 2.0f * __uint_as_float(v[jj]);
+                        mask |= (dt <= T ? 1u : 0u) << jj;
+                    }
+                }
+                if (nc - cb < 32) mask &= (1u << (nc - cb)) - 1u;
+                if (!live) mask = 0;
+                uint32_t km = 0;
+                while (mask) {
+                    const int jj = __ffs(mask) - 1;
+                    mask &= mask - 1u;
+                    const int col = cb + jj;
+                    float S = 0.0f;
+#pragma unroll
+                    for (int u2 = 0; u2 < 32; ++u2) S = (u2 == jj) ? __uint_as_float(v[u2]) : S;
+                    bool kp;
+                    if constexpr (IP) {
+                        kp = S >= fmaf(-w_ip, __ldg(cs + col), t_ip);
+                    } else {
+                        const float c2 = __ldg(cn + col);
+                        const float xc = xs * __ldg(cs + col);
+                        const float dt = (rn + c2) - 2.0f * S;
+                        const float e = 4.0f * a * xc + 4.768e-7f * (rn + c2 + 2.0f * xc) + 2.0f * rr * fabsf(dt);
+                        kp = dt - 1.0009765625f * e <= t;
+                    }
+                    if (kp) km |= 1u << jj;
+                }
+                keepm[ch] = km;
+                total += __popc(km);
+            }
+            uint32_t slot = 0;
+            if (total) slot = atomicAdd(&cand_cnt[row], total);
+            uint2* dst = cand + (long long)row * cap;
+#pragma unroll
+            for (int ch = 0; ch < BN / 32; ++ch) {
+                if (!__any_sync(0xffffffffu, keepm[ch] != 0u)) continue;
+                uint32_t v[32];
+                tmem_ld32(trow + (uint32_t)(acc * BN + ch * 32), v);
+                uint32_t km = keepm[ch];
+                while (km) {
+                    const int jj = __ffs(km) - 1;
+                    km &= km - 1u;
+                    const int col = n0 + ch * 32 + jj;
+                    if (slot < (uint32_t)cap) {
+                        float S = 0.0f;
+#pragma unroll
+                        for (int u2 = 0; u2 < 32; ++u2) S = (u2 == jj) ? __uint_as_float(v[u2]) : S;
+                        const float val = IP ? -2.0f * S : (rn + __ldg(cn + col)) - 2.0f * S;
+                        dst[slot] = make_uint2((uint32_t)col + col_off, __float_as_uint(val));
+                    }
+                    ++slot;
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && s_fail) atomicExch(err, s_fail);
+    if (warp == 5)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ARG_TMEM_COLS) : "memory");
+}
+
 namespace {
 // cmax[0] = max ||c||^2, cmax[1] = max ||c|| (non-negative floats order as their bits);
 // cmax must be zeroed first.
@@ -661,6 +832,42 @@ void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int 
     tc_argmin_kernel<<<(unsigned)ceil_div(nx, BM), ARG_THREADS, ARG_SMEM, st>>>(
         mx, mc, (int)nx, nc, dim, x, c, xn, cn, cs, cmax, keep, out_idx, out_val, over, n_over, err);
     check(cudaGetLastError(), "tc_argmin_kernel");
+}
+
+void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const float* c, long long nc,
+                                 long long c_stride, int dim, const float* xn, const float* cn, const float* cs,
+                                 const float* cmax, const float* tau, uint32_t col_off, uint2* cand,
+                                 uint32_t* cand_cnt, int cap, int* err, cudaStream_t st) {
+    if (nx <= 0 || nc <= 0) return;
+    if (!tc_screen_supported(dim)) throw CudaError("tc_filter: dim must be a multiple of 4 and >= 32");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
+        throw CudaError("tc_filter: operands must be 16-byte aligned");
+    if (nc > 0x7fffffffLL || nx > 0x7fffffffLL) throw CudaError("tc_filter: too many rows or columns");
+    const CUtensorMap mx = make_map(x, nx, dim, BM);
+    const CUtensorMap mc = make_map(c, nc, dim, BN, c_stride);
+    const long long row_blocks = ceil_div(nx, BM);
+    const long long col_tiles = ceil_div(nc, BN);
+    // Column shares: enough CTAs for a few waves of the SMs, at least 8 tiles per CTA so
+    // that the pipeline's fill and drain stay small next to its steady state.
+    long long splits = std::max<long long>(1, (148LL * 4 + row_blocks - 1) / row_blocks);
+    splits = std::min(splits, std::max<long long>(1, col_tiles / 8));
+    splits = std::min<long long>(splits, 65535);
+    const int per = (int)((col_tiles + splits - 1) / splits);
+    splits = (col_tiles + per - 1) / per;
+    if (row_blocks > 0x7fffffffLL) throw CudaError("tc_filter: too many row blocks");
+    dim3 grid((unsigned)row_blocks, (unsigned)splits);
+    if (ip) {
+        check(cudaFuncSetAttribute(tc_filter_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ARG_SMEM),
+              "cudaFuncSetAttribute(tc_filter)");
+        tc_filter_kernel<true><<<grid, ARG_THREADS, ARG_SMEM, st>>>(mx, mc, (int)nx, (int)nc, dim, per, xn, cn, cs,
+                                                                   cmax, tau, col_off, cand, cand_cnt, cap, err);
+    } else {
+        check(cudaFuncSetAttribute(tc_filter_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ARG_SMEM),
+              "cudaFuncSetAttribute(tc_filter)");
+        tc_filter_kernel<false><<<grid, ARG_THREADS, ARG_SMEM, st>>>(mx, mc, (int)nx, (int)nc, dim, per, xn, cn, cs,
+                                                                    cmax, tau, col_off, cand, cand_cnt, cap, err);
+    }
+    check(cudaGetLastError(), "tc_filter_kernel");
 }
 
 void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const float* val, uint32_t* out_idx,
