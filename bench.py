@@ -73,7 +73,7 @@ SCAN_KERNELS = {1: "scan_exact_kernel", 2: "scan_fast2_kernel", 3: "scan_blocked
 COARSE_KERNELS = {1: "l2_dist_kernel (CUDA cores)", 2: "tc_screen_kernel (tcgen05 tf32) + screen_select_kernel",
                   3: "sampled threshold + tc_screen_kernel filter (tcgen05 tf32) + flat_refine_kernel"}
 METRIC = "QPS at matched recall@10 (IVF-PQ, 10k-query batch) at 1/2/4/8 B200 vs CPU ref"
-LIST_SCAN_BYTES_PER_PAIR = (662.9e6 + 8.7e6) / 6.65e9   # ncu, main-pass launch on the 4M-vector case
+LIST_SCAN_BYTES_PER_PAIR = (556.5e6 + 10.6e6) / 2.209e9   # ncu, main-pass launch on the 2M-vector case
 
 
 def workload_name():
@@ -98,13 +98,20 @@ def parse():
                          "100M x 128, nlist 65,536, m 32, 100k queries, nprobe 64, k 100")
     # Smaller cases of the same workload, for profiler captures (the defaults are the
     # benchmark's sizes; a line measured with either flag names its sizes in config).
-    ap.add_argument("--n-base", type=int, default=0, help="base vectors (multiple of the 125,000-row chunk)")
+    ap.add_argument("--n-base", type=int, default=0,
+                    help="base vectors (multiple of the generated chunk: 125,000 rows, c5 6,250,000); "
+                         "k-means: points")
     ap.add_argument("--nq", type=int, default=0, help="queries in the batch")
     ap.add_argument("--scan", default="auto", choices=["auto", "tc", "blocked"],
                     help="FAST scan kernel: the engine's choice, the tensor-core list scan or the blocked scan")
     args = ap.parse_args()
-    global N_BASE, NQ, WORKLOAD, FLAT_N, FLAT_NQ
-    if args.workload == "flat":
+    global N_BASE, NQ, WORKLOAD, FLAT_N, FLAT_NQ, KM_N, C5_N, C5_NQ
+    if args.workload == "kmeans":
+        KM_N = args.n_base or KM_N
+    elif args.workload == "c5":
+        C5_N = max(C5_CHUNK, args.n_base // C5_CHUNK * C5_CHUNK) if args.n_base else C5_N
+        C5_NQ = args.nq or C5_NQ
+    elif args.workload == "flat":
         FLAT_N = max(FLAT_CHUNK, args.n_base // FLAT_CHUNK * FLAT_CHUNK) if args.n_base else FLAT_N
         FLAT_NQ = args.nq or FLAT_NQ
     else:
@@ -143,17 +150,36 @@ class ClockSampler:
         self.path = tempfile.mktemp(suffix=".csv")
         self.proc = None
 
+    def _lines(self):
+        try:
+            return [ln for ln in open(self.path) if ln.strip()]
+        except OSError:
+            return []
+
     def __enter__(self):
+        self.skip = 0
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait (bounded) for its first line so that
+        # the sampling runs through the timed region, which starts after this returns
+        t_end = time.time() + 5.0
+        while time.time() < t_end and not self._lines():
+            time.sleep(0.02)
+        self.skip = len(self._lines())
         return self
 
     def __exit__(self, *a):
         if self.proc is not None:
+            # a region shorter than the sampling period: take the next sample, right
+            # after it (the clocks have not moved yet)
+            t_end = time.time() + 0.5
+            while time.time() < t_end and len(self._lines()) <= self.skip:
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -161,14 +187,14 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        """The samples taken from the region's start to just after its end."""
+        lines = self._lines()
+        region = lines[self.skip:] or lines[-1:]
         rows = []
-        try:
-            for line in open(self.path):
-                p = [x.strip() for x in line.split(",")]
-                if len(p) >= 9 and p[1].replace(".", "").isdigit():
-                    rows.append(p)
-        except OSError:
-            pass
+        for line in region:
+            p = [x.strip() for x in line.split(",")]
+            if len(p) >= 9 and p[1].replace(".", "").isdigit():
+                rows.append(p)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = sorted(float(r[1]) for r in rows)
@@ -270,7 +296,7 @@ def list_stats(index, n_queries, scanned_entries):
 
 # ------------------------------------------------------------------------------- flat top-k
 FLAT_N, FLAT_NQ, FLAT_K, FLAT_CHUNK = 1_000_000, 10_000, 100, 125_000
-FLAT_FILTER_BYTES_PER_ROW = (929.28e6 + 39.77e6) / 300_000   # ncu, filter launch over a 300k-row base
+FLAT_FILTER_BYTES_PER_ROW = (839.23e6 + 36.71e6) / 250_000   # ncu, filter launch over a 250k-row base
 FLAT_METRIC = "QPS, exact flat top-k (inner product, k=100), 10k-query batch"
 FLAT_WORKLOAD = ("Exact brute-force k-NN (flat index): N=1,000,000 x d=768 fp32 ~N(0,1) then L2-normalised, "
                  "10,000 queries from the same distribution, inner product, k=100")
@@ -448,11 +474,11 @@ def main_flat(args):
         "roofline": {"bound": "tensor", "kernel": "tc_screen_kernel filter mode (tcgen05 kind::tf32)",
                      "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
                      "peak_source": f"{peak_kind} bf16 dense burst / 2 (tf32 dense rate)",
-                     # DRAM bytes of one filter launch, from the ncu capture in
-                     # profiles/tc_screen_kernel_filter_300kx768_nq2048.md (969 MB for a 300,000-row
-                     # base), scaled by base rows: the base is streamed once per launch.
+                     # DRAM bytes of one filter launch, from an ncu capture of the filter
+                     # over a smaller base, scaled by base rows: the base is streamed once
+                     # per launch.
                      "traffic": FLAT_FILTER_BYTES_PER_ROW * n_local,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 300k-row case, "
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 250k-row case, "
                                        "scaled by base rows (one level-0 filter launch per step)",
                      "algorithmic_flop_per_step": flop_launches, "kernel_ms_per_step": fk},
         "stage_ms": avg,
@@ -525,7 +551,8 @@ def main_kmeans(args):
     from vesper_db_b200.shard import GpuKmeansOps
     x = synth.gen_isotropic_mixture(torch, dev, KM_CENTRES, KM_DIM, KM_SIGMA, KM_N, 4242)
     torch.cuda.synchronize()
-    cfg = {"workload": KM_WORKLOAD, "n": KM_N, "dim": KM_DIM, "k": KM_K, "algorithm": "lloyd",
+    cfg = {"workload": KM_WORKLOAD.replace("2,000,000", f"{KM_N:,}"), "n": KM_N, "dim": KM_DIM, "k": KM_K,
+           "algorithm": "lloyd",
            "parallelism": "single GPU", "l2_policy": "inputs larger than L2 (1.02 GB of points per iteration)"}
     out_common = {"unit": "iterations/s", "higher_is_better": True, "n_gpus": 1, "steps": args.steps,
                   "warmup": args.warmup, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -663,7 +690,8 @@ def kmeans_cpu_leg(torch, dev, x, c):
     threads, cpu = reference_threads()
     ol = _oracle_lib()
     ref = ol.Reference(ol.REF_SO)
-    xs = x[:KM_CPU_SAMPLE].cpu().numpy()
+    n_s = min(KM_CPU_SAMPLE, KM_N)
+    xs = x[:n_s].cpu().numpy()
     cs = c.cpu().numpy()
     t = time.perf_counter()
     a_ref, _ = ref.kmeans_assign(xs, cs)
@@ -799,6 +827,7 @@ def main_c5(args):
             gt_d, sel = torch.topk(cd, C5_K, dim=1, largest=False)
             gt_i = torch.gather(ci, 1, sel)
     del buf, ids
+    torch.cuda.empty_cache()   # the search holds only the index and the queries
     if world > 1 and ours:
         gt_d, gt_i = merge_topk(gt_d, gt_i, C5_K)
     gt_np = gt_i.cpu().numpy()
@@ -847,6 +876,7 @@ def main_c5(args):
     with ClockSampler(local) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
+        torch.cuda.nvtx.range_push("timed_search")
         ev0.record()
         for _ in range(args.steps):
             res_d, res_i, res_n = one_search(queries)
@@ -854,6 +884,7 @@ def main_c5(args):
             steps_t.append(t)
             launches += t["kernel_launches"]
         ev1.record()
+        torch.cuda.nvtx.range_pop()
         barrier()
     ms_total = ev0.elapsed_time(ev1)
     if world > 1:
@@ -1059,6 +1090,7 @@ def build_ivfpq_workload(args, torch, dev, world, rank):
         gt_d, gt_i = merge_topk(gt_d, gt_i, K)
     del base, chunks
     torch.cuda.synchronize()
+    torch.cuda.empty_cache()   # the search holds only the index and the queries
     build = {"data_s": t_data, "train_s": t_train, "add_s": t_add, "opq_kept": rep.opq_kept,
              "err_unrot": rep.err_unrot, "err_opq": rep.err_opq}
     return index, queries, gt_i.cpu().numpy(), build
@@ -1306,12 +1338,12 @@ def main():
                     "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                     "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} (bf16 dense, burst)",
                     # DRAM bytes per launch: the ncu capture of one main-pass launch on the
-                    # 4M-vector case (671.6 MB for 6.65e9 (query, entry) pairs), scaled by
+                    # 2M-vector case (567.1 MB for 2.209e9 (query, entry) pairs), scaled by
                     # the pairs of one launch here (codes of each probed tile are read once
                     # per batch).
                     "traffic": LIST_SCAN_BYTES_PER_PAIR * entries / launches_per_search,
-                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4M-vector case, "
-                                      "scaled by (query, entry) pairs per launch",
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 2M-vector case "
+                                      "(--n-base 2000000 --nq 8192), scaled by (query, entry) pairs per launch",
                     "algorithmic_flop_per_search": flop, "kernel_ms_per_search": lk,
                     "launches_per_search": launches_per_search,
                     "scan_stage_ms": stage_ms["scan_ms"],

@@ -59,6 +59,22 @@ def test_two_pass(op, dim, nb, nq, k, oracle):
     assert t["candidates"] >= nq * k
 
 
+def test_l2_wide_norm_range(oracle):
+    """Two-pass L2 over rows whose norms span four decades, with queries at the origin,
+    near it and far out: the augmented screen (||c||^2 folded into the tensor-core
+    product) must keep every column the exact top-k needs whatever the norm ratio."""
+    rng = np.random.default_rng(77)
+    nb, dim, nq, k = 120000, 128, 96, 10
+    base = rng.standard_normal((nb, dim)).astype(np.float32)
+    base *= (10.0 ** rng.uniform(-2, 2, (nb, 1))).astype(np.float32)
+    q = rng.standard_normal((nq, dim)).astype(np.float32)
+    q *= (10.0 ** rng.uniform(-3, 2, (nq, 1))).astype(np.float32)
+    q[0] = 0.0
+    q[1] = base[5]
+    t = _check_equal(0, q, base, k, oracle, single=False)
+    assert t["overflow_queries"] == 0
+
+
 def test_unit_norm_inner_product_768(oracle):
     """The 1M x 768 inner-product workload's distribution (N(0,1) rows, L2-normalised)
     at 200k rows."""

@@ -273,3 +273,32 @@ def test_fused_argmin_ties_and_overflow(oracle, keep):
     dist = np.array([oracle.l2_sq(x[i], c[ref[i]]) for i in range(0, n, 97)], np.float32)
     assert np.array_equal(m.cpu().numpy()[::97], dist)
     ops.close()
+
+
+def test_fused_argmin_wide_norm_range(oracle):
+    """The fused arg-min (augmented screen: ||c||^2 inside the tensor-core product)
+    against the oracle when centroid norms span four decades and points sit at, near
+    and far from the origin."""
+    import torch
+
+    from vesper_db_b200.shard import GpuKmeansOps
+    rng = np.random.default_rng(5)
+    d, k, n = 96, 700, 40000
+    c = rng.standard_normal((k, d)).astype(np.float32)
+    c *= (10.0 ** rng.uniform(-2, 2, (k, 1))).astype(np.float32)
+    x = c[rng.integers(0, k, n)] + rng.standard_normal((n, d)).astype(np.float32) * \
+        (10.0 ** rng.uniform(-3, 1, (n, 1))).astype(np.float32)
+    x[:50] *= np.float32(1e-4)
+    x[50] = 0.0
+    x = x.astype(np.float32)
+    ref = oracle.assign(x, c)
+    ops = GpuKmeansOps()
+    xt, ct = torch.from_numpy(x).cuda(), torch.from_numpy(c).cuda()
+    a = torch.zeros(n, dtype=torch.int32, device="cuda")
+    m = torch.empty(n, dtype=torch.float32, device="cuda")
+    ops.assign(xt, ct, False, a, m)
+    torch.cuda.synchronize()
+    assert np.array_equal(a.cpu().numpy().view(np.uint32), ref)
+    dist = np.array([oracle.l2_sq(x[i], c[ref[i]]) for i in range(0, n, 89)], np.float32)
+    assert np.array_equal(m.cpu().numpy()[::89], dist)
+    ops.close()

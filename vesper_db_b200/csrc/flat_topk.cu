@@ -37,6 +37,7 @@ constexpr long long FLAT_STRIDE = 16;           // sample stride of the threshol
 constexpr size_t SCREEN_BUDGET = size_t(512) << 20;  // bytes of screen values per query chunk
 constexpr size_t CAND_BUDGET = size_t(1) << 30;  // bytes of kept-column lists per filter chunk
 constexpr long long FILTER_COLS = 65535LL * 256;  // columns per filter launch (grid.y limit)
+constexpr size_t AUG_BUDGET = size_t(1) << 30;     // bytes of an augmented L2 view (launch_aug_cols)
 
 // Ordering key: ascending (score, index) for L2, (-score, index) for inner products
 // (zero canonicalised so that -0 and +0 tie).
@@ -267,10 +268,10 @@ void refine_launch(const float* q, const float* base, long long ld, int dim, con
 // Sample stride of a view of n rows at top-k k: the sample's k-th best is about the
 // (k * stride)-th best of the view, so about k * stride columns survive the filter:
 // stride <= cap / (2k).  Below 2 the view is screened in one pass.
-long long flat_sample_stride(long long n, int k) {
+long long flat_sample_stride(long long n, int k, long long max_stride = FLAT_STRIDE) {
     const int cap = k <= 128 ? 4096 : 16384;
     const long long ke = std::min<long long>(k, n);
-    long long stride = std::min<long long>(FLAT_STRIDE, std::max(1, cap / (2 * k)));
+    long long stride = std::min<long long>(max_stride, std::max(1, cap / (2 * k)));
     while (stride > 1 && (n + stride - 1) / stride < ke) stride >>= 1;
     return stride;
 }
@@ -313,10 +314,10 @@ struct View {
 // one filtering screen and the refine.  `stats` (top level only) receives stage times.
 void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, const View& v, int k,
                uint32_t* out_idx, float* out_val, FlatWork& w, int depth, FlatStats* stats, cudaStream_t st,
-               Feed* feed = nullptr, long long single_max = FLAT_SINGLE) {
+               Feed* feed = nullptr, long long single_max = FLAT_SINGLE, long long max_stride = FLAT_STRIDE) {
     const int ke = (int)std::min<long long>(k, v.n);
     const int cap = k <= 128 ? 4096 : 16384;
-    const long long stride = flat_sample_stride(v.n, k);
+    const long long stride = flat_sample_stride(v.n, k, max_stride);
     if (v.n <= single_max || depth + 1 >= FlatWork::kLevels || stride < 2) {
         if (feed) feed->ready(v.n, st, w.launches);
         exact_rows(ip, q, nq, xn, v.base, v.n, v.ld, v.cn, dim, k, out_idx, out_val, w, st);
@@ -347,7 +348,7 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     const View sample = feed ? View{feed->sample_rows, ns, (long long)dim, L.cn.data(), L.cs.data()}
                              : View{v.base, ns, v.ld * stride, L.cn.data(), L.cs.data()};
     view_topk(ip, q, nq, xn, dim, sample, k, L.s_idx.data(), L.s_val.data(), w, depth + 1, nullptr, st, nullptr,
-              single_max);
+              single_max, max_stride);
     w.tau.reserve(nq);
     flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(L.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
     check(cudaGetLastError(), "flat_tau_kernel");
@@ -361,6 +362,16 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
     w.over.reserve(nq + 1);
     check(cudaMemsetAsync(w.cand_cnt.data(), 0, (size_t)nq * sizeof(uint32_t), st), "memset");
     check(cudaMemsetAsync(w.over.data() + nq, 0, sizeof(uint32_t), st), "memset");
+    // L2 on a resident view of bounded size (coarse centroids, k-means centres): the
+    // augmented operand moves ||c||^2 into the tensor-core product (launch_aug_cols).
+    const long long ldo = aug_ld(dim);
+    const float* caug = nullptr;
+    if (!ip && !feed && persistent_filter() && (size_t)v.n * (size_t)ldo * sizeof(float) <= AUG_BUDGET) {
+        w.caug.reserve((size_t)v.n * (size_t)ldo);
+        launch_aug_cols(v.base, v.n, dim, v.ld, v.cn, w.caug.data(), st);
+        ++w.launches;
+        caug = w.caug.data();
+    }
     float filter_ms = 0.0f, refine_ms = 0.0f;
     for (long long q0 = 0; q0 < nq; q0 += qc) {
         const long long n = std::min(qc, nq - q0);
@@ -376,7 +387,8 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
                 ++w.launches;
                 launch_tc_filter_persistent(ip, q + q0 * dim, n, v.base + c0 * v.ld, nc, v.ld, dim, xn + q0,
                                             v.cn + c0, v.cs + c0, w.cmax.data(), w.tau.data() + q0, (uint32_t)c0,
-                                            w.cand.data(), w.cand_cnt.data() + q0, cap, w.err.data(), st);
+                                            w.cand.data(), w.cand_cnt.data() + q0, cap, w.err.data(), st,
+                                            caug ? caug + c0 * ldo : nullptr);
             } else {
                 launch_tc_filter(ip, q + q0 * dim, n, v.base + c0 * v.ld, nc, v.ld, dim, xn + q0, v.cn + c0,
                                  v.cs + c0, w.tau.data() + q0, (uint32_t)c0, w.cand.data(), w.cand_cnt.data() + q0,
@@ -458,7 +470,7 @@ FlatWork::~FlatWork() {
 namespace {
 void flat_topk_body(bool ip, const float* q, long long nq, const float* base, long long nb, int dim, int k,
                     uint32_t* out_idx, float* out_score, FlatWork& w, cudaStream_t st, Feed* feed,
-                    long long single_max = FLAT_SINGLE) {
+                    long long single_max = FLAT_SINGLE, long long max_stride = FLAT_STRIDE) {
     if (!w.ev[0])
         for (auto& e : w.ev) check(cudaEventCreate(&e), "cudaEventCreate");
     const int ke = (int)std::min<long long>(k, nb);
@@ -482,7 +494,7 @@ void flat_topk_body(bool ip, const float* q, long long nq, const float* base, lo
     check(cudaEventRecord(w.ev[2], st), "event");
     FlatStats stats;
     const View v{base, nb, dim, w.cn.data(), w.csq.data()};
-    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st, feed, single_max);
+    view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st, feed, single_max, max_stride);
     if (k > ke) {
         pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
         check(cudaGetLastError(), "pad_topk_kernel");
@@ -543,13 +555,24 @@ __global__ void keep_on_tie_kernel(const float* __restrict__ x, long long n, int
 // launch_exact_nearest (a one-pass screen writes and re-reads nx * nc screen values).
 constexpr long long kNearestSingle = 1024;
 
+// Sample stride cap of launch_exact_nearest's threshold recursion.  Each level's filter
+// keeps about k x stride columns per row, all of which the refine re-scores; a smaller
+// stride adds sample levels.  Measured on the coarse probes (65,536 x 128 centroids,
+// 100k rows, k = 64: 32.1 / 28.7 / 32.3 ms at stride 16 / 8 / 4; 16,384 x 768, 10k
+// rows, k = 32: 2.34 / 2.95 ms at 16 / 8) the best keeps about 512 columns per row.
+// VGPU_NEAREST_STRIDE overrides it.
+long long nearest_stride(int k) {
+    if (const char* v = std::getenv("VGPU_NEAREST_STRIDE")) return std::max(2L, std::strtol(v, nullptr, 10));
+    return std::max<long long>(2, std::min<long long>(FLAT_STRIDE, 512 / std::max(1, k)));
+}
+
 void launch_exact_nearest(const float* x, long long nx, const float* c, long long nc, int dim, int k,
                           const uint32_t* keep, uint32_t* out_idx, float* out_val, FlatWork& w, cudaStream_t st) {
     w.last = FlatStats{};
     if (nx <= 0 || nc <= 0 || k <= 0) return;
     check_flat_args(x, c, nc, dim, k);
     if (keep && k != 1) throw CudaError("exact_nearest: the keep-on-tie rule applies to k = 1");
-    flat_topk_body(false, x, nx, c, nc, dim, k, out_idx, out_val, w, st, nullptr, kNearestSingle);
+    flat_topk_body(false, x, nx, c, nc, dim, k, out_idx, out_val, w, st, nullptr, kNearestSingle, nearest_stride(k));
     if (keep) {
         keep_on_tie_kernel<<<grid_for(nx * 8, 256), 256, 0, st>>>(x, nx, dim, c, keep, out_idx, out_val);
         check(cudaGetLastError(), "keep_on_tie_kernel");

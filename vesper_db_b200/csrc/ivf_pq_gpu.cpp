@@ -1130,8 +1130,10 @@ public:
         // chunk (rows of dim floats, dim % 4 == 0 on the tensor-core path); host queries
         // are copied into w_q.
         const bool filt = !ext_probe && filter_probe(on_device ? queries : d_cent.data());  // w_q is cudaMalloc'd
-        size_t qc = filt ? std::max<size_t>(1, kSearchTableBudget / (sizeof(float) * (size_t)m() * ksub))
-                         : std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist()));
+        // No distance matrix when the probe lists are given or come from the filter path.
+        const bool no_dist = filt || ext_probe;
+        size_t qc = no_dist ? std::max<size_t>(1, kSearchTableBudget / (sizeof(float) * (size_t)m() * ksub))
+                            : std::max<size_t>(1, kSearchDistBudget / (sizeof(float) * (size_t)nlist()));
         if (exact && has_rot) qc = std::min(qc, std::max<size_t>(1, kDistBudget / (sizeof(float) * np * dim)));
         qc = std::min(qc, nq);
         if (!filt && !ext_probe) w_D.reserve(qc * nlist());

@@ -1221,19 +1221,8 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
         for (int i = threadIdx.x; i < m * 64; i += FB_NT) dst[i] = __ldg(src + i);
     }
     // Per-probe prefixes (entries, blocks) and base terms.
-    if (threadIdx.x == 0) {
-        uint32_t ep = 0, bp = 0;
-        for (int t = 0; t < nscan; ++t) {
-            const uint32_t l = probe[q * nprobe + t];
-            eprefix[t] = ep;
-            bprefix[t] = bp;
-            ep += (uint32_t)(offs[l + 1] - offs[l]);
-            bp += (uint32_t)(blk_off[l + 1] - blk_off[l]);
-        }
-        eprefix[nscan] = ep;
-        bprefix[nscan] = bp;
-        cnt = 0; have = 0; tau = ~0ull;
-    }
+    if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nscan, offs, blk_off, eprefix, bprefix);
+    if (threadIdx.x == 0) { cnt = 0; have = 0; tau = ~0ull; }
     for (int t = threadIdx.x; t < nscan; t += FB_NT) base[t] = pbase[q * nprobe + t];
     __syncthreads();
     (void)lane;
@@ -1477,15 +1466,7 @@ __global__ void __launch_bounds__(256) split_merge_kernel(
     const int p2 = next_pow2(n < 2 ? 2 : n);
     const unsigned long long* src = part_keys + (long long)part_off[q] * k;
     for (int i = threadIdx.x; i < p2; i += 256) keys[i] = i < n ? src[i] : ~0ull;
-    if (threadIdx.x == 0) {
-        uint32_t ep = 0;
-        for (int t = 0; t < nscan; ++t) {
-            const uint32_t l = probe[q * nprobe + t];
-            eprefix[t] = ep;
-            ep += (uint32_t)(offs[l + 1] - offs[l]);
-        }
-        eprefix[nscan] = ep;
-    }
+    if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nscan, offs, nullptr, eprefix, nullptr);
     bitonic_sort_u64<256>(keys, p2);
     __shared__ int h_s;
     if (threadIdx.x == 0) {

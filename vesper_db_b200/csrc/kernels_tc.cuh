@@ -44,7 +44,7 @@ struct FlatWork {
         DeviceBuffer<float> cn, cs, s_val;
         DeviceBuffer<uint32_t> s_idx;
     } level[kLevels];
-    DeviceBuffer<float> xn, cn, csq, tau, dt, oq, oxn, o_val, cmax;
+    DeviceBuffer<float> xn, cn, csq, tau, dt, oq, oxn, o_val, cmax, caug;
     DeviceBuffer<uint32_t> cand_cnt, over, o_idx, o_rows;
     DeviceBuffer<uint2> cand;
     DeviceBuffer<int> err;
@@ -88,20 +88,30 @@ void launch_flat_topk_host(bool ip, const float* q, long long nq, const float* h
 // alias out_idx).  Rows whose candidate list overflowed are appended to over[] with
 // *n_over counting them (zero it first); they are left for the caller.  err receives a
 // nonzero code if a bounded wait expired.
+// caug: workspace of nc * aug_ld(dim) floats for the augmented centroid operand.
 bool tc_argmin_supported(int dim);
 void launch_col_max(const float* cn, const float* cs, int nc, float* cmax, cudaStream_t st);
 void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
                       const float* cs, const float* cmax, const uint32_t* keep, uint32_t* out_idx, float* out_val,
-                      uint32_t* over, uint32_t* n_over, int* err, cudaStream_t st);
+                      uint32_t* over, uint32_t* n_over, float* caug, int* err, cudaStream_t st);
+// The augmented centroid operand of the L2 screens (tc_argmin_kernel, tc_filter_kernel):
+// row i = (c_i, zeros to a multiple of 32, -hi, -lo, zeros), aug_ld(dim) floats, with
+// hi + lo the two-term tf32 split of ||c_i||^2 / 2 (cn[i] / 2); c's row i at c + i * c_ld.
+int aug_ld(int dim);
+void launch_aug_cols(const float* c, long long nc, int dim, long long c_ld, const float* cn, float* out,
+                     cudaStream_t st);
 void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const float* val, uint32_t* out_idx,
                          float* out_val, cudaStream_t st);
 // launch_tc_filter's keep rule on the persistent pipeline of tc_argmin_kernel (each CTA
 // walks a share of the column tiles for its 128 rows); cmax from launch_col_max over
-// the same columns' cn / cs.  Same outputs and semantics as launch_tc_filter.
+// the same columns' cn / cs.  Same outputs and semantics as launch_tc_filter.  caug
+// (L2 only, may be null): the same columns' augmented operand (launch_aug_cols), which
+// moves ||c||^2 into the tensor-core product; the kept values are then ||x||^2 - 2 S'.
 void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const float* c, long long nc,
                                  long long c_stride, int dim, const float* xn, const float* cn, const float* cs,
                                  const float* cmax, const float* tau, uint32_t col_off, uint2* cand,
-                                 uint32_t* cand_cnt, int cap, int* err, cudaStream_t st);
+                                 uint32_t* cand_cnt, int cap, int* err, cudaStream_t st,
+                                 const float* caug = nullptr);
 // out[i] = ||x_i||^2 (fp64 accumulation); row i at x + i * ld (ld = dim by default).
 void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStream_t st, long long ld = 0);
 // Per row: exact k nearest centroids (reference-order distances, ties to the lowest

@@ -88,8 +88,9 @@ void KmeansEngine::assign(const float* d_x, size_t n, int d, const float* d_c, u
         launch_col_max(cn_.data(), cs_.data(), (int)k, cmax_.data(), st_);
         check(cudaMemsetAsync(err_.data(), 0, sizeof(int), st_), "memset err");
         check(cudaMemsetAsync(over_.data() + n, 0, sizeof(uint32_t), st_), "memset over");
+        caug_.reserve((size_t)k * (size_t)aug_ld(d));
         launch_tc_argmin(d_x, (long long)n, d_c, (int)k, d, xn_.data(), cn_.data(), cs_.data(), cmax_.data(), kp,
-                         d_assign, d_mind, over_.data(), over_.data() + n, err_.data(), st_);
+                         d_assign, d_mind, over_.data(), over_.data() + n, caug_.data(), err_.data(), st_);
         int h[2] = {0, 0};
         check(cudaMemcpyAsync(&h[0], err_.data(), sizeof(int), cudaMemcpyDeviceToHost, st_), "d2h err");
         check(cudaMemcpyAsync(&h[1], over_.data() + n, sizeof(uint32_t), cudaMemcpyDeviceToHost, st_), "d2h over");

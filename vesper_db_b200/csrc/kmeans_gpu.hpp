@@ -91,7 +91,7 @@ public:
 
 private:
     cudaStream_t st_;
-    DeviceBuffer<float> D_, xn_, cn_, cs_, cmax_, mind_, kpp_, ox_, oval_;
+    DeviceBuffer<float> D_, xn_, cn_, cs_, cmax_, mind_, kpp_, ox_, oval_, caug_;
     DeviceBuffer<uint32_t> over_, oidx_, okeep_;
     uint32_t last_overflow_ = 0;
     DeviceBuffer<double> kpp_bsum_, kpp_u_;

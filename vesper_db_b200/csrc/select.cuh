@@ -142,4 +142,42 @@ __device__ int block_select_k(const float* vals, int n, int k, unsigned long lon
     return take;
 }
 
+// Per-probe prefix sums of one query's probed lists, run by one whole warp (a shuffle
+// scan per 32 probes instead of one thread walking them): eprefix[t] = entries of
+// probes 0..t-1, eprefix[nscan] = their total; the same for 128-entry blocks when
+// bprefix is given.  Integer sums: the values equal a sequential walk's.
+__device__ __forceinline__ void probe_prefixes_warp(const uint32_t* __restrict__ prow, int nscan,
+                                                    const uint64_t* __restrict__ offs,
+                                                    const uint64_t* __restrict__ blk_off, uint32_t* eprefix,
+                                                    uint32_t* bprefix) {
+    const int lane = threadIdx.x & 31;
+    uint32_t ec = 0, bc = 0;
+    for (int t0 = 0; t0 < nscan; t0 += 32) {
+        const int t = t0 + lane;
+        uint32_t e = 0, b = 0;
+        if (t < nscan) {
+            const uint32_t l = prow[t];
+            e = (uint32_t)(offs[l + 1] - offs[l]);
+            if (bprefix) b = (uint32_t)(blk_off[l + 1] - blk_off[l]);
+        }
+        uint32_t ie = e, ib = b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t ye = __shfl_up_sync(0xffffffffu, ie, o);
+            const uint32_t yb = __shfl_up_sync(0xffffffffu, ib, o);
+            if (lane >= o) { ie += ye; ib += yb; }
+        }
+        if (t < nscan) {
+            eprefix[t] = ec + ie - e;
+            if (bprefix) bprefix[t] = bc + ib - b;
+        }
+        ec += __shfl_sync(0xffffffffu, ie, 31);
+        bc += __shfl_sync(0xffffffffu, ib, 31);
+    }
+    if (lane == 0) {
+        eprefix[nscan] = ec;
+        if (bprefix) bprefix[nscan] = bc;
+    }
+}
+
 }  // namespace vgpu

@@ -369,8 +369,8 @@ void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, lon
 //   warp 5 (one lane)  tcgen05.mma.kind::tf32 into two 256-column TMEM accumulators, so
 //                      the next tile's products run while the epilogue reads the last;
 //   warps 0..3         epilogue, thread = row: for every column the screen value
-//                      Dt = ||x||^2 + ||c||^2 - 2S and its proven error eps (the filter
-//                      modes' bound), a running minimum U of the upper bounds Dt + eps,
+//                      Dt = ||x||^2 - 2S' and its proven error eps (screen_eps), a
+//                      running minimum U of the upper bounds Dt + eps,
 //                      and the columns whose lower bound Dt - eps is <= U kept in a
 //                      per-row list of ARG_CAP (compacted against the current U when it
 //                      fills).
@@ -381,10 +381,50 @@ void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, lon
 // for the caller to redo.  Every wait is bounded; on timeout the kernel records an
 // error code, stops, and frees its TMEM.
 // ---------------------------------------------------------------------------------
+// The augmented screen.  The tensor cores compute S' = <x, c> - ||c||^2 / 2 directly:
+// the centroid operand carries one more 32-column K-slice holding (-hi, -lo, 0, ...),
+// hi = tf32(||c||^2 / 2) and lo = tf32(||c||^2 / 2 - hi) (truncations, so both are
+// exact tf32 values and hi + lo is within 2^-21 ||c||^2 of ||c||^2 / 2), and the row
+// operand of that slice is a constant shared-memory tile of rows (1, 1, 0, ...).  One
+// extra K = 8 MMA per tile; the epilogue's screen value is Dt = fl(||x||^2 - 2 S'), and
+// a 32-column chunk is dismissed on fl(||x||^2 - 2 max S') alone (the rounding is
+// monotone, so that is the chunk's smallest Dt): one max per column on the common path.
+// screen_eps bounds the augmented value (screen_a, screen_r2).
+// ---------------------------------------------------------------------------------
 namespace {
 constexpr int ARG_CAP = 16;
 constexpr int ARG_THREADS = 192;
-constexpr int ARG_SMEM = STAGES * STAGE_BYTES + 1024 + 256 + ARG_CAP * BM * 8;
+constexpr int ONES_OFF = STAGES * STAGE_BYTES;   // the augmented slice's row operand (A_BYTES)
+constexpr int BAR_OFF = ONES_OFF + A_BYTES;      // barriers (256 bytes), then per-kernel arrays
+constexpr int ARG_SMEM = BAR_OFF + 256 + ARG_CAP * BM * 8 + 1024;
+constexpr int FILT_SMEM = BAR_OFF + 256 + 2 * BN * 4 + 1024;
+static_assert(ARG_SMEM <= 232448 && FILT_SMEM <= 232448, "shared memory per CTA");
+
+// Row r of the augmented slice's row operand, (1, 1, 0, ..., 0), in the 128-byte
+// swizzled K-major layout a TMA tile load produces (16-byte chunk j of row r at chunk
+// j ^ (r & 7)); then a proxy fence so the tensor cores see the generic-proxy stores.
+__device__ __forceinline__ void write_ones_row(unsigned char* ones, int r) {
+    uint4* row = reinterpret_cast<uint4*>(ones + r * 128);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        row[j ^ (r & 7)] = j == 0 ? make_uint4(0x3f800000u, 0x3f800000u, 0u, 0u) : make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// AND of v over the 128 epilogue threads (warps 0..3, named barrier 1); also a barrier
+// for them that publishes their earlier shared-memory writes.
+__device__ __forceinline__ bool epilogue_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
 constexpr uint32_t ARG_TMEM_COLS = 512;
 
 // The two pipeline roles of the persistent screens (tc_argmin_kernel, tc_filter_kernel),
@@ -394,38 +434,49 @@ constexpr uint32_t ARG_TMEM_COLS = 512;
 // accumulator's previous tile.  A failed (bounded) wait sets *fail and ends the role.
 __device__ __forceinline__ void screen_producer(unsigned char* smem, uint64_t* full, uint64_t* empty,
                                                 const CUtensorMap* map_x, const CUtensorMap* map_c, int m0,
-                                                int jt0, int ntiles, int kt, volatile int* fail) {
+                                                int jt0, int ntiles, int kt, bool aug, volatile int* fail) {
     int it = 0;
+    const int kslices = kt + (aug ? 1 : 0);
     for (int j = 0; j < ntiles && !*fail; ++j) {
-        for (int t = 0; t < kt; ++t, ++it) {
+        for (int t = 0; t < kslices; ++t, ++it) {
             const int s = it % STAGES;
             if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { *fail = 1; return; }
             unsigned char* a = smem + s * STAGE_BYTES;
-            mbar_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(a, map_x, t * BK, m0, &full[s]);
+            if (t < kt) {
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                tma_load_2d(a, map_x, t * BK, m0, &full[s]);
+            } else {
+                mbar_expect_tx(&full[s], B_BYTES);   // the augmented slice: centroid side only
+            }
             tma_load_2d(a + A_BYTES, map_c, t * BK, (jt0 + j) * BN, &full[s]);
         }
     }
 }
 
 __device__ __forceinline__ void screen_mma(unsigned char* smem, uint64_t* full, uint64_t* empty, uint64_t* acc_full,
-                                           uint64_t* acc_empty, uint32_t tmem, int ntiles, int kt,
+                                           uint64_t* acc_empty, uint32_t tmem, int ntiles, int kt, bool aug,
                                            volatile int* fail) {
     int it = 0;
+    const int kslices = kt + (aug ? 1 : 0);
+    const uint64_t ones_desc = sw128_kmajor_desc(smem_u32(smem + ONES_OFF));
     for (int j = 0; j < ntiles && !*fail; ++j) {
         const int acc = j & 1;
         if (j >= 2 && !mbar_wait(&acc_empty[acc], ((j >> 1) - 1) & 1)) { *fail = 4; return; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t td = tmem + (uint32_t)(acc * BN);
-        for (int t = 0; t < kt; ++t, ++it) {
+        for (int t = 0; t < kslices; ++t, ++it) {
             const int s = it % STAGES;
             if (!mbar_wait(&full[s], (it / STAGES) & 1)) { *fail = 2; return; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
             const uint64_t ad = sw128_kmajor_desc(a), bd = sw128_kmajor_desc(a + A_BYTES);
+            if (t < kt) {
 #pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk)
-                mma_tf32(td, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), (t > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < BK / 8; ++kk)
+                    mma_tf32(td, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), (t > 0 || kk > 0) ? 1u : 0u);
+            } else {
+                mma_tf32(td, ones_desc, bd, 1u);   // only K columns 0 and 1 of the slice are nonzero
+            }
             mma_commit(&empty[s]);
         }
         mma_commit(&acc_full[acc]);
@@ -441,15 +492,15 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
     uint32_t* __restrict__ over, uint32_t* __restrict__ n_over, int* __restrict__ err) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;     // [2]
     uint64_t* acc_empty = acc_full + 2;      // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-    // barriers in the first 256 bytes past the ring, then the candidate lists (the
-    // other 1024 bytes of ARG_SMEM's slack absorb the 1024-byte alignment of smem)
-    uint32_t* cand_col = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + 256);  // [ARG_CAP][BM]
-    float* cand_lb = reinterpret_cast<float*>(cand_col + ARG_CAP * BM);                         // [ARG_CAP][BM]
+    // barriers in the first 256 bytes past the ring and the ones tile, then the
+    // candidate lists (the last 1024 bytes of ARG_SMEM absorb the 1024-byte alignment)
+    uint32_t* cand_col = reinterpret_cast<uint32_t*>(smem + BAR_OFF + 256);  // [ARG_CAP][BM]
+    float* cand_lb = reinterpret_cast<float*>(cand_col + ARG_CAP * BM);      // [ARG_CAP][BM]
     __shared__ int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -469,15 +520,18 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    if (warp < 4) write_ones_row(smem + ONES_OFF, threadIdx.x);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 4) {
-        if (lane == 0) screen_producer(smem, full, empty, &map_x, &map_c, m0, 0, ntiles, kt, (volatile int*)&s_fail);
+        if (lane == 0)
+            screen_producer(smem, full, empty, &map_x, &map_c, m0, 0, ntiles, kt, true, (volatile int*)&s_fail);
     } else if (warp == 5) {
-        if (lane == 0) screen_mma(smem, full, empty, acc_full, acc_empty, tmem, ntiles, kt, (volatile int*)&s_fail);
+        if (lane == 0)
+            screen_mma(smem, full, empty, acc_full, acc_empty, tmem, ntiles, kt, true, (volatile int*)&s_fail);
     } else {
         // Epilogue: thread (warp w < 4, lane l) owns row 32w + l.
         const int r = warp * 32 + lane;
@@ -485,14 +539,15 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
         const bool live = row < nx;
         const float rn = live ? xn[row] : 0.0f;
         const float xs = sqrtf(rn);
-        const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;
+        const float a = screen_a(dim), r2 = screen_r2(dim);
         const float rr = (float)(dim / 8 + 8) * 1.1920929e-7f;
         // e(col) <= E0 + 2.002 rr |dt| over every column (cmax = the largest ||c||^2 and
         // ||c||), so dt > T = (U + E0)(1 + 4 rr) proves dt - e > U: most columns are
         // dismissed on dt alone.  U >= 0 (an upper bound of an exact distance), so such
         // a dt is positive.
         const float c2max = cmax[0], csmax = cmax[1];
-        const float E0 = 1.0009765625f * (4.0f * a * xs * csmax + 4.768e-7f * (rn + c2max + 2.0f * xs * csmax));
+        const float E0 = 1.0009765625f * (4.0f * a * xs * csmax + 4.0f * r2 * c2max +
+                                          4.768e-7f * (rn + c2max + 2.0f * xs * csmax));
         const float tgrow = 1.0f + 4.0f * rr + 1e-5f;   // + slack for the fp32 rounding of this test
         float U = FLT_MAX, T = FLT_MAX;
         int cnt = 0;
@@ -500,25 +555,28 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
         for (int j = 0; j < ntiles; ++j) {
             const int acc = j & 1;
+            const int n0 = j * BN;
             const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (j >> 1) & 1));
             if (!got) { s_fail = 3; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int n0 = j * BN;
             for (int ch = 0; ch < BN / 32; ++ch) {
                 uint32_t v[32];
+                __syncwarp();   // reconverge after the divergent screen before the collective load
                 tmem_ld32(trow + (uint32_t)(acc * BN + ch * 32), v);
                 const int cb = n0 + ch * 32;
                 if (cb >= nc) continue;   // uniform: the last tile's padding columns
-                // Fast screen: one coalesced load of the chunk's column norms, broadcast
-                // by shuffle; a column passes when its screen value can reach T.
-                const int colL = cb + lane;
-                const float c2L = colL < nc ? __ldg(cn + colL) : FLT_MAX;
+                // Fast screen: the chunk's smallest screen value is fl(rn - 2 max S')
+                // (monotone rounding); a chunk above T is dismissed, otherwise each
+                // column passes when its screen value can reach T.
+                float mx = -FLT_MAX;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) mx = fmaxf(mx, __uint_as_float(v[jj]));
+                if (!live || !(__fmaf_rn(-2.0f, mx, rn) <= T)) continue;
                 float dts[32];
                 uint32_t mask = 0;
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
-                    const float c2 = __shfl_sync(0xffffffffu, c2L, jj);
-                    dts[jj] = (rn + c2) - 2.0f * __uint_as_float(v[jj]);
+                    dts[jj] = __fmaf_rn(-2.0f, __uint_as_float(v[jj]), rn);
                     mask |= (dts[jj] <= T ? 1u : 0u) << jj;
                 }
                 if (nc - cb < 32) mask &= (1u << (nc - cb)) - 1u;   // columns past nc never pass
@@ -533,8 +591,8 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
                     for (int u = 0; u < 32; ++u) dt = (u == jj) ? dts[u] : dt;
                     const float c2 = __ldg(cn + col);
                     const float xc = xs * __ldg(cs + col);
-                    const float e = 1.0009765625f *
-                                    (4.0f * a * xc + 4.768e-7f * (rn + c2 + 2.0f * xc) + 2.0f * rr * fabsf(dt));
+                    const float e = 1.0009765625f * (4.0f * a * xc + 4.0f * r2 * c2 +
+                                                     4.768e-7f * (rn + c2 + 2.0f * xc) + 2.0f * rr * fabsf(dt));
                     const float lb = dt - e;
                     if (lb > U) continue;
                     if (dt + e < U) {
@@ -626,9 +684,11 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_argmin_kernel(
 // col_off, screen value), one atomic reservation per row per tile; a row's count may
 // exceed cap (the refine treats that as an overflow).  Most columns are dismissed on a
 // column-independent bound first (L2: Dt > (tau + E0)(1 + 4 rr + 1e-5); IP: S' below
-// the threshold at the largest ||c||), the exact test runs only for the rest.
+// the threshold at the largest ||c||), the exact test runs only for the rest.  AUG (L2
+// only): map_c is the augmented centroid operand and the screen value is ||x||^2 - 2 S';
+// otherwise the tile's column norms are staged in shared memory.
 // ---------------------------------------------------------------------------------
-template <bool IP>
+template <bool IP, bool AUG>
 __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
     const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_c, int nx, int nc, int dim,
     int tiles_per_cta, const float* __restrict__ xn, const float* __restrict__ cn, const float* __restrict__ cs,
@@ -636,11 +696,12 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
     uint32_t* __restrict__ cand_cnt, int cap, int* __restrict__ err) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    float* c2s = reinterpret_cast<float*>(smem + BAR_OFF + 256);   // [2][BN] (L2 without AUG)
     __shared__ int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -662,15 +723,18 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    if (AUG && warp < 4) write_ones_row(smem + ONES_OFF, threadIdx.x);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 4) {
-        if (lane == 0) screen_producer(smem, full, empty, &map_x, &map_c, m0, jt0, ntiles, kt, (volatile int*)&s_fail);
+        if (lane == 0)
+            screen_producer(smem, full, empty, &map_x, &map_c, m0, jt0, ntiles, kt, AUG, (volatile int*)&s_fail);
     } else if (warp == 5) {
-        if (lane == 0) screen_mma(smem, full, empty, acc_full, acc_empty, tmem, ntiles, kt, (volatile int*)&s_fail);
+        if (lane == 0)
+            screen_mma(smem, full, empty, acc_full, acc_empty, tmem, ntiles, kt, AUG, (volatile int*)&s_fail);
     } else {
         const int r = warp * 32 + lane;
         const int row = m0 + r;
@@ -678,11 +742,12 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
         const float rn = live ? xn[row] : 0.0f;
         const float xs = sqrtf(rn);
         const float t = live ? tau[row] : -FLT_MAX;
-        const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;
+        const float a = screen_a(dim), r2 = screen_r2(dim);
         const float rr = (float)(dim / 8 + 8) * 1.1920929e-7f;
         const float c2max = cmax[0], csmax = cmax[1];
         // L2 fast bound (as in tc_argmin_kernel, with the fixed tau in place of U)
-        const float E0 = 1.0009765625f * (4.0f * a * xs * csmax + 4.768e-7f * (rn + c2max + 2.0f * xs * csmax));
+        const float E0 = 1.0009765625f * (4.0f * a * xs * csmax + 4.0f * r2 * c2max +
+                                          4.768e-7f * (rn + c2max + 2.0f * xs * csmax));
         const float T = (t + E0) * (1.0f + 4.0f * rr + 1e-5f);
         // IP: keep iff S >= t_ip - w cs; below S_lo no column can be kept (w cs <= w csmax)
         const float w_ip = 2.0f * (a + rr + 2.4e-7f) * xs * 1.0009765625f;
@@ -691,32 +756,53 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
         for (int j = 0; j < ntiles; ++j) {
             const int acc = j & 1;
-            const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (j >> 1) & 1));
+            const int n0 = (jt0 + j) * BN;
+            float* c2t = c2s + acc * BN;
+            if constexpr (!IP && !AUG)
+                for (int i = r; i < BN; i += BM) c2t[i] = n0 + i < nc ? __ldg(cn + n0 + i) : FLT_MAX;
+            const bool got = epilogue_all(mbar_wait(&acc_full[acc], (j >> 1) & 1));
             if (!got) { s_fail = 3; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int n0 = (jt0 + j) * BN;
             uint32_t keepm[BN / 32];
             uint32_t total = 0;
 #pragma unroll
             for (int ch = 0; ch < BN / 32; ++ch) {
                 uint32_t v[32];
+                __syncwarp();   // reconverge after the divergent screen before the collective load
                 tmem_ld32(trow + (uint32_t)(acc * BN + ch * 32), v);
                 keepm[ch] = 0u;
                 const int cb = n0 + ch * 32;
                 if (cb >= nc) continue;
-                const int colL = cb + lane;
                 uint32_t mask = 0;
                 if constexpr (IP) {
+                    // dismiss the chunk when its largest dot product is below S_lo
+                    float mx = -FLT_MAX;
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) mx = fmaxf(mx, __uint_as_float(v[jj]));
+                    if (!live || !(mx >= S_lo)) continue;
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj) mask |= (__uint_as_float(v[jj]) >= S_lo ? 1u : 0u) << jj;
+                } else if constexpr (AUG) {
+                    // the chunk's smallest screen value is fl(rn - 2 max S')
+                    float mx = -FLT_MAX;
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) mx = fmaxf(mx, __uint_as_float(v[jj]));
+                    if (!live || !(__fmaf_rn(-2.0f, mx, rn) <= T)) continue;
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj)
+                        mask |= (__fmaf_rn(-2.0f, __uint_as_float(v[jj]), rn) <= T ? 1u : 0u) << jj;
                 } else {
-                    const float c2L = colL < nc ? __ldg(cn + colL) : FLT_MAX;
+                    const float* cc = c2t + ch * 32;
+                    float dts[32];
+                    float mn = FLT_MAX;
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj) {
-                        const float c2 = __shfl_sync(0xffffffffu, c2L, jj);
-                        const float dt = (rn + c2) - 2.0f * __uint_as_float(v[jj]);
-                        mask |= (dt <= T ? 1u : 0u) << jj;
+                        dts[jj] = __fmaf_rn(-2.0f, __uint_as_float(v[jj]), __fadd_rn(rn, cc[jj]));
+                        mn = fminf(mn, dts[jj]);
                     }
+                    if (!live || !(mn <= T)) continue;
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) mask |= (dts[jj] <= T ? 1u : 0u) << jj;
                 }
                 if (nc - cb < 32) mask &= (1u << (nc - cb)) - 1u;
                 if (!live) mask = 0;
@@ -734,8 +820,9 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
                     } else {
                         const float c2 = __ldg(cn + col);
                         const float xc = xs * __ldg(cs + col);
-                        const float dt = (rn + c2) - 2.0f * S;
-                        const float e = 4.0f * a * xc + 4.768e-7f * (rn + c2 + 2.0f * xc) + 2.0f * rr * fabsf(dt);
+                        const float dt = AUG ? __fmaf_rn(-2.0f, S, rn) : (rn + c2) - 2.0f * S;
+                        const float e = 4.0f * a * xc + 4.0f * r2 * c2 + 4.768e-7f * (rn + c2 + 2.0f * xc) +
+                                        2.0f * rr * fabsf(dt);
                         kp = dt - 1.0009765625f * e <= t;
                     }
                     if (kp) km |= 1u << jj;
@@ -760,7 +847,9 @@ __global__ void __launch_bounds__(ARG_THREADS, 1) tc_filter_kernel(
                         float S = 0.0f;
 #pragma unroll
                         for (int u2 = 0; u2 < 32; ++u2) S = (u2 == jj) ? __uint_as_float(v[u2]) : S;
-                        const float val = IP ? -2.0f * S : (rn + __ldg(cn + col)) - 2.0f * S;
+                        const float val = IP    ? -2.0f * S
+                                          : AUG ? __fmaf_rn(-2.0f, S, rn)
+                                                : (rn + __ldg(cn + col)) - 2.0f * S;
                         dst[slot] = make_uint2((uint32_t)col + col_off, __float_as_uint(val));
                     }
                     ++slot;
@@ -798,6 +887,28 @@ __global__ void col_max_kernel(const float* __restrict__ cn, const float* __rest
     }
 }
 
+// Row i of the augmented centroid operand: c_i (dim values, then zeros up to the next
+// multiple of BK), then the slice (-hi, -lo, 0, ...) of ||c_i||^2 / 2.
+__global__ void aug_cols_kernel(const float* __restrict__ c, long long nc, int dim, long long c_ld,
+                                const float* __restrict__ cn, float* __restrict__ out, int ldo) {
+    const int kd = ldo - BK;
+    const long long total = nc * (long long)ldo;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i / ldo;
+        const int j = (int)(i - row * ldo);
+        float v = 0.0f;
+        if (j < dim) {
+            v = c[row * c_ld + j];
+        } else if (j == kd || j == kd + 1) {
+            const float h = 0.5f * cn[row];
+            const float hi = __uint_as_float(__float_as_uint(h) & 0xffffe000u);   // tf32 truncation
+            const float lo = __uint_as_float(__float_as_uint(h - hi) & 0xffffe000u);
+            v = j == kd ? -hi : -lo;
+        }
+        out[i] = v;
+    }
+}
+
 __global__ void scatter_top1_kernel(const uint32_t* __restrict__ rows, int n, const uint32_t* __restrict__ idx,
                                     const float* __restrict__ val, uint32_t* __restrict__ out_idx,
                                     float* __restrict__ out_val) {
@@ -810,6 +921,17 @@ __global__ void scatter_top1_kernel(const uint32_t* __restrict__ rows, int n, co
 
 bool tc_argmin_supported(int dim) { return tc_screen_supported(dim); }
 
+int aug_ld(int dim) { return (dim + BK - 1) / BK * BK + BK; }
+
+void launch_aug_cols(const float* c, long long nc, int dim, long long c_ld, const float* cn, float* out,
+                     cudaStream_t st) {
+    if (nc <= 0) return;
+    const long long total = nc * (long long)aug_ld(dim);
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    aug_cols_kernel<<<blocks, 256, 0, st>>>(c, nc, dim, c_ld, cn, out, aug_ld(dim));
+    check(cudaGetLastError(), "aug_cols_kernel");
+}
+
 void launch_col_max(const float* cn, const float* cs, int nc, float* cmax, cudaStream_t st) {
     check(cudaMemsetAsync(cmax, 0, 2 * sizeof(float), st), "memset");
     if (nc <= 0) return;
@@ -819,14 +941,15 @@ void launch_col_max(const float* cn, const float* cs, int nc, float* cmax, cudaS
 
 void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
                       const float* cs, const float* cmax, const uint32_t* keep, uint32_t* out_idx, float* out_val,
-                      uint32_t* over, uint32_t* n_over, int* err, cudaStream_t st) {
+                      uint32_t* over, uint32_t* n_over, float* caug, int* err, cudaStream_t st) {
     if (nx <= 0 || nc <= 0) return;
     if (!tc_screen_supported(dim)) throw CudaError("tc_argmin: dim must be a multiple of 4 and >= 32");
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(caug)) & 15)
         throw CudaError("tc_argmin: operands must be 16-byte aligned");
     if (nx > 0x7fffffffLL) throw CudaError("tc_argmin: too many rows");
+    launch_aug_cols(c, nc, dim, dim, cn, caug, st);
     const CUtensorMap mx = make_map(x, nx, dim, BM);
-    const CUtensorMap mc = make_map(c, nc, dim, BN);
+    const CUtensorMap mc = make_map(caug, nc, aug_ld(dim), BN);
     check(cudaFuncSetAttribute(tc_argmin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ARG_SMEM),
           "cudaFuncSetAttribute(tc_argmin)");
     tc_argmin_kernel<<<(unsigned)ceil_div(nx, BM), ARG_THREADS, ARG_SMEM, st>>>(
@@ -837,14 +960,15 @@ void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int 
 void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const float* c, long long nc,
                                  long long c_stride, int dim, const float* xn, const float* cn, const float* cs,
                                  const float* cmax, const float* tau, uint32_t col_off, uint2* cand,
-                                 uint32_t* cand_cnt, int cap, int* err, cudaStream_t st) {
+                                 uint32_t* cand_cnt, int cap, int* err, cudaStream_t st, const float* caug) {
     if (nx <= 0 || nc <= 0) return;
     if (!tc_screen_supported(dim)) throw CudaError("tc_filter: dim must be a multiple of 4 and >= 32");
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c)) & 15)
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(caug)) & 15)
         throw CudaError("tc_filter: operands must be 16-byte aligned");
     if (nc > 0x7fffffffLL || nx > 0x7fffffffLL) throw CudaError("tc_filter: too many rows or columns");
+    const bool aug = !ip && caug;
     const CUtensorMap mx = make_map(x, nx, dim, BM);
-    const CUtensorMap mc = make_map(c, nc, dim, BN, c_stride);
+    const CUtensorMap mc = aug ? make_map(caug, nc, aug_ld(dim), BN) : make_map(c, nc, dim, BN, c_stride);
     const long long row_blocks = ceil_div(nx, BM);
     const long long col_tiles = ceil_div(nc, BN);
     // Column shares: enough CTAs for a few waves of the SMs, at least 8 tiles per CTA so
@@ -856,17 +980,19 @@ void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const fl
     splits = (col_tiles + per - 1) / per;
     if (row_blocks > 0x7fffffffLL) throw CudaError("tc_filter: too many row blocks");
     dim3 grid((unsigned)row_blocks, (unsigned)splits);
-    if (ip) {
-        check(cudaFuncSetAttribute(tc_filter_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ARG_SMEM),
-              "cudaFuncSetAttribute(tc_filter)");
-        tc_filter_kernel<true><<<grid, ARG_THREADS, ARG_SMEM, st>>>(mx, mc, (int)nx, (int)nc, dim, per, xn, cn, cs,
-                                                                   cmax, tau, col_off, cand, cand_cnt, cap, err);
-    } else {
-        check(cudaFuncSetAttribute(tc_filter_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ARG_SMEM),
-              "cudaFuncSetAttribute(tc_filter)");
-        tc_filter_kernel<false><<<grid, ARG_THREADS, ARG_SMEM, st>>>(mx, mc, (int)nx, (int)nc, dim, per, xn, cn, cs,
-                                                                    cmax, tau, col_off, cand, cand_cnt, cap, err);
-    }
+#define VGPU_FILTER_LAUNCH(IPV, AUGV)                                                                            \
+    do {                                                                                                         \
+        check(cudaFuncSetAttribute(tc_filter_kernel<IPV, AUGV>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                   FILT_SMEM),                                                                   \
+              "cudaFuncSetAttribute(tc_filter)");                                                                \
+        tc_filter_kernel<IPV, AUGV><<<grid, ARG_THREADS, FILT_SMEM, st>>>(mx, mc, (int)nx, (int)nc, dim, per, xn, \
+                                                                         cn, cs, cmax, tau, col_off, cand,       \
+                                                                         cand_cnt, cap, err);                    \
+    } while (0)
+    if (ip) VGPU_FILTER_LAUNCH(true, false);
+    else if (aug) VGPU_FILTER_LAUNCH(false, true);
+    else VGPU_FILTER_LAUNCH(false, false);
+#undef VGPU_FILTER_LAUNCH
     check(cudaGetLastError(), "tc_filter_kernel");
 }
 

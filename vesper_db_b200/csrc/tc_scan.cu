@@ -1154,15 +1154,7 @@ __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict_
         float4* dst = reinterpret_cast<float4*>(lut);
         for (int i = threadIdx.x; i < m * 64; i += 256) dst[i] = __ldg(src + i);
     }
-    if (threadIdx.x == 0) {
-        uint32_t ep = 0;
-        for (int t = 0; t < nprobe; ++t) {
-            const uint32_t l = probe[q * nprobe + t];
-            eprefix[t] = ep;
-            ep += (uint32_t)(offs[l + 1] - offs[l]);
-        }
-        eprefix[nprobe] = ep;
-    }
+    if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nprobe, offs, nullptr, eprefix, nullptr);
     __syncthreads();
     const int p2 = next_pow2(n < 2 ? 2 : (int)n);
     for (int i = threadIdx.x; i < p2; i += 256) {

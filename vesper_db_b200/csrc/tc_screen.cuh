@@ -6,13 +6,27 @@
 
 namespace vgpu {
 
-// Screening error bound.  tf32 truncation of both operands (relative 2^-10 each), fp32
-// accumulation over dim products, fp32 rounding of the epilogue and of the norms, and
-// the reference-order rounding of d_ref; times a safety factor of 2.
+// Relative error of a tf32 dot product against ||x|| ||c||: truncation of both operands
+// (2^-10 each) and fp32 accumulation over up to dim + 16 terms (the products and the
+// two norm terms of the augmented screen below), with 0.4 % headroom.
+__host__ __device__ __forceinline__ float screen_a(int dim) {
+    return 1.953125e-3f + (float)(dim + 16) * 1.1920929e-7f * 1.00390625f;
+}
+// The augmented L2 screen folds -||c||^2 / 2 into the product as two tf32 terms
+// (hi + lo, residual below 2^-21 ||c||^2) that are accumulated with the others: their
+// share of the accumulation error plus the residual, per unit of ||c||^2.
+__host__ __device__ __forceinline__ float screen_r2(int dim) {
+    return (float)(dim + 16) * 5.9604645e-8f * 1.00390625f + 4.7683716e-7f;
+}
+
+// Screening error bound of an L2 screen value Dt (||x||^2 + ||c||^2 - 2 S, or
+// ||x||^2 - 2 S' with the augmented S' = S - ||c||^2 / 2): the tf32 product, the
+// augmented norm terms, fp32 rounding of the epilogue and of the norms, and the
+// reference-order rounding of d_ref; times a safety factor of 2.
 __device__ __forceinline__ float screen_eps(float xn, float cn, float dt, int dim) {
-    const float a = 1.953125e-3f + (float)(dim + 8) * 1.1920929e-7f;   // 2^-9 + (dim+8) 2^-23
+    const float a = screen_a(dim);
     const float xc = sqrtf(xn * cn);
-    const float e = 2.0f * a * xc + 2.384e-7f * (xn + cn + 2.0f * xc) +
+    const float e = 2.0f * a * xc + 2.0f * screen_r2(dim) * cn + 2.384e-7f * (xn + cn + 2.0f * xc) +
                     (float)(dim / 8 + 8) * 1.1920929e-7f * fabsf(dt);
     return 2.0f * e + 1e-30f;
 }
