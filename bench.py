@@ -102,6 +102,8 @@ def parse():
                     help="base vectors (multiple of the generated chunk: 125,000 rows, c5 6,250,000); "
                          "k-means: points")
     ap.add_argument("--nq", type=int, default=0, help="queries in the batch")
+    ap.add_argument("--no-tau-exchange", action="store_true",
+                    help="several GPUs: each shard keeps its own k-th-distance bounds (no threshold exchange)")
     ap.add_argument("--scan", default="auto", choices=["auto", "tc", "blocked"],
                     help="FAST scan kernel: the engine's choice, the tensor-core list scan or the blocked scan")
     args = ap.parse_args()
@@ -786,7 +788,7 @@ def main_c5(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
     from vesper_db_b200 import IvfPqIndex
-    from vesper_db_b200.shard import chunks_of, merge_topk, probed_search
+    from vesper_db_b200.shard import ShardResults, ThresholdExchange, chunks_of, merge_topk, probed_search
     shard_world = world if ours else 1
     n_chunks = C5_N // C5_CHUNK
     my_chunks = chunks_of(rank if ours else 0, shard_world, n_chunks)
@@ -848,18 +850,25 @@ def main_c5(args):
     if args.impl == "reference":
         return c5_reference_arm(args, index, queries.cpu().numpy(), gt_rows, gt_np, build, list_stats_c5)
 
-    out_ids = torch.empty((C5_NQ, C5_K), dtype=torch.int64, device=dev)
-    out_d = torch.empty((C5_NQ, C5_K), dtype=torch.float32, device=dev)
-    out_n = torch.empty(C5_NQ, dtype=torch.int32, device=dev)
-    slot = torch.arange(C5_K, device=dev)[None, :]
-    probe_bufs = {}
+    probe_bufs, phase, tau_x = {}, {}, None
+    if world > 1:
+        shard_res = ShardResults(C5_NQ, C5_K, dev)
+        out_ids, out_d, out_n = shard_res.ids, shard_res.dist, shard_res.counts
+        if not args.no_tau_exchange:
+            tau_x = ThresholdExchange().install(index)
+    else:
+        out_ids = torch.empty((C5_NQ, C5_K), dtype=torch.int64, device=dev)
+        out_d = torch.empty((C5_NQ, C5_K), dtype=torch.float32, device=dev)
+        out_n = torch.empty(C5_NQ, dtype=torch.int32, device=dev)
 
-    def one_search(q):
+    def one_search(q, local=None):
         if world > 1:
-            probed_search(index, q, C5_K, C5_NPROBE, C5_NLIST, out_ids, out_d, out_n, probe_bufs)
-            d = torch.where(slot < out_n[:, None], out_d, torch.full_like(out_d, float("inf")))
-            md, mi = merge_topk(d, out_ids, C5_K)
-            return md, mi, torch.isfinite(md).sum(1)
+            probed_search(index, q, C5_K, C5_NPROBE, C5_NLIST, out_ids, out_d, out_n, probe_bufs, local=local,
+                          times=phase)
+            t0 = time.perf_counter()
+            md, mi, mn = shard_res.merge()
+            phase["merge_ms"] = phase.get("merge_ms", 0.0) + (time.perf_counter() - t0) * 1e3
+            return md, mi, mn
         index.search_batch_device(q.data_ptr(), C5_NQ, C5_K, C5_NPROBE, out_ids.data_ptr(), out_d.data_ptr(),
                                   out_n.data_ptr())
         return out_d, out_ids, out_n
@@ -873,6 +882,7 @@ def main_c5(args):
         one_search(queries)
     barrier()
     steps_t, launches = [], 0
+    phase.clear()
     with ClockSampler(local) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
@@ -896,19 +906,33 @@ def main_c5(args):
     recall = recall_at(gi_all[gt_rows], gt_np, C5_K)
     stage_ms = {k2: sum(t[k2] for t in steps_t) / len(steps_t) for k2 in steps_t[0] if k2.endswith("_ms")}
     timings = steps_t[-1]
+    shard_phase = None
+    if world > 1:
+        shard_phase = {k2: v / args.steps for k2, v in phase.items()}
+        names = sorted(stage_ms)
+        tt = torch.tensor([stage_ms[n] for n in names], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        shard_phase["stage_ms_max_over_ranks"] = dict(zip(names, tt.tolist()))
+        shard_phase["threshold_exchange"] = tau_x is not None
 
-    # e2e: pinned host queries in, merged results to the host, every step
+    # e2e: pinned host queries in (one GPU: the whole batch; several: each rank its
+    # slice, all-gathered with the probe lists), merged results to the host, every step
     q_host = torch.empty((C5_NQ, C5_DIM), dtype=torch.float32, pin_memory=True)
     q_host.copy_(queries)
     q_dev = torch.empty_like(queries)
+    per = C5_NQ // world
+    q_local = torch.empty((per, C5_DIM), dtype=torch.float32, device=dev) if world > 1 else None
     e2e_ms = []
     for s in range(args.warmup + args.steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         e0.record()
-        q_dev.copy_(q_host, non_blocking=True)
+        if world > 1:
+            q_local.copy_(q_host[rank * per:(rank + 1) * per], non_blocking=True)
+        else:
+            q_dev.copy_(q_host, non_blocking=True)
         torch.cuda.current_stream().synchronize()
-        md, mi, _ = one_search(q_dev)
+        md, mi, _ = one_search(q_dev, local=q_local)
         if rank == 0:
             mi.cpu(), md.cpu()
         e1.record()
@@ -952,10 +976,11 @@ def main_c5(args):
            "recall@100": recall, "recall_queries": C5_GT_Q,
            "e2e": {"value": C5_NQ / (e2e_step / 1e3), "unit": "queries/s", "h2d_bytes_per_step": C5_NQ * C5_DIM * 4,
                    "d2h_bytes_per_step": C5_NQ * C5_K * 12, "ms_per_step": e2e_step,
-                   "path": "pinned H2D of the batch, search (probe exchange, shard search, NCCL merge at N>1), "
+                   "path": "pinned H2D of the batch (N>1: each rank its slice, all-gathered with the probe "
+                           "lists), search (N>1: threshold exchange, packed result all-gather, device merge), "
                            "rank 0 copies the merged result to the host"},
            "gpu_launches": launches, "roofline": roofline, "stage_ms": stage_ms,
-           "outside_engine_ms": ms_step - stage_ms["total_ms"],
+           "outside_engine_ms": ms_step - stage_ms["total_ms"], "shard_phase_ms": shard_phase,
            "coarse_kernel": COARSE_KERNELS.get(timings["coarse_variant"], "?"), "build": build,
            "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -966,6 +991,8 @@ def main_c5(args):
                                    "sample": f"unavailable: {e}"}
     if rank == 0:
         print(json.dumps(out))
+    if world > 1:
+        index.set_threshold_exchange(None)
     index.close()
     if world > 1:
         dist.barrier()
@@ -1211,29 +1238,36 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
 
-    from vesper_db_b200.shard import merge_topk, probed_search
+    from vesper_db_b200.shard import ShardResults, ThresholdExchange, probed_search
     index, queries, gt_np, build = build_ivfpq_workload(args, torch, dev, world, rank)
     q_np = queries.cpu().numpy()
     if args.impl == "reference":
         return reference_arm(args, index, q_np, gt_np, build)
 
     # ------------------------------------------------------------------ our arm
-    out_ids = torch.empty((NQ, K), dtype=torch.int64, device=dev)
-    out_d = torch.empty((NQ, K), dtype=torch.float32, device=dev)
-    out_n = torch.empty(NQ, dtype=torch.int32, device=dev)
-    slot = torch.arange(K, device=dev)[None, :]
-
     # Multi-GPU: each rank probes 1/world of the batch (the coarse stage is the same on
-    # every shard) and the probe lists are all-gathered before the shard searches.
-    probe_bufs = {}
+    # every shard) and the probe lists are all-gathered before the shard searches; the
+    # shards share their per-query k-th-distance bounds (threshold exchange, an
+    # all-reduce MIN inside the search) and their packed results are all-gathered and
+    # merged on the device.
+    probe_bufs, phase, tau_x = {}, {}, None
+    if world > 1:
+        shard_res = ShardResults(NQ, K, dev)
+        out_ids, out_d, out_n = shard_res.ids, shard_res.dist, shard_res.counts
+        if not args.no_tau_exchange:
+            tau_x = ThresholdExchange().install(index)
+    else:
+        out_ids = torch.empty((NQ, K), dtype=torch.int64, device=dev)
+        out_d = torch.empty((NQ, K), dtype=torch.float32, device=dev)
+        out_n = torch.empty(NQ, dtype=torch.int32, device=dev)
 
-    def one_search(q, nprobe):
+    def one_search(q, nprobe, local=None):
         if world > 1:
-            probed_search(index, q, K, nprobe, NLIST, out_ids, out_d, out_n, probe_bufs)
-            # padded slots (fewer than k results on this shard) must not win the merge
-            d = torch.where(slot < out_n[:, None], out_d, torch.full_like(out_d, float("inf")))
-            md, mi = merge_topk(d, out_ids, K)
-            return md, mi, torch.isfinite(md).sum(1)
+            probed_search(index, q, K, nprobe, NLIST, out_ids, out_d, out_n, probe_bufs, local=local, times=phase)
+            t0 = time.perf_counter()
+            md, mi, mn = shard_res.merge()
+            phase["merge_ms"] = phase.get("merge_ms", 0.0) + (time.perf_counter() - t0) * 1e3
+            return md, mi, mn
         index.search_batch_device(q.data_ptr(), NQ, K, nprobe, out_ids.data_ptr(), out_d.data_ptr(),
                                   out_n.data_ptr())
         return out_d, out_ids, out_n
@@ -1247,6 +1281,7 @@ def main():
         one_search(queries, NPROBE)
     barrier()
     steps_t, launches = [], 0
+    phase.clear()
     with ClockSampler(local) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
@@ -1270,6 +1305,16 @@ def main():
     recall = recall_at(res_i.cpu().numpy(), gt_np, K)
     stage_ms = {k2: sum(t[k2] for t in steps_t) / len(steps_t) for k2 in steps_t[0] if k2.endswith("_ms")}
     timings = steps_t[-1]
+    shard_phase = None
+    if world > 1:
+        # host-side time per step of the sharded search's phases (rank 0; the library's
+        # calls are synchronous, the merge is only queued), and the slowest rank's stages
+        shard_phase = {k2: v / args.steps for k2, v in phase.items()}
+        names = sorted(stage_ms)
+        tt = torch.tensor([stage_ms[n] for n in names], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        shard_phase["stage_ms_max_over_ranks"] = dict(zip(names, tt.tolist()))
+        shard_phase["threshold_exchange"] = tau_x is not None
 
     # nprobe sweep: SWEEP_PASSES timed passes per nprobe, recall of the last pass
     sweep, gpu_results = [], {}
@@ -1295,12 +1340,15 @@ def main():
 
     # e2e: host query buffer in, host result out, every step.  One GPU: the reference's
     # C call vesper_ivfpq_search_batch with host buffers (copies inside the library).
-    # Several GPUs: each rank copies the batch from pinned host memory, runs the sharded
-    # search (probe exchange, shard search, merge) and rank 0 reads the merged result.
+    # Several GPUs: each rank copies its 1/world slice of the batch from pinned host
+    # memory, the slices travel with the probe exchange (NVLink), the sharded search
+    # runs, and rank 0 reads the merged result.
     q_host = torch.empty((NQ, DIM), dtype=torch.float32, pin_memory=True)
     q_host.copy_(queries)
     q_host_np = q_host.numpy()
     q_dev = torch.empty_like(queries)
+    per = NQ // world
+    q_local = torch.empty((per, DIM), dtype=torch.float32, device=dev)
     e2e_ms = []
     for s in range(args.warmup + args.steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1309,9 +1357,9 @@ def main():
         if world == 1:
             index.search_batch_c(q_host_np, K, NPROBE)
         else:
-            q_dev.copy_(q_host, non_blocking=True)
+            q_local.copy_(q_host[rank * per:(rank + 1) * per], non_blocking=True)
             torch.cuda.current_stream().synchronize()   # the library's stream does not wait on torch's
-            md, mi, _ = one_search(q_dev, NPROBE)
+            md, mi, _ = one_search(q_dev, NPROBE, local=q_local)
             if rank == 0:
                 mi.cpu(), md.cpu()
         e1.record()
@@ -1372,12 +1420,15 @@ def main():
         "e2e": {"value": NQ / (e2e_step / 1e3), "unit": "queries/s", "h2d_bytes_per_step": NQ * DIM * 4,
                 "d2h_bytes_per_step": NQ * K * 12, "ms_per_step": e2e_step,
                 "path": "vesper_ivfpq_search_batch (host buffers)" if world == 1 else
-                        "per rank: pinned H2D of the batch, probe exchange, shard search, NCCL merge; "
-                        "rank 0 copies the merged result to the host"},
+                        "per rank: pinned H2D of its 1/world slice of the batch, probe of the slice, NCCL "
+                        "all-gather of the slices and probe lists, shard search with the threshold exchange, "
+                        "NCCL all-gather of the packed results and the device merge; rank 0 copies the merged "
+                        "result to the host (h2d bytes summed over the ranks)"},
         "gpu_launches": launches,
         "roofline": roofline,
         "stage_ms": stage_ms,
         "outside_engine_ms": ms_step - stage_ms["total_ms"],
+        "shard_phase_ms": shard_phase,
         "coarse_kernel": COARSE_KERNELS.get(timings["coarse_variant"], "?"),
         "build": build,
         "clocks": clk.summary(),
@@ -1393,6 +1444,8 @@ def main():
                                    "kind": "reference", "sample": f"unavailable: {e}"}
     if rank == 0:
         print(json.dumps(out))
+    if world > 1:
+        index.set_threshold_exchange(None)
     index.close()
     if world > 1:
         dist.barrier()

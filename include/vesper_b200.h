@@ -135,6 +135,41 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
     const uint32_t* d_probe, const float* d_probe_d, uint64_t* d_out_ids, float* d_out_distances,
     uint32_t* d_out_counts);
 
+/* Threshold exchange between the shards of one database.  No counterpart in the
+ * reference (it has one index per process).  Several indexes, one per GPU, each hold a
+ * part of the base set and search the same batch with the same parameters; with an
+ * exchange set on each, every batch search (plain, device or probed; not the
+ * allocation-free one) calls fn once per query chunk, on the calling thread, with d_tau
+ * [n_queries] float on the index's device -- each query's upper bound of its k-th FAST
+ * distance over this index's shard, +inf where it has none -- and the index's CUDA
+ * stream (a cudaStream_t).  fn must leave the element-wise minimum over all shards in
+ * d_tau, ordered on that stream (an all-reduce MIN issued on it), and return 0; any
+ * other value fails the search with VESPER_ERROR_INVALID_PARAM.  The tensor-core list
+ * scan then keeps only entries that can reach the shared bound, so each shard refines
+ * about its share of the union's candidates; the union's top k (the per-shard results
+ * merged) is unchanged.  Searches that do not run the list scan pass +inf for every
+ * query, so the calls of all shards pair up.  fn must not call back into the index.
+ * fn = NULL removes the exchange. */
+typedef int (*vesper_ivfpq_tau_exchange_fn)(float* d_tau, size_t n_queries, void* cuda_stream, void* user);
+VESPER_C_API vesper_status_t vesper_ivfpq_set_threshold_exchange(vesper_index_t* index,
+                                                                 vesper_ivfpq_tau_exchange_fn fn, void* user);
+
+/* Merge of per-shard results on the device.  No counterpart in the reference (one
+ * index per process).  For a database split across GPUs, each shard's batch search
+ * returns per query up to k results sorted by distance (ids [nq x k], distances
+ * [nq x k], counts [nq]); after an all-gather, part p's arrays start at d_dist +
+ * p * dist_stride, d_ids + p * ids_stride and d_counts + p * counts_stride (strides in
+ * elements of each array).  Writes per query the k smallest over all parts -- ties to
+ * the lower part, then the earlier slot -- with slots past d_out_counts[q] padded like
+ * vesper_ivfpq_search_batch (id 0, the last distance).  d_out_counts may be NULL.
+ * 1 <= parts <= 64.  Device pointers; the kernel is queued on cuda_stream (a
+ * cudaStream_t, NULL = the legacy default stream) and the call does not wait for it. */
+VESPER_C_API vesper_status_t vesper_topk_merge_device(uint32_t parts, size_t nq, uint32_t k, const float* d_dist,
+                                                     size_t dist_stride, const uint64_t* d_ids, size_t ids_stride,
+                                                     const uint32_t* d_counts, size_t counts_stride,
+                                                     uint64_t* d_out_ids, float* d_out_distances,
+                                                     uint32_t* d_out_counts, void* cuda_stream);
+
 /* ---------------------------------------------------------------------------------
  * The rest of IvfPqIndex's API (include/vesper/index/ivf_pq.hpp:252-386), which the
  * reference reaches from C++ only.  Vectors are rebuilt exactly as the reference does:

@@ -144,3 +144,42 @@ def test_probed_search_gathers_every_slice(tmp_path):
         got = np.load(f"{out}.{r}.npz")
         assert np.array_equal(got["ids"], exp_ids) and np.array_equal(got["d"], exp_d)
     del fake
+
+
+def _tau_worker(rank, world, port, out_path):
+    import ctypes as C
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from vesper_db_b200.shard import ThresholdExchange
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        inf = np.float32(np.inf)
+        vals = [np.array([1.0, inf, 5.0, inf, -2.0], np.float32),
+                np.array([3.0, 4.0, 2.0, inf, -1.0], np.float32)][rank]
+
+        def view(ptr, n):
+            return torch.from_numpy(np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), (n,)))
+
+        tx = ThresholdExchange(view=view)
+        rc = tx(vals.ctypes.data, vals.size, None, None)
+        np.savez(f"{out_path}.{rank}", vals=vals, rc=rc, calls=tx.calls)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_threshold_exchange_takes_the_minimum_over_ranks(tmp_path):
+    """The exchange callback leaves the element-wise minimum of every rank's bounds in
+    the library's buffer (+inf where no rank has a bound) and reports success."""
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "tau")
+    mp.start_processes(_tau_worker, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    for r in range(2):
+        got = np.load(f"{out}.{r}.npz")
+        assert int(got["rc"]) == 0 and int(got["calls"]) == 1
+        assert np.array_equal(got["vals"], np.array([1.0, 4.0, 2.0, np.inf, -2.0], np.float32))

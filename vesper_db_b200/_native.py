@@ -37,6 +37,7 @@ EXPORTED = [
     "vesper_kmeans_params_init", "vesper_kmeans_fit", "vesper_kmeans_fit_device",
     "vesper_flat_topk", "vesper_flat_topk_device", "vesper_flat_get_last_timings",
     "vesper_ivfpq_probe_device", "vesper_ivfpq_search_batch_device_probed",
+    "vesper_ivfpq_set_threshold_exchange", "vesper_topk_merge_device",
     "vesper_ivfpq_reconstruct", "vesper_ivfpq_reconstruct_cluster", "vesper_ivfpq_get_cluster_assignment",
     "vesper_ivfpq_get_cluster_centroid", "vesper_ivfpq_update_cluster_centroid", "vesper_ivfpq_reassign_vector",
     "vesper_ivfpq_compact_inverted_list", "vesper_ivfpq_debug_explain_centroid_rank",
@@ -51,6 +52,10 @@ EXPORTED = [
     "vesper_mgr_disk_usage", "vesper_mgr_set_memory_budget_mb", "vesper_mgr_get_memory_budget_mb",
     "vesper_mgr_get_stats", "vesper_mgr_set_search_mode",
 ]
+
+# int fn(float* d_tau, size_t n_queries, void* cuda_stream, void* user)
+# (vesper_ivfpq_set_threshold_exchange)
+TAU_EXCHANGE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
 
 INDEX_HNSW = 0
 INDEX_IVF_PQ = 1
@@ -218,6 +223,9 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_ivfpq_probe_device": (st, [vp, vp, C.c_size_t, C.c_uint32, vp, vp]),
             "vesper_ivfpq_search_batch_device_probed": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx), vp, vp,
                                                              vp, vp, vp]),
+            "vesper_ivfpq_set_threshold_exchange": (st, [vp, TAU_EXCHANGE_FN, vp]),
+            "vesper_topk_merge_device": (st, [C.c_uint32, C.c_size_t, C.c_uint32, vp, C.c_size_t, vp, C.c_size_t,
+                                              vp, C.c_size_t, vp, vp, vp, vp]),
             "vesper_ivfpq_reconstruct": (st, [vp, C.c_uint64, f32p]),
             "vesper_ivfpq_reconstruct_cluster": (st, [vp, C.c_uint32, u64p, f32p, C.c_size_t,
                                                       C.POINTER(C.c_size_t)]),

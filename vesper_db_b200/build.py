@@ -54,24 +54,29 @@ def _run(cmd):
 def build(verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     deps = _headers()
-    objs, changed = [], False
+    objs, jobs = [], []
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")
         if _stale(obj, src, deps):
-            if verbose:
-                print("nvcc", os.path.basename(src), flush=True)
-            _run([NVCC, *NVCC_FLAGS, "-c", src, "-o", obj])
-            changed = True
+            jobs.append(("nvcc", [NVCC, *NVCC_FLAGS, "-c", src, "-o", obj]))
         objs.append(obj)
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cpp"))):
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")
         if _stale(obj, src, deps):
-            if verbose:
-                print("g++ ", os.path.basename(src), flush=True)
-            _run([CXX, *CXX_FLAGS, "-c", src, "-o", obj])
-            changed = True
+            jobs.append(("g++ ", [CXX, *CXX_FLAGS, "-c", src, "-o", obj]))
         objs.append(obj)
-    if changed or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
+    if jobs:
+        # translation units are independent: compile them concurrently
+        from concurrent.futures import ThreadPoolExecutor
+
+        def one(job):
+            if verbose:
+                print(job[0], os.path.basename(job[1][-3]), flush=True)
+            return _run(job[1])
+
+        with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as pool:
+            list(pool.map(one, jobs))
+    if jobs or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
         _run([NVCC, "-shared", "-Xlinker", "--no-undefined", "-gencode", "arch=compute_100a,code=sm_100a", "-cudart", "static",
               "-o", LIB, *objs, "-lpthread", "-ldl", "-lrt"])
     return LIB

@@ -128,6 +128,7 @@ public:
     std::vector<uint64_t> h_offs;   // [nlist + 1]
 
     DeviceBuffer<float> d_cent, d_cb, d_rot, d_rotT, d_rc, d_cn;
+    DeviceBuffer<float> d_rot3;   // [dim x 3 dim]: R split for the tensor-core query rotation
     mutable DeviceBuffer<int> d_err;
     mutable DeviceBuffer<float> w_xn, w_cn;
     DeviceBuffer<uint64_t> d_offs, d_ids;
@@ -144,12 +145,16 @@ public:
     DeviceBuffer<float> d_xnorm;
     mutable vgpu::TlWork tlw;
     mutable DeviceBuffer<float> w_pbase;
+    // threshold exchange between shards (set_threshold_exchange)
+    IvfPqIndex::ThresholdExchangeFn tau_fn = nullptr;
+    void* tau_user = nullptr;
+    mutable DeviceBuffer<float> w_tau_inf;
 
     double t_assign_ms = 0, t_encode_ms = 0, t_lists_ms = 0;
     mutable SearchTimings timings;
 
     // search workspace (grow-only), guarded by mu
-    mutable DeviceBuffer<float> w_q, w_D, w_probe_d, w_rq, w_rres, w_cand_d, w_out_d, w_T;
+    mutable DeviceBuffer<float> w_q, w_D, w_probe_d, w_rq, w_rq3, w_rres, w_cand_d, w_out_d, w_T;
     mutable DeviceBuffer<uint32_t> w_probe, w_cand_pos, w_cand_n, w_out_n, w_pair_q;
     mutable DeviceBuffer<uint64_t> w_out_ids;
     mutable DeviceBuffer<unsigned long long> w_scanned;
@@ -184,9 +189,16 @@ public:
             vgpu::launch_transpose(d_rot.data(), (int)dim, d_rotT.data(), st);
             d_rc.resize(h_cent.size());
             vgpu::launch_rotate_fast(d_cent.data(), nlist(), (int)dim, d_rot.data(), d_rc.data(), st);
+            if (vgpu::rotate_3xtf32_supported((int)dim)) {
+                d_rot3.resize(dim * dim * 3);
+                vgpu::prepare_rotation_3xtf32(d_rot.data(), (int)dim, d_rot3.data(), st);
+            } else {
+                d_rot3.release();
+            }
         } else {
             d_rot.release();
             d_rotT.release();
+            d_rot3.release();
             d_rc.resize(h_cent.size());
             d2d(d_rc.data(), d_cent.data(), h_cent.size(), st);
         }
@@ -244,6 +256,15 @@ public:
     // FAST-scan kernel for this call: the tensor-core list scan where the shapes allow
     // it and the batch scans enough entries per query to amortise its set-up, else the
     // blocked scan.  VGPU_SCAN=tc / blocked overrides the choice.
+    // VGPU_ROTATE=seq keeps FAST search on the sequential fp32 rotation kernel.
+    bool use_rotation_gemm() const {
+        static const bool off = [] {
+            const char* v = std::getenv("VGPU_ROTATE");
+            return v && std::string(v) == "seq";
+        }();
+        return !off && d_rot3.size() > 0;
+    }
+
     bool use_list_scan(size_t nq, uint32_t np) const {
         if (!has_blocks || np < 2 || !vgpu::tc_list_scan_supported((int)dim, (int)m(), (int)ksub)) return false;
         const char* v = std::getenv("VGPU_SCAN");
@@ -1158,6 +1179,13 @@ public:
             w_T.reserve(qc * (size_t)m() * ksub);
             w_pbase.reserve(qc * np);
         }
+        // FAST search rotates the queries with one tensor-core GEMM (3xTF32); EXACT
+        // search keeps the reference's sequential rotation.
+        const bool rot_gemm = !exact && has_rot && use_rotation_gemm();
+        if (rot_gemm) {
+            w_rq3.reserve(qc * dim * 3);
+            reset_err();
+        }
         const bool list_scan = !exact && use_list_scan(nq, np);
         const bool split_scan = !exact && !list_scan && has_blocks && use_split_scan();
         if (list_scan) {
@@ -1239,7 +1267,11 @@ public:
                                    (int)k, probe, d_offs.data(), d_ids.data(), oid, od, on, st);
             } else {
                 const float* rq = dq;
-                if (has_rot) {
+                if (rot_gemm) {
+                    vgpu::launch_rotate_3xtf32(dq, (long long)nc, (int)dim, d_rot3.data(), w_rq3.data(), w_rq.data(),
+                                               d_err.data(), st);
+                    rq = w_rq.data();
+                } else if (has_rot) {
                     vgpu::launch_rotate_fast(dq, (long long)nc, (int)dim, d_rot.data(), w_rq.data(), st);
                     rq = w_rq.data();
                 }
@@ -1257,6 +1289,7 @@ public:
                         a.vterm = d_vterm.data(); a.xnorm = d_xnorm.data(); a.cbb = d_cbb.data();
                         a.blk_off = d_blk_off.data(); a.bcodes = d_bcodes.data(); a.bvterm = d_bvterm.data();
                         a.ids = d_ids.data(); a.out_ids = oid; a.out_d = od; a.out_n = on; a.err = d_err.data();
+                        a.tau_fn = tau_fn; a.tau_user = tau_user;
                         vgpu::launch_tc_list_scan(a, tlw, st);
                     } else if (split_scan) {
                         vgpu::launch_scan_blocked_split(w_T.data(), (long long)nc, w_pbase.data(), probe,
@@ -1280,9 +1313,16 @@ public:
                 }
                 cudaEventRecord(ev[4], st);
             }
+            if (tau_fn && !list_scan) {
+                // this shard has no bound to offer, but the shards' calls must pair up
+                w_tau_inf.reserve(qc);
+                vgpu::launch_fill(w_tau_inf.data(), (long long)nc, __builtin_inff(), st);
+                if (tau_fn(w_tau_inf.data(), nc, st, tau_user) != 0)
+                    throw vgpu::CudaError("search: the threshold exchange failed");
+            }
             cudaEventRecord(ev[5], st);
             tm.kernel_launches += (ext_probe ? 1 : filt ? 1 + (uint32_t)w_flat.last.launches : 3) + (exact ? 2 : 2) +
-                                  (has_rot ? 1 : 0) + (tc && !filt ? 1 : 0) + (!exact && has_blocks ? 1 : 0) +
+                                  (has_rot ? (rot_gemm ? 2 : 1) : 0) + (tc && !filt ? 1 : 0) + (!exact && has_blocks ? 1 : 0) +
                                   (list_scan ? 12 : 0);
             tm.scan_variant = exact ? 1u : list_scan ? 4u : (has_blocks ? 3u : 2u);
             tm.coarse_variant = filt ? 3u : tc ? 2u : 1u;
@@ -1292,7 +1332,7 @@ public:
                 if (out_n) d2h(out_n + q0, on, nc, st);
             }
             sync(st);
-            if ((tc && !filt) || list_scan) check_err();
+            if ((tc && !filt) || list_scan || rot_gemm) check_err();
             float a = 0;
             cudaEventElapsedTime(&a, ev[0], ev[1]); tm.coarse_ms += a;
             cudaEventElapsedTime(&a, ev[1], ev[2]); tm.select_ms += a;
@@ -1490,6 +1530,12 @@ auto IvfPqIndex::search_batch_flat(const float* queries, std::size_t n_queries,
     }
 }
 
+void IvfPqIndex::set_threshold_exchange(ThresholdExchangeFn fn, void* user) {
+    std::lock_guard<std::mutex> lk(impl_->mu);
+    impl_->tau_fn = fn;
+    impl_->tau_user = fn ? user : nullptr;
+}
+
 auto IvfPqIndex::probe_device(const float* d_queries, std::size_t n_queries, std::uint32_t nprobe,
                               std::uint32_t* d_probe, float* d_probe_d) const -> std::expected<void, core::error> {
     DeviceGuard g(impl_->dev);
@@ -1558,7 +1604,7 @@ auto IvfPqIndex::get_stats() const noexcept -> Stats {
     s.n_lists = I.params.nlist;
     s.m = I.params.m;
     s.code_size = I.params.m;
-    s.memory_bytes = sizeof(Impl) + I.d_cent.bytes() + I.d_cb.bytes() + I.d_rot.bytes() + I.d_rotT.bytes() +
+    s.memory_bytes = sizeof(Impl) + I.d_cent.bytes() + I.d_cb.bytes() + I.d_rot.bytes() + I.d_rotT.bytes() + I.d_rot3.bytes() +
                      I.d_rc.bytes() + I.d_offs.bytes() + I.d_ids.bytes() + I.d_codes.bytes() + I.d_vterm.bytes() +
                      I.d_blk_off.bytes() + I.d_bcodes.bytes() + I.d_bvterm.bytes() + I.d_cbb.bytes() +
                      I.d_xnorm.bytes();

@@ -164,6 +164,20 @@ public:
                                     float* d_out_dist, std::uint32_t* d_out_counts) const
         -> std::expected<void, core::error>;
 
+    // Threshold exchange between the shards of one database (one index per GPU, each
+    // holding a part of the base set, all searching the same batch with the same
+    // parameters).  While set, every search calls fn once per query chunk, on the host,
+    // with d_tau [nq] on the index's device: each query's upper bound of its k-th FAST
+    // distance over this shard (+inf where the shard has none), and the index's CUDA
+    // stream.  fn must leave the element-wise minimum over all shards in d_tau, ordered
+    // on that stream (e.g. an all-reduce MIN issued on it), and return 0; any other
+    // return fails the search.  The tensor-core list scan then keeps only the entries
+    // that can reach the shared bound, so each shard refines about its share of the
+    // union's candidates; the union's top k is unchanged.  Searches that do not run the
+    // list scan pass +inf for every query.  fn = nullptr removes it.
+    using ThresholdExchangeFn = int (*)(float* d_tau, std::size_t n_queries, void* stream, void* user);
+    void set_threshold_exchange(ThresholdExchangeFn fn, void* user);
+
     // FAST-mode device search that allocates nothing: its temporary buffers come from
     // a fixed 64 MiB device array (noalloc_search.cu) instead of cudaMalloc.
     auto search_batch_device_noalloc(const float* d_queries, std::size_t n_queries,

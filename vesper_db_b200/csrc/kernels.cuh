@@ -9,6 +9,14 @@ namespace vgpu {
 constexpr int kMaxK = 1024;        // largest k / nprobe the selection kernels accept
 constexpr int kScanChunk = 2048;   // list entries scored per selection round
 
+// Per query, the k smallest of `parts` sorted per-shard top-k lists (shard_merge.cu):
+// part p's distances at dist + p dist_stride + q k, ids at ids + p ids_stride + q k,
+// counts at counts + p counts_stride + q; ties to the lower part, then the earlier
+// slot; slots past out_n padded with id 0 and the last distance.  parts <= 64.
+void launch_topk_merge(int parts, long long nq, int k, const float* dist, long long dist_stride, const uint64_t* ids,
+                       long long ids_stride, const uint32_t* counts, long long counts_stride, uint64_t* out_ids,
+                       float* out_d, uint32_t* out_n, cudaStream_t st);
+
 // D[i][j] = ||x_i - c_j||^2 in reference lane order, for i < nx, j < nc; D row stride ldd.
 void launch_l2_dist(const float* x, long long nx, const float* c, int nc, int dim, float* D,
                     long long ldd, cudaStream_t st);

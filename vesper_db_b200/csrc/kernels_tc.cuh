@@ -28,6 +28,14 @@ void launch_tc_screen_op(bool ip, const float* x, long long nx, const float* c, 
 void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, long long c_stride,
                       int dim, const float* xn, const float* cn, const float* cs, const float* tau, uint32_t col_off,
                       uint2* cand, uint32_t* cand_cnt, int cap, int* err, cudaStream_t st);
+// OPQ rotation of a query batch on the tensor cores (3xTF32, tc_coarse.cu): out[i] =
+// R x_i to a few 1e-7 relative (FAST search only; EXACT search, add() and training keep
+// the sequential fp32 rotation).  prepare_rotation_3xtf32 fills R3 [dim x 3 dim] once
+// per model; x3 is [n x 3 dim] scratch; err as for launch_tc_screen.
+bool rotate_3xtf32_supported(int dim);
+void prepare_rotation_3xtf32(const float* R, int dim, float* R3, cudaStream_t st);
+void launch_rotate_3xtf32(const float* x, long long n, int dim, const float* R3, float* x3, float* out, int* err,
+                          cudaStream_t st);
 // out[i] = sqrt(in[i]).
 void launch_sqrt(const float* in, long long n, float* out, cudaStream_t st);
 // Exact flat top-k (flat_topk.cu).  Stage times of the last call, in ms.
@@ -141,7 +149,7 @@ bool tc_list_scan_supported(int dim, int m, int ksub);
 // Per-batch scratch, grown on demand and reused.  bf16 arrays are held as uint16_t.
 struct TlWork {
     DeviceBuffer<uint16_t> rqb, qperm;
-    DeviceBuffer<float> rqn, tau, p1_d;
+    DeviceBuffer<float> rqn, tau, tau_x, p1_d;
     DeviceBuffer<uint64_t> p1_ids;
     DeviceBuffer<uint32_t> p1_n, cnt, cursor, seg_off, units, unit_off, unit_list, seg_meta, cand_cnt, counter;
     DeviceBuffer<uint32_t> p0, mcount, mins_off, run_lut;   // threshold pass over long nearest lists
@@ -189,6 +197,13 @@ struct TlScanArgs {
     float* out_d;
     uint32_t* out_n;
     int* err;
+    // Optional exchange of the per-query thresholds between the shards of one database
+    // (ThresholdExchangeFn, ivf_pq_gpu.hpp): called on the host after the threshold pass
+    // with tau_x [nq] on the device (+inf where this shard has no bound) and the stream;
+    // it must leave the element-wise minimum over every shard in tau_x, ordered on that
+    // stream, and return 0.
+    int (*tau_fn)(float* d_tau, size_t nq, void* stream, void* user) = nullptr;
+    void* tau_user = nullptr;
 };
 
 // FAST search results identical to launch_scan_blocked over all nprobe probes.

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(128, 1) tc_screen_kernel(const __grid_constant
     __syncthreads();
     if (s_fail == 0) {
         const int row = m0 + warp * 32 + lane;
-        const float rn = row < nx ? xn[row] : 0.0f;
+        const float rn = (row < nx && xn != nullptr) ? xn[row] : 0.0f;
         const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
         if constexpr (MODE <= 1) {
             for (int ch = 0; ch < BN / 32; ++ch) {
@@ -1006,6 +1006,65 @@ void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const
 __global__ void sqrt_kernel(const float* __restrict__ in, long long n, float* __restrict__ out) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = sqrtf(in[i]);
+}
+
+// ---------------------------------------------------------------------------------
+// OPQ rotation of a query batch as one tensor-core GEMM (3xTF32).
+//
+// out = X R^T with every fp32 operand split as v = hi(v) + lo(v): hi(v) = v rounded to
+// tf32 (10 mantissa bits, exact in a tf32 operand), lo(v) = v - hi(v) (exact in fp32,
+// |lo| <= 2^-11 |v|).  X R^T ~= hi(X) hi(R)^T + hi(X) lo(R)^T + lo(X) hi(R)^T is one
+// K = 3 dim contraction of X3 = [hi(X) | hi(X) | lo(X)] with R3 = [hi(R) | lo(R) | hi(R)]
+// on tc_screen_kernel (MODE 1 stores -2 S, so R3 carries a factor -1/2, which is exact).
+// Per term the error is about 2^-20 |x| |r| (the dropped lo lo product and the tf32
+// rounding of lo), against 2^-24 for an fp32 product, so the rotated query differs from
+// the sequential fp32 rotation by a few 1e-7 relative: well inside the 1e-4 relative
+// distance tolerance of FAST search, which is the only path that uses it.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ float tf32_hi(float v) {
+    const uint32_t b = __float_as_uint(v);
+    const float r = __uint_as_float((b + 0x1000u) & 0xffffe000u);  // round half away from zero on the magnitude
+    return isfinite(r) ? r : __uint_as_float(b & 0xffffe000u);
+}
+
+// order 0: [hi | hi | lo] (the row operand), 1: scale [hi | lo | hi] (the rotation).
+__global__ void tf32_split3_kernel(const float* __restrict__ x, long long n, int dim, int order, float scale,
+                                   float* __restrict__ out) {
+    const long long total = n * dim;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long row = e / dim;
+        const int c = (int)(e - row * dim);
+        const float v = x[e];
+        const float hi = tf32_hi(v), lo = v - hi;
+        float* o = out + row * 3 * dim + c;
+        if (order == 0) {
+            o[0] = hi; o[dim] = hi; o[2 * dim] = lo;
+        } else {
+            o[0] = scale * hi; o[dim] = scale * lo; o[2 * dim] = scale * hi;
+        }
+    }
+}
+
+bool rotate_3xtf32_supported(int dim) { return tc_screen_supported(3 * dim) && dim >= 32; }
+
+void prepare_rotation_3xtf32(const float* R, int dim, float* R3, cudaStream_t st) {
+    const long long total = (long long)dim * dim;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    tf32_split3_kernel<<<blocks, 256, 0, st>>>(R, dim, dim, 1, -0.5f, R3);
+    check(cudaGetLastError(), "tf32_split3_kernel");
+}
+
+void launch_rotate_3xtf32(const float* x, long long n, int dim, const float* R3, float* x3, float* out, int* err,
+                          cudaStream_t st) {
+    if (n <= 0) return;
+    if (!rotate_3xtf32_supported(dim)) throw CudaError("rotate_3xtf32: unsupported dimension");
+    const long long total = n * dim;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    tf32_split3_kernel<<<blocks, 256, 0, st>>>(x, n, dim, 0, 1.0f, x3);
+    check(cudaGetLastError(), "tf32_split3_kernel");
+    tc_screen_launch<1>(x3, n, R3, dim, 0, 3 * dim, nullptr, nullptr, out, dim, err, nullptr, nullptr, nullptr, 0, 0,
+                        st);
 }
 
 void launch_sqrt(const float* in, long long n, float* out, cudaStream_t st) {

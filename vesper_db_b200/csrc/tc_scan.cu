@@ -1046,6 +1046,25 @@ __global__ void tau_merge_kernel(const float* __restrict__ p1_d, const uint32_t*
     }
 }
 
+// Threshold exchange between shards: tau_x = tau where this shard has a bound, else
+// +inf; after the element-wise minimum over the shards, every query whose minimum is
+// finite takes it (and is screened, not sent to the fallback scan).  Any shard's bound
+// is an upper bound of the k-th distance over the union of the shards, so every entry
+// of the union's top k still passes each shard's keep rule.
+__global__ void tau_export_kernel(const float* __restrict__ tau, long long nq, float* __restrict__ tau_x) {
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x)
+        tau_x[q] = tau[q] > -FLT_MAX ? tau[q] : __int_as_float(0x7f800000);
+}
+
+__global__ void tau_import_kernel(const float* __restrict__ tau_x, long long nq, int cap, float* __restrict__ tau,
+                                  uint32_t* __restrict__ cand_cnt) {
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
+        const float t = tau_x[q];
+        if (t < __int_as_float(0x7f800000) && t > -FLT_MAX) tau[q] = fminf(tau[q] > -FLT_MAX ? tau[q] : t, t);
+        cand_cnt[q] = tau[q] > -FLT_MAX ? 0u : (uint32_t)cap + 1u;
+    }
+}
+
 __global__ void cand_stats_kernel(const uint32_t* __restrict__ cand_cnt, long long nq, uint32_t cap,
                                   unsigned long long* __restrict__ stats) {
     unsigned long long c = 0, f = 0;
@@ -1238,6 +1257,7 @@ void TlWork::reserve(long long nq, int nprobe, int nlist, int dim, int k, int ca
     unit_list.reserve(groups * (n_vectors / TL_M + (size_t)nlist + 1));
     rqb.reserve((size_t)nq * dim);
     tau.reserve(nq);
+    tau_x.reserve(nq);
     rqn.reserve(nq);
     cnt.reserve(nlist + 1);
     cursor.reserve(nlist + 1);
@@ -1426,6 +1446,14 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     tau_merge_kernel<<<gq, 256, 0, st>>>(w.p1_d.data(), w.p1_n.data(), w.run_lut.data(), a.nq, a.k, w.cap,
                                          w.tau.data(), w.cand_cnt.data());
     VGPU_LAUNCH("tau_merge_kernel");
+    if (a.tau_fn) {
+        tau_export_kernel<<<gq, 256, 0, st>>>(w.tau.data(), a.nq, w.tau_x.data());
+        VGPU_LAUNCH("tau_export_kernel");
+        if (a.tau_fn(w.tau_x.data(), (size_t)a.nq, st, a.tau_user) != 0)
+            throw CudaError("tc_list_scan: the threshold exchange failed");
+        tau_import_kernel<<<gq, 256, 0, st>>>(w.tau_x.data(), a.nq, w.cap, w.tau.data(), w.cand_cnt.data());
+        VGPU_LAUNCH("tau_import_kernel");
+    }
     check(cudaEventRecord(w.ev[1], st), "cudaEventRecord");
 
     // Pairs grouped by list; units per list; list-ordered query rows.

@@ -373,6 +373,16 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
     });
 }
 
+VESPER_C_API vesper_status_t vesper_ivfpq_set_threshold_exchange(vesper_index_t* index,
+                                                                 vesper_ivfpq_tau_exchange_fn fn, void* user) {
+    if (!index || !index->ivfpq) return VESPER_ERROR_INVALID_PARAM;
+    clear_error();
+    return guarded("set_threshold_exchange", [&] {
+        index->ivfpq->set_threshold_exchange(fn, user);
+        return VESPER_OK;
+    });
+}
+
 }  // extern "C"
 
 namespace {
@@ -906,6 +916,25 @@ VESPER_C_API vesper_status_t vesper_flat_get_last_timings(vesper_flat_timings_t*
     out->single_pass = (uint32_t)s.single_pass;
     out->kernel_launches = s.launches;
     return VESPER_OK;
+}
+
+VESPER_C_API vesper_status_t vesper_topk_merge_device(uint32_t parts, size_t nq, uint32_t k, const float* d_dist,
+                                                     size_t dist_stride, const uint64_t* d_ids, size_t ids_stride,
+                                                     const uint32_t* d_counts, size_t counts_stride,
+                                                     uint64_t* d_out_ids, float* d_out_distances,
+                                                     uint32_t* d_out_counts, void* cuda_stream) {
+    if (!d_dist || !d_ids || !d_counts || !d_out_ids || !d_out_distances || parts == 0 || parts > 64 || k == 0)
+        return VESPER_ERROR_INVALID_PARAM;
+    if (parts > 1 && (dist_stride < nq * k || ids_stride < nq * k || counts_stride < nq))
+        return VESPER_ERROR_INVALID_PARAM;
+    if (nq == 0) return VESPER_OK;
+    clear_error();
+    return guarded("topk_merge", [&] {
+        vgpu::launch_topk_merge((int)parts, (long long)nq, (int)k, d_dist, (long long)dist_stride, d_ids,
+                                (long long)ids_stride, d_counts, (long long)counts_stride, d_out_ids, d_out_distances,
+                                d_out_counts, static_cast<cudaStream_t>(cuda_stream));
+        return VESPER_OK;
+    });
 }
 
 VESPER_C_API int vesper_b200_device_count(void) {

@@ -40,13 +40,21 @@ def merge_topk(dist, ids, k: int, group=None):
 
 
 def probed_search(index, queries, k: int, nprobe: int, nlist: int, out_ids, out_d, out_n, bufs: dict,
-                  group=None, mode: int = 0):
+                  group=None, mode: int = 0, local=None, times: dict | None = None):
     """Search the whole batch over this rank's shard with the coarse stage split across
     ranks: rank r probes rows [r nq/W, (r+1) nq/W) (index.probe_device), the probe lists
     and distances are all-gathered, then index.search_batch_device_probed runs on the
     full batch.  queries [nq, dim] float32 and the outputs are tensors on the index's
     device; nq must be a multiple of the world size.  `bufs` caches the probe buffers
-    between calls."""
+    between calls.
+
+    local: this rank's rows of the batch, already on the device, when `queries` does not
+    hold the batch yet (a batch that arrives from the host: each rank copies only its
+    slice); the slices are all-gathered into `queries` after the probe.
+    times: if given, host-side milliseconds of the three phases are added to
+    times["probe_ms"], times["exchange_ms"] and times["search_ms"]."""
+    import time
+
     import torch
     import torch.distributed as dist_mod
 
@@ -65,15 +73,121 @@ def probed_search(index, queries, k: int, nprobe: int, nlist: int, out_ids, out_
                      torch.empty((nq // world, npq), dtype=torch.float32, device=dev))
     probe, probe_d, mine, mine_d = bufs[key]
     per = nq // world
-    index.probe_device(queries[rank * per:].data_ptr(), per, nprobe, mine.data_ptr(), mine_d.data_ptr())
+    if local is not None and tuple(local.shape) != (per, queries.shape[1]):
+        raise ValueError("probed_search: `local` must hold this rank's nq / world rows")
+    t0 = time.perf_counter()
+    mine_q = local if local is not None else queries[rank * per:]
+    index.probe_device(mine_q.data_ptr(), per, nprobe, mine.data_ptr(), mine_d.data_ptr())
+    t1 = time.perf_counter()
+    if local is not None:
+        dist_mod.all_gather_into_tensor(queries, local, group=group)
     dist_mod.all_gather_into_tensor(probe, mine, group=group)
     dist_mod.all_gather_into_tensor(probe_d, mine_d, group=group)
     # The library runs on its own stream and does not order itself after the caller's:
     # the gathered lists must be complete before the search starts.
     if probe.is_cuda:
         torch.cuda.current_stream(probe.device).synchronize()
+    t2 = time.perf_counter()
     index.search_batch_device_probed(queries.data_ptr(), nq, k, nprobe, probe.data_ptr(), probe_d.data_ptr(),
                                      out_ids.data_ptr(), out_d.data_ptr(), out_n.data_ptr(), mode=mode)
+    if times is not None:
+        t3 = time.perf_counter()
+        for key2, v in (("probe_ms", t1 - t0), ("exchange_ms", t2 - t1), ("search_ms", t3 - t2)):
+            times[key2] = times.get(key2, 0.0) + v * 1e3
+
+
+class _DeviceArray:
+    """A float32 vector at a raw device address, for torch.as_tensor (CUDA array
+    interface, no copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+
+class ThresholdExchange:
+    """The threshold exchange of a sharded database (vesper_ivfpq_set_threshold_exchange)
+    over torch.distributed: every rank's index hands its per-query upper bounds of the
+    k-th distance to `__call__`, which replaces them with the minimum over the ranks (an
+    all-reduce MIN issued on the index's stream, so no host wait).  Install on every
+    rank's index with `install`, before the first search; every rank must then search
+    the same batches with the same parameters, as the sharded search does anyway.
+
+    `view(ptr, n)` makes the tensor over the library's buffer (a CUDA view by default;
+    the CPU tests pass a host view)."""
+
+    def __init__(self, group=None, view=None):
+        self.group = group
+        self.view = view
+        self.error = None
+        self.calls = 0
+
+    def __call__(self, d_tau, n, stream, user) -> int:
+        try:
+            import torch
+            import torch.distributed as dist_mod
+            if self.view is not None:
+                t = self.view(d_tau, n)
+            else:
+                t = torch.as_tensor(_DeviceArray(d_tau, n), device=torch.device("cuda", torch.cuda.current_device()))
+            if t.is_cuda:
+                with torch.cuda.stream(torch.cuda.ExternalStream(stream, device=t.device)):
+                    dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MIN, group=self.group)
+            else:
+                dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MIN, group=self.group)
+            self.calls += 1
+            return 0
+        except Exception as e:  # reported to the library as a failed exchange
+            self.error = e
+            return 1
+
+    def install(self, index):
+        index.set_threshold_exchange(self)
+        return self
+
+
+class ShardResults:
+    """Per-rank result buffers of a sharded search, packed so that one all-gather moves
+    them, and the device merge (vesper_topk_merge_device) of the gathered parts.
+
+    `ids` int64 [nq, k], `dist` float32 [nq, k] and `counts` int32 [nq] are views into one
+    int32 buffer; the library's search writes them.  `merge()` all-gathers the buffer
+    over the group and merges the parts on the current CUDA stream, returning
+    (dist [nq, k], ids [nq, k], counts [nq]) of the whole database."""
+
+    def __init__(self, nq: int, k: int, device, group=None):
+        import torch
+        import torch.distributed as dist_mod
+        self.nq, self.k, self.group = nq, k, group
+        self.world = dist_mod.get_world_size(group)
+        nk = nq * k
+        off_ids = nk + (nk & 1)              # int64 view needs an 8-byte aligned offset
+        off_n = off_ids + 2 * nk
+        words = off_n + nq
+        words += words & 1                   # each part starts 8-byte aligned
+        self.words, self.off_ids, self.off_n = words, off_ids, off_n
+        self.buf = torch.zeros(words, dtype=torch.int32, device=device)
+        self.dist = self.buf[:nk].view(torch.float32).view(nq, k)
+        self.ids = self.buf[off_ids:off_ids + 2 * nk].view(torch.int64).view(nq, k)
+        self.counts = self.buf[off_n:off_n + nq]
+        self.gathered = torch.empty(self.world * words, dtype=torch.int32, device=device)
+        self.out_ids = torch.empty((nq, k), dtype=torch.int64, device=device)
+        self.out_d = torch.empty((nq, k), dtype=torch.float32, device=device)
+        self.out_n = torch.empty(nq, dtype=torch.int32, device=device)
+
+    def merge(self):
+        import torch
+        import torch.distributed as dist_mod
+
+        from . import _native as N
+        from .index import _check
+        dist_mod.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
+        g = self.gathered.data_ptr()
+        lib = N.load()
+        _check(lib, lib.vesper_topk_merge_device(
+            self.world, self.nq, self.k, g, self.words, g + 4 * self.off_ids, self.words // 2, g + 4 * self.off_n,
+            self.words, self.out_ids.data_ptr(), self.out_d.data_ptr(), self.out_n.data_ptr(),
+            torch.cuda.current_stream(self.buf.device).cuda_stream))
+        return self.out_d, self.out_ids, self.out_n
 
 
 # ------------------------------------------------------------------ sharded k-means
