@@ -296,6 +296,24 @@ def list_stats(index, n_queries, scanned_entries):
             "probed_entries_per_query": float(scanned_entries) / max(1, n_queries)}
 
 
+def list_scan_tiles(index, probe_np, tile=128, qchunk=128):
+    """Work the tensor-core list scan does for one batch: it pairs each probed list's
+    128-entry tiles with 128-query chunks of the queries that probe it, so partial tiles
+    and partial chunks are padded.  Returns the (query, entry) pairs of the batch and the
+    pairs its MMAs compute."""
+    import numpy as np
+    sizes = np.diff(index.list_offsets().astype(np.int64))
+    q_per_list = np.bincount(probe_np.reshape(-1).astype(np.int64), minlength=sizes.size)
+    pairs = float((sizes * q_per_list).sum())
+    padded = float(((-(-sizes // tile)) * tile * (-(-q_per_list // qchunk)) * qchunk).sum())
+    hot = q_per_list > 0
+    return {"pairs": pairs, "mma_pairs": padded, "mma_over_pairs": padded / max(pairs, 1.0),
+            "queries_per_probed_list_mean": float(q_per_list[hot].mean()) if hot.any() else 0.0,
+            "pairs_in_chunks_under_half_full": float((sizes * q_per_list)[(q_per_list % qchunk > 0) &
+                                                                         (q_per_list % qchunk < qchunk // 2)].sum())
+            / max(pairs, 1.0)}
+
+
 # ------------------------------------------------------------------------------- flat top-k
 FLAT_N, FLAT_NQ, FLAT_K, FLAT_CHUNK = 1_000_000, 10_000, 100, 125_000
 FLAT_FILTER_BYTES_PER_ROW = (839.23e6 + 36.71e6) / 250_000   # ncu, filter launch over a 250k-row base
@@ -1406,6 +1424,12 @@ def main():
                     "algorithmic_bytes_per_search": code_bytes, "scan_ms": stage_ms["scan_ms"]}
     ls = list_stats(index, NQ, entries)
     ls["probed_entries_per_query_at_mean_list_size"] = NPROBE * ls["mean"]
+    if world == 1:
+        # padding of the list scan's (tile, query chunk) pairs, from this batch's probe lists
+        pr = torch.empty((NQ, min(NPROBE, NLIST)), dtype=torch.int32, device=dev)
+        prd = torch.empty((NQ, min(NPROBE, NLIST)), dtype=torch.float32, device=dev)
+        index.probe_device(queries.data_ptr(), NQ, NPROBE, pr.data_ptr(), prd.data_ptr())
+        ls["list_scan_tiles"] = list_scan_tiles(index, pr.cpu().numpy())
     out = {
         "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",

@@ -6,7 +6,8 @@
   holding half of a base set, search the same batch; each one's exchange replaces its
   per-query bounds with the minimum over both (captured from a first pass, since both
   shards live in one process here).  The merged results must equal one index over the
-  whole base -- distances bit for bit, ids up to exact ties -- and each shard must
+  whole base -- distances to a few ulps (the summation order of an entry's table
+  entries follows its position in its list), ids up to ties -- and each shard must
   refine fewer candidates than without the exchange.
 """
 import os
@@ -17,6 +18,11 @@ import pytest
 from conftest import assert_topk_equivalent
 
 pytestmark = pytest.mark.gpu
+
+# A FAST distance adds the m table entries in an order that depends on the entry's lane
+# in its 128-entry block, i.e. on its position in the list, which differs between a shard
+# and the whole index: the same entry's distance can differ by a few ulps.
+SHARD_RTOL = 1e-5
 
 
 def _merge_device(d, ids, cnt, k):
@@ -150,7 +156,7 @@ def test_threshold_exchange_keeps_the_union_top_k(dim, m, nlist, n, nq, rot, k, 
         i = torch.from_numpy(np.stack([variant[r][0][0].astype(np.int64) for r in range(2)])).cuda()
         c = torch.from_numpy(np.stack([variant[r][0][2].astype(np.int32) for r in range(2)])).cuda()
         md, mi, mn = _merge_device(d, i, c, k)
-        assert_topk_equivalent(mi.astype(np.uint64), md, mn, ref[0], ref[1], ref[2], 0.0)
+        assert_topk_equivalent(mi.astype(np.uint64), md, mn, ref[0], ref[1], ref[2], SHARD_RTOL)
     assert sum(s[1] for s in shared) < sum(p[1] for p in plain)
 
 

@@ -191,7 +191,9 @@ public:
             vgpu::launch_rotate_fast(d_cent.data(), nlist(), (int)dim, d_rot.data(), d_rc.data(), st);
             if (vgpu::rotate_3xtf32_supported((int)dim)) {
                 d_rot3.resize(dim * dim * 3);
-                vgpu::prepare_rotation_3xtf32(d_rot.data(), (int)dim, d_rot3.data(), st);
+                // the rotation computes x R (apply_rotation), i.e. row j of the product's
+                // second operand is column j of R: the GEMM takes R^T
+                vgpu::prepare_rotation_3xtf32(d_rotT.data(), (int)dim, d_rot3.data(), st);
             } else {
                 d_rot3.release();
             }

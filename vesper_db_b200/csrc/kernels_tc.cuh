@@ -28,12 +28,13 @@ void launch_tc_screen_op(bool ip, const float* x, long long nx, const float* c, 
 void launch_tc_filter(bool ip, const float* x, long long nx, const float* c, long long nc, long long c_stride,
                       int dim, const float* xn, const float* cn, const float* cs, const float* tau, uint32_t col_off,
                       uint2* cand, uint32_t* cand_cnt, int cap, int* err, cudaStream_t st);
-// OPQ rotation of a query batch on the tensor cores (3xTF32, tc_coarse.cu): out[i] =
-// R x_i to a few 1e-7 relative (FAST search only; EXACT search, add() and training keep
-// the sequential fp32 rotation).  prepare_rotation_3xtf32 fills R3 [dim x 3 dim] once
-// per model; x3 is [n x 3 dim] scratch; err as for launch_tc_screen.
+// OPQ rotation of a query batch on the tensor cores (3xTF32, tc_coarse.cu): out[i][j] =
+// sum_k x_i[k] W[j][k] to a few 1e-7 relative, W = R^T for the x R of apply_rotation
+// (FAST search only; EXACT search, add() and training keep the sequential fp32
+// rotation).  prepare_rotation_3xtf32 fills W3 [dim x 3 dim] from W once per model; x3
+// is [n x 3 dim] scratch; err as for launch_tc_screen.
 bool rotate_3xtf32_supported(int dim);
-void prepare_rotation_3xtf32(const float* R, int dim, float* R3, cudaStream_t st);
+void prepare_rotation_3xtf32(const float* W, int dim, float* W3, cudaStream_t st);
 void launch_rotate_3xtf32(const float* x, long long n, int dim, const float* R3, float* x3, float* out, int* err,
                           cudaStream_t st);
 // out[i] = sqrt(in[i]).

@@ -1011,11 +1011,12 @@ __global__ void sqrt_kernel(const float* __restrict__ in, long long n, float* __
 // ---------------------------------------------------------------------------------
 // OPQ rotation of a query batch as one tensor-core GEMM (3xTF32).
 //
-// out = X R^T with every fp32 operand split as v = hi(v) + lo(v): hi(v) = v rounded to
-// tf32 (10 mantissa bits, exact in a tf32 operand), lo(v) = v - hi(v) (exact in fp32,
-// |lo| <= 2^-11 |v|).  X R^T ~= hi(X) hi(R)^T + hi(X) lo(R)^T + lo(X) hi(R)^T is one
-// K = 3 dim contraction of X3 = [hi(X) | hi(X) | lo(X)] with R3 = [hi(R) | lo(R) | hi(R)]
-// on tc_screen_kernel (MODE 1 stores -2 S, so R3 carries a factor -1/2, which is exact).
+// out = X W^T (W = R^T: the x R of apply_rotation) with every fp32 operand split as
+// v = hi(v) + lo(v): hi(v) = v rounded to tf32 (10 mantissa bits, exact in a tf32
+// operand), lo(v) = v - hi(v) (exact in fp32, |lo| <= 2^-11 |v|).
+// X W^T ~= hi(X) hi(W)^T + hi(X) lo(W)^T + lo(X) hi(W)^T is one K = 3 dim contraction of
+// X3 = [hi(X) | hi(X) | lo(X)] with W3 = [hi(W) | lo(W) | hi(W)] on tc_screen_kernel
+// (MODE 1 stores -2 S, so W3 carries a factor -1/2, which is exact).
 // Per term the error is about 2^-20 |x| |r| (the dropped lo lo product and the tf32
 // rounding of lo), against 2^-24 for an fp32 product, so the rotated query differs from
 // the sequential fp32 rotation by a few 1e-7 relative: well inside the 1e-4 relative
@@ -1048,10 +1049,10 @@ __global__ void tf32_split3_kernel(const float* __restrict__ x, long long n, int
 
 bool rotate_3xtf32_supported(int dim) { return tc_screen_supported(3 * dim) && dim >= 32; }
 
-void prepare_rotation_3xtf32(const float* R, int dim, float* R3, cudaStream_t st) {
+void prepare_rotation_3xtf32(const float* W, int dim, float* W3, cudaStream_t st) {
     const long long total = (long long)dim * dim;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
-    tf32_split3_kernel<<<blocks, 256, 0, st>>>(R, dim, dim, 1, -0.5f, R3);
+    tf32_split3_kernel<<<blocks, 256, 0, st>>>(W, dim, dim, 1, -0.5f, W3);
     check(cudaGetLastError(), "tf32_split3_kernel");
 }
 
