@@ -1192,7 +1192,7 @@ public:
         const bool split_scan = !exact && !list_scan && has_blocks && use_split_scan();
         if (list_scan) {
             int cap = kListScanCap;
-            if (const char* v = std::getenv("VGPU_LIST_CAP")) cap = std::clamp(std::atoi(v), 256, 16384);
+            if (const char* v = std::getenv("VGPU_LIST_CAP")) cap = std::clamp(std::atoi(v), 256, 4096);
             tlw.reserve((long long)qc, (int)np, (int)nlist(), (int)dim, (int)k, cap, n_vectors);
             vgpu::check(cudaMemsetAsync(tlw.stats.data(), 0, 2 * sizeof(unsigned long long), st), "memset");
             reset_err();

@@ -17,6 +17,7 @@
 
 #include "kernels.cuh"
 #include "select.cuh"
+#include "tc_common.cuh"
 
 namespace vgpu {
 
@@ -1215,16 +1216,15 @@ __global__ void __launch_bounds__(FB_NT, 1) scan_blocked_kernel(
     const long long q = items ? (long long)items[blockIdx.x].x : (long long)blockIdx.x;
     if (!items && only_over && only_over[q] <= over_cap) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    {
-        const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * 256);
-        float4* dst = reinterpret_cast<float4*>(lut);
-        for (int i = threadIdx.x; i < m * 64; i += FB_NT) dst[i] = __ldg(src + i);
-    }
+    // The query's table arrives by one bulk copy while the prefixes are computed.
+    __shared__ uint64_t lut_bar;
+    const float* tq = T + q * (long long)m * 256;
+    tc::lut_stage_begin(lut, tq, (uint32_t)(m * 256 * 4), &lut_bar);
     // Per-probe prefixes (entries, blocks) and base terms.
     if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nscan, offs, blk_off, eprefix, bprefix);
     if (threadIdx.x == 0) { cnt = 0; have = 0; tau = ~0ull; }
     for (int t = threadIdx.x; t < nscan; t += FB_NT) base[t] = pbase[q * nprobe + t];
-    __syncthreads();
+    tc::lut_stage_wait(lut, tq, (uint32_t)(m * 256 * 4), &lut_bar);
     (void)lane;
 
     auto merge = [&]() {

@@ -66,6 +66,51 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
     return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
+// One-dimensional bulk copy (TMA, no multicast) of `bytes` from global memory into this
+// CTA's shared memory, completing on `bar`.  Both addresses 16-byte aligned, bytes a
+// multiple of 16 and below 2^20 (the barrier's transaction count).
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool lut_stage_bulk(const float* dst, const float* src, uint32_t bytes) {
+    return ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 && bytes % 16 == 0 &&
+           bytes < (1u << 20);
+}
+
+// Staging of a per-query lookup table into shared memory.  lut_stage_begin: thread 0
+// initialises `bar` and starts one bulk copy of `bytes` from src into dst; the rest of the
+// CTA can do other work before lut_stage_wait, which every thread must call.  Plain loads
+// replace the bulk copy when the addresses or the size do not allow one.
+__device__ __forceinline__ void lut_stage_begin(float* dst, const float* src, uint32_t bytes, uint64_t* bar) {
+    if (threadIdx.x == 0 && lut_stage_bulk(dst, src, bytes)) {
+        mbar_init(bar, 1);
+        mbar_init_fence();
+        mbar_expect_tx(bar, bytes);
+        bulk_copy_g2s(dst, src, bytes, bar);
+    }
+}
+// The table is in dst when this returns (a barrier of the whole CTA ends it).  Returns
+// false if the bulk copy had not completed after two bounded waits; the table is then
+// loaded with plain loads instead, and the caller may record the event.
+__device__ __forceinline__ bool lut_stage_wait(float* dst, const float* src, uint32_t bytes, uint64_t* bar) {
+    const bool bulk = lut_stage_bulk(dst, src, bytes);
+    __syncthreads();  // the barrier's initialisation is visible to every thread
+    bool ok = true;
+    if (bulk) {
+        ok = mbar_wait(bar, 0);
+        if (!ok) ok = mbar_wait(bar, 0);  // still in flight: wait once more before giving up
+    }
+    const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+    if (!bulk || !all_ok) {
+        for (uint32_t i = threadIdx.x; i < bytes / 4; i += blockDim.x) dst[i] = src[i];
+        __syncthreads();
+    }
+    return all_ok;
+}
+
 __device__ __forceinline__ void commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");

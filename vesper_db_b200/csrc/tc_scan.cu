@@ -1159,42 +1159,73 @@ __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict_
                                                         const unsigned long long* __restrict__ cand,
                                                         const uint32_t* __restrict__ cand_cnt, int cap, int k,
                                                         uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
-                                                        uint32_t* __restrict__ out_n) {
+                                                        uint32_t* __restrict__ out_n, int* __restrict__ err) {
+    // Shared memory: [barrier, 16 B][table m*256 floats, later the sort keys][eprefix].
+    // The table arrives by one bulk copy while the probe prefixes and the candidates'
+    // metadata are read; once every candidate is scored, the keys (at most KPT per
+    // thread, held in registers meanwhile) overwrite the table, so one CTA needs little
+    // more than its table and two fit on an SM.
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int m = MC;
-    float* lut = reinterpret_cast<float*>(smem_raw);                                  // [m * 256]
-    unsigned long long* keys = reinterpret_cast<unsigned long long*>(lut + m * 256);  // [next_pow2(cap)]
-    uint32_t* eprefix = reinterpret_cast<uint32_t*>(keys + next_pow2(cap));           // [nprobe + 1]
+    constexpr int KPT = 16;                                                           // keys per thread
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
+    float* lut = reinterpret_cast<float*>(smem_raw + 16);                              // [m * 256]
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw + 16);   // [next_pow2(cap)]
+    const int region = m * 256 * 4 > next_pow2(cap) * 8 ? m * 256 * 4 : next_pow2(cap) * 8;
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(smem_raw + 16 + region);           // [nprobe + 1]
     const long long q = blockIdx.x;
     const uint32_t n = cand_cnt[q];
     if (n > (uint32_t)cap) return;
-    {
-        const float4* src = reinterpret_cast<const float4*>(T + q * (long long)m * 256);
-        float4* dst = reinterpret_cast<float4*>(lut);
-        for (int i = threadIdx.x; i < m * 64; i += 256) dst[i] = __ldg(src + i);
-    }
+    const float* tq = T + q * (long long)m * 256;
+    tc::lut_stage_begin(lut, tq, (uint32_t)(m * 256 * 4), bar);
     if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nprobe, offs, nullptr, eprefix, nullptr);
-    __syncthreads();
     const int p2 = next_pow2(n < 2 ? 2 : (int)n);
-    for (int i = threadIdx.x; i < p2; i += 256) {
-        unsigned long long key = ~0ull;
+    // Candidate metadata while the table is in flight: code row, (base + u) and the
+    // (probe slot, position in the list) of each of this thread's candidates.
+    const uint8_t* crow[KPT];
+    float dbase[KPT];
+    uint32_t slot[KPT], pos[KPT];
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+        const int i = (int)threadIdx.x + j * 256;
+        crow[j] = nullptr;
+        dbase[j] = 0.0f;
+        slot[j] = pos[j] = 0;
         if (i < (int)n) {
             const unsigned long long c = cand[q * cap + i];
             const uint32_t t = (uint32_t)(c >> 32), p = (uint32_t)c;
-            const uint32_t l = probe[q * nprobe + t];
-            const uint64_t e = offs[l] + p;
-            const uint8_t* cr = codes + e * m;
-            const int lane = (int)((p & 127u) >> 2);
+            const uint64_t e = offs[probe[q * nprobe + t]] + p;
+            crow[j] = codes + e * m;
+            dbase[j] = pbase[q * nprobe + t] + vterm[e];
+            slot[j] = t;
+            pos[j] = p;
+        }
+    }
+    if (!tc::lut_stage_wait(lut, tq, (uint32_t)(m * 256 * 4), bar) && threadIdx.x == 0 && err) atomicExch(err, 41);
+    // The blocked scan's arithmetic: the table entries added in the lane-rotated
+    // sub-space order of the entry's lane in its 128-entry block, then (base + u) + sum.
+    unsigned long long kr[KPT];
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+        kr[j] = ~0ull;
+        if (crow[j] != nullptr) {
+            const int lane = (int)((pos[j] & 127u) >> 2);
+            const uint8_t* cr = crow[j];
             float acc = 0.0f;
 #pragma unroll 8
             for (int r = 0; r < m; ++r) {
                 const int g = r / G, s_lo = (lane + r) & (G - 1);
                 acc += lut[(g * 256 + cr[g * G + s_lo]) * G + s_lo];
             }
-            const float dist = (pbase[q * nprobe + t] + vterm[e]) + acc;
-            key = ((unsigned long long)float_key(dist) << 32) | (eprefix[t] + p);
+            const float dist = dbase[j] + acc;
+            kr[j] = ((unsigned long long)float_key(dist) << 32) | (eprefix[slot[j]] + pos[j]);
         }
-        keys[i] = key;
+    }
+    __syncthreads();  // every read of the table is done: the keys take its place
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+        const int i = (int)threadIdx.x + j * 256;
+        if (i < p2) keys[i] = kr[j];
     }
     bitonic_sort_u64<256>(keys, p2);
     const int h = (int)n < k ? (int)n : k;
@@ -1463,7 +1494,10 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     check(cudaEventRecord(w.ev[3], st), "cudaEventRecord");
 
     // Refine the candidates; overflowed queries fall back to the blocked scan.
-    const size_t rsmem = (size_t)a.m * 256 * 4 + (size_t)next_pow2(w.cap) * 8 + (size_t)(a.nprobe + 1) * 4;
+    // [barrier][table, then the sort keys][probe prefixes] (tl_refine_kernel)
+    if (next_pow2(w.cap) > 256 * 16) throw CudaError("tc_list_scan: candidate cap above 4096");
+    const size_t rsmem = 16 + std::max((size_t)a.m * 256 * 4, (size_t)next_pow2(w.cap) * 8) +
+                         (size_t)(a.nprobe + 1) * 4;
     if (rsmem > 227 * 1024) throw CudaError("tc_list_scan: refine buffers do not fit in shared memory");
 #define VGPU_RF(MCV, GV)                                                                                    \
     do {                                                                                                    \
@@ -1472,7 +1506,7 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
               "cudaFuncSetAttribute(tl_refine)");                                                           \
         tl_refine_kernel<MCV, GV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                      \
             a.T, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids, w.cand.data(),               \
-            w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n);                                    \
+            w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n, a.err);                            \
     } while (0)
     if (a.m == 16) VGPU_RF(16, 16);
     else if (a.m == 32) VGPU_RF(32, 32);
