@@ -151,8 +151,14 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
  * query, so the calls of all shards pair up.  fn must not call back into the index.
  * fn = NULL removes the exchange. */
 typedef int (*vesper_ivfpq_tau_exchange_fn)(float* d_tau, size_t n_queries, void* cuda_stream, void* user);
+/* shard / shards: with shards > 1 this index computes its own bounds only for the
+ * queries q (0-based in the call's batch) with q % shards == shard and relies on the
+ * exchange for the rest, so each of W shards pays 1/W of the threshold pass; give every
+ * shard a different `shard` and the same `shards` (shards = 1: every query; shard must
+ * be below shards). */
 VESPER_C_API vesper_status_t vesper_ivfpq_set_threshold_exchange(vesper_index_t* index,
-                                                                 vesper_ivfpq_tau_exchange_fn fn, void* user);
+                                                                 vesper_ivfpq_tau_exchange_fn fn, void* user,
+                                                                 uint32_t shard, uint32_t shards);
 
 /* Merge of per-shard results on the device.  No counterpart in the reference (one
  * index per process).  For a database split across GPUs, each shard's batch search

@@ -100,11 +100,14 @@ def _with_env(key, val, f):
             os.environ[key] = old
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("dim,m,nlist,n,nq,rot,k,npb", [
     (128, 16, 64, 40000, 300, True, 10, 8),
     (128, 32, 48, 60000, 256, False, 100, 12),
 ])
-def test_threshold_exchange_keeps_the_union_top_k(dim, m, nlist, n, nq, rot, k, npb):
+def test_threshold_exchange_keeps_the_union_top_k(dim, m, nlist, n, nq, rot, k, npb, split):
+    """split: each shard runs its own threshold pass only for its half of the queries
+    (q % 2 == shard) and takes the other half's bounds from the exchange."""
     import torch
 
     from vesper_db_b200 import IvfPqIndex
@@ -136,12 +139,13 @@ def test_threshold_exchange_keeps_the_union_top_k(dim, m, nlist, n, nq, rot, k, 
         ref, _ = search(whole)
         plain = [search(ix) for ix in shards]
         taus = [[], []]
+        part_args = (lambda r: (r, 2)) if split else (lambda r: (0, 1))
         for r in range(2):                       # pass 1: record each shard's bounds
-            shards[r].set_threshold_exchange(_hook(taus[r]))
+            shards[r].set_threshold_exchange(_hook(taus[r]), *part_args(r))
             search(shards[r])
         calls = [[], []]
         for r in range(2):                       # pass 2: the minimum over both shards
-            shards[r].set_threshold_exchange(_hook(calls[r], taus[1 - r]))
+            shards[r].set_threshold_exchange(_hook(calls[r], taus[1 - r]), *part_args(r))
         shared = [search(ix) for ix in shards]
         for ix in shards:
             ix.set_threshold_exchange(None)
@@ -151,13 +155,18 @@ def test_threshold_exchange_keeps_the_union_top_k(dim, m, nlist, n, nq, rot, k, 
     assert all(len(c) == 1 for c in calls) and all(len(t) == 1 for t in taus)
     tau_min = torch.minimum(taus[0][0], taus[1][0])
     assert torch.isfinite(tau_min).all()
+    if split:   # each shard bounded only its own half
+        for r in range(2):
+            own = torch.arange(nq, device=taus[r][0].device) % 2 == r
+            assert torch.isinf(taus[r][0][~own]).all() and torch.isfinite(taus[r][0][own]).all()
     for variant in (plain, shared):
         d = torch.from_numpy(np.stack([variant[r][0][1] for r in range(2)])).cuda()
         i = torch.from_numpy(np.stack([variant[r][0][0].astype(np.int64) for r in range(2)])).cuda()
         c = torch.from_numpy(np.stack([variant[r][0][2].astype(np.int32) for r in range(2)])).cuda()
         md, mi, mn = _merge_device(d, i, c, k)
         assert_topk_equivalent(mi.astype(np.uint64), md, mn, ref[0], ref[1], ref[2], SHARD_RTOL)
-    assert sum(s[1] for s in shared) < sum(p[1] for p in plain)
+    if not split:   # each shard's bound is at least as tight as its own
+        assert sum(s[1] for s in shared) < sum(p[1] for p in plain)
 
 
 def test_exchange_sees_no_bound_without_the_list_scan():

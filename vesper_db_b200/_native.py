@@ -223,7 +223,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
             "vesper_ivfpq_probe_device": (st, [vp, vp, C.c_size_t, C.c_uint32, vp, vp]),
             "vesper_ivfpq_search_batch_device_probed": (st, [vp, vp, C.c_size_t, C.POINTER(SearchParamsEx), vp, vp,
                                                              vp, vp, vp]),
-            "vesper_ivfpq_set_threshold_exchange": (st, [vp, TAU_EXCHANGE_FN, vp]),
+            "vesper_ivfpq_set_threshold_exchange": (st, [vp, TAU_EXCHANGE_FN, vp, C.c_uint32, C.c_uint32]),
             "vesper_topk_merge_device": (st, [C.c_uint32, C.c_size_t, C.c_uint32, vp, C.c_size_t, vp, C.c_size_t,
                                               vp, C.c_size_t, vp, vp, vp, vp]),
             "vesper_ivfpq_reconstruct": (st, [vp, C.c_uint64, f32p]),

@@ -137,6 +137,9 @@ public:
     size_t n_vectors = 0;
     // Blocked copy of the lists for the FAST scan (built after every add / load).
     bool has_blocks = false;
+    // Mean size of the list holding a random entry (sum |l|^2 / sum |l|): the expected
+    // size of a list a query from the data's distribution probes.
+    double weighted_list_len = 0.0;
     DeviceBuffer<uint64_t> d_blk_off;
     DeviceBuffer<uint8_t> d_bcodes;
     DeviceBuffer<float> d_bvterm;
@@ -148,6 +151,7 @@ public:
     // threshold exchange between shards (set_threshold_exchange)
     IvfPqIndex::ThresholdExchangeFn tau_fn = nullptr;
     void* tau_user = nullptr;
+    uint32_t tau_shard = 0, tau_shards = 1;
     mutable DeviceBuffer<float> w_tau_inf;
 
     double t_assign_ms = 0, t_encode_ms = 0, t_lists_ms = 0;
@@ -229,7 +233,14 @@ public:
         d_xnorm.release();
         if (!vgpu::scan_blocked_supported((int)m(), (int)ksub)) return;
         std::vector<uint64_t> boff(nlist() + 1, 0);
-        for (uint32_t l = 0; l < nlist(); ++l) boff[l + 1] = boff[l] + (h_offs[l + 1] - h_offs[l] + 127) / 128;
+        double s1 = 0.0, s2 = 0.0;
+        for (uint32_t l = 0; l < nlist(); ++l) {
+            const double len = (double)(h_offs[l + 1] - h_offs[l]);
+            s1 += len;
+            s2 += len * len;
+            boff[l + 1] = boff[l] + (h_offs[l + 1] - h_offs[l] + 127) / 128;
+        }
+        weighted_list_len = s1 > 0 ? s2 / s1 : 0.0;
         const uint64_t nb = boff[nlist()];
         d_blk_off.resize(nlist() + 1);
         h2d(d_blk_off.data(), boff.data(), boff.size(), st);
@@ -272,7 +283,9 @@ public:
         const char* v = std::getenv("VGPU_SCAN");
         if (v && std::string(v) == "tc") return true;
         if (v && (std::string(v) == "blocked" || std::string(v) == "split")) return false;
-        const double per_query = (double)n_vectors / std::max<uint32_t>(nlist(), 1) * np;
+        // Expected entries a query scans: its probes weighted by list size (uneven lists
+        // put queries in the long ones), not the mean list size.
+        const double per_query = weighted_list_len * np;
         return per_query >= 1024.0 && nq >= 256;
     }
 
@@ -1288,10 +1301,11 @@ public:
                         a.T = w_T.data(); a.rq = rq; a.pbase = w_pbase.data(); a.probe = probe;
                         a.nq = (long long)nc; a.nprobe = (int)np; a.nlist = (int)nlist(); a.dim = (int)dim;
                         a.m = (int)m(); a.k = (int)k; a.offs = d_offs.data(); a.codes = d_codes.data();
-                        a.vterm = d_vterm.data(); a.xnorm = d_xnorm.data(); a.cbb = d_cbb.data();
+                        a.vterm = d_vterm.data(); a.xnorm = d_xnorm.data(); a.cbb = d_cbb.data(); a.cb = d_cb.data();
                         a.blk_off = d_blk_off.data(); a.bcodes = d_bcodes.data(); a.bvterm = d_bvterm.data();
                         a.ids = d_ids.data(); a.out_ids = oid; a.out_d = od; a.out_n = on; a.err = d_err.data();
                         a.tau_fn = tau_fn; a.tau_user = tau_user;
+                        a.tau_shard = tau_shard; a.tau_shards = tau_shards;
                         vgpu::launch_tc_list_scan(a, tlw, st);
                     } else if (split_scan) {
                         vgpu::launch_scan_blocked_split(w_T.data(), (long long)nc, w_pbase.data(), probe,
@@ -1532,10 +1546,14 @@ auto IvfPqIndex::search_batch_flat(const float* queries, std::size_t n_queries,
     }
 }
 
-void IvfPqIndex::set_threshold_exchange(ThresholdExchangeFn fn, void* user) {
+void IvfPqIndex::set_threshold_exchange(ThresholdExchangeFn fn, void* user, std::uint32_t shard,
+                                        std::uint32_t shards) {
+    if (shards == 0 || shard >= shards) throw vgpu::CudaError("set_threshold_exchange: shard must be below shards");
     std::lock_guard<std::mutex> lk(impl_->mu);
     impl_->tau_fn = fn;
     impl_->tau_user = fn ? user : nullptr;
+    impl_->tau_shard = fn ? shard : 0;
+    impl_->tau_shards = fn ? shards : 1;
 }
 
 auto IvfPqIndex::probe_device(const float* d_queries, std::size_t n_queries, std::uint32_t nprobe,

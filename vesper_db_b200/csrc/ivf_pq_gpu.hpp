@@ -175,8 +175,12 @@ public:
     // that can reach the shared bound, so each shard refines about its share of the
     // union's candidates; the union's top k is unchanged.  Searches that do not run the
     // list scan pass +inf for every query.  fn = nullptr removes it.
+    // shards > 1: this index runs its own threshold pass only for the queries q with
+    // q mod shards == shard and takes the other queries' bounds from the exchange, so
+    // each shard of a W-way database pays 1/W of the pass (shards = 1: every query).
     using ThresholdExchangeFn = int (*)(float* d_tau, std::size_t n_queries, void* stream, void* user);
-    void set_threshold_exchange(ThresholdExchangeFn fn, void* user);
+    void set_threshold_exchange(ThresholdExchangeFn fn, void* user, std::uint32_t shard = 0,
+                                std::uint32_t shards = 1);
 
     // FAST-mode device search that allocates nothing: its temporary buffers come from
     // a fixed 64 MiB device array (noalloc_search.cu) instead of cudaMalloc.

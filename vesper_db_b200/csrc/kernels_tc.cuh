@@ -190,6 +190,7 @@ struct TlScanArgs {
     const float* vterm;      // CSR per-entry terms
     const float* xnorm;      // CSR per-entry decoded norms
     const uint16_t* cbb;     // bf16 codebooks [m x 256 x dsub]
+    const float* cb = nullptr;  // fp32 codebooks [m x 256 x dsub] (the refine's table entries)
     const uint64_t* blk_off; // blocked copy (threshold scan and overflow fallback)
     const uint8_t* bcodes;
     const float* bvterm;
@@ -205,6 +206,9 @@ struct TlScanArgs {
     // stream, and return 0.
     int (*tau_fn)(float* d_tau, size_t nq, void* stream, void* user) = nullptr;
     void* tau_user = nullptr;
+    // With an exchange, this shard's own threshold pass covers only the queries q with
+    // q mod tau_shards == tau_shard; the exchange brings the other queries' bounds.
+    uint32_t tau_shard = 0, tau_shards = 1;
 };
 
 // FAST search results identical to launch_scan_blocked over all nprobe probes.

@@ -966,18 +966,23 @@ __global__ void query_prep_kernel(const float* __restrict__ rq, long long nq, in
 // Per query: nearest-list size L0; queries with L0 > small_max (and k <= 256) get their
 // threshold from the tensor-core pass over that list (pair kept in p0, 4 minima per
 // 128-entry tile), the others from the blocked scan (run flag).
+// Queries outside this shard's share (q mod shards != shard) get no threshold pass:
+// tau = -FLT_MAX (no bound) until the threshold exchange brings another shard's.
 __global__ void home_split_kernel(const uint32_t* __restrict__ probe, int nprobe, const float* __restrict__ pbase,
                                   const uint64_t* __restrict__ offs, long long nq, uint32_t small_max, int big_ok,
-                                  uint32_t* __restrict__ p0, float* __restrict__ pbase0, uint32_t* __restrict__ mcount,
-                                  uint32_t* __restrict__ run_lut) {
+                                  uint32_t shard, uint32_t shards, uint32_t* __restrict__ p0,
+                                  float* __restrict__ pbase0, uint32_t* __restrict__ mcount,
+                                  uint32_t* __restrict__ run_lut, float* __restrict__ tau) {
     for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
         const uint32_t l = probe[q * nprobe];
         const uint64_t L0 = offs[l + 1] - offs[l];
-        const bool big = big_ok && L0 > small_max;
+        const bool mine = shards <= 1 || (uint32_t)(q % shards) == shard;
+        const bool big = mine && big_ok && L0 > small_max;
         p0[q] = big ? l : kSkipPair;
         pbase0[q] = pbase[q * nprobe];
         mcount[q] = big ? (uint32_t)(4 * ((L0 + 127) / 128)) : 0u;
-        run_lut[q] = big ? 0u : 1u;
+        run_lut[q] = (mine && !big) ? 1u : 0u;
+        if (!mine) tau[q] = -FLT_MAX;
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) mcount[nq] = 0;
 }
@@ -1148,10 +1153,20 @@ __global__ void unit_count_kernel(const uint32_t* __restrict__ cnt, const uint64
 // Refine: exact FAST distances of the candidates (the blocked scan's arithmetic and
 // scan positions), then the k smallest keys.  Queries whose candidate list overflowed
 // are left to the blocked scan.
+//
+// The blocked scan adds the query's lookup-table entries T[s][c] = -2 * fma-chain over
+// t < dsub of rq[s dsub + t] * y[s][c][t] (from 0, t ascending: every table kernel's
+// arithmetic) in the lane-rotated sub-space order.  The refine computes exactly those
+// entries on the fly from the rotated query (staged in shared memory, dim floats) and
+// the fp32 codebook rows its candidates use, instead of reading the query's m x 256
+// table: a query has tens to a few thousand candidates, each needing m of its 256 x m
+// entries, so the table itself (96 KB per query at m = 96) would cost far more bytes.
 // ---------------------------------------------------------------------------------
-template <int MC, int G>
-__global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict__ T, const uint32_t* __restrict__ probe,
-                                                        int nprobe, const float* __restrict__ pbase,
+template <int DS>
+__global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict__ rq, int dim,
+                                                        const float* __restrict__ cb, int m, int G,
+                                                        const uint32_t* __restrict__ probe, int nprobe,
+                                                        const float* __restrict__ pbase,
                                                         const uint64_t* __restrict__ offs,
                                                         const uint8_t* __restrict__ codes,
                                                         const float* __restrict__ vterm,
@@ -1159,73 +1174,49 @@ __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict_
                                                         const unsigned long long* __restrict__ cand,
                                                         const uint32_t* __restrict__ cand_cnt, int cap, int k,
                                                         uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
-                                                        uint32_t* __restrict__ out_n, int* __restrict__ err) {
-    // Shared memory: [barrier, 16 B][table m*256 floats, later the sort keys][eprefix].
-    // The table arrives by one bulk copy while the probe prefixes and the candidates'
-    // metadata are read; once every candidate is scored, the keys (at most KPT per
-    // thread, held in registers meanwhile) overwrite the table, so one CTA needs little
-    // more than its table and two fit on an SM.
+                                                        uint32_t* __restrict__ out_n) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    constexpr int m = MC;
-    constexpr int KPT = 16;                                                           // keys per thread
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
-    float* lut = reinterpret_cast<float*>(smem_raw + 16);                              // [m * 256]
-    unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw + 16);   // [next_pow2(cap)]
-    const int region = m * 256 * 4 > next_pow2(cap) * 8 ? m * 256 * 4 : next_pow2(cap) * 8;
-    uint32_t* eprefix = reinterpret_cast<uint32_t*>(smem_raw + 16 + region);           // [nprobe + 1]
+    float* rqs = reinterpret_cast<float*>(smem_raw);                                         // [dim]
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(rqs + ((dim + 3) & ~3));  // [next_pow2(cap)]
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(keys + next_pow2(cap));                    // [nprobe + 1]
     const long long q = blockIdx.x;
     const uint32_t n = cand_cnt[q];
     if (n > (uint32_t)cap) return;
-    const float* tq = T + q * (long long)m * 256;
-    tc::lut_stage_begin(lut, tq, (uint32_t)(m * 256 * 4), bar);
+    for (int i = threadIdx.x; i < dim; i += 256) rqs[i] = rq[q * dim + i];
     if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nprobe, offs, nullptr, eprefix, nullptr);
+    __syncthreads();
     const int p2 = next_pow2(n < 2 ? 2 : (int)n);
-    // Candidate metadata while the table is in flight: code row, (base + u) and the
-    // (probe slot, position in the list) of each of this thread's candidates.
-    const uint8_t* crow[KPT];
-    float dbase[KPT];
-    uint32_t slot[KPT], pos[KPT];
-#pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-        const int i = (int)threadIdx.x + j * 256;
-        crow[j] = nullptr;
-        dbase[j] = 0.0f;
-        slot[j] = pos[j] = 0;
+    for (int i = threadIdx.x; i < p2; i += 256) {
+        unsigned long long key = ~0ull;
         if (i < (int)n) {
             const unsigned long long c = cand[q * cap + i];
             const uint32_t t = (uint32_t)(c >> 32), p = (uint32_t)c;
-            const uint64_t e = offs[probe[q * nprobe + t]] + p;
-            crow[j] = codes + e * m;
-            dbase[j] = pbase[q * nprobe + t] + vterm[e];
-            slot[j] = t;
-            pos[j] = p;
-        }
-    }
-    if (!tc::lut_stage_wait(lut, tq, (uint32_t)(m * 256 * 4), bar) && threadIdx.x == 0 && err) atomicExch(err, 41);
-    // The blocked scan's arithmetic: the table entries added in the lane-rotated
-    // sub-space order of the entry's lane in its 128-entry block, then (base + u) + sum.
-    unsigned long long kr[KPT];
-#pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-        kr[j] = ~0ull;
-        if (crow[j] != nullptr) {
-            const int lane = (int)((pos[j] & 127u) >> 2);
-            const uint8_t* cr = crow[j];
+            const uint32_t l = probe[q * nprobe + t];
+            const uint64_t e = offs[l] + p;
+            const uint8_t* cr = codes + e * m;
+            const int lane = (int)((p & 127u) >> 2);
             float acc = 0.0f;
-#pragma unroll 8
+#pragma unroll 4
             for (int r = 0; r < m; ++r) {
                 const int g = r / G, s_lo = (lane + r) & (G - 1);
-                acc += lut[(g * 256 + cr[g * G + s_lo]) * G + s_lo];
-            }
-            const float dist = dbase[j] + acc;
-            kr[j] = ((unsigned long long)float_key(dist) << 32) | (eprefix[slot[j]] + pos[j]);
-        }
-    }
-    __syncthreads();  // every read of the table is done: the keys take its place
+                const int sub = g * G + s_lo;
+                const float4* y = reinterpret_cast<const float4*>(cb + ((long long)sub * 256 + cr[sub]) * DS);
+                const float* x = rqs + sub * DS;
+                float a = 0.0f;
 #pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-        const int i = (int)threadIdx.x + j * 256;
-        if (i < p2) keys[i] = kr[j];
+                for (int v = 0; v < DS / 4; ++v) {
+                    const float4 yv = __ldg(y + v);
+                    a = fmaf(x[4 * v + 0], yv.x, a);
+                    a = fmaf(x[4 * v + 1], yv.y, a);
+                    a = fmaf(x[4 * v + 2], yv.z, a);
+                    a = fmaf(x[4 * v + 3], yv.w, a);
+                }
+                acc = __fadd_rn(acc, -2.0f * a);
+            }
+            const float dist = (pbase[q * nprobe + t] + vterm[e]) + acc;
+            key = ((unsigned long long)float_key(dist) << 32) | (eprefix[t] + p);
+        }
+        keys[i] = key;
     }
     bitonic_sort_u64<256>(keys, p2);
     const int h = (int)n < k ? (int)n : k;
@@ -1449,8 +1440,10 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
         if (std::string(v) == "tc") small_max = 0;
         if (std::string(v) == "lut") small_max = 0xffffffffu;
     }
+    const uint32_t shards = a.tau_fn ? std::max(a.tau_shards, 1u) : 1u;
     home_split_kernel<<<gq, 256, 0, st>>>(a.probe, a.nprobe, a.pbase, a.offs, a.nq, small_max, a.k <= 256 ? 1 : 0,
-                                          w.p0.data(), w.pbase0.data(), w.mcount.data(), w.run_lut.data());
+                                          a.tau_shard, shards, w.p0.data(), w.pbase0.data(), w.mcount.data(),
+                                          w.run_lut.data(), w.tau.data());
     VGPU_LAUNCH("home_split_kernel");
     size_t tmp = w.scan_tmp.size();
     check(cub::DeviceScan::ExclusiveSum(w.scan_tmp.data(), tmp, w.mcount.data(), w.mins_off.data(), (int)(a.nq + 1), st),
@@ -1494,25 +1487,23 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     check(cudaEventRecord(w.ev[3], st), "cudaEventRecord");
 
     // Refine the candidates; overflowed queries fall back to the blocked scan.
-    // [barrier][table, then the sort keys][probe prefixes] (tl_refine_kernel)
-    if (next_pow2(w.cap) > 256 * 16) throw CudaError("tc_list_scan: candidate cap above 4096");
-    const size_t rsmem = 16 + std::max((size_t)a.m * 256 * 4, (size_t)next_pow2(w.cap) * 8) +
-                         (size_t)(a.nprobe + 1) * 4;
+    // [rotated query][sort keys][probe prefixes] (tl_refine_kernel)
+    const size_t rsmem = (size_t)((a.dim + 3) & ~3) * 4 + (size_t)next_pow2(w.cap) * 8 + (size_t)(a.nprobe + 1) * 4;
     if (rsmem > 227 * 1024) throw CudaError("tc_list_scan: refine buffers do not fit in shared memory");
-#define VGPU_RF(MCV, GV)                                                                                    \
+    if (a.cb == nullptr) throw CudaError("tc_list_scan: the fp32 codebooks are required");
+    const int rdsub = a.dim / a.m, rG = a.m < 32 ? a.m : 32;
+#define VGPU_RF(DSV)                                                                                        \
     do {                                                                                                    \
-        check(cudaFuncSetAttribute(tl_refine_kernel<MCV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+        check(cudaFuncSetAttribute(tl_refine_kernel<DSV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)rsmem),                                                             \
               "cudaFuncSetAttribute(tl_refine)");                                                           \
-        tl_refine_kernel<MCV, GV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                      \
-            a.T, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids, w.cand.data(),               \
-            w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n, a.err);                            \
+        tl_refine_kernel<DSV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                          \
+            a.rq, a.dim, a.cb, a.m, rG, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids,        \
+            w.cand.data(), w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n);                     \
     } while (0)
-    if (a.m == 16) VGPU_RF(16, 16);
-    else if (a.m == 32) VGPU_RF(32, 32);
-    else if (a.m == 64) VGPU_RF(64, 32);
-    else if (a.m == 96) VGPU_RF(96, 32);
-    else VGPU_RF(128, 32);
+    if (rdsub == 4) VGPU_RF(4);
+    else if (rdsub == 8) VGPU_RF(8);
+    else VGPU_RF(16);
 #undef VGPU_RF
     VGPU_LAUNCH("tl_refine_kernel");
     check(cudaEventRecord(w.ev[4], st), "cudaEventRecord");

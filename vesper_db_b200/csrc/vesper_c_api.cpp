@@ -374,11 +374,12 @@ VESPER_C_API vesper_status_t vesper_ivfpq_search_batch_device_probed(
 }
 
 VESPER_C_API vesper_status_t vesper_ivfpq_set_threshold_exchange(vesper_index_t* index,
-                                                                 vesper_ivfpq_tau_exchange_fn fn, void* user) {
-    if (!index || !index->ivfpq) return VESPER_ERROR_INVALID_PARAM;
+                                                                 vesper_ivfpq_tau_exchange_fn fn, void* user,
+                                                                 uint32_t shard, uint32_t shards) {
+    if (!index || !index->ivfpq || shards == 0 || shard >= shards) return VESPER_ERROR_INVALID_PARAM;
     clear_error();
     return guarded("set_threshold_exchange", [&] {
-        index->ivfpq->set_threshold_exchange(fn, user);
+        index->ivfpq->set_threshold_exchange(fn, user, shard, shards);
         return VESPER_OK;
     });
 }

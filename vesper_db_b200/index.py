@@ -191,13 +191,15 @@ class IvfPqIndex:
             self._h, C.c_void_p(q_ptr), nq, C.byref(p), C.c_void_p(probe_ptr), C.c_void_p(probe_d_ptr),
             C.c_void_p(ids_ptr), C.c_void_p(d_ptr), C.c_void_p(counts_ptr) if counts_ptr else None))
 
-    def set_threshold_exchange(self, fn):
+    def set_threshold_exchange(self, fn, shard: int = 0, shards: int = 1):
         """Install fn(d_tau, n_queries, cuda_stream, user) -> int (an N.TAU_EXCHANGE_FN
         object, kept alive here) as the index's threshold exchange between shards, or
-        remove it with None (vesper_ivfpq_set_threshold_exchange)."""
+        remove it with None (vesper_ivfpq_set_threshold_exchange).  With shards > 1 this
+        index bounds only the queries q with q % shards == shard itself."""
         cb = fn if fn is None or isinstance(fn, N.TAU_EXCHANGE_FN) else N.TAU_EXCHANGE_FN(fn)
-        _check(self._lib, self._lib.vesper_ivfpq_set_threshold_exchange(self._h, cb if cb is not None else
-                                                                        N.TAU_EXCHANGE_FN(), None))
+        _check(self._lib, self._lib.vesper_ivfpq_set_threshold_exchange(
+            self._h, cb if cb is not None else N.TAU_EXCHANGE_FN(), None, shard if cb is not None else 0,
+            shards if cb is not None else 1))
         self._tau_cb = cb
 
     # ------------------------------------------------------------------ the rest of the index API

@@ -140,8 +140,14 @@ class ThresholdExchange:
             self.error = e
             return 1
 
-    def install(self, index):
-        index.set_threshold_exchange(self)
+    def install(self, index, split: bool = True):
+        """split: each rank runs the threshold pass for 1/world of the batch (queries q
+        with q % world == rank) and takes the others' bounds from the exchange."""
+        import torch.distributed as dist_mod
+        if split and dist_mod.is_initialized():
+            index.set_threshold_exchange(self, dist_mod.get_rank(self.group), dist_mod.get_world_size(self.group))
+        else:
+            index.set_threshold_exchange(self)
         return self
 
 
