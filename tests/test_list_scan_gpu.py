@@ -21,8 +21,9 @@ def _index():
     return IvfPqIndex()
 
 
-def _search(idx, q, k, npb, scan, threshold=None, cta=None):
-    env = {"VGPU_SCAN": scan, "VGPU_LIST_THRESHOLD": threshold, "VGPU_LIST_CTA": cta}
+def _search(idx, q, k, npb, scan, threshold=None, cta=None, refine_table_min=None):
+    env = {"VGPU_SCAN": scan, "VGPU_LIST_THRESHOLD": threshold, "VGPU_LIST_CTA": cta,
+           "VGPU_REFINE_TABLE_MIN": refine_table_min}
     old = {key: os.environ.get(key) for key in env}
     for key, val in env.items():
         if val is None:
@@ -80,6 +81,22 @@ def test_list_scan_equals_blocked_scan(dim, m, nlist, n, nq, rot, searches, thre
         assert np.array_equal(bn, tn)
         assert np.array_equal(bd, td)
         assert np.array_equal(bi, ti)
+
+
+@pytest.mark.parametrize("table_min", ["0", "1000000"])
+@pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES)
+def test_refine_paths_equal_blocked_scan(dim, m, nlist, n, nq, rot, searches, table_min):
+    """The refine reads a query's lookup table when it has many candidates and computes
+    its candidates' table entries from the rotated query and the codebook otherwise;
+    forced to either path for every query, the results stay the blocked scan's."""
+    rng = np.random.default_rng(dim + m + nlist)
+    idx, cent = _build(rng, dim, m, nlist, n, rot)
+    q = (cent[rng.integers(0, nlist, nq)] + 0.3 * rng.standard_normal((nq, dim))).astype(np.float32)
+    for k, npb in searches:
+        (bi, bd, bn), _ = _search(idx, q, k, npb, "blocked")
+        (ti, td, tn), vt = _search(idx, q, k, npb, "tc", refine_table_min=table_min)
+        assert vt == 4
+        assert np.array_equal(bn, tn) and np.array_equal(bd, td) and np.array_equal(bi, ti)
 
 
 @pytest.mark.parametrize("dim,m,nlist,n,nq,rot,searches", CASES)

@@ -1154,17 +1154,20 @@ __global__ void unit_count_kernel(const uint32_t* __restrict__ cnt, const uint64
 // scan positions), then the k smallest keys.  Queries whose candidate list overflowed
 // are left to the blocked scan.
 //
-// The blocked scan adds the query's lookup-table entries T[s][c] = -2 * fma-chain over
-// t < dsub of rq[s dsub + t] * y[s][c][t] (from 0, t ascending: every table kernel's
-// arithmetic) in the lane-rotated sub-space order.  The refine computes exactly those
-// entries on the fly from the rotated query (staged in shared memory, dim floats) and
-// the fp32 codebook rows its candidates use, instead of reading the query's m x 256
-// table: a query has tens to a few thousand candidates, each needing m of its 256 x m
-// entries, so the table itself (96 KB per query at m = 96) would cost far more bytes.
+// The blocked scan adds the query's lookup-table entries T[s][c] = -2 * (fma chain over
+// t < dsub of rq[s dsub + t] * y[s][c][t], from 0, t ascending: every table kernel's
+// arithmetic) in the lane-rotated sub-space order.  A query with many candidates reads
+// its table (m x 256 floats, one bulk copy into shared memory); one with few computes
+// just the entries its candidates use from the rotated query and the fp32 codebook rows
+// (m rows of dsub floats per candidate, L2-resident), which costs less than the table
+// below kRefineTableMin candidates -- the usual case on a shard of a multi-GPU database.
+// Both give the same floats, so the result is the blocked scan's bit for bit.
 // ---------------------------------------------------------------------------------
+constexpr uint32_t kRefineTableMin = 64;   // VGPU_REFINE_TABLE_MIN overrides it
+
 template <int DS>
-__global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict__ rq, int dim,
-                                                        const float* __restrict__ cb, int m, int G,
+__global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict__ T, const float* __restrict__ rq,
+                                                        int dim, const float* __restrict__ cb, int m, int G,
                                                         const uint32_t* __restrict__ probe, int nprobe,
                                                         const float* __restrict__ pbase,
                                                         const uint64_t* __restrict__ offs,
@@ -1174,49 +1177,107 @@ __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict_
                                                         const unsigned long long* __restrict__ cand,
                                                         const uint32_t* __restrict__ cand_cnt, int cap, int k,
                                                         uint64_t* __restrict__ out_ids, float* __restrict__ out_d,
-                                                        uint32_t* __restrict__ out_n) {
+                                                        uint32_t* __restrict__ out_n, int* __restrict__ err,
+                                                        uint32_t table_min) {
+    // Shared memory: [barrier, 16 B][region: the table, later the sort keys][rq][eprefix].
+    // With the table, the keys (at most KPT per thread, in registers meanwhile) overwrite
+    // it once every candidate is scored, so a CTA needs little more than one table.
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* rqs = reinterpret_cast<float*>(smem_raw);                                         // [dim]
-    unsigned long long* keys = reinterpret_cast<unsigned long long*>(rqs + ((dim + 3) & ~3));  // [next_pow2(cap)]
-    uint32_t* eprefix = reinterpret_cast<uint32_t*>(keys + next_pow2(cap));                    // [nprobe + 1]
+    constexpr int KPT = 16;                                                          // keys per thread
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
+    const int tbytes = m * 256 * 4;
+    const int region = tbytes > next_pow2(cap) * 8 ? tbytes : next_pow2(cap) * 8;
+    float* lut = reinterpret_cast<float*>(smem_raw + 16);                             // [m * 256]
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw + 16);  // [next_pow2(cap)]
+    float* rqs = reinterpret_cast<float*>(smem_raw + 16 + region);                    // [dim]
+    uint32_t* eprefix = reinterpret_cast<uint32_t*>(rqs + ((dim + 3) & ~3));          // [nprobe + 1]
     const long long q = blockIdx.x;
     const uint32_t n = cand_cnt[q];
     if (n > (uint32_t)cap) return;
-    for (int i = threadIdx.x; i < dim; i += 256) rqs[i] = rq[q * dim + i];
-    if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nprobe, offs, nullptr, eprefix, nullptr);
-    __syncthreads();
     const int p2 = next_pow2(n < 2 ? 2 : (int)n);
-    for (int i = threadIdx.x; i < p2; i += 256) {
-        unsigned long long key = ~0ull;
-        if (i < (int)n) {
-            const unsigned long long c = cand[q * cap + i];
-            const uint32_t t = (uint32_t)(c >> 32), p = (uint32_t)c;
-            const uint32_t l = probe[q * nprobe + t];
-            const uint64_t e = offs[l] + p;
-            const uint8_t* cr = codes + e * m;
-            const int lane = (int)((p & 127u) >> 2);
-            float acc = 0.0f;
+    const bool table = n > table_min;
+    const float* tq = T + q * (long long)m * 256;
+    if (table) tc::lut_stage_begin(lut, tq, (uint32_t)tbytes, bar);
+    else for (int i = threadIdx.x; i < dim; i += 256) rqs[i] = rq[q * dim + i];
+    if (threadIdx.x < 32) probe_prefixes_warp(probe + q * nprobe, nprobe, offs, nullptr, eprefix, nullptr);
+
+    if (!table) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < p2; i += 256) {
+            unsigned long long key = ~0ull;
+            if (i < (int)n) {
+                const unsigned long long c = cand[q * cap + i];
+                const uint32_t t = (uint32_t)(c >> 32), p = (uint32_t)c;
+                const uint64_t e = offs[probe[q * nprobe + t]] + p;
+                const uint8_t* cr = codes + e * m;
+                const int lane = (int)((p & 127u) >> 2);
+                float acc = 0.0f;
 #pragma unroll 4
-            for (int r = 0; r < m; ++r) {
-                const int g = r / G, s_lo = (lane + r) & (G - 1);
-                const int sub = g * G + s_lo;
-                const float4* y = reinterpret_cast<const float4*>(cb + ((long long)sub * 256 + cr[sub]) * DS);
-                const float* x = rqs + sub * DS;
-                float a = 0.0f;
+                for (int r = 0; r < m; ++r) {
+                    const int sub = (r / G) * G + ((lane + r) & (G - 1));
+                    const float4* y = reinterpret_cast<const float4*>(cb + ((long long)sub * 256 + cr[sub]) * DS);
+                    const float* x = rqs + sub * DS;
+                    float a = 0.0f;
 #pragma unroll
-                for (int v = 0; v < DS / 4; ++v) {
-                    const float4 yv = __ldg(y + v);
-                    a = fmaf(x[4 * v + 0], yv.x, a);
-                    a = fmaf(x[4 * v + 1], yv.y, a);
-                    a = fmaf(x[4 * v + 2], yv.z, a);
-                    a = fmaf(x[4 * v + 3], yv.w, a);
+                    for (int v = 0; v < DS / 4; ++v) {
+                        const float4 yv = __ldg(y + v);
+                        a = fmaf(x[4 * v + 0], yv.x, a);
+                        a = fmaf(x[4 * v + 1], yv.y, a);
+                        a = fmaf(x[4 * v + 2], yv.z, a);
+                        a = fmaf(x[4 * v + 3], yv.w, a);
+                    }
+                    acc = __fadd_rn(acc, -2.0f * a);
                 }
-                acc = __fadd_rn(acc, -2.0f * a);
+                const float dist = (pbase[q * nprobe + t] + vterm[e]) + acc;
+                key = ((unsigned long long)float_key(dist) << 32) | (eprefix[t] + p);
             }
-            const float dist = (pbase[q * nprobe + t] + vterm[e]) + acc;
-            key = ((unsigned long long)float_key(dist) << 32) | (eprefix[t] + p);
+            keys[i] = key;
         }
-        keys[i] = key;
+    } else {
+        // Candidate metadata while the table is in flight.
+        const uint8_t* crow[KPT];
+        float dbase[KPT];
+        uint32_t slot[KPT], pos[KPT];
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = (int)threadIdx.x + j * 256;
+            crow[j] = nullptr;
+            dbase[j] = 0.0f;
+            slot[j] = pos[j] = 0;
+            if (i < (int)n) {
+                const unsigned long long c = cand[q * cap + i];
+                const uint32_t t = (uint32_t)(c >> 32), p = (uint32_t)c;
+                const uint64_t e = offs[probe[q * nprobe + t]] + p;
+                crow[j] = codes + e * m;
+                dbase[j] = pbase[q * nprobe + t] + vterm[e];
+                slot[j] = t;
+                pos[j] = p;
+            }
+        }
+        if (!tc::lut_stage_wait(lut, tq, (uint32_t)tbytes, bar) && threadIdx.x == 0 && err) atomicExch(err, 41);
+        unsigned long long kr[KPT];
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            kr[j] = ~0ull;
+            if (crow[j] != nullptr) {
+                const int lane = (int)((pos[j] & 127u) >> 2);
+                const uint8_t* cr = crow[j];
+                float acc = 0.0f;
+#pragma unroll 8
+                for (int r = 0; r < m; ++r) {
+                    const int g = r / G, s_lo = (lane + r) & (G - 1);
+                    acc += lut[(g * 256 + cr[g * G + s_lo]) * G + s_lo];
+                }
+                const float dist = dbase[j] + acc;
+                kr[j] = ((unsigned long long)float_key(dist) << 32) | (eprefix[slot[j]] + pos[j]);
+            }
+        }
+        __syncthreads();  // every read of the table is done: the keys take its place
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = (int)threadIdx.x + j * 256;
+            if (i < p2) keys[i] = kr[j];
+        }
     }
     bitonic_sort_u64<256>(keys, p2);
     const int h = (int)n < k ? (int)n : k;
@@ -1487,19 +1548,23 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     check(cudaEventRecord(w.ev[3], st), "cudaEventRecord");
 
     // Refine the candidates; overflowed queries fall back to the blocked scan.
-    // [rotated query][sort keys][probe prefixes] (tl_refine_kernel)
-    const size_t rsmem = (size_t)((a.dim + 3) & ~3) * 4 + (size_t)next_pow2(w.cap) * 8 + (size_t)(a.nprobe + 1) * 4;
-    if (rsmem > 227 * 1024) throw CudaError("tc_list_scan: refine buffers do not fit in shared memory");
+    // [barrier][table, then the sort keys][rotated query][probe prefixes] (tl_refine_kernel)
+    if (next_pow2(w.cap) > 256 * 16) throw CudaError("tc_list_scan: candidate cap above 4096");
     if (a.cb == nullptr) throw CudaError("tc_list_scan: the fp32 codebooks are required");
+    const size_t rsmem = 16 + std::max((size_t)a.m * 256 * 4, (size_t)next_pow2(w.cap) * 8) +
+                         (size_t)((a.dim + 3) & ~3) * 4 + (size_t)(a.nprobe + 1) * 4;
+    if (rsmem > 227 * 1024) throw CudaError("tc_list_scan: refine buffers do not fit in shared memory");
     const int rdsub = a.dim / a.m, rG = a.m < 32 ? a.m : 32;
+    uint32_t table_min = kRefineTableMin;
+    if (const char* v = std::getenv("VGPU_REFINE_TABLE_MIN")) table_min = (uint32_t)std::strtoul(v, nullptr, 10);
 #define VGPU_RF(DSV)                                                                                        \
     do {                                                                                                    \
         check(cudaFuncSetAttribute(tl_refine_kernel<DSV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                    (int)rsmem),                                                             \
               "cudaFuncSetAttribute(tl_refine)");                                                           \
         tl_refine_kernel<DSV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                          \
-            a.rq, a.dim, a.cb, a.m, rG, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids,        \
-            w.cand.data(), w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n);                     \
+            a.T, a.rq, a.dim, a.cb, a.m, rG, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids,   \
+            w.cand.data(), w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n, a.err, table_min);  \
     } while (0)
     if (rdsub == 4) VGPU_RF(4);
     else if (rdsub == 8) VGPU_RF(8);
