@@ -155,7 +155,7 @@ def test_threshold_exchange_keeps_the_union_top_k(dim, m, nlist, n, nq, rot, k, 
     assert all(len(c) == 1 for c in calls) and all(len(t) == 1 for t in taus)
     tau_min = torch.minimum(taus[0][0], taus[1][0])
     assert torch.isfinite(tau_min).all()
-    if split:   # each shard bounded only its own half
+    if split:   # each shard bounded only its own half (every nearest list here holds >= 4k entries per shard)
         for r in range(2):
             own = torch.arange(nq, device=taus[r][0].device) % 2 == r
             assert torch.isinf(taus[r][0][~own]).all() and torch.isfinite(taus[r][0][own]).all()

@@ -967,16 +967,19 @@ __global__ void query_prep_kernel(const float* __restrict__ rq, long long nq, in
 // threshold from the tensor-core pass over that list (pair kept in p0, 4 minima per
 // 128-entry tile), the others from the blocked scan (run flag).
 // Queries outside this shard's share (q mod shards != shard) get no threshold pass:
-// tau = -FLT_MAX (no bound) until the threshold exchange brings another shard's.
+// tau = -FLT_MAX (no bound) until the threshold exchange brings another shard's.  A
+// query whose nearest list holds fewer than short_len entries here is bounded on every
+// shard all the same: its owner's part of the list may hold fewer than k entries and
+// give no bound, and such a pass is cheap.
 __global__ void home_split_kernel(const uint32_t* __restrict__ probe, int nprobe, const float* __restrict__ pbase,
                                   const uint64_t* __restrict__ offs, long long nq, uint32_t small_max, int big_ok,
-                                  uint32_t shard, uint32_t shards, uint32_t* __restrict__ p0,
+                                  uint32_t shard, uint32_t shards, uint64_t short_len, uint32_t* __restrict__ p0,
                                   float* __restrict__ pbase0, uint32_t* __restrict__ mcount,
                                   uint32_t* __restrict__ run_lut, float* __restrict__ tau) {
     for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < nq; q += (long long)gridDim.x * blockDim.x) {
         const uint32_t l = probe[q * nprobe];
         const uint64_t L0 = offs[l + 1] - offs[l];
-        const bool mine = shards <= 1 || (uint32_t)(q % shards) == shard;
+        const bool mine = shards <= 1 || (uint32_t)(q % shards) == shard || L0 < short_len;
         const bool big = mine && big_ok && L0 > small_max;
         p0[q] = big ? l : kSkipPair;
         pbase0[q] = pbase[q * nprobe];
@@ -1505,7 +1508,8 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     }
     const uint32_t shards = a.tau_fn ? std::max(a.tau_shards, 1u) : 1u;
     home_split_kernel<<<gq, 256, 0, st>>>(a.probe, a.nprobe, a.pbase, a.offs, a.nq, small_max, a.k <= 256 ? 1 : 0,
-                                          a.tau_shard, shards, w.p0.data(), w.pbase0.data(), w.mcount.data(),
+                                          a.tau_shard, shards, (uint64_t)4 * (uint64_t)a.k, w.p0.data(),
+                                          w.pbase0.data(), w.mcount.data(),
                                           w.run_lut.data(), w.tau.data());
     VGPU_LAUNCH("home_split_kernel");
     size_t tmp = w.scan_tmp.size();
