@@ -1170,9 +1170,9 @@ __global__ void unit_count_kernel(const uint32_t* __restrict__ cnt, const uint64
 // ---------------------------------------------------------------------------------
 constexpr uint32_t kRefineTableMin = 0;   // VGPU_REFINE_TABLE_MIN overrides it
 
-template <int DS>
+template <int MC, int G, int DS>
 __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict__ T, const float* __restrict__ rq,
-                                                        int dim, const float* __restrict__ cb, int m, int G,
+                                                        int dim, const float* __restrict__ cb,
                                                         const uint32_t* __restrict__ probe, int nprobe,
                                                         const float* __restrict__ pbase,
                                                         const uint64_t* __restrict__ offs,
@@ -1188,6 +1188,7 @@ __global__ void __launch_bounds__(256) tl_refine_kernel(const float* __restrict_
     // With the table, the keys (at most KPT per thread, in registers meanwhile) overwrite
     // it once every candidate is scored, so a CTA needs little more than one table.
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    constexpr int m = MC;
     constexpr int KPT = 16;                                                          // keys per thread
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
     const int tbytes = m * 256 * 4;
@@ -1560,21 +1561,31 @@ void launch_tc_list_scan(const TlScanArgs& a, TlWork& w, cudaStream_t st) {
     const size_t rsmem = 16 + std::max((size_t)a.m * 256 * 4, (size_t)next_pow2(w.cap) * 8) +
                          (size_t)((a.dim + 3) & ~3) * 4 + (size_t)(a.nprobe + 1) * 4;
     if (rsmem > 227 * 1024) throw CudaError("tc_list_scan: refine buffers do not fit in shared memory");
-    const int rdsub = a.dim / a.m, rG = a.m < 32 ? a.m : 32;
     uint32_t table_min = kRefineTableMin;
     if (const char* v = std::getenv("VGPU_REFINE_TABLE_MIN")) table_min = (uint32_t)std::strtoul(v, nullptr, 10);
-#define VGPU_RF(DSV)                                                                                        \
+#define VGPU_RF(MCV, GV, DSV)                                                                               \
     do {                                                                                                    \
-        check(cudaFuncSetAttribute(tl_refine_kernel<DSV>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
-                                   (int)rsmem),                                                             \
+        check(cudaFuncSetAttribute(tl_refine_kernel<MCV, GV, DSV>,                                          \
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem),               \
               "cudaFuncSetAttribute(tl_refine)");                                                           \
-        tl_refine_kernel<DSV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                          \
-            a.T, a.rq, a.dim, a.cb, a.m, rG, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids,   \
+        tl_refine_kernel<MCV, GV, DSV><<<(unsigned)a.nq, 256, rsmem, st>>>(                                 \
+            a.T, a.rq, a.dim, a.cb, a.probe, a.nprobe, a.pbase, a.offs, a.codes, a.vterm, a.ids,            \
             w.cand.data(), w.cand_cnt.data(), w.cap, a.k, a.out_ids, a.out_d, a.out_n, a.err, table_min);  \
     } while (0)
-    if (rdsub == 4) VGPU_RF(4);
-    else if (rdsub == 8) VGPU_RF(8);
-    else VGPU_RF(16);
+    // (m, dsub) pairs of tc_list_scan_supported: dim = m dsub <= 768, a multiple of 64
+    const int rdsub = a.dim / a.m;
+    if (a.m == 16 && rdsub == 4) VGPU_RF(16, 16, 4);
+    else if (a.m == 16 && rdsub == 8) VGPU_RF(16, 16, 8);
+    else if (a.m == 16) VGPU_RF(16, 16, 16);
+    else if (a.m == 32 && rdsub == 4) VGPU_RF(32, 32, 4);
+    else if (a.m == 32 && rdsub == 8) VGPU_RF(32, 32, 8);
+    else if (a.m == 32) VGPU_RF(32, 32, 16);
+    else if (a.m == 64 && rdsub == 4) VGPU_RF(64, 32, 4);
+    else if (a.m == 64 && rdsub == 8) VGPU_RF(64, 32, 8);
+    else if (a.m == 96 && rdsub == 4) VGPU_RF(96, 32, 4);
+    else if (a.m == 96 && rdsub == 8) VGPU_RF(96, 32, 8);
+    else if (a.m == 128 && rdsub == 4) VGPU_RF(128, 32, 4);
+    else throw CudaError("tc_list_scan: no refine kernel for this sub-quantizer shape");
 #undef VGPU_RF
     VGPU_LAUNCH("tl_refine_kernel");
     check(cudaEventRecord(w.ev[4], st), "cudaEventRecord");
