@@ -1458,6 +1458,9 @@ def main():
                         "NCCL all-gather of the packed results and the device merge; rank 0 copies the merged "
                         "result to the host (h2d bytes summed over the ranks)"},
         "gpu_launches": launches,
+        "gpu_launches_counted": "the library's own kernels in the search calls, from its launch counter; CUB scan "
+                                "kernels excluded" + ("; at N>1 the probe call and the merge kernel not included"
+                                                      if world > 1 else ""),
         "roofline": roofline,
         "stage_ms": stage_ms,
         "outside_engine_ms": ms_step - stage_ms["total_ms"],

@@ -18,7 +18,14 @@ inline void check(cudaError_t e, const char* what) {
     if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
 }
 #define VGPU_CHECK(x) ::vgpu::check((x), #x)
-#define VGPU_LAUNCH(what) ::vgpu::check(cudaGetLastError(), what)
+// Kernels this host thread has launched (every launch site of the library ends with
+// VGPU_LAUNCH, which counts it); a search reports the difference across the call.
+// Library kernels queued by CUB's device-wide scans and sorts are not counted.
+inline unsigned long long& thread_launches() {
+    static thread_local unsigned long long n = 0;
+    return n;
+}
+#define VGPU_LAUNCH(what) (++::vgpu::thread_launches(), ::vgpu::check(cudaGetLastError(), what))
 
 // Owning device allocation (cudaMalloc/cudaFree), movable, never copied.
 template <class T>

@@ -261,7 +261,7 @@ void refine_launch(const float* q, const float* base, long long ld, int dim, con
           "cudaFuncSetAttribute(flat_refine)");
     flat_refine_kernel<IP><<<(unsigned)nrows, FR_NT, smem, st>>>(q, base, ld, dim, xn, cn, cand, cnt, cap, k, ke,
                                                                 row0, out_idx, out_score, over, n_over);
-    check(cudaGetLastError(), "flat_refine_kernel");
+    VGPU_LAUNCH("flat_refine_kernel");
 }
 
 
@@ -339,9 +339,9 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
         launch_sqrt(L.cn.data(), ns, L.cs.data(), st);
     } else {
         gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cn, ns, stride, L.cn.data());
-        check(cudaGetLastError(), "gather_stride_kernel");
+        VGPU_LAUNCH("gather_stride_kernel");
         gather_stride_kernel<<<grid_for(ns, 256), 256, 0, st>>>(v.cs, ns, stride, L.cs.data());
-        check(cudaGetLastError(), "gather_stride_kernel");
+        VGPU_LAUNCH("gather_stride_kernel");
     }
     w.launches += 2;
     if (stats) check(cudaEventRecord(w.ev[1], st), "event");
@@ -351,7 +351,7 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
               single_max, max_stride);
     w.tau.reserve(nq);
     flat_tau_kernel<<<grid_for(nq, 256), 256, 0, st>>>(L.s_val.data(), nq, k, ke, ip ? 1 : 0, w.tau.data());
-    check(cudaGetLastError(), "flat_tau_kernel");
+    VGPU_LAUNCH("flat_tau_kernel");
     ++w.launches;
     if (stats) check(cudaEventRecord(w.ev[2], st), "event");
 
@@ -444,13 +444,13 @@ void view_topk(bool ip, const float* q, long long nq, const float* xn, int dim, 
               "d2d");
         gather_rows_kernel<<<std::min<uint32_t>(n_over, 4096), 256, 0, st>>>(q, xn, w.o_rows.data(), (int)n_over, dim,
                                                                              w.oq.data(), w.oxn.data());
-        check(cudaGetLastError(), "gather_rows_kernel");
+        VGPU_LAUNCH("gather_rows_kernel");
         exact_rows(ip, w.oq.data(), n_over, w.oxn.data(), v.base, v.n, v.ld, v.cn, dim, k, w.o_idx.data(),
                    w.o_val.data(), w, st);
         scatter_rows_kernel<<<std::min<uint32_t>(n_over, 4096), 128, 0, st>>>(w.o_idx.data(), w.o_val.data(),
                                                                               w.o_rows.data(), (int)n_over, k, out_idx,
                                                                               out_val);
-        check(cudaGetLastError(), "scatter_rows_kernel");
+        VGPU_LAUNCH("scatter_rows_kernel");
         w.launches += 2;
     }
 }
@@ -497,7 +497,7 @@ void flat_topk_body(bool ip, const float* q, long long nq, const float* base, lo
     view_topk(ip, q, nq, w.xn.data(), dim, v, k, out_idx, out_score, w, 0, &stats, st, feed, single_max, max_stride);
     if (k > ke) {
         pad_topk_kernel<<<grid_for(nq * (k - ke), 256), 256, 0, st>>>(nq, k, ke, ip, out_idx, out_score);
-        check(cudaGetLastError(), "pad_topk_kernel");
+        VGPU_LAUNCH("pad_topk_kernel");
         ++w.launches;
     }
     check(cudaEventRecord(w.ev[6], st), "event");
@@ -575,7 +575,7 @@ void launch_exact_nearest(const float* x, long long nx, const float* c, long lon
     flat_topk_body(false, x, nx, c, nc, dim, k, out_idx, out_val, w, st, nullptr, kNearestSingle, nearest_stride(k));
     if (keep) {
         keep_on_tie_kernel<<<grid_for(nx * 8, 256), 256, 0, st>>>(x, nx, dim, c, keep, out_idx, out_val);
-        check(cudaGetLastError(), "keep_on_tie_kernel");
+        VGPU_LAUNCH("keep_on_tie_kernel");
         ++w.launches;
     }
 }

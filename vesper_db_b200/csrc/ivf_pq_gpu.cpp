@@ -1211,6 +1211,7 @@ public:
             reset_err();
         }
         SearchTimings tm;
+        const unsigned long long launches0 = vgpu::thread_launches();
         w_scanned.reserve(1);
         vgpu::check(cudaMemsetAsync(w_scanned.data(), 0, sizeof(unsigned long long), st), "memset");
         for (size_t q0 = 0; q0 < nq; q0 += qc) {
@@ -1337,9 +1338,6 @@ public:
                     throw vgpu::CudaError("search: the threshold exchange failed");
             }
             cudaEventRecord(ev[5], st);
-            tm.kernel_launches += (ext_probe ? 1 : filt ? 1 + (uint32_t)w_flat.last.launches : 3) + (exact ? 2 : 2) +
-                                  (has_rot ? (rot_gemm ? 2 : 1) : 0) + (tc && !filt ? 1 : 0) + (!exact && has_blocks ? 1 : 0) +
-                                  (list_scan ? 12 : 0);
             tm.scan_variant = exact ? 1u : list_scan ? 4u : (has_blocks ? 3u : 2u);
             tm.coarse_variant = filt ? 3u : tc ? 2u : 1u;
             if (!on_device) {
@@ -1375,6 +1373,7 @@ public:
         d2h(&scanned, w_scanned.data(), 1, st);
         sync(st);
         tm.scanned_entries = scanned;
+        tm.kernel_launches = (uint32_t)(vgpu::thread_launches() - launches0);
         timings = tm;
         return {};
     }

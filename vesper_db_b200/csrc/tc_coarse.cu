@@ -333,7 +333,7 @@ void tc_screen_launch(const float* x, long long nx, const float* c, long long nc
                       : dim3((unsigned)ceil_div(nc, BN), (unsigned)ceil_div(nx, BM));
     tc_screen_kernel<MODE><<<grid, 128, SMEM_BYTES, st>>>(mx, mc, (int)nx, (int)nc, dim, xn, cn, Dt, ldd, err, tau,
                                                           cand, cand_cnt, cap, col_off, qfast, cs);
-    check(cudaGetLastError(), "tc_screen_kernel");
+    VGPU_LAUNCH("tc_screen_kernel");
 }
 }  // namespace
 
@@ -929,14 +929,14 @@ void launch_aug_cols(const float* c, long long nc, int dim, long long c_ld, cons
     const long long total = nc * (long long)aug_ld(dim);
     const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
     aug_cols_kernel<<<blocks, 256, 0, st>>>(c, nc, dim, c_ld, cn, out, aug_ld(dim));
-    check(cudaGetLastError(), "aug_cols_kernel");
+    VGPU_LAUNCH("aug_cols_kernel");
 }
 
 void launch_col_max(const float* cn, const float* cs, int nc, float* cmax, cudaStream_t st) {
     check(cudaMemsetAsync(cmax, 0, 2 * sizeof(float), st), "memset");
     if (nc <= 0) return;
     col_max_kernel<<<std::min(ceil_div(nc, 256), 148), 256, 0, st>>>(cn, cs, nc, cmax);
-    check(cudaGetLastError(), "col_max_kernel");
+    VGPU_LAUNCH("col_max_kernel");
 }
 
 void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int dim, const float* xn, const float* cn,
@@ -954,7 +954,7 @@ void launch_tc_argmin(const float* x, long long nx, const float* c, int nc, int 
           "cudaFuncSetAttribute(tc_argmin)");
     tc_argmin_kernel<<<(unsigned)ceil_div(nx, BM), ARG_THREADS, ARG_SMEM, st>>>(
         mx, mc, (int)nx, nc, dim, x, c, xn, cn, cs, cmax, keep, out_idx, out_val, over, n_over, err);
-    check(cudaGetLastError(), "tc_argmin_kernel");
+    VGPU_LAUNCH("tc_argmin_kernel");
 }
 
 void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const float* c, long long nc,
@@ -993,14 +993,14 @@ void launch_tc_filter_persistent(bool ip, const float* x, long long nx, const fl
     else if (aug) VGPU_FILTER_LAUNCH(false, true);
     else VGPU_FILTER_LAUNCH(false, false);
 #undef VGPU_FILTER_LAUNCH
-    check(cudaGetLastError(), "tc_filter_kernel");
+    VGPU_LAUNCH("tc_filter_kernel");
 }
 
 void launch_scatter_top1(const uint32_t* rows, int n, const uint32_t* idx, const float* val, uint32_t* out_idx,
                          float* out_val, cudaStream_t st) {
     if (n <= 0) return;
     scatter_top1_kernel<<<std::min(ceil_div(n, 256), 148 * 8), 256, 0, st>>>(rows, n, idx, val, out_idx, out_val);
-    check(cudaGetLastError(), "scatter_top1_kernel");
+    VGPU_LAUNCH("scatter_top1_kernel");
 }
 
 __global__ void sqrt_kernel(const float* __restrict__ in, long long n, float* __restrict__ out) {
@@ -1053,7 +1053,7 @@ void prepare_rotation_3xtf32(const float* W, int dim, float* W3, cudaStream_t st
     const long long total = (long long)dim * dim;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
     tf32_split3_kernel<<<blocks, 256, 0, st>>>(W, dim, dim, 1, -0.5f, W3);
-    check(cudaGetLastError(), "tf32_split3_kernel");
+    VGPU_LAUNCH("tf32_split3_kernel");
 }
 
 void launch_rotate_3xtf32(const float* x, long long n, int dim, const float* R3, float* x3, float* out, int* err,
@@ -1063,7 +1063,7 @@ void launch_rotate_3xtf32(const float* x, long long n, int dim, const float* R3,
     const long long total = n * dim;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
     tf32_split3_kernel<<<blocks, 256, 0, st>>>(x, n, dim, 0, 1.0f, x3);
-    check(cudaGetLastError(), "tf32_split3_kernel");
+    VGPU_LAUNCH("tf32_split3_kernel");
     tc_screen_launch<1>(x3, n, R3, dim, 0, 3 * dim, nullptr, nullptr, out, dim, err, nullptr, nullptr, nullptr, 0, 0,
                         st);
 }
@@ -1072,7 +1072,7 @@ void launch_sqrt(const float* in, long long n, float* out, cudaStream_t st) {
     if (n <= 0) return;
     const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
     sqrt_kernel<<<blocks, 256, 0, st>>>(in, n, out);
-    check(cudaGetLastError(), "sqrt_kernel");
+    VGPU_LAUNCH("sqrt_kernel");
 }
 
 // ---------------------------------------------------------------------------------
@@ -1095,7 +1095,7 @@ void launch_row_norms(const float* x, long long n, int dim, float* out, cudaStre
     if (n <= 0) return;
     const int blocks = (int)std::min<long long>((n * 32 + 255) / 256, 148LL * 32);
     row_norms_kernel<<<blocks, 256, 0, st>>>(x, n, dim, ld > 0 ? ld : dim, out);
-    check(cudaGetLastError(), "row_norms_kernel");
+    VGPU_LAUNCH("row_norms_kernel");
 }
 
 // ---------------------------------------------------------------------------------
@@ -1304,7 +1304,7 @@ void screen_select_launch(const float* Dt, long long n_rows, long long ldd, int 
           "cudaFuncSetAttribute(screen_select)");
     screen_select_kernel<IP><<<(unsigned)n_rows, SS_NT, smem, st>>>(Dt, ldd, nc, x, dim, cent, cent_ld, xn, cn, k,
                                                                     keep, out_idx, out_val, err);
-    check(cudaGetLastError(), "screen_select_kernel");
+    VGPU_LAUNCH("screen_select_kernel");
 }
 }  // namespace
 
