@@ -183,3 +183,41 @@ def test_threshold_exchange_takes_the_minimum_over_ranks(tmp_path):
         got = np.load(f"{out}.{r}.npz")
         assert int(got["rc"]) == 0 and int(got["calls"]) == 1
         assert np.array_equal(got["vals"], np.array([1.0, 4.0, 2.0, np.inf, -2.0], np.float32))
+
+
+@pytest.mark.parametrize("nq,k,world", [(7, 3, 2), (10, 10, 8), (1, 1, 3), (1000, 100, 4)])
+def test_shard_results_layout(nq, k, world):
+    """The packed per-rank result buffer: the ids view is 8-byte aligned and disjoint
+    from the distances and counts, and the (offset, stride) layout handed to the device
+    merge finds every part's arrays in the concatenation that an all-gather produces."""
+    import torch
+
+    from vesper_db_b200.shard import ShardResults
+    rng = np.random.default_rng(nq + k + world)
+    parts, want = [], []
+    for r in range(world):
+        sr = ShardResults(nq, k, "cpu", world=world)
+        d = rng.standard_normal((nq, k)).astype(np.float32)
+        i = rng.integers(-2**62, 2**62, (nq, k), dtype=np.int64)
+        c = rng.integers(0, k + 1, nq).astype(np.int32)
+        sr.dist.copy_(torch.from_numpy(d))
+        sr.ids.copy_(torch.from_numpy(i))
+        sr.counts.copy_(torch.from_numpy(c))
+        nk = nq * k
+        assert (4 * sr.off_ids) % 8 == 0 and sr.words % 2 == 0          # int64 views stay aligned in every part
+        assert 4 * nk <= 4 * sr.off_ids and 4 * sr.off_ids + 8 * nk <= 4 * sr.off_n  # disjoint regions
+        assert sr.off_n + nq <= sr.words
+        assert np.array_equal(sr.dist.numpy(), d) and np.array_equal(sr.ids.numpy(), i)
+        assert np.array_equal(sr.counts.numpy(), c)
+        parts.append(sr.buf.numpy().copy())
+        want.append((d, i, c))
+    g = np.concatenate(parts).tobytes()
+    lay = sr.parts_layout()
+    for r, (d, i, c) in enumerate(want):
+        o, st = lay["dist"]
+        got_d = np.frombuffer(g, np.float32, nq * k, o + 4 * r * st).reshape(nq, k)
+        o, st = lay["ids"]
+        got_i = np.frombuffer(g, np.int64, nq * k, o + 8 * r * st).reshape(nq, k)
+        o, st = lay["counts"]
+        got_c = np.frombuffer(g, np.int32, nq, o + 4 * r * st)
+        assert np.array_equal(got_d, d) and np.array_equal(got_i, i) and np.array_equal(got_c, c)

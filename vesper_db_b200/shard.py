@@ -160,11 +160,11 @@ class ShardResults:
     over the group and merges the parts on the current CUDA stream, returning
     (dist [nq, k], ids [nq, k], counts [nq]) of the whole database."""
 
-    def __init__(self, nq: int, k: int, device, group=None):
+    def __init__(self, nq: int, k: int, device, group=None, world: int | None = None):
         import torch
         import torch.distributed as dist_mod
         self.nq, self.k, self.group = nq, k, group
-        self.world = dist_mod.get_world_size(group)
+        self.world = world if world is not None else dist_mod.get_world_size(group)
         nk = nq * k
         off_ids = nk + (nk & 1)              # int64 view needs an 8-byte aligned offset
         off_n = off_ids + 2 * nk
@@ -180,6 +180,14 @@ class ShardResults:
         self.out_d = torch.empty((nq, k), dtype=torch.float32, device=device)
         self.out_n = torch.empty(nq, dtype=torch.int32, device=device)
 
+    def parts_layout(self):
+        """Where part p's arrays sit in the gathered buffer: (byte offset of its first
+        element from the buffer's start, stride between parts in elements of that array)
+        for the distances (float32), ids (int64) and counts (int32) -- the arguments of
+        vesper_topk_merge_device."""
+        return {"dist": (0, self.words), "ids": (4 * self.off_ids, self.words // 2),
+                "counts": (4 * self.off_n, self.words)}
+
     def merge(self):
         import torch
         import torch.distributed as dist_mod
@@ -188,11 +196,12 @@ class ShardResults:
         from .index import _check
         dist_mod.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
         g = self.gathered.data_ptr()
+        lay = self.parts_layout()
         lib = N.load()
         _check(lib, lib.vesper_topk_merge_device(
-            self.world, self.nq, self.k, g, self.words, g + 4 * self.off_ids, self.words // 2, g + 4 * self.off_n,
-            self.words, self.out_ids.data_ptr(), self.out_d.data_ptr(), self.out_n.data_ptr(),
-            torch.cuda.current_stream(self.buf.device).cuda_stream))
+            self.world, self.nq, self.k, g + lay["dist"][0], lay["dist"][1], g + lay["ids"][0], lay["ids"][1],
+            g + lay["counts"][0], lay["counts"][1], self.out_ids.data_ptr(), self.out_d.data_ptr(),
+            self.out_n.data_ptr(), torch.cuda.current_stream(self.buf.device).cuda_stream))
         return self.out_d, self.out_ids, self.out_n
 
 
