@@ -131,6 +131,52 @@ def _probe_worker(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
+def _probe_local_worker(rank, world, port, out_path):
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from vesper_db_b200.shard import probed_search
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        nq, k, nprobe = 12, 3, 5
+        full = torch.zeros((nq, 4), dtype=torch.float32)
+        full[:, 0] = torch.arange(nq, dtype=torch.float32) * 3
+        per = nq // world
+        local = full[rank * per:(rank + 1) * per].clone()
+        q = torch.full((nq, 4), -1.0)       # filled by the gather
+        ids = torch.zeros((nq, k), dtype=torch.int64)
+        d = torch.zeros((nq, k), dtype=torch.float32)
+        n = torch.zeros(nq, dtype=torch.int32)
+        times = {}
+        probed_search(_FakeProbeIndex(64), q, k, nprobe, 64, ids, d, n, {}, local=local, times=times)
+        np.savez(f"{out_path}.{rank}", q=q.numpy(), ids=ids.numpy(), d=d.numpy(),
+                 phases=np.array(sorted(times)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_probed_search_gathers_host_slices(tmp_path):
+    """A batch that arrives from the host: each rank holds only its slice (`local`); the
+    slices are all-gathered into the full batch with the probe lists, and every rank
+    then searches the same full batch."""
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "probe_local")
+    mp.start_processes(_probe_local_worker, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    full = np.zeros((12, 4), np.float32)
+    full[:, 0] = np.arange(12) * 3
+    exp_ids = np.array([[(int(i * 3) * 7 + j) % 64 for j in range(3)] for i in range(12)])
+    for r in range(2):
+        got = np.load(f"{out}.{r}.npz")
+        assert np.array_equal(got["q"], full)
+        assert np.array_equal(got["ids"], exp_ids)
+        assert list(got["phases"]) == ["exchange_ms", "probe_ms", "search_ms"]
+
+
 def test_probed_search_gathers_every_slice(tmp_path):
     """Two ranks each probe half of the batch; both must search the full batch with the
     probe lists a single rank would have computed."""
